@@ -1,0 +1,246 @@
+/*
+ * qkv.h -- C ABI of the B200-native q8_0 KV-cache and attention engine.
+ *
+ * This is the drop-in boundary for the full-attention path of QwFN-hybrid
+ * (thomaskleiven/QwFN-hybrid).  The reference reaches that path through C++ objects typed with
+ * ggml (qwfn::state, engine::snapshot_*, and the ggml_flash_attn_ext / ggml_cpy / ggml_set_rows
+ * nodes its graph builder emits).  ggml is not linked here, so every entry point below takes
+ * plain pointers and sizes instead; each one names the reference interface it replaces.
+ *
+ * Conventions (the reference's, carried over -- src/qwfn_check.h:21-27, src/qwfn_engine.cpp:
+ * 1023-1041):
+ *   - every call returns a qkv_status and never aborts; qkv_last_error() explains the failure;
+ *   - a recoverable failure leaves the engine as it was (no partial page allocation, an empty
+ *     snapshot handle);
+ *   - device work is stream-ordered on the cudaStream_t passed as `stream` (NULL = legacy
+ *     default stream); pointers called "device" must be device memory of the engine's GPU;
+ *   - one engine per GPU, driven by one host thread at a time (the reference serialises its
+ *     single engine behind a mutex, tools/qwfn_server.cpp:1-12).
+ *
+ * Cache layout.  Positions are grouped in 256-token pages drawn from a pool shared by all
+ * sequence slots; a per-slot block table maps page index -> page id, and page ids are shared by
+ * all attention layers (each layer has its own pool).  Within a page, each KV head holds four
+ * 64-token tiles of q8_0 data: int8 quantised K rows, int8 quantised V stored transposed, and
+ * the fp16 block scales.  The quantised values are exactly ggml's q8_0 blocks; qkv_read_rows()
+ * and qkv_gather_rows() return them in ggml's token-major block_q8_0 layout.
+ */
+#ifndef QKV_H
+#define QKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum qkv_status {
+    QKV_OK              = 0,
+    QKV_ERR_INVALID     = 1,  /* bad argument: null pointer, layer/slot/size out of range      */
+    QKV_ERR_NO_MEMORY   = 2,  /* device memory or page pool exhausted                           */
+    QKV_ERR_CUDA        = 3,  /* a CUDA runtime call failed                                     */
+    QKV_ERR_STATE       = 4,  /* not valid now: slot inactive, context exhausted, no snapshot   */
+    QKV_ERR_MISMATCH    = 5,  /* snapshot / blob does not fit this engine                       */
+    QKV_ERR_DEVICE      = 6,  /* a kernel reported a bounds violation or a wait that gave up    */
+    QKV_ERR_UNSUPPORTED = 7   /* shape or mode this build does not provide (host-only engine)   */
+} qkv_status;
+
+typedef struct qkv_engine qkv_engine;
+typedef struct qkv_snapshot qkv_snapshot;
+
+/* Shapes.  Replaces qwfn::state_config + the attention fields of qwfn::hparams
+ * (src/qwfn_state.h:28-37, src/qwfn_hparams.h:20-31, 44-48). */
+typedef struct qkv_config {
+    int32_t n_layer;        /* attention layers held by the engine (12)                          */
+    int32_t n_head;         /* query heads (16 in the configs, 24 in the model)                  */
+    int32_t n_head_kv;      /* KV heads (2)                                                      */
+    int32_t head_dim;       /* 256 (the only value this build provides)                          */
+    int32_t n_ctx;          /* positions per sequence                                            */
+    int32_t n_slots;        /* sequence slots                                                    */
+    int32_t n_pages;        /* 256-token pages in the pool; 0 = n_slots * ceil(n_ctx / 256)      */
+    int32_t rec_n_layer;    /* recurrent (DeltaNet) layers whose state rides in snapshots (36)   */
+    int32_t rec_head_dim;   /* DeltaNet state is [rec_head_dim, rec_head_dim, rec_n_head] F32    */
+    int32_t rec_n_head;     /* value heads (48 in the model, 32 in the synthetic config)         */
+    int32_t conv_channels;  /* conv state is [conv_hist, conv_channels] F32                      */
+    int32_t conv_hist;      /* d_conv - 1 (3)                                                    */
+    int32_t n_rollback;     /* rollback snapshots of the recurrent state kept per slot (0..4)    */
+    int32_t select_block;   /* tokens per selection block (64), 0 = no block summaries           */
+} qkv_config;
+
+/* ------------------------------------------------------------------ engine / state ------ */
+
+/* Replaces qwfn::state::init (src/qwfn_state.h:46-47, src/qwfn_state.cpp:21-46).  device < 0
+ * creates a host-only engine: page tables, refcounts and snapshots work, kernels return
+ * QKV_ERR_UNSUPPORTED (used to test the host logic on machines without a GPU). */
+qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine **out);
+/* Replaces qwfn::state::~state (src/qwfn_state.cpp:12-19). */
+void qkv_destroy(qkv_engine *eng);
+const char *qkv_last_error(const qkv_engine *eng);
+const char *qkv_status_string(qkv_status st);
+
+/* Replaces state::bytes() / state::summary() (src/qwfn_state.h:66-67, src/qwfn_state.cpp:154-173).
+ * Writes a NUL-terminated line into buf (truncated to cap). */
+qkv_status qkv_bytes(const qkv_engine *eng, size_t *device_bytes);
+qkv_status qkv_summary(const qkv_engine *eng, char *buf, size_t cap);
+
+/* Sequence slots.  The reference holds one sequence (src/qwfn_state.h:14-16); slots generalise
+ * it.  qkv_seq_reset replaces state::reset / engine::reset (src/qwfn_state.cpp:113-121,
+ * src/qwfn_engine.cpp:1055-1066): pages released, n_past = 0, recurrent and conv state zeroed. */
+qkv_status qkv_seq_alloc(qkv_engine *eng, int32_t slot);
+qkv_status qkv_seq_free(qkv_engine *eng, int32_t slot);
+qkv_status qkv_seq_reset(qkv_engine *eng, int32_t slot, void *stream);
+qkv_status qkv_seq_length(const qkv_engine *eng, int32_t slot, int32_t *n_past);
+/* Page ids of a slot's block table (host copy), for inspection and tests. */
+qkv_status qkv_seq_pages(const qkv_engine *eng, int32_t slot, int32_t *pages, int32_t cap, int32_t *n);
+qkv_status qkv_page_refcount(const qkv_engine *eng, int32_t page, int32_t *refcount);
+qkv_status qkv_pages_free(const qkv_engine *eng, int32_t *n_free);
+
+/* ------------------------------------------------------------------ kernel A -------------- */
+
+/* Quantise n_rows F32 rows of K and V (device, [n_rows][n_head_kv*head_dim]) to q8_0 and write
+ * them at positions pos .. pos+n_rows-1 of layer `layer` of `slot`.  Bit-exact with ggml's
+ * quantize_row_q8_0.  Pages are allocated on demand; a page shared with a snapshot is copied
+ * first (copy-on-write).  pos <= n_past is required; n_past becomes max(n_past, pos+n_rows).
+ * Replaces graph_builder::kv_append (src/qwfn_graph.cpp:370-384, ggml_cpy F32 -> Q8_0) and
+ * qsa_dec_kv_write (src/qwfn_graph.cpp:612-628, ggml_set_rows). */
+qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos,
+                      const float *K, const float *V, int32_t n_rows, void *stream);
+
+/* ------------------------------------------------------------------ kernel C -------------- */
+
+/* Decode / MTP-verify attention for n_seq sequences, T (1..4) query tokens each.
+ *   slots[n_seq], pos0[n_seq]: HOST arrays; query token t of sequence i sits at position
+ *       pos0[i] + t and sees cache cells c <= pos0[i] + t (causal among the T tokens), i.e. the
+ *       per-position npast masks of src/qwfn_graph.cpp:671-675 chained as in
+ *       src/qwfn_engine.cpp:2266-2281.  The rows of the T tokens must already be appended.
+ *   Q:   device F32 [n_seq][T][n_head][head_dim];  out: device F32, same shape.
+ *   sel_blocks: NULL for dense attention over cells 0..pos0+T-1, or device int32
+ *       [n_seq][n_head_kv][n_sel] 64-token block ids (from qkv_select_blocks; -1 = unused) for
+ *       sparse attention over those blocks only, read in place (no gather copy).
+ * softmax(scale * QK^T + mask) V with the query converted to q8_0, exact int32 block dots, F32
+ * softmax and accumulation -- ggml_flash_attn_ext with GGML_PREC_F32 over the q8_0 cache
+ * (src/qwfn_graph.cpp:461-471 and 697-699). */
+qkv_status qkv_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                           int32_t n_seq, const float *Q, int32_t T, float scale,
+                           const int32_t *sel_blocks, int32_t n_sel, float *out, void *stream);
+
+/* ------------------------------------------------------------------ kernel B -------------- */
+
+/* Recompute the per-block key summaries of blocks [b0, b1) of `slot`'s layer `layer` from the
+ * q8_0 cache (fp16 mean of the dequantised K rows of each 64-token block, per KV head).  Replaces
+ * qsa_dec_index's pooling and engine::qsa_pool_rebuild (src/qwfn_graph.cpp:282-301, 529-552,
+ * src/qwfn_engine.cpp:1107-1148) for the synthetic sparse config.  Needs select_block == 64. */
+qkv_status qkv_block_summary(qkv_engine *eng, int32_t layer, int32_t slot, int32_t b0, int32_t b1,
+                             void *stream);
+
+/* Score the blocks of each sequence against its T query tokens and keep top_k per KV head.
+ * Blocks 0 .. nb-1 with nb = ceil((pos0+T)/64) are candidates; block 0 and the last two are
+ * always kept (the 1e9 bias of src/qwfn_engine.cpp:1092-1096), the others are ranked by
+ * sum over the group's query heads and tokens of relu(q . summary) (src/qwfn_graph.cpp:560-574),
+ * ties by lower block index.  idx_out: device int32 [n_seq][n_head_kv][top_k], best first.
+ * scores_out: nullable device F32 [n_seq][n_head_kv][max_blocks] (max_blocks = n_ctx/64).
+ * Replaces qsa_dec_cells / qsa_top_k (src/qwfn_graph.cpp:556-579, 313-367). */
+qkv_status qkv_select_blocks(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                             int32_t n_seq, const float *Q, int32_t T, int32_t top_k,
+                             int32_t *idx_out, float *scores_out, void *stream);
+
+/* Raw gather of cache rows in ggml's layout: for each of n_cells positions (device int32),
+ * write the K and V q8_0 rows (n_head_kv*head_dim/32*34 bytes each) to K_out / V_out (device).
+ * Replaces graph_builder::qsa_gather's raw path (src/qwfn_graph.cpp:632-651). */
+qkv_status qkv_gather_rows(qkv_engine *eng, int32_t layer, int32_t slot, const int32_t *cells,
+                           int32_t n_cells, void *K_out, void *V_out, void *stream);
+/* Contiguous rows pos .. pos+n-1 in ggml's layout (the bytes a ggml view of the cache holds). */
+qkv_status qkv_read_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n,
+                         void *K_out, void *V_out, void *stream);
+/* The inverse: store ggml-layout q8_0 rows (device) at pos .. pos+n-1 (allocating pages). */
+qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n,
+                          const void *K_in, const void *V_in, void *stream);
+
+/* ------------------------------------------------------------------ kernel D -------------- */
+
+/* Chunked causal prefill: Tc query tokens at positions pos0 .. pos0+Tc-1 (their K/V rows
+ * already appended) attend to cells 0 .. pos0+t.  Q: device bf16 [Tc][n_head][head_dim] (raw
+ * bf16 bits); out: device F32 [Tc][n_head][head_dim].  Replaces the prefill
+ * ggml_flash_attn_ext call of graph_builder::sparse_attn (src/qwfn_graph.cpp:417-476) with the
+ * dense causal mask built in engine::build_attn_inputs (src/qwfn_engine.cpp:1238-1274). */
+qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0,
+                            const uint16_t *Q, int32_t Tc, float scale, float *out, void *stream);
+
+/* ------------------------------------------------------------------ kernel E -------------- */
+
+/* Snapshot of a slot's first n_past positions: its pages are shared (refcounted, no KV bytes
+ * move) and the recurrent/conv state is copied device-to-device.  Replaces
+ * engine::snapshot_save (src/qwfn_engine.h:296-311, src/qwfn_engine.cpp:988-1027), whose
+ * snapshot is a set of host blobs. */
+qkv_status qkv_snapshot_save(qkv_engine *eng, int32_t slot, qkv_snapshot **out, void *stream);
+/* Restore a snapshot into a slot, keeping its first n_keep positions (n_keep < 0: all).  The
+ * slot's old pages are released, the snapshot's pages are shared, a partly kept page is copied
+ * on the slot's first write into it, and the recurrent/conv state is copied back.  Replaces
+ * engine::snapshot_load (src/qwfn_engine.cpp:1029-1053) and the server's restore_or_reset
+ * (tools/qwfn_server.cpp:1380-1404). */
+qkv_status qkv_snapshot_restore(qkv_engine *eng, const qkv_snapshot *snap, int32_t slot, int32_t n_keep,
+                                void *stream);
+/* The same for many slots at once: one batched copy launch for all recurrent state. */
+qkv_status qkv_snapshot_restore_many(qkv_engine *eng, const qkv_snapshot *snap, const int32_t *slots,
+                                     const int32_t *n_keep, int32_t n, void *stream);
+void qkv_snapshot_release(qkv_engine *eng, qkv_snapshot *snap);
+qkv_status qkv_snapshot_info(const qkv_snapshot *snap, int32_t *n_past, size_t *host_bytes);
+/* Host blobs in the reference's snapshot_parts order (src/qwfn_engine.cpp:988-999): for each
+ * attention layer the first n_past K rows then V rows (ggml q8_0 layout), then for each
+ * recurrent layer its state then its conv history (F32).  dst/src are host memory. */
+qkv_status qkv_snapshot_to_host(qkv_engine *eng, const qkv_snapshot *snap, void *dst, size_t bytes,
+                                void *stream);
+qkv_status qkv_snapshot_from_host(qkv_engine *eng, const void *src, size_t bytes, int32_t n_past,
+                                  qkv_snapshot **out, void *stream);
+
+/* Rewind n_back positions after rejected drafts: restore the recurrent/conv state from
+ * rollback snapshot n_back-1 and set n_past -= n_back (cache rows are overwritten later).
+ * Replaces engine::rollback_n (src/qwfn_engine.cpp:3629-3660). */
+qkv_status qkv_rollback(qkv_engine *eng, int32_t slot, int32_t n_back, void *stream);
+/* Declare that rollback snapshots 0..depth-1 of a slot hold the state 1..depth tokens back (the
+ * DeltaNet step that wrote them calls this; the reference sets rb_valid_/rb_depth_ in
+ * eval_batch after a multi-token step, src/qwfn_engine.cpp:3630-3655). */
+qkv_status qkv_rollback_arm(qkv_engine *eng, int32_t slot, int32_t depth);
+
+/* Device pointers of a slot's recurrent state for the (out-of-scope) DeltaNet kernels:
+ * kind 0 = state [rec_head_dim, rec_head_dim, rec_n_head] F32, kind 1 = conv [conv_hist,
+ * conv_channels] F32; which 0 = live state, 1..n_rollback = rollback snapshot which-1.
+ * Replaces state::rs_state / rs_conv (src/qwfn_state.h:55-57). */
+qkv_status qkv_state_ptr(qkv_engine *eng, int32_t slot, int32_t rec_layer, int32_t kind, int32_t which,
+                         void **ptr, size_t *bytes);
+
+/* Description of a layer's page pool, for k_cache(il)/v_cache(il) style access
+ * (src/qwfn_state.h:50-53). */
+typedef struct qkv_cache_view {
+    void   *pool;          /* device base of the layer's page pool                       */
+    size_t  page_bytes;    /* bytes of one page (all KV heads, K and V)                  */
+    size_t  tile_bytes;    /* bytes of one 64-token tile of one KV head                  */
+    int32_t page_tokens;   /* 256                                                        */
+    int32_t tile_tokens;   /* 64                                                         */
+    int32_t n_pages;
+    int32_t n_head_kv;
+    int32_t head_dim;
+    const int32_t *block_table;  /* device [n_slots][max_pages_per_seq] page ids, -1 = none */
+    int32_t max_pages_per_seq;
+} qkv_cache_view;
+qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, qkv_cache_view *view);
+
+/* Reads (and clears) the device status word that checked kernels write on a bounds violation.
+ * Synchronises the stream. */
+qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code);
+
+/* Kernels this process has launched through the library so far (all engines, all devices). */
+qkv_status qkv_launch_count(uint64_t *count);
+
+/* ------------------------------------------------------------------ multi-GPU ------------ */
+
+/* Longest-processing-time partition of n independent sequences over n_ranks GPUs by cost
+ * (e.g. context length): owner[i] receives the rank of sequence i.  Sequences never split,
+ * so no collective is needed on the attention path. */
+qkv_status qkv_shard_lpt(const int64_t *cost, int32_t n, int32_t n_ranks, int32_t *owner);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QKV_H */

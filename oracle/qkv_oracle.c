@@ -1,0 +1,301 @@
+/*
+ * qkv_oracle.c -- CPU restatement of the reference's q8_0 KV / attention path.
+ * TEST INFRASTRUCTURE ONLY (see qkv_oracle.h): the checker, never the product.
+ *
+ * Built with -ffp-contract=off so that every product/sum below rounds exactly as written;
+ * the places that must be bit-exact (quantiser, block summaries, selection scores) spell out
+ * their fused multiply-adds with fmaf().
+ */
+#include "qkv_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int orc_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+/* ---------------------------------------------------------------- fp16 ---- */
+
+uint16_t orc_fp32_to_fp16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t exp  = (x >> 23) & 0xffu;
+    uint32_t man        = x & 0x7fffffu;
+    if (exp == 0xffu) return (uint16_t)(sign | 0x7c00u | (man ? (0x200u | (man >> 13)) : 0u));
+    const int32_t e = (int32_t)exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {                         /* fp16 subnormal (or zero) */
+        if (e < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        const int shift    = 14 - e;
+        uint32_t half      = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1u);
+        const uint32_t mid = 1u << (shift - 1);
+        if (rem > mid || (rem == mid && (half & 1u))) half++;
+        return (uint16_t)(sign | half);
+    }
+    uint32_t h         = sign | ((uint32_t)e << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;   /* a carry may reach inf: RNE */
+    return (uint16_t)h;
+}
+
+float orc_fp16_to_fp32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t exp  = (h >> 10) & 0x1fu;
+    const uint32_t man  = h & 0x3ffu;
+    uint32_t x;
+    if (exp == 0) {
+        if (man == 0) {
+            x = sign;
+        } else {
+            const float f = ldexpf((float)man, -24);
+            return sign ? -f : f;
+        }
+    } else if (exp == 31) {
+        x = sign | 0x7f800000u | (man << 13);
+    } else {
+        x = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+/* ---------------------------------------------------------------- q8_0 ---- */
+
+/* ggml quantize_row_q8_0_ref restated; the CUDA copy/set_rows quantiser of the same library
+ * computes the same d, id and roundf.  gguf-py quants.py:381-393 pins it. */
+void orc_quantize_row_q8_0(const float *x, uint8_t *y, int64_t k) {
+    const int64_t nb = k / ORC_QK8_0;
+    for (int64_t i = 0; i < nb; i++) {
+        const float *xb = x + i * ORC_QK8_0;
+        uint8_t *yb     = y + i * ORC_Q8_0_BYTES;
+        float amax = 0.0f;
+        for (int j = 0; j < ORC_QK8_0; j++) {
+            const float v = fabsf(xb[j]);
+            amax = v > amax ? v : amax;
+        }
+        const float d  = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = orc_fp32_to_fp16(d);
+        yb[0] = (uint8_t)(dh & 0xffu);
+        yb[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < ORC_QK8_0; j++) {
+            const float x0 = xb[j] * id;
+            yb[2 + j] = (uint8_t)(int8_t)roundf(x0);
+        }
+    }
+}
+
+void orc_dequantize_row_q8_0(const uint8_t *y, float *x, int64_t k) {
+    const int64_t nb = k / ORC_QK8_0;
+    for (int64_t i = 0; i < nb; i++) {
+        const uint8_t *yb = y + i * ORC_Q8_0_BYTES;
+        const float d = orc_fp16_to_fp32((uint16_t)(yb[0] | (yb[1] << 8)));
+        for (int j = 0; j < ORC_QK8_0; j++) x[i * ORC_QK8_0 + j] = (float)(int8_t)yb[2 + j] * d;
+    }
+}
+
+void orc_quantize_rows_q8_0(const float *x, uint8_t *y, int64_t n_rows, int64_t k, int n_threads) {
+    const int64_t rb = k / ORC_QK8_0 * ORC_Q8_0_BYTES;
+#pragma omp parallel for schedule(static) num_threads(n_threads > 0 ? n_threads : 1)
+    for (int64_t r = 0; r < n_rows; r++) orc_quantize_row_q8_0(x + r * k, y + r * rb, k);
+}
+
+/* ----------------------------------------------------------- attention ---- */
+
+/* ggml_vec_dot_q8_0_q8_0 restated: per block an exact integer dot, then
+ * sumf += (float)isum * (d_x * d_y) in block order. */
+static float dot_q8_0(const uint8_t *kx, const uint8_t *qy, int n) {
+    const int nb = n / ORC_QK8_0;
+    float sumf = 0.0f;
+    for (int ib = 0; ib < nb; ib++) {
+        const uint8_t *a = kx + ib * ORC_Q8_0_BYTES;
+        const uint8_t *b = qy + ib * ORC_Q8_0_BYTES;
+        int32_t isum = 0;
+        for (int j = 0; j < ORC_QK8_0; j++) isum += (int32_t)(int8_t)a[2 + j] * (int32_t)(int8_t)b[2 + j];
+        const float da = orc_fp16_to_fp32((uint16_t)(a[0] | (a[1] << 8)));
+        const float db = orc_fp16_to_fp32((uint16_t)(b[0] | (b[1] << 8)));
+        sumf += (float)isum * (da * db);
+    }
+    return sumf;
+}
+
+/* One query row (token t, head h) against a list of cells: the online-softmax loop of ggml's
+ * CPU flash_attn_ext (F32 accumulation, non-F16 V branch). */
+static void attn_row(const float *q, int head_dim, const uint8_t *K, const uint8_t *V, int64_t row_bytes,
+                     int64_t head_off, const int32_t *cells, int64_t n_cells, int32_t qpos, float scale,
+                     float *o, uint8_t *qq, float *v32) {
+    orc_quantize_row_q8_0(q, qq, head_dim);
+    float S = 0.0f, M = -INFINITY;
+    for (int i = 0; i < head_dim; i++) o[i] = 0.0f;
+    for (int64_t ic = 0; ic < n_cells; ic++) {
+        const int64_t c = cells ? cells[ic] : ic;
+        if (c > qpos) continue;                     /* mask == -inf: the cell is skipped */
+        float s = dot_q8_0(K + c * row_bytes + head_off, qq, head_dim);
+        s = s * scale;
+        const float Mold = M;
+        float ms = 1.0f, vs = 1.0f;
+        if (s > M) {
+            M  = s;
+            ms = expf(Mold - M);
+            for (int i = 0; i < head_dim; i++) o[i] *= ms;
+        } else {
+            vs = expf(s - M);
+        }
+        orc_dequantize_row_q8_0(V + c * row_bytes + head_off, v32, head_dim);
+        for (int i = 0; i < head_dim; i++) o[i] += v32[i] * vs;
+        S = S * ms + vs;
+    }
+    const float S_inv = S == 0.0f ? 0.0f : 1.0f / S;
+    for (int i = 0; i < head_dim; i++) o[i] *= S_inv;
+}
+
+void orc_attn_q8_0(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                   const uint8_t *K, const uint8_t *V, const int32_t *cells, int64_t n_cells,
+                   const int32_t *q_pos, float scale, float *out, int n_threads) {
+    const int64_t hrow      = (int64_t)head_dim / ORC_QK8_0 * ORC_Q8_0_BYTES;
+    const int64_t row_bytes = hrow * n_head_kv;
+    const int group         = n_head / n_head_kv;
+#pragma omp parallel num_threads(n_threads > 0 ? n_threads : 1)
+    {
+        uint8_t *qq = (uint8_t *)malloc((size_t)hrow);
+        float *v32  = (float *)malloc(sizeof(float) * (size_t)head_dim);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t th = 0; th < T * n_head; th++) {
+            const int64_t t = th / n_head;
+            const int h     = (int)(th % n_head);
+            attn_row(Q + th * head_dim, head_dim, K, V, row_bytes, (h / group) * hrow, cells, n_cells,
+                     q_pos[t], scale, out + th * head_dim, qq, v32);
+        }
+        free(qq);
+        free(v32);
+    }
+}
+
+void orc_attn_q8_0_sparse(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                          const uint8_t *K, const uint8_t *V, const int32_t *const *cells,
+                          const int64_t *n_cells, const int32_t *q_pos, float scale, float *out,
+                          int n_threads) {
+    const int64_t hrow      = (int64_t)head_dim / ORC_QK8_0 * ORC_Q8_0_BYTES;
+    const int64_t row_bytes = hrow * n_head_kv;
+    const int group         = n_head / n_head_kv;
+#pragma omp parallel num_threads(n_threads > 0 ? n_threads : 1)
+    {
+        uint8_t *qq = (uint8_t *)malloc((size_t)hrow);
+        float *v32  = (float *)malloc(sizeof(float) * (size_t)head_dim);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t th = 0; th < T * n_head; th++) {
+            const int64_t t = th / n_head;
+            const int h     = (int)(th % n_head);
+            const int kvh   = h / group;
+            attn_row(Q + th * head_dim, head_dim, K, V, row_bytes, kvh * hrow, cells[kvh], n_cells[kvh],
+                     q_pos[t], scale, out + th * head_dim, qq, v32);
+        }
+        free(qq);
+        free(v32);
+    }
+}
+
+/* ----------------------------------------------------------- selection ---- */
+
+void orc_block_summary(const uint8_t *K, int n_head_kv, int head_dim, int block_tokens,
+                       int64_t n_blocks, uint16_t *summary, int n_threads) {
+    const int64_t hrow      = (int64_t)head_dim / ORC_QK8_0 * ORC_Q8_0_BYTES;
+    const int64_t row_bytes = hrow * n_head_kv;
+    const float inv         = 1.0f / (float)block_tokens;
+#pragma omp parallel for schedule(static) num_threads(n_threads > 0 ? n_threads : 1)
+    for (int64_t hb = 0; hb < n_head_kv * n_blocks; hb++) {
+        const int h     = (int)(hb / n_blocks);
+        const int64_t b = hb % n_blocks;
+        for (int i = 0; i < head_dim; i++) {
+            const int blk = i / ORC_QK8_0, j = i % ORC_QK8_0;
+            float acc = 0.0f;
+            for (int t = 0; t < block_tokens; t++) {
+                const uint8_t *blkp = K + (b * block_tokens + t) * row_bytes + h * hrow + blk * ORC_Q8_0_BYTES;
+                const float d = orc_fp16_to_fp32((uint16_t)(blkp[0] | (blkp[1] << 8)));
+                acc = acc + d * (float)(int8_t)blkp[2 + j];   /* d*q is exact in fp32 */
+            }
+            summary[(h * n_blocks + b) * head_dim + i] = orc_fp32_to_fp16(acc * inv);
+        }
+    }
+}
+
+static float fixed_dot(const float *q, const uint16_t *s, int head_dim) {
+    /* eight lanes of 32 dims each, then a fixed pairwise tree */
+    float p[8];
+    const int lanes = head_dim / 32;
+    for (int l = 0; l < 8; l++) {
+        float acc = 0.0f;
+        if (l < lanes)
+            for (int i = 0; i < 32; i++) acc = fmaf(q[l * 32 + i], orc_fp16_to_fp32(s[l * 32 + i]), acc);
+        p[l] = acc;
+    }
+    return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+}
+
+typedef struct { float s; int32_t b; } scored_t;
+
+static int cmp_scored(const void *a, const void *b) {
+    const scored_t *x = (const scored_t *)a, *y = (const scored_t *)b;
+    if (x->s > y->s) return -1;
+    if (x->s < y->s) return 1;
+    return x->b < y->b ? -1 : (x->b > y->b);
+}
+
+void orc_select_blocks(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                       const uint16_t *summary, int64_t n_blocks, int top_k, int32_t *idx_out,
+                       float *scores_out) {
+    const int group = n_head / n_head_kv;
+    scored_t *sc    = (scored_t *)malloc(sizeof(scored_t) * (size_t)(n_blocks > 0 ? n_blocks : 1));
+    for (int h = 0; h < n_head_kv; h++) {
+        for (int64_t b = 0; b < n_blocks; b++) {
+            float score;
+            if (b == 0 || b >= n_blocks - 2) {
+                score = INFINITY;
+            } else {
+                const uint16_t *s = summary + (h * n_blocks + b) * head_dim;
+                score = 0.0f;
+                for (int64_t t = 0; t < T; t++)
+                    for (int j = 0; j < group; j++) {
+                        const float d = fixed_dot(Q + (t * n_head + h * group + j) * head_dim, s, head_dim);
+                        score = score + (d > 0.0f ? d : 0.0f);
+                    }
+            }
+            sc[b].s = score;
+            sc[b].b = (int32_t)b;
+            if (scores_out) scores_out[h * n_blocks + b] = score;
+        }
+        if (n_blocks <= top_k) {
+            for (int k = 0; k < top_k; k++) idx_out[h * top_k + k] = k < n_blocks ? k : -1;
+            continue;
+        }
+        qsort(sc, (size_t)n_blocks, sizeof(scored_t), cmp_scored);
+        for (int k = 0; k < top_k; k++) idx_out[h * top_k + k] = sc[k].b;
+    }
+    free(sc);
+}
+
+int64_t orc_blocks_to_cells(const int32_t *blocks, int top_k, int block_tokens, int64_t n_kv,
+                            int32_t *cells_out) {
+    int64_t n = 0;
+    for (int k = 0; k < top_k; k++) {
+        if (blocks[k] < 0) continue;
+        for (int t = 0; t < block_tokens; t++) {
+            const int64_t c = (int64_t)blocks[k] * block_tokens + t;
+            if (c < n_kv) cells_out[n++] = (int32_t)c;
+        }
+    }
+    return n;
+}

@@ -1,0 +1,111 @@
+/*
+ * qkv_oracle.h -- CPU restatement of the reference's q8_0 KV-cache / attention path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product (the qwfn_hybrid_b200 package, its
+ * libqkv.so, include/qkv.h) may call, link or load this code.  It is the checker that the
+ * parity tests, __graft_entry__.smoke() and bench.py's CPU-baseline arm compare against.
+ *
+ * What it restates (reference = thomaskleiven/QwFN-hybrid, whose arithmetic is ggml/llama.cpp
+ * at unslothai/llama.cpp@ca1426903, cloned by scripts/build.sh:8-15 and NOT vendored):
+ *
+ *   - q8_0 quantisation of F32 rows, as emitted by graph_builder::kv_append
+ *     (src/qwfn_graph.cpp:370-384, ggml_cpy F32 -> Q8_0) and qsa_dec_kv_write
+ *     (src/qwfn_graph.cpp:612-628, ggml_set_rows).  The published ggml algorithm
+ *     (quantize_row_q8_0_ref): d = amax/127 in fp32, id = d ? 1/d : 0, q = roundf(x*id),
+ *     d stored as IEEE fp16 (round to nearest even).  Pinned against gguf-py 0.19.0
+ *     gguf/quants.py:378-401 (class Q8_0, "bit-exact same results as ... ggml-quants.c").
+ *
+ *   - flash attention over a q8_0 cache: ggml_flash_attn_ext(q, k, v, mask, scale, 0, 0) with
+ *     GGML_PREC_F32 (src/qwfn_graph.cpp:461-471 prefill, 697-699 decode).  Semantics of ggml's
+ *     CPU kernel: the query row is converted to K's vec-dot type (q8_0), each KQ value is
+ *     sum_b (float)isum_b * (d_k,b * d_q,b), scaled, a -inf mask entry skips the cell, online
+ *     softmax in fp32 with expf, V rows dequantised to fp32 and accumulated, result / S
+ *     (0 when S == 0).  The cache views follow src/qwfn_graph.cpp:458-464: token-major rows of
+ *     n_head_kv*head_dim elements, head h at byte offset h*row_size(head_dim).
+ *
+ *   - the QSA-style block selection restated for the synthetic sparse config (score blocks
+ *     by query . block-summary, ReLU per query head then sum, as the lightning indexer does in
+ *     src/qwfn_graph.cpp:340-349 and 560-574; forced blocks as the 1e9 bias of
+ *     src/qwfn_engine.cpp:1092-1096; top-k as ggml_top_k, src/qwfn_graph.cpp:575-578).
+ *
+ * Parity status: the q8_0 quantiser is pinned (golden vectors from gguf-py, tests/golden/).
+ * The attention restatement is NOT pinned by any reference output: the reference ships no
+ * golden vector for this path and ggml is absent from this machine ("parity unpinned").
+ */
+#pragma once
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_QK8_0 32            /* elements per q8_0 block */
+#define ORC_Q8_0_BYTES 34       /* {fp16 d, int8 qs[32]} */
+
+/* IEEE binary16 <-> binary32, round to nearest even (subnormals kept). */
+uint16_t orc_fp32_to_fp16(float f);
+float    orc_fp16_to_fp32(uint16_t h);
+
+/* k must be a multiple of 32.  y receives k/32 blocks of 34 bytes (ggml block_q8_0 layout). */
+void orc_quantize_row_q8_0(const float *x, uint8_t *y, int64_t k);
+void orc_dequantize_row_q8_0(const uint8_t *y, float *x, int64_t k);
+/* n_rows independent rows of k elements (OpenMP over rows). */
+void orc_quantize_rows_q8_0(const float *x, uint8_t *y, int64_t n_rows, int64_t k, int n_threads);
+
+/*
+ * Attention of T query tokens over a q8_0 K/V cache in ggml's token-major layout.
+ *   Q        : float [T][n_head][head_dim]
+ *   K, V     : n_kv rows of row_bytes = n_head_kv*head_dim/32*34 bytes
+ *   cells    : the cache rows to visit, in order (NULL = rows 0..n_cells-1)
+ *   q_pos    : [T] position of each query token; cell c is visible to token t iff c <= q_pos[t]
+ *              (the causal -inf mask of src/qwfn_engine.cpp:1258-1270 / graph.cpp:671-675)
+ *   out      : float [T][n_head][head_dim]
+ * GQA: query head h reads KV head h / (n_head / n_head_kv).
+ */
+void orc_attn_q8_0(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                   const uint8_t *K, const uint8_t *V,
+                   const int32_t *cells, int64_t n_cells,
+                   const int32_t *q_pos, float scale, float *out, int n_threads);
+
+/*
+ * Per-block key summary of the synthetic sparse config: for KV head h and block b of
+ * `block_tokens` consecutive rows, summary[h][b][i] = fp16( (sum_t d*q) * (1/block_tokens) ),
+ * the sum taken in fp32 in row order t = 0..block_tokens-1 (each d*q is exact in fp32).
+ * Only whole blocks (b < n_blocks) are written.
+ */
+void orc_block_summary(const uint8_t *K, int n_head_kv, int head_dim, int block_tokens,
+                       int64_t n_blocks, uint16_t *summary, int n_threads);
+
+/*
+ * Block selection for one decode step of T query tokens:
+ *   score[h][b] = +inf                                  for forced blocks (0, nb-2, nb-1)
+ *               = sum_{t<T} sum_{j<G} relu(dot(Q[t][h*G+j], summary[h][b]))   otherwise
+ * where G = n_head/n_head_kv and dot() is the fixed-order product: eight partial sums over
+ * 32 consecutive dims each (fmaf, ascending dim), combined ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)).
+ * The ReLU'd dots are summed in fp32, t-major then j.  The top_k blocks per KV head are
+ * written to idx_out[h][0..top_k) ordered by score descending, ties by block index ascending.
+ * When n_blocks <= top_k every block is selected (ascending).  scores_out (nullable) gets
+ * [n_head_kv][n_blocks].
+ */
+void orc_select_blocks(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                       const uint16_t *summary, int64_t n_blocks, int top_k,
+                       int32_t *idx_out, float *scores_out);
+
+/* Expand selected blocks (per KV head) to cell ids: block b -> rows b*bt .. b*bt+bt-1, clipped
+ * to n_kv.  Returns the number of cells written to cells_out (capacity top_k*bt). */
+int64_t orc_blocks_to_cells(const int32_t *blocks, int top_k, int block_tokens, int64_t n_kv,
+                            int32_t *cells_out);
+
+/* Sparse attention for one KV head group: like orc_attn_q8_0 but each KV head h visits its own
+ * cell list cells[h][0..n_cells[h]). */
+void orc_attn_q8_0_sparse(const float *Q, int64_t T, int n_head, int n_head_kv, int head_dim,
+                          const uint8_t *K, const uint8_t *V,
+                          const int32_t *const *cells, const int64_t *n_cells,
+                          const int32_t *q_pos, float scale, float *out, int n_threads);
+
+int orc_max_threads(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,1015 @@
+// qkv_engine.cpp -- host side of the engine: page pool, block tables, sequence slots, snapshots,
+// rollback, and the C ABI of include/qkv.h.
+//
+// The reference keeps one sequence in contiguous per-layer ggml tensors (src/qwfn_state.cpp:
+// 48-111) and snapshots by copying their first n_past rows to host blobs (src/qwfn_engine.cpp:
+// 988-1053).  Here positions live in 256-token pages drawn from a pool; a slot's block table
+// maps page index -> page id (the same id in every layer's pool).  A snapshot shares pages by
+// reference count instead of copying them, and a write into a shared page copies it first.
+#include "qkv.h"
+#include "qkv_internal.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <numeric>
+#include <string>
+#include <vector>
+
+using namespace qkv;
+
+static std::atomic<uint64_t> g_launches{0};
+void qkv::count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+extern "C" qkv_status qkv_launch_count(uint64_t *count) {
+    if (!count) return QKV_ERR_INVALID;
+    *count = g_launches.load(std::memory_order_relaxed);
+    return QKV_OK;
+}
+
+struct qkv_snapshot {
+    qkv_engine          *eng = nullptr;
+    int32_t              n_past = 0;
+    std::vector<int32_t> pages;     // shared page ids (one reference each)
+    uint8_t             *rec = nullptr;  // device copy of the recurrent / conv state
+};
+
+struct qkv_engine {
+    qkv_config  cfg{};
+    int         device    = -1;
+    bool        host_only = true;
+    std::string err;
+    int         num_sms    = 0;
+    int32_t     max_pages  = 0;       // block-table row length
+    int32_t     n_pages    = 0;
+    int64_t     page_bytes = 0;
+    int64_t     rs_bytes = 0, conv_bytes = 0, rec_layer_bytes = 0, rec_slot_bytes = 0;
+    int32_t     max_blocks = 0;       // selection blocks per sequence
+    int32_t     max_nq     = 0;
+
+    std::vector<int32_t> refcnt;
+    std::vector<int32_t> free_pages;  // stack, lowest id on top
+    struct Slot {
+        bool                 active   = false;
+        bool                 dirty    = false;
+        int32_t              n_past   = 0;
+        int32_t              rb_depth = 0;
+        std::vector<int32_t> pages;
+    };
+    std::vector<Slot>    slots;
+    std::vector<int32_t> sum_valid;   // [slot][layer] whole blocks whose summary is current
+
+    std::vector<uint8_t *> pools;     // per layer
+    int32_t  *d_bt      = nullptr;    // [n_slots][max_pages]
+    uint8_t  *d_rec     = nullptr;    // [n_slots][rec_slot_bytes]
+    uint8_t  *d_rb      = nullptr;    // [n_slots][n_rollback][rec_slot_bytes]
+    uint16_t *d_summary = nullptr;    // [n_layer][n_slots][n_head_kv][max_blocks][HD]
+    float    *d_partial = nullptr;
+    size_t    partial_bytes = 0;
+    int32_t  *d_status  = nullptr;
+    size_t    device_bytes = 0;
+
+    // pinned upload ring for block-table rows: a block is reused only after its event fired
+    static constexpr int    RING_N     = 32;
+    static constexpr size_t RING_BLOCK = 512 * 1024;
+    uint8_t    *ring = nullptr;
+    cudaEvent_t ring_ev[RING_N]{};
+    bool        ring_used[RING_N]{};
+    int         ring_next = 0;
+
+    std::vector<qkv_snapshot *> snaps;
+};
+
+// ------------------------------------------------------------------------------------ helpers
+static qkv_status fail(qkv_engine *eng, qkv_status st, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (eng) eng->err = buf;
+    return st;
+}
+#define CK(eng, call)                                                                              \
+    do {                                                                                           \
+        const cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) return fail((eng), QKV_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+static cudaStream_t S(void *stream) { return reinterpret_cast<cudaStream_t>(stream); }
+
+static qkv_status use_device(qkv_engine *eng) {
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    int cur = -1;
+    CK(eng, cudaGetDevice(&cur));
+    if (cur != eng->device) CK(eng, cudaSetDevice(eng->device));
+    return QKV_OK;
+}
+
+static qkv_status check_slot(qkv_engine *eng, int32_t slot, bool must_be_active = true) {
+    if (slot < 0 || slot >= eng->cfg.n_slots) return fail(eng, QKV_ERR_INVALID, "slot %d outside [0, %d)", slot, eng->cfg.n_slots);
+    if (must_be_active && !eng->slots[slot].active) return fail(eng, QKV_ERR_STATE, "slot %d is not allocated", slot);
+    return QKV_OK;
+}
+static qkv_status check_layer(qkv_engine *eng, int32_t layer) {
+    if (layer < 0 || layer >= eng->cfg.n_layer) return fail(eng, QKV_ERR_INVALID, "layer %d outside [0, %d)", layer, eng->cfg.n_layer);
+    return QKV_OK;
+}
+
+static void page_ref(qkv_engine *eng, int32_t p) { eng->refcnt[p]++; }
+static void page_unref(qkv_engine *eng, int32_t p) {
+    if (--eng->refcnt[p] == 0) eng->free_pages.push_back(p);
+}
+static int32_t page_alloc(qkv_engine *eng) {
+    const int32_t p = eng->free_pages.back();
+    eng->free_pages.pop_back();
+    eng->refcnt[p] = 1;
+    return p;
+}
+static void release_pages(qkv_engine *eng, std::vector<int32_t> &pages) {
+    for (int32_t p : pages) page_unref(eng, p);
+    pages.clear();
+}
+static void invalidate_summaries(qkv_engine *eng, int32_t slot, int32_t from_pos) {
+    const int32_t blk = from_pos / TILE_TOK;
+    for (int l = 0; l < eng->cfg.n_layer; l++) {
+        int32_t &v = eng->sum_valid[(size_t)slot * eng->cfg.n_layer + l];
+        v = std::min(v, blk);
+    }
+}
+
+static PoolRef pool_ref(qkv_engine *eng, int32_t layer, const int32_t *bt_row) {
+    PoolRef pr;
+    pr.pool       = eng->pools[layer];
+    pr.bt         = bt_row;
+    pr.page_bytes = eng->page_bytes;
+    pr.n_pages    = eng->n_pages;
+    pr.max_pages  = eng->max_pages;
+    pr.n_head_kv  = eng->cfg.n_head_kv;
+    pr.status     = eng->d_status;
+    return pr;
+}
+
+// Reserve a ring block for `bytes` of uploads; returns its host pointer.
+static qkv_status ring_block(qkv_engine *eng, int &k, uint8_t *&host) {
+    k = eng->ring_next;
+    eng->ring_next = (k + 1) % qkv_engine::RING_N;
+    if (eng->ring_used[k]) CK(eng, cudaEventSynchronize(eng->ring_ev[k]));
+    host = eng->ring + (size_t)k * qkv_engine::RING_BLOCK;
+    return QKV_OK;
+}
+
+// Upload the block-table rows of all dirty slots (stream-ordered, from pinned staging).
+static qkv_status flush_tables(qkv_engine *eng, cudaStream_t st) {
+    if (eng->host_only) return QKV_OK;
+    const size_t row_bytes = (size_t)eng->max_pages * sizeof(int32_t);
+    const size_t per_block = qkv_engine::RING_BLOCK / row_bytes;
+    int k = -1;
+    uint8_t *host = nullptr;
+    size_t used = per_block;
+    for (int s = 0; s < eng->cfg.n_slots; s++) {
+        qkv_engine::Slot &sl = eng->slots[s];
+        if (!sl.dirty) continue;
+        if (used == per_block) {
+            if (k >= 0) {
+                CK(eng, cudaEventRecord(eng->ring_ev[k], st));
+                eng->ring_used[k] = true;
+            }
+            const qkv_status r = ring_block(eng, k, host);
+            if (r != QKV_OK) return r;
+            used = 0;
+        }
+        int32_t *row = reinterpret_cast<int32_t *>(host + used * row_bytes);
+        std::fill(row, row + eng->max_pages, -1);
+        std::copy(sl.pages.begin(), sl.pages.end(), row);
+        CK(eng, cudaMemcpyAsync(eng->d_bt + (size_t)s * eng->max_pages, row, row_bytes, cudaMemcpyHostToDevice, st));
+        used++;
+        sl.dirty = false;
+    }
+    if (k >= 0) {
+        CK(eng, cudaEventRecord(eng->ring_ev[k], st));
+        eng->ring_used[k] = true;
+    }
+    return QKV_OK;
+}
+
+// Upload an arbitrary small int32 array (e.g. a snapshot's page list) to a device buffer.
+static qkv_status upload_i32(qkv_engine *eng, const std::vector<int32_t> &v, int32_t *dst, cudaStream_t st) {
+    size_t off = 0;
+    while (off < v.size()) {
+        int k = 0;
+        uint8_t *host = nullptr;
+        const qkv_status r = ring_block(eng, k, host);
+        if (r != QKV_OK) return r;
+        const size_t n = std::min(v.size() - off, qkv_engine::RING_BLOCK / sizeof(int32_t));
+        memcpy(host, v.data() + off, n * sizeof(int32_t));
+        CK(eng, cudaMemcpyAsync(dst + off, host, n * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+        CK(eng, cudaEventRecord(eng->ring_ev[k], st));
+        eng->ring_used[k] = true;
+        off += n;
+    }
+    return QKV_OK;
+}
+
+// Make positions [pos, pos+n) of a slot writable: allocate missing pages and copy shared ones
+// (all layers of the page) before the caller's write.  All or nothing.
+static qkv_status reserve(qkv_engine *eng, int32_t slot, int32_t pos, int32_t n, cudaStream_t st) {
+    qkv_engine::Slot &sl = eng->slots[slot];
+    const int32_t first = pos / PAGE_TOK, last = (pos + n - 1) / PAGE_TOK;
+    if (last >= eng->max_pages) return fail(eng, QKV_ERR_STATE, "context exhausted: position %d >= n_ctx %d", pos + n - 1, eng->cfg.n_ctx);
+    size_t need = 0;
+    for (int32_t pi = first; pi <= last; pi++)
+        if (pi >= (int32_t)sl.pages.size() || eng->refcnt[sl.pages[pi]] > 1) need++;
+    if (need > eng->free_pages.size())
+        return fail(eng, QKV_ERR_NO_MEMORY, "page pool exhausted: need %zu pages, %zu free", need, eng->free_pages.size());
+    std::vector<CopyDesc> cow;
+    for (int32_t pi = first; pi <= last; pi++) {
+        if (pi >= (int32_t)sl.pages.size()) {
+            sl.pages.push_back(page_alloc(eng));
+            sl.dirty = true;
+        } else if (eng->refcnt[sl.pages[pi]] > 1) {
+            const int32_t old = sl.pages[pi], fresh = page_alloc(eng);
+            for (int l = 0; l < eng->cfg.n_layer && !eng->host_only; l++)
+                cow.push_back(CopyDesc{eng->pools[l] + (int64_t)old * eng->page_bytes,
+                                       eng->pools[l] + (int64_t)fresh * eng->page_bytes, eng->page_bytes});
+            page_unref(eng, old);
+            sl.pages[pi] = fresh;
+            sl.dirty = true;
+        }
+    }
+    if (!cow.empty() && !eng->host_only) CK(eng, launch_copy_batch(cow.data(), (int)cow.size(), eng->num_sms, st));
+    return QKV_OK;
+}
+
+// ------------------------------------------------------------------------------ create/destroy
+extern "C" const char *qkv_status_string(qkv_status st) {
+    switch (st) {
+        case QKV_OK: return "ok";
+        case QKV_ERR_INVALID: return "invalid argument";
+        case QKV_ERR_NO_MEMORY: return "out of memory";
+        case QKV_ERR_CUDA: return "CUDA error";
+        case QKV_ERR_STATE: return "invalid state";
+        case QKV_ERR_MISMATCH: return "layout mismatch";
+        case QKV_ERR_DEVICE: return "device-side error";
+        case QKV_ERR_UNSUPPORTED: return "unsupported";
+    }
+    return "unknown status";
+}
+
+extern "C" const char *qkv_last_error(const qkv_engine *eng) { return eng ? eng->err.c_str() : "null engine"; }
+
+static void free_device(qkv_engine *eng) {
+    if (eng->host_only) return;
+    for (uint8_t *p : eng->pools) cudaFree(p);
+    eng->pools.clear();
+    cudaFree(eng->d_bt);
+    cudaFree(eng->d_rec);
+    cudaFree(eng->d_rb);
+    cudaFree(eng->d_summary);
+    cudaFree(eng->d_partial);
+    cudaFree(eng->d_status);
+    if (eng->ring) cudaFreeHost(eng->ring);
+    for (auto &ev : eng->ring_ev)
+        if (ev) cudaEventDestroy(ev);
+}
+
+template <class T>
+static qkv_status dalloc(qkv_engine *eng, T *&ptr, size_t bytes, const char *what) {
+    if (bytes == 0) return QKV_OK;
+    void *p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(eng, QKV_ERR_NO_MEMORY, "cudaMalloc(%s, %.3f GB): %s", what, bytes / 1e9, cudaGetErrorString(e));
+    }
+    ptr = static_cast<T *>(p);
+    eng->device_bytes += bytes;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine **out) {
+    if (!cfg || !out) return QKV_ERR_INVALID;
+    *out = nullptr;
+    const qkv_config &c = *cfg;
+    if (c.n_layer < 1 || c.n_head < 1 || c.n_head_kv < 1 || c.n_head % c.n_head_kv || c.head_dim != HD ||
+        c.n_ctx < 1 || c.n_slots < 1 || c.n_pages < 0 || c.rec_n_layer < 0 || c.n_rollback < 0 || c.n_rollback > 4 ||
+        (c.select_block != 0 && c.select_block != TILE_TOK) || c.n_head_kv > 8 || c.n_head / c.n_head_kv > 16)
+        return QKV_ERR_INVALID;
+    if (c.rec_n_layer > 0 && (c.rec_head_dim < 1 || c.rec_n_head < 1 || c.conv_channels < 1 || c.conv_hist < 1))
+        return QKV_ERR_INVALID;
+    qkv_engine *eng = new (std::nothrow) qkv_engine;
+    if (!eng) return QKV_ERR_NO_MEMORY;
+    eng->cfg       = c;
+    eng->device    = device;
+    eng->host_only = device < 0;
+    eng->max_pages = (c.n_ctx + PAGE_TOK - 1) / PAGE_TOK;
+    eng->n_pages   = c.n_pages > 0 ? c.n_pages : c.n_slots * eng->max_pages;
+    eng->page_bytes = (int64_t)c.n_head_kv * TILES_PER_PAGE * TILE_BYTES;
+    eng->rs_bytes   = (int64_t)c.rec_head_dim * c.rec_head_dim * c.rec_n_head * 4;
+    eng->conv_bytes = (int64_t)c.conv_hist * c.conv_channels * 4;
+    eng->rs_bytes   = (eng->rs_bytes + 255) / 256 * 256;
+    eng->conv_bytes = (eng->conv_bytes + 255) / 256 * 256;
+    eng->rec_layer_bytes = c.rec_n_layer > 0 ? eng->rs_bytes + eng->conv_bytes : 0;
+    eng->rec_slot_bytes  = eng->rec_layer_bytes * c.rec_n_layer;
+    eng->max_blocks = c.select_block ? (c.n_ctx + TILE_TOK - 1) / TILE_TOK : 0;
+    eng->max_nq     = 4 * (c.n_head / c.n_head_kv);
+    eng->refcnt.assign(eng->n_pages, 0);
+    eng->free_pages.resize(eng->n_pages);
+    for (int32_t i = 0; i < eng->n_pages; i++) eng->free_pages[i] = eng->n_pages - 1 - i;
+    eng->slots.resize(c.n_slots);
+    eng->sum_valid.assign((size_t)c.n_slots * c.n_layer, 0);
+    if (!eng->host_only) {
+        qkv_status r = QKV_OK;
+        cudaError_t e = cudaSetDevice(device);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&eng->num_sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) {
+            r = fail(eng, QKV_ERR_CUDA, "device %d: %s", device, cudaGetErrorString(e));
+        }
+        eng->pools.assign(c.n_layer, nullptr);
+        for (int l = 0; l < c.n_layer && r == QKV_OK; l++)
+            r = dalloc(eng, eng->pools[l], (size_t)eng->n_pages * eng->page_bytes, "page pool");
+        if (r == QKV_OK) r = dalloc(eng, eng->d_bt, (size_t)c.n_slots * eng->max_pages * 4, "block table");
+        if (r == QKV_OK) r = dalloc(eng, eng->d_rec, (size_t)c.n_slots * eng->rec_slot_bytes, "recurrent state");
+        if (r == QKV_OK) r = dalloc(eng, eng->d_rb, (size_t)c.n_slots * c.n_rollback * eng->rec_slot_bytes, "rollback state");
+        if (r == QKV_OK)
+            r = dalloc(eng, eng->d_summary, (size_t)c.n_layer * c.n_slots * c.n_head_kv * eng->max_blocks * HD * 2,
+                       "block summaries");
+        if (r == QKV_OK) {
+            eng->partial_bytes = (size_t)2 * eng->num_sms * 8 * partial_stride(eng->max_nq) * sizeof(float);
+            r = dalloc(eng, eng->d_partial, eng->partial_bytes, "split-K partials");
+        }
+        if (r == QKV_OK) r = dalloc(eng, eng->d_status, 256, "status");
+        if (r == QKV_OK) {
+            e = cudaMallocHost(&eng->ring, (size_t)qkv_engine::RING_N * qkv_engine::RING_BLOCK);
+            for (int i = 0; i < qkv_engine::RING_N && e == cudaSuccess; i++)
+                e = cudaEventCreateWithFlags(&eng->ring_ev[i], cudaEventDisableTiming);
+            if (e != cudaSuccess) r = fail(eng, QKV_ERR_CUDA, "pinned upload ring: %s", cudaGetErrorString(e));
+        }
+        if (r == QKV_OK) {
+            e = cudaMemset(eng->d_bt, 0xff, (size_t)c.n_slots * eng->max_pages * 4);
+            if (e == cudaSuccess && eng->d_rec) e = cudaMemset(eng->d_rec, 0, (size_t)c.n_slots * eng->rec_slot_bytes);
+            if (e == cudaSuccess) e = cudaMemset(eng->d_status, 0, 256);
+            if (e == cudaSuccess) e = cudaDeviceSynchronize();
+            if (e != cudaSuccess) r = fail(eng, QKV_ERR_CUDA, "init: %s", cudaGetErrorString(e));
+        }
+        if (r != QKV_OK) {
+            free_device(eng);
+            delete eng;
+            return r;
+        }
+    }
+    *out = eng;
+    return QKV_OK;
+}
+
+extern "C" void qkv_destroy(qkv_engine *eng) {
+    if (!eng) return;
+    if (!eng->host_only) {
+        cudaSetDevice(eng->device);
+        cudaDeviceSynchronize();
+        for (qkv_snapshot *s : eng->snaps) cudaFree(s->rec);
+    }
+    for (qkv_snapshot *s : eng->snaps) delete s;
+    free_device(eng);
+    delete eng;
+}
+
+extern "C" qkv_status qkv_bytes(const qkv_engine *eng, size_t *device_bytes) {
+    if (!eng || !device_bytes) return QKV_ERR_INVALID;
+    *device_bytes = eng->device_bytes;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_summary(const qkv_engine *eng, char *buf, size_t cap) {
+    if (!eng || !buf || cap == 0) return QKV_ERR_INVALID;
+    const double kv = (double)eng->n_pages * eng->page_bytes * eng->cfg.n_layer;
+    snprintf(buf, cap,
+             "qkv engine on %s: %d attention layers, %d pages x %d tokens (%.3f GB q8_0 KV), %d slots, "
+             "recurrent %.1f MB/slot, %.3f GB on the device",
+             eng->host_only ? "host only" : "cuda", eng->cfg.n_layer, eng->n_pages, PAGE_TOK, kv / 1e9,
+             eng->cfg.n_slots, eng->rec_slot_bytes / 1e6, eng->device_bytes / 1e9);
+    return QKV_OK;
+}
+
+// ---------------------------------------------------------------------------------- slots
+extern "C" qkv_status qkv_seq_alloc(qkv_engine *eng, int32_t slot) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot, false);
+    if (r != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    if (sl.active) return fail(eng, QKV_ERR_STATE, "slot %d is already allocated", slot);
+    sl.active = true;
+    sl.n_past = 0;
+    sl.rb_depth = 0;
+    sl.pages.clear();
+    sl.dirty = true;
+    invalidate_summaries(eng, slot, 0);
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_seq_free(qkv_engine *eng, int32_t slot) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    release_pages(eng, sl.pages);
+    sl.active = false;
+    sl.n_past = 0;
+    sl.rb_depth = 0;
+    sl.dirty = true;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_seq_reset(qkv_engine *eng, int32_t slot, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    release_pages(eng, sl.pages);
+    sl.n_past = 0;
+    sl.rb_depth = 0;
+    sl.dirty = true;
+    invalidate_summaries(eng, slot, 0);
+    if (eng->host_only || eng->rec_slot_bytes == 0) return QKV_OK;
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    CK(eng, cudaMemsetAsync(eng->d_rec + (size_t)slot * eng->rec_slot_bytes, 0, eng->rec_slot_bytes, S(stream)));
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_seq_length(const qkv_engine *eng, int32_t slot, int32_t *n_past) {
+    if (!eng || !n_past || slot < 0 || slot >= eng->cfg.n_slots) return QKV_ERR_INVALID;
+    *n_past = eng->slots[slot].n_past;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_seq_pages(const qkv_engine *eng, int32_t slot, int32_t *pages, int32_t cap, int32_t *n) {
+    if (!eng || !n || slot < 0 || slot >= eng->cfg.n_slots || (cap > 0 && !pages)) return QKV_ERR_INVALID;
+    const auto &pg = eng->slots[slot].pages;
+    *n = (int32_t)pg.size();
+    for (int32_t i = 0; i < cap && i < (int32_t)pg.size(); i++) pages[i] = pg[i];
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_page_refcount(const qkv_engine *eng, int32_t page, int32_t *refcount) {
+    if (!eng || !refcount || page < 0 || page >= eng->n_pages) return QKV_ERR_INVALID;
+    *refcount = eng->refcnt[page];
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_pages_free(const qkv_engine *eng, int32_t *n_free) {
+    if (!eng || !n_free) return QKV_ERR_INVALID;
+    *n_free = (int32_t)eng->free_pages.size();
+    return QKV_OK;
+}
+
+// ------------------------------------------------------------------------------------ append
+extern "C" qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, const float *K,
+                                 const float *V, int32_t n_rows, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    if (n_rows < 1 || !K || !V) return fail(eng, QKV_ERR_INVALID, "append: %d rows, K=%p V=%p", n_rows, (const void *)K, (const void *)V);
+    if (pos < 0 || pos > sl.n_past) return fail(eng, QKV_ERR_INVALID, "append at %d: slot %d holds %d positions", pos, slot, sl.n_past);
+    if ((int64_t)pos + n_rows > eng->cfg.n_ctx) return fail(eng, QKV_ERR_STATE, "context exhausted: %d + %d > n_ctx %d", pos, n_rows, eng->cfg.n_ctx);
+    if (!eng->host_only && (r = use_device(eng)) != QKV_OK) return r;
+    if ((r = reserve(eng, slot, pos, n_rows, S(stream))) != QKV_OK) return r;
+    if (eng->host_only) {
+        sl.n_past = std::max(sl.n_past, pos + n_rows);
+        invalidate_summaries(eng, slot, pos);
+        return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: pages reserved, no rows written");
+    }
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    CK(eng, launch_append(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), pos, K, V, n_rows, S(stream)));
+    sl.n_past = std::max(sl.n_past, pos + n_rows);
+    invalidate_summaries(eng, slot, pos);
+    return QKV_OK;
+}
+
+// ------------------------------------------------------------------------------------ decode
+extern "C" qkv_status qkv_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                      int32_t n_seq, const float *Q, int32_t T, float scale,
+                                      const int32_t *sel_blocks, int32_t n_sel, float *out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK) return r;
+    if (!slots || !pos0 || n_seq < 1 || !Q || !out || T < 1 || T > 4)
+        return fail(eng, QKV_ERR_INVALID, "decode: n_seq %d, T %d (1..4), null pointer", n_seq, T);
+    if (sel_blocks && n_sel < 1) return fail(eng, QKV_ERR_INVALID, "decode: n_sel %d with a selection", n_sel);
+    const int G = eng->cfg.n_head / eng->cfg.n_head_kv;
+    if (T * G > decode_max_nq()) return fail(eng, QKV_ERR_UNSUPPORTED, "decode: %d query rows per KV head (max %d)", T * G, decode_max_nq());
+    for (int i = 0; i < n_seq; i++) {
+        if ((r = check_slot(eng, slots[i])) != QKV_OK) return r;
+        if (pos0[i] < 0 || pos0[i] + T > eng->slots[slots[i]].n_past)
+            return fail(eng, QKV_ERR_INVALID, "decode: sequence %d queries positions %d..%d but slot %d holds %d", i, pos0[i],
+                        pos0[i] + T - 1, slots[i], eng->slots[slots[i]].n_past);
+    }
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    const int H = eng->cfg.n_head_kv;
+    for (int base = 0; base < n_seq; base += MAX_SEQ) {
+        const int ns = std::min(MAX_SEQ, n_seq - base);
+        DecodeParams P;
+        memset(&P, 0, sizeof P);
+        P.pool = eng->pools[layer];
+        P.block_table = eng->d_bt;
+        P.Q = Q + (size_t)base * T * eng->cfg.n_head * HD;
+        P.out = out + (size_t)base * T * eng->cfg.n_head * HD;
+        P.partial = eng->d_partial;
+        P.sel = sel_blocks ? sel_blocks + (size_t)base * H * n_sel : nullptr;
+        P.status = eng->d_status;
+        P.page_bytes = eng->page_bytes;
+        P.n_pages = eng->n_pages;
+        P.max_pages = eng->max_pages;
+        P.n_head = eng->cfg.n_head;
+        P.n_head_kv = H;
+        P.G = G;
+        P.T = T;
+        P.nq = T * G;
+        P.n_seq = ns;
+        P.n_sel = n_sel;
+        P.scale = scale;
+        P.n_pairs = ns * H;
+        int64_t tiles = 0;
+        for (int i = 0; i < ns; i++) {
+            P.seq_slot[i] = slots[base + i];
+            P.seq_pos0[i] = pos0[base + i];
+            const int32_t per = sel_blocks ? n_sel : (pos0[base + i] + T + TILE_TOK - 1) / TILE_TOK;
+            for (int h = 0; h < H; h++) {
+                P.pair_tile0[i * H + h] = (int32_t)tiles;
+                tiles += per;
+            }
+        }
+        P.pair_tile0[ns * H] = (int32_t)tiles;
+        P.total_tiles = (int32_t)tiles;
+        // Split: about two tiles per CTA, at most 4 CTAs per SM.
+        int64_t ctas = std::max<int64_t>(1, tiles / 2);
+        ctas = std::min<int64_t>(ctas, (int64_t)eng->num_sms * 4);
+        ctas = std::min<int64_t>(ctas, tiles);
+        P.n_ctas = (int32_t)ctas;
+        if ((size_t)2 * ctas * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
+            return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small");
+        CK(eng, launch_decode(P, S(stream)));
+    }
+    return QKV_OK;
+}
+
+// --------------------------------------------------------------------------------- selection
+static qkv_status refresh_summaries(qkv_engine *eng, int32_t layer, int32_t slot, int32_t nb_whole, cudaStream_t st) {
+    int32_t &v = eng->sum_valid[(size_t)slot * eng->cfg.n_layer + layer];
+    if (v >= nb_whole) return QKV_OK;
+    uint16_t *sum = eng->d_summary + ((size_t)layer * eng->cfg.n_slots + slot) * eng->cfg.n_head_kv * eng->max_blocks * HD;
+    CK(eng, launch_block_summary(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), v, nb_whole, sum,
+                                 eng->max_blocks, st));
+    v = nb_whole;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_block_summary(qkv_engine *eng, int32_t layer, int32_t slot, int32_t b0, int32_t b1,
+                                        void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    if (!eng->cfg.select_block) return fail(eng, QKV_ERR_UNSUPPORTED, "engine created with select_block = 0");
+    const int32_t whole = eng->slots[slot].n_past / TILE_TOK;
+    if (b0 < 0 || b1 < b0 || b1 > whole) return fail(eng, QKV_ERR_INVALID, "summary blocks [%d, %d) outside the %d whole blocks", b0, b1, whole);
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    uint16_t *sum = eng->d_summary + ((size_t)layer * eng->cfg.n_slots + slot) * eng->cfg.n_head_kv * eng->max_blocks * HD;
+    CK(eng, launch_block_summary(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), b0, b1, sum,
+                                 eng->max_blocks, S(stream)));
+    int32_t &v = eng->sum_valid[(size_t)slot * eng->cfg.n_layer + layer];
+    if (b0 <= v) v = std::max(v, b1);
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_select_blocks(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                        int32_t n_seq, const float *Q, int32_t T, int32_t top_k, int32_t *idx_out,
+                                        float *scores_out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK) return r;
+    if (!eng->cfg.select_block) return fail(eng, QKV_ERR_UNSUPPORTED, "engine created with select_block = 0");
+    if (!slots || !pos0 || n_seq < 1 || !Q || !idx_out || T < 1 || T > 4 || top_k < 3)
+        return fail(eng, QKV_ERR_INVALID, "select: n_seq %d, T %d, top_k %d (>= 3)", n_seq, T, top_k);
+    for (int i = 0; i < n_seq; i++) {
+        if ((r = check_slot(eng, slots[i])) != QKV_OK) return r;
+        if (pos0[i] < 0 || pos0[i] + T > eng->slots[slots[i]].n_past)
+            return fail(eng, QKV_ERR_INVALID, "select: sequence %d positions beyond slot %d", i, slots[i]);
+    }
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    const int G = eng->cfg.n_head / eng->cfg.n_head_kv;
+    for (int base = 0; base < n_seq; base += MAX_SEQ) {
+        const int ns = std::min(MAX_SEQ, n_seq - base);
+        SelectParams P;
+        memset(&P, 0, sizeof P);
+        P.Q = Q + (size_t)base * T * eng->cfg.n_head * HD;
+        P.summary = eng->d_summary + (size_t)layer * eng->cfg.n_slots * eng->cfg.n_head_kv * eng->max_blocks * HD;
+        P.idx_out = idx_out + (size_t)base * eng->cfg.n_head_kv * top_k;
+        P.scores_out = scores_out ? scores_out + (size_t)base * eng->cfg.n_head_kv * eng->max_blocks : nullptr;
+        P.n_seq = ns;
+        P.T = T;
+        P.n_head = eng->cfg.n_head;
+        P.n_head_kv = eng->cfg.n_head_kv;
+        P.G = G;
+        P.top_k = top_k;
+        P.max_blocks = eng->max_blocks;
+        for (int i = 0; i < ns; i++) {
+            const int32_t slot = slots[base + i], n_kv = pos0[base + i] + T;
+            const int32_t nb = (n_kv + TILE_TOK - 1) / TILE_TOK;
+            P.seq_slot[i] = slot;
+            P.seq_nblk[i] = nb;
+            // scored blocks are 1 .. nb-3: whole blocks, summaries refreshed lazily
+            if ((r = refresh_summaries(eng, layer, slot, std::max(0, nb - 2), S(stream))) != QKV_OK) return r;
+        }
+        CK(eng, launch_select(P, S(stream)));
+    }
+    return QKV_OK;
+}
+
+// ---------------------------------------------------------------------------- row transforms
+static qkv_status rows_common(qkv_engine *eng, int32_t layer, int32_t slot, int32_t n) {
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    if (n < 0) return fail(eng, QKV_ERR_INVALID, "negative row count");
+    return use_device(eng);
+}
+
+extern "C" qkv_status qkv_gather_rows(qkv_engine *eng, int32_t layer, int32_t slot, const int32_t *cells, int32_t n_cells,
+                                      void *K_out, void *V_out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = rows_common(eng, layer, slot, n_cells);
+    if (r != QKV_OK) return r;
+    if (n_cells == 0) return QKV_OK;
+    if (!cells || !K_out || !V_out) return fail(eng, QKV_ERR_INVALID, "gather: null pointer");
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    CK(eng, launch_read_rows(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), cells, 0, n_cells,
+                             static_cast<uint8_t *>(K_out), static_cast<uint8_t *>(V_out), S(stream)));
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_read_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n, void *K_out,
+                                    void *V_out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = rows_common(eng, layer, slot, n);
+    if (r != QKV_OK) return r;
+    if (pos < 0 || pos + n > eng->slots[slot].n_past)
+        return fail(eng, QKV_ERR_INVALID, "read rows %d..%d: slot %d holds %d", pos, pos + n - 1, slot, eng->slots[slot].n_past);
+    if (n == 0) return QKV_OK;
+    if (!K_out || !V_out) return fail(eng, QKV_ERR_INVALID, "read rows: null pointer");
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    CK(eng, launch_read_rows(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), nullptr, pos, n,
+                             static_cast<uint8_t *>(K_out), static_cast<uint8_t *>(V_out), S(stream)));
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n,
+                                     const void *K_in, const void *V_in, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = rows_common(eng, layer, slot, n);
+    if (r != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    if (pos < 0 || pos > sl.n_past || (int64_t)pos + n > eng->cfg.n_ctx)
+        return fail(eng, QKV_ERR_INVALID, "write rows at %d: slot %d holds %d (n_ctx %d)", pos, slot, sl.n_past, eng->cfg.n_ctx);
+    if (n == 0) return QKV_OK;
+    if (!K_in || !V_in) return fail(eng, QKV_ERR_INVALID, "write rows: null pointer");
+    if ((r = reserve(eng, slot, pos, n, S(stream))) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    CK(eng, launch_write_rows(pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages), pos, n,
+                              static_cast<const uint8_t *>(K_in), static_cast<const uint8_t *>(V_in), S(stream)));
+    sl.n_past = std::max(sl.n_past, pos + n);
+    invalidate_summaries(eng, slot, pos);
+    return QKV_OK;
+}
+
+// ---------------------------------------------------------------------------------- prefill
+extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const uint16_t *Q,
+                                       int32_t Tc, float scale, float *out, void *stream) {
+    (void)layer; (void)slot; (void)pos0; (void)Q; (void)Tc; (void)scale; (void)out; (void)stream;
+    if (!eng) return QKV_ERR_INVALID;
+    return fail(eng, QKV_ERR_UNSUPPORTED, "prefill attention is not built yet");
+}
+
+// -------------------------------------------------------------------------------- snapshots
+static qkv_status rec_copy(qkv_engine *eng, const std::vector<CopyDesc> &d, cudaStream_t st) {
+    if (d.empty() || eng->host_only) return QKV_OK;
+    CK(eng, launch_copy_batch(d.data(), (int)d.size(), eng->num_sms, st));
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_snapshot_save(qkv_engine *eng, int32_t slot, qkv_snapshot **out, void *stream) {
+    if (!eng || !out) return QKV_ERR_INVALID;
+    *out = nullptr;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    if (!eng->host_only && (r = use_device(eng)) != QKV_OK) return r;
+    qkv_snapshot *snap = new (std::nothrow) qkv_snapshot;
+    if (!snap) return fail(eng, QKV_ERR_NO_MEMORY, "snapshot: host allocation");
+    const qkv_engine::Slot &sl = eng->slots[slot];
+    snap->eng = eng;
+    snap->n_past = sl.n_past;
+    if (!eng->host_only && eng->rec_slot_bytes > 0) {
+        r = dalloc(eng, snap->rec, eng->rec_slot_bytes, "snapshot recurrent state");
+        if (r != QKV_OK) {
+            delete snap;
+            return r;
+        }
+        eng->device_bytes -= eng->rec_slot_bytes;  // snapshots are reported separately
+        r = rec_copy(eng, {CopyDesc{eng->d_rec + (size_t)slot * eng->rec_slot_bytes, snap->rec, eng->rec_slot_bytes}},
+                     S(stream));
+        if (r != QKV_OK) {
+            cudaFree(snap->rec);
+            delete snap;
+            return r;
+        }
+    }
+    const int32_t np = (sl.n_past + PAGE_TOK - 1) / PAGE_TOK;
+    snap->pages.assign(sl.pages.begin(), sl.pages.begin() + np);
+    for (int32_t p : snap->pages) page_ref(eng, p);
+    eng->snaps.push_back(snap);
+    *out = snap;
+    return QKV_OK;
+}
+
+static qkv_status restore_one(qkv_engine *eng, const qkv_snapshot *snap, int32_t slot, int32_t n_keep,
+                              std::vector<CopyDesc> &copies) {
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    if (n_keep < 0) n_keep = snap->n_past;
+    if (n_keep > snap->n_past) return fail(eng, QKV_ERR_INVALID, "restore keeps %d of a %d-position snapshot", n_keep, snap->n_past);
+    qkv_engine::Slot &sl = eng->slots[slot];
+    // take the new references before dropping the old ones: restoring a slot's own snapshot
+    const int32_t np = (n_keep + PAGE_TOK - 1) / PAGE_TOK;
+    for (int32_t i = 0; i < np; i++) page_ref(eng, snap->pages[i]);
+    release_pages(eng, sl.pages);
+    sl.pages.assign(snap->pages.begin(), snap->pages.begin() + np);
+    sl.n_past = n_keep;
+    sl.rb_depth = 0;
+    sl.dirty = true;
+    invalidate_summaries(eng, slot, 0);
+    if (snap->rec) copies.push_back(CopyDesc{snap->rec, eng->d_rec + (size_t)slot * eng->rec_slot_bytes, eng->rec_slot_bytes});
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_snapshot_restore(qkv_engine *eng, const qkv_snapshot *snap, int32_t slot, int32_t n_keep,
+                                           void *stream) {
+    return qkv_snapshot_restore_many(eng, snap, &slot, &n_keep, 1, stream);
+}
+
+extern "C" qkv_status qkv_snapshot_restore_many(qkv_engine *eng, const qkv_snapshot *snap, const int32_t *slots,
+                                                const int32_t *n_keep, int32_t n, void *stream) {
+    if (!eng || !snap || !slots || n < 0) return QKV_ERR_INVALID;
+    if (snap->eng != eng) return fail(eng, QKV_ERR_MISMATCH, "snapshot belongs to another engine");
+    qkv_status r;
+    if (!eng->host_only && (r = use_device(eng)) != QKV_OK) return r;
+    for (int i = 0; i < n; i++) {   // validate everything before changing anything
+        if ((r = check_slot(eng, slots[i])) != QKV_OK) return r;
+        const int32_t k = n_keep ? n_keep[i] : -1;
+        if (k > snap->n_past) return fail(eng, QKV_ERR_INVALID, "restore keeps %d of a %d-position snapshot", k, snap->n_past);
+    }
+    std::vector<CopyDesc> copies;
+    for (int i = 0; i < n; i++)
+        if ((r = restore_one(eng, snap, slots[i], n_keep ? n_keep[i] : -1, copies)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    return rec_copy(eng, copies, S(stream));
+}
+
+extern "C" void qkv_snapshot_release(qkv_engine *eng, qkv_snapshot *snap) {
+    if (!eng || !snap || snap->eng != eng) return;
+    auto it = std::find(eng->snaps.begin(), eng->snaps.end(), snap);
+    if (it == eng->snaps.end()) return;
+    eng->snaps.erase(it);
+    for (int32_t p : snap->pages) page_unref(eng, p);
+    if (snap->rec && !eng->host_only) {
+        cudaSetDevice(eng->device);
+        cudaDeviceSynchronize();   // a restore may still be reading it
+        cudaFree(snap->rec);
+    }
+    delete snap;
+}
+
+extern "C" qkv_status qkv_snapshot_info(const qkv_snapshot *snap, int32_t *n_past, size_t *host_bytes) {
+    if (!snap) return QKV_ERR_INVALID;
+    const qkv_engine *eng = snap->eng;
+    if (n_past) *n_past = snap->n_past;
+    if (host_bytes)
+        *host_bytes = (size_t)eng->cfg.n_layer * 2 * snap->n_past * eng->cfg.n_head_kv * ROW_Q8 +
+                      (size_t)eng->cfg.rec_n_layer * ((size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4 +
+                                                      (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4);
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_snapshot_to_host(qkv_engine *eng, const qkv_snapshot *snap, void *dst, size_t bytes,
+                                           void *stream) {
+    if (!eng || !snap || !dst) return QKV_ERR_INVALID;
+    if (snap->eng != eng) return fail(eng, QKV_ERR_MISMATCH, "snapshot belongs to another engine");
+    size_t need = 0;
+    qkv_snapshot_info(snap, nullptr, &need);
+    if (bytes != need) return fail(eng, QKV_ERR_MISMATCH, "host blob is %zu bytes, snapshot needs %zu", bytes, need);
+    qkv_status r = use_device(eng);
+    if (r != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    const size_t rows = (size_t)snap->n_past * eng->cfg.n_head_kv * ROW_Q8;
+    uint8_t *out = static_cast<uint8_t *>(dst);
+    uint8_t *stage = nullptr;
+    int32_t *d_pages = nullptr;
+    if ((r = dalloc(eng, stage, std::max<size_t>(2 * rows, 16), "snapshot staging")) != QKV_OK) return r;
+    eng->device_bytes -= std::max<size_t>(2 * rows, 16);
+    if ((r = dalloc(eng, d_pages, std::max<size_t>(snap->pages.size(), 1) * 4, "snapshot pages")) != QKV_OK) {
+        cudaFree(stage);
+        return r;
+    }
+    eng->device_bytes -= std::max<size_t>(snap->pages.size(), 1) * 4;
+    auto done = [&](qkv_status s) {
+        cudaStreamSynchronize(st);
+        cudaFree(stage);
+        cudaFree(d_pages);
+        return s;
+    };
+    if ((r = upload_i32(eng, snap->pages, d_pages, st)) != QKV_OK) return done(r);
+    for (int l = 0; l < eng->cfg.n_layer && snap->n_past > 0; l++) {
+        if (launch_read_rows(pool_ref(eng, l, d_pages), nullptr, 0, snap->n_past, stage, stage + rows, st) != cudaSuccess ||
+            cudaMemcpyAsync(out, stage, 2 * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return done(fail(eng, QKV_ERR_CUDA, "snapshot export of layer %d: %s", l, cudaGetErrorString(cudaGetLastError())));
+        out += 2 * rows;
+    }
+    const size_t rs = (size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4;
+    const size_t cv = (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4;
+    for (int l = 0; l < eng->cfg.rec_n_layer; l++) {
+        const uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
+        if (cudaMemcpyAsync(out, base, rs, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out + rs, base + eng->rs_bytes, cv, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return done(fail(eng, QKV_ERR_CUDA, "snapshot export of recurrent layer %d", l));
+        out += rs + cv;
+    }
+    return done(QKV_OK);
+}
+
+extern "C" qkv_status qkv_snapshot_from_host(qkv_engine *eng, const void *src, size_t bytes, int32_t n_past,
+                                             qkv_snapshot **out, void *stream) {
+    if (!eng || !src || !out || n_past < 0) return QKV_ERR_INVALID;
+    *out = nullptr;
+    if (n_past > eng->cfg.n_ctx) return fail(eng, QKV_ERR_MISMATCH, "snapshot of %d positions exceeds n_ctx %d", n_past, eng->cfg.n_ctx);
+    qkv_status r = use_device(eng);
+    if (r != QKV_OK) return r;
+    qkv_snapshot probe;
+    probe.eng = eng;
+    probe.n_past = n_past;
+    size_t need = 0;
+    qkv_snapshot_info(&probe, nullptr, &need);
+    if (bytes != need) return fail(eng, QKV_ERR_MISMATCH, "host blob is %zu bytes, %d positions need %zu", bytes, n_past, need);
+    const int32_t np = (n_past + PAGE_TOK - 1) / PAGE_TOK;
+    if ((size_t)np > eng->free_pages.size()) return fail(eng, QKV_ERR_NO_MEMORY, "page pool exhausted");
+    qkv_snapshot *snap = new (std::nothrow) qkv_snapshot;
+    if (!snap) return fail(eng, QKV_ERR_NO_MEMORY, "snapshot: host allocation");
+    snap->eng = eng;
+    snap->n_past = n_past;
+    for (int32_t i = 0; i < np; i++) snap->pages.push_back(page_alloc(eng));
+    cudaStream_t st = S(stream);
+    const size_t rows = (size_t)n_past * eng->cfg.n_head_kv * ROW_Q8;
+    uint8_t *stage = nullptr;
+    int32_t *d_pages = nullptr;
+    auto undo = [&](qkv_status s) {
+        cudaStreamSynchronize(st);
+        cudaFree(stage);
+        cudaFree(d_pages);
+        for (int32_t p : snap->pages) page_unref(eng, p);
+        cudaFree(snap->rec);
+        delete snap;
+        return s;
+    };
+    if ((r = dalloc(eng, stage, std::max<size_t>(2 * rows, 16), "snapshot staging")) != QKV_OK) return undo(r);
+    eng->device_bytes -= std::max<size_t>(2 * rows, 16);
+    if ((r = dalloc(eng, d_pages, std::max<size_t>(np, 1) * 4, "snapshot pages")) != QKV_OK) return undo(r);
+    eng->device_bytes -= std::max<size_t>(np, 1) * 4;
+    if (eng->rec_slot_bytes > 0) {
+        if ((r = dalloc(eng, snap->rec, eng->rec_slot_bytes, "snapshot recurrent state")) != QKV_OK) return undo(r);
+        eng->device_bytes -= eng->rec_slot_bytes;
+        CK(eng, cudaMemsetAsync(snap->rec, 0, eng->rec_slot_bytes, st));
+    }
+    if ((r = upload_i32(eng, snap->pages, d_pages, st)) != QKV_OK) return undo(r);
+    const uint8_t *in = static_cast<const uint8_t *>(src);
+    for (int l = 0; l < eng->cfg.n_layer && n_past > 0; l++) {
+        if (cudaMemcpyAsync(stage, in, 2 * rows, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            launch_write_rows(pool_ref(eng, l, d_pages), 0, n_past, stage, stage + rows, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of layer %d", l));
+        in += 2 * rows;
+    }
+    const size_t rs = (size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4;
+    const size_t cv = (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4;
+    for (int l = 0; l < eng->cfg.rec_n_layer; l++) {
+        uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
+        if (cudaMemcpyAsync(base, in, rs, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(base + eng->rs_bytes, in + rs, cv, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of recurrent layer %d", l));
+        in += rs + cv;
+    }
+    cudaStreamSynchronize(st);
+    cudaFree(stage);
+    cudaFree(d_pages);
+    eng->snaps.push_back(snap);
+    *out = snap;
+    return QKV_OK;
+}
+
+// --------------------------------------------------------------------------------- rollback
+extern "C" qkv_status qkv_rollback_arm(qkv_engine *eng, int32_t slot, int32_t depth) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    if (depth < 0 || depth > eng->cfg.n_rollback)
+        return fail(eng, QKV_ERR_INVALID, "rollback depth %d outside [0, %d]", depth, eng->cfg.n_rollback);
+    eng->slots[slot].rb_depth = depth;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_rollback(qkv_engine *eng, int32_t slot, int32_t n_back, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    qkv_engine::Slot &sl = eng->slots[slot];
+    if (n_back < 1 || n_back > sl.rb_depth)
+        return fail(eng, QKV_ERR_STATE, "rollback: no snapshot of the state %d tokens back (depth %d)", n_back, sl.rb_depth);
+    if (n_back > sl.n_past) return fail(eng, QKV_ERR_STATE, "rollback of %d past position 0", n_back);
+    if (!eng->host_only) {
+        if ((r = use_device(eng)) != QKV_OK) return r;
+        if (eng->rec_slot_bytes > 0) {
+            const uint8_t *src = eng->d_rb + ((size_t)slot * eng->cfg.n_rollback + (n_back - 1)) * eng->rec_slot_bytes;
+            if ((r = rec_copy(eng, {CopyDesc{src, eng->d_rec + (size_t)slot * eng->rec_slot_bytes, eng->rec_slot_bytes}},
+                              S(stream))) != QKV_OK)
+                return r;
+        }
+    }
+    sl.n_past -= n_back;
+    sl.rb_depth = 0;
+    invalidate_summaries(eng, slot, sl.n_past);
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_state_ptr(qkv_engine *eng, int32_t slot, int32_t rec_layer, int32_t kind, int32_t which,
+                                    void **ptr, size_t *bytes) {
+    if (!eng || !ptr) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot, false);
+    if (r != QKV_OK) return r;
+    if (rec_layer < 0 || rec_layer >= eng->cfg.rec_n_layer || kind < 0 || kind > 1 || which < 0 || which > eng->cfg.n_rollback)
+        return fail(eng, QKV_ERR_INVALID, "state_ptr: layer %d kind %d which %d", rec_layer, kind, which);
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine has no device state");
+    uint8_t *base = which == 0 ? eng->d_rec + (size_t)slot * eng->rec_slot_bytes
+                               : eng->d_rb + ((size_t)slot * eng->cfg.n_rollback + (which - 1)) * eng->rec_slot_bytes;
+    base += (size_t)rec_layer * eng->rec_layer_bytes + (kind ? eng->rs_bytes : 0);
+    *ptr = base;
+    if (bytes)
+        *bytes = kind ? (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4
+                      : (size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, qkv_cache_view *view) {
+    if (!eng || !view || layer < 0 || layer >= eng->cfg.n_layer) return QKV_ERR_INVALID;
+    view->pool = eng->host_only ? nullptr : eng->pools[layer];
+    view->page_bytes = (size_t)eng->page_bytes;
+    view->tile_bytes = TILE_BYTES;
+    view->page_tokens = PAGE_TOK;
+    view->tile_tokens = TILE_TOK;
+    view->n_pages = eng->n_pages;
+    view->n_head_kv = eng->cfg.n_head_kv;
+    view->head_dim = HD;
+    view->block_table = eng->d_bt;
+    view->max_pages_per_seq = eng->max_pages;
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code) {
+    if (!eng || !code) return QKV_ERR_INVALID;
+    qkv_status r = use_device(eng);
+    if (r != QKV_OK) return r;
+    int32_t h = 0;
+    CK(eng, cudaMemcpyAsync(&h, eng->d_status, 4, cudaMemcpyDeviceToHost, S(stream)));
+    CK(eng, cudaStreamSynchronize(S(stream)));
+    CK(eng, cudaMemsetAsync(eng->d_status, 0, 4, S(stream)));
+    *code = h;
+    return h ? fail(eng, QKV_ERR_DEVICE, "device status 0x%x (1 = bad page, 2 = bad index)", h) : QKV_OK;
+}
+
+// ------------------------------------------------------------------------------- multi-GPU
+extern "C" qkv_status qkv_shard_lpt(const int64_t *cost, int32_t n, int32_t n_ranks, int32_t *owner) {
+    if (n < 0 || n_ranks < 1 || (n > 0 && (!cost || !owner))) return QKV_ERR_INVALID;
+    std::vector<int32_t> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return cost[a] > cost[b]; });
+    std::vector<int64_t> load(n_ranks, 0);
+    for (int32_t i : order) {
+        int32_t best = 0;
+        for (int32_t k = 1; k < n_ranks; k++)
+            if (load[k] < load[best]) best = k;
+        owner[i] = best;
+        load[best] += cost[i];
+    }
+    return QKV_OK;
+}

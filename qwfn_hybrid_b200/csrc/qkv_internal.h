@@ -1,0 +1,124 @@
+// qkv_internal.h -- cache layout constants and kernel launch interfaces shared by the engine
+// (qkv_engine.cpp) and the kernels (*.cu).  Not part of the public ABI (include/qkv.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace qkv {
+
+// Kernels launched by this library (qkv_launch_count); bumped by every launch helper.
+void count_launches(uint64_t n);
+
+// ---- q8_0 and head geometry ---------------------------------------------------------------
+constexpr int HD         = 256;         // head_dim (the only value provided)
+constexpr int QK         = 32;          // q8_0 block
+constexpr int NBLK       = HD / QK;     // 8 q8_0 blocks per head row
+constexpr int ROW_Q8     = NBLK * 34;   // 272 bytes of ggml block_q8_0 per head row
+
+// ---- pages and tiles ------------------------------------------------------------------------
+// A page holds 256 positions of one layer.  Per KV head it holds four 64-token tiles, each a
+// contiguous 34816-byte record, so that one bulk copy moves everything attention needs for
+// 64 tokens of one head:
+//   [0, 16384)      K quants, token-major: token t's 256 int8 at t*256, its 16-byte chunks
+//                   XOR-swizzled by kswz(t) (bank-conflict-free ldmatrix of 8 token rows)
+//   [16384, 32768)  V quants, transposed: dim i's 64 int8 (tokens) at 16384 + i*64, its four
+//                   16-byte chunks XOR-swizzled by (i>>1)&3
+//   [32768, 33792)  K scales, fp16 [64 tokens][8 blocks]
+//   [33792, 34816)  V scales, fp16 [8 blocks][64 tokens]
+// Page = [head][tile] records; page bytes = n_head_kv * 4 * 34816 (278528 for two heads, the
+// same bytes as 256 ggml q8_0 K and V rows of 544 bytes).
+constexpr int PAGE_TOK       = 256;
+constexpr int TILE_TOK       = 64;
+constexpr int TILES_PER_PAGE = PAGE_TOK / TILE_TOK;
+constexpr int TILE_KQ        = 0;
+constexpr int TILE_VQ        = 16384;
+constexpr int TILE_KD        = 32768;
+constexpr int TILE_VD        = 33792;
+constexpr int TILE_BYTES     = 34816;
+
+__host__ __device__ __forceinline__ int kswz(int t) { return (((t >> 2) & 3) << 1) | (t & 1); }
+// byte offset of K quant (token t, element j) inside a tile
+__host__ __device__ __forceinline__ int k_off(int t, int j) {
+    return TILE_KQ + t * HD + ((((j >> 4) ^ kswz(t))) << 4) + (j & 15);
+}
+// byte offset of V quant (element i, token t) inside a tile
+__host__ __device__ __forceinline__ int v_off(int i, int t) {
+    return TILE_VQ + i * TILE_TOK + ((((t >> 4) ^ ((i >> 1) & 3))) << 4) + (t & 15);
+}
+__host__ __device__ __forceinline__ int kd_off(int t, int b) { return TILE_KD + (t * NBLK + b) * 2; }
+__host__ __device__ __forceinline__ int vd_off(int b, int t) { return TILE_VD + (b * TILE_TOK + t) * 2; }
+
+// Device status word bits (qkv_device_status).
+constexpr int32_t ST_BAD_PAGE  = 1;    // a block-table entry was < 0 or >= n_pages
+constexpr int32_t ST_BAD_INDEX = 2;    // a cell / block index outside the sequence
+
+// ---- kernel A and layout transforms ------------------------------------------------------------
+struct PoolRef {
+    uint8_t       *pool;          // layer pool base
+    const int32_t *bt;            // block-table row of the slot (device)
+    int64_t        page_bytes;
+    int32_t        n_pages;
+    int32_t        max_pages;     // length of the block-table row
+    int32_t        n_head_kv;
+    int32_t       *status;
+};
+
+cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const float *V, int32_t n_rows,
+                          cudaStream_t st);
+// cells == nullptr: rows pos .. pos+n-1
+cudaError_t launch_read_rows(const PoolRef &pr, const int32_t *cells, int32_t pos, int32_t n, uint8_t *K_out,
+                             uint8_t *V_out, cudaStream_t st);
+cudaError_t launch_write_rows(const PoolRef &pr, int32_t pos, int32_t n, const uint8_t *K_in, const uint8_t *V_in,
+                              cudaStream_t st);
+
+// ---- kernel E: batched device copies ------------------------------------------------------------
+constexpr int COPY_MAX = 64;
+struct CopyDesc {
+    const uint8_t *src;
+    uint8_t       *dst;
+    int64_t        bytes;          // multiple of 16, both pointers 16-byte aligned
+};
+cudaError_t launch_copy_batch(const CopyDesc *descs, int n, int num_sms, cudaStream_t st);
+
+// ---- kernel B ---------------------------------------------------------------------------------
+cudaError_t launch_block_summary(const PoolRef &pr, int32_t b0, int32_t b1, uint16_t *summary, int32_t max_blocks,
+                                 cudaStream_t st);
+
+constexpr int MAX_SEQ = 64;
+struct SelectParams {
+    const float    *Q;            // [n_seq][T][n_head][HD]
+    const uint16_t *summary;      // layer base: [slot][n_head_kv][max_blocks][HD] fp16
+    int32_t        *idx_out;      // [n_seq][n_head_kv][top_k]
+    float          *scores_out;   // nullable [n_seq][n_head_kv][max_blocks]
+    int32_t n_seq, T, n_head, n_head_kv, G, top_k, max_blocks;
+    int32_t seq_slot[MAX_SEQ];
+    int32_t seq_nblk[MAX_SEQ];    // candidate blocks of each sequence
+};
+cudaError_t launch_select(const SelectParams &p, cudaStream_t st);
+
+// ---- kernel C -----------------------------------------------------------------------------------
+constexpr int MAX_PAIRS = MAX_SEQ * 8;
+struct DecodeParams {
+    const uint8_t *pool;
+    const int32_t *block_table;   // [n_slots][max_pages]
+    const float   *Q;             // [n_seq][T][n_head][HD]
+    float         *out;           // [n_seq][T][n_head][HD]
+    float         *partial;       // scratch: [2*n_ctas][nq*HD + 2*nq]
+    const int32_t *sel;           // nullable [n_seq][n_head_kv][n_sel] block ids
+    int32_t       *status;
+    int64_t page_bytes;
+    int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_ctas, n_pairs, total_tiles;
+    float   scale;
+    int32_t seq_slot[MAX_SEQ];
+    int32_t seq_pos0[MAX_SEQ];
+    int32_t pair_tile0[MAX_PAIRS + 1];   // prefix of tiles over pairs (pair = seq*n_head_kv + head)
+};
+// partial record size in floats for nq query rows
+__host__ __device__ __forceinline__ int64_t partial_stride(int nq) { return (int64_t)nq * HD + 2 * nq; }
+
+cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);
+int decode_max_nq();
+
+}  // namespace qkv

@@ -1,0 +1,304 @@
+// qkv_kernels.cu -- kernel A (q8_0 append), the ggml-layout transforms (read / gather / write
+// rows), kernel E (batched device copies) and kernel B (block summaries, block selection).
+//
+// All of these move or reshape bytes; none is compute bound.  They are written for the HBM:
+// 16-byte vector accesses where the layout allows, grids sized from the SM count.
+#include "qkv_internal.h"
+
+#include <cuda_fp16.h>
+
+namespace qkv {
+
+__device__ __forceinline__ uint8_t *tile_ptr(const PoolRef &pr, int32_t pos, int h) {
+    if (pos < 0 || (pos >> 8) >= pr.max_pages) return nullptr;
+    const int32_t page = pr.bt[pos >> 8];
+    if (page < 0 || page >= pr.n_pages) return nullptr;
+    return pr.pool + (int64_t)page * pr.page_bytes + (int64_t)(h * TILES_PER_PAGE + ((pos >> 6) & 3)) * TILE_BYTES;
+}
+
+// ------------------------------------------------------------------------------------ kernel A
+// q8_0 quantisation, restating ggml's quantize_row_q8_0 (and its CUDA set_rows/cpy twin):
+// d = amax / 127 (IEEE division), id = d ? 1/d : 0 (IEEE reciprocal), q = roundf(x * id)
+// (half away from zero), d stored as fp16 with round-to-nearest-even.  One warp per 32-element
+// block: lane j owns element j.
+__device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t &q, __half &dh) {
+    float amax = fabsf(x);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d  = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    q  = (int8_t)(int)roundf(__fmul_rn(x, id));
+    dh = __float2half_rn(d);
+    (void)lane;
+}
+
+__global__ void __launch_bounds__(256) k_append(PoolRef pr, int32_t pos, const float *__restrict__ K,
+                                                const float *__restrict__ V, int32_t n_rows) {
+    const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    const int per_row = pr.n_head_kv * NBLK;
+    if (warp >= n_rows * per_row) return;
+    const int r = warp / per_row, hb = warp % per_row, h = hb / NBLK, b = hb % NBLK;
+    const int32_t p = pos + r;
+    uint8_t *tile = tile_ptr(pr, p, h);
+    if (!tile) {
+        if (lane == 0) atomicOr(pr.status, ST_BAD_PAGE);
+        return;
+    }
+    const int t = p & 63, dim = b * QK + lane;
+    const int64_t src = (int64_t)r * pr.n_head_kv * HD + h * HD + dim;
+    int8_t q;
+    __half dh;
+    quant_block_warp(K[src], lane, q, dh);
+    tile[k_off(t, dim)] = (uint8_t)q;
+    if (lane == 0) *reinterpret_cast<__half *>(tile + kd_off(t, b)) = dh;
+    quant_block_warp(V[src], lane, q, dh);
+    tile[v_off(dim, t)] = (uint8_t)q;
+    if (lane == 0) *reinterpret_cast<__half *>(tile + vd_off(b, t)) = dh;
+}
+
+cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const float *V, int32_t n_rows,
+                          cudaStream_t st) {
+    const int64_t warps = (int64_t)n_rows * pr.n_head_kv * NBLK;
+    const int blocks = (int)((warps * 32 + 255) / 256);
+    k_append<<<blocks, 256, 0, st>>>(pr, pos, K, V, n_rows);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+// --------------------------------------------------------------------- ggml-layout transforms
+// One warp per (row, head, block): 32 quants + the fp16 scale, moved between the page layout
+// and ggml's block_q8_0 rows {fp16 d, int8 qs[32]} (34 bytes, head h at h*272 in a row).
+__global__ void __launch_bounds__(256) k_read_rows(PoolRef pr, const int32_t *__restrict__ cells, int32_t pos,
+                                                   int32_t n, uint8_t *__restrict__ K_out,
+                                                   uint8_t *__restrict__ V_out) {
+    const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    const int per_row = pr.n_head_kv * NBLK;
+    if (warp >= n * per_row) return;
+    const int r = warp / per_row, hb = warp % per_row, h = hb / NBLK, b = hb % NBLK;
+    const int32_t p = cells ? cells[r] : pos + r;
+    const int64_t row_bytes = (int64_t)pr.n_head_kv * ROW_Q8;
+    uint8_t *ko = K_out + r * row_bytes + h * ROW_Q8 + b * 34;
+    uint8_t *vo = V_out + r * row_bytes + h * ROW_Q8 + b * 34;
+    const uint8_t *tile = p >= 0 ? tile_ptr(pr, p, h) : nullptr;
+    if (!tile) {
+        if (lane == 0) atomicOr(pr.status, p >= 0 ? ST_BAD_PAGE : ST_BAD_INDEX);
+        return;
+    }
+    const int t = p & 63, dim = b * QK + lane;
+    ko[2 + lane] = tile[k_off(t, dim)];
+    vo[2 + lane] = tile[v_off(dim, t)];
+    if (lane < 2) {
+        ko[lane] = tile[kd_off(t, b) + lane];
+        vo[lane] = tile[vd_off(b, t) + lane];
+    }
+}
+
+__global__ void __launch_bounds__(256) k_write_rows(PoolRef pr, int32_t pos, int32_t n, const uint8_t *__restrict__ K_in,
+                                                    const uint8_t *__restrict__ V_in) {
+    const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    const int per_row = pr.n_head_kv * NBLK;
+    if (warp >= n * per_row) return;
+    const int r = warp / per_row, hb = warp % per_row, h = hb / NBLK, b = hb % NBLK;
+    const int32_t p = pos + r;
+    const int64_t row_bytes = (int64_t)pr.n_head_kv * ROW_Q8;
+    const uint8_t *ki = K_in + r * row_bytes + h * ROW_Q8 + b * 34;
+    const uint8_t *vi = V_in + r * row_bytes + h * ROW_Q8 + b * 34;
+    uint8_t *tile = tile_ptr(pr, p, h);
+    if (!tile) {
+        if (lane == 0) atomicOr(pr.status, ST_BAD_PAGE);
+        return;
+    }
+    const int t = p & 63, dim = b * QK + lane;
+    tile[k_off(t, dim)] = ki[2 + lane];
+    tile[v_off(dim, t)] = vi[2 + lane];
+    if (lane < 2) {
+        tile[kd_off(t, b) + lane] = ki[lane];
+        tile[vd_off(b, t) + lane] = vi[lane];
+    }
+}
+
+cudaError_t launch_read_rows(const PoolRef &pr, const int32_t *cells, int32_t pos, int32_t n, uint8_t *K_out,
+                             uint8_t *V_out, cudaStream_t st) {
+    const int64_t warps = (int64_t)n * pr.n_head_kv * NBLK;
+    k_read_rows<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(pr, cells, pos, n, K_out, V_out);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_write_rows(const PoolRef &pr, int32_t pos, int32_t n, const uint8_t *K_in, const uint8_t *V_in,
+                              cudaStream_t st) {
+    const int64_t warps = (int64_t)n * pr.n_head_kv * NBLK;
+    k_write_rows<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(pr, pos, n, K_in, V_in);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------ kernel E
+// Batched copies (snapshot restore, copy-on-write of shared pages, rollback).  The descriptors
+// travel by value; every copy is cut into 64 KiB chunks that a grid sized to the SM count
+// walks with 16-byte loads and stores.  (One launch instead of one cudaMemcpyAsync per slot.)
+struct CopyBatch {
+    int32_t  n;
+    int64_t  chunk0[COPY_MAX + 1];
+    CopyDesc d[COPY_MAX];
+};
+constexpr int64_t COPY_CHUNK = 65536;
+
+__global__ void __launch_bounds__(512) k_copy_batch(const CopyBatch cb) {
+    const int64_t total = cb.chunk0[cb.n];
+    for (int64_t c = blockIdx.x; c < total; c += gridDim.x) {
+        int i = 0;
+        while (cb.chunk0[i + 1] <= c) i++;
+        const int64_t off   = (c - cb.chunk0[i]) * COPY_CHUNK;
+        const int64_t bytes = min(COPY_CHUNK, cb.d[i].bytes - off);
+        const uint4 *s = reinterpret_cast<const uint4 *>(cb.d[i].src + off);
+        uint4 *d       = reinterpret_cast<uint4 *>(cb.d[i].dst + off);
+        const int64_t n16 = bytes >> 4;
+        for (int64_t k = threadIdx.x; k < n16; k += blockDim.x) d[k] = __ldcs(s + k);
+    }
+}
+
+cudaError_t launch_copy_batch(const CopyDesc *descs, int n, int num_sms, cudaStream_t st) {
+    for (int base = 0; base < n; base += COPY_MAX) {
+        CopyBatch cb;
+        cb.n = n - base < COPY_MAX ? n - base : COPY_MAX;
+        cb.chunk0[0] = 0;
+        for (int i = 0; i < cb.n; i++) {
+            cb.d[i] = descs[base + i];
+            cb.chunk0[i + 1] = cb.chunk0[i] + (cb.d[i].bytes + COPY_CHUNK - 1) / COPY_CHUNK;
+        }
+        if (cb.chunk0[cb.n] == 0) continue;
+        int64_t grid = cb.chunk0[cb.n];
+        const int64_t cap = (int64_t)num_sms * 4;
+        if (grid > cap) grid = cap;
+        k_copy_batch<<<(int)grid, 512, 0, st>>>(cb);
+        count_launches(1);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// ------------------------------------------------------------------------------------ kernel B0
+// Block summary: summary[h][b][i] = fp16((sum_{t<64} d_t * q_t,i) * (1/64)), the sum in fp32 in
+// token order (each d*q is exact in fp32).  One CTA of 256 threads per (block, head), thread i
+// owns element i.
+__global__ void __launch_bounds__(256) k_block_summary(PoolRef pr, int32_t b0, uint16_t *__restrict__ summary,
+                                                       int32_t max_blocks) {
+    const int b = b0 + blockIdx.x, h = blockIdx.y, i = threadIdx.x;
+    const uint8_t *tile = tile_ptr(pr, b * TILE_TOK, h);
+    if (!tile) {
+        if (i == 0) atomicOr(pr.status, ST_BAD_PAGE);
+        return;
+    }
+    float acc = 0.0f;
+    for (int t = 0; t < TILE_TOK; t++) {
+        const float d = __half2float(*reinterpret_cast<const __half *>(tile + kd_off(t, i >> 5)));
+        const float q = (float)(int8_t)tile[k_off(t, i)];
+        acc = __fadd_rn(acc, __fmul_rn(d, q));
+    }
+    const __half s = __float2half_rn(__fmul_rn(acc, 1.0f / (float)TILE_TOK));
+    summary[((int64_t)h * max_blocks + b) * HD + i] = __half_as_ushort(s);
+}
+
+cudaError_t launch_block_summary(const PoolRef &pr, int32_t b0, int32_t b1, uint16_t *summary, int32_t max_blocks,
+                                 cudaStream_t st) {
+    if (b1 <= b0) return cudaSuccess;
+    dim3 grid(b1 - b0, pr.n_head_kv);
+    k_block_summary<<<grid, 256, 0, st>>>(pr, b0, summary, max_blocks);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------ kernel B1
+// Block scores and top-k.  One CTA of 256 threads per (sequence, KV head).  Groups of 8 lanes
+// compute one dot product in the oracle's fixed order: lane l takes dims 32l..32l+31 with
+// sequential fmaf, then a fixed tree over the 8 lanes.  The group's lane 0 sums relu(dot) over
+// the G*T query rows in order (t-major), so the score of every block is bit-exact with the CPU
+// restatement.  Ranking: score descending, block index ascending; a candidate's rank is the
+// number of candidates ahead of it (early exit once >= top_k).
+__global__ void __launch_bounds__(256) k_select(const SelectParams p) {
+    extern __shared__ float sm_sel[];
+    const int s = blockIdx.x, h = blockIdx.y;
+    const int nq = p.T * p.G;
+    float *qs     = sm_sel;                 // [nq][HD]
+    float *scores = sm_sel + nq * HD;       // [max_blocks]
+    const int slot = p.seq_slot[s], nb = p.seq_nblk[s];
+    for (int e = threadIdx.x; e < nq * HD; e += blockDim.x) {
+        const int n = e / HD, i = e % HD, t = n / p.G, j = n % p.G;
+        qs[e] = p.Q[(((int64_t)s * p.T + t) * p.n_head + h * p.G + j) * HD + i];
+    }
+    __syncthreads();
+    // Warp-uniform loop: each warp takes 4 blocks per round (one per 8-lane group); every lane
+    // runs the shuffles, groups past the end or on a forced block discard their result.
+    const int lane8 = threadIdx.x & 7, grp = (threadIdx.x & 31) >> 3;
+    const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    const uint16_t *sum_base = p.summary + ((int64_t)slot * p.n_head_kv + h) * p.max_blocks * HD;
+    for (int bw = warp * 4; bw < nb; bw += nwarp * 4) {
+        const int b = bw + grp;
+        const bool forced = b == 0 || b >= nb - 2;
+        const bool live   = b < nb && !forced;
+        float sv[32];
+        const uint16_t *srow = sum_base + (int64_t)(live ? b : 0) * HD + lane8 * 32;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint4 w = live ? reinterpret_cast<const uint4 *>(srow)[k] : make_uint4(0, 0, 0, 0);
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&w);
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const float2 f = __half22float2(hh[m]);
+                sv[k * 8 + m * 2]     = f.x;
+                sv[k * 8 + m * 2 + 1] = f.y;
+            }
+        }
+        float score = 0.0f;
+        for (int n = 0; n < nq; n++) {
+            const float *q = qs + n * HD + lane8 * 32;
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; k++) acc = __fmaf_rn(q[k], sv[k], acc);
+            // fixed tree: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+            score = __fadd_rn(score, acc > 0.0f ? acc : 0.0f);
+        }
+        if (forced) score = __int_as_float(0x7f800000);
+        if (lane8 == 0 && b < nb) {
+            scores[b] = score;
+            if (p.scores_out) p.scores_out[((int64_t)s * p.n_head_kv + h) * p.max_blocks + b] = score;
+        }
+    }
+    __syncthreads();
+    int32_t *out = p.idx_out + ((int64_t)s * p.n_head_kv + h) * p.top_k;
+    if (nb <= p.top_k) {
+        for (int k = threadIdx.x; k < p.top_k; k += blockDim.x) out[k] = k < nb ? k : -1;
+        return;
+    }
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+        const float si = scores[i];
+        int rank = 0;
+        for (int j = 0; j < nb && rank < p.top_k; j++) {
+            const float sj = scores[j];
+            rank += (sj > si) || (sj == si && j < i);
+        }
+        if (rank < p.top_k) out[rank] = i;
+    }
+}
+
+cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
+    const size_t smem = ((size_t)p.T * p.G * HD + p.max_blocks) * sizeof(float);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid(p.n_seq, p.n_head_kv);
+    k_select<<<grid, 256, smem, st>>>(p);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace qkv

@@ -90,6 +90,11 @@ qkv_status qkv_seq_alloc(qkv_engine *eng, int32_t slot);
 qkv_status qkv_seq_free(qkv_engine *eng, int32_t slot);
 qkv_status qkv_seq_reset(qkv_engine *eng, int32_t slot, void *stream);
 qkv_status qkv_seq_length(const qkv_engine *eng, int32_t slot, int32_t *n_past);
+/* Make positions 0 .. n_tokens-1 of a slot backed by private pages now (allocating, copying
+ * shared pages), so later appends in that range touch no host state; n_past is unchanged.  Lets
+ * a caller capture decode steps in a CUDA graph.  The reference allocates its cache whole at
+ * init (src/qwfn_state.cpp:93-111). */
+qkv_status qkv_seq_reserve(qkv_engine *eng, int32_t slot, int32_t n_tokens, void *stream);
 /* Page ids of a slot's block table (host copy), for inspection and tests. */
 qkv_status qkv_seq_pages(const qkv_engine *eng, int32_t slot, int32_t *pages, int32_t cap, int32_t *n);
 qkv_status qkv_page_refcount(const qkv_engine *eng, int32_t page, int32_t *refcount);
@@ -123,6 +128,16 @@ qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos,
 qkv_status qkv_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
                            int32_t n_seq, const float *Q, int32_t T, float scale,
                            const int32_t *sel_blocks, int32_t n_sel, float *out, void *stream);
+
+/* Kernel A fused into kernel C: append the T new K/V rows of each sequence at pos0[i] (device F32
+ * [n_seq][T][n_head_kv*head_dim]; bit-exact q8_0 as qkv_append) and run the dense decode of
+ * qkv_attn_decode over cells 0..pos0[i]+t, in one launch.  Same position rules as qkv_append
+ * (pos0[i] <= n_past; n_past becomes max(n_past, pos0[i]+T)); each slot at most once.  This is
+ * the reference's set_rows + flash_attn_ext pair of one decode graph (src/qwfn_graph.cpp:612-628,
+ * 697-699) as a single kernel. */
+qkv_status qkv_append_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                  int32_t n_seq, const float *K, const float *V, const float *Q, int32_t T,
+                                  float scale, float *out, void *stream);
 
 /* ------------------------------------------------------------------ kernel B -------------- */
 

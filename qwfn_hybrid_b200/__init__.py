@@ -21,8 +21,8 @@ OK, ERR_INVALID, ERR_NO_MEMORY, ERR_CUDA, ERR_STATE, ERR_MISMATCH, ERR_DEVICE, E
 # Every symbol include/qkv.h declares (checked by tests/test_abi.py).
 EXPORTS = [
     "qkv_create", "qkv_destroy", "qkv_last_error", "qkv_status_string", "qkv_bytes", "qkv_summary",
-    "qkv_seq_alloc", "qkv_seq_free", "qkv_seq_reset", "qkv_seq_length", "qkv_seq_pages", "qkv_page_refcount",
-    "qkv_pages_free", "qkv_append", "qkv_attn_decode", "qkv_block_summary", "qkv_select_blocks",
+    "qkv_seq_alloc", "qkv_seq_free", "qkv_seq_reset", "qkv_seq_length", "qkv_seq_reserve", "qkv_seq_pages", "qkv_page_refcount",
+    "qkv_pages_free", "qkv_append", "qkv_attn_decode", "qkv_append_attn_decode", "qkv_block_summary", "qkv_select_blocks",
     "qkv_gather_rows", "qkv_read_rows", "qkv_write_rows", "qkv_attn_prefill", "qkv_snapshot_save",
     "qkv_snapshot_restore", "qkv_snapshot_restore_many", "qkv_snapshot_release", "qkv_snapshot_info",
     "qkv_snapshot_to_host", "qkv_snapshot_from_host", "qkv_rollback", "qkv_rollback_arm", "qkv_state_ptr",
@@ -68,9 +68,11 @@ def lib() -> ctypes.CDLL:
         "qkv_bytes": [P, ctypes.POINTER(SZ)], "qkv_summary": [P, ctypes.c_char_p, SZ],
         "qkv_seq_alloc": [P, I32], "qkv_seq_free": [P, I32], "qkv_seq_reset": [P, I32, P],
         "qkv_seq_length": [P, I32, pI32], "qkv_seq_pages": [P, I32, pI32, I32, pI32],
+        "qkv_seq_reserve": [P, I32, I32, P],
         "qkv_page_refcount": [P, I32, pI32], "qkv_pages_free": [P, pI32],
         "qkv_append": [P, I32, I32, I32, P, P, I32, P],
         "qkv_attn_decode": [P, I32, pI32, pI32, I32, P, I32, F32, P, I32, P, P],
+        "qkv_append_attn_decode": [P, I32, pI32, pI32, I32, P, P, P, I32, F32, P, P],
         "qkv_block_summary": [P, I32, I32, I32, I32, P],
         "qkv_select_blocks": [P, I32, pI32, pI32, I32, P, I32, I32, P, P, P],
         "qkv_gather_rows": [P, I32, I32, P, I32, P, P, P],
@@ -234,6 +236,9 @@ class Engine:
         self._check(lib().qkv_seq_length(self.handle, slot, ctypes.byref(n)))
         return n.value
 
+    def reserve(self, slot: int, n_tokens: int, stream=None) -> None:
+        self._check(lib().qkv_seq_reserve(self.handle, slot, n_tokens, _stream(stream) if self.device >= 0 else None))
+
     def pages(self, slot: int) -> list[int]:
         n = ctypes.c_int32()
         self._check(lib().qkv_seq_pages(self.handle, slot, None, 0, ctypes.byref(n)))
@@ -280,6 +285,11 @@ class Engine:
         n = len(slots)
         self._check(lib().qkv_attn_decode(self.handle, layer, _i32_array(slots), _i32_array(pos0), n, _ptr(Q), T,
                                           scale, _ptr(sel), n_sel, _ptr(out), _stream(stream)))
+
+    def append_attn_decode(self, layer: int, slots, pos0, K, V, Q, T: int, scale: float, out, stream=None) -> None:
+        """Fused kernel A + C: append T rows per sequence at pos0 and attend (one launch)."""
+        self._check(lib().qkv_append_attn_decode(self.handle, layer, _i32_array(slots), _i32_array(pos0), len(slots),
+                                                 _ptr(K), _ptr(V), _ptr(Q), T, scale, _ptr(out), _stream(stream)))
 
     def block_summary(self, layer: int, slot: int, b0: int, b1: int, stream=None) -> None:
         self._check(lib().qkv_block_summary(self.handle, layer, slot, b0, b1, _stream(stream)))

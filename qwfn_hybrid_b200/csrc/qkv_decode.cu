@@ -1,270 +1,641 @@
 // qkv_decode.cu -- kernel C: split-K decode / MTP-verify attention over the paged q8_0 cache.
 //
-// Work plan (host-built, passed by value): pair = (sequence, KV head); each pair owns a run of
-// 64-token tiles (dense: tiles 0..ceil(n_kv/64)-1; sparse: the selected block ids).  The runs of
-// all pairs are laid end to end and cut into n_ctas equal ranges, one per CTA, so ragged
-// batches balance by tiles rather than by sequences.  A CTA whose range holds a pair whole
-// writes that pair's output; a pair cut by range boundaries leaves one partial (m, l, acc) per
-// CTA and a combine kernel merges them in CTA order (deterministic, no atomics, no waits).
+// Work plan (host-built, passed by value).  A pair is (sequence, KV head); its tiles are the
+// 64-token tiles of the sequence (dense) or the selected block ids (sparse).  Each pair is cut
+// into `units` contiguous tile ranges in proportion to its length, and every CTA runs exactly one
+// unit, so a ragged batch balances by tiles.  CTAs are launched as clusters of CN; a unit's
+// result (running max m, row sum l, unnormalised O) stays in shared memory and the units of a
+// pair inside one cluster are merged through distributed shared memory.  A pair spread over
+// several clusters leaves one partial per cluster in global memory and the cluster that arrives
+// last (a per-pair atomic counter, no waiting) merges them.  One launch per call, no combine
+// kernel; the merge order is fixed, so results do not depend on which cluster finishes last.
 //
-// Per pair, the G*T query rows of the KV head's group are quantised to q8_0 exactly as ggml's
+// Per unit, the G*T query rows of the KV head's group are quantised to q8_0 exactly as ggml's
 // CPU flash_attn_ext quantises its query row, so every QK value is sum_b isum_b * (d_k * d_q)
 // with an exact integer block dot.
+//
+// CTA = 4 warps, 2 CTAs per SM.  Tiles (34816 B: K quants, V quants transposed, scales) stream
+// into a 2-stage shared-memory ring with 1-D bulk copies (cp.async.bulk, the TMA engine; no
+// multicast) completing on mbarriers.  Per tile:
+//   QK  warp w: its 16 tokens x all query rows.  mma.m16n8k32 s8 per q8_0 block, A = K rows
+//       (token order permuted by pi16() so that a movmatrix transpose of P lands in the PV B
+//       layout), B = quantised Q.  The accumulator input is 0x4B400000 so the int32 dot d comes
+//       out as the float 12582912 + d; one packed subtract recovers d exactly, then
+//       S += d * (dq * dk) with packed f32x2 arithmetic.
+//   softmax: tile max across the 4 warps via shared memory, exp2, P -> f16 -> movmatrix -> smem.
+//   PV  warp w: its 64 dims x all query rows over the 64 tokens.  mma.m16n8k16 f16 with
+//       A = V^T int8 widened to f16 exactly (byte permute + bias subtract) and B = P * dv.
+// Optional fused append (dense only): the unit owning a tile that holds one of the T new
+// positions quantises those rows (kernel A's rounding), stores them in the cache and patches its
+// shared-memory copy of the tile before use.
 #include "qkv_internal.h"
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
-namespace qkv {
+namespace cg = cooperative_groups;
 
-__device__ __forceinline__ int find_pair(const DecodeParams &P, int64_t x) {
-    int lo = 0, hi = P.n_pairs - 1;
+namespace qkv {
+namespace dec {
+
+constexpr int CN = 8;   // CTAs per cluster
+constexpr int NSTAGE = 2;
+constexpr int PSTR   = 80;      // halves per P row in smem (64 tokens + pad: conflict-free LDS.64)
+constexpr int QSTR   = 288;     // bytes per quantised query row (256 + pad)
+constexpr uint32_t MAGIC_I = 0x4B400000u;
+constexpr float    MAGIC_F = 12582912.0f;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up after limit_ns (a copy that never lands) instead of spinning forever.
+__device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, phase)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, phase)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1, uint32_t c) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+// int8 x4 (two's complement) -> two f16x2 holding the exact values: bytes 0,1 -> lo, 2,3 -> hi.
+__device__ __forceinline__ void s8x4_to_f16(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t u = w ^ 0x80808080u;                  // x + 128 as unsigned bytes
+    const uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);  // f16 1024 + u (exact)
+    const uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), bias);
+    __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), bias);
+    lo = *reinterpret_cast<uint32_t *>(&ha);
+    hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+// Row order of the 16 K rows of a QK mma: A row m holds token pi(m) of the warp's 16 tokens, so
+// after movmatrix a thread's P pairs are the consecutive tokens 4*tig .. 4*tig+3 that the PV
+// A fragment (one int8x4 word of V^T) covers.
+__device__ __forceinline__ int pi16(int m) { return ((m & 6) << 1) | (m & 1) | ((m & 8) >> 2); }
+// Byte position of element e (0..31) of a quantised query block in the fragment order
+// [tig][b0 word, b1 word]: one LDS.64 fetches both B registers of an m16n8k32 B fragment.
+__device__ __forceinline__ int qperm(int e) { return ((e & 15) >> 2) * 8 + ((e >> 4) << 2) + (e & 3); }
+
+
+template <int NT>
+struct Smem {
+    static constexpr int NQ = NT * 8;
+    uint8_t  tile[NSTAGE][TILE_BYTES];   // after the tile loop: the unit's O rows [NQ][HD] fp32
+    uint8_t  qq[NQ * QSTR];
+    float    qd[NBLK * NQ];
+    float    red[4 * NQ];
+    float    lred[4 * NQ];
+    float    ml[2 * NQ];                 // the unit's m (natural log domain) and l per row
+    __half   ps[NQ * PSTR];
+    uint64_t full[NSTAGE];
+    int32_t  merge_flag;
+};
+
+struct Unit {
+    int s, h, p;          // sequence, KV head, pair = s * n_head_kv + h
+    int t0, t1;           // tile range of the pair this unit runs
+    int pu0, pu1;         // unit range of the pair
+};
+
+__device__ __forceinline__ Unit unit_of(const DecodeParams &P, int u) {
+    int lo = 0, hi = P.n_seq - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (P.pair_tile0[mid] <= x) lo = mid; else hi = mid - 1;
+        if (P.seq_unit0[mid] <= u) lo = mid; else hi = mid - 1;
     }
-    return lo;
-}
-__host__ __device__ __forceinline__ int64_t cta_begin(int64_t c, int64_t total, int64_t n_ctas) {
-    return c * total / n_ctas;
-}
-__host__ __device__ __forceinline__ int cta_of(int64_t x, int64_t total, int64_t n_ctas) {
-    return (int)(((x + 1) * n_ctas - 1) / total);
-}
-
-__device__ __forceinline__ void quant_block(float x, int8_t &q, __half &dh) {
-    float amax = fabsf(x);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d  = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-    q  = (int8_t)(int)roundf(__fmul_rn(x, id));
-    dh = __float2half_rn(d);
+    Unit x;
+    x.s = lo;
+    const int per = P.seq_units[lo], tiles = P.seq_tiles[lo];
+    const int off = u - P.seq_unit0[lo];
+    x.h = off / per;
+    const int r = off % per;
+    x.p = lo * P.n_head_kv + x.h;
+    x.t0 = (int)((int64_t)tiles * r / per);
+    x.t1 = (int)((int64_t)tiles * (r + 1) / per);
+    x.pu0 = P.seq_unit0[lo] + x.h * per;
+    x.pu1 = x.pu0 + per;
+    return x;
 }
 
-// Quantise the pair's query rows into shared memory: qq[n][256] int8, qd[n][8] fp32 (the fp16
-// scale widened).  Rows n >= nq are zero.  Called by all threads of the CTA (warp per block).
-template <int NQ>
-__device__ __forceinline__ void load_query(const DecodeParams &P, int s, int h, int8_t *qq, float *qd) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
-    for (int blk = warp; blk < NQ * NBLK; blk += nwarp) {
-        const int n = blk / NBLK, b = blk % NBLK;
-        float xv = 0.0f;
-        if (n < P.nq) {
-            const int t = n / P.G, j = n % P.G;
-            xv = P.Q[(((int64_t)s * P.T + t) * P.n_head + h * P.G + j) * HD + b * QK + lane];
-        }
-        int8_t q;
-        __half dh;
-        quant_block(xv, q, dh);
-        qq[n * HD + b * QK + lane] = q;
-        if (lane == 0) qd[n * NBLK + b] = __half2float(dh);
+struct TileRef {
+    int32_t  blk;   // block id (64-token tile of the sequence); -1 skip, -2 bad index, -3 bad page
+    uint8_t *src;   // global tile address
+};
+
+__device__ __forceinline__ TileRef tile_ref(const DecodeParams &P, const Unit &U, int k) {
+    TileRef r{-1, nullptr};
+    const int blkid = P.sel ? P.sel[((int64_t)U.s * P.n_head_kv + U.h) * P.n_sel + k] : k;
+    if (blkid < 0) return r;
+    const int n_kv = P.seq_pos0[U.s] + P.T;
+    if (blkid >= (n_kv + TILE_TOK - 1) / TILE_TOK) {
+        r.blk = -2;
+        return r;
+    }
+    const int32_t page = P.block_table[(int64_t)P.seq_slot[U.s] * P.max_pages + (blkid >> 2)];
+    if (page < 0 || page >= P.n_pages) {
+        r.blk = -3;
+        return r;
+    }
+    r.blk = blkid;
+    r.src = const_cast<uint8_t *>(P.pool) + (int64_t)page * P.page_bytes +
+            (int64_t)(U.h * TILES_PER_PAGE + (blkid & 3)) * TILE_BYTES;
+    return r;
+}
+
+// Producer (one thread): start the copy of the unit's i-th tile into stage i % NSTAGE.
+template <int NT>
+__device__ __forceinline__ void issue_tile(const DecodeParams &P, Smem<NT> &sm, const Unit &U, int i) {
+    const TileRef r = tile_ref(P, U, U.t0 + i);
+    uint64_t *bar = &sm.full[i % NSTAGE];
+    if (r.blk >= 0) {
+        fence_proxy_async();
+        mbar_expect_tx(bar, TILE_BYTES);
+        bulk_load(sm.tile[i % NSTAGE], r.src, TILE_BYTES, bar);
+    } else {
+        if (r.blk < -1) atomicOr(P.status, r.blk == -2 ? ST_BAD_INDEX : ST_BAD_PAGE);
+        mbar_arrive(bar);
     }
 }
 
-// ------------------------------------------------------------------------------ CUDA-core path
-template <int NQ>
-__global__ void __launch_bounds__(128) k_decode_simple(const DecodeParams P) {
-    extern __shared__ __align__(16) uint8_t sm[];
-    uint8_t *tile = sm;
-    int8_t *qq    = reinterpret_cast<int8_t *>(sm + TILE_BYTES);
-    float *qd     = reinterpret_cast<float *>(qq + NQ * HD);
-    float *S      = qd + NQ * NBLK;     // [NQ][64]
-    float *alpha  = S + NQ * TILE_TOK;  // [NQ]
-    float *mrow   = alpha + NQ;
-    float *lrow   = mrow + NQ;
-    const int tid = threadIdx.x;
-    const int c   = blockIdx.x;
-    const int64_t a   = cta_begin(c, P.total_tiles, P.n_ctas);
-    const int64_t bnd = cta_begin(c + 1, P.total_tiles, P.n_ctas);
-    if (a >= bnd) return;
-    int p = find_pair(P, a);
-    const int p_first = p;
-    const int d0 = tid * 2, vb = d0 / QK;
-    for (int64_t x = a; x < bnd; p++) {
-        const int64_t ps = P.pair_tile0[p], pe = P.pair_tile0[p + 1];
-        if (pe <= x) continue;
-        const int64_t xe = pe < bnd ? pe : bnd;
-        const int s = p / P.n_head_kv, h = p % P.n_head_kv;
-        const int slot = P.seq_slot[s], pos0 = P.seq_pos0[s];
-        const int n_kv = pos0 + P.T;
-        const int32_t *bt = P.block_table + (int64_t)slot * P.max_pages;
-        load_query<NQ>(P, s, h, qq, qd);
-        if (tid < NQ) {
-            mrow[tid] = -INFINITY;
-            lrow[tid] = 0.0f;
+// Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h, store
+// them in the cache tile in global memory and in the shared-memory copy.  Warp per 32-element
+// block; the rounding is kernel A's.
+__device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &U, uint8_t *gtile, uint8_t *stile,
+                                             int cell0) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int pos0 = P.seq_pos0[U.s];
+    const int r0 = max(pos0, cell0), r1 = min(pos0 + P.T, cell0 + TILE_TOK);
+    const int work = (r1 - r0) * NBLK * 2;
+    for (int wi = warp; wi < work; wi += 4) {
+        const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
+        const float *src = (kv ? P.Vnew : P.Knew) +
+                           (((int64_t)U.s * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK;
+        const float x = src[lane];
+        float amax = fabsf(x);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d  = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+        const uint8_t q = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x, id));
+        const __half dh = __float2half_rn(d);
+        const int t = row - cell0, dim = b * QK + lane;
+        const int qo = kv ? v_off(dim, t) : k_off(t, dim);
+        const int so = kv ? vd_off(b, t) : kd_off(t, b);
+        stile[qo] = q;
+        gtile[qo] = q;
+        if (lane == 0) {
+            *reinterpret_cast<__half *>(stile + so) = dh;
+            *reinterpret_cast<__half *>(gtile + so) = dh;
         }
-        float acc[NQ][2];
+    }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
+    constexpr int NQ = NT * 8;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem<NT> &sm = *reinterpret_cast<Smem<NT> *>(smem_raw);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, tig = lane & 3;
+    const int u = blockIdx.x;
+    const int k = u / CN;   // cluster index
+    const bool has_unit = u < P.n_units;
+    Unit U{};
+    int n_tiles = 0;
+    if (has_unit) {
+        U = unit_of(P, u);
+        n_tiles = U.t1 - U.t0;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < NSTAGE; s++) mbar_init(&sm.full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < NSTAGE && i < n_tiles; i++) issue_tile<NT>(P, sm, U, i);
+    }
+    float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
+    const float c2 = P.scale * 1.4426950408889634f;        // softmax in base 2
+    bool aborted = false;   // warp-uniform: a tile copy did not land within the wait limit
+
+    if (has_unit) {
+        const int s = U.s, h = U.h, pos0 = P.seq_pos0[s];
+        // ---- quantise the pair's query rows (q8_0, as ggml's CPU path does) -------------------
+        for (int gid = tid; gid < NQ * 32; gid += 128) {
+            const int n = gid >> 5, e8 = gid & 31, b = e8 >> 2, sub = e8 & 3;
+            float v[8];
+            if (n < P.nq) {
+                const int t = n / P.G, jj = n % P.G;
+                const float4 *src = reinterpret_cast<const float4 *>(
+                    P.Q + (((int64_t)s * P.T + t) * P.n_head + h * P.G + jj) * HD + b * QK + sub * 8);
+                const float4 u0 = src[0], u1 = src[1];
+                v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+                v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+            } else {
 #pragma unroll
-        for (int n = 0; n < NQ; n++) acc[n][0] = acc[n][1] = 0.0f;
-        __syncthreads();
-        for (int64_t k = x - ps; k < xe - ps; k++) {
-            const int blkid = P.sel ? P.sel[((int64_t)s * P.n_head_kv + h) * P.n_sel + k] : (int)k;
-            if (blkid < 0) continue;
-            const bool in_seq = blkid < (n_kv + TILE_TOK - 1) / TILE_TOK;
-            const int32_t page = in_seq ? bt[blkid >> 2] : -1;
-            if (page < 0 || page >= P.n_pages) {
-                if (tid == 0) atomicOr(P.status, in_seq ? ST_BAD_PAGE : ST_BAD_INDEX);
-                continue;
+                for (int q = 0; q < 8; q++) v[q] = 0.0f;
             }
-            const uint4 *g = reinterpret_cast<const uint4 *>(
-                P.pool + (int64_t)page * P.page_bytes + (int64_t)(h * TILES_PER_PAGE + (blkid & 3)) * TILE_BYTES);
-            for (int i = tid; i < TILE_BYTES / 16; i += blockDim.x) reinterpret_cast<uint4 *>(tile)[i] = g[i];
-            __syncthreads();
-            for (int e = tid; e < NQ * TILE_TOK; e += blockDim.x) {
-                const int n = e / TILE_TOK, tok = e % TILE_TOK;
-                const int cell = blkid * TILE_TOK + tok;
-                float sc = -INFINITY;
-                if (n < P.nq && cell <= pos0 + n / P.G) {
-                    float sumf = 0.0f;
+            float amax = 0.0f;
 #pragma unroll
-                    for (int b = 0; b < NBLK; b++) {
-                        const int4 k0 = *reinterpret_cast<const int4 *>(tile + tok * HD + (((2 * b) ^ kswz(tok)) << 4));
-                        const int4 k1 = *reinterpret_cast<const int4 *>(tile + tok * HD + (((2 * b + 1) ^ kswz(tok)) << 4));
-                        const int4 q0 = *reinterpret_cast<const int4 *>(qq + n * HD + b * QK);
-                        const int4 q1 = *reinterpret_cast<const int4 *>(qq + n * HD + b * QK + 16);
-                        int isum = 0;
-                        isum = __dp4a(k0.x, q0.x, isum);
-                        isum = __dp4a(k0.y, q0.y, isum);
-                        isum = __dp4a(k0.z, q0.z, isum);
-                        isum = __dp4a(k0.w, q0.w, isum);
-                        isum = __dp4a(k1.x, q1.x, isum);
-                        isum = __dp4a(k1.y, q1.y, isum);
-                        isum = __dp4a(k1.z, q1.z, isum);
-                        isum = __dp4a(k1.w, q1.w, isum);
-                        const float dk = __half2float(*reinterpret_cast<const __half *>(tile + kd_off(tok, b)));
-                        sumf = __fadd_rn(sumf, __fmul_rn((float)isum, __fmul_rn(dk, qd[n * NBLK + b])));
-                    }
-                    sc = __fmul_rn(sumf, P.scale);
-                }
-                S[e] = sc;
-            }
-            __syncthreads();
-            if (tid < NQ) {
-                float *row = S + tid * TILE_TOK;
-                float mt = -INFINITY;
-                for (int tok = 0; tok < TILE_TOK; tok++) mt = fmaxf(mt, row[tok]);
-                const float mold = mrow[tid], mnew = fmaxf(mold, mt);
-                float al = 1.0f, ls = 0.0f;
-                if (mnew == -INFINITY) {
-                    for (int tok = 0; tok < TILE_TOK; tok++) row[tok] = 0.0f;
-                } else {
-                    al = expf(mold - mnew);
-                    for (int tok = 0; tok < TILE_TOK; tok++) {
-                        const float pv = expf(row[tok] - mnew);
-                        row[tok] = pv;
-                        ls += pv;
-                    }
-                }
-                alpha[tid] = al;
-                mrow[tid]  = mnew;
-                lrow[tid]  = lrow[tid] * al + ls;
-            }
-            __syncthreads();
+            for (int q = 0; q < 8; q++) amax = fmaxf(amax, fabsf(v[q]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float d  = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+            uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-            for (int n = 0; n < NQ; n++) {
-                acc[n][0] *= alpha[n];
-                acc[n][1] *= alpha[n];
+            for (int q = 0; q < 4; q++) {
+                w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[q], id)) << (8 * q);
+                w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[4 + q], id)) << (8 * q);
             }
-            for (int tok = 0; tok < TILE_TOK; tok++) {
-                const float dv = __half2float(*reinterpret_cast<const __half *>(tile + vd_off(vb, tok)));
-                const float v0 = dv * (float)(int8_t)tile[v_off(d0, tok)];
-                const float v1 = dv * (float)(int8_t)tile[v_off(d0 + 1, tok)];
-#pragma unroll
-                for (int n = 0; n < NQ; n++) {
-                    const float pv = S[n * TILE_TOK + tok];
-                    acc[n][0] = fmaf(pv, v0, acc[n][0]);
-                    acc[n][1] = fmaf(pv, v1, acc[n][1]);
-                }
-            }
-            __syncthreads();
+            uint8_t *row = sm.qq + n * QSTR + b * 32;
+            *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
+            *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
+            if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
         }
-        if (x == ps && xe == pe) {
+        // last visible position of each of this lane's query rows (padding rows: nothing visible)
+        int qlim[NT][2];
 #pragma unroll
-            for (int n = 0; n < NQ; n++) {
-                if (n >= P.nq) break;
-                const float l = lrow[n], inv = l == 0.0f ? 0.0f : 1.0f / l;
-                const int t = n / P.G, j = n % P.G;
-                float *o = P.out + (((int64_t)s * P.T + t) * P.n_head + h * P.G + j) * HD + d0;
-                *reinterpret_cast<float2 *>(o) = make_float2(acc[n][0] * inv, acc[n][1] * inv);
-            }
-        } else {
-            const int pslot = 2 * c + (p == p_first ? 0 : 1);
-            float *rec = P.partial + pslot * partial_stride(P.nq);
+        for (int j = 0; j < NT; j++)
 #pragma unroll
-            for (int n = 0; n < NQ; n++) {
-                if (n >= P.nq) break;
-                *reinterpret_cast<float2 *>(rec + n * HD + d0) = make_float2(acc[n][0], acc[n][1]);
+            for (int e = 0; e < 2; e++) {
+                const int n = 8 * j + 2 * tig + e;
+                qlim[j][e] = n < P.nq ? pos0 + n / P.G : -1;
             }
-            if (tid < P.nq) {
-                rec[P.nq * HD + tid]        = mrow[tid];
-                rec[P.nq * HD + P.nq + tid] = lrow[tid];
-            }
+        // per-lane constants of the QK A fragment (the K row this lane addresses in ldmatrix)
+        const int lm = lane & 7, lmat = lane >> 3;
+        const int k_tok = 16 * w + pi16(lm + 8 * (lmat & 1));
+        const int k_key = kswz(k_tok), k_hi = lmat >> 1;
+        const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);
+        const int v_dim0 = 64 * w + 8 * lmat + lm;   // PV A fragment rows (+32 for the second half)
+
+        float m2[NT][2], lsum[NT][2], O[4][NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            m2[j][0] = m2[j][1] = -INFINITY;
+            lsum[j][0] = lsum[j][1] = 0.0f;
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) O[mt][j][0] = O[mt][j][1] = O[mt][j][2] = O[mt][j][3] = 0.0f;
         }
         __syncthreads();
-        x = xe;
-    }
-}
 
-// ------------------------------------------------------------------------------------ combine
-// One CTA per (pair, query row), one thread per element; partials merged in CTA order.
-__global__ void __launch_bounds__(256) k_combine(const DecodeParams P) {
-    const int p = blockIdx.x, n = blockIdx.y, d = threadIdx.x;
-    const int64_t ps = P.pair_tile0[p], pe = P.pair_tile0[p + 1];
-    if (pe <= ps) return;
-    const int c_lo = cta_of(ps, P.total_tiles, P.n_ctas), c_hi = cta_of(pe - 1, P.total_tiles, P.n_ctas);
-    if (c_lo == c_hi) return;
+        for (int i = 0; i < n_tiles; i++) {
+            const int stage = i % NSTAGE;
+            const uint32_t phase = (uint32_t)((i / NSTAGE) & 1);
+            const bool landed = mbar_wait(&sm.full[stage], phase, aborted ? 10000000ull : 2000000000ull);
+            aborted = aborted || !__all_sync(0xffffffffu, landed);
+            const TileRef tr = tile_ref(P, U, U.t0 + i);   // the decision the producer made
+            uint8_t *tile = sm.tile[stage];
+            const bool live = tr.blk >= 0 && !aborted;
+            const int cell0 = tr.blk * TILE_TOK;
+            if (P.Knew && tr.blk >= 0 && cell0 + TILE_TOK > pos0) {   // CTA-uniform
+                fused_append(P, U, tr.src, tile, cell0);
+                __syncthreads();
+            }
+            // ---------------- QK for this warp's 16 tokens ----------------------------------
+            float S[NT][4];
+#pragma unroll
+            for (int j = 0; j < NT; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+            if (live) {
+                const uint4 dkl = *reinterpret_cast<const uint4 *>(tile + TILE_KD + tk_lo * 16);
+                const uint4 dkh = *reinterpret_cast<const uint4 *>(tile + TILE_KD + tk_hi * 16);
+                const __half *dkl_h = reinterpret_cast<const __half *>(&dkl);
+                const __half *dkh_h = reinterpret_cast<const __half *>(&dkh);
+                const uint32_t kbase = smem_u32(tile) + k_tok * HD;
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(kbase + (((2 * b + k_hi) ^ k_key) << 4), a0, a1, a2, a3);
+                    const float dlo = __half2float(dkl_h[b]), dhi = __half2float(dkh_h[b]);
+#pragma unroll
+                    for (int j = 0; j < NT; j++) {
+                        const uint2 bq = *reinterpret_cast<const uint2 *>(sm.qq + (8 * j + g) * QSTR + b * 32 + tig * 8);
+                        uint32_t dd[4];
+                        mma_s8(dd, a0, a1, a2, a3, bq.x, bq.y, MAGIC_I);
+                        const float2 dq = *reinterpret_cast<const float2 *>(&sm.qd[b * NQ + 8 * j + 2 * tig]);
+                        const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(dd[0]), __uint_as_float(dd[1])),
+                                                      make_float2(-MAGIC_F, -MAGIC_F));
+                        const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(dd[2]), __uint_as_float(dd[3])),
+                                                      make_float2(-MAGIC_F, -MAGIC_F));
+                        const float2 wlo = __fmul2_rn(dq, make_float2(dlo, dlo));
+                        const float2 whi = __fmul2_rn(dq, make_float2(dhi, dhi));
+                        const float2 s01 = __ffma2_rn(f01, wlo, make_float2(S[j][0], S[j][1]));
+                        const float2 s23 = __ffma2_rn(f23, whi, make_float2(S[j][2], S[j][3]));
+                        S[j][0] = s01.x; S[j][1] = s01.y; S[j][2] = s23.x; S[j][3] = s23.y;
+                    }
+                }
+            }
+            // mask: rows past a query's position, padding rows, skipped tiles
+            const int clo = cell0 + tk_lo, chi = cell0 + tk_hi;
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                if (!live || clo > qlim[j][0]) S[j][0] = -INFINITY;
+                if (!live || clo > qlim[j][1]) S[j][1] = -INFINITY;
+                if (!live || chi > qlim[j][0]) S[j][2] = -INFINITY;
+                if (!live || chi > qlim[j][1]) S[j][3] = -INFINITY;
+            }
+            // ---------------- tile max across the CTA ---------------------------------------
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                float mx0 = fmaxf(S[j][0], S[j][2]), mx1 = fmaxf(S[j][1], S[j][3]);
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+                }
+                if (g == 0) {
+                    sm.red[w * NQ + 8 * j + 2 * tig]     = mx0;
+                    sm.red[w * NQ + 8 * j + 2 * tig + 1] = mx1;
+                }
+            }
+            __syncthreads();
+            // every warp is past the previous tile: its stage can be refilled
+            if (tid == 0 && i >= 1 && i + NSTAGE - 1 < n_tiles) issue_tile<NT>(P, sm, U, i + NSTAGE - 1);
+            float alpha[NT][2];
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int n = 8 * j + 2 * tig + e;
+                    const float tm =
+                        fmaxf(fmaxf(sm.red[n], sm.red[NQ + n]), fmaxf(sm.red[2 * NQ + n], sm.red[3 * NQ + n]));
+                    const float mnew = fmaxf(m2[j][e], tm * c2);
+                    alpha[j][e] = mnew == -INFINITY ? 1.0f : exp2f(m2[j][e] - mnew);
+                    m2[j][e] = mnew;
+                }
+                float pr[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float mm = m2[j][e & 1];
+                    pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
+                }
+                lsum[j][0] = fmaf(lsum[j][0], alpha[j][0], pr[0] + pr[2]);
+                lsum[j][1] = fmaf(lsum[j][1], alpha[j][1], pr[1] + pr[3]);
+                const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));   // tokens 4tig, 4tig+1 of row 8j+g
+                const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));   // tokens 4tig+2, 4tig+3
+                *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
+            }
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    const float2 al = make_float2(alpha[j][0], alpha[j][1]);
+                    const float2 o01 = __fmul2_rn(make_float2(O[mt][j][0], O[mt][j][1]), al);
+                    const float2 o23 = __fmul2_rn(make_float2(O[mt][j][2], O[mt][j][3]), al);
+                    O[mt][j][0] = o01.x; O[mt][j][1] = o01.y; O[mt][j][2] = o23.x; O[mt][j][3] = o23.y;
+                }
+            __syncthreads();
+            // ---------------- PV for this warp's 64 dims ------------------------------------
+            if (live) {
+                const uint32_t vbase = smem_u32(tile) + TILE_VQ;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    uint32_t va[8];
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        const int dim = v_dim0 + 32 * half;
+                        ldsm_x4(vbase + dim * TILE_TOK + ((kk ^ ((dim >> 1) & 3)) << 4), va[4 * half], va[4 * half + 1],
+                                va[4 * half + 2], va[4 * half + 3]);
+                    }
+#pragma unroll
+                    for (int bb = 0; bb < 2; bb++) {   // the warp's two q8_0 blocks (32 dims each)
+                        const int blk = 2 * w + bb;
+                        const uint2 dv =
+                            *reinterpret_cast<const uint2 *>(tile + TILE_VD + (blk * TILE_TOK + 16 * kk + 4 * tig) * 2);
+                        uint32_t alo[2], ahi[2], blo[2], bhi[2];
+                        s8x4_to_f16(va[4 * bb + 0], alo[0], ahi[0]);
+                        s8x4_to_f16(va[4 * bb + 1], alo[1], ahi[1]);
+                        s8x4_to_f16(va[4 * bb + 2], blo[0], bhi[0]);
+                        s8x4_to_f16(va[4 * bb + 3], blo[1], bhi[1]);
+#pragma unroll
+                        for (int j = 0; j < NT; j++) {
+                            const uint2 pb =
+                                *reinterpret_cast<const uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * kk + 4 * tig]);
+                            const uint32_t b0 = hmul2(pb.x, dv.x), b1 = hmul2(pb.y, dv.y);
+                            mma_f16(O[2 * bb][j], alo[0], alo[1], ahi[0], ahi[1], b0, b1);
+                            mma_f16(O[2 * bb + 1][j], blo[0], blo[1], bhi[0], bhi[1], b0, b1);
+                        }
+                    }
+                }
+            }
+        }
+        // ---------------- unit epilogue: row sums; O, m, l into shared memory ---------------------
+#pragma unroll
+        for (int j = 0; j < NT; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                float v = lsum[j][e];
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (g == 0) sm.lred[w * NQ + 8 * j + 2 * tig + e] = v;
+            }
+        __syncthreads();   // all tile reads done: the stages become the O buffer
+#pragma unroll
+        for (int j = 0; j < NT; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int n = 8 * j + 2 * tig + e;
+#pragma unroll
+                for (int mt = 0; mt < 4; mt++) {
+                    const int d0 = 64 * w + 16 * mt + g;
+                    obuf[n * HD + d0]     = O[mt][j][e];
+                    obuf[n * HD + d0 + 8] = O[mt][j][2 + e];
+                }
+                if (w == 0 && g == 0) {
+                    sm.ml[n]      = m2[j][e] == -INFINITY ? -INFINITY : m2[j][e] * 0.6931471805599453f;
+                    sm.ml[NQ + n] = sm.lred[n] + sm.lred[NQ + n] + sm.lred[2 * NQ + n] + sm.lred[3 * NQ + n];
+                }
+            }
+        if (aborted && lane == 0) atomicOr(P.status, ST_TIMEOUT);
+    }
+    cluster.sync();   // #1: every unit's O, m, l visible to the cluster
+
+    // ---- merge the units of each pair inside the cluster (distributed shared memory) -------------
+    bool extends = false;   // this unit's pair reaches beyond the cluster
+    int gb = 0, gs = 1, me = 0;
+    if (has_unit) {
+        gb = max(U.pu0, k * CN);
+        const int ge = min(U.pu1, (k + 1) * CN);
+        gs = ge - gb;
+        me = u - gb;
+        extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
+        const int first_pair_unit = k * CN;   // slot 0 belongs to the pair of the cluster's first unit
+        float *slot = P.partial + (2 * k + (U.pu0 <= first_pair_unit ? 0 : 1)) * partial_stride(P.nq);
+        for (int n = me; n < P.nq; n += gs) {
+            float M = -INFINITY;
+            for (int r = 0; r < gs; r++) {
+                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
+                M = fmaxf(M, rml[n]);
+            }
+            float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
+            for (int r = 0; r < gs; r++) {
+                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
+                const float m = rml[n];
+                if (m == -INFINITY) continue;
+                const float wgt = expf(m - M);
+                L = fmaf(rml[NQ + n], wgt, L);
+                const float *ro = cluster.map_shared_rank(obuf, (gb + r) % CN) + n * HD;
+                o0 = fmaf(ro[tid], wgt, o0);
+                o1 = fmaf(ro[tid + 128], wgt, o1);
+            }
+            if (!extends) {
+                const int t = n / P.G, jj = n % P.G;
+                float *o = P.out + (((int64_t)U.s * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
+                const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+                o[tid] = o0 * inv;
+                o[tid + 128] = o1 * inv;
+            } else {
+                slot[n * HD + tid] = o0;
+                slot[n * HD + tid + 128] = o1;
+                if (tid == 0) {
+                    slot[P.nq * HD + n] = M;
+                    slot[P.nq * HD + P.nq + n] = L;
+                }
+            }
+        }
+        if (extends) __threadfence();
+    }
+    cluster.sync();   // #2: cluster partials written; remote reads of O done
+    if (has_unit && extends && me == 0 && tid == 0) {
+        const int n_cl = (U.pu1 - 1) / CN - U.pu0 / CN + 1;
+        const int old = atomicAdd(&P.counters[U.p], 1);
+        sm.merge_flag = old == n_cl - 1;
+    }
+    cluster.sync();   // #3: the group leader's decision is visible
+    const bool merge = has_unit && extends && *cluster.map_shared_rank(&sm.merge_flag, gb % CN);
+    cluster.sync();   // #4: nobody reads another CTA's shared memory after this point
+    if (!merge) return;
+    // ---- last cluster of an extended pair: merge the per-cluster partials in cluster order -------
+    __threadfence();
+    const int k_lo = U.pu0 / CN, k_hi = (U.pu1 - 1) / CN;
     const int64_t stride = partial_stride(P.nq);
-    float M = -INFINITY;
-    for (int c = c_lo; c <= c_hi; c++) {
-        const int pslot = 2 * c + (find_pair(P, cta_begin(c, P.total_tiles, P.n_ctas)) == p ? 0 : 1);
-        M = fmaxf(M, __ldcg(P.partial + pslot * stride + P.nq * HD + n));
-    }
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-        for (int c = c_lo; c <= c_hi; c++) {
-            const int pslot = 2 * c + (find_pair(P, cta_begin(c, P.total_tiles, P.n_ctas)) == p ? 0 : 1);
-            const float *rec = P.partial + pslot * stride;
+    for (int n = me; n < P.nq; n += gs) {
+        float M = -INFINITY;
+        for (int kk = k_lo; kk <= k_hi; kk++) {
+            const float *rec = P.partial + (2 * kk + (kk == k_lo && U.pu0 != kk * CN ? 1 : 0)) * stride;
+            M = fmaxf(M, __ldcg(rec + P.nq * HD + n));
+        }
+        float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
+        for (int kk = k_lo; kk <= k_hi; kk++) {
+            const float *rec = P.partial + (2 * kk + (kk == k_lo && U.pu0 != kk * CN ? 1 : 0)) * stride;
             const float m = __ldcg(rec + P.nq * HD + n);
             if (m == -INFINITY) continue;
-            const float w = expf(m - M);
-            L = fmaf(__ldcg(rec + P.nq * HD + P.nq + n), w, L);
-            O = fmaf(__ldcg(rec + n * HD + d), w, O);
+            const float wgt = expf(m - M);
+            L = fmaf(__ldcg(rec + P.nq * HD + P.nq + n), wgt, L);
+            o0 = fmaf(__ldcg(rec + n * HD + tid), wgt, o0);
+            o1 = fmaf(__ldcg(rec + n * HD + tid + 128), wgt, o1);
         }
+        const int t = n / P.G, jj = n % P.G;
+        float *o = P.out + (((int64_t)U.s * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
+        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+        o[tid] = o0 * inv;
+        o[tid + 128] = o1 * inv;
     }
-    const int s = p / P.n_head_kv, h = p % P.n_head_kv, t = n / P.G, j = n % P.G;
-    P.out[(((int64_t)s * P.T + t) * P.n_head + h * P.G + j) * HD + d] = L == 0.0f ? 0.0f : O * (1.0f / L);
+    if (me == 0 && tid == 0) P.counters[U.p] = 0;   // ready for the next launch
 }
 
-template <int NQ>
-static cudaError_t launch_simple(const DecodeParams &p, cudaStream_t st) {
-    const size_t smem = TILE_BYTES + NQ * HD + NQ * NBLK * 4 + NQ * TILE_TOK * 4 + 3 * NQ * 4;
-    cudaError_t e = cudaFuncSetAttribute(k_decode_simple<NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}  // namespace dec
+
+template <int NT>
+static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
+    const size_t smem = sizeof(dec::Smem<NT>);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    k_decode_simple<NQ><<<p.n_ctas, 128, smem, st>>>(p);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        e = cudaFuncSetAttribute(dec::k_decode<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_ctas);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = dec::CN;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, dec::k_decode<NT>, p);
     count_launches(1);
-    return cudaGetLastError();
+    return e;
 }
 
-int decode_max_nq() { return 32; }
+int decode_max_nq() { return 64; }
+int decode_cluster() { return dec::CN; }
 
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
-    cudaError_t e;
-    if (p.nq <= 8) e = launch_simple<8>(p, st);
-    else if (p.nq <= 16) e = launch_simple<16>(p, st);
-    else if (p.nq <= 24) e = launch_simple<24>(p, st);
-    else if (p.nq <= 32) e = launch_simple<32>(p, st);
-    else return cudaErrorInvalidValue;
-    if (e != cudaSuccess) return e;
-    bool split = false;
-    for (int q = 0; q < p.n_pairs && !split; q++) {
-        const int64_t ps = p.pair_tile0[q], pe = p.pair_tile0[q + 1];
-        if (pe > ps) split = cta_of(ps, p.total_tiles, p.n_ctas) != cta_of(pe - 1, p.total_tiles, p.n_ctas);
+    switch ((p.nq + 7) / 8) {
+        case 1: return launch_nt<1>(p, st);
+        case 2: return launch_nt<2>(p, st);
+        case 3: return launch_nt<3>(p, st);
+        case 4: return launch_nt<4>(p, st);
+        case 5: return launch_nt<5>(p, st);
+        case 6: return launch_nt<6>(p, st);
+        case 7: return launch_nt<7>(p, st);
+        case 8: return launch_nt<8>(p, st);
+        default: return cudaErrorInvalidValue;
     }
-    if (!split) return cudaSuccess;
-    dim3 grid(p.n_pairs, p.nq);
-    k_combine<<<grid, 256, 0, st>>>(p);
-    count_launches(1);
-    return cudaGetLastError();
 }
 
 }  // namespace qkv

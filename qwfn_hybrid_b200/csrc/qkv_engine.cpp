@@ -13,6 +13,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <numeric>
@@ -67,8 +68,9 @@ struct qkv_engine {
     uint8_t  *d_rec     = nullptr;    // [n_slots][rec_slot_bytes]
     uint8_t  *d_rb      = nullptr;    // [n_slots][n_rollback][rec_slot_bytes]
     uint16_t *d_summary = nullptr;    // [n_layer][n_slots][n_head_kv][max_blocks][HD]
-    float    *d_partial = nullptr;
+    float    *d_partial = nullptr;    // kernel C: per-cluster partial records
     size_t    partial_bytes = 0;
+    int32_t  *d_counters = nullptr;   // kernel C: per-pair arrival counters (zero between launches)
     int32_t  *d_status  = nullptr;
     size_t    device_bytes = 0;
 
@@ -270,6 +272,7 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_rb);
     cudaFree(eng->d_summary);
     cudaFree(eng->d_partial);
+    cudaFree(eng->d_counters);
     cudaFree(eng->d_status);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
@@ -338,8 +341,12 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
             r = dalloc(eng, eng->d_summary, (size_t)c.n_layer * c.n_slots * c.n_head_kv * eng->max_blocks * HD * 2,
                        "block summaries");
         if (r == QKV_OK) {
-            eng->partial_bytes = (size_t)2 * eng->num_sms * 8 * partial_stride(eng->max_nq) * sizeof(float);
+            // at most ~2 units per SM plus one per sequence of a launch, in clusters: 2 records each
+            const size_t max_units = (size_t)eng->num_sms * 2 + (size_t)2 * MAX_SEQ * c.n_head_kv;
+            eng->partial_bytes = 2 * ((max_units + decode_cluster() - 1) / decode_cluster() + 1) *
+                                 partial_stride(eng->max_nq) * sizeof(float);
             r = dalloc(eng, eng->d_partial, eng->partial_bytes, "split-K partials");
+            if (r == QKV_OK) r = dalloc(eng, eng->d_counters, (size_t)MAX_PAIRS * 4, "split-K counters");
         }
         if (r == QKV_OK) r = dalloc(eng, eng->d_status, 256, "status");
         if (r == QKV_OK) {
@@ -352,6 +359,7 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
             e = cudaMemset(eng->d_bt, 0xff, (size_t)c.n_slots * eng->max_pages * 4);
             if (e == cudaSuccess && eng->d_rec) e = cudaMemset(eng->d_rec, 0, (size_t)c.n_slots * eng->rec_slot_bytes);
             if (e == cudaSuccess) e = cudaMemset(eng->d_status, 0, 256);
+            if (e == cudaSuccess) e = cudaMemset(eng->d_counters, 0, (size_t)MAX_PAIRS * 4);
             if (e == cudaSuccess) e = cudaDeviceSynchronize();
             if (e != cudaSuccess) r = fail(eng, QKV_ERR_CUDA, "init: %s", cudaGetErrorString(e));
         }
@@ -445,6 +453,17 @@ extern "C" qkv_status qkv_seq_length(const qkv_engine *eng, int32_t slot, int32_
     return QKV_OK;
 }
 
+extern "C" qkv_status qkv_seq_reserve(qkv_engine *eng, int32_t slot, int32_t n_tokens, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r = check_slot(eng, slot);
+    if (r != QKV_OK) return r;
+    if (n_tokens < 0 || n_tokens > eng->cfg.n_ctx) return fail(eng, QKV_ERR_INVALID, "reserve %d of n_ctx %d", n_tokens, eng->cfg.n_ctx);
+    if (n_tokens == 0) return QKV_OK;
+    if (!eng->host_only && (r = use_device(eng)) != QKV_OK) return r;
+    if ((r = reserve(eng, slot, 0, n_tokens, S(stream))) != QKV_OK) return r;
+    return flush_tables(eng, S(stream));
+}
+
 extern "C" qkv_status qkv_seq_pages(const qkv_engine *eng, int32_t slot, int32_t *pages, int32_t cap, int32_t *n) {
     if (!eng || !n || slot < 0 || slot >= eng->cfg.n_slots || (cap > 0 && !pages)) return QKV_ERR_INVALID;
     const auto &pg = eng->slots[slot].pages;
@@ -490,71 +509,132 @@ extern "C" qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, i
 }
 
 // ------------------------------------------------------------------------------------ decode
-extern "C" qkv_status qkv_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
-                                      int32_t n_seq, const float *Q, int32_t T, float scale,
-                                      const int32_t *sel_blocks, int32_t n_sel, float *out, void *stream) {
+// Plan one launch of kernel C for sequences [base, base+ns): every pair (sequence, KV head) is
+// cut into units in proportion to its tiles so that about two CTAs per SM carry equal work.
+static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int ns,
+                                const float *Q, int32_t T, float scale, const int32_t *sel, int32_t n_sel,
+                                const float *Knew, const float *Vnew, float *out, cudaStream_t st) {
+    const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H, CN = decode_cluster();
+    DecodeParams P;
+    memset(&P, 0, sizeof P);
+    P.pool = eng->pools[layer];
+    P.block_table = eng->d_bt;
+    P.Q = Q;
+    P.out = out;
+    P.partial = eng->d_partial;
+    P.counters = eng->d_counters;
+    P.sel = sel;
+    P.Knew = Knew;
+    P.Vnew = Vnew;
+    P.status = eng->d_status;
+    P.page_bytes = eng->page_bytes;
+    P.n_pages = eng->n_pages;
+    P.max_pages = eng->max_pages;
+    P.n_head = eng->cfg.n_head;
+    P.n_head_kv = H;
+    P.G = G;
+    P.T = T;
+    P.nq = T * G;
+    P.n_seq = ns;
+    P.n_sel = n_sel;
+    P.scale = scale;
+    int64_t total = 0;
+    for (int i = 0; i < ns; i++) {
+        P.seq_slot[i] = slots[i];
+        P.seq_pos0[i] = pos0[i];
+        P.seq_tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
+        total += (int64_t)H * P.seq_tiles[i];
+    }
+    const int64_t target = (int64_t)eng->num_sms * 2;   // two resident CTAs per SM
+    int64_t units = 0;
+    for (int i = 0; i < ns; i++) {
+        int64_t u = (int64_t)((double)P.seq_tiles[i] * target / (double)total + 0.5);
+        u = std::max<int64_t>(1, std::min<int64_t>(u, P.seq_tiles[i]));
+        P.seq_units[i] = (int32_t)u;
+        P.seq_unit0[i] = (int32_t)units;
+        units += u * H;
+    }
+    P.seq_unit0[ns] = (int32_t)units;
+    P.n_units = (int32_t)units;
+    P.n_ctas = (int32_t)((units + CN - 1) / CN * CN);
+    if ((size_t)2 * (P.n_ctas / CN) * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
+        return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small for %d units", P.n_units);
+    CK(eng, launch_decode(P, st));
+    return QKV_OK;
+}
+
+static qkv_status decode_common(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                int32_t n_seq, const float *Q, int32_t T, float scale, const int32_t *sel_blocks,
+                                int32_t n_sel, const float *Knew, const float *Vnew, float *out, void *stream) {
     if (!eng) return QKV_ERR_INVALID;
     qkv_status r;
     if ((r = check_layer(eng, layer)) != QKV_OK) return r;
     if (!slots || !pos0 || n_seq < 1 || !Q || !out || T < 1 || T > 4)
         return fail(eng, QKV_ERR_INVALID, "decode: n_seq %d, T %d (1..4), null pointer", n_seq, T);
     if (sel_blocks && n_sel < 1) return fail(eng, QKV_ERR_INVALID, "decode: n_sel %d with a selection", n_sel);
+    const bool fused = Knew != nullptr;
+    if (fused && (!Vnew || sel_blocks)) return fail(eng, QKV_ERR_INVALID, "fused append needs K and V and dense attention");
     const int G = eng->cfg.n_head / eng->cfg.n_head_kv;
     if (T * G > decode_max_nq()) return fail(eng, QKV_ERR_UNSUPPORTED, "decode: %d query rows per KV head (max %d)", T * G, decode_max_nq());
     for (int i = 0; i < n_seq; i++) {
         if ((r = check_slot(eng, slots[i])) != QKV_OK) return r;
-        if (pos0[i] < 0 || pos0[i] + T > eng->slots[slots[i]].n_past)
+        for (int j = 0; j < i; j++)
+            if (fused && slots[j] == slots[i]) return fail(eng, QKV_ERR_INVALID, "fused append: slot %d twice", slots[i]);
+        const int32_t n_past = eng->slots[slots[i]].n_past;
+        if (fused) {
+            if (pos0[i] < 0 || pos0[i] > n_past || (int64_t)pos0[i] + T > eng->cfg.n_ctx)
+                return fail(eng, QKV_ERR_INVALID, "fused append at %d: slot %d holds %d (n_ctx %d)", pos0[i], slots[i], n_past, eng->cfg.n_ctx);
+        } else if (pos0[i] < 0 || pos0[i] + T > n_past) {
             return fail(eng, QKV_ERR_INVALID, "decode: sequence %d queries positions %d..%d but slot %d holds %d", i, pos0[i],
-                        pos0[i] + T - 1, slots[i], eng->slots[slots[i]].n_past);
+                        pos0[i] + T - 1, slots[i], n_past);
+        }
     }
     if ((r = use_device(eng)) != QKV_OK) return r;
-    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if (fused) {
+        // reserve every sequence's rows first: a failure leaves no sequence half-appended
+        size_t need = 0;
+        for (int i = 0; i < n_seq; i++) {
+            const qkv_engine::Slot &sl = eng->slots[slots[i]];
+            for (int32_t pi = pos0[i] / PAGE_TOK; pi <= (pos0[i] + T - 1) / PAGE_TOK; pi++)
+                if (pi >= (int32_t)sl.pages.size() || eng->refcnt[sl.pages[pi]] > 1) need++;
+        }
+        if (need > eng->free_pages.size())
+            return fail(eng, QKV_ERR_NO_MEMORY, "page pool exhausted: need %zu pages, %zu free", need, eng->free_pages.size());
+        for (int i = 0; i < n_seq; i++)
+            if ((r = reserve(eng, slots[i], pos0[i], T, st)) != QKV_OK) return r;
+    }
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
     const int H = eng->cfg.n_head_kv;
+    const size_t qrow = (size_t)T * eng->cfg.n_head * HD, krow = (size_t)T * H * HD;
     for (int base = 0; base < n_seq; base += MAX_SEQ) {
         const int ns = std::min(MAX_SEQ, n_seq - base);
-        DecodeParams P;
-        memset(&P, 0, sizeof P);
-        P.pool = eng->pools[layer];
-        P.block_table = eng->d_bt;
-        P.Q = Q + (size_t)base * T * eng->cfg.n_head * HD;
-        P.out = out + (size_t)base * T * eng->cfg.n_head * HD;
-        P.partial = eng->d_partial;
-        P.sel = sel_blocks ? sel_blocks + (size_t)base * H * n_sel : nullptr;
-        P.status = eng->d_status;
-        P.page_bytes = eng->page_bytes;
-        P.n_pages = eng->n_pages;
-        P.max_pages = eng->max_pages;
-        P.n_head = eng->cfg.n_head;
-        P.n_head_kv = H;
-        P.G = G;
-        P.T = T;
-        P.nq = T * G;
-        P.n_seq = ns;
-        P.n_sel = n_sel;
-        P.scale = scale;
-        P.n_pairs = ns * H;
-        int64_t tiles = 0;
-        for (int i = 0; i < ns; i++) {
-            P.seq_slot[i] = slots[base + i];
-            P.seq_pos0[i] = pos0[base + i];
-            const int32_t per = sel_blocks ? n_sel : (pos0[base + i] + T + TILE_TOK - 1) / TILE_TOK;
-            for (int h = 0; h < H; h++) {
-                P.pair_tile0[i * H + h] = (int32_t)tiles;
-                tiles += per;
-            }
-        }
-        P.pair_tile0[ns * H] = (int32_t)tiles;
-        P.total_tiles = (int32_t)tiles;
-        // Split: about two tiles per CTA, at most 4 CTAs per SM.
-        int64_t ctas = std::max<int64_t>(1, tiles / 2);
-        ctas = std::min<int64_t>(ctas, (int64_t)eng->num_sms * 4);
-        ctas = std::min<int64_t>(ctas, tiles);
-        P.n_ctas = (int32_t)ctas;
-        if ((size_t)2 * ctas * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
-            return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small");
-        CK(eng, launch_decode(P, S(stream)));
+        if ((r = decode_launch(eng, layer, slots + base, pos0 + base, ns, Q + base * qrow, T, scale,
+                               sel_blocks ? sel_blocks + (size_t)base * H * n_sel : nullptr, n_sel,
+                               fused ? Knew + base * krow : nullptr, fused ? Vnew + base * krow : nullptr,
+                               out + base * qrow, st)) != QKV_OK)
+            return r;
     }
+    if (fused)
+        for (int i = 0; i < n_seq; i++) {
+            qkv_engine::Slot &sl = eng->slots[slots[i]];
+            sl.n_past = std::max(sl.n_past, pos0[i] + T);
+            invalidate_summaries(eng, slots[i], pos0[i]);
+        }
     return QKV_OK;
+}
+
+extern "C" qkv_status qkv_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                      int32_t n_seq, const float *Q, int32_t T, float scale,
+                                      const int32_t *sel_blocks, int32_t n_sel, float *out, void *stream) {
+    return decode_common(eng, layer, slots, pos0, n_seq, Q, T, scale, sel_blocks, n_sel, nullptr, nullptr, out, stream);
+}
+
+extern "C" qkv_status qkv_append_attn_decode(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                             int32_t n_seq, const float *K, const float *V, const float *Q, int32_t T,
+                                             float scale, float *out, void *stream) {
+    if (!K || !V) return eng ? fail(eng, QKV_ERR_INVALID, "fused append: null K or V") : QKV_ERR_INVALID;
+    return decode_common(eng, layer, slots, pos0, n_seq, Q, T, scale, nullptr, 0, K, V, out, stream);
 }
 
 // --------------------------------------------------------------------------------- selection

@@ -53,6 +53,7 @@ __host__ __device__ __forceinline__ int vd_off(int b, int t) { return TILE_VD + 
 // Device status word bits (qkv_device_status).
 constexpr int32_t ST_BAD_PAGE  = 1;    // a block-table entry was < 0 or >= n_pages
 constexpr int32_t ST_BAD_INDEX = 2;    // a cell / block index outside the sequence
+constexpr int32_t ST_TIMEOUT   = 4;    // a bounded wait on a tile copy gave up
 
 // ---- kernel A and layout transforms ------------------------------------------------------------
 struct PoolRef {
@@ -105,20 +106,25 @@ struct DecodeParams {
     const int32_t *block_table;   // [n_slots][max_pages]
     const float   *Q;             // [n_seq][T][n_head][HD]
     float         *out;           // [n_seq][T][n_head][HD]
-    float         *partial;       // scratch: [2*n_ctas][nq*HD + 2*nq]
+    float         *partial;       // scratch: 2 records per cluster of [nq*HD + 2*nq] floats
+    int32_t       *counters;      // scratch: per pair, zero between launches
     const int32_t *sel;           // nullable [n_seq][n_head_kv][n_sel] block ids
+    const float   *Knew, *Vnew;   // nullable [n_seq][T][n_head_kv*HD]: fused append (dense only)
     int32_t       *status;
     int64_t page_bytes;
-    int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_ctas, n_pairs, total_tiles;
+    int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_units, n_ctas;
     float   scale;
     int32_t seq_slot[MAX_SEQ];
     int32_t seq_pos0[MAX_SEQ];
-    int32_t pair_tile0[MAX_PAIRS + 1];   // prefix of tiles over pairs (pair = seq*n_head_kv + head)
+    int32_t seq_tiles[MAX_SEQ];      // tiles of each pair of the sequence
+    int32_t seq_units[MAX_SEQ];      // units (CTAs) per pair of the sequence
+    int32_t seq_unit0[MAX_SEQ + 1];  // prefix of n_head_kv * seq_units
 };
 // partial record size in floats for nq query rows
 __host__ __device__ __forceinline__ int64_t partial_stride(int nq) { return (int64_t)nq * HD + 2 * nq; }
 
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);
 int decode_max_nq();
+int decode_cluster();
 
 }  // namespace qkv

@@ -155,3 +155,48 @@ def test_sparse_select_fewer_blocks_than_topk(cuda, qkvlib, oracle):
 def test_sparse_config4_full_size(cuda, qkvlib, oracle):
     """ctx 73728, 64-token blocks, top-32 per KV head, T = 3."""
     sparse_case(cuda, qkvlib, oracle, n_kv=73728, T=3, top_k=32, seed=3)
+
+
+@pytest.mark.parametrize("T", [1, 3, 4])
+def test_fused_append_decode_vs_oracle(cuda, qkvlib, oracle, T):
+    """Kernel A fused into kernel C: the appended bytes and the attention both match."""
+    lens = [1500, 64 - T, 255, 3]
+    eng = engine(qkvlib, n_slots=5)
+    K0, V0, Kn, Vn = {}, {}, {}, {}
+    for i, n in enumerate(lens):
+        eng.seq_alloc(i)
+        K0[i], V0[i] = normal(200 + i, (n, 512)), normal(300 + i, (n, 512))
+        append_rows(eng, 0, i, 0, K0[i], V0[i])
+        Kn[i], Vn[i] = normal(400 + i, (T, 512)), normal(500 + i, (T, 512))
+    import torch
+    Q = normal(9, (len(lens), T, 16, HD))
+    q = to_dev(Q)
+    out = torch.empty_like(q)
+    eng.append_attn_decode(0, list(range(len(lens))), lens, to_dev(np.stack([Kn[i] for i in range(len(lens))])),
+                           to_dev(np.stack([Vn[i] for i in range(len(lens))])), q, T, 1 / 16, out)
+    torch.cuda.synchronize()
+    assert eng.device_status() == 0
+    got = out.cpu().numpy()
+    for i, n in enumerate(lens):
+        assert eng.n_past(i) == n + T
+        Kall, Vall = np.concatenate([K0[i], Kn[i]]), np.concatenate([V0[i], Vn[i]])
+        Kq, Vq = read_rows(eng, 0, i, 0, n + T)
+        assert np.array_equal(Kq, oracle.quantize_rows(Kall)) and np.array_equal(Vq, oracle.quantize_rows(Vall))
+        ref = oracle.attn(Q[i], Kq, Vq, np.arange(n, n + T), 2, 1 / 16)
+        assert_close(got[i], ref, f"fused seq {i}")
+
+
+def test_decode_many_units_many_clusters(cuda, qkvlib, oracle):
+    """A long and a short sequence: the long pairs span many clusters (last-arriver merge)."""
+    lens = [40000, 100]
+    eng = engine(qkvlib, n_slots=2, n_ctx=40960)
+    kv = {}
+    for i, n in enumerate(lens):
+        eng.seq_alloc(i)
+        kv[i] = fill_seq(eng, oracle, 0, i, n, seed=700 + i)
+    Q = normal(8, (2, 2, 16, HD))
+    for rep in range(2):   # counters must be reset for the next launch
+        got = decode(eng, 0, [0, 1], [n - 2 for n in lens], Q, 2)
+        for i, n in enumerate(lens):
+            ref = oracle.attn(Q[i], kv[i][0], kv[i][1], np.arange(n - 2, n), 2, 1 / 16)
+            assert_close(got[i], ref, f"rep {rep} seq {i}")

@@ -90,10 +90,10 @@ qkv_status qkv_seq_alloc(qkv_engine *eng, int32_t slot);
 qkv_status qkv_seq_free(qkv_engine *eng, int32_t slot);
 qkv_status qkv_seq_reset(qkv_engine *eng, int32_t slot, void *stream);
 qkv_status qkv_seq_length(const qkv_engine *eng, int32_t slot, int32_t *n_past);
-/* Make positions 0 .. n_tokens-1 of a slot backed by private pages now (allocating, copying
- * shared pages), so later appends in that range touch no host state; n_past is unchanged.  Lets
- * a caller capture decode steps in a CUDA graph.  The reference allocates its cache whole at
- * init (src/qwfn_state.cpp:93-111). */
+/* Make the positions a slot will append next, n_past .. n_tokens-1, writable now (allocating
+ * pages, copying a shared page that holds n_past), so the appends touch no host state; n_past is
+ * unchanged.  Lets a caller capture decode steps in a CUDA graph.  The reference allocates its
+ * cache whole at init (src/qwfn_state.cpp:93-111). */
 qkv_status qkv_seq_reserve(qkv_engine *eng, int32_t slot, int32_t n_tokens, void *stream);
 /* Page ids of a slot's block table (host copy), for inspection and tests. */
 qkv_status qkv_seq_pages(const qkv_engine *eng, int32_t slot, int32_t *pages, int32_t cap, int32_t *n);

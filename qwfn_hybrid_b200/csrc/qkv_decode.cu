@@ -145,13 +145,17 @@ struct Smem {
     float    red[4 * NQ];
     float    lred[4 * NQ];
     float    ml[2 * NQ];                 // the unit's m (natural log domain) and l per row
+    float    wm[(NQ + CN) * CN];         // in-cluster merge: per (owned row, member) m, then weight
+    float    wl[(NQ + CN) * CN];         //                   per (owned row, member) l
+    float    rowM[NQ + CN], rowL[NQ + CN];
     __half   ps[NQ * PSTR];
     uint64_t full[NSTAGE];
     int32_t  merge_flag;
 };
 
 struct Unit {
-    int s, h, p;          // sequence, KV head, pair = s * n_head_kv + h
+    int s, h, p;          // plan position of the sequence, KV head, pair = s * n_head_kv + h
+    int io;               // the sequence's index in the caller's arrays (Q, out, K/V new, selection)
     int t0, t1;           // tile range of the pair this unit runs
     int pu0, pu1;         // unit range of the pair
 };
@@ -164,6 +168,7 @@ __device__ __forceinline__ Unit unit_of(const DecodeParams &P, int u) {
     }
     Unit x;
     x.s = lo;
+    x.io = P.seq_idx[lo];
     const int per = P.seq_units[lo], tiles = P.seq_tiles[lo];
     const int off = u - P.seq_unit0[lo];
     x.h = off / per;
@@ -183,7 +188,7 @@ struct TileRef {
 
 __device__ __forceinline__ TileRef tile_ref(const DecodeParams &P, const Unit &U, int k) {
     TileRef r{-1, nullptr};
-    const int blkid = P.sel ? P.sel[((int64_t)U.s * P.n_head_kv + U.h) * P.n_sel + k] : k;
+    const int blkid = P.sel ? P.sel[((int64_t)U.io * P.n_head_kv + U.h) * P.n_sel + k] : k;
     if (blkid < 0) return r;
     const int n_kv = P.seq_pos0[U.s] + P.T;
     if (blkid >= (n_kv + TILE_TOK - 1) / TILE_TOK) {
@@ -228,7 +233,7 @@ __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &
     for (int wi = warp; wi < work; wi += 4) {
         const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
         const float *src = (kv ? P.Vnew : P.Knew) +
-                           (((int64_t)U.s * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK;
+                           (((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK;
         const float x = src[lane];
         float amax = fabsf(x);
 #pragma unroll
@@ -273,17 +278,26 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
     float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
     const float c2 = P.scale * 1.4426950408889634f;        // softmax in base 2
     bool aborted = false;   // warp-uniform: a tile copy did not land within the wait limit
-
+    // The units of this unit's pair inside the cluster form a group of gs CTAs (ranks gb..gb+gs-1
+    // mod CN); member `me` owns query rows me, me+gs, ... for the Q quantisation and the merge.
+    int gb = 0, gs = 1, me = 0;
+    bool extends = false;   // the pair has units in other clusters too
     if (has_unit) {
-        const int s = U.s, h = U.h, pos0 = P.seq_pos0[s];
-        // ---- quantise the pair's query rows (q8_0, as ggml's CPU path does) -------------------
-        for (int gid = tid; gid < NQ * 32; gid += 128) {
-            const int n = gid >> 5, e8 = gid & 31, b = e8 >> 2, sub = e8 & 3;
+        gb = max(U.pu0, k * CN);
+        gs = min(U.pu1, (k + 1) * CN) - gb;
+        me = u - gb;
+        extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
+        // ---- quantise this member's query rows (q8_0, as ggml's CPU path does) ----------------
+        // 32 threads per row, 8 consecutive elements each (4 threads per 32-element block).
+        const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
+        const int rows_mine = (NQ - me + gs - 1) / gs;
+        for (int pass = 0; pass * 4 < rows_mine; pass++) {
+            const int ri = pass * 4 + (tid >> 5), e8 = tid & 31, b = e8 >> 2, sub = e8 & 3;
+            const int n = me + ri * gs;
             float v[8];
-            if (n < P.nq) {
+            if (ri < rows_mine && n < P.nq) {
                 const int t = n / P.G, jj = n % P.G;
-                const float4 *src = reinterpret_cast<const float4 *>(
-                    P.Q + (((int64_t)s * P.T + t) * P.n_head + h * P.G + jj) * HD + b * QK + sub * 8);
+                const float4 *src = reinterpret_cast<const float4 *>(qsrc + ((int64_t)t * P.n_head + jj) * HD + e8 * 8);
                 const float4 u0 = src[0], u1 = src[1];
                 v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
                 v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
@@ -304,11 +318,34 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                 w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[q], id)) << (8 * q);
                 w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[4 + q], id)) << (8 * q);
             }
-            uint8_t *row = sm.qq + n * QSTR + b * 32;
-            *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
-            *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
-            if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
+            if (ri < rows_mine) {
+                uint8_t *row = sm.qq + n * QSTR + b * 32;
+                *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
+                *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
+                if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
+            }
         }
+    }
+    cluster.sync();   // #0: every member's query rows are ready
+    if (has_unit && gs > 1) {
+        // fetch the rows the other members quantised (distributed shared memory, one round)
+        constexpr int CH = QSTR / 16;
+        for (int e = tid; e < NQ * CH; e += 128) {
+            const int n = e / CH, c = e % CH, r = n % gs;
+            if (r == me) continue;
+            const uint4 *src = cluster.map_shared_rank(reinterpret_cast<const uint4 *>(sm.qq + n * QSTR), (gb + r) % CN);
+            reinterpret_cast<uint4 *>(sm.qq + n * QSTR)[c] = src[c];
+        }
+        for (int e = tid; e < NQ * NBLK; e += 128) {
+            const int n = e % NQ, r = n % gs;
+            if (r == me) continue;
+            sm.qd[e] = *cluster.map_shared_rank(&sm.qd[e], (gb + r) % CN);
+        }
+    }
+    cluster.sync();   // #0b: remote rows copied; shared memory of peers no longer read
+
+    if (has_unit) {
+        const int pos0 = P.seq_pos0[U.s];
         // last visible position of each of this lane's query rows (padding rows: nothing visible)
         int qlim[NT][2];
 #pragma unroll
@@ -507,45 +544,79 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
     cluster.sync();   // #1: every unit's O, m, l visible to the cluster
 
     // ---- merge the units of each pair inside the cluster (distributed shared memory) -------------
-    bool extends = false;   // this unit's pair reaches beyond the cluster
-    int gb = 0, gs = 1, me = 0;
+    // Round 1: lane (row ri, member r) fetches m, l; 8-lane shuffles give the row max, the member
+    // weights and the row sum.  Round 2: the O rows, two at a time, 4*CN remote loads in flight.
+    const int R = has_unit ? (P.nq - me + gs - 1) / gs : 0;   // rows this member merges
     if (has_unit) {
-        gb = max(U.pu0, k * CN);
-        const int ge = min(U.pu1, (k + 1) * CN);
-        gs = ge - gb;
-        me = u - gb;
-        extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
+        const int e_end = (R * CN + 31) & ~31;
+        for (int e = tid; e < e_end; e += 128) {
+            const int ri = e / CN, r = e % CN;
+            const bool ok = e < R * CN && r < gs;
+            float m = -INFINITY, l = 0.0f;
+            if (ok) {
+                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
+                m = rml[me + ri * gs];
+                l = rml[NQ + me + ri * gs];
+            }
+            float M = m;
+#pragma unroll
+            for (int o = 1; o < CN; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float wgt = m == -INFINITY ? 0.0f : expf(m - M);
+            float L = l * wgt;
+#pragma unroll
+            for (int o = 1; o < CN; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            if (e < R * CN) {
+                sm.wm[e] = wgt;
+                if (r == 0) {
+                    sm.rowM[ri] = M;
+                    sm.rowL[ri] = L;
+                }
+            }
+        }
+        __syncthreads();
+        const float *ro[CN];
+#pragma unroll
+        for (int r = 0; r < CN; r++) ro[r] = cluster.map_shared_rank(obuf, (gb + (r < gs ? r : 0)) % CN);
         const int first_pair_unit = k * CN;   // slot 0 belongs to the pair of the cluster's first unit
         float *slot = P.partial + (2 * k + (U.pu0 <= first_pair_unit ? 0 : 1)) * partial_stride(P.nq);
-        for (int n = me; n < P.nq; n += gs) {
-            float M = -INFINITY;
-            for (int r = 0; r < gs; r++) {
-                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
-                M = fmaxf(M, rml[n]);
+        for (int ri = 0; ri < R; ri += 2) {
+            float v[2][2][CN];   // [row of the pair][dim half][member]
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const int n = me + (ri + rr) * gs;
+                const bool okr = ri + rr < R;
+#pragma unroll
+                for (int r = 0; r < CN; r++) {
+                    const bool ok = okr && r < gs;
+                    v[rr][0][r] = ok ? ro[r][n * HD + tid] : 0.0f;
+                    v[rr][1][r] = ok ? ro[r][n * HD + tid + 128] : 0.0f;
+                }
             }
-            float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
-            for (int r = 0; r < gs; r++) {
-                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
-                const float m = rml[n];
-                if (m == -INFINITY) continue;
-                const float wgt = expf(m - M);
-                L = fmaf(rml[NQ + n], wgt, L);
-                const float *ro = cluster.map_shared_rank(obuf, (gb + r) % CN) + n * HD;
-                o0 = fmaf(ro[tid], wgt, o0);
-                o1 = fmaf(ro[tid + 128], wgt, o1);
-            }
-            if (!extends) {
-                const int t = n / P.G, jj = n % P.G;
-                float *o = P.out + (((int64_t)U.s * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
-                const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-                o[tid] = o0 * inv;
-                o[tid + 128] = o1 * inv;
-            } else {
-                slot[n * HD + tid] = o0;
-                slot[n * HD + tid + 128] = o1;
-                if (tid == 0) {
-                    slot[P.nq * HD + n] = M;
-                    slot[P.nq * HD + P.nq + n] = L;
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                if (ri + rr >= R) break;
+                const int n = me + (ri + rr) * gs;
+                float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+                for (int r = 0; r < CN; r++) {
+                    const float wgt = r < gs ? sm.wm[(ri + rr) * CN + r] : 0.0f;
+                    o0 = fmaf(v[rr][0][r], wgt, o0);
+                    o1 = fmaf(v[rr][1][r], wgt, o1);
+                }
+                const float L = sm.rowL[ri + rr];
+                if (!extends) {
+                    const int t = n / P.G, jj = n % P.G;
+                    float *o = P.out + (((int64_t)U.io * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
+                    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+                    o[tid] = o0 * inv;
+                    o[tid + 128] = o1 * inv;
+                } else {
+                    slot[n * HD + tid] = o0;
+                    slot[n * HD + tid + 128] = o1;
+                    if (tid == 0) {
+                        slot[P.nq * HD + n] = sm.rowM[ri + rr];
+                        slot[P.nq * HD + P.nq + n] = L;
+                    }
                 }
             }
         }
@@ -553,39 +624,79 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
     }
     cluster.sync();   // #2: cluster partials written; remote reads of O done
     if (has_unit && extends && me == 0 && tid == 0) {
+        // the group leader counts this cluster in and tells the members whether it was the last
         const int n_cl = (U.pu1 - 1) / CN - U.pu0 / CN + 1;
-        const int old = atomicAdd(&P.counters[U.p], 1);
-        sm.merge_flag = old == n_cl - 1;
+        const int last = atomicAdd(&P.counters[U.p], 1) == n_cl - 1;
+        for (int r = 0; r < gs; r++) *cluster.map_shared_rank(&sm.merge_flag, (gb + r) % CN) = last;
     }
-    cluster.sync();   // #3: the group leader's decision is visible
-    const bool merge = has_unit && extends && *cluster.map_shared_rank(&sm.merge_flag, gb % CN);
-    cluster.sync();   // #4: nobody reads another CTA's shared memory after this point
-    if (!merge) return;
+    cluster.sync();   // #3: the decision is in every member's shared memory; no remote access after this
+    if (!(has_unit && extends && sm.merge_flag)) return;
     // ---- last cluster of an extended pair: merge the per-cluster partials in cluster order -------
+    // Round 1 loads (m, l) of every (owned row, cluster); a warp per row reduces them to weights
+    // in the (now free) tile buffer; round 2 sums the O rows with up to 64 loads in flight.
     __threadfence();
-    const int k_lo = U.pu0 / CN, k_hi = (U.pu1 - 1) / CN;
+    const int k_lo = U.pu0 / CN, k_hi = (U.pu1 - 1) / CN, nc = k_hi - k_lo + 1;
     const int64_t stride = partial_stride(P.nq);
-    for (int n = me; n < P.nq; n += gs) {
+    const float *rec0 = P.partial + (2 * k_lo + (U.pu0 != k_lo * CN ? 1 : 0)) * stride;
+    const float *rec1 = P.partial + 2 * (k_lo + 1) * stride;   // cluster k_lo + c (c >= 1): slot 0
+    auto rec = [&](int c) { return c == 0 ? rec0 : rec1 + (int64_t)(c - 1) * 2 * stride; };
+    float *wm = obuf, *wl = obuf + R * nc;
+    for (int e = tid; e < R * nc; e += 128) {
+        const int ri = e / nc, c = e % nc, n = me + ri * gs;
+        wm[e] = __ldcg(rec(c) + P.nq * HD + n);
+        wl[e] = __ldcg(rec(c) + P.nq * HD + P.nq + n);
+    }
+    __syncthreads();
+    for (int ri = w; ri < R; ri += 4) {
         float M = -INFINITY;
-        for (int kk = k_lo; kk <= k_hi; kk++) {
-            const float *rec = P.partial + (2 * kk + (kk == k_lo && U.pu0 != kk * CN ? 1 : 0)) * stride;
-            M = fmaxf(M, __ldcg(rec + P.nq * HD + n));
+        for (int c = lane; c < nc; c += 32) M = fmaxf(M, wm[ri * nc + c]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        for (int c = lane; c < nc; c += 32) {
+            const float m = wm[ri * nc + c];
+            const float wgt = m == -INFINITY ? 0.0f : expf(m - M);
+            wm[ri * nc + c] = wgt;
+            L = fmaf(wl[ri * nc + c], wgt, L);
         }
-        float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
-        for (int kk = k_lo; kk <= k_hi; kk++) {
-            const float *rec = P.partial + (2 * kk + (kk == k_lo && U.pu0 != kk * CN ? 1 : 0)) * stride;
-            const float m = __ldcg(rec + P.nq * HD + n);
-            if (m == -INFINITY) continue;
-            const float wgt = expf(m - M);
-            L = fmaf(__ldcg(rec + P.nq * HD + P.nq + n), wgt, L);
-            o0 = fmaf(__ldcg(rec + n * HD + tid), wgt, o0);
-            o1 = fmaf(__ldcg(rec + n * HD + tid + 128), wgt, o1);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (lane == 0) sm.rowL[ri] = L;
+    }
+    __syncthreads();
+    for (int ri = 0; ri < R; ri += 4) {
+        float o[4][2] = {};
+        for (int c0 = 0; c0 < nc; c0 += 8) {
+            float v[4][8][2];
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const bool ok = ri + rr < R && c0 + q < nc;
+                    const float *r = rec(ok ? c0 + q : 0) + (me + (ri + rr) * gs) * HD;
+                    v[rr][q][0] = ok ? __ldcg(r + tid) : 0.0f;
+                    v[rr][q][1] = ok ? __ldcg(r + tid + 128) : 0.0f;
+                }
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const float wgt = ri + rr < R && c0 + q < nc ? wm[(ri + rr) * nc + c0 + q] : 0.0f;
+                    o[rr][0] = fmaf(v[rr][q][0], wgt, o[rr][0]);
+                    o[rr][1] = fmaf(v[rr][q][1], wgt, o[rr][1]);
+                }
         }
-        const int t = n / P.G, jj = n % P.G;
-        float *o = P.out + (((int64_t)U.s * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
-        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-        o[tid] = o0 * inv;
-        o[tid + 128] = o1 * inv;
+#pragma unroll
+        for (int rr = 0; rr < 4; rr++) {
+            if (ri + rr >= R) break;
+            const int n = me + (ri + rr) * gs;
+            const float L = sm.rowL[ri + rr];
+            const int t = n / P.G, jj = n % P.G;
+            float *out = P.out + (((int64_t)U.io * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
+            const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+            out[tid] = o[rr][0] * inv;
+            out[tid + 128] = o[rr][1] * inv;
+        }
     }
     if (me == 0 && tid == 0) P.counters[U.p] = 0;   // ready for the next launch
 }
@@ -623,6 +734,49 @@ static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
 
 int decode_max_nq() { return 64; }
 int decode_cluster() { return dec::CN; }
+
+template <int NT>
+static int max_clusters_nt() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cached[dev]) return cached[dev];
+    const size_t smem = sizeof(dec::Smem<NT>);
+    if (cudaFuncSetAttribute(dec::k_decode<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(dec::CN * 64);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = dec::CN;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, dec::k_decode<NT>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cached[dev] = n;
+    return n;
+}
+
+int decode_max_clusters(int nq) {
+    switch ((nq + 7) / 8) {
+        case 1: return max_clusters_nt<1>();
+        case 2: return max_clusters_nt<2>();
+        case 3: return max_clusters_nt<3>();
+        case 4: return max_clusters_nt<4>();
+        case 5: return max_clusters_nt<5>();
+        case 6: return max_clusters_nt<6>();
+        case 7: return max_clusters_nt<7>();
+        case 8: return max_clusters_nt<8>();
+        default: return 0;
+    }
+}
 
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
     switch ((p.nq + 7) / 8) {

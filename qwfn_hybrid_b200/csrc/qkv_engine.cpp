@@ -458,9 +458,10 @@ extern "C" qkv_status qkv_seq_reserve(qkv_engine *eng, int32_t slot, int32_t n_t
     qkv_status r = check_slot(eng, slot);
     if (r != QKV_OK) return r;
     if (n_tokens < 0 || n_tokens > eng->cfg.n_ctx) return fail(eng, QKV_ERR_INVALID, "reserve %d of n_ctx %d", n_tokens, eng->cfg.n_ctx);
-    if (n_tokens == 0) return QKV_OK;
+    const int32_t from = eng->slots[slot].n_past;
+    if (n_tokens <= from) return QKV_OK;
     if (!eng->host_only && (r = use_device(eng)) != QKV_OK) return r;
-    if ((r = reserve(eng, slot, 0, n_tokens, S(stream))) != QKV_OK) return r;
+    if ((r = reserve(eng, slot, from, n_tokens - from, S(stream))) != QKV_OK) return r;
     return flush_tables(eng, S(stream));
 }
 
@@ -538,25 +539,51 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.n_seq = ns;
     P.n_sel = n_sel;
     P.scale = scale;
+    // Units: proportional to tiles, about one wave of co-resident clusters in total.  A pair with
+    // CN or more units gets a multiple of CN and those sequences go first, so their pairs fill
+    // whole clusters (merged in shared memory only where a pair spans clusters).
+    std::vector<int32_t> tiles(ns), units(ns);
     int64_t total = 0;
     for (int i = 0; i < ns; i++) {
-        P.seq_slot[i] = slots[i];
-        P.seq_pos0[i] = pos0[i];
-        P.seq_tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
-        total += (int64_t)H * P.seq_tiles[i];
+        tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
+        total += (int64_t)H * tiles[i];
     }
-    const int64_t target = (int64_t)eng->num_sms * 2;   // two resident CTAs per SM
-    int64_t units = 0;
-    for (int i = 0; i < ns; i++) {
-        int64_t u = (int64_t)((double)P.seq_tiles[i] * target / (double)total + 0.5);
-        u = std::max<int64_t>(1, std::min<int64_t>(u, P.seq_tiles[i]));
-        P.seq_units[i] = (int32_t)u;
-        P.seq_unit0[i] = (int32_t)units;
-        units += u * H;
+    const int max_cl = decode_max_clusters(T * G);
+    const int64_t target = (int64_t)(max_cl > 0 ? max_cl : eng->num_sms / 4) * CN;
+    double scale_u = (double)target / (double)total;
+    int64_t n_units = 0;
+    for (int attempt = 0; attempt < 8; attempt++) {
+        n_units = 0;
+        for (int i = 0; i < ns; i++) {
+            int64_t u = (int64_t)((double)tiles[i] * scale_u);
+            if (u >= CN) u -= u % CN;
+            u = std::max<int64_t>(1, std::min<int64_t>(u, tiles[i]));
+            units[i] = (int32_t)u;
+            n_units += u * H;
+        }
+        if (n_units <= target) break;
+        scale_u *= 0.9 * (double)target / (double)n_units;
     }
-    P.seq_unit0[ns] = (int32_t)units;
-    P.n_units = (int32_t)units;
-    P.n_ctas = (int32_t)((units + CN - 1) / CN * CN);
+    std::vector<int32_t> order(ns);
+    for (int i = 0; i < ns; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+        const bool fa = units[a] % CN == 0 && units[a] >= CN, fb = units[b] % CN == 0 && units[b] >= CN;
+        return fa != fb ? fa : units[a] > units[b];
+    });
+    int64_t acc = 0;
+    for (int j = 0; j < ns; j++) {
+        const int i = order[j];
+        P.seq_idx[j] = i;
+        P.seq_slot[j] = slots[i];
+        P.seq_pos0[j] = pos0[i];
+        P.seq_tiles[j] = tiles[i];
+        P.seq_units[j] = units[i];
+        P.seq_unit0[j] = (int32_t)acc;
+        acc += (int64_t)units[i] * H;
+    }
+    P.seq_unit0[ns] = (int32_t)acc;
+    P.n_units = (int32_t)acc;
+    P.n_ctas = (int32_t)((acc + CN - 1) / CN * CN);
     if ((size_t)2 * (P.n_ctas / CN) * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
         return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small for %d units", P.n_units);
     CK(eng, launch_decode(P, st));

@@ -114,6 +114,8 @@ struct DecodeParams {
     int64_t page_bytes;
     int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_units, n_ctas;
     float   scale;
+    // per plan position j (sequences ordered by units, largest first):
+    int32_t seq_idx[MAX_SEQ];        // the sequence's index in the caller's arrays
     int32_t seq_slot[MAX_SEQ];
     int32_t seq_pos0[MAX_SEQ];
     int32_t seq_tiles[MAX_SEQ];      // tiles of each pair of the sequence
@@ -126,5 +128,6 @@ __host__ __device__ __forceinline__ int64_t partial_stride(int nq) { return (int
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);
 int decode_max_nq();
 int decode_cluster();
+int decode_max_clusters(int nq);   // co-resident clusters of the decode kernel (0 = unknown)
 
 }  // namespace qkv

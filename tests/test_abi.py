@@ -169,3 +169,16 @@ def test_shard_lpt(qkvlib):
     assert qkvlib.shard_lpt([4, 4], 1) == [0, 0]
     with pytest.raises(qkvlib.QkvError):
         qkvlib.shard_lpt([1], 0)
+
+
+def test_reserve_covers_only_future_positions(qkvlib):
+    eng = host_engine(qkvlib, n_pages=8)
+    eng.seq_alloc(0)
+    with pytest.raises(qkvlib.QkvError):
+        eng.append(0, 0, 0, 1, 1, n_rows=512)     # two full pages
+    snap = eng.snapshot_save(0)
+    eng.reserve(0, 700)                            # shared full pages stay shared, one new page
+    assert [eng.refcount(p) for p in eng.pages(0)] == [2, 2, 1] and eng.n_past(0) == 512
+    eng.reserve(0, 100)                            # nothing to do below n_past
+    assert len(eng.pages(0)) == 3
+    snap.release()

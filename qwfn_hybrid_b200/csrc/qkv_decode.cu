@@ -39,7 +39,6 @@ namespace qkv {
 namespace dec {
 
 constexpr int CN = 8;   // CTAs per cluster
-constexpr int NSTAGE = 2;
 constexpr int PSTR   = 80;      // halves per P row in smem (64 tokens + pad: conflict-free LDS.64)
 constexpr int QSTR   = 288;     // bytes per quantised query row (256 + pad)
 constexpr uint32_t MAGIC_I = 0x4B400000u;
@@ -136,20 +135,28 @@ __device__ __forceinline__ int pi16(int m) { return ((m & 6) << 1) | (m & 1) | (
 __device__ __forceinline__ int qperm(int e) { return ((e & 15) >> 2) * 8 + ((e >> 4) << 2) + (e & 3); }
 
 
+// Stages of the tile ring: one 34816-byte stage per CTA keeps 4 CTAs (16 warps) per SM; the
+// O buffer of the epilogue reuses the stages, so wide query groups (NQ > 34) take two.
+template <int NT>
+struct Stages { static constexpr int N = NT * 8 * HD * 4 <= TILE_BYTES ? 1 : 2; };
+
 template <int NT>
 struct Smem {
     static constexpr int NQ = NT * 8;
-    uint8_t  tile[NSTAGE][TILE_BYTES];   // after the tile loop: the unit's O rows [NQ][HD] fp32
+    static constexpr int NS = Stages<NT>::N;
+    uint8_t  tile[NS][TILE_BYTES];       // after the tile loop: the unit's O rows [NQ][HD] fp32
     uint8_t  qq[NQ * QSTR];
     float    qd[NBLK * NQ];
-    float    red[4 * NQ];
-    float    lred[4 * NQ];
+    __half   ps[NQ * PSTR];              // P of the current tile, [row][token]
+    float    red[4 * NQ];                // chunk maxima of warps that outgrew the reference
+    float    lpart[4 * NQ];              // per-warp row sums (epilogue)
+    int32_t  flag[4];                    // warp outgrew the softmax reference in this tile
     float    ml[2 * NQ];                 // the unit's m (natural log domain) and l per row
-    float    wm[(NQ + CN) * CN];         // in-cluster merge: per (owned row, member) m, then weight
-    float    wl[(NQ + CN) * CN];         //                   per (owned row, member) l
+    float    wm[(NQ + CN) * CN];         // in-cluster merge: per (owned row, member) weight
     float    rowM[NQ + CN], rowL[NQ + CN];
-    __half   ps[NQ * PSTR];
-    uint64_t full[NSTAGE];
+    uint64_t full[NS];
+    int32_t  stage_blk[NS];              // block id of the tile in each stage (-1 skip, < -1 error)
+    uint8_t *stage_src[NS];              // its global address (the fused append writes through it)
     int32_t  merge_flag;
 };
 
@@ -206,47 +213,64 @@ __device__ __forceinline__ TileRef tile_ref(const DecodeParams &P, const Unit &U
     return r;
 }
 
-// Producer (one thread): start the copy of the unit's i-th tile into stage i % NSTAGE.
+// One thread: start the copy of the unit's i-th tile into stage i % NS.
 template <int NT>
-__device__ __forceinline__ void issue_tile(const DecodeParams &P, Smem<NT> &sm, const Unit &U, int i) {
-    const TileRef r = tile_ref(P, U, U.t0 + i);
-    uint64_t *bar = &sm.full[i % NSTAGE];
+__device__ __forceinline__ void issue_ref(const DecodeParams &P, Smem<NT> &sm, const TileRef &r, int i) {
+    constexpr int NS = Smem<NT>::NS;
+    uint64_t *bar = &sm.full[i % NS];
+    sm.stage_blk[i % NS] = r.blk;    // published to the consumers by the barrier's completion
+    sm.stage_src[i % NS] = r.src;
     if (r.blk >= 0) {
         fence_proxy_async();
         mbar_expect_tx(bar, TILE_BYTES);
-        bulk_load(sm.tile[i % NSTAGE], r.src, TILE_BYTES, bar);
+        bulk_load(sm.tile[i % NS], r.src, TILE_BYTES, bar);
     } else {
         if (r.blk < -1) atomicOr(P.status, r.blk == -2 ? ST_BAD_INDEX : ST_BAD_PAGE);
         mbar_arrive(bar);
     }
 }
+template <int NT>
+__device__ __forceinline__ void issue_tile(const DecodeParams &P, Smem<NT> &sm, const Unit &U, int i) {
+    issue_ref<NT>(P, sm, tile_ref(P, U, U.t0 + i), i);
+}
 
 // Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h, store
 // them in the cache tile in global memory and in the shared-memory copy.  Warp per 32-element
-// block; the rounding is kernel A's.
+// block, all of a warp's loads issued before the first is used; the rounding is kernel A's.
 __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &U, uint8_t *gtile, uint8_t *stile,
                                              int cell0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int pos0 = P.seq_pos0[U.s];
     const int r0 = max(pos0, cell0), r1 = min(pos0 + P.T, cell0 + TILE_TOK);
-    const int work = (r1 - r0) * NBLK * 2;
-    for (int wi = warp; wi < work; wi += 4) {
+    const int work = (r1 - r0) * NBLK * 2;   // (row, block, K or V) items, at most 4 * 8 * 2
+    constexpr int MAXW = 4 * NBLK * 2 / 4;   // items per warp
+    float x[MAXW];
+#pragma unroll
+    for (int q = 0; q < MAXW; q++) {
+        const int wi = warp + 4 * q;
+        x[q] = 0.0f;
+        if (wi < work) {
+            const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
+            x[q] = (kv ? P.Vnew : P.Knew)[(((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK + lane];
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < MAXW; q++) {
+        const int wi = warp + 4 * q;
+        if (wi >= work) break;   // warp-uniform
         const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
-        const float *src = (kv ? P.Vnew : P.Knew) +
-                           (((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK;
-        const float x = src[lane];
-        float amax = fabsf(x);
+        float amax = fabsf(x[q]);
 #pragma unroll
         for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float d  = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-        const uint8_t q = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x, id));
+        const uint8_t qv = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x[q], id));
         const __half dh = __float2half_rn(d);
         const int t = row - cell0, dim = b * QK + lane;
         const int qo = kv ? v_off(dim, t) : k_off(t, dim);
         const int so = kv ? vd_off(b, t) : kd_off(t, b);
-        stile[qo] = q;
-        gtile[qo] = q;
+        stile[qo] = qv;
+        gtile[qo] = qv;
         if (lane == 0) {
             *reinterpret_cast<__half *>(stile + so) = dh;
             *reinterpret_cast<__half *>(gtile + so) = dh;
@@ -254,9 +278,16 @@ __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &
     }
 }
 
+// CTA = 4 warps, up to 4 CTAs per SM.  Per 64-token tile, warp w computes QK for tokens
+// 16w..16w+15 and PV for dims 64w..64w+63; P crosses between them through shared memory.  The
+// softmax uses a per-row reference held in registers (identical in every warp); a warp whose
+// scores outgrow it by more than 2^4 posts its maximum and the whole CTA moves the reference
+// (rescaling O and the row sums) before PV -- rare after the first tile, so a tile normally costs
+// two barriers: P ready, stage free.
 template <int NT>
-__global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
+__global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodeParams P) {
     constexpr int NQ = NT * 8;
+    constexpr int NS = Smem<NT>::NS;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem<NT> &sm = *reinterpret_cast<Smem<NT> *>(smem_raw);
     cg::cluster_group cluster = cg::this_cluster();
@@ -266,48 +297,57 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
     const bool has_unit = u < P.n_units;
     Unit U{};
     int n_tiles = 0;
-    if (has_unit) {
-        U = unit_of(P, u);
-        n_tiles = U.t1 - U.t0;
-    }
-    if (tid == 0) {
-        for (int s = 0; s < NSTAGE; s++) mbar_init(&sm.full[s], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int i = 0; i < NSTAGE && i < n_tiles; i++) issue_tile<NT>(P, sm, U, i);
-    }
-    float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
-    const float c2 = P.scale * 1.4426950408889634f;        // softmax in base 2
-    bool aborted = false;   // warp-uniform: a tile copy did not land within the wait limit
-    // The units of this unit's pair inside the cluster form a group of gs CTAs (ranks gb..gb+gs-1
-    // mod CN); member `me` owns query rows me, me+gs, ... for the Q quantisation and the merge.
     int gb = 0, gs = 1, me = 0;
     bool extends = false;   // the pair has units in other clusters too
     if (has_unit) {
+        U = unit_of(P, u);
+        n_tiles = U.t1 - U.t0;
         gb = max(U.pu0, k * CN);
         gs = min(U.pu1, (k + 1) * CN) - gb;
         me = u - gb;
         extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
-        // ---- quantise this member's query rows (q8_0, as ggml's CPU path does) ----------------
-        // 32 threads per row, 8 consecutive elements each (4 threads per 32-element block).
+    }
+    float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
+    bool aborted = false;
+
+    if (has_unit) {
+        const int pos0 = P.seq_pos0[U.s];
+        const float c2 = P.scale * 1.4426950408889634f;   // softmax in base 2
+        // ---- query rows: loads first (in flight while thread 0 starts the tile copies) --------
+        // 32 threads per row, 8 elements each (4 threads per 32-element block).
         const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
-        const int rows_mine = (NQ - me + gs - 1) / gs;
-        for (int pass = 0; pass * 4 < rows_mine; pass++) {
-            const int ri = pass * 4 + (tid >> 5), e8 = tid & 31, b = e8 >> 2, sub = e8 & 3;
-            const int n = me + ri * gs;
-            float v[8];
-            if (ri < rows_mine && n < P.nq) {
+        constexpr int QP = (NQ + 3) / 4;   // rows per warp
+        // thread 0 looks up the first tiles' pages before the query loads, so both are in flight
+        TileRef first[NS];
+        if (tid == 0)
+            for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+        float qv[QP][8];
+#pragma unroll
+        for (int it = 0; it < QP; it++) {
+            const int n = it * 4 + w;
+            if (n < P.nq) {
                 const int t = n / P.G, jj = n % P.G;
-                const float4 *src = reinterpret_cast<const float4 *>(qsrc + ((int64_t)t * P.n_head + jj) * HD + e8 * 8);
+                const float4 *src = reinterpret_cast<const float4 *>(qsrc + ((int64_t)t * P.n_head + jj) * HD + lane * 8);
                 const float4 u0 = src[0], u1 = src[1];
-                v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
-                v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+                qv[it][0] = u0.x; qv[it][1] = u0.y; qv[it][2] = u0.z; qv[it][3] = u0.w;
+                qv[it][4] = u1.x; qv[it][5] = u1.y; qv[it][6] = u1.z; qv[it][7] = u1.w;
             } else {
 #pragma unroll
-                for (int q = 0; q < 8; q++) v[q] = 0.0f;
+                for (int q = 0; q < 8; q++) qv[it][q] = 0.0f;
             }
+        }
+        if (tid == 0) {
+            for (int st = 0; st < NS; st++) mbar_init(&sm.full[st], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            for (int st = 0; st < NS && st < n_tiles; st++) issue_ref<NT>(P, sm, first[st], st);
+        }
+        // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row
+#pragma unroll
+        for (int it = 0; it < QP; it++) {
+            const int n = it * 4 + w, b = lane >> 2, sub = lane & 3;
             float amax = 0.0f;
 #pragma unroll
-            for (int q = 0; q < 8; q++) amax = fmaxf(amax, fabsf(v[q]));
+            for (int q = 0; q < 8; q++) amax = fmaxf(amax, fabsf(qv[it][q]));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
             const float d  = __fdiv_rn(amax, 127.0f);
@@ -315,85 +355,60 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
             uint32_t w0 = 0, w1 = 0;
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-                w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[q], id)) << (8 * q);
-                w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[4 + q], id)) << (8 * q);
+                w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][q], id)) << (8 * q);
+                w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][4 + q], id)) << (8 * q);
             }
-            if (ri < rows_mine) {
+            if (n < NQ) {
                 uint8_t *row = sm.qq + n * QSTR + b * 32;
                 *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
                 *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
                 if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
             }
         }
-    }
-    cluster.sync();   // #0: every member's query rows are ready
-    if (has_unit && gs > 1) {
-        // fetch the rows the other members quantised (distributed shared memory, one round)
-        constexpr int CH = QSTR / 16;
-        for (int e = tid; e < NQ * CH; e += 128) {
-            const int n = e / CH, c = e % CH, r = n % gs;
-            if (r == me) continue;
-            const uint4 *src = cluster.map_shared_rank(reinterpret_cast<const uint4 *>(sm.qq + n * QSTR), (gb + r) % CN);
-            reinterpret_cast<uint4 *>(sm.qq + n * QSTR)[c] = src[c];
-        }
-        for (int e = tid; e < NQ * NBLK; e += 128) {
-            const int n = e % NQ, r = n % gs;
-            if (r == me) continue;
-            sm.qd[e] = *cluster.map_shared_rank(&sm.qd[e], (gb + r) % CN);
-        }
-    }
-    cluster.sync();   // #0b: remote rows copied; shared memory of peers no longer read
-
-    if (has_unit) {
-        const int pos0 = P.seq_pos0[U.s];
-        // last visible position of each of this lane's query rows (padding rows: nothing visible)
-        int qlim[NT][2];
+        int qlim[NT][2];    // last visible position of this lane's query rows (padding: none)
+        float mref[NT][2];  // softmax reference per row, log2 domain (the same in every warp)
+        float lsum[NT][2];  // this warp's row sums over its tokens, relative to mref
+        float O[4][NT][4];  // this warp's 64 dims x the query rows
 #pragma unroll
         for (int j = 0; j < NT; j++)
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int n = 8 * j + 2 * tig + e;
                 qlim[j][e] = n < P.nq ? pos0 + n / P.G : -1;
+                mref[j][e] = -INFINITY;
+                lsum[j][e] = 0.0f;
             }
-        // per-lane constants of the QK A fragment (the K row this lane addresses in ldmatrix)
+#pragma unroll
+        for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+            for (int j = 0; j < NT; j++) O[mt][j][0] = O[mt][j][1] = O[mt][j][2] = O[mt][j][3] = 0.0f;
         const int lm = lane & 7, lmat = lane >> 3;
-        const int k_tok = 16 * w + pi16(lm + 8 * (lmat & 1));
+        const int k_tok = 16 * w + pi16(lm + 8 * (lmat & 1));   // K row this lane addresses in ldmatrix
         const int k_key = kswz(k_tok), k_hi = lmat >> 1;
-        const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);
-        const int v_dim0 = 64 * w + 8 * lmat + lm;   // PV A fragment rows (+32 for the second half)
-
-        float m2[NT][2], lsum[NT][2], O[4][NT][4];
-#pragma unroll
-        for (int j = 0; j < NT; j++) {
-            m2[j][0] = m2[j][1] = -INFINITY;
-            lsum[j][0] = lsum[j][1] = 0.0f;
-#pragma unroll
-            for (int mt = 0; mt < 4; mt++) O[mt][j][0] = O[mt][j][1] = O[mt][j][2] = O[mt][j][3] = 0.0f;
-        }
-        __syncthreads();
+        const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);   // tokens of the S rows
+        const int v_dim0 = 64 * w + 8 * lmat + lm;   // V^T row this lane addresses (+32: second block)
+        __syncthreads();   // query rows ready, barriers initialised
 
         for (int i = 0; i < n_tiles; i++) {
-            const int stage = i % NSTAGE;
-            const uint32_t phase = (uint32_t)((i / NSTAGE) & 1);
-            const bool landed = mbar_wait(&sm.full[stage], phase, aborted ? 10000000ull : 2000000000ull);
+            const int stage = i % NS;
+            const bool landed = mbar_wait(&sm.full[stage], (uint32_t)((i / NS) & 1), aborted ? 10000000ull : 2000000000ull);
             aborted = aborted || !__all_sync(0xffffffffu, landed);
-            const TileRef tr = tile_ref(P, U, U.t0 + i);   // the decision the producer made
+            const int blk = sm.stage_blk[stage];
             uint8_t *tile = sm.tile[stage];
-            const bool live = tr.blk >= 0 && !aborted;
-            const int cell0 = tr.blk * TILE_TOK;
-            if (P.Knew && tr.blk >= 0 && cell0 + TILE_TOK > pos0) {   // CTA-uniform
-                fused_append(P, U, tr.src, tile, cell0);
+            const bool live = blk >= 0 && !aborted;
+            const int cell0 = blk * TILE_TOK;
+            if (P.Knew && blk >= 0 && cell0 + TILE_TOK > pos0) {   // uniform over the CTA
+                __syncthreads();
+                fused_append(P, U, sm.stage_src[stage], tile, cell0);
                 __syncthreads();
             }
-            // ---------------- QK for this warp's 16 tokens ----------------------------------
+            // ---------------- QK for this warp's 16 tokens ----------------------------------------
             float S[NT][4];
 #pragma unroll
             for (int j = 0; j < NT; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
             if (live) {
-                const uint4 dkl = *reinterpret_cast<const uint4 *>(tile + TILE_KD + tk_lo * 16);
-                const uint4 dkh = *reinterpret_cast<const uint4 *>(tile + TILE_KD + tk_hi * 16);
-                const __half *dkl_h = reinterpret_cast<const __half *>(&dkl);
-                const __half *dkh_h = reinterpret_cast<const __half *>(&dkh);
+                const __half *dkl_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_lo * 16);
+                const __half *dkh_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_hi * 16);
                 const uint32_t kbase = smem_u32(tile) + k_tok * HD;
 #pragma unroll
                 for (int b = 0; b < NBLK; b++) {
@@ -418,67 +433,97 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                     }
                 }
             }
-            // mask: rows past a query's position, padding rows, skipped tiles
+            // ---------------- mask; does this warp outgrow the reference? -----------------------
             const int clo = cell0 + tk_lo, chi = cell0 + tk_hi;
+            bool over = false;
 #pragma unroll
             for (int j = 0; j < NT; j++) {
                 if (!live || clo > qlim[j][0]) S[j][0] = -INFINITY;
                 if (!live || clo > qlim[j][1]) S[j][1] = -INFINITY;
                 if (!live || chi > qlim[j][0]) S[j][2] = -INFINITY;
                 if (!live || chi > qlim[j][1]) S[j][3] = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < 4; e++) over = over || S[j][e] * c2 > mref[j][e & 1] + 4.0f;
             }
-            // ---------------- tile max across the CTA ---------------------------------------
+            const bool warp_over = __any_sync(0xffffffffu, over);
+            if (warp_over) {
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    float mx0 = fmaxf(S[j][0], S[j][2]), mx1 = fmaxf(S[j][1], S[j][3]);
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+                    }
+                    if (g == 0) {
+                        sm.red[w * NQ + 8 * j + 2 * tig]     = mx0 * c2;
+                        sm.red[w * NQ + 8 * j + 2 * tig + 1] = mx1 * c2;
+                    }
+                }
+            }
+            if (lane == 0) sm.flag[w] = warp_over;
+            // P relative to the current reference (rewritten below if the reference moves)
+            float psum[NT][2];
 #pragma unroll
             for (int j = 0; j < NT; j++) {
-                float mx0 = fmaxf(S[j][0], S[j][2]), mx1 = fmaxf(S[j][1], S[j][3]);
-#pragma unroll
-                for (int o = 4; o < 32; o <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-                }
-                if (g == 0) {
-                    sm.red[w * NQ + 8 * j + 2 * tig]     = mx0;
-                    sm.red[w * NQ + 8 * j + 2 * tig + 1] = mx1;
-                }
-            }
-            __syncthreads();
-            // every warp is past the previous tile: its stage can be refilled
-            if (tid == 0 && i >= 1 && i + NSTAGE - 1 < n_tiles) issue_tile<NT>(P, sm, U, i + NSTAGE - 1);
-            float alpha[NT][2];
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const int n = 8 * j + 2 * tig + e;
-                    const float tm =
-                        fmaxf(fmaxf(sm.red[n], sm.red[NQ + n]), fmaxf(sm.red[2 * NQ + n], sm.red[3 * NQ + n]));
-                    const float mnew = fmaxf(m2[j][e], tm * c2);
-                    alpha[j][e] = mnew == -INFINITY ? 1.0f : exp2f(m2[j][e] - mnew);
-                    m2[j][e] = mnew;
-                }
                 float pr[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float mm = m2[j][e & 1];
+                    const float mm = mref[j][e & 1];
                     pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
                 }
-                lsum[j][0] = fmaf(lsum[j][0], alpha[j][0], pr[0] + pr[2]);
-                lsum[j][1] = fmaf(lsum[j][1], alpha[j][1], pr[1] + pr[3]);
-                const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));   // tokens 4tig, 4tig+1 of row 8j+g
-                const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));   // tokens 4tig+2, 4tig+3
-                *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
+                psum[j][0] = pr[0] + pr[2];
+                psum[j][1] = pr[1] + pr[3];
+                if (!warp_over) {
+                    const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));   // tokens 4tig, 4tig+1 of row 8j+g
+                    const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));   // tokens 4tig+2, 4tig+3
+                    *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
+                }
             }
-#pragma unroll
-            for (int mt = 0; mt < 4; mt++)
+            __syncthreads();   // barrier 1: P (or the posted maxima) of every warp are in shared memory
+            if (sm.flag[0] | sm.flag[1] | sm.flag[2] | sm.flag[3]) {
+                // ---- the reference moves: new reference, rescale O and sums, rewrite every P -------
 #pragma unroll
                 for (int j = 0; j < NT; j++) {
-                    const float2 al = make_float2(alpha[j][0], alpha[j][1]);
-                    const float2 o01 = __fmul2_rn(make_float2(O[mt][j][0], O[mt][j][1]), al);
-                    const float2 o23 = __fmul2_rn(make_float2(O[mt][j][2], O[mt][j][3]), al);
-                    O[mt][j][0] = o01.x; O[mt][j][1] = o01.y; O[mt][j][2] = o23.x; O[mt][j][3] = o23.y;
+                    float alpha[2];
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int n = 8 * j + 2 * tig + e;
+                        float mn = mref[j][e];
+#pragma unroll
+                        for (int ww = 0; ww < 4; ww++)
+                            if (sm.flag[ww]) mn = fmaxf(mn, sm.red[ww * NQ + n]);
+                        alpha[e] = mref[j][e] == -INFINITY ? 0.0f : exp2f(mref[j][e] - mn);
+                        mref[j][e] = mn;
+                        lsum[j][e] *= alpha[e];
+                    }
+                    const float2 al = make_float2(alpha[0], alpha[1]);
+#pragma unroll
+                    for (int mt = 0; mt < 4; mt++) {
+                        const float2 o01 = __fmul2_rn(make_float2(O[mt][j][0], O[mt][j][1]), al);
+                        const float2 o23 = __fmul2_rn(make_float2(O[mt][j][2], O[mt][j][3]), al);
+                        O[mt][j][0] = o01.x; O[mt][j][1] = o01.y; O[mt][j][2] = o23.x; O[mt][j][3] = o23.y;
+                    }
+                    float pr[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float mm = mref[j][e & 1];
+                        pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
+                    }
+                    psum[j][0] = pr[0] + pr[2];
+                    psum[j][1] = pr[1] + pr[3];
+                    const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));
+                    const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));
+                    *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
                 }
-            __syncthreads();
-            // ---------------- PV for this warp's 64 dims ------------------------------------
+                __syncthreads();   // rewritten P visible
+            }
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                lsum[j][0] += psum[j][0];
+                lsum[j][1] += psum[j][1];
+            }
+            // ---------------- PV for this warp's 64 dims ------------------------------------------
             if (live) {
                 const uint32_t vbase = smem_u32(tile) + TILE_VQ;
 #pragma unroll
@@ -492,9 +537,9 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                     }
 #pragma unroll
                     for (int bb = 0; bb < 2; bb++) {   // the warp's two q8_0 blocks (32 dims each)
-                        const int blk = 2 * w + bb;
+                        const int blkv = 2 * w + bb;
                         const uint2 dv =
-                            *reinterpret_cast<const uint2 *>(tile + TILE_VD + (blk * TILE_TOK + 16 * kk + 4 * tig) * 2);
+                            *reinterpret_cast<const uint2 *>(tile + TILE_VD + (blkv * TILE_TOK + 16 * kk + 4 * tig) * 2);
                         uint32_t alo[2], ahi[2], blo[2], bhi[2];
                         s8x4_to_f16(va[4 * bb + 0], alo[0], ahi[0]);
                         s8x4_to_f16(va[4 * bb + 1], alo[1], ahi[1]);
@@ -502,8 +547,7 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                         s8x4_to_f16(va[4 * bb + 3], blo[1], bhi[1]);
 #pragma unroll
                         for (int j = 0; j < NT; j++) {
-                            const uint2 pb =
-                                *reinterpret_cast<const uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * kk + 4 * tig]);
+                            const uint2 pb = *reinterpret_cast<const uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * kk + 4 * tig]);
                             const uint32_t b0 = hmul2(pb.x, dv.x), b1 = hmul2(pb.y, dv.y);
                             mma_f16(O[2 * bb][j], alo[0], alo[1], ahi[0], ahi[1], b0, b1);
                             mma_f16(O[2 * bb + 1][j], blo[0], blo[1], bhi[0], bhi[1], b0, b1);
@@ -511,8 +555,10 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                     }
                 }
             }
+            __syncthreads();   // barrier 2: the stage and P are free
+            if (tid == 0 && i + NS < n_tiles) issue_tile<NT>(P, sm, U, i + NS);
         }
-        // ---------------- unit epilogue: row sums; O, m, l into shared memory ---------------------
+        // ---------------- unit epilogue: O, m, l into shared memory ------------------------------
 #pragma unroll
         for (int j = 0; j < NT; j++)
 #pragma unroll
@@ -520,9 +566,8 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                 float v = lsum[j][e];
 #pragma unroll
                 for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (g == 0) sm.lred[w * NQ + 8 * j + 2 * tig + e] = v;
+                if (g == 0) sm.lpart[w * NQ + 8 * j + 2 * tig + e] = v;
             }
-        __syncthreads();   // all tile reads done: the stages become the O buffer
 #pragma unroll
         for (int j = 0; j < NT; j++)
 #pragma unroll
@@ -534,11 +579,18 @@ __global__ void __launch_bounds__(128, 2) k_decode(const DecodeParams P) {
                     obuf[n * HD + d0]     = O[mt][j][e];
                     obuf[n * HD + d0 + 8] = O[mt][j][2 + e];
                 }
-                if (w == 0 && g == 0) {
-                    sm.ml[n]      = m2[j][e] == -INFINITY ? -INFINITY : m2[j][e] * 0.6931471805599453f;
-                    sm.ml[NQ + n] = sm.lred[n] + sm.lred[NQ + n] + sm.lred[2 * NQ + n] + sm.lred[3 * NQ + n];
-                }
             }
+        __syncthreads();
+        if (w == 0 && g == 0) {
+#pragma unroll
+            for (int j = 0; j < NT; j++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int n = 8 * j + 2 * tig + e;
+                    sm.ml[n] = mref[j][e] == -INFINITY ? -INFINITY : mref[j][e] * 0.6931471805599453f;
+                    sm.ml[NQ + n] = sm.lpart[n] + sm.lpart[NQ + n] + sm.lpart[2 * NQ + n] + sm.lpart[3 * NQ + n];
+                }
+        }
         if (aborted && lane == 0) atomicOr(P.status, ST_TIMEOUT);
     }
     cluster.sync();   // #1: every unit's O, m, l visible to the cluster

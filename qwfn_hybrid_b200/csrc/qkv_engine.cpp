@@ -556,8 +556,9 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
         n_units = 0;
         for (int i = 0; i < ns; i++) {
             int64_t u = (int64_t)((double)tiles[i] * scale_u);
+            u = std::min<int64_t>(u, tiles[i] / 2);   // at least two tiles per unit
             if (u >= CN) u -= u % CN;
-            u = std::max<int64_t>(1, std::min<int64_t>(u, tiles[i]));
+            u = std::max<int64_t>(1, u);
             units[i] = (int32_t)u;
             n_units += u * H;
         }

@@ -240,6 +240,20 @@ typedef struct qkv_cache_view {
 } qkv_cache_view;
 qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, qkv_cache_view *view);
 
+/* Allocation-free dense decode.  No counterpart in the reference: it exists for callers that must
+ * not allocate device memory -- a custom op inside ggml's graph executor (memory planned ahead by
+ * ggml-alloc, nothing may grow mid-graph) or code under an allocator that owns the whole device.
+ * Same attention as qkv_attn_decode over a cache described by a qkv_cache_view (from
+ * qkv_cache_view_get; block_table has n_slots rows), Q/out device F32 [n_seq][T][n_head][head_dim].
+ * The split-K scratch is a fixed 2.02 MiB array compiled into the library (held on every GPU that
+ * loads it until exit), so T * n_head / n_head_kv must be <= 32 (else QKV_ERR_UNSUPPORTED).
+ * Calls share that array: calls that overlap on the GPU race.  The first call on a device looks
+ * up the array's address and should come before any stream capture.  Bounds violations seen by
+ * the kernel are not reported by this entry point. */
+qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t n_slots, const int32_t *slots,
+                                  const int32_t *pos0, int32_t n_seq, int32_t n_head, const float *Q,
+                                  int32_t T, float scale, float *out, void *stream);
+
 /* Reads (and clears) the device status word that checked kernels write on a bounds violation.
  * Synchronises the stream. */
 qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code);

@@ -26,7 +26,7 @@ EXPORTS = [
     "qkv_gather_rows", "qkv_read_rows", "qkv_write_rows", "qkv_attn_prefill", "qkv_snapshot_save",
     "qkv_snapshot_restore", "qkv_snapshot_restore_many", "qkv_snapshot_release", "qkv_snapshot_info",
     "qkv_snapshot_to_host", "qkv_snapshot_from_host", "qkv_rollback", "qkv_rollback_arm", "qkv_state_ptr",
-    "qkv_cache_view_get", "qkv_device_status", "qkv_launch_count", "qkv_shard_lpt",
+    "qkv_cache_view_get", "qkv_attn_decode_static", "qkv_device_status", "qkv_launch_count", "qkv_shard_lpt",
 ]
 
 

@@ -28,8 +28,11 @@
 // Optional fused append (dense only): the unit owning a tile that holds one of the T new
 // positions quantises those rows (kernel A's rounding), stores them in the cache and patches its
 // shared-memory copy of the tile before use.
+#include "qkv.h"
 #include "qkv_internal.h"
 
+#include <algorithm>
+#include <cstring>
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
@@ -845,3 +848,138 @@ cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
 }
 
 }  // namespace qkv
+
+// ============================================================================================
+// Allocation-free decode: qkv_attn_decode_static (include/qkv.h).
+//
+// For callers that must not allocate device memory -- e.g. a custom op running inside ggml's
+// graph executor, whose memory is planned ahead by ggml-alloc and may not grow mid-graph, or code
+// running under an allocator that owns all of the device's memory.  The kernel's split-K scratch
+// lives in the file-scope arrays below (2.02 MiB of partial records + pair counters), allocated
+// once by the CUDA module on every GPU that loads the library and held until exit.  Every call
+// shares them: calls that overlap on the GPU race; the counters are cleared at the start of
+// every call.
+// ============================================================================================
+namespace qkv {
+namespace stat {
+
+constexpr int MAX_NQ       = 32;   // query rows per KV head (T * n_head / n_head_kv)
+constexpr int MAX_CLUSTERS = 32;   // clusters of 8 CTAs per launch
+constexpr int64_t PARTIAL_FLOATS = 2LL * MAX_CLUSTERS * (MAX_NQ * HD + 2 * MAX_NQ);
+
+static __device__ __align__(256) float   g_partial[PARTIAL_FLOATS];
+static __device__ __align__(256) int32_t g_counters[MAX_PAIRS];
+static __device__ __align__(256) int32_t g_status[64];
+
+struct Scratch {
+    float   *partial  = nullptr;
+    int32_t *counters = nullptr;
+    int32_t *status   = nullptr;
+};
+
+// Device addresses of the arrays for the current device, resolved once per device.  In host
+// code the arrays' names are host-side stand-ins, never device addresses.
+static cudaError_t scratch_for_current_device(Scratch &out) {
+    static Scratch cached[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!cached[dev].partial) {
+        Scratch s;
+        if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.partial), g_partial)) != cudaSuccess) return e;
+        if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.counters), g_counters)) != cudaSuccess) return e;
+        if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.status), g_status)) != cudaSuccess) return e;
+        cached[dev] = s;
+    }
+    out = cached[dev];
+    return cudaSuccess;
+}
+
+}  // namespace stat
+}  // namespace qkv
+
+extern "C" qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t n_slots, const int32_t *slots,
+                                             const int32_t *pos0, int32_t n_seq, int32_t n_head, const float *Q,
+                                             int32_t T, float scale, float *out, void *stream) {
+    using namespace qkv;
+    if (!view || !view->pool || !view->block_table || !slots || !pos0 || !Q || !out || n_seq < 1 || n_slots < 1)
+        return QKV_ERR_INVALID;
+    const int H = view->n_head_kv;
+    if (view->head_dim != HD || view->page_tokens != PAGE_TOK || view->tile_tokens != TILE_TOK ||
+        view->tile_bytes != (size_t)TILE_BYTES || view->page_bytes != (size_t)H * TILES_PER_PAGE * TILE_BYTES ||
+        H < 1 || H > 8 || n_head < 1 || n_head % H || T < 1 || T > 4 || view->n_pages < 1 || view->max_pages_per_seq < 1)
+        return QKV_ERR_INVALID;
+    const int G = n_head / H;
+    if (T * G > stat::MAX_NQ) return QKV_ERR_UNSUPPORTED;   // beyond the static scratch: T*n_head/n_head_kv <= 32
+    for (int i = 0; i < n_seq; i++)
+        if (slots[i] < 0 || slots[i] >= n_slots || pos0[i] < 0 ||
+            (int64_t)pos0[i] + T > (int64_t)view->max_pages_per_seq * PAGE_TOK)
+            return QKV_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    stat::Scratch sc;
+    if (stat::scratch_for_current_device(sc) != cudaSuccess) return QKV_ERR_CUDA;
+    if (cudaMemsetAsync(sc.counters, 0, sizeof(int32_t) * MAX_PAIRS, st) != cudaSuccess ||
+        cudaMemsetAsync(sc.status, 0, sizeof(int32_t), st) != cudaSuccess)
+        return QKV_ERR_CUDA;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return QKV_ERR_CUDA;
+    const int CN = decode_cluster();
+    int max_cl = decode_max_clusters(T * G);
+    if (max_cl <= 0) max_cl = sms / 4;
+    max_cl = max_cl < stat::MAX_CLUSTERS ? max_cl : stat::MAX_CLUSTERS;
+    const int64_t target = (int64_t)max_cl * CN;
+    // sequences per launch: every pair needs at least one unit within the cluster budget
+    const int per_launch = (int)std::min<int64_t>(MAX_SEQ, std::max<int64_t>(1, target / H));
+    for (int base = 0; base < n_seq; base += per_launch) {
+        const int ns = n_seq - base < per_launch ? n_seq - base : per_launch;
+        DecodeParams P;
+        memset(&P, 0, sizeof P);
+        P.pool = static_cast<const uint8_t *>(view->pool);
+        P.block_table = view->block_table;
+        P.Q = Q + (size_t)base * T * n_head * HD;
+        P.out = out + (size_t)base * T * n_head * HD;
+        P.partial = sc.partial;
+        P.counters = sc.counters;
+        P.status = sc.status;
+        P.page_bytes = (int64_t)view->page_bytes;
+        P.n_pages = view->n_pages;
+        P.max_pages = view->max_pages_per_seq;
+        P.n_head = n_head;
+        P.n_head_kv = H;
+        P.G = G;
+        P.T = T;
+        P.nq = T * G;
+        P.n_seq = ns;
+        P.scale = scale;
+        int64_t total = 0;
+        int32_t tiles[MAX_SEQ], units[MAX_SEQ];
+        for (int i = 0; i < ns; i++) {
+            tiles[i] = (pos0[base + i] + T + TILE_TOK - 1) / TILE_TOK;
+            total += (int64_t)H * tiles[i];
+        }
+        int64_t acc = 0;
+        for (int i = 0; i < ns; i++) {   // units in proportion to tiles, >= 1, whole clusters <= budget
+            int64_t u = (int64_t)((double)tiles[i] * (double)(target - (int64_t)ns * H) / (double)total);
+            u = std::min<int64_t>(u, tiles[i] / 2);
+            u = std::max<int64_t>(1, u);
+            units[i] = (int32_t)u;
+        }
+        for (int i = 0; i < ns; i++) {
+            P.seq_idx[i] = i;
+            P.seq_slot[i] = slots[base + i];
+            P.seq_pos0[i] = pos0[base + i];
+            P.seq_tiles[i] = tiles[i];
+            P.seq_units[i] = units[i];
+            P.seq_unit0[i] = (int32_t)acc;
+            acc += (int64_t)units[i] * H;
+        }
+        P.seq_unit0[ns] = (int32_t)acc;
+        P.n_units = (int32_t)acc;
+        P.n_ctas = (int32_t)((acc + CN - 1) / CN * CN);
+        if (P.n_ctas / CN > stat::MAX_CLUSTERS) return QKV_ERR_UNSUPPORTED;
+        if (launch_decode(P, st) != cudaSuccess) return QKV_ERR_CUDA;
+    }
+    return QKV_OK;
+}

@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
                     help="cfg2 (default, the headline line): BASELINE configs[1]; cfg5: configs[4]")
+    ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
 
@@ -362,7 +363,7 @@ def run_cfg5(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import qwfn_hybrid_b200 as Q
-    ctx = config5_contexts()
+    ctx = config5_contexts()[:args.seqs]
     owner = Q.shard_lpt(ctx, ws)
     mine = [i for i in range(len(ctx)) if owner[i] == rank]
     n = len(mine)
@@ -464,8 +465,8 @@ def run_cfg5(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
         "data": "synthetic N(0,1) (torch Philox, seed 4+1000*rank); contexts from numpy default_rng(4)",
-        "config": {"workload": "configs[4]: 64 ragged sequences (ctx 1219..61356, sum 1300814), 12 layers, paged "
-                               "256-token pages, 8192-token shared-prefix snapshot, T=1",
+        "config": {"workload": f"configs[4]: {len(ctx)} of 64 ragged sequences (ctx 1219..61356, sum 1300814 for all "
+                               "64), 12 layers, paged 256-token pages, 8192-token shared-prefix snapshot, T=1",
                    "parallelism": f"sequence-sharded x{ws} (LPT by context, no collective)",
                    "l2": "inputs larger than L2 (17 GB of KV per step)"},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,

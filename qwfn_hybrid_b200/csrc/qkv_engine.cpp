@@ -10,6 +10,7 @@
 #include "qkv_internal.h"
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -72,6 +73,12 @@ struct qkv_engine {
     size_t    partial_bytes = 0;
     int32_t  *d_counters = nullptr;   // kernel C: per-pair arrival counters (zero between launches)
     int32_t  *d_status  = nullptr;
+    // kernel D scratch, allocated by the first prefill call
+    uint8_t  *d_pf_q        = nullptr;    // query tiles
+    float    *d_pf_partial  = nullptr;    // split-segment partials
+    int32_t  *d_pf_counters = nullptr;    // [tiles][4]
+    int32_t  *d_pf_plan     = nullptr;    // segments, tile parts, CTA offsets
+    int32_t   pf_max_tiles = 0, pf_max_parts = 0, pf_plan_ints = 0;
     size_t    device_bytes = 0;
 
     // pinned upload ring for block-table rows: a block is reused only after its event fired
@@ -274,6 +281,10 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_partial);
     cudaFree(eng->d_counters);
     cudaFree(eng->d_status);
+    cudaFree(eng->d_pf_q);
+    cudaFree(eng->d_pf_partial);
+    cudaFree(eng->d_pf_counters);
+    cudaFree(eng->d_pf_plan);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
         if (ev) cudaEventDestroy(ev);
@@ -795,11 +806,154 @@ extern "C" qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slo
 }
 
 // ---------------------------------------------------------------------------------- prefill
+// Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); tile t needs KV tiles
+// 0 .. nk[t]-1 (causal: up to its last query's position).  The flattened sequence of all
+// (tile, KV tile) pairs is cut into n_ctas equal runs; each run is a list of segments.  A tile
+// covered by more than one segment gets one partial record per segment.
+struct PfPlan {
+    std::vector<int32_t> segs;        // 4 per segment: tile, kt0, kt1, part
+    std::vector<int32_t> tile_parts;  // 2 per tile: parts, first part
+    std::vector<int32_t> cta_seg;     // n_ctas + 1
+    int32_t n_parts = 0, max_parts = 0;
+};
+static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPlan &pl) {
+    const int n_tiles = (int)nk.size();
+    pl.segs.clear();
+    pl.cta_seg.assign(n_ctas + 1, 0);
+    std::vector<int32_t> count(n_tiles, 0);
+    int t = 0, off = 0;
+    for (int c = 0; c < n_ctas; c++) {
+        pl.cta_seg[c] = (int32_t)(pl.segs.size() / 4);
+        int64_t left = W * (c + 1) / n_ctas - W * c / n_ctas;
+        while (left > 0) {
+            const int n = (int)std::min<int64_t>(left, nk[t] - off);
+            pl.segs.insert(pl.segs.end(), {t, off, off + n, -1});
+            count[t]++;
+            left -= n;
+            off += n;
+            if (off == nk[t]) {
+                t++;
+                off = 0;
+            }
+        }
+    }
+    pl.cta_seg[n_ctas] = (int32_t)(pl.segs.size() / 4);
+    pl.tile_parts.assign(2 * n_tiles, 0);
+    pl.n_parts = 0;
+    pl.max_parts = 0;
+    for (int i = 0; i < n_tiles; i++) {
+        pl.max_parts = std::max(pl.max_parts, count[i]);
+        pl.tile_parts[2 * i] = count[i];
+        pl.tile_parts[2 * i + 1] = count[i] > 1 ? pl.n_parts : -1;
+        if (count[i] > 1) pl.n_parts += count[i];
+    }
+    std::vector<int32_t> next(n_tiles, 0);
+    for (size_t i = 0; i < pl.segs.size(); i += 4) {
+        const int tile = pl.segs[i];
+        if (count[tile] > 1) pl.segs[i + 3] = pl.tile_parts[2 * tile + 1] + next[tile]++;
+    }
+}
+
+static qkv_status pf_scratch(qkv_engine *eng) {
+    if (eng->d_pf_q) return QKV_OK;
+    const int G = eng->cfg.n_head / eng->cfg.n_head_kv, tpt = PF_ROWS / G;
+    eng->pf_max_tiles = eng->cfg.n_head_kv * ((PF_MAX_TC + tpt - 1) / tpt);
+    eng->pf_max_parts = 2 * eng->num_sms;   // every CTA boundary splits at most one tile in two
+    eng->pf_plan_ints = 4 * (eng->pf_max_tiles + eng->num_sms) + 2 * eng->pf_max_tiles + eng->num_sms + 1;
+    qkv_status r = dalloc(eng, eng->d_pf_q, (size_t)eng->pf_max_tiles * PF_QTILE, "prefill query tiles");
+    if (r == QKV_OK)
+        r = dalloc(eng, eng->d_pf_partial, (size_t)eng->pf_max_parts * pf_part_floats() * 4, "prefill partials");
+    if (r == QKV_OK) r = dalloc(eng, eng->d_pf_counters, (size_t)eng->pf_max_tiles * 4 * 4, "prefill counters");
+    if (r == QKV_OK) r = dalloc(eng, eng->d_pf_plan, (size_t)eng->pf_plan_ints * 4, "prefill plan");
+    if (r == QKV_OK) CK(eng, cudaMemset(eng->d_pf_counters, 0, (size_t)eng->pf_max_tiles * 4 * 4));
+    if (r != QKV_OK) {
+        cudaFree(eng->d_pf_q);
+        cudaFree(eng->d_pf_partial);
+        cudaFree(eng->d_pf_counters);
+        cudaFree(eng->d_pf_plan);
+        eng->d_pf_q = nullptr;
+        eng->d_pf_partial = nullptr;
+        eng->d_pf_counters = nullptr;
+        eng->d_pf_plan = nullptr;
+    }
+    return r;
+}
+
 extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const uint16_t *Q,
                                        int32_t Tc, float scale, float *out, void *stream) {
-    (void)layer; (void)slot; (void)pos0; (void)Q; (void)Tc; (void)scale; (void)out; (void)stream;
     if (!eng) return QKV_ERR_INVALID;
-    return fail(eng, QKV_ERR_UNSUPPORTED, "prefill attention is not built yet");
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H;
+    if (!Q || !out || Tc < 1 || Tc > PF_MAX_TC || pos0 < 0 || !std::isfinite(scale))
+        return fail(eng, QKV_ERR_INVALID, "prefill: Q=%p out=%p Tc=%d (1..%d) pos0=%d", (const void *)Q, (void *)out, Tc,
+                    PF_MAX_TC, pos0);
+    if (PF_ROWS % G) return fail(eng, QKV_ERR_UNSUPPORTED, "prefill: q-heads per KV head %d must divide %d", G, PF_ROWS);
+    const qkv_engine::Slot &sl = eng->slots[slot];
+    if ((int64_t)pos0 + Tc > sl.n_past)
+        return fail(eng, QKV_ERR_STATE, "prefill: positions %d..%d not appended (slot %d holds %d)", pos0, pos0 + Tc - 1,
+                    slot, sl.n_past);
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    if ((r = pf_scratch(eng)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
+
+    const int tpt = PF_ROWS / G, n_groups = (Tc + tpt - 1) / tpt, n_tiles = H * n_groups;
+    std::vector<int32_t> nk(n_tiles);
+    int64_t W = 0;
+    for (int t = 0; t < n_tiles; t++) {
+        const int g = t % n_groups, last_tok = std::min((g + 1) * tpt, Tc) - 1;
+        nk[t] = (pos0 + last_tok) / TILE_TOK + 1;
+        W += nk[t];
+    }
+    PfPlan pl;
+    int n_ctas = (int)std::min<int64_t>(eng->num_sms, W);
+    for (;;) {
+        pf_build(nk, W, n_ctas, pl);
+        if (pl.max_parts <= PF_MAX_PARTS || n_ctas == 1) break;
+        n_ctas = std::max(1, n_ctas * 3 / 4);
+    }
+    if (pl.n_parts > eng->pf_max_parts || pl.max_parts > PF_MAX_PARTS)
+        return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %d parts (max %d), %d per tile", pl.n_parts, eng->pf_max_parts,
+                    pl.max_parts);
+    std::vector<int32_t> ints;
+    ints.reserve(pl.segs.size() + pl.tile_parts.size() + pl.cta_seg.size());
+    ints.insert(ints.end(), pl.segs.begin(), pl.segs.end());
+    const size_t off_tiles = ints.size();
+    ints.insert(ints.end(), pl.tile_parts.begin(), pl.tile_parts.end());
+    const size_t off_cta = ints.size();
+    ints.insert(ints.end(), pl.cta_seg.begin(), pl.cta_seg.end());
+    if ((int64_t)ints.size() > eng->pf_plan_ints) return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %zu ints", ints.size());
+    if ((r = upload_i32(eng, ints, eng->d_pf_plan, S(stream))) != QKV_OK) return r;
+
+    PrefillParams P;
+    memset(&P, 0, sizeof P);
+    P.pool = eng->pools[layer];
+    P.bt = eng->d_bt + (size_t)slot * eng->max_pages;
+    P.Q = Q;
+    P.qtiles = eng->d_pf_q;
+    P.out = out;
+    P.partial = eng->d_pf_partial;
+    P.counters = eng->d_pf_counters;
+    P.status = eng->d_status;
+    P.segs = reinterpret_cast<const int4 *>(eng->d_pf_plan);
+    P.tile_parts = reinterpret_cast<const int2 *>(eng->d_pf_plan + off_tiles);
+    P.cta_seg = eng->d_pf_plan + off_cta;
+    P.page_bytes = eng->page_bytes;
+    P.n_pages = eng->n_pages;
+    P.max_pages = eng->max_pages;
+    P.n_head = eng->cfg.n_head;
+    P.n_head_kv = H;
+    P.G = G;
+    P.tpt = tpt;
+    P.n_groups = n_groups;
+    P.n_tiles = n_tiles;
+    P.Tc = Tc;
+    P.pos0 = pos0;
+    P.n_kv = pos0 + Tc;
+    P.n_ctas = n_ctas;
+    P.scale_log2 = scale * 1.4426950408889634f;
+    CK(eng, launch_prefill(P, S(stream)));
+    return QKV_OK;
 }
 
 // -------------------------------------------------------------------------------- snapshots

@@ -1,0 +1,603 @@
+// qkv_prefill.cu -- kernel D: chunked causal prefill attention over the paged q8_0 cache on the
+// 5th-generation tensor cores (tcgen05.mma kind::f16, fp32 accumulators in tensor memory).
+//
+// Semantics follow ggml's CPU flash_attn_ext with q8_0 K/V (the reference's prefill call,
+// src/qwfn_graph.cpp:417-476, with the causal mask of src/qwfn_engine.cpp:1238-1274): every query
+// row is quantised to q8_0 (ggml's quantize_row_q8_0 rounding), scores are q.k * scale, softmax
+// in fp32, V dequantised.  On the tensor cores the operands are fp16: a query element becomes
+// fp16(d_q * q) and a cache element fp16(d * q) (one rounding each; the int8 and fp16 scale are
+// exact), products accumulate in fp32.
+//
+// Tile: 128 rows = (128 / G) query tokens x the G q-heads sharing one KV head, so each K/V tile
+// is dequantised once for all of them.  A CTA (16 warps, one per SM) runs a contiguous run of
+// segments (tile, KV range) from a host plan that gives every CTA the same number of KV tiles.
+//   warp 0      TMEM allocation; one thread issues all MMAs and the query-tile bulk copies
+//   warps 4-7   softmax: thread r owns row r (TMEM lane r): S row from TMEM, causal mask,
+//               online softmax with a lazily raised reference max (O in TMEM rescaled only when
+//               the row max grows by more than 2^8), P as fp16 into shared memory
+//   warps 8-15  producers: read q8_0 K/V tiles from the pages, dequantise to fp16 into the
+//               128-byte-swizzled K-major layouts the MMAs read
+// Per KV tile j (stage s = j % 2):  S[s] = Q K_j^T  (M128 N64 K256: 16 MMAs),  then after the
+// softmax wrote P_j:  O += P_j V_j  (M128 N256 K64: 4 MMAs).  S_{j+1} is issued before PV_j so
+// the tensor core works while the softmax runs.  Every wait is bounded (ST_TIMEOUT, then all
+// roles leave their loops, the issuing thread drains its MMAs and the CTA frees its TMEM).
+#include "qkv.h"
+#include "qkv_internal.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace qkv {
+namespace pf {
+
+constexpr int NTHR = 512;
+constexpr int KT   = TILE_TOK;         // keys per KV tile
+// shared memory map, offsets from a 1024-byte aligned base
+constexpr int SM_Q   = 0;              // [4 k-atoms][128 rows][128 B]
+constexpr int SM_K   = 65536;          // 2 stages x [4 k-atoms][64 keys][128 B]
+constexpr int SM_V   = 131072;         // 2 stages x [256 dims][128 B] (64 keys)
+constexpr int SM_P   = 196608;         // 2 x [128 rows][128 B] (64 keys)
+constexpr int SM_BAR = 229376;
+constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+// tensor memory columns
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
+constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
+
+struct Bars {
+    uint64_t kv_full[2];    // producers (256 arrivals): K_j and V_j in stage s
+    uint64_t pv_done[2];    // commit after PV_j: stage s and P buffer s free, O holds tile j
+    uint64_t s_full[2];     // commit after S_j
+    uint64_t s_empty[2];    // softmax (128 arrivals): S buffer read
+    uint64_t p_full[2];     // softmax (128 arrivals): P_j written (and O rescaled)
+    uint64_t q_full;        // query tile landed (expect_tx)
+    uint64_t q_empty;       // commit after the last S of a segment
+    uint64_t drain;         // commit before exit
+    uint32_t tmem;
+    int32_t  abort;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for the phase of `parity` to complete.  Returns false when another role aborted or the
+// wait ran past WAIT_NS (then it raises the abort flag and ST_TIMEOUT itself).
+__device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars *B, int32_t *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 32; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*(volatile int32_t *)&B->abort) return false;
+        if (global_ns() - t0 > WAIT_NS) {
+            *(volatile int32_t *)&B->abort = 1;
+            atomicOr(status, ST_TIMEOUT);
+            return false;
+        }
+    }
+}
+// Bounded wait that ignores the abort flag (draining in-flight asynchronous work before exit).
+__device__ __noinline__ void drain_bar(uint64_t *bar, uint32_t parity, int32_t *status) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > WAIT_NS) {
+            atomicOr(status, ST_TIMEOUT);
+            return;
+        }
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+// Fields: start address >> 4 [0,14), leading offset >> 4 [16,30) (unused by swizzled K-major),
+// stride offset >> 4 [32,46), fixed 0b001 [46,49), base offset 0, swizzle mode 2 (128 B) [61,64).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: D f32 (bit 4), A/B f16 (format 0), both K-major, N >> 3 at
+// bit 17, M >> 4 at bit 24.
+constexpr uint32_t idesc_f16(int M, int N) { return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24); }
+constexpr uint32_t IDESC_S  = idesc_f16(PF_ROWS, KT);
+constexpr uint32_t IDESC_PV = idesc_f16(PF_ROWS, HD);
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+#define PF_R32(v)                                                                                                   \
+    "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),     \
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),      \
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),     \
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+#define PF_W32(v)                                                                                                   \
+    "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),   \
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), \
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), \
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+// 32 consecutive columns of the warp's 32 lanes: thread i gets lane (base lane + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : PF_R32(v)
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        PF_W32(v)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint4 ldg_nc16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void sts16(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+// int8 x4 (two's complement) -> two f16x2 holding the exact values: bytes 0,1 -> lo, 2,3 -> hi.
+__device__ __forceinline__ void s8x4_to_f16(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t u = w ^ 0x80808080u;                      // x + 128 as unsigned bytes
+    const uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);  // f16 1024 + u (exact)
+    const uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), bias);
+    __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), bias);
+    lo = *reinterpret_cast<uint32_t *>(&ha);
+    hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+// 128-byte-swizzled address of 16-byte chunk c (0..7) of row r in a [rows][128 B] block.
+__device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) { return base + r * 128 + ((c ^ (r & 7)) << 4); }
+
+// ---------------------------------------------------------------------------------------------
+// Query preparation: bf16 rows -> q8_0 (ggml quantize_row_q8_0 rounding) -> fp16(d * q), written
+// as the 64 KiB A-operand image of each tile.  One warp per row; lane l holds elements 8l..8l+7.
+__global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= P.n_tiles * PF_ROWS) return;
+    const int tile = warp / PF_ROWS, r = warp % PF_ROWS;
+    const int kvh = tile / P.n_groups, g = tile % P.n_groups;
+    const int tok = g * P.tpt + r / P.G, head = kvh * P.G + r % P.G;
+    uint4 o = make_uint4(0, 0, 0, 0);
+    if (tok < P.Tc) {
+        const uint4 raw = ldg_nc16(P.Q + ((int64_t)tok * P.n_head + head) * HD + lane * 8);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            x[2 * i]     = __uint_as_float(w[i] << 16);
+            x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d  = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const __half dh = __float2half_rn(d);
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const __half a = __hmul(__float2half_rn(roundf(__fmul_rn(x[2 * i], id))), dh);
+            const __half b = __hmul(__float2half_rn(roundf(__fmul_rn(x[2 * i + 1], id))), dh);
+            h[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+        }
+        o = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    uint8_t *dst = P.qtiles + (int64_t)tile * PF_QTILE + (lane >> 3) * (PF_ROWS * 128) + r * 128 + (((lane & 7) ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4 *>(dst) = o;
+}
+
+// ---------------------------------------------------------------------------------------------
+struct Seg {
+    int tile, kt0, nk, part;
+};
+__device__ __forceinline__ Seg seg_of(const PrefillParams &P, int i) {
+    const int4 s = P.segs[i];
+    return Seg{s.x, s.y, s.z - s.y, s.w};
+}
+
+// Producer: dequantise KV tile kt of KV head kvh into stage s.  256 threads; thread pt owns
+// K chunk (16 dims) pt & 15 of keys (pt >> 4) + 16 i and V chunk (16 keys) pt & 3 of dims
+// (pt >> 2) + 64 i, i = 0..3.  Keys at or beyond n_kv become zeros.
+__device__ __forceinline__ void produce(const PrefillParams &P, uint32_t sbase, int pt, int kvh, int kt, int s) {
+    const int pi = kt >> 2;
+    const int32_t page = pi < P.max_pages ? P.bt[pi] : -1;
+    const bool bad = page < 0 || page >= P.n_pages;
+    if (bad && pt == 0) atomicOr(P.status, ST_BAD_PAGE);
+    const uint8_t *src = P.pool + (bad ? 0 : (int64_t)page * P.page_bytes) + (int64_t)(kvh * TILES_PER_PAGE + (kt & 3)) * TILE_BYTES;
+    const int nvalid = bad ? 0 : min(KT, P.n_kv - kt * KT);
+
+    const int kc = pt & 15, vc = pt & 3;
+    uint4 kq[4], vq[4], vd0[4], vd1[4];
+    uint32_t kd[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int key = (pt >> 4) + 16 * i;
+        const int dim = (pt >> 2) + 64 * i;
+        if (!bad) {
+            kq[i] = ldg_nc16(src + TILE_KQ + key * HD + ((kc ^ kswz(key)) << 4));
+            kd[i] = *reinterpret_cast<const uint16_t *>(src + kd_off(key, kc >> 1));
+            vq[i] = ldg_nc16(src + TILE_VQ + dim * KT + ((vc ^ ((dim >> 1) & 3)) << 4));
+            const uint8_t *vd = src + vd_off(dim >> 5, vc * 16);
+            vd0[i] = ldg_nc16(vd);
+            vd1[i] = ldg_nc16(vd + 16);
+        } else {
+            kq[i] = vq[i] = vd0[i] = vd1[i] = make_uint4(0, 0, 0, 0);
+            kd[i] = 0;
+        }
+    }
+    const uint32_t kbase = sbase + SM_K + s * 32768, vbase = sbase + SM_V + s * 32768;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int key = (pt >> 4) + 16 * i;
+        const uint32_t d2 = key < nvalid ? (kd[i] | (kd[i] << 16)) : 0u;
+        const uint32_t w[4] = {kq[i].x, kq[i].y, kq[i].z, kq[i].w};
+        uint32_t h[8];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            uint32_t lo, hi;
+            s8x4_to_f16(w[e], lo, hi);
+            h[2 * e]     = hmul2(lo, d2);
+            h[2 * e + 1] = hmul2(hi, d2);
+        }
+        const uint32_t atom = kbase + (kc >> 2) * (KT * 128);
+        sts16(swz(atom, key, (kc & 3) * 2), make_uint4(h[0], h[1], h[2], h[3]));
+        sts16(swz(atom, key, (kc & 3) * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int dim = (pt >> 2) + 64 * i;
+        const uint32_t w[4]  = {vq[i].x, vq[i].y, vq[i].z, vq[i].w};
+        const uint32_t dv[8] = {vd0[i].x, vd0[i].y, vd0[i].z, vd0[i].w, vd1[i].x, vd1[i].y, vd1[i].z, vd1[i].w};
+        uint32_t h[8];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            uint32_t lo, hi;
+            s8x4_to_f16(w[e], lo, hi);
+            const int t0 = vc * 16 + 4 * e;   // tokens t0 .. t0+3
+            const uint32_t m0 = t0 + 1 < nvalid ? 0xffffffffu : (t0 < nvalid ? 0x0000ffffu : 0u);
+            const uint32_t m1 = t0 + 3 < nvalid ? 0xffffffffu : (t0 + 2 < nvalid ? 0x0000ffffu : 0u);
+            h[2 * e]     = hmul2(lo, dv[2 * e] & m0);
+            h[2 * e + 1] = hmul2(hi, dv[2 * e + 1] & m1);
+        }
+        sts16(swz(vbase, dim, vc * 2), make_uint4(h[0], h[1], h[2], h[3]));
+        sts16(swz(vbase, dim, vc * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
+    }
+}
+
+__global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(sm);
+    Bars *B = reinterpret_cast<Bars *>(sm + SM_BAR);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s0 = P.cta_seg[blockIdx.x], s1 = P.cta_seg[blockIdx.x + 1];
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&B->kv_full[i], 256);
+            mbar_init(&B->pv_done[i], 1);
+            mbar_init(&B->s_full[i], 1);
+            mbar_init(&B->s_empty[i], 128);
+            mbar_init(&B->p_full[i], 128);
+        }
+        mbar_init(&B->q_full, 1);
+        mbar_init(&B->q_empty, 1);
+        mbar_init(&B->drain, 1);
+        B->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B->tmem)),
+                     "r"(TM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = B->tmem;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ MMA issue
+        if (lane == 0) {
+            bool ok = true;
+            int q_pending = -1;   // parity of a query copy still in flight after an abort
+            uint32_t it = 0;
+            const uint32_t qa = sbase + SM_Q, ka = sbase + SM_K, va = sbase + SM_V, pa = sbase + SM_P;
+            auto issue_pv = [&](uint32_t j, bool first) -> bool {
+                const uint32_t s = j & 1;
+                if (!wait_bar(&B->p_full[s], (j >> 1) & 1, B, P.status)) return false;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < KT / 16; kk++)
+                    mma_f16(tmem + TM_O, sdesc(pa + s * 16384 + kk * 32), sdesc(va + s * 32768 + kk * 32), IDESC_PV,
+                            (first && kk == 0) ? 0u : 1u);
+                mma_commit(&B->pv_done[s]);
+                return true;
+            };
+            for (int si = s0; si < s1 && ok; si++) {
+                const Seg sg = seg_of(P, si);
+                if (si > s0 && !(ok = wait_bar(&B->q_empty, (si - s0 - 1) & 1, B, P.status))) break;
+                mbar_expect_tx(&B->q_full, PF_QTILE);
+                const uint8_t *qsrc = P.qtiles + (int64_t)sg.tile * PF_QTILE;
+#pragma unroll
+                for (int c = 0; c < 4; c++) bulk_load(sm + SM_Q + c * 16384, qsrc + c * 16384, 16384, &B->q_full);
+                if (!(ok = wait_bar(&B->q_full, (si - s0) & 1, B, P.status))) {
+                    q_pending = (si - s0) & 1;
+                    break;
+                }
+                tc_fence_after();
+                for (int k = 0; k < sg.nk && ok; k++) {
+                    const uint32_t j = it + k, s = j & 1, ph = (j >> 1) & 1;
+                    if (!(ok = wait_bar(&B->kv_full[s], ph, B, P.status))) break;
+                    if (j >= 2 && !(ok = wait_bar(&B->s_empty[s], ph ^ 1, B, P.status))) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; kk++)
+                        mma_f16(tmem + TM_S + s * KT, sdesc(qa + (kk >> 2) * 16384 + (kk & 3) * 32),
+                                sdesc(ka + s * 32768 + (kk >> 2) * 8192 + (kk & 3) * 32), IDESC_S, kk > 0 ? 1u : 0u);
+                    mma_commit(&B->s_full[s]);
+                    if (k == sg.nk - 1) mma_commit(&B->q_empty);
+                    if (k >= 1) ok = issue_pv(j - 1, k == 1);
+                }
+                if (ok) ok = issue_pv(it + sg.nk - 1, sg.nk == 1);
+                it += sg.nk;
+            }
+            if (q_pending >= 0) drain_bar(&B->q_full, (uint32_t)q_pending, P.status);
+            mma_commit(&B->drain);
+            drain_bar(&B->drain, 0, P.status);
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------------------ softmax
+        // Control flow is kept warp-uniform (tcgen05.ld/st are warp-collective): every wait's
+        // result is agreed with __all_sync.  Split segments are merged per warp (32 rows) with a
+        // per-(tile, warp) arrival counter, so no barrier spans warps.
+        const int r = tid - 128, wq = warp & 3;
+        const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+        auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+            return __all_sync(0xffffffffu, wait_bar(bar, parity, B, P.status));
+        };
+        uint32_t it = 0;
+        bool ok = true;
+        for (int si = s0; si < s1 && ok; si++) {
+            const Seg sg = seg_of(P, si);
+            const int kvh = sg.tile / P.n_groups, g = sg.tile % P.n_groups;
+            const int tok = g * P.tpt + r / P.G, head = kvh * P.G + r % P.G;
+            const int qpos = tok < P.Tc ? P.pos0 + tok : -1;
+            float m_ref = -INFINITY, l = 0.f;
+            for (int k = 0; k < sg.nk; k++) {
+                const uint32_t j = it + k, s = j & 1, ph = (j >> 1) & 1;
+                if (!(ok = wait_all(&B->s_full[s], ph))) break;
+                tc_fence_after();
+                uint32_t v0[32], v1[32];
+                tmem_ld32(tmem + lane_base + TM_S + s * KT, v0);
+                tmem_ld32(tmem + lane_base + TM_S + s * KT + 32, v1);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(&B->s_empty[s]);
+                const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
+                float x[64];
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    x[c]      = c < nvis ? __uint_as_float(v0[c]) * P.scale_log2 : -INFINITY;
+                    x[c + 32] = c + 32 < nvis ? __uint_as_float(v1[c]) * P.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, fmaxf(x[c], x[c + 32]));
+                }
+                // lazily raised reference max: O and l are rescaled only when a row max grows
+                // by more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
+                const bool need = mx > m_ref + 8.0f;
+                const float f = (need && m_ref != -INFINITY) ? exp2f(m_ref - mx) : 1.0f;
+                const bool rescale = k > 0 && __any_sync(0xffffffffu, f != 1.0f);
+                if (need) m_ref = mx;
+                l *= f;
+                if (j >= 2 && !(ok = wait_all(&B->pv_done[s], ph ^ 1))) break;
+                const uint32_t prow = sbase + SM_P + s * 16384;
+#pragma unroll
+                for (int c8 = 0; c8 < 8; c8++) {
+                    uint32_t h[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float a = x[c8 * 8 + 2 * e], b = x[c8 * 8 + 2 * e + 1];
+                        const float pa = a == -INFINITY ? 0.f : exp2f(a - m_ref);
+                        const float pb = b == -INFINITY ? 0.f : exp2f(b - m_ref);
+                        const __half2 hp = __floats2half2_rn(pa, pb);
+                        l += __low2float(hp) + __high2float(hp);
+                        h[e] = *reinterpret_cast<const uint32_t *>(&hp);
+                    }
+                    sts16(swz(prow, r, c8), make_uint4(h[0], h[1], h[2], h[3]));
+                }
+                if (rescale) {
+                    // O holds PV of the previous tile: rescale it once that product has landed
+                    if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c8 = 0; c8 < HD / 32; c8++) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+                        tmem_st32(tmem + lane_base + TM_O + c8 * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+                fence_proxy_async();
+                tc_fence_before();
+                mbar_arrive(&B->p_full[s]);
+            }
+            if (!ok) break;
+            // ---- epilogue: O of the segment
+            const uint32_t jl = it + sg.nk - 1;
+            if (!(ok = wait_all(&B->pv_done[jl & 1], (jl >> 1) & 1))) break;
+            tc_fence_after();
+            if (sg.part < 0) {
+                const float inv = l > 0.f ? 1.0f / l : 0.f;
+                float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
+#pragma unroll 1
+                for (int c8 = 0; c8 < HD / 32; c8++) {
+                    uint32_t o[32];
+                    tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
+                    tmem_wait_ld();
+                    if (tok < P.Tc) {
+#pragma unroll
+                        for (int c = 0; c < 32; c += 4)
+                            *reinterpret_cast<float4 *>(dst + c8 * 32 + c) =
+                                make_float4(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv,
+                                            __uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+                    }
+                }
+            } else {
+                float *rec = P.partial + (int64_t)sg.part * pf_part_floats();
+#pragma unroll 1
+                for (int c8 = 0; c8 < HD / 32; c8++) {
+                    uint32_t o[32];
+                    tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 32; c += 4)
+                        __stcg(reinterpret_cast<float4 *>(rec + r * HD + c8 * 32 + c),
+                               make_float4(__uint_as_float(o[c]), __uint_as_float(o[c + 1]), __uint_as_float(o[c + 2]),
+                                           __uint_as_float(o[c + 3])));
+                }
+                __stcg(rec + PF_ROWS * HD + r, m_ref);
+                __stcg(rec + PF_ROWS * HD + PF_ROWS + r, l);
+                __threadfence();
+                __syncwarp();
+                const int2 tp = P.tile_parts[sg.tile];
+                int last = 0;
+                if (lane == 0) last = atomicAdd(&P.counters[sg.tile * 4 + wq], 1) == tp.x - 1;
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    __threadfence();
+                    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
+                    float w[PF_MAX_PARTS];
+                    float M = -INFINITY, L = 0.f;
+                    for (int p = 0; p < tp.x; p++) M = fmaxf(M, __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + r));
+#pragma unroll
+                    for (int p = 0; p < PF_MAX_PARTS; p++) {
+                        w[p] = 0.f;
+                        if (p < tp.x) {
+                            const float mp = __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + r);
+                            w[p] = mp == -INFINITY ? 0.f : exp2f(mp - M);
+                            L += w[p] * __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + PF_ROWS + r);
+                        }
+                    }
+                    const float inv = L > 0.f ? 1.0f / L : 0.f;
+                    if (tok < P.Tc) {
+                        float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
+#pragma unroll 1
+                        for (int c = 0; c < HD; c += 4) {
+                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                            for (int p = 0; p < PF_MAX_PARTS; p++) {
+                                if (p < tp.x) {
+                                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + p * pf_part_floats() + r * HD + c));
+                                    acc.x += w[p] * v.x;
+                                    acc.y += w[p] * v.y;
+                                    acc.z += w[p] * v.z;
+                                    acc.w += w[p] * v.w;
+                                }
+                            }
+                            *reinterpret_cast<float4 *>(dst + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                        }
+                    }
+                    if (lane == 0) P.counters[sg.tile * 4 + wq] = 0;
+                }
+            }
+            tc_fence_before();
+            it += sg.nk;
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------------ producers
+        const int pt = tid - 256;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int si = s0; si < s1 && ok; si++) {
+            const Seg sg = seg_of(P, si);
+            const int kvh = sg.tile / P.n_groups;
+            for (int k = 0; k < sg.nk; k++) {
+                const uint32_t j = it + k, s = j & 1;
+                if (j >= 2 && !(ok = wait_bar(&B->pv_done[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
+                produce(P, sbase, pt, kvh, sg.kt0 + k, s);
+                fence_proxy_async();
+                mbar_arrive(&B->kv_full[s]);
+            }
+            it += sg.nk;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS) : "memory");
+    }
+}
+
+}  // namespace pf
+
+cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        const cudaError_t e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int64_t rows = (int64_t)p.n_tiles * PF_ROWS;
+    pf::k_prefill_q<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    pf::k_prefill<<<p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st>>>(p);
+    count_launches(2);
+    return cudaGetLastError();
+}
+
+}  // namespace qkv

@@ -46,8 +46,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
-                    help="cfg2 (default, the headline line): BASELINE configs[1]; cfg5: configs[4]")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2",
+                    help="cfg2 (default, the headline line): BASELINE configs[1]; cfg3: configs[2] chunked "
+                         "prefill; cfg5: configs[4]")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
@@ -478,6 +479,151 @@ def run_cfg5(args) -> None:
     }), flush=True)
 
 
+# ----------------------------------------------------------------------------- config 3
+PF_N, PF_C = 16384, 512
+
+
+def prefill_flops() -> float:
+    """Causal QK^T + PV flops of the whole 16384-token prompt: 4 * H_q * d * sum_t (t + 1)."""
+    return 4.0 * N_HEAD * HD * (PF_N * (PF_N + 1) / 2)
+
+
+def cpu_prefill_baseline(chunks=(8, 15, 16, 23)) -> dict:
+    """The oracle on a sample of config-3 chunks whose mean work equals the mean chunk's."""
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+    threads = O.max_threads()
+    r = np.random.default_rng(2)
+    n_kv = (max(chunks) + 1) * PF_C
+    K = O.quantize_rows(r.standard_normal((n_kv, N_HEAD_KV * HD), dtype=np.float32), threads)
+    V = O.quantize_rows(r.standard_normal((n_kv, N_HEAD_KV * HD), dtype=np.float32), threads)
+    import torch
+    Qf = torch.from_numpy(r.standard_normal((len(chunks), PF_C, N_HEAD, HD), dtype=np.float32)).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+    for i, c in enumerate(chunks):
+        O.attn(Qf[i], K, V, c * PF_C + np.arange(PF_C, dtype=np.int32), N_HEAD_KV, SCALE, n_cells=(c + 1) * PF_C,
+               threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": len(chunks) * PF_C / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"config-3 chunks {list(chunks)} (512 queries each over {[(c + 1) * PF_C for c in chunks]} "
+                      f"cached keys; mean work = the mean chunk's); oracle/qkv_oracle.c, {threads} threads"}
+
+
+def run_cfg3(args) -> None:
+    """a 16384-token prompt prefilled in 32 chunks of 512 on one layer; every chunk
+    appends its 512 K/V rows (kernel A) and runs causal attention of its bf16 queries over the whole
+    cache so far (kernel D, tcgen05).  One step = the whole prompt."""
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import qwfn_hybrid_b200 as Q
+    gen = torch.Generator(device=dev).manual_seed(2 + 1000 * rank)
+    K = torch.randn(PF_N, N_HEAD_KV * HD, generator=gen, device=dev)
+    V = torch.randn(PF_N, N_HEAD_KV * HD, generator=gen, device=dev)
+    Qb = torch.randn(PF_N, N_HEAD, HD, generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
+    out = torch.empty(PF_N, N_HEAD, HD, device=dev)
+    eng = Q.Engine(n_layer=1, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=PF_N, n_slots=1, device=local)
+    eng.seq_alloc(0)
+    nch = PF_N // PF_C
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for c in range(nch):
+            a, b = c * PF_C, (c + 1) * PF_C
+            eng.append(0, 0, a, K[a:b], V[a:b])
+            eng.attn_prefill(0, 0, a, Qb[a:b], PF_C, SCALE, out[a:b])
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # kernel-D time alone (the prefill calls of one step, CUDA events on the launching stream)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nch)]
+    for c in range(nch):
+        a, b = c * PF_C, (c + 1) * PF_C
+        eng.append(0, 0, a, K[a:b], V[a:b])
+        evs[c][0].record(stream)
+        eng.attn_prefill(0, 0, a, Qb[a:b], PF_C, SCALE, out[a:b])
+        evs[c][1].record(stream)
+    torch.cuda.synchronize()
+    attn_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = Q.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = Q.launch_count() - launches0
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if eng.device_status() != 0:
+        raise RuntimeError("device status reported a bounds violation")
+    # end to end through the API: each chunk's K, V and Q from pinned host memory, its output back
+    hK, hV, hQ = K.cpu().pin_memory(), V.cpu().pin_memory(), Qb.cpu().pin_memory()
+    hO = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dK, dV, dQ, dO = torch.empty_like(K), torch.empty_like(V), torch.empty_like(Qb), torch.empty_like(out)
+    e2e_steps = max(1, min(args.steps, 3))
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(e2e_steps):
+        for c in range(nch):
+            a, b = c * PF_C, (c + 1) * PF_C
+            dK[a:b].copy_(hK[a:b], non_blocking=True)
+            dV[a:b].copy_(hV[a:b], non_blocking=True)
+            dQ[a:b].copy_(hQ[a:b], non_blocking=True)
+            eng.append(0, 0, a, dK[a:b], dV[a:b])
+            eng.attn_prefill(0, 0, a, dQ[a:b], PF_C, SCALE, dO[a:b])
+            hO[a:b].copy_(dO[a:b], non_blocking=True)
+    x1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1) / e2e_steps
+    if ws > 1:
+        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, attn_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    peak, peak_src = 1590.0, "fallback"
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peak, peak_src = json.load(open(pk)).get("bf16_tflops", peak), "measured bf16_tflops (burst)"
+    tflops = prefill_flops() / (attn_ms * 1e-3) / 1e12
+    line = {
+        "metric": "chunked-prefill tokens/s over q8_0 KV (16384-token prompt, 512-token chunks)",
+        "value": ws * PF_N * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 tcgen05 (q8_0-rounded operands) + f32 softmax/accumulate",
+        "data": "synthetic N(0,1) (torch Philox, seed 2+1000*rank), Q bf16",
+        "config": {"workload": "configs[2]: 16384-token prompt, 32 chunks of 512, 1 layer, 16q/2kv x 256, q8_0 KV, "
+                               "each chunk appends 512 rows then attends causally over the whole cache",
+                   "parallelism": f"independent prompts x{ws} (replicas, no collective)",
+                   "l2": "inputs larger than L2 (134 MB of bf16 queries + 268 MB of outputs per step)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
+                     "peak_source": peak_src, "traffic": None,
+                     "kernel": "k_prefill_q + k_prefill per chunk (CUDA events around each qkv_attn_prefill call)",
+                     "flops_per_step": prefill_flops(), "attn_ms_per_step": attn_ms},
+        "e2e": {"value": ws * PF_N / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": (K.numel() + V.numel()) * 4 + Qb.numel() * 2,
+                "d2h_bytes_per_step": out.numel() * 4},
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_prefill_baseline()
+    print(json.dumps(line), flush=True)
+
+
 class _DevRange:
     """A device address range as a float32 tensor (CUDA array interface)."""
 
@@ -492,6 +638,8 @@ def main():
         run_reference(args)
     elif args.workload == "cfg5":
         run_cfg5(args)
+    elif args.workload == "cfg3":
+        run_cfg3(args)
     else:
         run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

@@ -15,8 +15,10 @@
 //   warps 4-7   softmax: thread r owns row r (TMEM lane r): S row from TMEM, causal mask,
 //               online softmax with a lazily raised reference max (O in TMEM rescaled only when
 //               the row max grows by more than 2^8), P as fp16 into shared memory
-//   warps 8-15  producers: read q8_0 K/V tiles from the pages, dequantise to fp16 into the
-//               128-byte-swizzled K-major layouts the MMAs read
+//   warps 8-11  K producers, warps 12-15 V producers: read q8_0 tiles from the pages (issued
+//               before the stage is free), dequantise to fp16 into the 128-byte-swizzled K-major
+//               layouts the MMAs read.  A K stage frees when its S MMA completes, a V stage when
+//               its PV MMA completes, so K of tile j+2 is written while PV of tile j runs.
 // Per KV tile j (stage s = j % 2):  S[s] = Q K_j^T  (M128 N64 K256: 16 MMAs),  then after the
 // softmax wrote P_j:  O += P_j V_j  (M128 N256 K64: 4 MMAs).  S_{j+1} is issued before PV_j so
 // the tensor core works while the softmax runs.  Every wait is bounded (ST_TIMEOUT, then all
@@ -42,10 +44,13 @@ constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 // tensor memory columns
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
+constexpr int MAX_MERGE = 24;
 
 struct Bars {
-    uint64_t kv_full[2];    // producers (256 arrivals): K_j and V_j in stage s
-    uint64_t pv_done[2];    // commit after PV_j: stage s and P buffer s free, O holds tile j
+    uint64_t k_full[2];     // K producers (128 arrivals): K_j in stage s
+    uint64_t v_full[2];     // V producers (128 arrivals): V_j in stage s
+    uint64_t k_free[2];     // commit after S_j: K stage s free
+    uint64_t pv_done[2];    // commit after PV_j: V stage s and P buffer s free, O holds tile j
     uint64_t s_full[2];     // commit after S_j
     uint64_t s_empty[2];    // softmax (128 arrivals): S buffer read
     uint64_t p_full[2];     // softmax (128 arrivals): P_j written (and O rescaled)
@@ -54,6 +59,8 @@ struct Bars {
     uint64_t drain;         // commit before exit
     uint32_t tmem;
     int32_t  abort;
+    int32_t  n_merge;             // split tiles (x4 row quarters) this CTA completed last
+    int32_t  merge[MAX_MERGE];
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
@@ -165,6 +172,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
         PF_W32(v)
         : "memory");
 }
+// 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = +0)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -234,6 +247,44 @@ __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
     *reinterpret_cast<uint4 *>(dst) = o;
 }
 
+// Merge the partial records of split tile `tile` for row `row`, float4 columns c0, c0+step, ...
+// into the output: O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p.
+__device__ __forceinline__ void merge_rows(const PrefillParams &P, int tile, int row, int step, int c0) {
+    const int2 tp = P.tile_parts[tile];
+    const int kvh = tile / P.n_groups, g = tile % P.n_groups;
+    const int tok = g * P.tpt + row / P.G, head = kvh * P.G + row % P.G;
+    if (tok >= P.Tc) return;
+    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
+    float w[PF_MAX_PARTS];
+    float M = -INFINITY, L = 0.f;
+#pragma unroll
+    for (int p = 0; p < PF_MAX_PARTS; p++)
+        w[p] = p < tp.x ? __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + row) : -INFINITY;
+#pragma unroll
+    for (int p = 0; p < PF_MAX_PARTS; p++) M = fmaxf(M, w[p]);
+#pragma unroll
+    for (int p = 0; p < PF_MAX_PARTS; p++) {
+        w[p] = w[p] == -INFINITY ? 0.f : ex2(w[p] - M);
+        if (p < tp.x) L += w[p] * __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + PF_ROWS + row);
+    }
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
+    for (int c = c0; c < HD / 4; c += step) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < PF_MAX_PARTS; p++) {
+            if (p < tp.x) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + p * pf_part_floats() + row * HD) + c);
+                acc.x += w[p] * v.x;
+                acc.y += w[p] * v.y;
+                acc.z += w[p] * v.z;
+                acc.w += w[p] * v.w;
+            }
+        }
+        reinterpret_cast<float4 *>(dst)[c] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 struct Seg {
     int tile, kt0, nk, part;
@@ -243,42 +294,54 @@ __device__ __forceinline__ Seg seg_of(const PrefillParams &P, int i) {
     return Seg{s.x, s.y, s.z - s.y, s.w};
 }
 
-// Producer: dequantise KV tile kt of KV head kvh into stage s.  256 threads; thread pt owns
-// K chunk (16 dims) pt & 15 of keys (pt >> 4) + 16 i and V chunk (16 keys) pt & 3 of dims
-// (pt >> 2) + 64 i, i = 0..3.  Keys at or beyond n_kv become zeros.
-__device__ __forceinline__ void produce(const PrefillParams &P, uint32_t sbase, int pt, int kvh, int kt, int s) {
+// Source of KV tile kt of KV head kvh in the pages; nvalid = keys of it below n_kv (0 when the
+// block table is bad, which is reported in the status word).
+struct TileSrc {
+    const uint8_t *src;
+    int nvalid;
+};
+__device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int kt, bool report) {
     const int pi = kt >> 2;
     const int32_t page = pi < P.max_pages ? P.bt[pi] : -1;
-    const bool bad = page < 0 || page >= P.n_pages;
-    if (bad && pt == 0) atomicOr(P.status, ST_BAD_PAGE);
-    const uint8_t *src = P.pool + (bad ? 0 : (int64_t)page * P.page_bytes) + (int64_t)(kvh * TILES_PER_PAGE + (kt & 3)) * TILE_BYTES;
-    const int nvalid = bad ? 0 : min(KT, P.n_kv - kt * KT);
+    if (page < 0 || page >= P.n_pages) {
+        if (report) atomicOr(P.status, ST_BAD_PAGE);
+        return TileSrc{nullptr, 0};
+    }
+    return TileSrc{P.pool + (int64_t)page * P.page_bytes + (int64_t)(kvh * TILES_PER_PAGE + (kt & 3)) * TILE_BYTES,
+                   min(KT, P.n_kv - kt * KT)};
+}
 
-    const int kc = pt & 15, vc = pt & 3;
-    uint4 kq[4], vq[4], vd0[4], vd1[4];
-    uint32_t kd[4];
+// K producer thread t (0..127): 16-dim chunk kc = t & 15 of keys (t >> 4) + 8 i, i = 0..7.
+// Raw bytes are loaded before the stage is known to be free, converted after.
+struct KLoad {
+    uint4    q[8];
+    uint32_t d[8];
+    int      nvalid;
+};
+__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int kt, KLoad &L) {
+    const TileSrc ts = tile_src(P, kvh, kt, t == 0);
+    L.nvalid = ts.nvalid;
+    const int kc = t & 15;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int key = (pt >> 4) + 16 * i;
-        const int dim = (pt >> 2) + 64 * i;
-        if (!bad) {
-            kq[i] = ldg_nc16(src + TILE_KQ + key * HD + ((kc ^ kswz(key)) << 4));
-            kd[i] = *reinterpret_cast<const uint16_t *>(src + kd_off(key, kc >> 1));
-            vq[i] = ldg_nc16(src + TILE_VQ + dim * KT + ((vc ^ ((dim >> 1) & 3)) << 4));
-            const uint8_t *vd = src + vd_off(dim >> 5, vc * 16);
-            vd0[i] = ldg_nc16(vd);
-            vd1[i] = ldg_nc16(vd + 16);
+    for (int i = 0; i < 8; i++) {
+        const int key = (t >> 4) + 8 * i;
+        if (ts.src) {
+            L.q[i] = ldg_nc16(ts.src + TILE_KQ + key * HD + ((kc ^ kswz(key)) << 4));
+            L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(key, kc >> 1));
         } else {
-            kq[i] = vq[i] = vd0[i] = vd1[i] = make_uint4(0, 0, 0, 0);
-            kd[i] = 0;
+            L.q[i] = make_uint4(0, 0, 0, 0);
+            L.d[i] = 0;
         }
     }
-    const uint32_t kbase = sbase + SM_K + s * 32768, vbase = sbase + SM_V + s * 32768;
+}
+__device__ __forceinline__ void k_store(uint32_t kbase, int t, const KLoad &L) {
+    const int kc = t & 15;
+    const uint32_t atom = kbase + (kc >> 2) * (KT * 128);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int key = (pt >> 4) + 16 * i;
-        const uint32_t d2 = key < nvalid ? (kd[i] | (kd[i] << 16)) : 0u;
-        const uint32_t w[4] = {kq[i].x, kq[i].y, kq[i].z, kq[i].w};
+    for (int i = 0; i < 8; i++) {
+        const int key = (t >> 4) + 8 * i;
+        const uint32_t d2 = key < L.nvalid ? (L.d[i] | (L.d[i] << 16)) : 0u;
+        const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t h[8];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
@@ -287,25 +350,56 @@ __device__ __forceinline__ void produce(const PrefillParams &P, uint32_t sbase, 
             h[2 * e]     = hmul2(lo, d2);
             h[2 * e + 1] = hmul2(hi, d2);
         }
-        const uint32_t atom = kbase + (kc >> 2) * (KT * 128);
         sts16(swz(atom, key, (kc & 3) * 2), make_uint4(h[0], h[1], h[2], h[3]));
         sts16(swz(atom, key, (kc & 3) * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
     }
+}
+
+// V producer thread t (0..127): tokens 16 vc .. 16 vc + 15 (vc = t & 3) of the 8 dims
+// 32 b + 8 sub + i (b = t >> 4, sub = (t >> 2) & 3, i = 0..7), which share one set of scales.
+struct VLoad {
+    uint4 q[8];
+    uint4 d0, d1;
+    int   nvalid;
+};
+__device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, VLoad &L) {
+    const TileSrc ts = tile_src(P, kvh, kt, false);
+    L.nvalid = ts.nvalid;
+    const int b = t >> 4, vc = t & 3, d0 = 32 * b + 8 * ((t >> 2) & 3);
+    if (ts.src) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int dim = (pt >> 2) + 64 * i;
-        const uint32_t w[4]  = {vq[i].x, vq[i].y, vq[i].z, vq[i].w};
-        const uint32_t dv[8] = {vd0[i].x, vd0[i].y, vd0[i].z, vd0[i].w, vd1[i].x, vd1[i].y, vd1[i].z, vd1[i].w};
+        for (int i = 0; i < 8; i++) {
+            const int dim = d0 + i;
+            L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * KT + ((vc ^ ((dim >> 1) & 3)) << 4));
+        }
+        const uint8_t *vd = ts.src + vd_off(b, vc * 16);
+        L.d0 = ldg_nc16(vd);
+        L.d1 = ldg_nc16(vd + 16);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) L.q[i] = make_uint4(0, 0, 0, 0);
+        L.d0 = L.d1 = make_uint4(0, 0, 0, 0);
+    }
+}
+__device__ __forceinline__ void v_store(uint32_t vbase, int t, const VLoad &L) {
+    const int vc = t & 3, d0 = 32 * (t >> 4) + 8 * ((t >> 2) & 3);
+    uint32_t dv[8] = {L.d0.x, L.d0.y, L.d0.z, L.d0.w, L.d1.x, L.d1.y, L.d1.z, L.d1.w};
+#pragma unroll
+    for (int e = 0; e < 8; e++) {   // tokens 16 vc + 2e, +1: zero scales past n_kv
+        const int t0 = vc * 16 + 2 * e;
+        dv[e] &= t0 + 1 < L.nvalid ? 0xffffffffu : (t0 < L.nvalid ? 0x0000ffffu : 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int dim = d0 + i;
+        const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t h[8];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             uint32_t lo, hi;
             s8x4_to_f16(w[e], lo, hi);
-            const int t0 = vc * 16 + 4 * e;   // tokens t0 .. t0+3
-            const uint32_t m0 = t0 + 1 < nvalid ? 0xffffffffu : (t0 < nvalid ? 0x0000ffffu : 0u);
-            const uint32_t m1 = t0 + 3 < nvalid ? 0xffffffffu : (t0 + 2 < nvalid ? 0x0000ffffu : 0u);
-            h[2 * e]     = hmul2(lo, dv[2 * e] & m0);
-            h[2 * e + 1] = hmul2(hi, dv[2 * e + 1] & m1);
+            h[2 * e]     = hmul2(lo, dv[2 * e]);
+            h[2 * e + 1] = hmul2(hi, dv[2 * e + 1]);
         }
         sts16(swz(vbase, dim, vc * 2), make_uint4(h[0], h[1], h[2], h[3]));
         sts16(swz(vbase, dim, vc * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
@@ -322,7 +416,9 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
-            mbar_init(&B->kv_full[i], 256);
+            mbar_init(&B->k_full[i], 128);
+            mbar_init(&B->v_full[i], 128);
+            mbar_init(&B->k_free[i], 1);
             mbar_init(&B->pv_done[i], 1);
             mbar_init(&B->s_full[i], 1);
             mbar_init(&B->s_empty[i], 128);
@@ -332,6 +428,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         mbar_init(&B->q_empty, 1);
         mbar_init(&B->drain, 1);
         B->abort = 0;
+        B->n_merge = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -354,6 +451,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             const uint32_t qa = sbase + SM_Q, ka = sbase + SM_K, va = sbase + SM_V, pa = sbase + SM_P;
             auto issue_pv = [&](uint32_t j, bool first) -> bool {
                 const uint32_t s = j & 1;
+                if (!wait_bar(&B->v_full[s], (j >> 1) & 1, B, P.status)) return false;
                 if (!wait_bar(&B->p_full[s], (j >> 1) & 1, B, P.status)) return false;
                 tc_fence_after();
 #pragma unroll
@@ -377,7 +475,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 tc_fence_after();
                 for (int k = 0; k < sg.nk && ok; k++) {
                     const uint32_t j = it + k, s = j & 1, ph = (j >> 1) & 1;
-                    if (!(ok = wait_bar(&B->kv_full[s], ph, B, P.status))) break;
+                    if (!(ok = wait_bar(&B->k_full[s], ph, B, P.status))) break;
                     if (j >= 2 && !(ok = wait_bar(&B->s_empty[s], ph ^ 1, B, P.status))) break;
                     tc_fence_after();
 #pragma unroll
@@ -385,6 +483,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                         mma_f16(tmem + TM_S + s * KT, sdesc(qa + (kk >> 2) * 16384 + (kk & 3) * 32),
                                 sdesc(ka + s * 32768 + (kk >> 2) * 8192 + (kk & 3) * 32), IDESC_S, kk > 0 ? 1u : 0u);
                     mma_commit(&B->s_full[s]);
+                    mma_commit(&B->k_free[s]);
                     if (k == sg.nk - 1) mma_commit(&B->q_empty);
                     if (k >= 1) ok = issue_pv(j - 1, k == 1);
                 }
@@ -425,37 +524,52 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 tc_fence_before();
                 mbar_arrive(&B->s_empty[s]);
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
-                float x[64];
-                float mx = -INFINITY;
+                float2 x2[32];   // raw scores; masked keys -inf (2^-inf = 0 below)
+                float smax = -INFINITY;
+                if (__all_sync(0xffffffffu, nvis == KT)) {
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    x[c]      = c < nvis ? __uint_as_float(v0[c]) * P.scale_log2 : -INFINITY;
-                    x[c + 32] = c + 32 < nvis ? __uint_as_float(v1[c]) * P.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, fmaxf(x[c], x[c + 32]));
+                    for (int c = 0; c < 16; c++) {
+                        x2[c]      = make_float2(__uint_as_float(v0[2 * c]), __uint_as_float(v0[2 * c + 1]));
+                        x2[c + 16] = make_float2(__uint_as_float(v1[2 * c]), __uint_as_float(v1[2 * c + 1]));
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 16; c++) {
+                        x2[c]      = make_float2(2 * c < nvis ? __uint_as_float(v0[2 * c]) : -INFINITY,
+                                                 2 * c + 1 < nvis ? __uint_as_float(v0[2 * c + 1]) : -INFINITY);
+                        x2[c + 16] = make_float2(2 * c + 32 < nvis ? __uint_as_float(v1[2 * c]) : -INFINITY,
+                                                 2 * c + 33 < nvis ? __uint_as_float(v1[2 * c + 1]) : -INFINITY);
+                    }
                 }
+#pragma unroll
+                for (int c = 0; c < 32; c++) smax = fmaxf(smax, fmaxf(x2[c].x, x2[c].y));
+                const float mx = smax * P.scale_log2;   // scale > 0: max of scaled = scaled max
                 // lazily raised reference max: O and l are rescaled only when a row max grows
                 // by more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
                 const bool need = mx > m_ref + 8.0f;
-                const float f = (need && m_ref != -INFINITY) ? exp2f(m_ref - mx) : 1.0f;
+                const float f = (need && m_ref != -INFINITY) ? ex2(m_ref - mx) : 1.0f;
                 const bool rescale = k > 0 && __any_sync(0xffffffffu, f != 1.0f);
                 if (need) m_ref = mx;
                 l *= f;
                 if (j >= 2 && !(ok = wait_all(&B->pv_done[s], ph ^ 1))) break;
                 const uint32_t prow = sbase + SM_P + s * 16384;
+                const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: all p = 0
+                const float2 sc2 = make_float2(P.scale_log2, P.scale_log2), nm2 = make_float2(-mu, -mu);
+                float2 l2 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int c8 = 0; c8 < 8; c8++) {
                     uint32_t h[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const float a = x[c8 * 8 + 2 * e], b = x[c8 * 8 + 2 * e + 1];
-                        const float pa = a == -INFINITY ? 0.f : exp2f(a - m_ref);
-                        const float pb = b == -INFINITY ? 0.f : exp2f(b - m_ref);
-                        const __half2 hp = __floats2half2_rn(pa, pb);
-                        l += __low2float(hp) + __high2float(hp);
+                        const float2 y = __ffma2_rn(x2[c8 * 4 + e], sc2, nm2);
+                        const float2 p = make_float2(ex2(y.x), ex2(y.y));
+                        l2 = __fadd2_rn(l2, p);
+                        const __half2 hp = __floats2half2_rn(p.x, p.y);
                         h[e] = *reinterpret_cast<const uint32_t *>(&hp);
                     }
                     sts16(swz(prow, r, c8), make_uint4(h[0], h[1], h[2], h[3]));
                 }
+                l += l2.x + l2.y;
                 if (rescale) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
@@ -515,50 +629,23 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 __syncwarp();
                 const int2 tp = P.tile_parts[sg.tile];
                 int last = 0;
-                if (lane == 0) last = atomicAdd(&P.counters[sg.tile * 4 + wq], 1) == tp.x - 1;
+                if (lane == 0 && atomicAdd(&P.counters[sg.tile * 4 + wq], 1) == tp.x - 1) {
+                    P.counters[sg.tile * 4 + wq] = 0;   // ready for the next launch
+                    const int idx = atomicAdd(&B->n_merge, 1);
+                    if (idx < MAX_MERGE) B->merge[idx] = sg.tile * 4 + wq;
+                    else last = 1;   // list full: merge here
+                }
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     __threadfence();
-                    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
-                    float w[PF_MAX_PARTS];
-                    float M = -INFINITY, L = 0.f;
-                    for (int p = 0; p < tp.x; p++) M = fmaxf(M, __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + r));
-#pragma unroll
-                    for (int p = 0; p < PF_MAX_PARTS; p++) {
-                        w[p] = 0.f;
-                        if (p < tp.x) {
-                            const float mp = __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + r);
-                            w[p] = mp == -INFINITY ? 0.f : exp2f(mp - M);
-                            L += w[p] * __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + PF_ROWS + r);
-                        }
-                    }
-                    const float inv = L > 0.f ? 1.0f / L : 0.f;
-                    if (tok < P.Tc) {
-                        float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
-#pragma unroll 1
-                        for (int c = 0; c < HD; c += 4) {
-                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                            for (int p = 0; p < PF_MAX_PARTS; p++) {
-                                if (p < tp.x) {
-                                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + p * pf_part_floats() + r * HD + c));
-                                    acc.x += w[p] * v.x;
-                                    acc.y += w[p] * v.y;
-                                    acc.z += w[p] * v.z;
-                                    acc.w += w[p] * v.w;
-                                }
-                            }
-                            *reinterpret_cast<float4 *>(dst + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-                        }
-                    }
-                    if (lane == 0) P.counters[sg.tile * 4 + wq] = 0;
+                    merge_rows(P, sg.tile, 32 * wq + lane, 1, 0);
                 }
             }
             tc_fence_before();
             it += sg.nk;
         }
-    } else if (warp >= 8) {
-        // ------------------------------------------------------------------ producers
-        const int pt = tid - 256;
+    } else if (warp >= 8 && warp < 12) {
+        // ------------------------------------------------------------------ K producers
+        const int t = tid - 256;
         uint32_t it = 0;
         bool ok = true;
         for (int si = s0; si < s1 && ok; si++) {
@@ -566,10 +653,31 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             const int kvh = sg.tile / P.n_groups;
             for (int k = 0; k < sg.nk; k++) {
                 const uint32_t j = it + k, s = j & 1;
-                if (j >= 2 && !(ok = wait_bar(&B->pv_done[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
-                produce(P, sbase, pt, kvh, sg.kt0 + k, s);
+                KLoad L;
+                k_load(P, t, kvh, sg.kt0 + k, L);
+                if (j >= 2 && !(ok = wait_bar(&B->k_free[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
+                k_store(sbase + SM_K + s * 32768, t, L);
                 fence_proxy_async();
-                mbar_arrive(&B->kv_full[s]);
+                mbar_arrive(&B->k_full[s]);
+            }
+            it += sg.nk;
+        }
+    } else if (warp >= 12) {
+        // ------------------------------------------------------------------ V producers
+        const int t = tid - 384;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int si = s0; si < s1 && ok; si++) {
+            const Seg sg = seg_of(P, si);
+            const int kvh = sg.tile / P.n_groups;
+            for (int k = 0; k < sg.nk; k++) {
+                const uint32_t j = it + k, s = j & 1;
+                VLoad L;
+                v_load(P, t, kvh, sg.kt0 + k, L);
+                if (j >= 2 && !(ok = wait_bar(&B->pv_done[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
+                v_store(sbase + SM_V + s * 32768, t, L);
+                fence_proxy_async();
+                mbar_arrive(&B->v_full[s]);
             }
             it += sg.nk;
         }
@@ -579,6 +687,17 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
     if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS) : "memory");
+    }
+    // Split tiles whose last part finished in this CTA: all 512 threads merge them, each thread
+    // one (row, 16-column group) pair at a time with every part's load in flight together.
+    const int n_merge = min(B->n_merge, MAX_MERGE);
+    if (n_merge > 0) {
+        __threadfence();
+        for (int item = 0; item < n_merge; item++) {
+            const int tile = B->merge[item] >> 2, q = B->merge[item] & 3;
+            // 32 rows x 64 float4 columns; thread: row 32 q + (tid >> 4), columns (tid & 15) + 16 i
+            merge_rows(P, tile, 32 * q + (tid >> 4), 16, tid & 15);
+        }
     }
 }
 

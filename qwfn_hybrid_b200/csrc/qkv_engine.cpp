@@ -806,8 +806,8 @@ extern "C" qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slo
 }
 
 // ---------------------------------------------------------------------------------- prefill
-// Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); tile t needs KV tiles
-// 0 .. nk[t]-1 (causal: up to its last query's position).  The flattened sequence of all
+// Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); tile t needs 128-key KV
+// tiles 0 .. nk[t]-1 (causal: up to its last query's position).  The flattened sequence of all
 // (tile, KV tile) pairs is cut into n_ctas equal runs; each run is a list of segments.  A tile
 // covered by more than one segment gets one partial record per segment.
 struct PfPlan {
@@ -902,7 +902,7 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     int64_t W = 0;
     for (int t = 0; t < n_tiles; t++) {
         const int g = t % n_groups, last_tok = std::min((g + 1) * tpt, Tc) - 1;
-        nk[t] = (pos0 + last_tok) / TILE_TOK + 1;
+        nk[t] = (pos0 + last_tok) / PF_KT + 1;
         W += nk[t];
     }
     PfPlan pl;

@@ -135,6 +135,7 @@ int decode_max_clusters(int nq);   // co-resident clusters of the decode kernel 
 // range is cut into segments (contiguous 64-token KV tiles); every CTA runs a contiguous run of
 // segments.  A tile cut into more than one segment is merged by its last-arriving segment.
 constexpr int PF_ROWS      = 128;
+constexpr int PF_KT        = 128;              // keys per KV tile of kernel D
 constexpr int PF_MAX_TC    = 4096;             // query tokens per call
 constexpr int PF_MAX_PARTS = 8;                // segments of one tile
 constexpr int PF_QTILE     = PF_ROWS * HD * 2; // bytes of one fp16 query tile

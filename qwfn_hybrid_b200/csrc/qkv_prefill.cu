@@ -29,37 +29,38 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 namespace qkv {
 namespace pf {
 
 constexpr int NTHR = 512;
-constexpr int KT   = TILE_TOK;         // keys per KV tile
+constexpr int KT   = PF_KT;            // keys per KV tile (N of S, K of PV): two page tiles
+static_assert(KT == 2 * TILE_TOK, "a KV tile is two 64-token page tiles");
 // shared memory map, offsets from a 1024-byte aligned base
-constexpr int SM_Q   = 0;              // [4 k-atoms][128 rows][128 B]
-constexpr int SM_K   = 65536;          // 2 stages x [4 k-atoms][64 keys][128 B]
-constexpr int SM_V   = 131072;         // 2 stages x [256 dims][128 B] (64 keys)
-constexpr int SM_P   = 196608;         // 2 x [128 rows][128 B] (64 keys)
-constexpr int SM_BAR = 229376;
+constexpr int SM_Q       = 0;          // A of S: [4 k-atoms][128 rows][128 B]
+constexpr int SM_RING    = 65536;      // NSLOT x 32 KiB half tiles (K: 128 keys x 128 dims; V: 256 dims x 64 keys)
+constexpr int NSLOT      = 5;
+constexpr int SLOT_BYTES = 32768;
+constexpr int SM_BAR     = SM_RING + NSLOT * SLOT_BYTES;
 constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
-// tensor memory columns
+// tensor memory columns: O, then two S buffers (P of a tile is stored over its S)
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
-constexpr int MAX_MERGE = 24;
+constexpr int MAX_MERGE = 16;
 
 struct Bars {
-    uint64_t k_full[2];     // K producers (128 arrivals): K_j in stage s
-    uint64_t v_full[2];     // V producers (128 arrivals): V_j in stage s
-    uint64_t k_free[2];     // commit after S_j: K stage s free
-    uint64_t pv_done[2];    // commit after PV_j: V stage s and P buffer s free, O holds tile j
-    uint64_t s_full[2];     // commit after S_j
-    uint64_t s_empty[2];    // softmax (128 arrivals): S buffer read
-    uint64_t p_full[2];     // softmax (128 arrivals): P_j written (and O rescaled)
-    uint64_t q_full;        // query tile landed (expect_tx)
-    uint64_t q_empty;       // commit after the last S of a segment
-    uint64_t drain;         // commit before exit
+    uint64_t slot_full[NSLOT];   // producers (128 arrivals): half tile in the slot
+    uint64_t slot_free[NSLOT];   // commit after the MMAs reading the slot
+    uint64_t s_full[2];          // commit after S_j
+    uint64_t p_full[2];          // softmax (128 arrivals): P_j stored (and O rescaled)
+    uint64_t pv_done[2];         // commit after PV_j
+    uint64_t q_full;             // query tile landed (expect_tx)
+    uint64_t q_empty;            // commit after the last S of a segment
+    uint64_t drain;              // commit before exit
     uint32_t tmem;
     int32_t  abort;
-    int32_t  n_merge;             // split tiles (x4 row quarters) this CTA completed last
+    int32_t  n_merge;            // split tiles (x4 row quarters) this CTA completed last
     int32_t  merge[MAX_MERGE];
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
@@ -74,12 +75,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase completes (or ~20 us
+// pass) instead of spinning on issue slots the working warps need.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
         : "memory");
     return ok != 0;
 }
@@ -94,7 +97,8 @@ __device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars *B, i
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
-        for (int i = 0; i < 32; i++)
+#pragma unroll 1
+        for (int i = 0; i < 4; i++)
             if (mbar_try_wait(bar, parity)) return true;
         if (*(volatile int32_t *)&B->abort) return false;
         if (global_ns() - t0 > WAIT_NS) {
@@ -136,7 +140,16 @@ constexpr uint32_t idesc_f16(int M, int N) { return (1u << 4) | ((uint32_t)(N >>
 constexpr uint32_t IDESC_S  = idesc_f16(PF_ROWS, KT);
 constexpr uint32_t IDESC_PV = idesc_f16(PF_ROWS, HD);
 
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A x B^T, A from tensor memory (M rows in lanes, K packed two per column)
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A x B^T, both from shared memory
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
@@ -177,6 +190,13 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -294,13 +314,15 @@ __device__ __forceinline__ Seg seg_of(const PrefillParams &P, int i) {
     return Seg{s.x, s.y, s.z - s.y, s.w};
 }
 
-// Source of KV tile kt of KV head kvh in the pages; nvalid = keys of it below n_kv (0 when the
-// block table is bad, which is reported in the status word).
+// Source of 64-token page tile kt of KV head kvh; nvalid = its keys below n_kv (<= 0: none, no
+// loads).  A block-table entry outside the pool is reported in the status word.
 struct TileSrc {
     const uint8_t *src;
     int nvalid;
 };
 __device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int kt, bool report) {
+    const int nvalid = min(TILE_TOK, P.n_kv - kt * TILE_TOK);
+    if (nvalid <= 0) return TileSrc{nullptr, 0};
     const int pi = kt >> 2;
     const int32_t page = pi < P.max_pages ? P.bt[pi] : -1;
     if (page < 0 || page >= P.n_pages) {
@@ -308,71 +330,84 @@ __device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int
         return TileSrc{nullptr, 0};
     }
     return TileSrc{P.pool + (int64_t)page * P.page_bytes + (int64_t)(kvh * TILES_PER_PAGE + (kt & 3)) * TILE_BYTES,
-                   min(KT, P.n_kv - kt * KT)};
+                   nvalid};
 }
 
-// K producer thread t (0..127): 16-dim chunk kc = t & 15 of keys (t >> 4) + 8 i, i = 0..7.
-// Raw bytes are loaded before the stage is known to be free, converted after.
+// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0..127): 16-dim chunk
+// kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 i, kb = 2 (t >> 4) + ((t >> 2) & 1),
+// i = 0..7 (i < 4 in page tile 2T, else 2T+1).  A warp reads 4 keys x 128 contiguous bytes per
+// i; the 8 lanes of a shared-store phase cover keys kb, kb+1 x chunks 0..3 of one atom, whose
+// swizzled 16-byte positions are all distinct (no bank conflicts).
 struct KLoad {
     uint4    q[8];
     uint32_t d[8];
-    int      nvalid;
+    int      nvalid[2];
 };
-__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int kt, KLoad &L) {
-    const TileSrc ts = tile_src(P, kvh, kt, t == 0);
-    L.nvalid = ts.nvalid;
-    const int kc = t & 15;
+__device__ __forceinline__ int k_chunk(int t) { return (t & 3) | (((t >> 3) & 1) << 2); }
+__device__ __forceinline__ int k_key0(int t) { return 2 * (t >> 4) + ((t >> 2) & 1); }
+__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int h, KLoad &L) {
+    const int kc = 8 * h + k_chunk(t), kb = k_key0(t);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int key = (t >> 4) + 8 * i;
-        if (ts.src) {
-            L.q[i] = ldg_nc16(ts.src + TILE_KQ + key * HD + ((kc ^ kswz(key)) << 4));
-            L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(key, kc >> 1));
-        } else {
-            L.q[i] = make_uint4(0, 0, 0, 0);
-            L.d[i] = 0;
+    for (int sub = 0; sub < 2; sub++) {
+        const TileSrc ts = tile_src(P, kvh, 2 * T + sub, t == 0 && h == 0);
+        L.nvalid[sub] = ts.nvalid;
+#pragma unroll
+        for (int i = 4 * sub; i < 4 * sub + 4; i++) {
+            const int tk = (kb + 16 * i) & 63;
+            if (ts.src) {
+                L.q[i] = ldg_nc16(ts.src + TILE_KQ + tk * HD + ((kc ^ kswz(tk)) << 4));
+                L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(tk, kc >> 1));
+            } else {
+                L.q[i] = make_uint4(0, 0, 0, 0);
+                L.d[i] = 0;
+            }
         }
     }
 }
-__device__ __forceinline__ void k_store(uint32_t kbase, int t, const KLoad &L) {
-    const int kc = t & 15;
-    const uint32_t atom = kbase + (kc >> 2) * (KT * 128);
+// K half image: [2 atoms of 64 dims][128 keys][128 B], 128-byte swizzled.
+__device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
+    const int kc = k_chunk(t), kb = k_key0(t);
+    const uint32_t atom = slot + (kc >> 2) * (KT * 128);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const int key = (t >> 4) + 8 * i;
-        const uint32_t d2 = key < L.nvalid ? (L.d[i] | (L.d[i] << 16)) : 0u;
+        const int key = kb + 16 * i;
+        const uint32_t d2 = (key & 63) < L.nvalid[i >> 2] ? (L.d[i] | (L.d[i] << 16)) : 0u;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
-        uint32_t h[8];
+        uint32_t hh[8];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             uint32_t lo, hi;
             s8x4_to_f16(w[e], lo, hi);
-            h[2 * e]     = hmul2(lo, d2);
-            h[2 * e + 1] = hmul2(hi, d2);
+            hh[2 * e]     = hmul2(lo, d2);
+            hh[2 * e + 1] = hmul2(hi, d2);
         }
-        sts16(swz(atom, key, (kc & 3) * 2), make_uint4(h[0], h[1], h[2], h[3]));
-        sts16(swz(atom, key, (kc & 3) * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
+        sts16(swz(atom, key, (kc & 3) * 2), make_uint4(hh[0], hh[1], hh[2], hh[3]));
+        sts16(swz(atom, key, (kc & 3) * 2 + 1), make_uint4(hh[4], hh[5], hh[6], hh[7]));
     }
 }
 
-// V producer thread t (0..127): tokens 16 vc .. 16 vc + 15 (vc = t & 3) of the 8 dims
-// 32 b + 8 sub + i (b = t >> 4, sub = (t >> 2) & 3, i = 0..7), which share one set of scales.
+// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0..127): tokens
+// 16 vc .. 16 vc + 15 (vc = t & 3) of the 8 dims 32 b + sub + 4 i (b = t >> 4,
+// sub = (t >> 2) & 3, i = 0..7), all in q8_0 block b, so they share one set of scales.  Per i a
+// warp reads 2 x 4 consecutive dims x 64 bytes; a shared-store phase covers 2 adjacent dims (rows
+// of different swizzle parity) x 4 chunks: no bank conflicts.
 struct VLoad {
     uint4 q[8];
     uint4 d0, d1;
     int   nvalid;
 };
+__device__ __forceinline__ int v_dim0(int t) { return 32 * (t >> 4) + ((t >> 2) & 3); }
 __device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, VLoad &L) {
     const TileSrc ts = tile_src(P, kvh, kt, false);
     L.nvalid = ts.nvalid;
-    const int b = t >> 4, vc = t & 3, d0 = 32 * b + 8 * ((t >> 2) & 3);
+    const int vc = t & 3, d0 = v_dim0(t);
     if (ts.src) {
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const int dim = d0 + i;
-            L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * KT + ((vc ^ ((dim >> 1) & 3)) << 4));
+            const int dim = d0 + 4 * i;
+            L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * TILE_TOK + ((vc ^ ((dim >> 1) & 3)) << 4));
         }
-        const uint8_t *vd = ts.src + vd_off(b, vc * 16);
+        const uint8_t *vd = ts.src + vd_off(t >> 4, vc * 16);
         L.d0 = ldg_nc16(vd);
         L.d1 = ldg_nc16(vd + 16);
     } else {
@@ -381,8 +416,9 @@ __device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, i
         L.d0 = L.d1 = make_uint4(0, 0, 0, 0);
     }
 }
-__device__ __forceinline__ void v_store(uint32_t vbase, int t, const VLoad &L) {
-    const int vc = t & 3, d0 = 32 * (t >> 4) + 8 * ((t >> 2) & 3);
+// V half image: [256 dims][128 B = 64 keys], 128-byte swizzled.
+__device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
+    const int vc = t & 3, d0 = v_dim0(t);
     uint32_t dv[8] = {L.d0.x, L.d0.y, L.d0.z, L.d0.w, L.d1.x, L.d1.y, L.d1.z, L.d1.w};
 #pragma unroll
     for (int e = 0; e < 8; e++) {   // tokens 16 vc + 2e, +1: zero scales past n_kv
@@ -391,18 +427,75 @@ __device__ __forceinline__ void v_store(uint32_t vbase, int t, const VLoad &L) {
     }
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const int dim = d0 + i;
+        const int dim = d0 + 4 * i;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
-        uint32_t h[8];
+        uint32_t hh[8];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             uint32_t lo, hi;
             s8x4_to_f16(w[e], lo, hi);
-            h[2 * e]     = hmul2(lo, dv[2 * e]);
-            h[2 * e + 1] = hmul2(hi, dv[2 * e + 1]);
+            hh[2 * e]     = hmul2(lo, dv[2 * e]);
+            hh[2 * e + 1] = hmul2(hi, dv[2 * e + 1]);
         }
-        sts16(swz(vbase, dim, vc * 2), make_uint4(h[0], h[1], h[2], h[3]));
-        sts16(swz(vbase, dim, vc * 2 + 1), make_uint4(h[4], h[5], h[6], h[7]));
+        sts16(swz(slot, dim, vc * 2), make_uint4(hh[0], hh[1], hh[2], hh[3]));
+        sts16(swz(slot, dim, vc * 2 + 1), make_uint4(hh[4], hh[5], hh[6], hh[7]));
+    }
+}
+
+// Ring order of a segment's K/V tiles: K_0, then (K_k, V_{k-1}) for k = 1 .. nk-1, then V_{nk-1}
+// (the MMA issue order S_0, S_1, PV_0, S_2, PV_1, ...).  Every op fills two ring slots.
+__device__ __forceinline__ uint32_t op_k(int k) { return k == 0 ? 0u : (uint32_t)(2 * k - 1); }
+__device__ __forceinline__ uint32_t op_v(int k, int nk) { return k == nk - 1 ? (uint32_t)(2 * nk - 1) : (uint32_t)(2 * k + 2); }
+
+// One producer group's walk over its half tiles in ring order (K group: the K ops, V group: the
+// V ops), software-pipelined by one half tile.
+template <bool KGRP>
+__device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_t sbase, int t, int s0, int s1) {
+    using Load = typename std::conditional<KGRP, KLoad, VLoad>::type;
+    // walk of this group's half tiles: segment si, tile k, half h; ring op of the tile = op0 + op_k/op_v
+    int si = s0, k = 0, h = 0;
+    uint32_t op0 = 0;
+    Seg sg{};
+    if (si < s1) sg = seg_of(P, si);
+    auto load_next = [&](Load &L, uint32_t &u) -> bool {   // false: walk finished
+        if (si >= s1) return false;
+        const int kvh = sg.tile / P.n_groups;
+        if constexpr (KGRP) {
+            k_load(P, t, kvh, sg.kt0 + k, h, L);
+            u = 2 * (op0 + op_k(k)) + h;
+        } else {
+            v_load(P, t, kvh, 2 * (sg.kt0 + k) + h, L);
+            u = 2 * (op0 + op_v(k, sg.nk)) + h;
+        }
+        if (++h == 2) {
+            h = 0;
+            if (++k == sg.nk) {
+                k = 0;
+                op0 += 2 * sg.nk;
+                if (++si < s1) sg = seg_of(P, si);
+            }
+        }
+        return true;
+    };
+    auto store = [&](const Load &ld, uint32_t u) -> bool {
+        const uint32_t sl = u % NSLOT;
+        if (u >= NSLOT && !wait_bar(&B->slot_free[sl], ((u / NSLOT) - 1) & 1, B, P.status)) return false;
+        const uint32_t slot = sbase + SM_RING + sl * SLOT_BYTES;
+        if constexpr (KGRP) k_store(slot, t, ld);
+        else v_store(slot, t, ld);
+        fence_proxy_async();
+        mbar_arrive(&B->slot_full[sl]);
+        return true;
+    };
+    // one half tile in flight while the previous one is converted and stored
+    Load A, Bn;
+    uint32_t uA = 0, uB = 0;
+    if (!load_next(A, uA)) return;
+    for (;;) {
+        const bool hasB = load_next(Bn, uB);
+        if (!store(A, uA) || !hasB) return;
+        const bool hasA = load_next(A, uA);
+        if (!store(Bn, uB) || !hasA) return;
     }
 }
 
@@ -415,14 +508,14 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
     const int s0 = P.cta_seg[blockIdx.x], s1 = P.cta_seg[blockIdx.x + 1];
 
     if (tid == 0) {
+        for (int i = 0; i < NSLOT; i++) {
+            mbar_init(&B->slot_full[i], 128);
+            mbar_init(&B->slot_free[i], 1);
+        }
         for (int i = 0; i < 2; i++) {
-            mbar_init(&B->k_full[i], 128);
-            mbar_init(&B->v_full[i], 128);
-            mbar_init(&B->k_free[i], 1);
-            mbar_init(&B->pv_done[i], 1);
             mbar_init(&B->s_full[i], 1);
-            mbar_init(&B->s_empty[i], 128);
             mbar_init(&B->p_full[i], 128);
+            mbar_init(&B->pv_done[i], 1);
         }
         mbar_init(&B->q_full, 1);
         mbar_init(&B->q_empty, 1);
@@ -442,23 +535,49 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
     tc_fence_after();
     const uint32_t tmem = B->tmem;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ MMA issue
-        if (lane == 0) {
+    if (warp < 4) {
+        // ------------------------------------------------------------------ MMA issue (warp 0)
+        if (warp == 0 && lane == 0) {
             bool ok = true;
             int q_pending = -1;   // parity of a query copy still in flight after an abort
-            uint32_t it = 0;
-            const uint32_t qa = sbase + SM_Q, ka = sbase + SM_K, va = sbase + SM_V, pa = sbase + SM_P;
-            auto issue_pv = [&](uint32_t j, bool first) -> bool {
-                const uint32_t s = j & 1;
-                if (!wait_bar(&B->v_full[s], (j >> 1) & 1, B, P.status)) return false;
-                if (!wait_bar(&B->p_full[s], (j >> 1) & 1, B, P.status)) return false;
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < KT / 16; kk++)
-                    mma_f16(tmem + TM_O, sdesc(pa + s * 16384 + kk * 32), sdesc(va + s * 32768 + kk * 32), IDESC_PV,
-                            (first && kk == 0) ? 0u : 1u);
-                mma_commit(&B->pv_done[s]);
+            uint32_t it = 0, op0 = 0;
+            const uint32_t qa = sbase + SM_Q, ra = sbase + SM_RING;
+            // wait for ring slot u (the u-th half-tile of this CTA); returns its address
+            auto slot_wait = [&](uint32_t u, uint32_t &addr) -> bool {
+                const uint32_t sl = u % NSLOT;
+                addr = ra + sl * SLOT_BYTES;
+                return wait_bar(&B->slot_full[sl], (u / NSLOT) & 1, B, P.status);
+            };
+            auto issue_s = [&](uint32_t j, uint32_t op) -> bool {
+                const uint32_t d = tmem + TM_S + (j & 1) * KT;
+                for (int h = 0; h < 2; h++) {
+                    uint32_t kaddr;
+                    if (!slot_wait(2 * op + h, kaddr)) return false;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int kk = 0; kk < 8; kk++)
+                        mma_f16_ss(d, sdesc(qa + (2 * h + (kk >> 2)) * 16384 + (kk & 3) * 32),
+                                   sdesc(kaddr + (kk >> 2) * (KT * 128) + (kk & 3) * 32), IDESC_S,
+                                   (h == 0 && kk == 0) ? 0u : 1u);
+                    mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
+                }
+                mma_commit(&B->s_full[j & 1]);
+                return true;
+            };
+            auto issue_pv = [&](uint32_t j, uint32_t op, bool first) -> bool {
+                const uint32_t b = j & 1;
+                if (!wait_bar(&B->p_full[b], (j >> 1) & 1, B, P.status)) return false;
+                for (int h = 0; h < 2; h++) {
+                    uint32_t vaddr;
+                    if (!slot_wait(2 * op + h, vaddr)) return false;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * KT + (4 * h + kk) * 8, sdesc(vaddr + kk * 32),
+                                   IDESC_PV, (first && h == 0 && kk == 0) ? 0u : 1u);
+                    mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
+                }
+                mma_commit(&B->pv_done[b]);
                 return true;
             };
             for (int si = s0; si < s1 && ok; si++) {
@@ -474,32 +593,27 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 }
                 tc_fence_after();
                 for (int k = 0; k < sg.nk && ok; k++) {
-                    const uint32_t j = it + k, s = j & 1, ph = (j >> 1) & 1;
-                    if (!(ok = wait_bar(&B->k_full[s], ph, B, P.status))) break;
-                    if (j >= 2 && !(ok = wait_bar(&B->s_empty[s], ph ^ 1, B, P.status))) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < HD / 16; kk++)
-                        mma_f16(tmem + TM_S + s * KT, sdesc(qa + (kk >> 2) * 16384 + (kk & 3) * 32),
-                                sdesc(ka + s * 32768 + (kk >> 2) * 8192 + (kk & 3) * 32), IDESC_S, kk > 0 ? 1u : 0u);
-                    mma_commit(&B->s_full[s]);
-                    mma_commit(&B->k_free[s]);
-                    if (k == sg.nk - 1) mma_commit(&B->q_empty);
-                    if (k >= 1) ok = issue_pv(j - 1, k == 1);
+                    ok = issue_s(it + k, op0 + op_k(k));
+                    if (ok && k == sg.nk - 1) mma_commit(&B->q_empty);
+                    if (ok && k >= 1) ok = issue_pv(it + k - 1, op0 + op_v(k - 1, sg.nk), k == 1);
                 }
-                if (ok) ok = issue_pv(it + sg.nk - 1, sg.nk == 1);
+                if (ok) ok = issue_pv(it + sg.nk - 1, op0 + op_v(sg.nk - 1, sg.nk), sg.nk == 1);
                 it += sg.nk;
+                op0 += 2 * sg.nk;
             }
             if (q_pending >= 0) drain_bar(&B->q_full, (uint32_t)q_pending, P.status);
             mma_commit(&B->drain);
             drain_bar(&B->drain, 0, P.status);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp < 8) {
         // ------------------------------------------------------------------ softmax
-        // Control flow is kept warp-uniform (tcgen05.ld/st are warp-collective): every wait's
-        // result is agreed with __all_sync.  Split segments are merged per warp (32 rows) with a
-        // per-(tile, warp) arrival counter, so no barrier spans warps.
+        // Thread r owns row r (TMEM lane r).  Control flow is warp-uniform (tcgen05.ld/st are
+        // warp-collective): every wait's result is agreed with __all_sync.  Per 128-key tile the
+        // S row is read in four 32-column chunks and P (fp16 pairs) kept in registers; if a chunk
+        // raises the row max by more than 2^8 over the reference, the reference moves up and the
+        // tile's P so far, l and (at the end) O are rescaled.  P is then stored over the S
+        // columns it came from (the next MMA into this buffer is issued after PV reads P).
         const int r = tid - 128, wq = warp & 3;
         const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
         auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
@@ -514,63 +628,56 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             const int qpos = tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
             for (int k = 0; k < sg.nk; k++) {
-                const uint32_t j = it + k, s = j & 1, ph = (j >> 1) & 1;
-                if (!(ok = wait_all(&B->s_full[s], ph))) break;
+                const uint32_t j = it + k, b = j & 1;
+                if (!(ok = wait_all(&B->s_full[b], (j >> 1) & 1))) break;
                 tc_fence_after();
-                uint32_t v0[32], v1[32];
-                tmem_ld32(tmem + lane_base + TM_S + s * KT, v0);
-                tmem_ld32(tmem + lane_base + TM_S + s * KT + 32, v1);
-                tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(&B->s_empty[s]);
+                const uint32_t scol = tmem + lane_base + TM_S + b * KT;
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
-                float2 x2[32];   // raw scores; masked keys -inf (2^-inf = 0 below)
+                const bool full = __all_sync(0xffffffffu, nvis == KT);
+                // pass 1: row max over the tile (keys past the row's position are -inf)
                 float smax = -INFINITY;
-                if (__all_sync(0xffffffffu, nvis == KT)) {
+#pragma unroll 1
+                for (int c = 0; c < KT / 32; c++) {
+                    uint32_t v[32];
+                    tmem_ld32(scol + 32 * c, v);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 16; c++) {
-                        x2[c]      = make_float2(__uint_as_float(v0[2 * c]), __uint_as_float(v0[2 * c + 1]));
-                        x2[c + 16] = make_float2(__uint_as_float(v1[2 * c]), __uint_as_float(v1[2 * c + 1]));
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 16; c++) {
-                        x2[c]      = make_float2(2 * c < nvis ? __uint_as_float(v0[2 * c]) : -INFINITY,
-                                                 2 * c + 1 < nvis ? __uint_as_float(v0[2 * c + 1]) : -INFINITY);
-                        x2[c + 16] = make_float2(2 * c + 32 < nvis ? __uint_as_float(v1[2 * c]) : -INFINITY,
-                                                 2 * c + 33 < nvis ? __uint_as_float(v1[2 * c + 1]) : -INFINITY);
-                    }
+                    for (int e = 0; e < 32; e++)
+                        smax = fmaxf(smax, (full || 32 * c + e < nvis) ? __uint_as_float(v[e]) : -INFINITY);
                 }
-#pragma unroll
-                for (int c = 0; c < 32; c++) smax = fmaxf(smax, fmaxf(x2[c].x, x2[c].y));
+                // lazily raised reference max: O and l are rescaled only when a row max grows by
+                // more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
                 const float mx = smax * P.scale_log2;   // scale > 0: max of scaled = scaled max
-                // lazily raised reference max: O and l are rescaled only when a row max grows
-                // by more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
                 const bool need = mx > m_ref + 8.0f;
-                const float f = (need && m_ref != -INFINITY) ? ex2(m_ref - mx) : 1.0f;
-                const bool rescale = k > 0 && __any_sync(0xffffffffu, f != 1.0f);
+                const float F = (need && m_ref != -INFINITY) ? ex2(m_ref - mx) : 1.0f;
                 if (need) m_ref = mx;
-                l *= f;
-                if (j >= 2 && !(ok = wait_all(&B->pv_done[s], ph ^ 1))) break;
-                const uint32_t prow = sbase + SM_P + s * 16384;
-                const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: all p = 0
+                l *= F;
+                const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: p = 0
                 const float2 sc2 = make_float2(P.scale_log2, P.scale_log2), nm2 = make_float2(-mu, -mu);
+                // pass 2: P = 2^(s * scale - m) as fp16 pairs, stored over the S columns already read
+                // (chunk c's 32 keys -> P columns 16c .. 16c+15, inside S columns 0 .. 32c+31)
                 float2 l2 = make_float2(0.f, 0.f);
+#pragma unroll 1
+                for (int c = 0; c < KT / 32; c++) {
+                    uint32_t v[32];
+                    tmem_ld32(scol + 32 * c, v);
+                    tmem_wait_ld();
+                    uint32_t pr[16];
 #pragma unroll
-                for (int c8 = 0; c8 < 8; c8++) {
-                    uint32_t h[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float2 y = __ffma2_rn(x2[c8 * 4 + e], sc2, nm2);
+                    for (int e = 0; e < 16; e++) {
+                        const int i = 32 * c + 2 * e;
+                        const float2 y = __ffma2_rn(make_float2(full || i < nvis ? __uint_as_float(v[2 * e]) : -INFINITY,
+                                                                full || i + 1 < nvis ? __uint_as_float(v[2 * e + 1]) : -INFINITY),
+                                                    sc2, nm2);
                         const float2 p = make_float2(ex2(y.x), ex2(y.y));
                         l2 = __fadd2_rn(l2, p);
                         const __half2 hp = __floats2half2_rn(p.x, p.y);
-                        h[e] = *reinterpret_cast<const uint32_t *>(&hp);
+                        pr[e] = *reinterpret_cast<const uint32_t *>(&hp);
                     }
-                    sts16(swz(prow, r, c8), make_uint4(h[0], h[1], h[2], h[3]));
+                    tmem_st16(scol + 16 * c, pr);
                 }
                 l += l2.x + l2.y;
-                if (rescale) {
+                if (k > 0 && __any_sync(0xffffffffu, F != 1.0f)) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
                     tc_fence_after();
@@ -580,14 +687,13 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                         tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * F);
                         tmem_st32(tmem + lane_base + TM_O + c8 * 32, o);
                     }
-                    tmem_wait_st();
                 }
-                fence_proxy_async();
+                tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&B->p_full[s]);
+                mbar_arrive(&B->p_full[b]);
             }
             if (!ok) break;
             // ---- epilogue: O of the segment
@@ -643,44 +749,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             tc_fence_before();
             it += sg.nk;
         }
-    } else if (warp >= 8 && warp < 12) {
-        // ------------------------------------------------------------------ K producers
-        const int t = tid - 256;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int si = s0; si < s1 && ok; si++) {
-            const Seg sg = seg_of(P, si);
-            const int kvh = sg.tile / P.n_groups;
-            for (int k = 0; k < sg.nk; k++) {
-                const uint32_t j = it + k, s = j & 1;
-                KLoad L;
-                k_load(P, t, kvh, sg.kt0 + k, L);
-                if (j >= 2 && !(ok = wait_bar(&B->k_free[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
-                k_store(sbase + SM_K + s * 32768, t, L);
-                fence_proxy_async();
-                mbar_arrive(&B->k_full[s]);
-            }
-            it += sg.nk;
-        }
-    } else if (warp >= 12) {
-        // ------------------------------------------------------------------ V producers
-        const int t = tid - 384;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int si = s0; si < s1 && ok; si++) {
-            const Seg sg = seg_of(P, si);
-            const int kvh = sg.tile / P.n_groups;
-            for (int k = 0; k < sg.nk; k++) {
-                const uint32_t j = it + k, s = j & 1;
-                VLoad L;
-                v_load(P, t, kvh, sg.kt0 + k, L);
-                if (j >= 2 && !(ok = wait_bar(&B->pv_done[s], ((j >> 1) & 1) ^ 1, B, P.status))) break;
-                v_store(sbase + SM_V + s * 32768, t, L);
-                fence_proxy_async();
-                mbar_arrive(&B->v_full[s]);
-            }
-            it += sg.nk;
-        }
+    } else {
+        // ------------------------------------------------------------------ producers
+        // warps 8-11 fill the K halves, warps 12-15 the V halves of the ring.  Loads run one half
+        // tile ahead: the next half's bytes are in flight while this one is converted and stored.
+        if (warp < 12) produce<true>(P, B, sbase, tid - 256, s0, s1);
+        else produce<false>(P, B, sbase, tid - 384, s0, s1);
     }
     tc_fence_before();
     __syncthreads();
@@ -695,7 +769,6 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         __threadfence();
         for (int item = 0; item < n_merge; item++) {
             const int tile = B->merge[item] >> 2, q = B->merge[item] & 3;
-            // 32 rows x 64 float4 columns; thread: row 32 q + (tid >> 4), columns (tid & 15) + 16 i
             merge_rows(P, tile, 32 * q + (tid >> 4), 16, tid & 15);
         }
     }

@@ -26,8 +26,8 @@
 //   PV  warp w: its 64 dims x all query rows over the 64 tokens.  mma.m16n8k16 f16 with
 //       A = V^T int8 widened to f16 exactly (byte permute + bias subtract) and B = P * dv.
 // Optional fused append (dense only): the unit owning a tile that holds one of the T new
-// positions quantises those rows (kernel A's rounding), stores them in the cache and patches its
-// shared-memory copy of the tile before use.
+// positions quantises those rows (kernel A's rounding) in its prologue and stores them in the
+// page, then starts the bulk copy of that tile, which thus brings the new rows with it.
 #include "qkv.h"
 #include "qkv_internal.h"
 
@@ -159,7 +159,6 @@ struct Smem {
     float    rowM[NQ + CN], rowL[NQ + CN];
     uint64_t full[NS];
     int32_t  stage_blk[NS];              // block id of the tile in each stage (-1 skip, < -1 error)
-    uint8_t *stage_src[NS];              // its global address (the fused append writes through it)
     int32_t  merge_flag;
 };
 
@@ -184,8 +183,11 @@ __device__ __forceinline__ Unit unit_of(const DecodeParams &P, int u) {
     x.h = off / per;
     const int r = off % per;
     x.p = lo * P.n_head_kv + x.h;
-    x.t0 = (int)((int64_t)tiles * r / per);
-    x.t1 = (int)((int64_t)tiles * (r + 1) / per);
+    // the first tiles % per units take one tile more, so the pair's last unit -- the one holding
+    // the newest positions and any fused append -- has the fewest
+    const int base = tiles / per, rem = tiles % per;
+    x.t0 = r * base + min(r, rem);
+    x.t1 = x.t0 + base + (r < rem ? 1 : 0);
     x.pu0 = P.seq_unit0[lo] + x.h * per;
     x.pu1 = x.pu0 + per;
     return x;
@@ -222,7 +224,6 @@ __device__ __forceinline__ void issue_ref(const DecodeParams &P, Smem<NT> &sm, c
     constexpr int NS = Smem<NT>::NS;
     uint64_t *bar = &sm.full[i % NS];
     sm.stage_blk[i % NS] = r.blk;    // published to the consumers by the barrier's completion
-    sm.stage_src[i % NS] = r.src;
     if (r.blk >= 0) {
         fence_proxy_async();
         mbar_expect_tx(bar, TILE_BYTES);
@@ -237,48 +238,45 @@ __device__ __forceinline__ void issue_tile(const DecodeParams &P, Smem<NT> &sm, 
     issue_ref<NT>(P, sm, tile_ref(P, U, U.t0 + i), i);
 }
 
-// Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h, store
-// them in the cache tile in global memory and in the shared-memory copy.  Warp per 32-element
-// block, all of a warp's loads issued before the first is used; the rounding is kernel A's.
-__device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &U, uint8_t *gtile, uint8_t *stile,
-                                             int cell0) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h and store
+// them in the cache tile in global memory.  One thread per (row, 32-element block, K or V): it
+// loads its 32 values with eight vector loads and rounds them exactly as kernel A does.
+__device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &U, uint8_t *gtile, int cell0) {
     const int pos0 = P.seq_pos0[U.s];
     const int r0 = max(pos0, cell0), r1 = min(pos0 + P.T, cell0 + TILE_TOK);
-    const int work = (r1 - r0) * NBLK * 2;   // (row, block, K or V) items, at most 4 * 8 * 2
-    constexpr int MAXW = 4 * NBLK * 2 / 4;   // items per warp
-    float x[MAXW];
+    const int work = (r1 - r0) * NBLK * 2;   // at most 4 * 8 * 2 = 64 <= blockDim
+    const int wi = threadIdx.x;
+    if (wi >= work) return;
+    const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
+    const float4 *src = reinterpret_cast<const float4 *>(
+        (kv ? P.Vnew : P.Knew) + (((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK);
+    float x[QK];
 #pragma unroll
-    for (int q = 0; q < MAXW; q++) {
-        const int wi = warp + 4 * q;
-        x[q] = 0.0f;
-        if (wi < work) {
-            const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
-            x[q] = (kv ? P.Vnew : P.Knew)[(((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK + lane];
-        }
+    for (int i = 0; i < QK / 4; i++) {
+        const float4 v = src[i];
+        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
     }
+    float amax = 0.0f;
 #pragma unroll
-    for (int q = 0; q < MAXW; q++) {
-        const int wi = warp + 4 * q;
-        if (wi >= work) break;   // warp-uniform
-        const int kv = wi & 1, b = (wi >> 1) % NBLK, row = r0 + (wi >> 1) / NBLK;
-        float amax = fabsf(x[q]);
+    for (int i = 0; i < QK; i++) amax = fmaxf(amax, fabsf(x[i]));
+    const float d  = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    uint32_t q[QK / 4];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float d  = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-        const uint8_t qv = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x[q], id));
-        const __half dh = __float2half_rn(d);
-        const int t = row - cell0, dim = b * QK + lane;
-        const int qo = kv ? v_off(dim, t) : k_off(t, dim);
-        const int so = kv ? vd_off(b, t) : kd_off(t, b);
-        stile[qo] = qv;
-        gtile[qo] = qv;
-        if (lane == 0) {
-            *reinterpret_cast<__half *>(stile + so) = dh;
-            *reinterpret_cast<__half *>(gtile + so) = dh;
-        }
+    for (int i = 0; i < QK / 4; i++) {
+        q[i] = 0;
+#pragma unroll
+        for (int e = 0; e < 4; e++) q[i] |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(x[4 * i + e], id)) << (8 * e);
     }
+    const int t = row - cell0;
+    if (!kv) {   // two swizzled 16-byte chunks of the token's K row
+        *reinterpret_cast<uint4 *>(gtile + TILE_KQ + t * HD + (((2 * b) ^ kswz(t)) << 4)) = make_uint4(q[0], q[1], q[2], q[3]);
+        *reinterpret_cast<uint4 *>(gtile + TILE_KQ + t * HD + (((2 * b + 1) ^ kswz(t)) << 4)) = make_uint4(q[4], q[5], q[6], q[7]);
+    } else {     // V is stored transposed: one byte in each of the block's 32 dims
+#pragma unroll
+        for (int e = 0; e < QK; e++) gtile[v_off(b * QK + e, t)] = (uint8_t)(q[e >> 2] >> (8 * (e & 3)));
+    }
+    *reinterpret_cast<__half *>(gtile + (kv ? vd_off(b, t) : kd_off(t, b))) = __float2half_rn(d);
 }
 
 // CTA = 4 warps, up to 4 CTAs per SM.  Per 64-token tile, warp w computes QK for tokens
@@ -321,6 +319,10 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
         constexpr int QP = (NQ + 3) / 4;   // rows per warp
         // thread 0 looks up the first tiles' pages before the query loads, so both are in flight
+        // fused append (dense only): tiles nb_lo .. nb_hi hold the T new positions; the unit that
+        // owns one writes the new rows into the page before it copies that tile in (below)
+        const int nb_lo = pos0 / TILE_TOK, nb_hi = (pos0 + P.T - 1) / TILE_TOK;
+        const bool appends = P.Knew != nullptr && U.t1 > nb_lo && U.t0 <= nb_hi;
         TileRef first[NS];
         if (tid == 0)
             for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
@@ -342,7 +344,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         if (tid == 0) {
             for (int st = 0; st < NS; st++) mbar_init(&sm.full[st], 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-            for (int st = 0; st < NS && st < n_tiles; st++) issue_ref<NT>(P, sm, first[st], st);
+            for (int st = 0; st < NS && st < n_tiles; st++)
+                if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref<NT>(P, sm, first[st], st);
         }
         // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row
 #pragma unroll
@@ -390,7 +393,17 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         const int k_key = kswz(k_tok), k_hi = lmat >> 1;
         const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);   // tokens of the S rows
         const int v_dim0 = 64 * w + 8 * lmat + lm;   // V^T row this lane addresses (+32: second block)
+        if (appends) {
+            for (int t = max(U.t0, nb_lo); t <= min(U.t1 - 1, nb_hi); t++) {
+                const TileRef r = tile_ref(P, U, t);
+                if (r.blk >= 0) fused_append(P, U, r.src, t * TILE_TOK);
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");   // the rows before the bulk copy reads them
+        }
         __syncthreads();   // query rows ready, barriers initialised
+        if (appends && tid == 0)   // the first tiles held back for the append
+            for (int st = 0; st < NS && st < n_tiles; st++)
+                if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref<NT>(P, sm, first[st], st);
 
         for (int i = 0; i < n_tiles; i++) {
             const int stage = i % NS;
@@ -400,11 +413,6 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             uint8_t *tile = sm.tile[stage];
             const bool live = blk >= 0 && !aborted;
             const int cell0 = blk * TILE_TOK;
-            if (P.Knew && blk >= 0 && cell0 + TILE_TOK > pos0) {   // uniform over the CTA
-                __syncthreads();
-                fused_append(P, U, sm.stage_src[stage], tile, cell0);
-                __syncthreads();
-            }
             // ---------------- QK for this warp's 16 tokens ----------------------------------------
             float S[NT][4];
 #pragma unroll

@@ -576,6 +576,19 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
         if (n_units <= target) break;
         scale_u *= 0.9 * (double)target / (double)n_units;
     }
+    // The launch lasts as long as its longest unit: where the budget allows, raise a pair's units
+    // (whole clusters) until the most tiles any unit gets drops by one.
+    for (int i = 0; i < ns; i++) {
+        const int64_t u = units[i];
+        const int64_t k = (tiles[i] + u - 1) / u;
+        if (k <= 1 || u < CN) continue;
+        int64_t u2 = (tiles[i] + k - 2) / (k - 1);
+        u2 = (u2 + CN - 1) / CN * CN;
+        if (n_units + (u2 - u) * H <= target) {
+            n_units += (u2 - u) * H;
+            units[i] = (int32_t)u2;
+        }
+    }
     std::vector<int32_t> order(ns);
     for (int i = 0; i < ns; i++) order[i] = i;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) {

@@ -318,14 +318,18 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         // 32 threads per row, 8 elements each (4 threads per 32-element block).
         const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
         constexpr int QP = (NQ + 3) / 4;   // rows per warp
-        // thread 0 looks up the first tiles' pages before the query loads, so both are in flight
         // fused append (dense only): tiles nb_lo .. nb_hi hold the T new positions; the unit that
         // owns one writes the new rows into the page before it copies that tile in (below)
         const int nb_lo = pos0 / TILE_TOK, nb_hi = (pos0 + P.T - 1) / TILE_TOK;
         const bool appends = P.Knew != nullptr && U.t1 > nb_lo && U.t0 <= nb_hi;
-        TileRef first[NS];
-        if (tid == 0)
-            for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+        if (appends) {   // the new rows' 128-byte blocks, into L1 now for the append below
+            const int r0 = max(pos0, max(U.t0, nb_lo) * TILE_TOK), nrow = min(pos0 + P.T, U.t1 * TILE_TOK) - r0;
+            if (tid < nrow * NBLK * 2) {
+                const int kv = tid & 1, b = (tid >> 1) % NBLK, row = r0 + (tid >> 1) / NBLK;
+                const float *src = (kv ? P.Vnew : P.Knew) + (((int64_t)U.io * P.T + (row - pos0)) * P.n_head_kv + U.h) * HD + b * QK;
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(src));
+            }
+        }
         float qv[QP][8];
 #pragma unroll
         for (int it = 0; it < QP; it++) {
@@ -341,6 +345,11 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 for (int q = 0; q < 8; q++) qv[it][q] = 0.0f;
             }
         }
+        // thread 0 resolves the first tiles' pages once its query loads are in flight (the branch
+        // on a loaded page would otherwise hold those loads back)
+        TileRef first[NS];
+        if (tid == 0)
+            for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
         if (tid == 0) {
             for (int st = 0; st < NS; st++) mbar_init(&sm.full[st], 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

@@ -295,19 +295,25 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, tig = lane & 3;
     const int u = blockIdx.x;
     const int k = u / CN;   // cluster index
+    // The next launch on the stream may start as soon as every CTA of this one got here; it then
+    // waits (below) until this grid has completed and its writes are visible.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bool has_unit = u < P.n_units;
     Unit U{};
     int n_tiles = 0;
     int gb = 0, gs = 1, me = 0;
     bool extends = false;   // the pair has units in other clusters too
     if (has_unit) {
-        U = unit_of(P, u);
+        U = unit_of(P, u);   // kernel parameters only
         n_tiles = U.t1 - U.t0;
         gb = max(U.pu0, k * CN);
         gs = min(U.pu1, (k + 1) * CN) - gb;
         me = u - gb;
         extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
     }
+    // Everything global below (pages, block table, queries, new rows, scratch, output) may have
+    // been written by the previous kernel on the stream: wait for it to complete.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
     bool aborted = false;
 
@@ -792,13 +798,17 @@ static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = dec::CN;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // programmatic dependent launch: this grid may become resident while the previous kernel on
+    // the stream finishes (if that kernel triggers, as k_decode does); it waits before any read
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, dec::k_decode<NT>, p);
     count_launches(1);
     return e;
@@ -820,13 +830,17 @@ static int max_clusters_nt() {
     cfg.gridDim = dim3(dec::CN * 64);
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = dec::CN;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // programmatic dependent launch: this grid may become resident while the previous kernel on
+    // the stream finishes (if that kernel triggers, as k_decode does); it waits before any read
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, dec::k_decode<NT>, &cfg) != cudaSuccess) {
         cudaGetLastError();

@@ -76,7 +76,6 @@ struct qkv_engine {
     // kernel D scratch, allocated by the first prefill call
     uint8_t  *d_pf_q        = nullptr;    // query tiles
     float    *d_pf_partial  = nullptr;    // split-segment partials
-    int32_t  *d_pf_counters = nullptr;    // [tiles][4]
     int32_t  *d_pf_plan     = nullptr;    // segments, tile parts, CTA offsets
     int32_t   pf_max_tiles = 0, pf_max_parts = 0, pf_plan_ints = 0;
     size_t    device_bytes = 0;
@@ -283,7 +282,6 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_status);
     cudaFree(eng->d_pf_q);
     cudaFree(eng->d_pf_partial);
-    cudaFree(eng->d_pf_counters);
     cudaFree(eng->d_pf_plan);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
@@ -821,13 +819,13 @@ extern "C" qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slo
 // ---------------------------------------------------------------------------------- prefill
 // Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); tile t needs 128-key KV
 // tiles 0 .. nk[t]-1 (causal: up to its last query's position).  The flattened sequence of all
-// (tile, KV tile) pairs is cut into n_ctas equal runs; each run is a list of segments.  A tile
-// covered by more than one segment gets one partial record per segment.
+// (tile, KV tile) pairs is cut into n_ctas equal runs; each run is a list of segments, and every
+// segment writes one partial record (parts of a tile are consecutive, in KV order).
 struct PfPlan {
     std::vector<int32_t> segs;        // 4 per segment: tile, kt0, kt1, part
     std::vector<int32_t> tile_parts;  // 2 per tile: parts, first part
     std::vector<int32_t> cta_seg;     // n_ctas + 1
-    int32_t n_parts = 0, max_parts = 0;
+    int32_t n_parts = 0;
 };
 static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPlan &pl) {
     const int n_tiles = (int)nk.size();
@@ -853,17 +851,15 @@ static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPl
     pl.cta_seg[n_ctas] = (int32_t)(pl.segs.size() / 4);
     pl.tile_parts.assign(2 * n_tiles, 0);
     pl.n_parts = 0;
-    pl.max_parts = 0;
     for (int i = 0; i < n_tiles; i++) {
-        pl.max_parts = std::max(pl.max_parts, count[i]);
         pl.tile_parts[2 * i] = count[i];
-        pl.tile_parts[2 * i + 1] = count[i] > 1 ? pl.n_parts : -1;
-        if (count[i] > 1) pl.n_parts += count[i];
+        pl.tile_parts[2 * i + 1] = pl.n_parts;
+        pl.n_parts += count[i];
     }
     std::vector<int32_t> next(n_tiles, 0);
     for (size_t i = 0; i < pl.segs.size(); i += 4) {
         const int tile = pl.segs[i];
-        if (count[tile] > 1) pl.segs[i + 3] = pl.tile_parts[2 * tile + 1] + next[tile]++;
+        pl.segs[i + 3] = pl.tile_parts[2 * tile + 1] + next[tile]++;
     }
 }
 
@@ -871,22 +867,18 @@ static qkv_status pf_scratch(qkv_engine *eng) {
     if (eng->d_pf_q) return QKV_OK;
     const int G = eng->cfg.n_head / eng->cfg.n_head_kv, tpt = PF_ROWS / G;
     eng->pf_max_tiles = eng->cfg.n_head_kv * ((PF_MAX_TC + tpt - 1) / tpt);
-    eng->pf_max_parts = 2 * eng->num_sms;   // every CTA boundary splits at most one tile in two
+    eng->pf_max_parts = eng->pf_max_tiles + eng->num_sms;   // every CTA boundary adds at most one segment
     eng->pf_plan_ints = 4 * (eng->pf_max_tiles + eng->num_sms) + 2 * eng->pf_max_tiles + eng->num_sms + 1;
     qkv_status r = dalloc(eng, eng->d_pf_q, (size_t)eng->pf_max_tiles * PF_QTILE, "prefill query tiles");
     if (r == QKV_OK)
         r = dalloc(eng, eng->d_pf_partial, (size_t)eng->pf_max_parts * pf_part_floats() * 4, "prefill partials");
-    if (r == QKV_OK) r = dalloc(eng, eng->d_pf_counters, (size_t)eng->pf_max_tiles * 4 * 4, "prefill counters");
     if (r == QKV_OK) r = dalloc(eng, eng->d_pf_plan, (size_t)eng->pf_plan_ints * 4, "prefill plan");
-    if (r == QKV_OK) CK(eng, cudaMemset(eng->d_pf_counters, 0, (size_t)eng->pf_max_tiles * 4 * 4));
     if (r != QKV_OK) {
         cudaFree(eng->d_pf_q);
         cudaFree(eng->d_pf_partial);
-        cudaFree(eng->d_pf_counters);
         cudaFree(eng->d_pf_plan);
         eng->d_pf_q = nullptr;
         eng->d_pf_partial = nullptr;
-        eng->d_pf_counters = nullptr;
         eng->d_pf_plan = nullptr;
     }
     return r;
@@ -919,15 +911,10 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
         W += nk[t];
     }
     PfPlan pl;
-    int n_ctas = (int)std::min<int64_t>(eng->num_sms, W);
-    for (;;) {
-        pf_build(nk, W, n_ctas, pl);
-        if (pl.max_parts <= PF_MAX_PARTS || n_ctas == 1) break;
-        n_ctas = std::max(1, n_ctas * 3 / 4);
-    }
-    if (pl.n_parts > eng->pf_max_parts || pl.max_parts > PF_MAX_PARTS)
-        return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %d parts (max %d), %d per tile", pl.n_parts, eng->pf_max_parts,
-                    pl.max_parts);
+    const int n_ctas = (int)std::min<int64_t>(eng->num_sms, W);
+    pf_build(nk, W, n_ctas, pl);
+    if (pl.n_parts > eng->pf_max_parts)
+        return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %d parts (max %d)", pl.n_parts, eng->pf_max_parts);
     std::vector<int32_t> ints;
     ints.reserve(pl.segs.size() + pl.tile_parts.size() + pl.cta_seg.size());
     ints.insert(ints.end(), pl.segs.begin(), pl.segs.end());
@@ -946,7 +933,6 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     P.qtiles = eng->d_pf_q;
     P.out = out;
     P.partial = eng->d_pf_partial;
-    P.counters = eng->d_pf_counters;
     P.status = eng->d_status;
     P.segs = reinterpret_cast<const int4 *>(eng->d_pf_plan);
     P.tile_parts = reinterpret_cast<const int2 *>(eng->d_pf_plan + off_tiles);

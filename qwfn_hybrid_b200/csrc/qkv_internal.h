@@ -132,13 +132,15 @@ int decode_max_clusters(int nq);   // co-resident clusters of the decode kernel 
 
 // ---- kernel D -----------------------------------------------------------------------------------
 // A prefill tile is 128 rows = (128 / G) query tokens x the G q-heads of one KV head.  Its KV
-// range is cut into segments (contiguous 64-token KV tiles); every CTA runs a contiguous run of
-// segments.  A tile cut into more than one segment is merged by its last-arriving segment.
+// range is cut into segments (contiguous 128-key KV tiles); every CTA runs a contiguous run of
+// segments.  Each segment leaves a partial record (unnormalised O, row max, row sum); a second
+// kernel merges the records of every tile and writes the output.
 constexpr int PF_ROWS      = 128;
 constexpr int PF_KT        = 128;              // keys per KV tile of kernel D
 constexpr int PF_MAX_TC    = 4096;             // query tokens per call
-constexpr int PF_MAX_PARTS = 8;                // segments of one tile
 constexpr int PF_QTILE     = PF_ROWS * HD * 2; // bytes of one fp16 query tile
+// partial record: O as [HD/4 float4 columns][PF_ROWS rows][4] (a warp's rows are adjacent, so the
+// epilogue's stores coalesce), then m[PF_ROWS] (log2 domain), then l[PF_ROWS]
 __host__ __device__ __forceinline__ int64_t pf_part_floats() { return (int64_t)PF_ROWS * HD + 2 * PF_ROWS; }
 struct PrefillParams {
     const uint8_t  *pool;
@@ -146,11 +148,10 @@ struct PrefillParams {
     const uint16_t *Q;            // bf16 bits [Tc][n_head][HD]
     uint8_t        *qtiles;       // scratch [n_tiles][PF_QTILE]: q8_0-rounded queries, fp16, MMA layout
     float          *out;          // [Tc][n_head][HD]
-    float          *partial;      // scratch [parts][pf_part_floats()]
-    int32_t        *counters;     // scratch [n_tiles][4] (per tile and row quarter), zero between launches
+    float          *partial;      // scratch [parts][pf_part_floats()], one record per segment
     int32_t        *status;
     const int32_t  *cta_seg;      // [n_ctas + 1] first segment of each CTA
-    const int4     *segs;         // {tile, kv tile begin, kv tile end, part or -1}
+    const int4     *segs;         // {tile, kv tile begin, kv tile end, part}
     const int2     *tile_parts;   // {number of parts, first part}
     int64_t page_bytes;
     int32_t n_pages, max_pages, n_head, n_head_kv, G, tpt, n_groups, n_tiles, Tc, pos0, n_kv, n_ctas;

@@ -10,7 +10,8 @@
 //
 // Tile: 128 rows = (128 / G) query tokens x the G q-heads sharing one KV head, so each K/V tile
 // is dequantised once for all of them.  A CTA (16 warps, one per SM) runs a contiguous run of
-// segments (tile, KV range) from a host plan that gives every CTA the same number of KV tiles.
+// segments (tile, KV range) from a host plan that gives every CTA the same number of KV tiles;
+// each segment leaves a partial record, merged per tile by k_prefill_merge.
 //   warp 0      TMEM allocation; one thread issues all MMAs and the query-tile bulk copies
 //   warps 4-7   softmax: thread r owns row r (TMEM lane r): S row from TMEM, causal mask,
 //               online softmax with a lazily raised reference max (O in TMEM rescaled only when
@@ -47,7 +48,6 @@ constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 // tensor memory columns: O, then two S buffers (P of a tile is stored over its S)
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
-constexpr int MAX_MERGE = 16;
 
 struct Bars {
     uint64_t slot_full[NSLOT];   // producers (128 arrivals): half tile in the slot
@@ -60,8 +60,6 @@ struct Bars {
     uint64_t drain;              // commit before exit
     uint32_t tmem;
     int32_t  abort;
-    int32_t  n_merge;            // split tiles (x4 row quarters) this CTA completed last
-    int32_t  merge[MAX_MERGE];
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
@@ -265,44 +263,6 @@ __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
     }
     uint8_t *dst = P.qtiles + (int64_t)tile * PF_QTILE + (lane >> 3) * (PF_ROWS * 128) + r * 128 + (((lane & 7) ^ (r & 7)) << 4);
     *reinterpret_cast<uint4 *>(dst) = o;
-}
-
-// Merge the partial records of split tile `tile` for row `row`, float4 columns c0, c0+step, ...
-// into the output: O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p.
-__device__ __forceinline__ void merge_rows(const PrefillParams &P, int tile, int row, int step, int c0) {
-    const int2 tp = P.tile_parts[tile];
-    const int kvh = tile / P.n_groups, g = tile % P.n_groups;
-    const int tok = g * P.tpt + row / P.G, head = kvh * P.G + row % P.G;
-    if (tok >= P.Tc) return;
-    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
-    float w[PF_MAX_PARTS];
-    float M = -INFINITY, L = 0.f;
-#pragma unroll
-    for (int p = 0; p < PF_MAX_PARTS; p++)
-        w[p] = p < tp.x ? __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + row) : -INFINITY;
-#pragma unroll
-    for (int p = 0; p < PF_MAX_PARTS; p++) M = fmaxf(M, w[p]);
-#pragma unroll
-    for (int p = 0; p < PF_MAX_PARTS; p++) {
-        w[p] = w[p] == -INFINITY ? 0.f : ex2(w[p] - M);
-        if (p < tp.x) L += w[p] * __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + PF_ROWS + row);
-    }
-    const float inv = L > 0.f ? 1.0f / L : 0.f;
-    float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
-    for (int c = c0; c < HD / 4; c += step) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int p = 0; p < PF_MAX_PARTS; p++) {
-            if (p < tp.x) {
-                const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + p * pf_part_floats() + row * HD) + c);
-                acc.x += w[p] * v.x;
-                acc.y += w[p] * v.y;
-                acc.z += w[p] * v.z;
-                acc.w += w[p] * v.w;
-            }
-        }
-        reinterpret_cast<float4 *>(dst)[c] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -521,7 +481,6 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         mbar_init(&B->q_empty, 1);
         mbar_init(&B->drain, 1);
         B->abort = 0;
-        B->n_merge = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -623,8 +582,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         bool ok = true;
         for (int si = s0; si < s1 && ok; si++) {
             const Seg sg = seg_of(P, si);
-            const int kvh = sg.tile / P.n_groups, g = sg.tile % P.n_groups;
-            const int tok = g * P.tpt + r / P.G, head = kvh * P.G + r % P.G;
+            const int tok = (sg.tile % P.n_groups) * P.tpt + r / P.G;
             const int qpos = tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
             for (int k = 0; k < sg.nk; k++) {
@@ -700,23 +658,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             const uint32_t jl = it + sg.nk - 1;
             if (!(ok = wait_all(&B->pv_done[jl & 1], (jl >> 1) & 1))) break;
             tc_fence_after();
-            if (sg.part < 0) {
-                const float inv = l > 0.f ? 1.0f / l : 0.f;
-                float *dst = P.out + ((int64_t)tok * P.n_head + head) * HD;
-#pragma unroll 1
-                for (int c8 = 0; c8 < HD / 32; c8++) {
-                    uint32_t o[32];
-                    tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
-                    tmem_wait_ld();
-                    if (tok < P.Tc) {
-#pragma unroll
-                        for (int c = 0; c < 32; c += 4)
-                            *reinterpret_cast<float4 *>(dst + c8 * 32 + c) =
-                                make_float4(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv,
-                                            __uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-                    }
-                }
-            } else {
+            {   // the segment's partial record; stores of a warp cover 32 adjacent rows
                 float *rec = P.partial + (int64_t)sg.part * pf_part_floats();
 #pragma unroll 1
                 for (int c8 = 0; c8 < HD / 32; c8++) {
@@ -724,27 +666,13 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                     tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 32; c += 4)
-                        __stcg(reinterpret_cast<float4 *>(rec + r * HD + c8 * 32 + c),
-                               make_float4(__uint_as_float(o[c]), __uint_as_float(o[c + 1]), __uint_as_float(o[c + 2]),
-                                           __uint_as_float(o[c + 3])));
+                    for (int q = 0; q < 8; q++)
+                        __stcg(reinterpret_cast<float4 *>(rec) + (int64_t)(c8 * 8 + q) * PF_ROWS + r,
+                               make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
+                                           __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3])));
                 }
                 __stcg(rec + PF_ROWS * HD + r, m_ref);
                 __stcg(rec + PF_ROWS * HD + PF_ROWS + r, l);
-                __threadfence();
-                __syncwarp();
-                const int2 tp = P.tile_parts[sg.tile];
-                int last = 0;
-                if (lane == 0 && atomicAdd(&P.counters[sg.tile * 4 + wq], 1) == tp.x - 1) {
-                    P.counters[sg.tile * 4 + wq] = 0;   // ready for the next launch
-                    const int idx = atomicAdd(&B->n_merge, 1);
-                    if (idx < MAX_MERGE) B->merge[idx] = sg.tile * 4 + wq;
-                    else last = 1;   // list full: merge here
-                }
-                if (__shfl_sync(0xffffffffu, last, 0)) {
-                    __threadfence();
-                    merge_rows(P, sg.tile, 32 * wq + lane, 1, 0);
-                }
             }
             tc_fence_before();
             it += sg.nk;
@@ -762,15 +690,52 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS) : "memory");
     }
-    // Split tiles whose last part finished in this CTA: all 512 threads merge them, each thread
-    // one (row, 16-column group) pair at a time with every part's load in flight together.
-    const int n_merge = min(B->n_merge, MAX_MERGE);
-    if (n_merge > 0) {
-        __threadfence();
-        for (int item = 0; item < n_merge; item++) {
-            const int tile = B->merge[item] >> 2, q = B->merge[item] & 3;
-            merge_rows(P, tile, 32 * q + (tid >> 4), 16, tid & 15);
+}
+
+// Merge of the segments' partial records of every tile: O = sum_p 2^(m_p - M) O_p / sum_p
+// 2^(m_p - M) l_p, parts in order.  CTA = (tile, 32-row quarter), 256 threads.  Reads: thread
+// (row = t & 31, column group t >> 5) walks 8 float4 columns, adjacent threads adjacent rows
+// (coalesced in the record layout); the rows go through shared memory so that the output, rows of
+// 256 contiguous floats, is written by threads along each row.
+constexpr int MG_ROWS = 32;
+__global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
+    __shared__ float4 rows[MG_ROWS][HD / 4 + 1];
+    const int tile = blockIdx.x >> 2, r0 = (blockIdx.x & 3) * MG_ROWS;
+    const int t = threadIdx.x, rr = t & (MG_ROWS - 1), fg = t >> 5, row = r0 + rr;
+    const int2 tp = P.tile_parts[tile];
+    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
+    float M = -INFINITY;
+    for (int p = 0; p < tp.x; p++) M = fmaxf(M, __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + row));
+    float4 acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll 1
+    for (int p = 0; p < tp.x; p++) {
+        const float *rec = base + p * pf_part_floats();
+        const float mp = __ldcg(rec + PF_ROWS * HD + row);
+        const float w = mp == -INFINITY ? 0.f : ex2(mp - M);
+        L += w * __ldcg(rec + PF_ROWS * HD + PF_ROWS + row);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(rec) + (int64_t)(fg * 8 + i) * PF_ROWS + row);
+            acc[i].x += w * v.x;
+            acc[i].y += w * v.y;
+            acc[i].z += w * v.z;
+            acc[i].w += w * v.w;
         }
+    }
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        rows[rr][fg * 8 + i] = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
+    __syncthreads();
+    const int kvh = tile / P.n_groups, g = tile % P.n_groups;
+#pragma unroll 1
+    for (int e = t; e < MG_ROWS * (HD / 4); e += 256) {
+        const int q = e & (HD / 4 - 1), rw = r0 + e / (HD / 4);
+        const int tok = g * P.tpt + rw / P.G, head = kvh * P.G + rw % P.G;
+        if (tok < P.Tc) reinterpret_cast<float4 *>(P.out + ((int64_t)tok * P.n_head + head) * HD)[q] = rows[e / (HD / 4)][q];
     }
 }
 
@@ -788,7 +753,9 @@ cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     pf::k_prefill<<<p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st>>>(p);
-    count_launches(2);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    pf::k_prefill_merge<<<p.n_tiles * (PF_ROWS / pf::MG_ROWS), 256, 0, st>>>(p);
+    count_launches(3);
     return cudaGetLastError();
 }
 

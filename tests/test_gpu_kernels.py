@@ -160,8 +160,10 @@ def test_sparse_config4_full_size(cuda, qkvlib, oracle):
 @pytest.mark.parametrize("T", [1, 3, 4])
 def test_fused_append_decode_vs_oracle(cuda, qkvlib, oracle, T):
     """Kernel A fused into kernel C: the appended bytes and the attention both match."""
-    lens = [1500, 64 - T, 255, 3]
-    eng = engine(qkvlib, n_slots=5)
+    # 6334 and 20478: the new rows straddle two tiles of sequences long enough that different
+    # units may own them (each unit writes its rows into the page before copying that tile in)
+    lens = [1500, 64 - T, 255, 3, 6334, 20478]
+    eng = engine(qkvlib, n_slots=6, n_ctx=20608)
     K0, V0, Kn, Vn = {}, {}, {}, {}
     for i, n in enumerate(lens):
         eng.seq_alloc(i)
@@ -200,3 +202,17 @@ def test_decode_many_units_many_clusters(cuda, qkvlib, oracle):
         for i, n in enumerate(lens):
             ref = oracle.attn(Q[i], kv[i][0], kv[i][1], np.arange(n - 2, n), 2, 1 / 16)
             assert_close(got[i], ref, f"rep {rep} seq {i}")
+
+
+def test_decode_widest_group_t4_g16(cuda, qkvlib, oracle):
+    """The largest query group a pair holds: T=4 tokens x 16 q-heads over one KV head (64 rows)."""
+    eng = engine(qkvlib, n_head=16, n_head_kv=1)
+    eng.seq_alloc(0)
+    n, T = 3001, 4
+    Kf, Vf = normal(31, (n, HD)), normal(32, (n, HD))
+    append_rows(eng, 0, 0, 0, Kf, Vf)
+    K, V = read_rows(eng, 0, 0, 0, n, n_head_kv=1)
+    Q = normal(33, (T, 16, HD))
+    got = decode(eng, 0, [0], [n - T], Q, T)
+    ref = oracle.attn(Q, K, V, np.arange(n - T, n), 1, 1 / 16)
+    assert_close(got.reshape(ref.shape), ref, "T=4 G=16")

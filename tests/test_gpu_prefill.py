@@ -99,3 +99,22 @@ def test_prefill_rejects_unappended_and_bad_sizes(qkvlib):
         eng.attn_prefill(0, 0, 0, q, 32, 1 / 16, out)
         torch.cuda.synchronize()
         assert eng.device_status() == 0
+
+
+def test_prefill_group_of_sixteen(oracle, qkvlib):
+    # 16 q-heads per KV head: tiles of 8 tokens x 16 heads
+    got, ref = run_prefill(oracle, qkvlib, n_kv=700, pos0=290, Tc=410, seed=27, n_head=16, n_head_kv=1)
+    assert_close(got, ref, "G=16")
+
+
+def test_prefill_one_head_per_kv_head(oracle, qkvlib):
+    # G = 1: tiles of 128 tokens of one head
+    got, ref = run_prefill(oracle, qkvlib, n_kv=900, pos0=500, Tc=400, seed=28, n_head=2, n_head_kv=2)
+    assert_close(got, ref, "G=1")
+
+
+@pytest.mark.parametrize("n_kv", [256, 257, 384])
+def test_prefill_single_query_at_boundaries(oracle, qkvlib, n_kv):
+    # one query token whose position ends a page, starts one, or ends a 128-key tile
+    got, ref = run_prefill(oracle, qkvlib, n_kv=n_kv, pos0=n_kv - 1, Tc=1, seed=29 + n_kv)
+    assert_close(got, ref, f"Tc=1 at {n_kv - 1}")

@@ -9,14 +9,14 @@
 // exact), products accumulate in fp32.
 //
 // Tile: 128 rows = (128 / G) query tokens x the G q-heads sharing one KV head, so each K/V tile
-// is dequantised once for all of them.  A CTA (16 warps, one per SM) runs a contiguous run of
+// is dequantised once for all of them.  A CTA (24 warps, one per SM) runs a contiguous run of
 // segments (tile, KV range) from a host plan that gives every CTA the same number of KV tiles;
 // each segment leaves a partial record, merged per tile by k_prefill_merge.
 //   warp 0      TMEM allocation; one thread issues all MMAs and the query-tile bulk copies
 //   warps 4-7   softmax: thread r owns row r (TMEM lane r): S row from TMEM, causal mask,
 //               online softmax with a lazily raised reference max (O in TMEM rescaled only when
 //               the row max grows by more than 2^8), P as fp16 into shared memory
-//   warps 8-11  K producers, warps 12-15 V producers: read q8_0 tiles from the pages (issued
+//   warps 8-15  K producers, warps 16-23 V producers: read q8_0 tiles from the pages (issued
 //               before the stage is free), dequantise to fp16 into the 128-byte-swizzled K-major
 //               layouts the MMAs read.  A K stage frees when its S MMA completes, a V stage when
 //               its PV MMA completes, so K of tile j+2 is written while PV of tile j runs.
@@ -35,7 +35,7 @@
 namespace qkv {
 namespace pf {
 
-constexpr int NTHR = 512;
+constexpr int NTHR = 768;
 constexpr int KT   = PF_KT;            // keys per KV tile (N of S, K of PV): two page tiles
 static_assert(KT == 2 * TILE_TOK, "a KV tile is two 64-token page tiles");
 // shared memory map, offsets from a 1024-byte aligned base
@@ -50,7 +50,7 @@ constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
 
 struct Bars {
-    uint64_t slot_full[NSLOT];   // producers (128 arrivals): half tile in the slot
+    uint64_t slot_full[NSLOT];   // producers (256 arrivals): half tile in the slot
     uint64_t slot_free[NSLOT];   // commit after the MMAs reading the slot
     uint64_t s_full[2];          // commit after S_j
     uint64_t p_full[2];          // softmax (128 arrivals): P_j stored (and O rescaled)
@@ -293,18 +293,19 @@ __device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int
                    nvalid};
 }
 
-// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0..127): 16-dim chunk
-// kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 i, kb = 2 (t >> 4) + ((t >> 2) & 1),
-// i = 0..7 (i < 4 in page tile 2T, else 2T+1).  A warp reads 4 keys x 128 contiguous bytes per
-// i; the 8 lanes of a shared-store phase cover keys kb, kb+1 x chunks 0..3 of one atom, whose
-// swizzled 16-byte positions are all distinct (no bank conflicts).
+// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0..255): 16-dim chunk
+// kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 (2 i + g), kb = 2 ((t >> 4) & 7) +
+// ((t >> 2) & 1), g = t >> 7, i = 0..3 (i < 2 in page tile 2T, else 2T+1).  A warp reads 4 keys x
+// 128 contiguous bytes per i; the 8 lanes of a shared-store phase cover keys kb, kb+1 x chunks 0..3
+// of one atom, whose swizzled 16-byte positions are all distinct (no bank conflicts).
+constexpr int KPT = 4;   // K chunks per producer thread and half tile
 struct KLoad {
-    uint4    q[8];
-    uint32_t d[8];
+    uint4    q[KPT];
+    uint32_t d[KPT];
     int      nvalid[2];
 };
 __device__ __forceinline__ int k_chunk(int t) { return (t & 3) | (((t >> 3) & 1) << 2); }
-__device__ __forceinline__ int k_key0(int t) { return 2 * (t >> 4) + ((t >> 2) & 1); }
+__device__ __forceinline__ int k_key0(int t) { return 2 * ((t >> 4) & 7) + ((t >> 2) & 1) + 16 * (t >> 7); }
 __device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int h, KLoad &L) {
     const int kc = 8 * h + k_chunk(t), kb = k_key0(t);
 #pragma unroll
@@ -312,8 +313,8 @@ __device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, i
         const TileSrc ts = tile_src(P, kvh, 2 * T + sub, t == 0 && h == 0);
         L.nvalid[sub] = ts.nvalid;
 #pragma unroll
-        for (int i = 4 * sub; i < 4 * sub + 4; i++) {
-            const int tk = (kb + 16 * i) & 63;
+        for (int i = 2 * sub; i < 2 * sub + 2; i++) {
+            const int tk = (kb + 32 * i) & 63;
             if (ts.src) {
                 L.q[i] = ldg_nc16(ts.src + TILE_KQ + tk * HD + ((kc ^ kswz(tk)) << 4));
                 L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(tk, kc >> 1));
@@ -329,9 +330,9 @@ __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     const int kc = k_chunk(t), kb = k_key0(t);
     const uint32_t atom = slot + (kc >> 2) * (KT * 128);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int key = kb + 16 * i;
-        const uint32_t d2 = (key & 63) < L.nvalid[i >> 2] ? (L.d[i] | (L.d[i] << 16)) : 0u;
+    for (int i = 0; i < KPT; i++) {
+        const int key = kb + 32 * i;
+        const uint32_t d2 = (key & 63) < L.nvalid[i >> 1] ? (L.d[i] | (L.d[i] << 16)) : 0u;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -346,33 +347,34 @@ __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     }
 }
 
-// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0..127): tokens
-// 16 vc .. 16 vc + 15 (vc = t & 3) of the 8 dims 32 b + sub + 4 i (b = t >> 4,
-// sub = (t >> 2) & 3, i = 0..7), all in q8_0 block b, so they share one set of scales.  Per i a
-// warp reads 2 x 4 consecutive dims x 64 bytes; a shared-store phase covers 2 adjacent dims (rows
-// of different swizzle parity) x 4 chunks: no bank conflicts.
+// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0..255): tokens
+// 16 vc .. 16 vc + 15 (vc = t & 3) of the 4 dims 32 b + sub + 4 (2 i + g) (b = (t >> 4) & 7,
+// sub = (t >> 2) & 3, g = t >> 7, i = 0..3), all in q8_0 block b, so they share one set of
+// scales.  Per i a warp reads 2 x 4 consecutive dims x 64 bytes; a shared-store phase covers 2
+// adjacent dims (rows of different swizzle parity) x 4 chunks: no bank conflicts.
+constexpr int VPT = 4;   // V dims per producer thread and half tile
 struct VLoad {
-    uint4 q[8];
+    uint4 q[VPT];
     uint4 d0, d1;
     int   nvalid;
 };
-__device__ __forceinline__ int v_dim0(int t) { return 32 * (t >> 4) + ((t >> 2) & 3); }
+__device__ __forceinline__ int v_dim0(int t) { return 32 * ((t >> 4) & 7) + ((t >> 2) & 3) + 4 * (t >> 7); }
 __device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, VLoad &L) {
     const TileSrc ts = tile_src(P, kvh, kt, false);
     L.nvalid = ts.nvalid;
     const int vc = t & 3, d0 = v_dim0(t);
     if (ts.src) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int dim = d0 + 4 * i;
+        for (int i = 0; i < VPT; i++) {
+            const int dim = d0 + 8 * i;
             L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * TILE_TOK + ((vc ^ ((dim >> 1) & 3)) << 4));
         }
-        const uint8_t *vd = ts.src + vd_off(t >> 4, vc * 16);
+        const uint8_t *vd = ts.src + vd_off((t >> 4) & 7, vc * 16);
         L.d0 = ldg_nc16(vd);
         L.d1 = ldg_nc16(vd + 16);
     } else {
 #pragma unroll
-        for (int i = 0; i < 8; i++) L.q[i] = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < VPT; i++) L.q[i] = make_uint4(0, 0, 0, 0);
         L.d0 = L.d1 = make_uint4(0, 0, 0, 0);
     }
 }
@@ -386,8 +388,8 @@ __device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
         dv[e] &= t0 + 1 < L.nvalid ? 0xffffffffu : (t0 < L.nvalid ? 0x0000ffffu : 0u);
     }
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int dim = d0 + 4 * i;
+    for (int i = 0; i < VPT; i++) {
+        const int dim = d0 + 8 * i;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -469,7 +471,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&B->slot_full[i], 128);
+            mbar_init(&B->slot_full[i], 256);
             mbar_init(&B->slot_free[i], 1);
         }
         for (int i = 0; i < 2; i++) {
@@ -679,10 +681,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         }
     } else {
         // ------------------------------------------------------------------ producers
-        // warps 8-11 fill the K halves, warps 12-15 the V halves of the ring.  Loads run one half
+        // warps 8-15 fill the K halves, warps 16-23 the V halves of the ring.  Loads run one half
         // tile ahead: the next half's bytes are in flight while this one is converted and stored.
-        if (warp < 12) produce<true>(P, B, sbase, tid - 256, s0, s1);
-        else produce<false>(P, B, sbase, tid - 384, s0, s1);
+        if (warp < 16) produce<true>(P, B, sbase, tid - 256, s0, s1);
+        else produce<false>(P, B, sbase, tid - 512, s0, s1);
     }
     tc_fence_before();
     __syncthreads();

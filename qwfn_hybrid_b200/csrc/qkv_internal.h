@@ -140,8 +140,9 @@ constexpr int PF_KT        = 128;              // keys per KV tile of kernel D
 constexpr int PF_MAX_TC    = 4096;             // query tokens per call
 constexpr int PF_QTILE     = PF_ROWS * HD * 2; // bytes of one fp16 query tile
 // partial record: O as [HD/4 float4 columns][PF_ROWS rows][4] (a warp's rows are adjacent, so the
-// epilogue's stores coalesce), then m[PF_ROWS] (log2 domain), then l[PF_ROWS]
-__host__ __device__ __forceinline__ int64_t pf_part_floats() { return (int64_t)PF_ROWS * HD + 2 * PF_ROWS; }
+// epilogue's stores coalesce), then m[PF_ROWS] (log2 domain), then the row sums l[2][PF_ROWS] of
+// the two key halves (l = l[0] + l[1])
+__host__ __device__ __forceinline__ int64_t pf_part_floats() { return (int64_t)PF_ROWS * HD + 3 * PF_ROWS; }
 struct PrefillParams {
     const uint8_t  *pool;
     const int32_t  *bt;           // block-table row of the slot

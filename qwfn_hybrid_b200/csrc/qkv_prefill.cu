@@ -35,7 +35,13 @@
 namespace qkv {
 namespace pf {
 
-constexpr int NTHR = 768;
+// warps: 0 MMA issue, 1 .. 4 SMX_GROUPS softmax, then 4 NGRP K producers and 4 NGRP V producers
+constexpr int SMX_GROUPS = 2;          // softmax warp groups (column halves of S)
+constexpr int NGRP       = 1;          // 128-thread producer groups per operand
+constexpr bool PROD_DB   = false;      // producers double-buffer their loads
+constexpr int PW_K       = 1 + 4 * SMX_GROUPS;
+constexpr int PW_V       = PW_K + 4 * NGRP;
+constexpr int NTHR       = 32 * (PW_V + 4 * NGRP);
 constexpr int KT   = PF_KT;            // keys per KV tile (N of S, K of PV): two page tiles
 static_assert(KT == 2 * TILE_TOK, "a KV tile is two 64-token page tiles");
 // shared memory map, offsets from a 1024-byte aligned base
@@ -50,10 +56,11 @@ constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
 
 struct Bars {
-    uint64_t slot_full[NSLOT];   // producers (256 arrivals): half tile in the slot
+    uint64_t slot_full[NSLOT];   // producers (128 NGRP arrivals): half tile in the slot
     uint64_t slot_free[NSLOT];   // commit after the MMAs reading the slot
     uint64_t s_full[2];          // commit after S_j
-    uint64_t p_full[2];          // softmax (128 arrivals): P_j stored (and O rescaled)
+    uint64_t s_read[2];          // softmax (256 arrivals): both halves read S_j (P may overwrite it)
+    uint64_t p_full[2];          // softmax (256 arrivals): P_j stored (and O rescaled)
     uint64_t pv_done[2];         // commit after PV_j
     uint64_t q_full;             // query tile landed (expect_tx)
     uint64_t q_empty;            // commit after the last S of a segment
@@ -89,9 +96,19 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Non-blocking test of the phase of `parity`.
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Wait for the phase of `parity` to complete.  Returns false when another role aborted or the
 // wait ran past WAIT_NS (then it raises the abort flag and ST_TIMEOUT itself).
-__device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars *B, int32_t *status) {
+__device__ __noinline__ bool wait_bar_slow(uint64_t *bar, uint32_t parity, Bars *B, int32_t *status) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
@@ -105,6 +122,10 @@ __device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars *B, i
             return false;
         }
     }
+}
+// A phase that already completed is seen inline, without the call.
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars *B, int32_t *status) {
+    return mbar_test(bar, parity) || wait_bar_slow(bar, parity, B, status);
 }
 // Bounded wait that ignores the abort flag (draining in-flight asynchronous work before exit).
 __device__ __noinline__ void drain_bar(uint64_t *bar, uint32_t parity, int32_t *status) {
@@ -199,6 +220,60 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// Max of the thread's S row (KT columns from TMEM address scol); columns >= nvis count as -inf
+// unless FULL.  Read in 32-column chunks, each reduced as a tree.
+template <bool FULL>
+__device__ __forceinline__ float row_max(uint32_t scol, int nvis) {
+    float m = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < KT / 32; c++) {
+        uint32_t v[32];
+        tmem_ld32(scol + 32 * c, v);
+        tmem_wait_ld();
+        float x[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) x[e] = (FULL || 32 * c + e < nvis) ? __uint_as_float(v[e]) : -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
+        m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
+    }
+    return m;
+}
+// P = 2^(s * sl2 - mu) of keys 64 half .. 64 half + 63 of the thread's row, stored as fp16 pairs:
+// chunk c's 32 keys go to columns 16 c + 32 half .. +15, inside the S columns this half already
+// read.  Returns the sum of the P values.
+template <bool FULL>
+__device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, float sl2, float mu) {
+    const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-mu, -mu);
+    float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int c = 2 * half; c < 2 * half + 2; c++) {
+        uint32_t v[32];
+        tmem_ld32(scol + 32 * c, v);
+        tmem_wait_ld();
+        uint32_t pr[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            const int i = 32 * c + 2 * e;
+            const float2 y = __ffma2_rn(make_float2(FULL || i < nvis ? __uint_as_float(v[2 * e]) : -INFINITY,
+                                                    FULL || i + 1 < nvis ? __uint_as_float(v[2 * e + 1]) : -INFINITY),
+                                        sc2, nm2);
+            const float2 p = make_float2(ex2(y.x), ex2(y.y));
+            if (e & 1) lb = __fadd2_rn(lb, p);
+            else la = __fadd2_rn(la, p);
+            const __half2 hp = __floats2half2_rn(p.x, p.y);
+            pr[e] = *reinterpret_cast<const uint32_t *>(&hp);
+        }
+        tmem_st16(scol + 16 * c + 32 * half, pr);
+    }
+    return (la.x + lb.x) + (la.y + lb.y);
+}
+
 __device__ __forceinline__ uint4 ldg_nc16(const void *p) {
     uint4 v;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
@@ -280,11 +355,15 @@ struct TileSrc {
     const uint8_t *src;
     int nvalid;
 };
-__device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int kt, bool report) {
+// Page-table entry of page tile kt (-1 past the table).
+__device__ __forceinline__ int32_t page_of(const PrefillParams &P, int kt) {
+    const int pi = kt >> 2;
+    return pi < P.max_pages ? __ldg(P.bt + pi) : -1;
+}
+// Page tile kt of KV head kvh, whose page-table entry is `page`.
+__device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int kt, int32_t page, bool report) {
     const int nvalid = min(TILE_TOK, P.n_kv - kt * TILE_TOK);
     if (nvalid <= 0) return TileSrc{nullptr, 0};
-    const int pi = kt >> 2;
-    const int32_t page = pi < P.max_pages ? P.bt[pi] : -1;
     if (page < 0 || page >= P.n_pages) {
         if (report) atomicOr(P.status, ST_BAD_PAGE);
         return TileSrc{nullptr, 0};
@@ -293,12 +372,13 @@ __device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int
                    nvalid};
 }
 
-// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0..255): 16-dim chunk
-// kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 (2 i + g), kb = 2 ((t >> 4) & 7) +
-// ((t >> 2) & 1), g = t >> 7, i = 0..3 (i < 2 in page tile 2T, else 2T+1).  A warp reads 4 keys x
-// 128 contiguous bytes per i; the 8 lanes of a shared-store phase cover keys kb, kb+1 x chunks 0..3
-// of one atom, whose swizzled 16-byte positions are all distinct (no bank conflicts).
-constexpr int KPT = 4;   // K chunks per producer thread and half tile
+// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0 .. 128 NGRP - 1):
+// 16-dim chunk kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 NGRP i, kb =
+// 2 ((t >> 4) & 7) + ((t >> 2) & 1) + 16 (t >> 7), i = 0 .. KPT-1 (the first KPT/2 in page tile 2T,
+// the rest in 2T+1).  A warp reads 4 keys x 128 contiguous bytes per i; the 8 lanes of a
+// shared-store phase cover keys kb, kb+1 x chunks 0..3 of one atom, whose swizzled 16-byte
+// positions are all distinct (no bank conflicts).
+constexpr int KPT = 8 / NGRP;   // K chunks per producer thread and half tile
 struct KLoad {
     uint4    q[KPT];
     uint32_t d[KPT];
@@ -306,15 +386,15 @@ struct KLoad {
 };
 __device__ __forceinline__ int k_chunk(int t) { return (t & 3) | (((t >> 3) & 1) << 2); }
 __device__ __forceinline__ int k_key0(int t) { return 2 * ((t >> 4) & 7) + ((t >> 2) & 1) + 16 * (t >> 7); }
-__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int h, KLoad &L) {
+__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int h, int32_t page, KLoad &L) {
     const int kc = 8 * h + k_chunk(t), kb = k_key0(t);
 #pragma unroll
     for (int sub = 0; sub < 2; sub++) {
-        const TileSrc ts = tile_src(P, kvh, 2 * T + sub, t == 0 && h == 0);
+        const TileSrc ts = tile_src(P, kvh, 2 * T + sub, page, t == 0 && h == 0);
         L.nvalid[sub] = ts.nvalid;
 #pragma unroll
-        for (int i = 2 * sub; i < 2 * sub + 2; i++) {
-            const int tk = (kb + 32 * i) & 63;
+        for (int i = sub * KPT / 2; i < (sub + 1) * KPT / 2; i++) {
+            const int tk = (kb + 16 * NGRP * i) & 63;
             if (ts.src) {
                 L.q[i] = ldg_nc16(ts.src + TILE_KQ + tk * HD + ((kc ^ kswz(tk)) << 4));
                 L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(tk, kc >> 1));
@@ -331,8 +411,8 @@ __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     const uint32_t atom = slot + (kc >> 2) * (KT * 128);
 #pragma unroll
     for (int i = 0; i < KPT; i++) {
-        const int key = kb + 32 * i;
-        const uint32_t d2 = (key & 63) < L.nvalid[i >> 1] ? (L.d[i] | (L.d[i] << 16)) : 0u;
+        const int key = kb + 16 * NGRP * i;
+        const uint32_t d2 = (key & 63) < L.nvalid[i / (KPT / 2)] ? (L.d[i] | (L.d[i] << 16)) : 0u;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -347,26 +427,26 @@ __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     }
 }
 
-// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0..255): tokens
-// 16 vc .. 16 vc + 15 (vc = t & 3) of the 4 dims 32 b + sub + 4 (2 i + g) (b = (t >> 4) & 7,
-// sub = (t >> 2) & 3, g = t >> 7, i = 0..3), all in q8_0 block b, so they share one set of
+// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0 .. 128 NGRP - 1): tokens
+// 16 vc .. 16 vc + 15 (vc = t & 3) of the dims d0 + 4 NGRP i, d0 = 32 b + ((t >> 2) & 3) +
+// 4 (t >> 7), b = (t >> 4) & 7, i = 0 .. VPT-1, all in q8_0 block b, so they share one set of
 // scales.  Per i a warp reads 2 x 4 consecutive dims x 64 bytes; a shared-store phase covers 2
 // adjacent dims (rows of different swizzle parity) x 4 chunks: no bank conflicts.
-constexpr int VPT = 4;   // V dims per producer thread and half tile
+constexpr int VPT = 8 / NGRP;   // V dims per producer thread and half tile
 struct VLoad {
     uint4 q[VPT];
     uint4 d0, d1;
     int   nvalid;
 };
 __device__ __forceinline__ int v_dim0(int t) { return 32 * ((t >> 4) & 7) + ((t >> 2) & 3) + 4 * (t >> 7); }
-__device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, VLoad &L) {
-    const TileSrc ts = tile_src(P, kvh, kt, false);
+__device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, int32_t page, VLoad &L) {
+    const TileSrc ts = tile_src(P, kvh, kt, page, false);
     L.nvalid = ts.nvalid;
     const int vc = t & 3, d0 = v_dim0(t);
     if (ts.src) {
 #pragma unroll
         for (int i = 0; i < VPT; i++) {
-            const int dim = d0 + 8 * i;
+            const int dim = d0 + 4 * NGRP * i;
             L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * TILE_TOK + ((vc ^ ((dim >> 1) & 3)) << 4));
         }
         const uint8_t *vd = ts.src + vd_off((t >> 4) & 7, vc * 16);
@@ -389,7 +469,7 @@ __device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
     }
 #pragma unroll
     for (int i = 0; i < VPT; i++) {
-        const int dim = d0 + 8 * i;
+        const int dim = d0 + 4 * NGRP * i;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -415,18 +495,24 @@ template <bool KGRP>
 __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_t sbase, int t, int s0, int s1) {
     using Load = typename std::conditional<KGRP, KLoad, VLoad>::type;
     // walk of this group's half tiles: segment si, tile k, half h; ring op of the tile = op0 + op_k/op_v
+    // The page-table entry of the next KV tile is loaded one step ahead, so that its latency is
+    // not in front of the tile's data loads.
     int si = s0, k = 0, h = 0;
     uint32_t op0 = 0;
     Seg sg{};
-    if (si < s1) sg = seg_of(P, si);
+    int32_t page = -1;
+    if (si < s1) {
+        sg = seg_of(P, si);
+        page = page_of(P, 2 * sg.kt0);
+    }
     auto load_next = [&](Load &L, uint32_t &u) -> bool {   // false: walk finished
         if (si >= s1) return false;
         const int kvh = sg.tile / P.n_groups;
         if constexpr (KGRP) {
-            k_load(P, t, kvh, sg.kt0 + k, h, L);
+            k_load(P, t, kvh, sg.kt0 + k, h, page, L);
             u = 2 * (op0 + op_k(k)) + h;
         } else {
-            v_load(P, t, kvh, 2 * (sg.kt0 + k) + h, L);
+            v_load(P, t, kvh, 2 * (sg.kt0 + k) + h, page, L);
             u = 2 * (op0 + op_v(k, sg.nk)) + h;
         }
         if (++h == 2) {
@@ -436,6 +522,7 @@ __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_
                 op0 += 2 * sg.nk;
                 if (++si < s1) sg = seg_of(P, si);
             }
+            if (si < s1) page = page_of(P, 2 * (sg.kt0 + k));
         }
         return true;
     };
@@ -449,15 +536,24 @@ __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_
         mbar_arrive(&B->slot_full[sl]);
         return true;
     };
-    // one half tile in flight while the previous one is converted and stored
-    Load A, Bn;
-    uint32_t uA = 0, uB = 0;
-    if (!load_next(A, uA)) return;
-    for (;;) {
-        const bool hasB = load_next(Bn, uB);
-        if (!store(A, uA) || !hasB) return;
-        const bool hasA = load_next(A, uA);
-        if (!store(Bn, uB) || !hasA) return;
+    if constexpr (PROD_DB) {
+        // one half tile in flight while the previous one is converted and stored
+        Load A, Bn;
+        uint32_t uA = 0, uB = 0;
+        if (!load_next(A, uA)) return;
+        for (;;) {
+            const bool hasB = load_next(Bn, uB);
+            if (!store(A, uA) || !hasB) return;
+            const bool hasA = load_next(A, uA);
+            if (!store(Bn, uB) || !hasA) return;
+        }
+    } else {
+        // the next half tile's loads are issued as soon as this one is stored, so they are in
+        // flight while its slot is awaited
+        Load A;
+        uint32_t uA = 0;
+        while (load_next(A, uA))
+            if (!store(A, uA)) return;
     }
 }
 
@@ -471,12 +567,13 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&B->slot_full[i], 256);
+            mbar_init(&B->slot_full[i], 128 * NGRP);
             mbar_init(&B->slot_free[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&B->s_full[i], 1);
-            mbar_init(&B->p_full[i], 128);
+            mbar_init(&B->s_read[i], 128 * SMX_GROUPS);
+            mbar_init(&B->p_full[i], 128 * SMX_GROUPS);
             mbar_init(&B->pv_done[i], 1);
         }
         mbar_init(&B->q_full, 1);
@@ -496,9 +593,9 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
     tc_fence_after();
     const uint32_t tmem = B->tmem;
 
-    if (warp < 4) {
+    if (warp == 0) {
         // ------------------------------------------------------------------ MMA issue (warp 0)
-        if (warp == 0 && lane == 0) {
+        if (lane == 0) {
             bool ok = true;
             int q_pending = -1;   // parity of a query copy still in flight after an abort
             uint32_t it = 0, op0 = 0;
@@ -515,10 +612,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                     uint32_t kaddr;
                     if (!slot_wait(2 * op + h, kaddr)) return false;
                     tc_fence_after();
-#pragma unroll 1
+                    // descriptor start addresses advance by (bytes >> 4) in the low field
+                    const uint64_t qd = sdesc(qa + 2 * h * 16384), kd = sdesc(kaddr);
+#pragma unroll
                     for (int kk = 0; kk < 8; kk++)
-                        mma_f16_ss(d, sdesc(qa + (2 * h + (kk >> 2)) * 16384 + (kk & 3) * 32),
-                                   sdesc(kaddr + (kk >> 2) * (KT * 128) + (kk & 3) * 32), IDESC_S,
+                        mma_f16_ss(d, qd + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                                   kd + (uint64_t)(((kk >> 2) * (KT * 128) + (kk & 3) * 32) >> 4), IDESC_S,
                                    (h == 0 && kk == 0) ? 0u : 1u);
                     mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
                 }
@@ -532,9 +631,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                     uint32_t vaddr;
                     if (!slot_wait(2 * op + h, vaddr)) return false;
                     tc_fence_after();
-#pragma unroll 1
+                    const uint64_t vd = sdesc(vaddr);
+#pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * KT + (4 * h + kk) * 8, sdesc(vaddr + kk * 32),
+                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * KT + 64 * h + kk * 8, vd + (uint64_t)((kk * 32) >> 4),
                                    IDESC_PV, (first && h == 0 && kk == 0) ? 0u : 1u);
                     mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
                 }
@@ -567,16 +667,18 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             drain_bar(&B->drain, 0, P.status);
         }
         __syncwarp();
-    } else if (warp < 8) {
+    } else if (warp < 1 + 4 * SMX_GROUPS) {
         // ------------------------------------------------------------------ softmax
-        // Thread r owns row r (TMEM lane r).  Control flow is warp-uniform (tcgen05.ld/st are
-        // warp-collective): every wait's result is agreed with __all_sync.  Per 128-key tile the
-        // S row is read in four 32-column chunks and P (fp16 pairs) kept in registers; if a chunk
-        // raises the row max by more than 2^8 over the reference, the reference moves up and the
-        // tile's P so far, l and (at the end) O are rescaled.  P is then stored over the S
-        // columns it came from (the next MMA into this buffer is issued after PV reads P).
-        const int r = tid - 128, wq = warp & 3;
-        const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+        // Warps 1-4 (half 0) and 5-8 (half 1): warp w reads TMEM lanes 32 (w & 3) .. +31, so
+        // thread r owns row r in both halves.  Control flow is warp-uniform (tcgen05.ld/st are
+        // warp-collective): every wait's result is agreed with __all_sync.  Per 128-key tile both
+        // halves read the whole S row for its max (so both raise the lazily raised reference the
+        // same way), meet at s_read, then half h turns keys 64h .. 64h+63 into P (fp16 pairs) and
+        // stores them over S columns 64h .. 64h+31, which only it read since the meeting.  If the
+        // row max grows by more than 2^8 over the reference, the reference moves up and l and O
+        // (half h rescales O columns 128h .. 128h+127) are scaled down.
+        const int half = (warp - 1) >> 2, r = (warp & 3) * 32 + lane;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, wait_bar(bar, parity, B, P.status));
         };
@@ -594,17 +696,9 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 const uint32_t scol = tmem + lane_base + TM_S + b * KT;
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
                 const bool full = __all_sync(0xffffffffu, nvis == KT);
-                // pass 1: row max over the tile (keys past the row's position are -inf)
-                float smax = -INFINITY;
-#pragma unroll 1
-                for (int c = 0; c < KT / 32; c++) {
-                    uint32_t v[32];
-                    tmem_ld32(scol + 32 * c, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; e++)
-                        smax = fmaxf(smax, (full || 32 * c + e < nvis) ? __uint_as_float(v[e]) : -INFINITY);
-                }
+                const float smax = full ? row_max<true>(scol, nvis) : row_max<false>(scol, nvis);
+                tc_fence_before();
+                mbar_arrive(&B->s_read[b]);
                 // lazily raised reference max: O and l are rescaled only when a row max grows by
                 // more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
                 const float mx = smax * P.scale_log2;   // scale > 0: max of scaled = scaled max
@@ -613,36 +707,16 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 if (need) m_ref = mx;
                 l *= F;
                 const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: p = 0
-                const float2 sc2 = make_float2(P.scale_log2, P.scale_log2), nm2 = make_float2(-mu, -mu);
-                // pass 2: P = 2^(s * scale - m) as fp16 pairs, stored over the S columns already read
-                // (chunk c's 32 keys -> P columns 16c .. 16c+15, inside S columns 0 .. 32c+31)
-                float2 l2 = make_float2(0.f, 0.f);
-#pragma unroll 1
-                for (int c = 0; c < KT / 32; c++) {
-                    uint32_t v[32];
-                    tmem_ld32(scol + 32 * c, v);
-                    tmem_wait_ld();
-                    uint32_t pr[16];
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const int i = 32 * c + 2 * e;
-                        const float2 y = __ffma2_rn(make_float2(full || i < nvis ? __uint_as_float(v[2 * e]) : -INFINITY,
-                                                                full || i + 1 < nvis ? __uint_as_float(v[2 * e + 1]) : -INFINITY),
-                                                    sc2, nm2);
-                        const float2 p = make_float2(ex2(y.x), ex2(y.y));
-                        l2 = __fadd2_rn(l2, p);
-                        const __half2 hp = __floats2half2_rn(p.x, p.y);
-                        pr[e] = *reinterpret_cast<const uint32_t *>(&hp);
-                    }
-                    tmem_st16(scol + 16 * c, pr);
-                }
-                l += l2.x + l2.y;
+                if (!(ok = wait_all(&B->s_read[b], (j >> 1) & 1))) break;
+                tc_fence_after();
+                l += full ? row_p<true>(scol, half, nvis, P.scale_log2, mu)
+                          : row_p<false>(scol, half, nvis, P.scale_log2, mu);
                 if (k > 0 && __any_sync(0xffffffffu, F != 1.0f)) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c8 = 0; c8 < HD / 32; c8++) {
+                    for (int c8 = 4 * half; c8 < 4 * half + 4; c8++) {
                         uint32_t o[32];
                         tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
                         tmem_wait_ld();
@@ -656,14 +730,14 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 mbar_arrive(&B->p_full[b]);
             }
             if (!ok) break;
-            // ---- epilogue: O of the segment
+            // ---- epilogue: this half's O columns of the segment's partial record
             const uint32_t jl = it + sg.nk - 1;
             if (!(ok = wait_all(&B->pv_done[jl & 1], (jl >> 1) & 1))) break;
             tc_fence_after();
-            {   // the segment's partial record; stores of a warp cover 32 adjacent rows
+            {   // stores of a warp cover 32 adjacent rows
                 float *rec = P.partial + (int64_t)sg.part * pf_part_floats();
 #pragma unroll 1
-                for (int c8 = 0; c8 < HD / 32; c8++) {
+                for (int c8 = 4 * half; c8 < 4 * half + 4; c8++) {
                     uint32_t o[32];
                     tmem_ld32(tmem + lane_base + TM_O + c8 * 32, o);
                     tmem_wait_ld();
@@ -673,8 +747,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                                make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
                                            __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3])));
                 }
-                __stcg(rec + PF_ROWS * HD + r, m_ref);
-                __stcg(rec + PF_ROWS * HD + PF_ROWS + r, l);
+                if (half == 0) __stcg(rec + PF_ROWS * HD + r, m_ref);
+                __stcg(rec + PF_ROWS * HD + (1 + half) * PF_ROWS + r, l);
             }
             tc_fence_before();
             it += sg.nk;
@@ -683,8 +757,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         // ------------------------------------------------------------------ producers
         // warps 8-15 fill the K halves, warps 16-23 the V halves of the ring.  Loads run one half
         // tile ahead: the next half's bytes are in flight while this one is converted and stored.
-        if (warp < 16) produce<true>(P, B, sbase, tid - 256, s0, s1);
-        else produce<false>(P, B, sbase, tid - 512, s0, s1);
+        if (warp < PW_V) produce<true>(P, B, sbase, tid - 32 * PW_K, s0, s1);
+        else produce<false>(P, B, sbase, tid - 32 * PW_V, s0, s1);
     }
     tc_fence_before();
     __syncthreads();
@@ -717,7 +791,7 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
         const float *rec = base + p * pf_part_floats();
         const float mp = __ldcg(rec + PF_ROWS * HD + row);
         const float w = mp == -INFINITY ? 0.f : ex2(mp - M);
-        L += w * __ldcg(rec + PF_ROWS * HD + PF_ROWS + row);
+        L += w * (__ldcg(rec + PF_ROWS * HD + PF_ROWS + row) + __ldcg(rec + PF_ROWS * HD + 2 * PF_ROWS + row));
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const float4 v = __ldcg(reinterpret_cast<const float4 *>(rec) + (int64_t)(fg * 8 + i) * PF_ROWS + row);

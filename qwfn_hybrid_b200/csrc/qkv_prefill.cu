@@ -304,6 +304,8 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) { return ba
 // Query preparation: bf16 rows -> q8_0 (ggml quantize_row_q8_0 rounding) -> fp16(d * q), written
 // as the 64 KiB A-operand image of each tile.  One warp per row; lane l holds elements 8l..8l+7.
 __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
+    // k_prefill may become resident now; it waits for this grid before reading the query tiles
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (warp >= P.n_tiles * PF_ROWS) return;
     const int tile = warp / PF_ROWS, r = warp % PF_ROWS;
@@ -564,6 +566,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
     Bars *B = reinterpret_cast<Bars *>(sm + SM_BAR);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s0 = P.cta_seg[blockIdx.x], s1 = P.cta_seg[blockIdx.x + 1];
+    // Launched with programmatic stream serialisation after k_prefill_q: everything up to the
+    // first query-tile copy (barriers, TMEM, the producers' K/V tiles, which earlier launches
+    // wrote) overlaps that kernel; the issuing thread waits for it before the copy.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; i++) {
@@ -641,6 +647,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
                 mma_commit(&B->pv_done[b]);
                 return true;
             };
+            asm volatile("griddepcontrol.wait;" ::: "memory");   // query tiles of k_prefill_q
             for (int si = s0; si < s1 && ok; si++) {
                 const Seg sg = seg_of(P, si);
                 if (si > s0 && !(ok = wait_bar(&B->q_empty, (si - s0 - 1) & 1, B, P.status))) break;
@@ -778,6 +785,7 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
     __shared__ float4 rows[MG_ROWS][HD / 4 + 1];
     const int tile = blockIdx.x >> 2, r0 = (blockIdx.x & 3) * MG_ROWS;
     const int t = threadIdx.x, rr = t & (MG_ROWS - 1), fg = t >> 5, row = r0 + rr;
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // partial records of k_prefill
     const int2 tp = P.tile_parts[tile];
     const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
     float M = -INFINITY;
@@ -817,22 +825,42 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
 
 }  // namespace pf
 
+// Launch of a kernel that may start while the previous kernel on the stream finishes
+// (programmatic dependent launch); it synchronises itself with griddepcontrol.wait.
+template <typename K>
+static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                              const PrefillParams &p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     const int64_t rows = (int64_t)p.n_tiles * PF_ROWS;
     pf::k_prefill_q<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    pf::k_prefill<<<p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    pf::k_prefill_merge<<<p.n_tiles * (PF_ROWS / pf::MG_ROWS), 256, 0, st>>>(p);
+    if ((e = launch_pdl(pf::k_prefill, (unsigned)p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st, p)) != cudaSuccess) return e;
+    if ((e = launch_pdl(pf::k_prefill_merge, (unsigned)(p.n_tiles * (PF_ROWS / pf::MG_ROWS)), 256, 0, st, p)) != cudaSuccess)
+        return e;
     count_launches(3);
-    return cudaGetLastError();
+    return cudaSuccess;
 }
 
 }  // namespace qkv

@@ -3,18 +3,17 @@
 // Work plan (host-built, passed by value).  A pair is (sequence, KV head); its tiles are the
 // 64-token tiles of the sequence (dense) or the selected block ids (sparse).  Each pair is cut
 // into `units` contiguous tile ranges in proportion to its length, and every CTA runs exactly one
-// unit, so a ragged batch balances by tiles.  CTAs are launched as clusters of CN; a unit's
-// result (running max m, row sum l, unnormalised O) stays in shared memory and the units of a
-// pair inside one cluster are merged through distributed shared memory.  A pair spread over
-// several clusters leaves one partial per cluster in global memory and the cluster that arrives
-// last (a per-pair atomic counter, no waiting) merges them.  One launch per call, no combine
-// kernel; the merge order is fixed, so results do not depend on which cluster finishes last.
+// unit, so a ragged batch balances by tiles.  A pair with one unit writes its output directly;
+// otherwise every unit leaves a partial record (running max m, row sum l, unnormalised O) and
+// k_decode_merge, launched right behind (programmatic dependent launch, so its CTAs are resident
+// before the last units finish), combines each (pair, query row) in a fixed order: results do
+// not depend on which unit finishes last.
 //
 // Per unit, the G*T query rows of the KV head's group are quantised to q8_0 exactly as ggml's
 // CPU flash_attn_ext quantises its query row, so every QK value is sum_b isum_b * (d_k * d_q)
 // with an exact integer block dot.
 //
-// CTA = 4 warps, 2 CTAs per SM.  Tiles (34816 B: K quants, V quants transposed, scales) stream
+// CTA = 4 warps, 2-4 CTAs per SM.  Tiles (34816 B: K quants, V quants transposed, scales) stream
 // into a 2-stage shared-memory ring with 1-D bulk copies (cp.async.bulk, the TMA engine; no
 // multicast) completing on mbarriers.  Per tile:
 //   QK  warp w: its 16 tokens x all query rows.  mma.m16n8k32 s8 per q8_0 block, A = K rows
@@ -33,15 +32,12 @@
 
 #include <algorithm>
 #include <cstring>
-#include <cooperative_groups.h>
 #include <cuda_fp16.h>
-
-namespace cg = cooperative_groups;
 
 namespace qkv {
 namespace dec {
 
-constexpr int CN = 8;   // CTAs per cluster
+constexpr int PF_TILES = 2;   // tiles per unit prefetched into L2 before the previous launch ends
 constexpr int PSTR   = 80;      // halves per P row in smem (64 tokens + pad: conflict-free LDS.64)
 constexpr int QSTR   = 288;     // bytes per quantised query row (256 + pad)
 constexpr uint32_t MAGIC_I = 0x4B400000u;
@@ -88,6 +84,10 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
                  : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -138,15 +138,17 @@ __device__ __forceinline__ int pi16(int m) { return ((m & 6) << 1) | (m & 1) | (
 __device__ __forceinline__ int qperm(int e) { return ((e & 15) >> 2) * 8 + ((e >> 4) << 2) + (e & 3); }
 
 
-// Stages of the tile ring: one 34816-byte stage per CTA keeps 4 CTAs (16 warps) per SM; the
-// O buffer of the epilogue reuses the stages, so wide query groups (NQ > 34) take two.
+// Stages of the tile ring: one 34816-byte stage per CTA keeps 4 CTAs (16 warps) per SM; two let
+// a unit's second tile load while the first is processed (the host takes two when a launch has
+// at most two units per SM).  The O buffer of the epilogue reuses the stages, so wide query
+// groups (NQ > 34) always take two.
 template <int NT>
 struct Stages { static constexpr int N = NT * 8 * HD * 4 <= TILE_BYTES ? 1 : 2; };
 
-template <int NT>
+template <int NT, int NSR>
 struct Smem {
     static constexpr int NQ = NT * 8;
-    static constexpr int NS = Stages<NT>::N;
+    static constexpr int NS = NSR > Stages<NT>::N ? NSR : Stages<NT>::N;
     uint8_t  tile[NS][TILE_BYTES];       // after the tile loop: the unit's O rows [NQ][HD] fp32
     uint8_t  qq[NQ * QSTR];
     float    qd[NBLK * NQ];
@@ -154,12 +156,9 @@ struct Smem {
     float    red[4 * NQ];                // chunk maxima of warps that outgrew the reference
     float    lpart[4 * NQ];              // per-warp row sums (epilogue)
     int32_t  flag[4];                    // warp outgrew the softmax reference in this tile
-    float    ml[2 * NQ];                 // the unit's m (natural log domain) and l per row
-    float    wm[(NQ + CN) * CN];         // in-cluster merge: per (owned row, member) weight
-    float    rowM[NQ + CN], rowL[NQ + CN];
+    float    ml[2 * NQ];                 // the unit's m (log2 domain) and l per row
     uint64_t full[NS];
     int32_t  stage_blk[NS];              // block id of the tile in each stage (-1 skip, < -1 error)
-    int32_t  merge_flag;
 };
 
 struct Unit {
@@ -219,9 +218,9 @@ __device__ __forceinline__ TileRef tile_ref(const DecodeParams &P, const Unit &U
 }
 
 // One thread: start the copy of the unit's i-th tile into stage i % NS.
-template <int NT>
-__device__ __forceinline__ void issue_ref(const DecodeParams &P, Smem<NT> &sm, const TileRef &r, int i) {
-    constexpr int NS = Smem<NT>::NS;
+template <typename SM>
+__device__ __forceinline__ void issue_ref(const DecodeParams &P, SM &sm, const TileRef &r, int i) {
+    constexpr int NS = SM::NS;
     uint64_t *bar = &sm.full[i % NS];
     sm.stage_blk[i % NS] = r.blk;    // published to the consumers by the barrier's completion
     if (r.blk >= 0) {
@@ -233,9 +232,9 @@ __device__ __forceinline__ void issue_ref(const DecodeParams &P, Smem<NT> &sm, c
         mbar_arrive(bar);
     }
 }
-template <int NT>
-__device__ __forceinline__ void issue_tile(const DecodeParams &P, Smem<NT> &sm, const Unit &U, int i) {
-    issue_ref<NT>(P, sm, tile_ref(P, U, U.t0 + i), i);
+template <typename SM>
+__device__ __forceinline__ void issue_tile(const DecodeParams &P, SM &sm, const Unit &U, int i) {
+    issue_ref(P, sm, tile_ref(P, U, U.t0 + i), i);
 }
 
 // Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h and store
@@ -285,31 +284,46 @@ __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &
 // scores outgrow it by more than 2^4 posts its maximum and the whole CTA moves the reference
 // (rescaling O and the row sums) before PV -- rare after the first tile, so a tile normally costs
 // two barriers: P ready, stage free.
-template <int NT>
+template <int NT, int NSR>
 __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodeParams P) {
     constexpr int NQ = NT * 8;
-    constexpr int NS = Smem<NT>::NS;
+    using SM = Smem<NT, NSR>;
+    constexpr int NS = SM::NS;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    Smem<NT> &sm = *reinterpret_cast<Smem<NT> *>(smem_raw);
-    cg::cluster_group cluster = cg::this_cluster();
+    SM &sm = *reinterpret_cast<SM *>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, tig = lane & 3;
     const int u = blockIdx.x;
-    const int k = u / CN;   // cluster index
     // The next launch on the stream may start as soon as every CTA of this one got here; it then
     // waits (below) until this grid has completed and its writes are visible.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bool has_unit = u < P.n_units;
     Unit U{};
     int n_tiles = 0;
-    int gb = 0, gs = 1, me = 0;
-    bool extends = false;   // the pair has units in other clusters too
+    TileRef first[NS];      // thread 0: the unit's first tiles
     if (has_unit) {
         U = unit_of(P, u);   // kernel parameters only
         n_tiles = U.t1 - U.t0;
-        gb = max(U.pu0, k * CN);
-        gs = min(U.pu1, (k + 1) * CN) - gb;
-        me = u - gb;
-        extends = U.pu0 < k * CN || U.pu1 > (k + 1) * CN;
+        // While the previous kernel finishes, pull this unit's query rows and first tiles into L2.
+        // No kernel of this library writes queries or the block table; a page the previous
+        // launch appends to is updated in L2 by those stores, so a prefetch is never stale.
+        // (Selected block ids come from the previous kernel: sparse units prefetch queries only.)
+        const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
+        for (int e = tid; e < P.nq * (HD * 4 / 128); e += 128) {
+            const int n = e / (HD * 4 / 128), t = n / P.G, jj = n % P.G;
+            prefetch_l2(qsrc + ((int64_t)t * P.n_head + jj) * HD + (e % (HD * 4 / 128)) * 32);
+        }
+        if (!P.sel && tid < min(n_tiles, PF_TILES)) {
+            const TileRef r = tile_ref(P, U, U.t0 + tid);
+            if (r.blk >= 0) bulk_prefetch_l2(r.src, TILE_BYTES);
+        }
+        // thread 0: the barriers, and the first tiles' pages (dense), resolved before the wait
+        if (tid == 0) {
+            for (int st = 0; st < NS; st++) {
+                mbar_init(&sm.full[st], 1);
+                first[st] = !P.sel && st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
     }
     // Everything global below (pages, block table, queries, new rows, scratch, output) may have
     // been written by the previous kernel on the stream: wait for it to complete.
@@ -351,16 +365,13 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 for (int q = 0; q < 8; q++) qv[it][q] = 0.0f;
             }
         }
-        // thread 0 resolves the first tiles' pages once its query loads are in flight (the branch
-        // on a loaded page would otherwise hold those loads back)
-        TileRef first[NS];
-        if (tid == 0)
-            for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+        // thread 0 starts the first tiles' copies once its query loads are in flight (sparse
+        // units resolve their block ids only now: the previous kernel wrote them)
         if (tid == 0) {
-            for (int st = 0; st < NS; st++) mbar_init(&sm.full[st], 1);
-            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            if (P.sel)
+                for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             for (int st = 0; st < NS && st < n_tiles; st++)
-                if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref<NT>(P, sm, first[st], st);
+                if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st);
         }
         // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row
 #pragma unroll
@@ -418,7 +429,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         __syncthreads();   // query rows ready, barriers initialised
         if (appends && tid == 0)   // the first tiles held back for the append
             for (int st = 0; st < NS && st < n_tiles; st++)
-                if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref<NT>(P, sm, first[st], st);
+                if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref(P, sm, first[st], st);
 
         for (int i = 0; i < n_tiles; i++) {
             const int stage = i % NS;
@@ -582,7 +593,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 }
             }
             __syncthreads();   // barrier 2: the stage and P are free
-            if (tid == 0 && i + NS < n_tiles) issue_tile<NT>(P, sm, U, i + NS);
+            if (tid == 0 && i + NS < n_tiles) issue_tile(P, sm, U, i + NS);
         }
         // ---------------- unit epilogue: O, m, l into shared memory ------------------------------
 #pragma unroll
@@ -613,253 +624,218 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int n = 8 * j + 2 * tig + e;
-                    sm.ml[n] = mref[j][e] == -INFINITY ? -INFINITY : mref[j][e] * 0.6931471805599453f;
+                    sm.ml[n] = mref[j][e];   // log2 domain
                     sm.ml[NQ + n] = sm.lpart[n] + sm.lpart[NQ + n] + sm.lpart[2 * NQ + n] + sm.lpart[3 * NQ + n];
                 }
         }
         if (aborted && lane == 0) atomicOr(P.status, ST_TIMEOUT);
-    }
-    cluster.sync();   // #1: every unit's O, m, l visible to the cluster
-
-    // ---- merge the units of each pair inside the cluster (distributed shared memory) -------------
-    // Round 1: lane (row ri, member r) fetches m, l; 8-lane shuffles give the row max, the member
-    // weights and the row sum.  Round 2: the O rows, two at a time, 4*CN remote loads in flight.
-    const int R = has_unit ? (P.nq - me + gs - 1) / gs : 0;   // rows this member merges
-    if (has_unit) {
-        const int e_end = (R * CN + 31) & ~31;
-        for (int e = tid; e < e_end; e += 128) {
-            const int ri = e / CN, r = e % CN;
-            const bool ok = e < R * CN && r < gs;
-            float m = -INFINITY, l = 0.0f;
-            if (ok) {
-                const float *rml = cluster.map_shared_rank(sm.ml, (gb + r) % CN);
-                m = rml[me + ri * gs];
-                l = rml[NQ + me + ri * gs];
-            }
-            float M = m;
-#pragma unroll
-            for (int o = 1; o < CN; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            const float wgt = m == -INFINITY ? 0.0f : expf(m - M);
-            float L = l * wgt;
-#pragma unroll
-            for (int o = 1; o < CN; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-            if (e < R * CN) {
-                sm.wm[e] = wgt;
-                if (r == 0) {
-                    sm.rowM[ri] = M;
-                    sm.rowL[ri] = L;
-                }
-            }
-        }
         __syncthreads();
-        const float *ro[CN];
-#pragma unroll
-        for (int r = 0; r < CN; r++) ro[r] = cluster.map_shared_rank(obuf, (gb + (r < gs ? r : 0)) % CN);
-        const int first_pair_unit = k * CN;   // slot 0 belongs to the pair of the cluster's first unit
-        float *slot = P.partial + (2 * k + (U.pu0 <= first_pair_unit ? 0 : 1)) * partial_stride(P.nq);
-        for (int ri = 0; ri < R; ri += 2) {
-            float v[2][2][CN];   // [row of the pair][dim half][member]
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                const int n = me + (ri + rr) * gs;
-                const bool okr = ri + rr < R;
-#pragma unroll
-                for (int r = 0; r < CN; r++) {
-                    const bool ok = okr && r < gs;
-                    v[rr][0][r] = ok ? ro[r][n * HD + tid] : 0.0f;
-                    v[rr][1][r] = ok ? ro[r][n * HD + tid + 128] : 0.0f;
-                }
-            }
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                if (ri + rr >= R) break;
-                const int n = me + (ri + rr) * gs;
-                float o0 = 0.0f, o1 = 0.0f;
-#pragma unroll
-                for (int r = 0; r < CN; r++) {
-                    const float wgt = r < gs ? sm.wm[(ri + rr) * CN + r] : 0.0f;
-                    o0 = fmaf(v[rr][0][r], wgt, o0);
-                    o1 = fmaf(v[rr][1][r], wgt, o1);
-                }
-                const float L = sm.rowL[ri + rr];
-                if (!extends) {
-                    const int t = n / P.G, jj = n % P.G;
-                    float *o = P.out + (((int64_t)U.io * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
-                    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-                    o[tid] = o0 * inv;
-                    o[tid + 128] = o1 * inv;
-                } else {
-                    slot[n * HD + tid] = o0;
-                    slot[n * HD + tid + 128] = o1;
-                    if (tid == 0) {
-                        slot[P.nq * HD + n] = sm.rowM[ri + rr];
-                        slot[P.nq * HD + P.nq + n] = L;
-                    }
-                }
+        // ---------------- the unit's result: the output itself when the pair has one unit, else
+        // its partial record for k_decode_merge.  Thread: float4 column tid & 63 of rows
+        // (tid >> 6) + 2i, so each row's 1 KiB is written by 64 adjacent threads.
+        const bool single = U.pu1 - U.pu0 == 1;
+        float *rec = P.partial + (int64_t)u * partial_stride(P.nq);
+        const int q4 = tid & 63;
+        for (int n = tid >> 6; n < P.nq; n += 2) {
+            const float4 o = reinterpret_cast<const float4 *>(obuf + n * HD)[q4];
+            if (single) {
+                const float L = sm.ml[NQ + n], inv = L == 0.0f ? 0.0f : 1.0f / L;
+                const int t = n / P.G, jj = n % P.G;
+                float *orow = P.out + (((int64_t)U.io * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
+                reinterpret_cast<float4 *>(orow)[q4] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+            } else {
+                reinterpret_cast<float4 *>(rec + n * HD)[q4] = o;
             }
         }
-        if (extends) __threadfence();
+        if (!single && tid < P.nq) {
+            rec[P.nq * HD + tid] = sm.ml[tid];
+            rec[P.nq * HD + P.nq + tid] = sm.ml[NQ + tid];
+        }
     }
-    cluster.sync();   // #2: cluster partials written; remote reads of O done
-    if (has_unit && extends && me == 0 && tid == 0) {
-        // the group leader counts this cluster in and tells the members whether it was the last
-        const int n_cl = (U.pu1 - 1) / CN - U.pu0 / CN + 1;
-        const int last = atomicAdd(&P.counters[U.p], 1) == n_cl - 1;
-        for (int r = 0; r < gs; r++) *cluster.map_shared_rank(&sm.merge_flag, (gb + r) % CN) = last;
-    }
-    cluster.sync();   // #3: the decision is in every member's shared memory; no remote access after this
-    if (!(has_unit && extends && sm.merge_flag)) return;
-    // ---- last cluster of an extended pair: merge the per-cluster partials in cluster order -------
-    // Round 1 loads (m, l) of every (owned row, cluster); a warp per row reduces them to weights
-    // in the (now free) tile buffer; round 2 sums the O rows with up to 64 loads in flight.
-    __threadfence();
-    const int k_lo = U.pu0 / CN, k_hi = (U.pu1 - 1) / CN, nc = k_hi - k_lo + 1;
+}
+
+// Merge of the partial records of the pairs with more than one unit (plan positions first, so
+// pairs 0 .. n_merge-1): CTA = (pair, query row, quarter of the dims), MG_THREADS threads.
+// O = sum_u 2^(m_u - M) O_u / sum_u 2^(m_u - M) l_u in a fixed order: thread group gi (one float4
+// column of the quarter each) sums the units gi, gi + MG_GROUPS, ... and the groups are added in
+// order.  The first MG_GROUPS * MG_UNROLL units' O columns are loaded together with (m, l), so a
+// pair of up to that many units costs one round trip to L2.
+constexpr int MG_THREADS = 512, MG_SPLIT = 4, MG_LANES = HD / 4 / MG_SPLIT, MG_GROUPS = MG_THREADS / MG_LANES;
+constexpr int MG_MAX_UNITS = 1024, MG_UNROLL = 8;
+static_assert(MG_MAX_UNITS <= 2 * MG_THREADS, "two (m, l) pairs per thread");
+__global__ void __launch_bounds__(MG_THREADS) k_decode_merge(const DecodeParams P) {
+    __shared__ float wgt[MG_MAX_UNITS];
+    __shared__ float4 part[MG_GROUPS][MG_LANES];
+    __shared__ float red[2][MG_THREADS / 32];
+    // The next launch on the stream may become resident now; it waits for this grid.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+    const int dq = blockIdx.x % MG_SPLIT, rowid = blockIdx.x / MG_SPLIT;
+    const int pair = rowid / P.nq, n = rowid % P.nq;
+    const int s = pair / P.n_head_kv, h = pair % P.n_head_kv;
+    const int nu = min(P.seq_units[s], MG_MAX_UNITS), u0 = P.seq_unit0[s] + h * P.seq_units[s];
     const int64_t stride = partial_stride(P.nq);
-    const float *rec0 = P.partial + (2 * k_lo + (U.pu0 != k_lo * CN ? 1 : 0)) * stride;
-    const float *rec1 = P.partial + 2 * (k_lo + 1) * stride;   // cluster k_lo + c (c >= 1): slot 0
-    auto rec = [&](int c) { return c == 0 ? rec0 : rec1 + (int64_t)(c - 1) * 2 * stride; };
-    float *wm = obuf, *wl = obuf + R * nc;
-    for (int e = tid; e < R * nc; e += 128) {
-        const int ri = e / nc, c = e % nc, n = me + ri * gs;
-        wm[e] = __ldcg(rec(c) + P.nq * HD + n);
-        wl[e] = __ldcg(rec(c) + P.nq * HD + P.nq + n);
+    const int gi = tid / MG_LANES, ql = tid % MG_LANES, q4 = dq * MG_LANES + ql;
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the records of k_decode
+    const float *base = P.partial + (int64_t)u0 * stride;
+    auto ocol = [&](int i) {   // this thread's float4 of unit i's row (i clamped into range)
+        return __ldcg(reinterpret_cast<const float4 *>(base + (int64_t)min(i, nu - 1) * stride + n * HD) + q4);
+    };
+    // (m, l) of up to two units per thread, and the first batch of O columns, in flight together
+    float m[2], l[2], M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int i = tid + k * MG_THREADS;
+        m[k] = i < nu ? __ldcg(base + (int64_t)i * stride + P.nq * HD + n) : -INFINITY;
+        l[k] = i < nu ? __ldcg(base + (int64_t)i * stride + P.nq * HD + P.nq + n) : 0.0f;
     }
+    float4 v[MG_UNROLL];
+#pragma unroll
+    for (int k = 0; k < MG_UNROLL; k++) v[k] = ocol(gi + k * MG_GROUPS);
+    M = fmaxf(m[0], m[1]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[0][wp] = M;
     __syncthreads();
-    for (int ri = w; ri < R; ri += 4) {
-        float M = -INFINITY;
-        for (int c = lane; c < nc; c += 32) M = fmaxf(M, wm[ri * nc + c]);
+    M = red[0][0];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = 0.0f;
-        for (int c = lane; c < nc; c += 32) {
-            const float m = wm[ri * nc + c];
-            const float wgt = m == -INFINITY ? 0.0f : expf(m - M);
-            wm[ri * nc + c] = wgt;
-            L = fmaf(wl[ri * nc + c], wgt, L);
-        }
+    for (int k = 1; k < MG_THREADS / 32; k++) M = fmaxf(M, red[0][k]);
+    float L = 0.0f;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        if (lane == 0) sm.rowL[ri] = L;
+    for (int k = 0; k < 2; k++) {
+        const int i = tid + k * MG_THREADS;
+        const float w = m[k] == -INFINITY ? 0.0f : exp2f(m[k] - M);
+        if (i < nu) wgt[i] = w;
+        L = fmaf(w, l[k], L);
     }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) red[1][wp] = L;
+    __syncthreads();   // weights and partial sums visible
+    L = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MG_THREADS / 32; k++) L += red[1][k];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = gi;; i0 += MG_GROUPS * MG_UNROLL) {
+#pragma unroll
+        for (int k = 0; k < MG_UNROLL; k++) {
+            const int i = i0 + k * MG_GROUPS;
+            const float w = i < nu ? wgt[i] : 0.0f;
+            acc.x = fmaf(v[k].x, w, acc.x);
+            acc.y = fmaf(v[k].y, w, acc.y);
+            acc.z = fmaf(v[k].z, w, acc.z);
+            acc.w = fmaf(v[k].w, w, acc.w);
+        }
+        if (i0 + MG_GROUPS * MG_UNROLL >= nu) break;
+#pragma unroll
+        for (int k = 0; k < MG_UNROLL; k++) v[k] = ocol(i0 + MG_GROUPS * MG_UNROLL + k * MG_GROUPS);
+    }
+    part[gi][ql] = acc;
     __syncthreads();
-    for (int ri = 0; ri < R; ri += 4) {
-        float o[4][2] = {};
-        for (int c0 = 0; c0 < nc; c0 += 8) {
-            float v[4][8][2];
+    if (tid < MG_LANES) {
+        float4 o = part[0][tid];
 #pragma unroll
-            for (int rr = 0; rr < 4; rr++)
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const bool ok = ri + rr < R && c0 + q < nc;
-                    const float *r = rec(ok ? c0 + q : 0) + (me + (ri + rr) * gs) * HD;
-                    v[rr][q][0] = ok ? __ldcg(r + tid) : 0.0f;
-                    v[rr][q][1] = ok ? __ldcg(r + tid + 128) : 0.0f;
-                }
-#pragma unroll
-            for (int rr = 0; rr < 4; rr++)
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const float wgt = ri + rr < R && c0 + q < nc ? wm[(ri + rr) * nc + c0 + q] : 0.0f;
-                    o[rr][0] = fmaf(v[rr][q][0], wgt, o[rr][0]);
-                    o[rr][1] = fmaf(v[rr][q][1], wgt, o[rr][1]);
-                }
+        for (int k = 1; k < MG_GROUPS; k++) {
+            const float4 b = part[k][tid];
+            o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
         }
-#pragma unroll
-        for (int rr = 0; rr < 4; rr++) {
-            if (ri + rr >= R) break;
-            const int n = me + (ri + rr) * gs;
-            const float L = sm.rowL[ri + rr];
-            const int t = n / P.G, jj = n % P.G;
-            float *out = P.out + (((int64_t)U.io * P.T + t) * P.n_head + U.h * P.G + jj) * HD;
-            const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-            out[tid] = o[rr][0] * inv;
-            out[tid + 128] = o[rr][1] * inv;
-        }
+        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+        const int t = n / P.G, jj = n % P.G;
+        float *orow = P.out + (((int64_t)P.seq_idx[s] * P.T + t) * P.n_head + h * P.G + jj) * HD;
+        reinterpret_cast<float4 *>(orow)[dq * MG_LANES + tid] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
-    if (me == 0 && tid == 0) P.counters[U.p] = 0;   // ready for the next launch
 }
 
 }  // namespace dec
 
-template <int NT>
-static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
-    const size_t smem = sizeof(dec::Smem<NT>);
+// Launch with programmatic stream serialisation: the grid may become resident while the previous
+// kernel on the stream finishes (if that kernel triggers, as k_decode and k_decode_merge do); it
+// waits (griddepcontrol.wait) before reading anything that kernel may have written.
+template <typename K>
+static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                              const DecodeParams &p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+template <int NT, int NSR>
+static cudaError_t configure_nt() {
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        e = cudaFuncSetAttribute(dec::k_decode<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.n_ctas);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = dec::CN;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    // programmatic dependent launch: this grid may become resident while the previous kernel on
-    // the stream finishes (if that kernel triggers, as k_decode does); it waits before any read
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, dec::k_decode<NT>, p);
-    count_launches(1);
+    if (dev >= 0 && dev < 64 && configured[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(dec::k_decode<NT, NSR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(dec::Smem<NT, NSR>));
+    if (e == cudaSuccess && dev >= 0 && dev < 64) configured[dev] = true;
     return e;
 }
 
-int decode_max_nq() { return 64; }
-int decode_cluster() { return dec::CN; }
-
-template <int NT>
-static int max_clusters_nt() {
+// Co-resident CTAs of the decode kernel (0 = unknown).
+template <int NT, int NSR>
+static int max_ctas_nt() {
     static int cached[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (cached[dev]) return cached[dev];
-    const size_t smem = sizeof(dec::Smem<NT>);
-    if (cudaFuncSetAttribute(dec::k_decode<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return 0;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(dec::CN * 64);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = dec::CN;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    // programmatic dependent launch: this grid may become resident while the previous kernel on
-    // the stream finishes (if that kernel triggers, as k_decode does); it waits before any read
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, dec::k_decode<NT>, &cfg) != cudaSuccess) {
+    int per_sm = 0, sms = 0;
+    if (configure_nt<NT, NSR>() != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec::k_decode<NT, NSR>, 128, sizeof(dec::Smem<NT, NSR>)) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
-    cached[dev] = n;
-    return n;
+    cached[dev] = per_sm * sms;
+    return cached[dev];
 }
 
-int decode_max_clusters(int nq) {
+template <int NT, int NSR>
+static cudaError_t launch_ns(const DecodeParams &p, cudaStream_t st) {
+    cudaError_t e = configure_nt<NT, NSR>();
+    if (e != cudaSuccess) return e;
+    if ((e = launch_pdl(dec::k_decode<NT, NSR>, (unsigned)p.n_units, 128, sizeof(dec::Smem<NT, NSR>), st, p)) !=
+        cudaSuccess)
+        return e;
+    count_launches(1);
+    if (p.n_merge > 0) {
+        if ((e = launch_pdl(dec::k_decode_merge, (unsigned)(p.n_merge * p.nq * dec::MG_SPLIT), dec::MG_THREADS, 0, st,
+                            p)) != cudaSuccess)
+            return e;
+        count_launches(1);
+    }
+    return cudaSuccess;
+}
+
+// Two tile stages when every unit fits co-resident with them, else one (more CTAs per SM).
+template <int NT>
+static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
+    if (dec::Stages<NT>::N == 2 || p.n_units <= max_ctas_nt<NT, 2>()) return launch_ns<NT, 2>(p, st);
+    return launch_ns<NT, 1>(p, st);
+}
+
+int decode_max_nq() { return 64; }
+int decode_merge_max_units() { return dec::MG_MAX_UNITS; }
+
+int decode_max_ctas(int nq) {
     switch ((nq + 7) / 8) {
-        case 1: return max_clusters_nt<1>();
-        case 2: return max_clusters_nt<2>();
-        case 3: return max_clusters_nt<3>();
-        case 4: return max_clusters_nt<4>();
-        case 5: return max_clusters_nt<5>();
-        case 6: return max_clusters_nt<6>();
-        case 7: return max_clusters_nt<7>();
-        case 8: return max_clusters_nt<8>();
+        case 1: return max_ctas_nt<1, 1>();
+        case 2: return max_ctas_nt<2, 1>();
+        case 3: return max_ctas_nt<3, 1>();
+        case 4: return max_ctas_nt<4, 1>();
+        case 5: return max_ctas_nt<5, 1>();
+        case 6: return max_ctas_nt<6, 1>();
+        case 7: return max_ctas_nt<7, 1>();
+        case 8: return max_ctas_nt<8, 1>();
         default: return 0;
     }
 }
@@ -885,26 +861,23 @@ cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
 //
 // For callers that must not allocate device memory -- e.g. a custom op running inside ggml's
 // graph executor, whose memory is planned ahead by ggml-alloc and may not grow mid-graph, or code
-// running under an allocator that owns all of the device's memory.  The kernel's split-K scratch
-// lives in the file-scope arrays below (2.02 MiB of partial records + pair counters), allocated
-// once by the CUDA module on every GPU that loads the library and held until exit.  Every call
-// shares them: calls that overlap on the GPU race; the counters are cleared at the start of
-// every call.
+// running under an allocator that owns all of the device's memory.  The kernels' split-K scratch
+// lives in the file-scope arrays below (6.3 MiB of partial records for up to 192 units of 32
+// query rows), allocated once by the CUDA module on every GPU that loads the library and held
+// until exit.  Every call shares them: calls that overlap on the GPU race.
 // ============================================================================================
 namespace qkv {
 namespace stat {
 
-constexpr int MAX_NQ       = 32;   // query rows per KV head (T * n_head / n_head_kv)
-constexpr int MAX_CLUSTERS = 32;   // clusters of 8 CTAs per launch
-constexpr int64_t PARTIAL_FLOATS = 2LL * MAX_CLUSTERS * (MAX_NQ * HD + 2 * MAX_NQ);
+constexpr int MAX_NQ    = 32;    // query rows per KV head (T * n_head / n_head_kv)
+constexpr int MAX_UNITS = 192;   // units (CTAs) per launch
+constexpr int64_t PARTIAL_FLOATS = (int64_t)MAX_UNITS * (MAX_NQ * HD + 2 * MAX_NQ);
 
 static __device__ __align__(256) float   g_partial[PARTIAL_FLOATS];
-static __device__ __align__(256) int32_t g_counters[MAX_PAIRS];
 static __device__ __align__(256) int32_t g_status[64];
 
 struct Scratch {
     float   *partial  = nullptr;
-    int32_t *counters = nullptr;
     int32_t *status   = nullptr;
 };
 
@@ -919,7 +892,6 @@ static cudaError_t scratch_for_current_device(Scratch &out) {
     if (!cached[dev].partial) {
         Scratch s;
         if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.partial), g_partial)) != cudaSuccess) return e;
-        if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.counters), g_counters)) != cudaSuccess) return e;
         if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.status), g_status)) != cudaSuccess) return e;
         cached[dev] = s;
     }
@@ -950,18 +922,14 @@ extern "C" qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     stat::Scratch sc;
     if (stat::scratch_for_current_device(sc) != cudaSuccess) return QKV_ERR_CUDA;
-    if (cudaMemsetAsync(sc.counters, 0, sizeof(int32_t) * MAX_PAIRS, st) != cudaSuccess ||
-        cudaMemsetAsync(sc.status, 0, sizeof(int32_t), st) != cudaSuccess)
-        return QKV_ERR_CUDA;
+    if (cudaMemsetAsync(sc.status, 0, sizeof(int32_t), st) != cudaSuccess) return QKV_ERR_CUDA;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return QKV_ERR_CUDA;
-    const int CN = decode_cluster();
-    int max_cl = decode_max_clusters(T * G);
-    if (max_cl <= 0) max_cl = sms / 4;
-    max_cl = max_cl < stat::MAX_CLUSTERS ? max_cl : stat::MAX_CLUSTERS;
-    const int64_t target = (int64_t)max_cl * CN;
-    // sequences per launch: every pair needs at least one unit within the cluster budget
+    int max_ctas = decode_max_ctas(T * G);
+    if (max_ctas <= 0) max_ctas = sms * 2;
+    const int64_t target = std::min<int64_t>(max_ctas, stat::MAX_UNITS);
+    // sequences per launch: every pair needs at least one unit within the budget
     const int per_launch = (int)std::min<int64_t>(MAX_SEQ, std::max<int64_t>(1, target / H));
     for (int base = 0; base < n_seq; base += per_launch) {
         const int ns = n_seq - base < per_launch ? n_seq - base : per_launch;
@@ -972,7 +940,6 @@ extern "C" qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t
         P.Q = Q + (size_t)base * T * n_head * HD;
         P.out = out + (size_t)base * T * n_head * HD;
         P.partial = sc.partial;
-        P.counters = sc.counters;
         P.status = sc.status;
         P.page_bytes = (int64_t)view->page_bytes;
         P.n_pages = view->n_pages;
@@ -991,25 +958,32 @@ extern "C" qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t
             total += (int64_t)H * tiles[i];
         }
         int64_t acc = 0;
-        for (int i = 0; i < ns; i++) {   // units in proportion to tiles, >= 1, whole clusters <= budget
+        for (int i = 0; i < ns; i++) {   // units in proportion to tiles, >= 1, in total <= budget
             int64_t u = (int64_t)((double)tiles[i] * (double)(target - (int64_t)ns * H) / (double)total);
-            u = std::min<int64_t>(u, tiles[i] / 2);
+            u = std::min<int64_t>(std::min<int64_t>(u, tiles[i] / 2), decode_merge_max_units());
             u = std::max<int64_t>(1, u);
             units[i] = (int32_t)u;
         }
-        for (int i = 0; i < ns; i++) {
-            P.seq_idx[i] = i;
-            P.seq_slot[i] = slots[base + i];
-            P.seq_pos0[i] = pos0[base + i];
-            P.seq_tiles[i] = tiles[i];
-            P.seq_units[i] = units[i];
-            P.seq_unit0[i] = (int32_t)acc;
+        // multi-unit pairs first (the merge kernel takes pairs 0 .. n_merge-1)
+        int order[MAX_SEQ];
+        for (int i = 0; i < ns; i++) order[i] = i;
+        std::stable_sort(order, order + ns, [&](int a, int b) { return units[a] > units[b]; });
+        int n_multi = 0;
+        for (int j = 0; j < ns; j++) {
+            const int i = order[j];
+            P.seq_idx[j] = i;
+            P.seq_slot[j] = slots[base + i];
+            P.seq_pos0[j] = pos0[base + i];
+            P.seq_tiles[j] = tiles[i];
+            P.seq_units[j] = units[i];
+            P.seq_unit0[j] = (int32_t)acc;
             acc += (int64_t)units[i] * H;
+            n_multi += units[i] > 1;
         }
         P.seq_unit0[ns] = (int32_t)acc;
         P.n_units = (int32_t)acc;
-        P.n_ctas = (int32_t)((acc + CN - 1) / CN * CN);
-        if (P.n_ctas / CN > stat::MAX_CLUSTERS) return QKV_ERR_UNSUPPORTED;
+        P.n_merge = n_multi * H;
+        if (P.n_units > stat::MAX_UNITS) return QKV_ERR_UNSUPPORTED;
         if (launch_decode(P, st) != cudaSuccess) return QKV_ERR_CUDA;
     }
     return QKV_OK;

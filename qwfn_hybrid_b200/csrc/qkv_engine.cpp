@@ -71,7 +71,6 @@ struct qkv_engine {
     uint16_t *d_summary = nullptr;    // [n_layer][n_slots][n_head_kv][max_blocks][HD]
     float    *d_partial = nullptr;    // kernel C: per-cluster partial records
     size_t    partial_bytes = 0;
-    int32_t  *d_counters = nullptr;   // kernel C: per-pair arrival counters (zero between launches)
     int32_t  *d_status  = nullptr;
     // kernel D scratch, allocated by the first prefill call
     uint8_t  *d_pf_q        = nullptr;    // query tiles
@@ -278,7 +277,6 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_rb);
     cudaFree(eng->d_summary);
     cudaFree(eng->d_partial);
-    cudaFree(eng->d_counters);
     cudaFree(eng->d_status);
     cudaFree(eng->d_pf_q);
     cudaFree(eng->d_pf_partial);
@@ -350,12 +348,16 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
             r = dalloc(eng, eng->d_summary, (size_t)c.n_layer * c.n_slots * c.n_head_kv * eng->max_blocks * HD * 2,
                        "block summaries");
         if (r == QKV_OK) {
-            // at most ~2 units per SM plus one per sequence of a launch, in clusters: 2 records each
-            const size_t max_units = (size_t)eng->num_sms * 2 + (size_t)2 * MAX_SEQ * c.n_head_kv;
-            eng->partial_bytes = 2 * ((max_units + decode_cluster() - 1) / decode_cluster() + 1) *
-                                 partial_stride(eng->max_nq) * sizeof(float);
+            // one record per unit: at most one wave of co-resident CTAs plus one unit per pair of
+            // a launch, for the widest query group of each kernel instance
+            size_t need = 0;
+            for (int nq = 8; nq <= std::min((eng->max_nq + 7) & ~7, decode_max_nq()); nq += 8) {
+                const int ctas = decode_max_ctas(nq);
+                const size_t max_units = (size_t)(ctas > 0 ? ctas : eng->num_sms * 8) + (size_t)MAX_SEQ * c.n_head_kv;
+                need = std::max(need, max_units * (size_t)partial_stride(nq) * sizeof(float));
+            }
+            eng->partial_bytes = need;
             r = dalloc(eng, eng->d_partial, eng->partial_bytes, "split-K partials");
-            if (r == QKV_OK) r = dalloc(eng, eng->d_counters, (size_t)MAX_PAIRS * 4, "split-K counters");
         }
         if (r == QKV_OK) r = dalloc(eng, eng->d_status, 256, "status");
         if (r == QKV_OK) {
@@ -368,7 +370,6 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
             e = cudaMemset(eng->d_bt, 0xff, (size_t)c.n_slots * eng->max_pages * 4);
             if (e == cudaSuccess && eng->d_rec) e = cudaMemset(eng->d_rec, 0, (size_t)c.n_slots * eng->rec_slot_bytes);
             if (e == cudaSuccess) e = cudaMemset(eng->d_status, 0, 256);
-            if (e == cudaSuccess) e = cudaMemset(eng->d_counters, 0, (size_t)MAX_PAIRS * 4);
             if (e == cudaSuccess) e = cudaDeviceSynchronize();
             if (e != cudaSuccess) r = fail(eng, QKV_ERR_CUDA, "init: %s", cudaGetErrorString(e));
         }
@@ -524,7 +525,7 @@ extern "C" qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, i
 static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int ns,
                                 const float *Q, int32_t T, float scale, const int32_t *sel, int32_t n_sel,
                                 const float *Knew, const float *Vnew, float *out, cudaStream_t st) {
-    const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H, CN = decode_cluster();
+    const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H;
     DecodeParams P;
     memset(&P, 0, sizeof P);
     P.pool = eng->pools[layer];
@@ -532,7 +533,6 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.Q = Q;
     P.out = out;
     P.partial = eng->d_partial;
-    P.counters = eng->d_counters;
     P.sel = sel;
     P.Knew = Knew;
     P.Vnew = Vnew;
@@ -548,25 +548,25 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.n_seq = ns;
     P.n_sel = n_sel;
     P.scale = scale;
-    // Units: proportional to tiles, about one wave of co-resident clusters in total.  A pair with
-    // CN or more units gets a multiple of CN and those sequences go first, so their pairs fill
-    // whole clusters (merged in shared memory only where a pair spans clusters).
+    // Units: proportional to tiles, about one wave of co-resident CTAs in total, at least two
+    // tiles each.  A pair with one unit writes its output itself; the units of the others leave
+    // partial records for the merge kernel, which takes the pairs at the front of the plan.
     std::vector<int32_t> tiles(ns), units(ns);
     int64_t total = 0;
     for (int i = 0; i < ns; i++) {
         tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
         total += (int64_t)H * tiles[i];
     }
-    const int max_cl = decode_max_clusters(T * G);
-    const int64_t target = (int64_t)(max_cl > 0 ? max_cl : eng->num_sms / 4) * CN;
+    const int max_ctas = decode_max_ctas(T * G);
+    const int64_t target = max_ctas > 0 ? max_ctas : (int64_t)eng->num_sms * 2;
+    const int64_t umax = decode_merge_max_units();
     double scale_u = (double)target / (double)total;
     int64_t n_units = 0;
     for (int attempt = 0; attempt < 8; attempt++) {
         n_units = 0;
         for (int i = 0; i < ns; i++) {
             int64_t u = (int64_t)((double)tiles[i] * scale_u);
-            u = std::min<int64_t>(u, tiles[i] / 2);   // at least two tiles per unit
-            if (u >= CN) u -= u % CN;
+            u = std::min<int64_t>(std::min<int64_t>(u, tiles[i] / 2), umax);
             u = std::max<int64_t>(1, u);
             units[i] = (int32_t)u;
             n_units += u * H;
@@ -575,25 +575,22 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
         scale_u *= 0.9 * (double)target / (double)n_units;
     }
     // The launch lasts as long as its longest unit: where the budget allows, raise a pair's units
-    // (whole clusters) until the most tiles any unit gets drops by one.
+    // until the most tiles any unit gets drops by one.
     for (int i = 0; i < ns; i++) {
         const int64_t u = units[i];
         const int64_t k = (tiles[i] + u - 1) / u;
-        if (k <= 1 || u < CN) continue;
-        int64_t u2 = (tiles[i] + k - 2) / (k - 1);
-        u2 = (u2 + CN - 1) / CN * CN;
-        if (n_units + (u2 - u) * H <= target) {
+        if (k <= 1) continue;
+        const int64_t u2 = std::min<int64_t>((tiles[i] + k - 2) / (k - 1), umax);
+        if (u2 > u && n_units + (u2 - u) * H <= target) {
             n_units += (u2 - u) * H;
             units[i] = (int32_t)u2;
         }
     }
     std::vector<int32_t> order(ns);
     for (int i = 0; i < ns; i++) order[i] = i;
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
-        const bool fa = units[a] % CN == 0 && units[a] >= CN, fb = units[b] % CN == 0 && units[b] >= CN;
-        return fa != fb ? fa : units[a] > units[b];
-    });
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return units[a] > units[b]; });
     int64_t acc = 0;
+    int n_multi = 0;
     for (int j = 0; j < ns; j++) {
         const int i = order[j];
         P.seq_idx[j] = i;
@@ -603,11 +600,12 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
         P.seq_units[j] = units[i];
         P.seq_unit0[j] = (int32_t)acc;
         acc += (int64_t)units[i] * H;
+        n_multi += units[i] > 1;
     }
     P.seq_unit0[ns] = (int32_t)acc;
     P.n_units = (int32_t)acc;
-    P.n_ctas = (int32_t)((acc + CN - 1) / CN * CN);
-    if ((size_t)2 * (P.n_ctas / CN) * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
+    P.n_merge = n_multi * H;
+    if ((size_t)P.n_units * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
         return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small for %d units", P.n_units);
     CK(eng, launch_decode(P, st));
     return QKV_OK;

@@ -106,13 +106,13 @@ struct DecodeParams {
     const int32_t *block_table;   // [n_slots][max_pages]
     const float   *Q;             // [n_seq][T][n_head][HD]
     float         *out;           // [n_seq][T][n_head][HD]
-    float         *partial;       // scratch: 2 records per cluster of [nq*HD + 2*nq] floats
-    int32_t       *counters;      // scratch: per pair, zero between launches
+    float         *partial;       // scratch: one record per unit of [nq*HD + 2*nq] floats
     const int32_t *sel;           // nullable [n_seq][n_head_kv][n_sel] block ids
     const float   *Knew, *Vnew;   // nullable [n_seq][T][n_head_kv*HD]: fused append (dense only)
     int32_t       *status;
     int64_t page_bytes;
-    int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_units, n_ctas;
+    int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_units;
+    int32_t n_merge;              // pairs with more than one unit: plan positions first, pairs 0 .. n_merge-1
     float   scale;
     // per plan position j (sequences ordered by units, largest first):
     int32_t seq_idx[MAX_SEQ];        // the sequence's index in the caller's arrays
@@ -122,13 +122,14 @@ struct DecodeParams {
     int32_t seq_units[MAX_SEQ];      // units (CTAs) per pair of the sequence
     int32_t seq_unit0[MAX_SEQ + 1];  // prefix of n_head_kv * seq_units
 };
-// partial record size in floats for nq query rows
+// partial record size in floats for nq query rows: O [nq][HD] unnormalised, m [nq] (log2
+// domain), l [nq]
 __host__ __device__ __forceinline__ int64_t partial_stride(int nq) { return (int64_t)nq * HD + 2 * nq; }
 
-cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);
+cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);   // k_decode, then k_decode_merge
 int decode_max_nq();
-int decode_cluster();
-int decode_max_clusters(int nq);   // co-resident clusters of the decode kernel (0 = unknown)
+int decode_max_ctas(int nq);       // co-resident CTAs of the decode kernel (0 = unknown)
+int decode_merge_max_units();      // units per pair the merge kernel takes
 
 // ---- kernel D -----------------------------------------------------------------------------------
 // A prefill tile is 128 rows = (128 / G) query tokens x the G q-heads of one KV head.  Its KV

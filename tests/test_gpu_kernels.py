@@ -188,8 +188,9 @@ def test_fused_append_decode_vs_oracle(cuda, qkvlib, oracle, T):
         assert_close(got[i], ref, f"fused seq {i}")
 
 
-def test_decode_many_units_many_clusters(cuda, qkvlib, oracle):
-    """A long and a short sequence: the long pairs span many clusters (last-arriver merge)."""
+def test_decode_many_units_with_merge(cuda, qkvlib, oracle):
+    """A long and a short sequence: the long pairs are split over many units (merge kernel), the
+    short one runs as single-unit pairs that write their output directly."""
     lens = [40000, 100]
     eng = engine(qkvlib, n_slots=2, n_ctx=40960)
     kv = {}
@@ -197,7 +198,7 @@ def test_decode_many_units_many_clusters(cuda, qkvlib, oracle):
         eng.seq_alloc(i)
         kv[i] = fill_seq(eng, oracle, 0, i, n, seed=700 + i)
     Q = normal(8, (2, 2, 16, HD))
-    for rep in range(2):   # counters must be reset for the next launch
+    for rep in range(2):   # the scratch records are reused by the next launch
         got = decode(eng, 0, [0, 1], [n - 2 for n in lens], Q, 2)
         for i, n in enumerate(lens):
             ref = oracle.attn(Q[i], kv[i][0], kv[i][1], np.arange(n - 2, n), 2, 1 / 16)

@@ -323,13 +323,15 @@ def run_ours(args) -> None:
         "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
         "data": "synthetic N(0,1) (torch Philox, seed 1+1000*rank); no model or prompts available",
         "config": dict(CONFIG, parallelism=f"sequence-sharded x{ws} (independent sequence per GPU, no collective)",
-                       timing="the K steps replayed from one CUDA graph (one fused append+attention launch "
-                              "per layer), device-resident inputs"),
+                       timing="the K steps replayed from one CUDA graph (per layer: the fused append+attention "
+                              "kernel and its split-K merge), device-resident inputs"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "frac_of_8000": achieved / 8000.0, "peak_source": peak_note,
-                     "kernel": "k_decode (fused q8_0 append + split-K verify attention), one launch per layer",
+                     "kernel": "k_decode (fused q8_0 append + split-K verify attention) and its k_decode_merge, "
+                               "per layer",
                      "bytes_per_launch": statistics.mean(dec_bytes), "ms_per_launch": ms_launch,
-                     "ms_per_launch_note": "graph time / launches: includes the gaps between launches",
+                     "ms_per_launch_note": "graph time / layers: both kernels of a layer and the gaps between "
+                                           "layers",
                      "traffic": traffic, "traffic_source": traffic_src},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": N_LAYER * (T * N_HEAD * HD * 4 + 2 * T * N_HEAD_KV * HD * 4),
@@ -472,7 +474,7 @@ def run_cfg5(args) -> None:
                    "l2": "inputs larger than L2 (17 GB of KV per step)"},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,
                      "frac_of_8000": per_gpu / 8000.0, "peak_source": hbm_src,
-                     "kernel": "k_decode, one launch per layer over all sequences"},
+                     "kernel": "k_decode (and k_decode_merge for split pairs), per layer over all sequences"},
         "snapshot_restore": {"ms": restore_ms, "slots_per_gpu_max": max(sum(1 for o in owner if o == r) for r in range(ws)),
                              "recurrent_bytes_per_slot": rec_bytes,
                              "copy_gbs": 2 * rec_bytes * n / (restore_ms * 1e-3) / 1e9 if restore_ms > 0 else None},

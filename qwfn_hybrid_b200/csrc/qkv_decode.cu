@@ -746,6 +746,57 @@ __global__ void __launch_bounds__(MG_THREADS) k_decode_merge(const DecodeParams 
     }
 }
 
+// The same merge for pairs of at most MR_MAX_UNITS units (wide batches: many pairs, few units
+// each): CTA = (pair, MR_ROWS query rows), 64 threads per row, one float4 column each; every
+// thread loads the (m, l) and O columns of all the pair's units at once and sums them in unit
+// order.
+constexpr int MR_ROWS = 8, MR_MAX_UNITS = 16;
+__global__ void __launch_bounds__(64 * MR_ROWS) k_decode_merge_rows(const DecodeParams P) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int tid = threadIdx.x, q4 = tid & 63;
+    const int nrb = (P.nq + MR_ROWS - 1) / MR_ROWS;
+    const int pair = blockIdx.x / nrb, n = (blockIdx.x % nrb) * MR_ROWS + (tid >> 6);
+    const int s = pair / P.n_head_kv, h = pair % P.n_head_kv;
+    const int nu = min(P.seq_units[s], MR_MAX_UNITS), u0 = P.seq_unit0[s] + h * P.seq_units[s];
+    const int64_t stride = partial_stride(P.nq);
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the records of k_decode
+    if (n >= P.nq) return;
+    const float *base = P.partial + (int64_t)u0 * stride;
+    float m[MR_MAX_UNITS], l[MR_MAX_UNITS];
+    float4 v[MR_MAX_UNITS];
+#pragma unroll
+    for (int k = 0; k < MR_MAX_UNITS; k++) {
+        if (k < nu) {
+            const float *rec = base + (int64_t)k * stride;
+            m[k] = __ldcg(rec + P.nq * HD + n);
+            l[k] = __ldcg(rec + P.nq * HD + P.nq + n);
+            v[k] = __ldcg(reinterpret_cast<const float4 *>(rec + n * HD) + q4);
+        } else {
+            m[k] = -INFINITY;
+            l[k] = 0.0f;
+            v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < MR_MAX_UNITS; k++) M = fmaxf(M, m[k]);
+    float L = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < MR_MAX_UNITS; k++) {
+        const float w = m[k] == -INFINITY ? 0.0f : exp2f(m[k] - M);
+        L = fmaf(w, l[k], L);
+        acc.x = fmaf(v[k].x, w, acc.x);
+        acc.y = fmaf(v[k].y, w, acc.y);
+        acc.z = fmaf(v[k].z, w, acc.z);
+        acc.w = fmaf(v[k].w, w, acc.w);
+    }
+    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+    const int t = n / P.G, jj = n % P.G;
+    float *orow = P.out + (((int64_t)P.seq_idx[s] * P.T + t) * P.n_head + h * P.G + jj) * HD;
+    reinterpret_cast<float4 *>(orow)[q4] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
 }  // namespace dec
 
 // Launch with programmatic stream serialisation: the grid may become resident while the previous
@@ -808,9 +859,13 @@ static cudaError_t launch_ns(const DecodeParams &p, cudaStream_t st) {
         return e;
     count_launches(1);
     if (p.n_merge > 0) {
-        if ((e = launch_pdl(dec::k_decode_merge, (unsigned)(p.n_merge * p.nq * dec::MG_SPLIT), dec::MG_THREADS, 0, st,
-                            p)) != cudaSuccess)
-            return e;
+        // pairs are in plan order, most units first
+        if (p.seq_units[0] <= dec::MR_MAX_UNITS)
+            e = launch_pdl(dec::k_decode_merge_rows, (unsigned)(p.n_merge * ((p.nq + dec::MR_ROWS - 1) / dec::MR_ROWS)),
+                           64 * dec::MR_ROWS, 0, st, p);
+        else
+            e = launch_pdl(dec::k_decode_merge, (unsigned)(p.n_merge * p.nq * dec::MG_SPLIT), dec::MG_THREADS, 0, st, p);
+        if (e != cudaSuccess) return e;
         count_launches(1);
     }
     return cudaSuccess;

@@ -138,12 +138,16 @@ __device__ __forceinline__ int pi16(int m) { return ((m & 6) << 1) | (m & 1) | (
 __device__ __forceinline__ int qperm(int e) { return ((e & 15) >> 2) * 8 + ((e >> 4) << 2) + (e & 3); }
 
 
+// Row stride (floats) of the epilogue's O buffer: rows 4 banks apart, so a warp's stores (4 rows x
+// 8 consecutive dims) hit 32 distinct banks; 16-byte aligned rows for the float4 reads.
+constexpr int OSTR = HD + 4;
+
 // Stages of the tile ring: one 34816-byte stage per CTA keeps 4 CTAs (16 warps) per SM; two let
 // a unit's second tile load while the first is processed (the host takes two when a launch has
 // at most two units per SM).  The O buffer of the epilogue reuses the stages, so wide query
 // groups (NQ > 34) always take two.
 template <int NT>
-struct Stages { static constexpr int N = NT * 8 * HD * 4 <= TILE_BYTES ? 1 : 2; };
+struct Stages { static constexpr int N = NT * 8 * OSTR * 4 <= TILE_BYTES ? 1 : 2; };
 
 template <int NT, int NSR>
 struct Smem {
@@ -328,7 +332,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     // Everything global below (pages, block table, queries, new rows, scratch, output) may have
     // been written by the previous kernel on the stream: wait for it to complete.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][HD], valid after the tile loop
+    float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][OSTR], valid after the tile loop
     bool aborted = false;
 
     if (has_unit) {
@@ -613,8 +617,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
 #pragma unroll
                 for (int mt = 0; mt < 4; mt++) {
                     const int d0 = 64 * w + 16 * mt + g;
-                    obuf[n * HD + d0]     = O[mt][j][e];
-                    obuf[n * HD + d0 + 8] = O[mt][j][2 + e];
+                    obuf[n * OSTR + d0]     = O[mt][j][e];
+                    obuf[n * OSTR + d0 + 8] = O[mt][j][2 + e];
                 }
             }
         __syncthreads();
@@ -637,7 +641,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         float *rec = P.partial + (int64_t)u * partial_stride(P.nq);
         const int q4 = tid & 63;
         for (int n = tid >> 6; n < P.nq; n += 2) {
-            const float4 o = reinterpret_cast<const float4 *>(obuf + n * HD)[q4];
+            const float4 o = reinterpret_cast<const float4 *>(obuf + n * OSTR)[q4];
             if (single) {
                 const float L = sm.ml[NQ + n], inv = L == 0.0f ? 0.0f : 1.0f / L;
                 const int t = n / P.G, jj = n % P.G;

@@ -77,6 +77,7 @@ struct qkv_engine {
     float    *d_pf_partial  = nullptr;    // split-segment partials
     int32_t  *d_pf_plan     = nullptr;    // segments, tile parts, CTA offsets
     int32_t   pf_max_tiles = 0, pf_max_parts = 0, pf_plan_ints = 0;
+    PfPlanInline pf_plan_inline;   // host copy of a small plan, passed with the launch
     size_t    device_bytes = 0;
 
     // pinned upload ring for block-table rows: a block is reused only after its event fired
@@ -920,8 +921,15 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     ints.insert(ints.end(), pl.tile_parts.begin(), pl.tile_parts.end());
     const size_t off_cta = ints.size();
     ints.insert(ints.end(), pl.cta_seg.begin(), pl.cta_seg.end());
-    if ((int64_t)ints.size() > eng->pf_plan_ints) return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %zu ints", ints.size());
-    if ((r = upload_i32(eng, ints, eng->d_pf_plan, S(stream))) != QKV_OK) return r;
+    // small plans travel with the launch; larger ones are uploaded ahead of the kernels
+    const bool inline_plan = ints.size() <= (size_t)PF_PLAN_INLINE;
+    if (!inline_plan) {
+        if ((int64_t)ints.size() > eng->pf_plan_ints)
+            return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %zu ints", ints.size());
+        if ((r = upload_i32(eng, ints, eng->d_pf_plan, S(stream))) != QKV_OK) return r;
+    } else {
+        std::copy(ints.begin(), ints.end(), eng->pf_plan_inline.v);
+    }
 
     PrefillParams P;
     memset(&P, 0, sizeof P);
@@ -935,6 +943,9 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     P.segs = reinterpret_cast<const int4 *>(eng->d_pf_plan);
     P.tile_parts = reinterpret_cast<const int2 *>(eng->d_pf_plan + off_tiles);
     P.cta_seg = eng->d_pf_plan + off_cta;
+    P.plan_inline = inline_plan;
+    P.off_tiles = (int32_t)off_tiles;
+    P.off_cta = (int32_t)off_cta;
     P.page_bytes = eng->page_bytes;
     P.n_pages = eng->n_pages;
     P.max_pages = eng->max_pages;
@@ -949,7 +960,7 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     P.n_kv = pos0 + Tc;
     P.n_ctas = n_ctas;
     P.scale_log2 = scale * 1.4426950408889634f;
-    CK(eng, launch_prefill(P, S(stream)));
+    CK(eng, launch_prefill(P, eng->pf_plan_inline, S(stream)));
     return QKV_OK;
 }
 

@@ -152,13 +152,22 @@ struct PrefillParams {
     float          *out;          // [Tc][n_head][HD]
     float          *partial;      // scratch [parts][pf_part_floats()], one record per segment
     int32_t        *status;
+    // the plan, in device memory, or (plan_inline) in the launch's PfPlanInline at int offsets 0
+    // (segs), off_tiles (tile_parts), off_cta (cta_seg)
     const int32_t  *cta_seg;      // [n_ctas + 1] first segment of each CTA
     const int4     *segs;         // {tile, kv tile begin, kv tile end, part}
     const int2     *tile_parts;   // {number of parts, first part}
+    int32_t plan_inline, off_tiles, off_cta;
     int64_t page_bytes;
     int32_t n_pages, max_pages, n_head, n_head_kv, G, tpt, n_groups, n_tiles, Tc, pos0, n_kv, n_ctas;
     float   scale_log2;           // softmax scale x log2(e)
 };
-cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st);
+// A plan of up to PF_PLAN_INLINE ints travels with the launch (kernel parameters), so a call
+// needs no host-to-device copy ahead of its kernels.
+constexpr int PF_PLAN_INLINE = 2048;
+struct alignas(16) PfPlanInline {
+    int32_t v[PF_PLAN_INLINE];
+};
+cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st);
 
 }  // namespace qkv

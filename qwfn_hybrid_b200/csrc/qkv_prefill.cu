@@ -304,8 +304,11 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) { return ba
 // Query preparation: bf16 rows -> q8_0 (ggml quantize_row_q8_0 rounding) -> fp16(d * q), written
 // as the 64 KiB A-operand image of each tile.  One warp per row; lane l holds elements 8l..8l+7.
 __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
-    // k_prefill may become resident now; it waits for this grid before reading the query tiles
+    // k_prefill may become resident now; it waits for this grid before reading the query tiles.
+    // This grid itself may have started early: the queries may come from the kernel before it,
+    // and the previous call's k_prefill reads the query tiles this grid rewrites.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (warp >= P.n_tiles * PF_ROWS) return;
     const int tile = warp / PF_ROWS, r = warp % PF_ROWS;
@@ -346,8 +349,8 @@ __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
 struct Seg {
     int tile, kt0, nk, part;
 };
-__device__ __forceinline__ Seg seg_of(const PrefillParams &P, int i) {
-    const int4 s = P.segs[i];
+__device__ __forceinline__ Seg seg_of(const int4 *segs, int i) {
+    const int4 s = segs[i];
     return Seg{s.x, s.y, s.z - s.y, s.w};
 }
 
@@ -494,7 +497,8 @@ __device__ __forceinline__ uint32_t op_v(int k, int nk) { return k == nk - 1 ? (
 // One producer group's walk over its half tiles in ring order (K group: the K ops, V group: the
 // V ops), software-pipelined by one half tile.
 template <bool KGRP>
-__device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_t sbase, int t, int s0, int s1) {
+__device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs, Bars *B, uint32_t sbase, int t, int s0,
+                                        int s1) {
     using Load = typename std::conditional<KGRP, KLoad, VLoad>::type;
     // walk of this group's half tiles: segment si, tile k, half h; ring op of the tile = op0 + op_k/op_v
     // The page-table entry of the next KV tile is loaded one step ahead, so that its latency is
@@ -504,7 +508,7 @@ __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_
     Seg sg{};
     int32_t page = -1;
     if (si < s1) {
-        sg = seg_of(P, si);
+        sg = seg_of(segs, si);
         page = page_of(P, 2 * sg.kt0);
     }
     auto load_next = [&](Load &L, uint32_t &u) -> bool {   // false: walk finished
@@ -522,7 +526,7 @@ __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_
             if (++k == sg.nk) {
                 k = 0;
                 op0 += 2 * sg.nk;
-                if (++si < s1) sg = seg_of(P, si);
+                if (++si < s1) sg = seg_of(segs, si);
             }
             if (si < s1) page = page_of(P, 2 * (sg.kt0 + k));
         }
@@ -559,13 +563,16 @@ __device__ __forceinline__ void produce(const PrefillParams &P, Bars *B, uint32_
     }
 }
 
-__global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
+__global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ PrefillParams P,
+                                                     const __grid_constant__ PfPlanInline PL) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(sm);
     Bars *B = reinterpret_cast<Bars *>(sm + SM_BAR);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int s0 = P.cta_seg[blockIdx.x], s1 = P.cta_seg[blockIdx.x + 1];
+    const int4 *segs = P.plan_inline ? reinterpret_cast<const int4 *>(PL.v) : P.segs;
+    const int32_t *cta_seg = P.plan_inline ? PL.v + P.off_cta : P.cta_seg;
+    const int s0 = cta_seg[blockIdx.x], s1 = cta_seg[blockIdx.x + 1];
     // Launched with programmatic stream serialisation after k_prefill_q: everything up to the
     // first query-tile copy (barriers, TMEM, the producers' K/V tiles, which earlier launches
     // wrote) overlaps that kernel; the issuing thread waits for it before the copy.
@@ -649,7 +656,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
             };
             asm volatile("griddepcontrol.wait;" ::: "memory");   // query tiles of k_prefill_q
             for (int si = s0; si < s1 && ok; si++) {
-                const Seg sg = seg_of(P, si);
+                const Seg sg = seg_of(segs, si);
                 if (si > s0 && !(ok = wait_bar(&B->q_empty, (si - s0 - 1) & 1, B, P.status))) break;
                 mbar_expect_tx(&B->q_full, PF_QTILE);
                 const uint8_t *qsrc = P.qtiles + (int64_t)sg.tile * PF_QTILE;
@@ -692,7 +699,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         uint32_t it = 0;
         bool ok = true;
         for (int si = s0; si < s1 && ok; si++) {
-            const Seg sg = seg_of(P, si);
+            const Seg sg = seg_of(segs, si);
             const int tok = (sg.tile % P.n_groups) * P.tpt + r / P.G;
             const int qpos = tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
@@ -764,8 +771,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
         // ------------------------------------------------------------------ producers
         // warps 8-15 fill the K halves, warps 16-23 the V halves of the ring.  Loads run one half
         // tile ahead: the next half's bytes are in flight while this one is converted and stored.
-        if (warp < PW_V) produce<true>(P, B, sbase, tid - 32 * PW_K, s0, s1);
-        else produce<false>(P, B, sbase, tid - 32 * PW_V, s0, s1);
+        if (warp < PW_V) produce<true>(P, segs, B, sbase, tid - 32 * PW_K, s0, s1);
+        else produce<false>(P, segs, B, sbase, tid - 32 * PW_V, s0, s1);
     }
     tc_fence_before();
     __syncthreads();
@@ -781,12 +788,15 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const PrefillParams P) {
 // (coalesced in the record layout); the rows go through shared memory so that the output, rows of
 // 256 contiguous floats, is written by threads along each row.
 constexpr int MG_ROWS = 32;
-__global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
+__global__ void __launch_bounds__(256) k_prefill_merge(const __grid_constant__ PrefillParams P,
+                                                       const __grid_constant__ PfPlanInline PL) {
     __shared__ float4 rows[MG_ROWS][HD / 4 + 1];
     const int tile = blockIdx.x >> 2, r0 = (blockIdx.x & 3) * MG_ROWS;
     const int t = threadIdx.x, rr = t & (MG_ROWS - 1), fg = t >> 5, row = r0 + rr;
+    // the next call's k_prefill_q may become resident now (it waits for this grid)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");   // partial records of k_prefill
-    const int2 tp = P.tile_parts[tile];
+    const int2 tp = (P.plan_inline ? reinterpret_cast<const int2 *>(PL.v + P.off_tiles) : P.tile_parts)[tile];
     const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
     float M = -INFINITY;
     for (int p = 0; p < tp.x; p++) M = fmaxf(M, __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + row));
@@ -827,9 +837,8 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const PrefillParams P) {
 
 // Launch of a kernel that may start while the previous kernel on the stream finishes
 // (programmatic dependent launch); it synchronises itself with griddepcontrol.wait.
-template <typename K>
-static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t st,
-                              const PrefillParams &p) {
+template <typename K, typename... A>
+static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t st, const A &...args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(block);
@@ -840,10 +849,13 @@ static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t sm
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, p);
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st) {
+// The three kernels of a call, each launched behind its predecessor (programmatic dependent
+// launch): k_prefill_q waits for whatever precedes it before reading the queries, k_prefill and
+// k_prefill_merge wait for the kernel before them (see the kernels).
+cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st) {
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -854,10 +866,10 @@ cudaError_t launch_prefill(const PrefillParams &p, cudaStream_t st) {
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     const int64_t rows = (int64_t)p.n_tiles * PF_ROWS;
-    pf::k_prefill_q<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = launch_pdl(pf::k_prefill, (unsigned)p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st, p)) != cudaSuccess) return e;
-    if ((e = launch_pdl(pf::k_prefill_merge, (unsigned)(p.n_tiles * (PF_ROWS / pf::MG_ROWS)), 256, 0, st, p)) != cudaSuccess)
+    if ((e = launch_pdl(pf::k_prefill_q, (unsigned)((rows + 7) / 8), 256, 0, st, p)) != cudaSuccess) return e;
+    if ((e = launch_pdl(pf::k_prefill, (unsigned)p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st, p, plan)) != cudaSuccess) return e;
+    if ((e = launch_pdl(pf::k_prefill_merge, (unsigned)(p.n_tiles * (PF_ROWS / pf::MG_ROWS)), 256, 0, st, p, plan)) !=
+        cudaSuccess)
         return e;
     count_launches(3);
     return cudaSuccess;

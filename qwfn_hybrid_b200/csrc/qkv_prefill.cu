@@ -783,46 +783,67 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
 }
 
 // Merge of the segments' partial records of every tile: O = sum_p 2^(m_p - M) O_p / sum_p
-// 2^(m_p - M) l_p, parts in order.  CTA = (tile, 32-row quarter), 256 threads.  Reads: thread
-// (row = t & 31, column group t >> 5) walks 8 float4 columns, adjacent threads adjacent rows
-// (coalesced in the record layout); the rows go through shared memory so that the output, rows of
-// 256 contiguous floats, is written by threads along each row.
-constexpr int MG_ROWS = 32;
+// 2^(m_p - M) l_p, parts in order (batches of MG_PB parts, the running max rescaled between
+// batches).  CTA = (tile, MG_ROWS rows), 256 threads.  Thread (row = t % MG_ROWS, column group
+// t / MG_ROWS) loads its 4 float4 columns and (m, l) of a whole batch at once -- one round trip to
+// L2 for up to MG_PB parts; adjacent threads read adjacent rows (coalesced in the record layout).
+// The rows go through shared memory so that the output, rows of 256 contiguous floats, is written
+// by threads along each row.
+constexpr int MG_ROWS = 16, MG_PB = 4;
 __global__ void __launch_bounds__(256) k_prefill_merge(const __grid_constant__ PrefillParams P,
                                                        const __grid_constant__ PfPlanInline PL) {
     __shared__ float4 rows[MG_ROWS][HD / 4 + 1];
-    const int tile = blockIdx.x >> 2, r0 = (blockIdx.x & 3) * MG_ROWS;
-    const int t = threadIdx.x, rr = t & (MG_ROWS - 1), fg = t >> 5, row = r0 + rr;
+    constexpr int QTR = PF_ROWS / MG_ROWS;
+    const int tile = blockIdx.x / QTR, r0 = (blockIdx.x % QTR) * MG_ROWS;
+    const int t = threadIdx.x, rr = t % MG_ROWS, fg = t / MG_ROWS, row = r0 + rr;
     // the next call's k_prefill_q may become resident now (it waits for this grid)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");   // partial records of k_prefill
     const int2 tp = (P.plan_inline ? reinterpret_cast<const int2 *>(PL.v + P.off_tiles) : P.tile_parts)[tile];
     const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
-    float M = -INFINITY;
-    for (int p = 0; p < tp.x; p++) M = fmaxf(M, __ldcg(base + p * pf_part_floats() + PF_ROWS * HD + row));
-    float4 acc[8];
+    float M = -INFINITY, L = 0.f;
+    float4 acc[4];
 #pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float L = 0.f;
-#pragma unroll 1
-    for (int p = 0; p < tp.x; p++) {
-        const float *rec = base + p * pf_part_floats();
-        const float mp = __ldcg(rec + PF_ROWS * HD + row);
-        const float w = mp == -INFINITY ? 0.f : ex2(mp - M);
-        L += w * (__ldcg(rec + PF_ROWS * HD + PF_ROWS + row) + __ldcg(rec + PF_ROWS * HD + 2 * PF_ROWS + row));
+    for (int i = 0; i < 4; i++) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p0 = 0; p0 < tp.x; p0 += MG_PB) {
+        float m[MG_PB], l[MG_PB];
+        float4 v[MG_PB][4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(rec) + (int64_t)(fg * 8 + i) * PF_ROWS + row);
-            acc[i].x += w * v.x;
-            acc[i].y += w * v.y;
-            acc[i].z += w * v.z;
-            acc[i].w += w * v.w;
+        for (int k = 0; k < MG_PB; k++) {
+            const float *rec = base + (int64_t)min(p0 + k, tp.x - 1) * pf_part_floats();   // clamped: weight 0
+            m[k] = p0 + k < tp.x ? __ldcg(rec + PF_ROWS * HD + row) : -INFINITY;
+            l[k] = __ldcg(rec + PF_ROWS * HD + PF_ROWS + row) + __ldcg(rec + PF_ROWS * HD + 2 * PF_ROWS + row);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                v[k][i] = __ldcg(reinterpret_cast<const float4 *>(rec) + (int64_t)(fg * 4 + i) * PF_ROWS + row);
         }
+        float Mn = M;
+#pragma unroll
+        for (int k = 0; k < MG_PB; k++) Mn = fmaxf(Mn, m[k]);
+        const float a = M == -INFINITY ? 0.f : ex2(M - Mn);   // rescale of the earlier batches
+        L *= a;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            acc[i].x *= a; acc[i].y *= a; acc[i].z *= a; acc[i].w *= a;
+        }
+#pragma unroll
+        for (int k = 0; k < MG_PB; k++) {
+            const float w = m[k] == -INFINITY ? 0.f : ex2(m[k] - Mn);
+            L = fmaf(w, l[k], L);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                acc[i].x = fmaf(w, v[k][i].x, acc[i].x);
+                acc[i].y = fmaf(w, v[k][i].y, acc[i].y);
+                acc[i].z = fmaf(w, v[k][i].z, acc[i].z);
+                acc[i].w = fmaf(w, v[k][i].w, acc[i].w);
+            }
+        }
+        M = Mn;
     }
     const float inv = L > 0.f ? 1.0f / L : 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; i++)
-        rows[rr][fg * 8 + i] = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
+    for (int i = 0; i < 4; i++)
+        rows[rr][fg * 4 + i] = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
     __syncthreads();
     const int kvh = tile / P.n_groups, g = tile % P.n_groups;
 #pragma unroll 1

@@ -816,14 +816,16 @@ extern "C" qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slo
 }
 
 // ---------------------------------------------------------------------------------- prefill
-// Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); tile t needs 128-key KV
-// tiles 0 .. nk[t]-1 (causal: up to its last query's position).  The flattened sequence of all
-// (tile, KV tile) pairs is cut into n_ctas equal runs; each run is a list of segments, and every
-// segment writes one partial record (parts of a tile are consecutive, in KV order).
+// Plan for kernel D.  Tiles are (KV head, group of 128/G query tokens); two groups of a KV head
+// (2p, 2p+1) form a pair tile, run by a CTA pair, which needs 128-key KV tiles 0 .. nk-1 (causal:
+// up to the pair's last query position).  The flattened sequence of all (pair tile, KV tile)
+// items is cut into n_runs equal runs, one per CTA pair; each run is a list of segments, and every
+// segment is one part of its pair tile (parts of a pair tile consecutive, in KV order), with the
+// partial records 2 part + 0 and 2 part + 1 of its two tiles.
 struct PfPlan {
-    std::vector<int32_t> segs;        // 4 per segment: tile, kt0, kt1, part
-    std::vector<int32_t> tile_parts;  // 2 per tile: parts, first part
-    std::vector<int32_t> cta_seg;     // n_ctas + 1
+    std::vector<int32_t> segs;        // 4 per segment: pair tile, kt0, kt1, part
+    std::vector<int32_t> tile_parts;  // 2 per pair tile: parts, first part
+    std::vector<int32_t> cta_seg;     // n_runs + 1
     int32_t n_parts = 0;
 };
 static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPlan &pl) {
@@ -866,11 +868,11 @@ static qkv_status pf_scratch(qkv_engine *eng) {
     if (eng->d_pf_q) return QKV_OK;
     const int G = eng->cfg.n_head / eng->cfg.n_head_kv, tpt = PF_ROWS / G;
     eng->pf_max_tiles = eng->cfg.n_head_kv * ((PF_MAX_TC + tpt - 1) / tpt);
-    eng->pf_max_parts = eng->pf_max_tiles + eng->num_sms;   // every CTA boundary adds at most one segment
+    eng->pf_max_parts = eng->pf_max_tiles + eng->num_sms;   // every run boundary adds at most one segment
     eng->pf_plan_ints = 4 * (eng->pf_max_tiles + eng->num_sms) + 2 * eng->pf_max_tiles + eng->num_sms + 1;
     qkv_status r = dalloc(eng, eng->d_pf_q, (size_t)eng->pf_max_tiles * PF_QTILE, "prefill query tiles");
     if (r == QKV_OK)
-        r = dalloc(eng, eng->d_pf_partial, (size_t)eng->pf_max_parts * pf_part_floats() * 4, "prefill partials");
+        r = dalloc(eng, eng->d_pf_partial, (size_t)2 * eng->pf_max_parts * pf_part_floats() * 4, "prefill partials");
     if (r == QKV_OK) r = dalloc(eng, eng->d_pf_plan, (size_t)eng->pf_plan_ints * 4, "prefill plan");
     if (r != QKV_OK) {
         cudaFree(eng->d_pf_q);
@@ -902,16 +904,19 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     if ((r = flush_tables(eng, S(stream))) != QKV_OK) return r;
 
     const int tpt = PF_ROWS / G, n_groups = (Tc + tpt - 1) / tpt, n_tiles = H * n_groups;
-    std::vector<int32_t> nk(n_tiles);
+    const int n_gpairs = (n_groups + 1) / 2, n_ptiles = H * n_gpairs;
+    std::vector<int32_t> nk(n_ptiles);
     int64_t W = 0;
-    for (int t = 0; t < n_tiles; t++) {
-        const int g = t % n_groups, last_tok = std::min((g + 1) * tpt, Tc) - 1;
+    for (int t = 0; t < n_ptiles; t++) {
+        const int gp = t % n_gpairs, last_tok = std::min((2 * gp + 2) * tpt, Tc) - 1;
         nk[t] = (pos0 + last_tok) / PF_KT + 1;
         W += nk[t];
     }
     PfPlan pl;
-    const int n_ctas = (int)std::min<int64_t>(eng->num_sms, W);
-    pf_build(nk, W, n_ctas, pl);
+    int max_pairs = prefill_max_pairs();
+    if (max_pairs <= 0) max_pairs = eng->num_sms / 2;
+    const int n_runs = (int)std::min<int64_t>(max_pairs, W);
+    pf_build(nk, W, n_runs, pl);
     if (pl.n_parts > eng->pf_max_parts)
         return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %d parts (max %d)", pl.n_parts, eng->pf_max_parts);
     std::vector<int32_t> ints;
@@ -954,11 +959,12 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     P.G = G;
     P.tpt = tpt;
     P.n_groups = n_groups;
+    P.n_gpairs = n_gpairs;
     P.n_tiles = n_tiles;
     P.Tc = Tc;
     P.pos0 = pos0;
     P.n_kv = pos0 + Tc;
-    P.n_ctas = n_ctas;
+    P.n_ctas = 2 * n_runs;
     P.scale_log2 = scale * 1.4426950408889634f;
     CK(eng, launch_prefill(P, eng->pf_plan_inline, S(stream)));
     return QKV_OK;

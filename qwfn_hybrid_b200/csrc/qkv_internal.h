@@ -132,10 +132,11 @@ int decode_max_ctas(int nq);       // co-resident CTAs of the decode kernel (0 =
 int decode_merge_max_units();      // units per pair the merge kernel takes
 
 // ---- kernel D -----------------------------------------------------------------------------------
-// A prefill tile is 128 rows = (128 / G) query tokens x the G q-heads of one KV head.  Its KV
-// range is cut into segments (contiguous 128-key KV tiles); every CTA runs a contiguous run of
-// segments.  Each segment leaves a partial record (unnormalised O, row max, row sum); a second
-// kernel merges the records of every tile and writes the output.
+// A prefill tile is 128 rows = (128 / G) query tokens x the G q-heads of one KV head.  Two tiles
+// of a KV head (query groups 2p, 2p+1: a pair tile) run on a CTA pair whose MMAs cover both.  The
+// KV range of a pair tile is cut into segments (contiguous 128-key KV tiles); every pair runs a
+// contiguous run of segments.  Each segment leaves two partial records (one per tile: unnormalised
+// O, row max, row sums); a second kernel merges the records of every tile and writes the output.
 constexpr int PF_ROWS      = 128;
 constexpr int PF_KT        = 128;              // keys per KV tile of kernel D
 constexpr int PF_MAX_TC    = 4096;             // query tokens per call
@@ -159,7 +160,9 @@ struct PrefillParams {
     const int2     *tile_parts;   // {number of parts, first part}
     int32_t plan_inline, off_tiles, off_cta;
     int64_t page_bytes;
-    int32_t n_pages, max_pages, n_head, n_head_kv, G, tpt, n_groups, n_tiles, Tc, pos0, n_kv, n_ctas;
+    int32_t n_pages, max_pages, n_head, n_head_kv, G, tpt, n_groups, n_tiles, Tc, pos0, n_kv;
+    int32_t n_gpairs;             // pairs of query groups per KV head (the plan's pair tiles: kvh * n_gpairs + pair)
+    int32_t n_ctas;               // 2 per pair run
     float   scale_log2;           // softmax scale x log2(e)
 };
 // A plan of up to PF_PLAN_INLINE ints travels with the launch (kernel parameters), so a call
@@ -169,5 +172,6 @@ struct alignas(16) PfPlanInline {
     int32_t v[PF_PLAN_INLINE];
 };
 cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st);
+int prefill_max_pairs();   // co-resident CTA pairs of kernel D (0 = unknown)
 
 }  // namespace qkv

@@ -38,7 +38,6 @@ namespace pf {
 // warps: 0 MMA issue, 1 .. 4 SMX_GROUPS softmax, then 4 NGRP K producers and 4 NGRP V producers
 constexpr int SMX_GROUPS = 2;          // softmax warp groups (column halves of S)
 constexpr int NGRP       = 1;          // 128-thread producer groups per operand
-constexpr bool PROD_DB   = false;      // producers double-buffer their loads
 constexpr int PW_K       = 1 + 4 * SMX_GROUPS;
 constexpr int PW_V       = PW_K + 4 * NGRP;
 constexpr int NTHR       = 32 * (PW_V + 4 * NGRP);
@@ -46,7 +45,7 @@ constexpr int KT   = PF_KT;            // keys per KV tile (N of S, K of PV): tw
 static_assert(KT == 2 * TILE_TOK, "a KV tile is two 64-token page tiles");
 // shared memory map, offsets from a 1024-byte aligned base
 constexpr int SM_Q       = 0;          // A of S: [4 k-atoms][128 rows][128 B]
-constexpr int SM_RING    = 65536;      // NSLOT x 32 KiB half tiles (K: 128 keys x 128 dims; V: 256 dims x 64 keys)
+constexpr int SM_RING    = 65536;      // NSLOT x 32 KiB slots: this CTA's half of a K tile (64 keys x 256 dims) or V tile (128 dims x 128 keys)
 constexpr int NSLOT      = 5;
 constexpr int SLOT_BYTES = 32768;
 constexpr int SM_BAR     = SM_RING + NSLOT * SLOT_BYTES;
@@ -55,16 +54,21 @@ constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
 
+// Barriers.  The MMAs of a CTA pair are issued by the pair's leader (cluster rank 0); the
+// barriers the issuing thread waits on live in the leader and both CTAs arrive on them (the
+// follower through its cluster address); the MMAs' commits arrive on the barrier of the same
+// name in both CTAs (multicast).
 struct Bars {
-    uint64_t slot_full[NSLOT];   // producers (128 NGRP arrivals): half tile in the slot
-    uint64_t slot_free[NSLOT];   // commit after the MMAs reading the slot
-    uint64_t s_full[2];          // commit after S_j
-    uint64_t s_read[2];          // softmax (256 arrivals): both halves read S_j (P may overwrite it)
-    uint64_t p_full[2];          // softmax (256 arrivals): P_j stored (and O rescaled)
-    uint64_t pv_done[2];         // commit after PV_j
-    uint64_t q_full;             // query tile landed (expect_tx)
-    uint64_t q_empty;            // commit after the last S of a segment
-    uint64_t drain;              // commit before exit
+    uint64_t slot_full[NSLOT];   // leader: producers of both CTAs (2 x 128 NGRP arrivals): the pair's slot u filled
+    uint64_t slot_free[NSLOT];   // both: commit after the MMAs reading slot u
+    uint64_t s_full[2];          // both: commit after S_j
+    uint64_t s_read[2];          // both, local: the CTA's softmax groups (256 arrivals) read S_j
+    uint64_t p_full[2];          // leader: softmax of both CTAs (2 x 256 arrivals): P_j stored (and O rescaled)
+    uint64_t pv_done[2];         // both: commit after PV_j
+    uint64_t q_full;             // both, local: the CTA's query tile landed (expect_tx)
+    uint64_t q_peer;             // leader: the follower's query tile landed (1 arrival)
+    uint64_t q_empty;            // both: commit after the last S of a segment
+    uint64_t drain;              // leader: commit before exit
     uint32_t tmem;
     int32_t  abort;
 };
@@ -154,30 +158,58 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor, kind::f16: D f32 (bit 4), A/B f16 (format 0), both K-major, N >> 3 at
-// bit 17, M >> 4 at bit 24.
+// bit 17, M >> 4 at bit 24.  The pair's MMAs are M = 256: rows 0-127 in the leader, 128-255 in
+// the follower; B is split along N (the leader holds rows 0 .. N/2-1 of B, the follower the rest).
 constexpr uint32_t idesc_f16(int M, int N) { return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24); }
-constexpr uint32_t IDESC_S  = idesc_f16(PF_ROWS, KT);
-constexpr uint32_t IDESC_PV = idesc_f16(PF_ROWS, HD);
+constexpr uint32_t IDESC_S  = idesc_f16(2 * PF_ROWS, KT);
+constexpr uint32_t IDESC_PV = idesc_f16(2 * PF_ROWS, HD);
 
-// D[tmem] (+)= A x B^T, A from tensor memory (M rows in lanes, K packed two per column)
+// The pair's D[tmem] (+)= A x B^T, A from tensor memory (each CTA's 128 rows in its lanes, K
+// packed two per column), B from shared memory (each CTA its half of B's rows)
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// D[tmem] (+)= A x B^T, both from shared memory
+// The pair's D[tmem] (+)= A x B^T, both from shared memory (each CTA its 128 rows of A and its
+// half of B's rows)
 __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// Commit of the pair's MMAs issued so far by this thread: one arrival on `bar` (the same shared
+// offset) in both CTAs of the pair.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"((uint16_t)3)
                  : "memory");
+}
+// ... one arrival on `bar` of the issuing CTA only.
+__device__ __forceinline__ void mma_commit_own(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of both CTAs of the pair.
+__device__ __forceinline__ void pair_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrival on the leader's (cluster rank 0) copy of barrier `bar`, release at cluster scope: the
+// follower's shared-memory stores before it are visible to the MMAs the leader issues after it.
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t *bar) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(a) : "r"(smem_u32(bar)));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
 }
 #define PF_R32(v)                                                                                                   \
     "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),     \
@@ -377,47 +409,42 @@ __device__ __forceinline__ TileSrc tile_src(const PrefillParams &P, int kvh, int
                    nvalid};
 }
 
-// K half h (dims 128h .. 128h+127) of 128-key tile T, K-producer thread t (0 .. 128 NGRP - 1):
-// 16-dim chunk kc = (t & 3) | ((t >> 3) & 1) << 2 of the half for keys kb + 16 NGRP i, kb =
-// 2 ((t >> 4) & 7) + ((t >> 2) & 1) + 16 (t >> 7), i = 0 .. KPT-1 (the first KPT/2 in page tile 2T,
-// the rest in 2T+1).  A warp reads 4 keys x 128 contiguous bytes per i; the 8 lanes of a
-// shared-store phase cover keys kb, kb+1 x chunks 0..3 of one atom, whose swizzled 16-byte
-// positions are all distinct (no bank conflicts).
-constexpr int KPT = 8 / NGRP;   // K chunks per producer thread and half tile
+// This CTA's half of K tile T: keys 64 rank .. +63 (page tile 2T + rank), all 256 dims; the slot
+// holds [4 atoms of 64 dims][64 keys][128 B], 128-byte swizzled.  K-producer thread t (0..127):
+// 16-dim chunk kc = 4 ((t >> 3) & 3) + (t & 3) for keys 2 (t >> 5) + ((t >> 2) & 1) + 8 i,
+// i = 0..7.  A warp reads 2 keys x 256 contiguous bytes per i; the 8 lanes of a shared-store phase
+// cover 2 keys (different swizzle rows) x 4 chunks of one atom: no bank conflicts.
+constexpr int KPT = 8;   // K chunks per producer thread and tile
 struct KLoad {
     uint4    q[KPT];
     uint32_t d[KPT];
-    int      nvalid[2];
+    int      nvalid;
 };
-__device__ __forceinline__ int k_chunk(int t) { return (t & 3) | (((t >> 3) & 1) << 2); }
-__device__ __forceinline__ int k_key0(int t) { return 2 * ((t >> 4) & 7) + ((t >> 2) & 1) + 16 * (t >> 7); }
-__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int h, int32_t page, KLoad &L) {
-    const int kc = 8 * h + k_chunk(t), kb = k_key0(t);
+__device__ __forceinline__ int k_chunk(int t) { return 4 * ((t >> 3) & 3) + (t & 3); }
+__device__ __forceinline__ int k_key0(int t) { return 2 * (t >> 5) + ((t >> 2) & 1); }
+__device__ __forceinline__ void k_load(const PrefillParams &P, int t, int kvh, int T, int rank, int32_t page, KLoad &L) {
+    const int kc = k_chunk(t), kb = k_key0(t);
+    const TileSrc ts = tile_src(P, kvh, 2 * T + rank, page, t == 0);
+    L.nvalid = ts.nvalid;
 #pragma unroll
-    for (int sub = 0; sub < 2; sub++) {
-        const TileSrc ts = tile_src(P, kvh, 2 * T + sub, page, t == 0 && h == 0);
-        L.nvalid[sub] = ts.nvalid;
-#pragma unroll
-        for (int i = sub * KPT / 2; i < (sub + 1) * KPT / 2; i++) {
-            const int tk = (kb + 16 * NGRP * i) & 63;
-            if (ts.src) {
-                L.q[i] = ldg_nc16(ts.src + TILE_KQ + tk * HD + ((kc ^ kswz(tk)) << 4));
-                L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(tk, kc >> 1));
-            } else {
-                L.q[i] = make_uint4(0, 0, 0, 0);
-                L.d[i] = 0;
-            }
+    for (int i = 0; i < KPT; i++) {
+        const int tk = kb + 8 * i;
+        if (ts.src) {
+            L.q[i] = ldg_nc16(ts.src + TILE_KQ + tk * HD + ((kc ^ kswz(tk)) << 4));
+            L.d[i] = *reinterpret_cast<const uint16_t *>(ts.src + kd_off(tk, kc >> 1));
+        } else {
+            L.q[i] = make_uint4(0, 0, 0, 0);
+            L.d[i] = 0;
         }
     }
 }
-// K half image: [2 atoms of 64 dims][128 keys][128 B], 128-byte swizzled.
 __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     const int kc = k_chunk(t), kb = k_key0(t);
-    const uint32_t atom = slot + (kc >> 2) * (KT * 128);
+    const uint32_t atom = slot + (kc >> 2) * (64 * 128);
 #pragma unroll
     for (int i = 0; i < KPT; i++) {
-        const int key = kb + 16 * NGRP * i;
-        const uint32_t d2 = (key & 63) < L.nvalid[i / (KPT / 2)] ? (L.d[i] | (L.d[i] << 16)) : 0u;
+        const int key = kb + 8 * i;
+        const uint32_t d2 = key < L.nvalid ? (L.d[i] | (L.d[i] << 16)) : 0u;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -432,29 +459,31 @@ __device__ __forceinline__ void k_store(uint32_t slot, int t, const KLoad &L) {
     }
 }
 
-// V half v (keys 64v .. 64v+63 = page tile 2T+v), V-producer thread t (0 .. 128 NGRP - 1): tokens
-// 16 vc .. 16 vc + 15 (vc = t & 3) of the dims d0 + 4 NGRP i, d0 = 32 b + ((t >> 2) & 3) +
-// 4 (t >> 7), b = (t >> 4) & 7, i = 0 .. VPT-1, all in q8_0 block b, so they share one set of
-// scales.  Per i a warp reads 2 x 4 consecutive dims x 64 bytes; a shared-store phase covers 2
-// adjacent dims (rows of different swizzle parity) x 4 chunks: no bank conflicts.
-constexpr int VPT = 8 / NGRP;   // V dims per producer thread and half tile
+// This CTA's half of V tile T: dims 128 rank .. +127, keys 0..127 (page tiles 2T, 2T+1); the slot
+// holds [2 atoms of 64 keys][128 dims][128 B], 128-byte swizzled.  V-producer thread t (0..127):
+// tokens 16 vc .. +15 (vc = t & 3) of page tile 2T + a (a = (t >> 3) & 1) for the 8 dims
+// 32 bl + dd + 4 i (bl = t >> 5, dd = ((t >> 2) & 1) | ((t >> 4) & 1) << 1, i = 0..7), all in
+// q8_0 block bl of the half, so they share one set of scales.  Per i a warp reads 4 consecutive
+// dims x 64 bytes of each page tile; a shared-store phase covers 2 adjacent dims (rows of
+// different swizzle parity) x 4 chunks: no bank conflicts.
+constexpr int VPT = 8;   // V dims per producer thread and tile
 struct VLoad {
     uint4 q[VPT];
     uint4 d0, d1;
     int   nvalid;
 };
-__device__ __forceinline__ int v_dim0(int t) { return 32 * ((t >> 4) & 7) + ((t >> 2) & 3) + 4 * (t >> 7); }
-__device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int kt, int32_t page, VLoad &L) {
-    const TileSrc ts = tile_src(P, kvh, kt, page, false);
+__device__ __forceinline__ int v_dim0(int t) { return 32 * (t >> 5) + (((t >> 2) & 1) | (((t >> 4) & 1) << 1)); }
+__device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, int T, int rank, int32_t page, VLoad &L) {
+    const int vc = t & 3, a = (t >> 3) & 1, d0 = 128 * rank + v_dim0(t);
+    const TileSrc ts = tile_src(P, kvh, 2 * T + a, page, false);
     L.nvalid = ts.nvalid;
-    const int vc = t & 3, d0 = v_dim0(t);
     if (ts.src) {
 #pragma unroll
         for (int i = 0; i < VPT; i++) {
-            const int dim = d0 + 4 * NGRP * i;
+            const int dim = d0 + 4 * i;
             L.q[i] = ldg_nc16(ts.src + TILE_VQ + dim * TILE_TOK + ((vc ^ ((dim >> 1) & 3)) << 4));
         }
-        const uint8_t *vd = ts.src + vd_off((t >> 4) & 7, vc * 16);
+        const uint8_t *vd = ts.src + vd_off(d0 >> 5, vc * 16);
         L.d0 = ldg_nc16(vd);
         L.d1 = ldg_nc16(vd + 16);
     } else {
@@ -463,9 +492,9 @@ __device__ __forceinline__ void v_load(const PrefillParams &P, int t, int kvh, i
         L.d0 = L.d1 = make_uint4(0, 0, 0, 0);
     }
 }
-// V half image: [256 dims][128 B = 64 keys], 128-byte swizzled.
 __device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
-    const int vc = t & 3, d0 = v_dim0(t);
+    const int vc = t & 3, a = (t >> 3) & 1, d0 = v_dim0(t);
+    const uint32_t atom = slot + a * (128 * 128);
     uint32_t dv[8] = {L.d0.x, L.d0.y, L.d0.z, L.d0.w, L.d1.x, L.d1.y, L.d1.z, L.d1.w};
 #pragma unroll
     for (int e = 0; e < 8; e++) {   // tokens 16 vc + 2e, +1: zero scales past n_kv
@@ -474,7 +503,7 @@ __device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
     }
 #pragma unroll
     for (int i = 0; i < VPT; i++) {
-        const int dim = d0 + 4 * NGRP * i;
+        const int dim = d0 + 4 * i;
         const uint32_t w[4] = {L.q[i].x, L.q[i].y, L.q[i].z, L.q[i].w};
         uint32_t hh[8];
 #pragma unroll
@@ -484,26 +513,25 @@ __device__ __forceinline__ void v_store(uint32_t slot, int t, const VLoad &L) {
             hh[2 * e]     = hmul2(lo, dv[2 * e]);
             hh[2 * e + 1] = hmul2(hi, dv[2 * e + 1]);
         }
-        sts16(swz(slot, dim, vc * 2), make_uint4(hh[0], hh[1], hh[2], hh[3]));
-        sts16(swz(slot, dim, vc * 2 + 1), make_uint4(hh[4], hh[5], hh[6], hh[7]));
+        sts16(swz(atom, dim, vc * 2), make_uint4(hh[0], hh[1], hh[2], hh[3]));
+        sts16(swz(atom, dim, vc * 2 + 1), make_uint4(hh[4], hh[5], hh[6], hh[7]));
     }
 }
 
-// Ring order of a segment's K/V tiles: K_0, then (K_k, V_{k-1}) for k = 1 .. nk-1, then V_{nk-1}
-// (the MMA issue order S_0, S_1, PV_0, S_2, PV_1, ...).  Every op fills two ring slots.
+// Ring order of a segment's K/V ops (each one slot): K_0, then (K_k, V_{k-1}) for k = 1 .. nk-1,
+// then V_{nk-1} (the MMA issue order S_0, S_1, PV_0, S_2, PV_1, ...).
 __device__ __forceinline__ uint32_t op_k(int k) { return k == 0 ? 0u : (uint32_t)(2 * k - 1); }
 __device__ __forceinline__ uint32_t op_v(int k, int nk) { return k == nk - 1 ? (uint32_t)(2 * nk - 1) : (uint32_t)(2 * k + 2); }
 
-// One producer group's walk over its half tiles in ring order (K group: the K ops, V group: the
-// V ops), software-pipelined by one half tile.
+// One producer group's walk over this CTA's halves of its ops in ring order (K group: the K
+// ops, V group: the V ops).  The next op's loads are issued as soon as the last one is stored,
+// so they are in flight while its slot is awaited; the page-table entry of the next KV tile is
+// loaded one step ahead.  Every store ends with an arrival on the leader's slot_full.
 template <bool KGRP>
-__device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs, Bars *B, uint32_t sbase, int t, int s0,
-                                        int s1) {
+__device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs, Bars *B, uint32_t sbase, int t,
+                                        int rank, int s0, int s1) {
     using Load = typename std::conditional<KGRP, KLoad, VLoad>::type;
-    // walk of this group's half tiles: segment si, tile k, half h; ring op of the tile = op0 + op_k/op_v
-    // The page-table entry of the next KV tile is loaded one step ahead, so that its latency is
-    // not in front of the tile's data loads.
-    int si = s0, k = 0, h = 0;
+    int si = s0, k = 0;
     uint32_t op0 = 0;
     Seg sg{};
     int32_t page = -1;
@@ -513,23 +541,20 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
     }
     auto load_next = [&](Load &L, uint32_t &u) -> bool {   // false: walk finished
         if (si >= s1) return false;
-        const int kvh = sg.tile / P.n_groups;
+        const int kvh = sg.tile / P.n_gpairs;
         if constexpr (KGRP) {
-            k_load(P, t, kvh, sg.kt0 + k, h, page, L);
-            u = 2 * (op0 + op_k(k)) + h;
+            k_load(P, t, kvh, sg.kt0 + k, rank, page, L);
+            u = op0 + op_k(k);
         } else {
-            v_load(P, t, kvh, 2 * (sg.kt0 + k) + h, page, L);
-            u = 2 * (op0 + op_v(k, sg.nk)) + h;
+            v_load(P, t, kvh, sg.kt0 + k, rank, page, L);
+            u = op0 + op_v(k, sg.nk);
         }
-        if (++h == 2) {
-            h = 0;
-            if (++k == sg.nk) {
-                k = 0;
-                op0 += 2 * sg.nk;
-                if (++si < s1) sg = seg_of(segs, si);
-            }
-            if (si < s1) page = page_of(P, 2 * (sg.kt0 + k));
+        if (++k == sg.nk) {
+            k = 0;
+            op0 += 2 * sg.nk;
+            if (++si < s1) sg = seg_of(segs, si);
         }
+        if (si < s1) page = page_of(P, 2 * (sg.kt0 + k));
         return true;
     };
     auto store = [&](const Load &ld, uint32_t u) -> bool {
@@ -539,28 +564,13 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
         if constexpr (KGRP) k_store(slot, t, ld);
         else v_store(slot, t, ld);
         fence_proxy_async();
-        mbar_arrive(&B->slot_full[sl]);
+        mbar_arrive_leader(&B->slot_full[sl]);
         return true;
     };
-    if constexpr (PROD_DB) {
-        // one half tile in flight while the previous one is converted and stored
-        Load A, Bn;
-        uint32_t uA = 0, uB = 0;
-        if (!load_next(A, uA)) return;
-        for (;;) {
-            const bool hasB = load_next(Bn, uB);
-            if (!store(A, uA) || !hasB) return;
-            const bool hasA = load_next(A, uA);
-            if (!store(Bn, uB) || !hasA) return;
-        }
-    } else {
-        // the next half tile's loads are issued as soon as this one is stored, so they are in
-        // flight while its slot is awaited
-        Load A;
-        uint32_t uA = 0;
-        while (load_next(A, uA))
-            if (!store(A, uA)) return;
-    }
+    Load A;
+    uint32_t uA = 0;
+    while (load_next(A, uA))
+        if (!store(A, uA)) return;
 }
 
 __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ PrefillParams P,
@@ -570,106 +580,108 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
     const uint32_t sbase = smem_u32(sm);
     Bars *B = reinterpret_cast<Bars *>(sm + SM_BAR);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank = (int)cluster_rank();   // 0: leader (issues the pair's MMAs), 1: follower
     const int4 *segs = P.plan_inline ? reinterpret_cast<const int4 *>(PL.v) : P.segs;
     const int32_t *cta_seg = P.plan_inline ? PL.v + P.off_cta : P.cta_seg;
-    const int s0 = cta_seg[blockIdx.x], s1 = cta_seg[blockIdx.x + 1];
+    const int pr = blockIdx.x >> 1;   // the pair's run of segments
+    const int s0 = cta_seg[pr], s1 = cta_seg[pr + 1];
     // Launched with programmatic stream serialisation after k_prefill_q: everything up to the
     // first query-tile copy (barriers, TMEM, the producers' K/V tiles, which earlier launches
-    // wrote) overlaps that kernel; the issuing thread waits for it before the copy.
+    // wrote) overlaps that kernel; the copying threads wait for it before the copy.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&B->slot_full[i], 128 * NGRP);
+            mbar_init(&B->slot_full[i], 2 * 128 * NGRP);
             mbar_init(&B->slot_free[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&B->s_full[i], 1);
             mbar_init(&B->s_read[i], 128 * SMX_GROUPS);
-            mbar_init(&B->p_full[i], 128 * SMX_GROUPS);
+            mbar_init(&B->p_full[i], 2 * 128 * SMX_GROUPS);
             mbar_init(&B->pv_done[i], 1);
         }
         mbar_init(&B->q_full, 1);
+        mbar_init(&B->q_peer, 1);
         mbar_init(&B->q_empty, 1);
         mbar_init(&B->drain, 1);
         B->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B->tmem)),
+    if (warp == 0) {   // both CTAs' warp 0: the pair's tensor memory
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B->tmem)),
                      "r"(TM_COLS)
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    pair_sync();   // both CTAs' barriers initialised and TMEM allocated before any cross-CTA arrival
     tc_fence_after();
     const uint32_t tmem = B->tmem;
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ MMA issue (warp 0)
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
+            // -------------------------------------------------------------- MMA issue (leader)
             bool ok = true;
             int q_pending = -1;   // parity of a query copy still in flight after an abort
             uint32_t it = 0, op0 = 0;
             const uint32_t qa = sbase + SM_Q, ra = sbase + SM_RING;
-            // wait for ring slot u (the u-th half-tile of this CTA); returns its address
+            // wait for ring slot u (the u-th op of the pair); returns its address
             auto slot_wait = [&](uint32_t u, uint32_t &addr) -> bool {
                 const uint32_t sl = u % NSLOT;
                 addr = ra + sl * SLOT_BYTES;
                 return wait_bar(&B->slot_full[sl], (u / NSLOT) & 1, B, P.status);
             };
-            auto issue_s = [&](uint32_t j, uint32_t op) -> bool {
+            auto issue_s = [&](uint32_t j, uint32_t u) -> bool {
+                uint32_t kaddr;
+                if (!slot_wait(u, kaddr)) return false;
+                tc_fence_after();
                 const uint32_t d = tmem + TM_S + (j & 1) * KT;
-                for (int h = 0; h < 2; h++) {
-                    uint32_t kaddr;
-                    if (!slot_wait(2 * op + h, kaddr)) return false;
-                    tc_fence_after();
-                    // descriptor start addresses advance by (bytes >> 4) in the low field
-                    const uint64_t qd = sdesc(qa + 2 * h * 16384), kd = sdesc(kaddr);
+                // descriptor start addresses advance by (bytes >> 4) in the low field
+                const uint64_t qd = sdesc(qa), kd = sdesc(kaddr);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++)
-                        mma_f16_ss(d, qd + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
-                                   kd + (uint64_t)(((kk >> 2) * (KT * 128) + (kk & 3) * 32) >> 4), IDESC_S,
-                                   (h == 0 && kk == 0) ? 0u : 1u);
-                    mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
-                }
-                mma_commit(&B->s_full[j & 1]);
+                for (int kk = 0; kk < HD / 16; kk++)
+                    mma_f16_ss(d, qd + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                               kd + (uint64_t)(((kk >> 2) * (64 * 128) + (kk & 3) * 32) >> 4), IDESC_S, kk ? 1u : 0u);
+                mma_commit_pair(&B->slot_free[u % NSLOT]);
+                mma_commit_pair(&B->s_full[j & 1]);
                 return true;
             };
-            auto issue_pv = [&](uint32_t j, uint32_t op, bool first) -> bool {
+            auto issue_pv = [&](uint32_t j, uint32_t u, bool first) -> bool {
                 const uint32_t b = j & 1;
                 if (!wait_bar(&B->p_full[b], (j >> 1) & 1, B, P.status)) return false;
-                for (int h = 0; h < 2; h++) {
-                    uint32_t vaddr;
-                    if (!slot_wait(2 * op + h, vaddr)) return false;
-                    tc_fence_after();
-                    const uint64_t vd = sdesc(vaddr);
+                uint32_t vaddr;
+                if (!slot_wait(u, vaddr)) return false;
+                tc_fence_after();
+                const uint64_t vd = sdesc(vaddr);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * KT + 64 * h + kk * 8, vd + (uint64_t)((kk * 32) >> 4),
-                                   IDESC_PV, (first && h == 0 && kk == 0) ? 0u : 1u);
-                    mma_commit(&B->slot_free[(2 * op + h) % NSLOT]);
-                }
-                mma_commit(&B->pv_done[b]);
+                for (int kk = 0; kk < KT / 16; kk++)   // P of keys 16 kk..: columns 64 (kk >> 2) + 8 (kk & 3)
+                    mma_f16_ts(tmem + TM_O, tmem + TM_S + b * KT + 64 * (kk >> 2) + 8 * (kk & 3),
+                               vd + (uint64_t)(((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4), IDESC_PV,
+                               (first && kk == 0) ? 0u : 1u);
+                mma_commit_pair(&B->slot_free[u % NSLOT]);
+                mma_commit_pair(&B->pv_done[b]);
                 return true;
             };
             asm volatile("griddepcontrol.wait;" ::: "memory");   // query tiles of k_prefill_q
             for (int si = s0; si < s1 && ok; si++) {
                 const Seg sg = seg_of(segs, si);
                 if (si > s0 && !(ok = wait_bar(&B->q_empty, (si - s0 - 1) & 1, B, P.status))) break;
+                // the leader's tile of the pair (2 gp) always exists
+                const int tile = (sg.tile / P.n_gpairs) * P.n_groups + 2 * (sg.tile % P.n_gpairs);
                 mbar_expect_tx(&B->q_full, PF_QTILE);
-                const uint8_t *qsrc = P.qtiles + (int64_t)sg.tile * PF_QTILE;
+                const uint8_t *qsrc = P.qtiles + (int64_t)tile * PF_QTILE;
 #pragma unroll
                 for (int c = 0; c < 4; c++) bulk_load(sm + SM_Q + c * 16384, qsrc + c * 16384, 16384, &B->q_full);
                 if (!(ok = wait_bar(&B->q_full, (si - s0) & 1, B, P.status))) {
                     q_pending = (si - s0) & 1;
                     break;
                 }
+                if (!(ok = wait_bar(&B->q_peer, (si - s0) & 1, B, P.status))) break;
                 tc_fence_after();
                 for (int k = 0; k < sg.nk && ok; k++) {
                     ok = issue_s(it + k, op0 + op_k(k));
-                    if (ok && k == sg.nk - 1) mma_commit(&B->q_empty);
+                    if (ok && k == sg.nk - 1) mma_commit_pair(&B->q_empty);
                     if (ok && k >= 1) ok = issue_pv(it + k - 1, op0 + op_v(k - 1, sg.nk), k == 1);
                 }
                 if (ok) ok = issue_pv(it + sg.nk - 1, op0 + op_v(sg.nk - 1, sg.nk), sg.nk == 1);
@@ -677,20 +689,46 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 op0 += 2 * sg.nk;
             }
             if (q_pending >= 0) drain_bar(&B->q_full, (uint32_t)q_pending, P.status);
-            mma_commit(&B->drain);
+            mma_commit_own(&B->drain);
             drain_bar(&B->drain, 0, P.status);
+        } else if (lane == 0) {
+            // -------------------------------------------------------------- follower: its query tiles
+            // For each segment: once the pair's previous S MMAs are done with the query buffer,
+            // copy this CTA's query tile (rows 128-255 of the pair's MMAs) and tell the leader.
+            bool ok = true;
+            int q_pending = -1;
+            asm volatile("griddepcontrol.wait;" ::: "memory");   // query tiles of k_prefill_q
+            for (int si = s0; si < s1 && ok; si++) {
+                const Seg sg = seg_of(segs, si);
+                if (si > s0 && !(ok = wait_bar(&B->q_empty, (si - s0 - 1) & 1, B, P.status))) break;
+                const int g = 2 * (sg.tile % P.n_gpairs) + 1;
+                if (g < P.n_groups) {
+                    mbar_expect_tx(&B->q_full, PF_QTILE);
+                    const uint8_t *qsrc = P.qtiles + ((int64_t)(sg.tile / P.n_gpairs) * P.n_groups + g) * PF_QTILE;
+#pragma unroll
+                    for (int c = 0; c < 4; c++) bulk_load(sm + SM_Q + c * 16384, qsrc + c * 16384, 16384, &B->q_full);
+                } else {
+                    mbar_arrive(&B->q_full);   // no second tile in this pair: rows fully masked
+                }
+                if (!(ok = wait_bar(&B->q_full, (si - s0) & 1, B, P.status))) {
+                    q_pending = (si - s0) & 1;
+                    break;
+                }
+                mbar_arrive_leader(&B->q_peer);
+            }
+            if (q_pending >= 0) drain_bar(&B->q_full, (uint32_t)q_pending, P.status);
         }
         __syncwarp();
     } else if (warp < 1 + 4 * SMX_GROUPS) {
         // ------------------------------------------------------------------ softmax
         // Warps 1-4 (half 0) and 5-8 (half 1): warp w reads TMEM lanes 32 (w & 3) .. +31, so
-        // thread r owns row r in both halves.  Control flow is warp-uniform (tcgen05.ld/st are
-        // warp-collective): every wait's result is agreed with __all_sync.  Per 128-key tile both
-        // halves read the whole S row for its max (so both raise the lazily raised reference the
-        // same way), meet at s_read, then half h turns keys 64h .. 64h+63 into P (fp16 pairs) and
-        // stores them over S columns 64h .. 64h+31, which only it read since the meeting.  If the
-        // row max grows by more than 2^8 over the reference, the reference moves up and l and O
-        // (half h rescales O columns 128h .. 128h+127) are scaled down.
+        // thread r owns row r of this CTA's tile in both halves.  Control flow is warp-uniform
+        // (tcgen05.ld/st are warp-collective): every wait's result is agreed with __all_sync.  Per
+        // 128-key tile both halves read the whole S row for its max (so both raise the lazily
+        // raised reference the same way), meet at s_read, then half h turns keys 64h .. 64h+63
+        // into P (fp16 pairs) and stores them over S columns 64h .. 64h+31, which only it read
+        // since the meeting.  If the row max grows by more than 2^8 over the reference, the
+        // reference moves up and l and O (half h rescales O columns 128h .. 128h+127) are scaled.
         const int half = (warp - 1) >> 2, r = (warp & 3) * 32 + lane;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
@@ -700,8 +738,9 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
         bool ok = true;
         for (int si = s0; si < s1 && ok; si++) {
             const Seg sg = seg_of(segs, si);
-            const int tok = (sg.tile % P.n_groups) * P.tpt + r / P.G;
-            const int qpos = tok < P.Tc ? P.pos0 + tok : -1;
+            const int g = 2 * (sg.tile % P.n_gpairs) + rank;   // this CTA's query group (n_groups: none)
+            const int tok = g * P.tpt + r / P.G;
+            const int qpos = g < P.n_groups && tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
             for (int k = 0; k < sg.nk; k++) {
                 const uint32_t j = it + k, b = j & 1;
@@ -741,15 +780,15 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&B->p_full[b]);
+                mbar_arrive_leader(&B->p_full[b]);
             }
             if (!ok) break;
             // ---- epilogue: this half's O columns of the segment's partial record
             const uint32_t jl = it + sg.nk - 1;
             if (!(ok = wait_all(&B->pv_done[jl & 1], (jl >> 1) & 1))) break;
             tc_fence_after();
-            {   // stores of a warp cover 32 adjacent rows
-                float *rec = P.partial + (int64_t)sg.part * pf_part_floats();
+            if (g < P.n_groups) {   // records 2 part + rank; stores of a warp cover 32 adjacent rows
+                float *rec = P.partial + (int64_t)(2 * sg.part + rank) * pf_part_floats();
 #pragma unroll 1
                 for (int c8 = 4 * half; c8 < 4 * half + 4; c8++) {
                     uint32_t o[32];
@@ -769,16 +808,16 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
         }
     } else {
         // ------------------------------------------------------------------ producers
-        // warps 8-15 fill the K halves, warps 16-23 the V halves of the ring.  Loads run one half
-        // tile ahead: the next half's bytes are in flight while this one is converted and stored.
-        if (warp < PW_V) produce<true>(P, segs, B, sbase, tid - 32 * PW_K, s0, s1);
-        else produce<false>(P, segs, B, sbase, tid - 32 * PW_V, s0, s1);
+        // warps 9-12 fill this CTA's halves of the K tiles, warps 13-16 its halves of the V tiles.
+        if (warp < PW_V) produce<true>(P, segs, B, sbase, tid - 32 * PW_K, rank, s0, s1);
+        else produce<false>(P, segs, B, sbase, tid - 32 * PW_V, rank, s0, s1);
     }
     tc_fence_before();
     __syncthreads();
+    pair_sync();   // the leader's MMAs are drained: neither CTA's tensor or shared memory is in use
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS) : "memory");
     }
 }
 
@@ -799,8 +838,11 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const __grid_constant__ P
     // the next call's k_prefill_q may become resident now (it waits for this grid)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");   // partial records of k_prefill
-    const int2 tp = (P.plan_inline ? reinterpret_cast<const int2 *>(PL.v + P.off_tiles) : P.tile_parts)[tile];
-    const float *base = P.partial + (int64_t)tp.y * pf_part_floats();
+    // the tile's pair tile and its CTA in the pair: record of part i = 2 (first + i) + rank
+    const int kvh0 = tile / P.n_groups, g0 = tile % P.n_groups;
+    const int2 tp = (P.plan_inline ? reinterpret_cast<const int2 *>(PL.v + P.off_tiles)
+                                   : P.tile_parts)[kvh0 * P.n_gpairs + (g0 >> 1)];
+    const float *base = P.partial + (int64_t)(2 * tp.y + (g0 & 1)) * pf_part_floats();
     float M = -INFINITY, L = 0.f;
     float4 acc[4];
 #pragma unroll
@@ -810,7 +852,7 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const __grid_constant__ P
         float4 v[MG_PB][4];
 #pragma unroll
         for (int k = 0; k < MG_PB; k++) {
-            const float *rec = base + (int64_t)min(p0 + k, tp.x - 1) * pf_part_floats();   // clamped: weight 0
+            const float *rec = base + (int64_t)2 * min(p0 + k, tp.x - 1) * pf_part_floats();   // clamped: weight 0
             m[k] = p0 + k < tp.x ? __ldcg(rec + PF_ROWS * HD + row) : -INFINITY;
             l[k] = __ldcg(rec + PF_ROWS * HD + PF_ROWS + row) + __ldcg(rec + PF_ROWS * HD + 2 * PF_ROWS + row);
 #pragma unroll
@@ -875,20 +917,62 @@ static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t sm
 
 // The three kernels of a call, each launched behind its predecessor (programmatic dependent
 // launch): k_prefill_q waits for whatever precedes it before reading the queries, k_prefill and
-// k_prefill_merge wait for the kernel before them (see the kernels).
-cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st) {
+// k_prefill_merge wait for the kernel before them (see the kernels).  k_prefill runs as clusters
+// of two CTAs (the MMA pairs).
+static cudaError_t configure_prefill() {
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64 && configured[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) configured[dev] = true;
+    return e;
+}
+
+static void prefill_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&attr)[2], unsigned grid, cudaStream_t st) {
+    cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(pf::NTHR);
+    cfg.dynamicSmemBytes = pf::SMEM_BYTES;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+}
+
+int prefill_max_pairs() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cached[dev]) return cached[dev];
+    if (configure_prefill() != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    prefill_config(cfg, attr, 2 * 64, nullptr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, pf::k_prefill, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
     }
+    cached[dev] = n;
+    return n;
+}
+
+cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st) {
+    cudaError_t e = configure_prefill();
+    if (e != cudaSuccess) return e;
     const int64_t rows = (int64_t)p.n_tiles * PF_ROWS;
     if ((e = launch_pdl(pf::k_prefill_q, (unsigned)((rows + 7) / 8), 256, 0, st, p)) != cudaSuccess) return e;
-    if ((e = launch_pdl(pf::k_prefill, (unsigned)p.n_ctas, pf::NTHR, pf::SMEM_BYTES, st, p, plan)) != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    prefill_config(cfg, attr, (unsigned)p.n_ctas, st);
+    if ((e = cudaLaunchKernelEx(&cfg, pf::k_prefill, p, plan)) != cudaSuccess) return e;
     if ((e = launch_pdl(pf::k_prefill_merge, (unsigned)(p.n_tiles * (PF_ROWS / pf::MG_ROWS)), 256, 0, st, p, plan)) !=
         cudaSuccess)
         return e;

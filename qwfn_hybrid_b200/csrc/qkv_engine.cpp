@@ -828,20 +828,32 @@ struct PfPlan {
     std::vector<int32_t> cta_seg;     // n_runs + 1
     int32_t n_parts = 0;
 };
-static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPlan &pl) {
-    const int n_tiles = (int)nk.size();
-    pl.segs.clear();
-    pl.cta_seg.assign(n_ctas + 1, 0);
-    std::vector<int32_t> count(n_tiles, 0);
-    int t = 0, off = 0;
-    for (int c = 0; c < n_ctas; c++) {
-        pl.cta_seg[c] = (int32_t)(pl.segs.size() / 4);
-        int64_t left = W * (c + 1) / n_ctas - W * c / n_ctas;
-        while (left > 0) {
-            const int n = (int)std::min<int64_t>(left, nk[t] - off);
-            pl.segs.insert(pl.segs.end(), {t, off, off + n, -1});
-            count[t]++;
-            left -= n;
+// Greedy cut of the flattened (pair tile, KV tile) sequence into runs of cost <= budget, where a
+// run pays PF_SEG_COST KV tiles for every segment after its first (the finished segment's
+// epilogue and the next query tiles).  Returns the runs used; with `segs`, records the segments
+// {pair tile, kt0, kt1} and the run starts.
+constexpr double PF_SEG_COST = 2.5;
+static int pf_cut(const std::vector<int32_t> &nk, double budget, std::vector<int32_t> *segs,
+                  std::vector<int32_t> *run_seg) {
+    int runs = 0;
+    size_t t = 0;
+    int off = 0;
+    while (t < nk.size()) {
+        if (run_seg) run_seg->push_back((int32_t)(segs->size() / 4));
+        runs++;
+        double left = budget;
+        bool first = true;
+        while (t < nk.size()) {
+            const double avail = left - (first ? 0.0 : PF_SEG_COST);
+            int n = (int)std::floor(avail + 1e-9);
+            if (n < 1) {
+                if (!first) break;
+                n = 1;   // a run takes at least one KV tile
+            }
+            n = std::min(n, nk[t] - off);
+            if (segs) segs->insert(segs->end(), {(int32_t)t, off, off + n, -1});
+            left = avail - n;
+            first = false;
             off += n;
             if (off == nk[t]) {
                 t++;
@@ -849,7 +861,27 @@ static void pf_build(const std::vector<int32_t> &nk, int64_t W, int n_ctas, PfPl
             }
         }
     }
-    pl.cta_seg[n_ctas] = (int32_t)(pl.segs.size() / 4);
+    return runs;
+}
+
+// Plan of one launch: the smallest run budget whose greedy cut fits n_runs runs (binary search;
+// the cut may need fewer), then every segment's part index (parts of a pair tile consecutive, in
+// KV order).
+static void pf_build(const std::vector<int32_t> &nk, int64_t W, int &n_runs, PfPlan &pl) {
+    const int n_tiles = (int)nk.size();
+    double lo = (double)W / n_runs, hi = lo + 2 * PF_SEG_COST + 2;
+    while (pf_cut(nk, hi, nullptr, nullptr) > n_runs) hi *= 1.5;
+    for (int i = 0; i < 40 && hi - lo > 0.01; i++) {
+        const double mid = 0.5 * (lo + hi);
+        if (pf_cut(nk, mid, nullptr, nullptr) <= n_runs) hi = mid;
+        else lo = mid;
+    }
+    pl.segs.clear();
+    pl.cta_seg.clear();
+    n_runs = pf_cut(nk, hi, &pl.segs, &pl.cta_seg);
+    std::vector<int32_t> count(n_tiles, 0);
+    for (size_t i = 0; i < pl.segs.size(); i += 4) count[pl.segs[i]]++;
+    pl.cta_seg.push_back((int32_t)(pl.segs.size() / 4));
     pl.tile_parts.assign(2 * n_tiles, 0);
     pl.n_parts = 0;
     for (int i = 0; i < n_tiles; i++) {
@@ -915,8 +947,8 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     PfPlan pl;
     int max_pairs = prefill_max_pairs();
     if (max_pairs <= 0) max_pairs = eng->num_sms / 2;
-    const int n_runs = (int)std::min<int64_t>(max_pairs, W);
-    pf_build(nk, W, n_runs, pl);
+    int n_runs = (int)std::min<int64_t>(max_pairs, W);
+    pf_build(nk, W, n_runs, pl);   // may use fewer runs
     if (pl.n_parts > eng->pf_max_parts)
         return fail(eng, QKV_ERR_NO_MEMORY, "prefill plan: %d parts (max %d)", pl.n_parts, eng->pf_max_parts);
     std::vector<int32_t> ints;

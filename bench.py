@@ -615,7 +615,7 @@ def run_cfg3(args) -> None:
                    "l2": "inputs larger than L2 (134 MB of bf16 queries + 268 MB of outputs per step)"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
                      "peak_source": peak_src, "traffic": None,
-                     "kernel": "k_prefill_q + k_prefill per chunk (CUDA events around each qkv_attn_prefill call)",
+                     "kernel": "k_prefill_q + k_prefill + k_prefill_merge per chunk (CUDA events around each qkv_attn_prefill call)",
                      "flops_per_step": prefill_flops(), "attn_ms_per_step": attn_ms},
         "e2e": {"value": ws * PF_N / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": (K.numel() + V.numel()) * 4 + Qb.numel() * 2,

@@ -258,42 +258,47 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     return d;
 }
 // Max of the thread's S row (KT columns from TMEM address scol); columns >= nvis count as -inf
-// unless FULL.  Read in 32-column chunks, each reduced as a tree.
+// unless FULL.  Read 64 columns per round trip (two loads, one wait), each 32 reduced as a tree.
 template <bool FULL>
 __device__ __forceinline__ float row_max(uint32_t scol, int nvis) {
     float m = -INFINITY;
 #pragma unroll 1
-    for (int c = 0; c < KT / 32; c++) {
-        uint32_t v[32];
-        tmem_ld32(scol + 32 * c, v);
+    for (int c = 0; c < KT / 32; c += 2) {
+        uint32_t v[2][32];
+        tmem_ld32(scol + 32 * c, v[0]);
+        tmem_ld32(scol + 32 * c + 32, v[1]);
         tmem_wait_ld();
-        float x[32];
 #pragma unroll
-        for (int e = 0; e < 32; e++) x[e] = (FULL || 32 * c + e < nvis) ? __uint_as_float(v[e]) : -INFINITY;
+        for (int h = 0; h < 2; h++) {
+            float x[32];
 #pragma unroll
-        for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
-        m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
+            for (int e = 0; e < 32; e++) x[e] = (FULL || 32 * (c + h) + e < nvis) ? __uint_as_float(v[h][e]) : -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
+            m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
+        }
     }
     return m;
 }
-// P = 2^(s * sl2 - mu) of keys 64 half .. 64 half + 63 of the thread's row, stored as fp16 pairs:
-// chunk c's 32 keys go to columns 16 c + 32 half .. +15, inside the S columns this half already
+// P = 2^(s * sl2 - mu) of keys 64 half .. 64 half + 63 of the thread's row (one round trip),
+// stored as fp16 pairs in columns 64 half .. 64 half + 31, inside the S columns this half just
 // read.  Returns the sum of the P values.
 template <bool FULL>
 __device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, float sl2, float mu) {
     const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-mu, -mu);
     float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
-#pragma unroll 1
-    for (int c = 2 * half; c < 2 * half + 2; c++) {
-        uint32_t v[32];
-        tmem_ld32(scol + 32 * c, v);
-        tmem_wait_ld();
+    uint32_t v[2][32];
+    tmem_ld32(scol + 64 * half, v[0]);
+    tmem_ld32(scol + 64 * half + 32, v[1]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
         uint32_t pr[16];
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-            const int i = 32 * c + 2 * e;
-            const float2 y = __ffma2_rn(make_float2(FULL || i < nvis ? __uint_as_float(v[2 * e]) : -INFINITY,
-                                                    FULL || i + 1 < nvis ? __uint_as_float(v[2 * e + 1]) : -INFINITY),
+            const int i = 64 * half + 32 * h + 2 * e;
+            const float2 y = __ffma2_rn(make_float2(FULL || i < nvis ? __uint_as_float(v[h][2 * e]) : -INFINITY,
+                                                    FULL || i + 1 < nvis ? __uint_as_float(v[h][2 * e + 1]) : -INFINITY),
                                         sc2, nm2);
             const float2 p = make_float2(ex2(y.x), ex2(y.y));
             if (e & 1) lb = __fadd2_rn(lb, p);
@@ -301,7 +306,7 @@ __device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, float 
             const __half2 hp = __floats2half2_rn(p.x, p.y);
             pr[e] = *reinterpret_cast<const uint32_t *>(&hp);
         }
-        tmem_st16(scol + 16 * c + 32 * half, pr);
+        tmem_st16(scol + 64 * half + 16 * h, pr);
     }
     return (la.x + lb.x) + (la.y + lb.y);
 }

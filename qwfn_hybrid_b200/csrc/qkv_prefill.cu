@@ -204,9 +204,15 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void pair_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrival on the leader's (cluster rank 0) copy of barrier `bar`, release at cluster scope: the
-// follower's shared-memory stores before it are visible to the MMAs the leader issues after it.
-__device__ __forceinline__ void mbar_arrive_leader(uint64_t *bar) {
+// Arrival on the leader's (cluster rank 0) copy of barrier `bar`.  From the follower: through
+// the barrier's cluster address, release at cluster scope, so that the follower's shared and
+// tensor memory stores before it are visible to the MMAs the leader issues after it.  The
+// leader's own threads arrive locally (CTA scope, the single-CTA pattern).
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t *bar, int rank) {
+    if (rank == 0) {
+        mbar_arrive(bar);
+        return;
+    }
     uint32_t a;
     asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(a) : "r"(smem_u32(bar)));
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
@@ -569,7 +575,7 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
         if constexpr (KGRP) k_store(slot, t, ld);
         else v_store(slot, t, ld);
         fence_proxy_async();
-        mbar_arrive_leader(&B->slot_full[sl]);
+        mbar_arrive_leader(&B->slot_full[sl], rank);
         return true;
     };
     Load A;
@@ -719,7 +725,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                     q_pending = (si - s0) & 1;
                     break;
                 }
-                mbar_arrive_leader(&B->q_peer);
+                mbar_arrive_leader(&B->q_peer, rank);
             }
             if (q_pending >= 0) drain_bar(&B->q_full, (uint32_t)q_pending, P.status);
         }
@@ -785,7 +791,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive_leader(&B->p_full[b]);
+                mbar_arrive_leader(&B->p_full[b], rank);
             }
             if (!ok) break;
             // ---- epilogue: this half's O columns of the segment's partial record

@@ -121,10 +121,23 @@ def _ptr(x) -> int | None:
     return x.data_ptr()
 
 
+_cur_stream = None   # () -> raw cudaStream_t of torch's current stream on the current device, or None
+
+
 def _stream(stream) -> int | None:
+    """Raw stream handle: torch's current stream when None (looked up without building a Stream
+    object, a few microseconds per call otherwise), an int as is, else `stream.cuda_stream`."""
+    global _cur_stream
     if stream is None:
-        import torch
-        return torch.cuda.current_stream().cuda_stream if torch.cuda.is_available() else None
+        if _cur_stream is None:
+            import torch
+            if not torch.cuda.is_available():
+                _cur_stream = lambda: None
+            else:
+                raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+                dev = torch.cuda.current_device
+                _cur_stream = (lambda: raw(dev())) if raw else (lambda: torch.cuda.current_stream().cuda_stream)
+        return _cur_stream()
     if isinstance(stream, int):
         return stream
     return stream.cuda_stream

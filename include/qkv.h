@@ -208,6 +208,41 @@ qkv_status qkv_snapshot_to_host(qkv_engine *eng, const qkv_snapshot *snap, void 
 qkv_status qkv_snapshot_from_host(qkv_engine *eng, const void *src, size_t bytes, int32_t n_past,
                                   qkv_snapshot **out, void *stream);
 
+/* ------------------------------------------------------------------ saved-sequence store --- */
+
+/* Saved sequences keyed by their token ids, held as device snapshots (shared pages + a device
+ * copy of the recurrent state) instead of host blobs.  Replaces the server's saved_seq list and
+ * its restore / shared-prefix logic (tools/qwfn_server.cpp:764-800, 1380-1430): at most
+ * max_entries sequences (the reference keeps 4) holding at most cap_bytes of device memory
+ * (snapshot pages in every layer + recurrent copy; the reference caps host bytes by
+ * QWFN_SNAP_MB), least recently used first out.  Bound to one engine; destroy it before the
+ * engine. */
+typedef struct qkv_store qkv_store;
+qkv_status qkv_store_create(qkv_engine *eng, size_t cap_bytes, int32_t max_entries, qkv_store **out);
+void qkv_store_destroy(qkv_store *store);
+/* Snapshot a slot whose n_past equals n_tok and keep it under tok[0..n_tok) (server save_seq,
+ * tools/qwfn_server.cpp:771-780): an entry with equal tokens is replaced; a snapshot above the
+ * cap is not kept (*kept = 0, not an error); older entries leave until both limits hold. */
+qkv_status qkv_store_save(qkv_store *store, int32_t slot, const int32_t *tok, int32_t n_tok, int32_t *kept,
+                          void *stream);
+/* Restore into slot the longest saved sequence that prompt[0..n_prompt) strictly extends and make
+ * it the most recently used (*n_restored = its length); with none, or if its restore fails,
+ * reset the slot (*n_restored = 0).  The server's restore_or_reset after its set-aside step
+ * (tools/qwfn_server.cpp:1380-1404, best_saved 782-794); the set-aside is a qkv_store_save. */
+qkv_status qkv_store_restore_or_reset(qkv_store *store, int32_t slot, const int32_t *prompt, int32_t n_prompt,
+                                      int32_t *n_restored, void *stream);
+/* Where a fresh prefill should stop once to save a prefix it shares with a saved sequence
+ * (shared_prefix_split, tools/qwfn_server.cpp:1410-1430): the longest common prefix L with any
+ * entry if n_consumed < min_prefix, L >= min_prefix, L + 16 < n_prompt, L >= n_consumed + 2 and
+ * no entry is exactly that prefix; else 0.  The reference's min_prefix is 2048. */
+qkv_status qkv_store_prefix_split(const qkv_store *store, const int32_t *prompt, int32_t n_prompt,
+                                  int32_t n_consumed, int32_t min_prefix, int32_t *split_at);
+/* Drop the n least recently used entries (e.g. when the page pool runs out). */
+qkv_status qkv_store_evict(qkv_store *store, int32_t n);
+/* Entries and the device bytes they hold; entry i in LRU order (0 = least recently used). */
+qkv_status qkv_store_info(const qkv_store *store, int32_t *n_entries, size_t *bytes);
+qkv_status qkv_store_entry(const qkv_store *store, int32_t i, int32_t *n_tok, size_t *bytes);
+
 /* Rewind n_back positions after rejected drafts: restore the recurrent/conv state from
  * rollback snapshot n_back-1 and set n_past -= n_back (cache rows are overwritten later).
  * Replaces engine::rollback_n (src/qwfn_engine.cpp:3629-3660). */

@@ -27,6 +27,8 @@ EXPORTS = [
     "qkv_snapshot_restore", "qkv_snapshot_restore_many", "qkv_snapshot_release", "qkv_snapshot_info",
     "qkv_snapshot_to_host", "qkv_snapshot_from_host", "qkv_rollback", "qkv_rollback_arm", "qkv_state_ptr",
     "qkv_cache_view_get", "qkv_attn_decode_static", "qkv_device_status", "qkv_launch_count", "qkv_shard_lpt",
+    "qkv_store_create", "qkv_store_destroy", "qkv_store_save", "qkv_store_restore_or_reset",
+    "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
 ]
 
 
@@ -92,6 +94,11 @@ def lib() -> ctypes.CDLL:
         "qkv_device_status": [P, P, pI32],
         "qkv_shard_lpt": [ctypes.POINTER(I64), I32, I32, pI32],
         "qkv_launch_count": [ctypes.POINTER(ctypes.c_uint64)],
+        "qkv_store_create": [P, SZ, I32, ctypes.POINTER(P)], "qkv_store_destroy": [P],
+        "qkv_store_save": [P, I32, pI32, I32, pI32, P],
+        "qkv_store_restore_or_reset": [P, I32, pI32, I32, pI32, P],
+        "qkv_store_prefix_split": [P, pI32, I32, I32, I32, pI32], "qkv_store_evict": [P, I32],
+        "qkv_store_info": [P, pI32, ctypes.POINTER(SZ)], "qkv_store_entry": [P, I32, pI32, ctypes.POINTER(SZ)],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -99,6 +106,7 @@ def lib() -> ctypes.CDLL:
         fn.restype = ctypes.c_int
     L.qkv_destroy.restype = None
     L.qkv_snapshot_release.restype = None
+    L.qkv_store_destroy.restype = None
     L.qkv_last_error.restype = ctypes.c_char_p
     L.qkv_status_string.restype = ctypes.c_char_p
     _lib = L
@@ -183,6 +191,60 @@ class Snapshot:
         if not self.released:
             lib().qkv_snapshot_release(self.engine.handle, self.handle)
             self.released = True
+
+
+class Store:
+    """Saved sequences on the device keyed by token ids: the reference server's saved_seq list with
+    restore_or_reset and shared_prefix_split (tools/qwfn_server.cpp:764-800, 1380-1430)."""
+
+    def __init__(self, engine: "Engine", cap_bytes: int, max_entries: int = 4):
+        self.engine = engine
+        h = ctypes.c_void_p()
+        engine._check(lib().qkv_store_create(engine.handle, cap_bytes, max_entries, ctypes.byref(h)))
+        self.handle = h.value
+
+    def _s(self, stream):
+        return _stream(stream) if self.engine.device >= 0 else None
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().qkv_store_destroy(self.handle)
+            self.handle = None
+
+    def save(self, slot: int, tokens, stream=None) -> bool:
+        kept = ctypes.c_int32()
+        self.engine._check(lib().qkv_store_save(self.handle, slot, _i32_array(tokens), len(tokens),
+                                                ctypes.byref(kept), self._s(stream)))
+        return bool(kept.value)
+
+    def restore_or_reset(self, slot: int, prompt, stream=None) -> int:
+        n = ctypes.c_int32()
+        self.engine._check(lib().qkv_store_restore_or_reset(self.handle, slot, _i32_array(prompt), len(prompt),
+                                                            ctypes.byref(n), self._s(stream)))
+        return n.value
+
+    def prefix_split(self, prompt, n_consumed: int, min_prefix: int = 2048) -> int:
+        at = ctypes.c_int32()
+        self.engine._check(lib().qkv_store_prefix_split(self.handle, _i32_array(prompt), len(prompt), n_consumed,
+                                                        min_prefix, ctypes.byref(at)))
+        return at.value
+
+    def evict(self, n: int = 1) -> None:
+        self.engine._check(lib().qkv_store_evict(self.handle, n))
+
+    def info(self) -> tuple[int, int]:
+        n, b = ctypes.c_int32(), ctypes.c_size_t()
+        self.engine._check(lib().qkv_store_info(self.handle, ctypes.byref(n), ctypes.byref(b)))
+        return n.value, b.value
+
+    def entries(self) -> list[tuple[int, int]]:
+        """(token count, device bytes) per entry, least recently used first."""
+        out = []
+        for i in range(self.info()[0]):
+            n, b = ctypes.c_int32(), ctypes.c_size_t()
+            self.engine._check(lib().qkv_store_entry(self.handle, i, ctypes.byref(n), ctypes.byref(b)))
+            out.append((n.value, b.value))
+        return out
 
 
 class Engine:

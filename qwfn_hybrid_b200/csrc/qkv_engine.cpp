@@ -109,6 +109,13 @@ static qkv_status fail(qkv_engine *eng, qkv_status st, const char *fmt, ...) {
 
 static cudaStream_t S(void *stream) { return reinterpret_cast<cudaStream_t>(stream); }
 
+qkv_status qkv::engine_fail(qkv_engine *eng, qkv_status st, const char *msg) { return fail(eng, st, "%s", msg); }
+
+size_t qkv::snapshot_held_bytes(const qkv_snapshot *snap) {
+    const qkv_engine *eng = snap->eng;
+    return snap->pages.size() * (size_t)eng->page_bytes * eng->cfg.n_layer + (size_t)eng->rec_slot_bytes;
+}
+
 static qkv_status use_device(qkv_engine *eng) {
     if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
     int cur = -1;

@@ -6,6 +6,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "qkv.h"
+
 namespace qkv {
 
 // Kernels launched by this library (qkv_launch_count); bumped by every launch helper.
@@ -173,5 +175,12 @@ struct alignas(16) PfPlanInline {
 };
 cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cudaStream_t st);
 int prefill_max_pairs();   // co-resident CTA pairs of kernel D (0 = unknown)
+
+// ---- host side shared by the engine and the saved-sequence store (qkv_store.cpp) ---------------
+// Sets the engine's last error (qkv_last_error) to msg and returns st.
+qkv_status engine_fail(qkv_engine *eng, qkv_status st, const char *msg);
+// Device bytes a snapshot holds: its pages in every layer's pool plus its recurrent-state copy
+// (counted on host-only engines too, where nothing is allocated).
+size_t snapshot_held_bytes(const qkv_snapshot *snap);
 
 }  // namespace qkv

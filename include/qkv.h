@@ -171,6 +171,63 @@ qkv_status qkv_read_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t p
 qkv_status qkv_write_rows(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n,
                           const void *K_in, const void *V_in, void *stream);
 
+/* ------------------------------------------------------------------ QSA lightning indexer -- */
+
+/* The model's own sparse-attention selector (src/qwfn_graph.cpp:280-367, 529-579,
+ * src/qwfn_engine.cpp:1072-1148), decode path.  Per token the caller supplies the indexer's raw
+ * key (F32 [key_len], after k_proj) and its query (F32 [n_head][key_len], after q_proj, q_norm
+ * and rope: idx_query, src/qwfn_graph.cpp:303-311); the projections need the model's weights
+ * and stay with the caller.  The engine keeps the raw keys as fp16 (the reference's F16
+ * idx_cache) and, for every block of `ratio` cells once its last cell is written, the pooled
+ * key fp16( rope( rms_norm(mean of the ratio raw keys) * k_norm ) ) at the block's first position
+ * (qsa_pool_blocks).  Text positions: the rope sections then all read the same position, so the
+ * interleaved multi-section rope is the NEOX-paired rotation of the first rope_dim dims with
+ * theta_i = p * freq_base^(-2i/rope_dim) (built as ggml's CPU rope does, by repeated fp32
+ * multiplication).  Both live in pages parallel to the KV pages (same page ids), so snapshots,
+ * restores and copy-on-write carry them. */
+typedef struct qkv_indexer_config {
+    int32_t n_head;         /* indexer heads (4)                                                */
+    int32_t key_len;        /* 128 (the only value this build provides)                         */
+    int32_t ratio;          /* cells per block (4, the only value this build provides)          */
+    int32_t top_k;          /* cells kept per token (2048): k_blocks = ceil((top_k+ratio-1)/ratio) */
+    int32_t rope_dim;       /* dims rotated (64; even, <= key_len)                              */
+    float   rope_freq_base; /* 1e7                                                              */
+    float   rms_eps;        /* 1e-6                                                             */
+} qkv_indexer_config;
+/* Turns the indexer on (once, before any indexer call); k_norm: host F32 [n_layer][key_len]
+ * (indexer.k_norm.weight per attention layer), NULL = all ones. */
+qkv_status qkv_indexer_enable(qkv_engine *eng, const qkv_indexer_config *cfg, const float *k_norm);
+/* Store n_rows raw keys (device F32 [n_rows][key_len]) at positions pos .. pos+n_rows-1 of a
+ * slot (pos <= the slot's n_past; its pages must exist: append the K/V rows first) and pool
+ * every block whose last cell is among them.  Replaces the indexer-key copy and pooling of
+ * qsa_top_k / qsa_dec_index (src/qwfn_graph.cpp:330-336, 529-552). */
+qkv_status qkv_idx_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, const float *k_raw,
+                          int32_t n_rows, void *stream);
+/* Block selection for T tokens per sequence at positions pos0[i] .. pos0[i]+T-1 (each token t
+ * selects for itself, as the reference's chained verify does).  For the token at position p:
+ * whole blocks b < (p+1)/ratio score sum_h relu(fp16(q_h) . pooled_b) (qsa_dec_cells,
+ * src/qwfn_graph.cpp:556-579); the block holding p, if incomplete, is always kept (the 1e9
+ * bias, src/qwfn_engine.cpp:1092-1096); the best k_blocks blocks in all are kept, ties by lower
+ * block index, or every block 0 .. p/ratio when there are no more than k_blocks.  q_idx: device
+ * F32 [n_seq][T][n_head][key_len]; blocks_out: device int32 [n_seq][T][k_blocks], ascending
+ * block ids, -1 after the n_out_out[i][t] kept ones; scores_out (nullable): device F32
+ * [n_seq][T][n_ctx/ratio], the scores of the whole blocks. */
+qkv_status qkv_idx_select(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int32_t n_seq,
+                          const float *q_idx, int32_t T, int32_t *blocks_out, int32_t *n_out_out, float *scores_out,
+                          void *stream);
+/* Sparse decode with the indexer: select as qkv_idx_select, gather each token's kept cells
+ * (those <= its position) into scratch pages, and attend to them with the decode kernel --
+ * the reference's qsa_dec_cells + cell mask + raw qsa_gather + ggml_flash_attn_ext
+ * (src/qwfn_graph.cpp:653-705).  Q/out as qkv_attn_decode. */
+qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                               int32_t n_seq, const float *q_idx, const float *Q, int32_t T, float scale, float *out,
+                               void *stream);
+/* Stored indexer data for tests and snapshots: raw keys of positions pos .. pos+n-1 (device fp16
+ * [n][key_len]) and pooled keys of blocks b0 .. b0+n_blk-1 (device fp16 [n_blk][key_len]); either
+ * output may be NULL. */
+qkv_status qkv_idx_read(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n, uint16_t *keys_out,
+                        int32_t b0, int32_t n_blk, uint16_t *pooled_out, void *stream);
+
 /* ------------------------------------------------------------------ kernel D -------------- */
 
 /* Chunked causal prefill: Tc query tokens at positions pos0 .. pos0+Tc-1 (their K/V rows

@@ -48,6 +48,12 @@ def lib():
         L.orc_blocks_to_cells.argtypes = [P, i32, i32, i64, P]
         L.orc_blocks_to_cells.restype = i64
         L.orc_max_threads.restype = i32
+        L.orc_idx_rope_table.argtypes = [i64, i32, f32, P]
+        L.orc_idx_pool.argtypes = [P, i64, P, f32, i32, P, P]
+        L.orc_idx_score.argtypes = [P, i32, P]
+        L.orc_idx_score.restype = f32
+        L.orc_idx_select.argtypes = [P, i32, P, i64, i32, P, P]
+        L.orc_idx_select.restype = i64
         _lib = L
     return _lib
 
@@ -152,3 +158,38 @@ def blocks_to_cells(blocks: np.ndarray, block_tokens: int, n_kv: int) -> np.ndar
     out = np.empty(blocks.shape[0] * block_tokens, dtype=np.int32)
     n = lib().orc_blocks_to_cells(_p(blocks), blocks.shape[0], block_tokens, n_kv, _p(out))
     return out[:n]
+
+
+# ---- QSA lightning indexer (decode path) ------------------------------------------------------
+IDX_KEY, IDX_R = 128, 4
+
+
+def idx_rope_table(n_blocks: int, rope_dim: int, freq_base: float) -> np.ndarray:
+    """float32 [n_blocks, rope_dim/2, 2] {cos, sin} at block positions 4b."""
+    out = np.zeros((n_blocks, max(rope_dim // 2, 1), 2), dtype=np.float32)
+    lib().orc_idx_rope_table(n_blocks, rope_dim, ctypes.c_float(freq_base), _p(out))
+    return out
+
+
+def idx_pool(keys16: np.ndarray, n_blocks: int, norm_w: np.ndarray, eps: float, rope_dim: int,
+             freq_base: float) -> np.ndarray:
+    """Raw fp16 key bits uint16 [>= 4*n_blocks, 128] -> pooled fp16 bits uint16 [n_blocks, 128]."""
+    keys16 = np.ascontiguousarray(keys16[:IDX_R * n_blocks], dtype=np.uint16)
+    cs = idx_rope_table(n_blocks, rope_dim, freq_base)
+    w = np.ascontiguousarray(norm_w, dtype=np.float32)
+    out = np.empty((n_blocks, IDX_KEY), dtype=np.uint16)
+    lib().orc_idx_pool(_p(keys16), n_blocks, _p(w), ctypes.c_float(eps), rope_dim, _p(cs), _p(out))
+    return out
+
+
+def idx_select(q: np.ndarray, pooled: np.ndarray, pos: int, k_blocks: int):
+    """q float32 [n_head, 128]; pooled uint16 [>= (pos+1)//4, 128].  Returns (kept block ids
+    ascending, scores of the whole blocks)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    pooled = np.ascontiguousarray(pooled, dtype=np.uint16)
+    whole = (pos + 1) // IDX_R
+    scores = np.zeros(max(whole, 1), dtype=np.float32)
+    blocks = np.empty(k_blocks, dtype=np.int32)
+    n = lib().orc_idx_select(_p(q), q.shape[0], _p(pooled), pos, k_blocks, _p(scores), _p(blocks))
+    return blocks[:n].copy(), scores[:whole]
+

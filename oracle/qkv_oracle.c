@@ -299,3 +299,123 @@ int64_t orc_blocks_to_cells(const int32_t *blocks, int top_k, int block_tokens, 
     }
     return n;
 }
+
+/* ------------------------------------------------------ QSA lightning indexer ---- */
+
+/* lane-0 value of an xor butterfly sum 16, 8, 4, 2, 1 over 32 lanes */
+static float bfly32(const float *v_in) {
+    float v[32], t[32];
+    memcpy(v, v_in, sizeof v);
+    for (int o = 16; o; o >>= 1) {
+        for (int l = 0; l < 32; l++) t[l] = v[l] + v[l ^ o];
+        memcpy(v, t, sizeof v);
+    }
+    return v[0];
+}
+
+void orc_idx_rope_table(int64_t n_blocks, int rope_dim, float freq_base, float *cs) {
+    const int half = rope_dim / 2;
+    const float theta_scale = powf(freq_base, -2.0f / (float)(rope_dim > 0 ? rope_dim : 1));
+    for (int64_t b = 0; b < n_blocks; b++) {
+        float th = (float)(b * ORC_IDX_R);
+        for (int i = 0; i < half; i++) {
+            cs[(b * half + i) * 2 + 0] = cosf(th);
+            cs[(b * half + i) * 2 + 1] = sinf(th);
+            th *= theta_scale;
+        }
+    }
+}
+
+void orc_idx_pool(const uint16_t *keys, int64_t n_blocks, const float *norm_w, float eps, int rope_dim,
+                  const float *cs, uint16_t *pooled) {
+    const int half = rope_dim / 2;
+    for (int64_t b = 0; b < n_blocks; b++) {
+        float x[ORC_IDX_KEY], y[ORC_IDX_KEY], part[32];
+        for (int d = 0; d < ORC_IDX_KEY; d++) {
+            float a = orc_fp16_to_fp32(keys[(b * ORC_IDX_R) * ORC_IDX_KEY + d]);
+            for (int m = 1; m < ORC_IDX_R; m++) a = a + orc_fp16_to_fp32(keys[(b * ORC_IDX_R + m) * ORC_IDX_KEY + d]);
+            x[d] = a * (1.0f / ORC_IDX_R);
+        }
+        for (int l = 0; l < 32; l++) {
+            float s = x[4 * l] * x[4 * l];
+            for (int j = 1; j < 4; j++) s = s + x[4 * l + j] * x[4 * l + j];
+            part[l] = s;
+        }
+        const float s = bfly32(part);
+        const float scale = 1.0f / sqrtf(s * (1.0f / ORC_IDX_KEY) + eps);
+        for (int d = 0; d < ORC_IDX_KEY; d++) y[d] = (x[d] * scale) * norm_w[d];
+        for (int d = 0; d < ORC_IDX_KEY; d++) {
+            float o = y[d];
+            if (d < half) {
+                const float c = cs[(b * half + d) * 2], sn = cs[(b * half + d) * 2 + 1];
+                o = y[d] * c - y[d + half] * sn;
+            } else if (d < 2 * half) {
+                const int i = d - half;
+                const float c = cs[(b * half + i) * 2], sn = cs[(b * half + i) * 2 + 1];
+                o = y[i] * sn + y[d] * c;
+            }
+            pooled[b * ORC_IDX_KEY + d] = orc_fp32_to_fp16(o);
+        }
+    }
+}
+
+float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b) {
+    double tot = 0.0;
+    for (int h = 0; h < n_head; h++) {
+        float part[32];
+        for (int l = 0; l < 32; l++) {
+            float a = 0.0f;
+            for (int j = 0; j < 4; j++) {
+                const int d = 4 * l + j;
+                const float qh = orc_fp16_to_fp32(orc_fp32_to_fp16(q[h * ORC_IDX_KEY + d]));
+                const float p = qh * orc_fp16_to_fp32(pooled_b[d]);
+                a = j == 0 ? p : a + p;
+            }
+            part[l] = a;
+        }
+        const float dot = bfly32(part);
+        tot = tot + (double)(dot > 0.0f ? dot : 0.0f);
+    }
+    return (float)tot;
+}
+
+typedef struct { float s; int32_t b; } idx_scored_t;
+
+static int cmp_idx_scored(const void *a, const void *b) {
+    const idx_scored_t *x = (const idx_scored_t *)a, *y = (const idx_scored_t *)b;
+    if (x->s != y->s) return x->s > y->s ? -1 : 1;
+    return (x->b > y->b) - (x->b < y->b);
+}
+
+static int cmp_i32(const void *a, const void *b) {
+    const int32_t x = *(const int32_t *)a, y = *(const int32_t *)b;
+    return (x > y) - (x < y);
+}
+
+int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64_t pos, int k_blocks,
+                       float *scores, int32_t *blocks_out) {
+    const int64_t whole = (pos + 1) / ORC_IDX_R, b_last = pos / ORC_IDX_R;
+    const int tail = b_last >= whole;
+    for (int k = 0; k < k_blocks; k++) blocks_out[k] = -1;
+    idx_scored_t *sc = (idx_scored_t *)malloc(sizeof(idx_scored_t) * (size_t)(whole > 0 ? whole : 1));
+    for (int64_t b = 0; b < whole; b++) {
+        sc[b].s = orc_idx_score(q, n_head, pooled + b * ORC_IDX_KEY);
+        sc[b].b = (int32_t)b;
+        if (scores) scores[b] = sc[b].s;
+    }
+    int64_t n;
+    if (b_last + 1 <= k_blocks) {
+        for (int64_t b = 0; b <= b_last; b++) blocks_out[b] = (int32_t)b;
+        n = b_last + 1;
+    } else {
+        const int need = k_blocks - tail;
+        qsort(sc, (size_t)whole, sizeof(idx_scored_t), cmp_idx_scored);
+        for (int k = 0; k < need; k++) blocks_out[k] = sc[k].b;
+        qsort(blocks_out, (size_t)need, sizeof(int32_t), cmp_i32);
+        if (tail) blocks_out[need] = (int32_t)b_last;
+        n = k_blocks;
+    }
+    free(sc);
+    return n;
+}
+

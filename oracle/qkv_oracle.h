@@ -104,6 +104,41 @@ void orc_attn_q8_0_sparse(const float *Q, int64_t T, int n_head, int n_head_kv, 
                           const int32_t *const *cells, const int64_t *n_cells,
                           const int32_t *q_pos, float scale, float *out, int n_threads);
 
+/*
+ * QSA lightning indexer, decode path (the reference's own selector: src/qwfn_graph.cpp:280-311
+ * qsa_pool_blocks / idx_query, 529-579 qsa_dec_index / qsa_dec_cells; bias and bucket
+ * src/qwfn_engine.cpp:1072-1105).  Key length 128, 4 cells per block.  Every fp32 step has a
+ * fixed order, the one the device kernels use (lane l of a warp owns dims 4l..4l+3; cross-lane
+ * sums are xor butterflies 16,8,4,2,1, emulated here), so pooled keys, scores and kept blocks
+ * must match the device bit for bit.  ggml's own summation orders differ between its CPU and
+ * CUDA backends, so these bits are this build's definition; the semantics are the reference's.
+ */
+#define ORC_IDX_KEY 128
+#define ORC_IDX_R   4
+
+/* cs[b][i] = {cosf(th_i), sinf(th_i)}, th_0 = (float)(4b), th_{i+1} = th_i * powf(base, -2/rope_dim)
+ * (ggml's CPU rope cache: one fp32 multiplication per pair), i < rope_dim/2. */
+void orc_idx_rope_table(int64_t n_blocks, int rope_dim, float freq_base, float *cs);
+
+/* Pooled key of blocks 0..n_blocks-1 from the raw fp16 keys [4*n_blocks][128]:
+ *   x = (((k0 + k1) + k2) + k3) * 0.25;  s = butterfly of ((x0^2 + x1^2) + x2^2) + x3^2 per lane;
+ *   y = (x * (1 / sqrtf(s * (1/128) + eps))) * w;
+ *   rotate pairs (i, i + rope_dim/2): y_i c - y_j s, y_i s + y_j c;  store fp16 (RNE). */
+void orc_idx_pool(const uint16_t *keys, int64_t n_blocks, const float *norm_w, float eps, int rope_dim,
+                  const float *cs, uint16_t *pooled);
+
+/* Score of one pooled key: (float) of the double sum over heads of max(0, butterfly of
+ * ((q0 k0 + q1 k1) + q2 k2) + q3 k3 per lane), q rounded to fp16 first. */
+float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b);
+
+/* Kept blocks for the token at position pos (ascending; returns how many, the rest of
+ * blocks_out is -1): every block 0..pos/4 when there are no more than k_blocks, else the
+ * incomplete tail block (if pos+1 is not a multiple of 4) and the best remaining whole blocks
+ * b < (pos+1)/4 by score (descending, ties by lower index).  scores (nullable) gets the whole
+ * blocks' scores. */
+int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64_t pos, int k_blocks,
+                       float *scores, int32_t *blocks_out);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus

@@ -29,6 +29,7 @@ EXPORTS = [
     "qkv_cache_view_get", "qkv_attn_decode_static", "qkv_device_status", "qkv_launch_count", "qkv_shard_lpt",
     "qkv_store_create", "qkv_store_destroy", "qkv_store_save", "qkv_store_restore_or_reset",
     "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
+    "qkv_indexer_enable", "qkv_idx_append", "qkv_idx_select", "qkv_attn_decode_qsa", "qkv_idx_read",
 ]
 
 
@@ -42,6 +43,12 @@ class QkvConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "n_layer", "n_head", "n_head_kv", "head_dim", "n_ctx", "n_slots", "n_pages", "rec_n_layer",
         "rec_head_dim", "rec_n_head", "conv_channels", "conv_hist", "n_rollback", "select_block")]
+
+
+class QkvIndexerConfig(ctypes.Structure):
+    _fields_ = [("n_head", ctypes.c_int32), ("key_len", ctypes.c_int32), ("ratio", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("rope_dim", ctypes.c_int32), ("rope_freq_base", ctypes.c_float),
+                ("rms_eps", ctypes.c_float)]
 
 
 class QkvCacheView(ctypes.Structure):
@@ -99,6 +106,11 @@ def lib() -> ctypes.CDLL:
         "qkv_store_restore_or_reset": [P, I32, pI32, I32, pI32, P],
         "qkv_store_prefix_split": [P, pI32, I32, I32, I32, pI32], "qkv_store_evict": [P, I32],
         "qkv_store_info": [P, pI32, ctypes.POINTER(SZ)], "qkv_store_entry": [P, I32, pI32, ctypes.POINTER(SZ)],
+        "qkv_indexer_enable": [P, ctypes.POINTER(QkvIndexerConfig), P],
+        "qkv_idx_append": [P, I32, I32, I32, P, I32, P],
+        "qkv_idx_select": [P, I32, pI32, pI32, I32, P, I32, P, P, P, P],
+        "qkv_attn_decode_qsa": [P, I32, pI32, pI32, I32, P, P, I32, F32, P, P],
+        "qkv_idx_read": [P, I32, I32, I32, I32, P, I32, I32, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -387,6 +399,39 @@ class Engine:
     def attn_prefill(self, layer: int, slot: int, pos0: int, Q, Tc: int, scale: float, out, stream=None) -> None:
         self._check(lib().qkv_attn_prefill(self.handle, layer, slot, pos0, _ptr(Q), Tc, scale, _ptr(out),
                                            _stream(stream)))
+
+    # -- QSA lightning indexer ------------------------------------------------------------------
+    def indexer_enable(self, n_head: int = 4, top_k: int = 2048, rope_dim: int = 64, rope_freq_base: float = 1e7,
+                       rms_eps: float = 1e-6, k_norm=None) -> int:
+        """Returns k_blocks (blocks kept per token).  k_norm: numpy float32 [n_layer, 128] or None."""
+        c = QkvIndexerConfig(n_head, 128, 4, top_k, rope_dim, rope_freq_base, rms_eps)
+        w = None
+        if k_norm is not None:
+            import numpy as np
+            self._knorm = np.ascontiguousarray(k_norm, dtype=np.float32)
+            w = self._knorm.ctypes.data
+        self._check(lib().qkv_indexer_enable(self.handle, ctypes.byref(c), w))
+        self.k_blocks = (top_k + 3 + 3) // 4
+        return self.k_blocks
+
+    def idx_append(self, layer: int, slot: int, pos: int, k_raw, n_rows: int | None = None, stream=None) -> None:
+        n = n_rows if n_rows is not None else int(k_raw.shape[0])
+        self._check(lib().qkv_idx_append(self.handle, layer, slot, pos, _ptr(k_raw), n, _stream(stream)))
+
+    def idx_select(self, layer: int, slots, pos0, q_idx, T: int, blocks_out, n_out, scores_out=None,
+                   stream=None) -> None:
+        self._check(lib().qkv_idx_select(self.handle, layer, _i32_array(slots), _i32_array(pos0), len(slots),
+                                          _ptr(q_idx), T, _ptr(blocks_out), _ptr(n_out), _ptr(scores_out),
+                                          _stream(stream)))
+
+    def attn_decode_qsa(self, layer: int, slots, pos0, q_idx, Q, T: int, scale: float, out, stream=None) -> None:
+        self._check(lib().qkv_attn_decode_qsa(self.handle, layer, _i32_array(slots), _i32_array(pos0), len(slots),
+                                               _ptr(q_idx), _ptr(Q), T, scale, _ptr(out), _stream(stream)))
+
+    def idx_read(self, layer: int, slot: int, pos: int = 0, n: int = 0, keys_out=None, b0: int = 0, n_blk: int = 0,
+                 pooled_out=None, stream=None) -> None:
+        self._check(lib().qkv_idx_read(self.handle, layer, slot, pos, n, _ptr(keys_out), b0, n_blk, _ptr(pooled_out),
+                                        _stream(stream)))
 
     # -- snapshots / rollback (engine::snapshot_* surface) -------------------------------------
     def snapshot_save(self, slot: int, stream=None) -> Snapshot:

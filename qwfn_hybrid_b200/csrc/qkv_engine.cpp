@@ -89,6 +89,23 @@ struct qkv_engine {
     int         ring_next = 0;
 
     std::vector<qkv_snapshot *> snaps;
+
+    // QSA lightning indexer (qkv_indexer_enable)
+    bool                   idx_on = false;
+    qkv_indexer_config     icfg{};
+    int32_t                k_blocks = 0;      // blocks kept per token
+    int32_t                idx_max_blk = 0;   // blocks of n_ctx
+    std::vector<uint8_t *> idx_pools;         // per layer, n_pages x IDX_PAGE_BYTES
+    float2   *d_rope  = nullptr;              // [idx_max_blk][rope_dim/2] {cos, sin}
+    float    *d_knorm = nullptr;              // [n_layer][IDX_KEY]
+    // qkv_attn_decode_qsa scratch (grown on demand): scores, kept blocks, dense copies of the
+    // kept cells (dst_pages pages per (sequence, token) entry) and their block table
+    float    *d_iscore = nullptr;
+    int32_t  *d_isel = nullptr, *d_inout = nullptr;
+    int32_t   iscratch_v = 0;
+    uint8_t  *d_vpool = nullptr;
+    int32_t  *d_vbt = nullptr;
+    int32_t   vpool_v = 0, dst_pages = 0;
 };
 
 // ------------------------------------------------------------------------------------ helpers
@@ -250,6 +267,9 @@ static qkv_status reserve(qkv_engine *eng, int32_t slot, int32_t pos, int32_t n,
             for (int l = 0; l < eng->cfg.n_layer && !eng->host_only; l++)
                 cow.push_back(CopyDesc{eng->pools[l] + (int64_t)old * eng->page_bytes,
                                        eng->pools[l] + (int64_t)fresh * eng->page_bytes, eng->page_bytes});
+            for (size_t l = 0; l < eng->idx_pools.size() && !eng->host_only; l++)
+                cow.push_back(CopyDesc{eng->idx_pools[l] + (int64_t)old * IDX_PAGE_BYTES,
+                                       eng->idx_pools[l] + (int64_t)fresh * IDX_PAGE_BYTES, IDX_PAGE_BYTES});
             page_unref(eng, old);
             sl.pages[pi] = fresh;
             sl.dirty = true;
@@ -289,6 +309,15 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_pf_q);
     cudaFree(eng->d_pf_partial);
     cudaFree(eng->d_pf_plan);
+    for (uint8_t *p : eng->idx_pools) cudaFree(p);
+    eng->idx_pools.clear();
+    cudaFree(eng->d_rope);
+    cudaFree(eng->d_knorm);
+    cudaFree(eng->d_iscore);
+    cudaFree(eng->d_isel);
+    cudaFree(eng->d_inout);
+    cudaFree(eng->d_vpool);
+    cudaFree(eng->d_vbt);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
         if (ev) cudaEventDestroy(ev);
@@ -530,14 +559,23 @@ extern "C" qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, i
 // ------------------------------------------------------------------------------------ decode
 // Plan one launch of kernel C for sequences [base, base+ns): every pair (sequence, KV head) is
 // cut into units in proportion to its tiles so that about two CTAs per SM carry equal work.
+// Where kernel C reads from: by default the layer's pool through the engine's block table; the
+// indexer path points it at dense scratch copies of the kept cells instead.
+struct DecodeSrc {
+    uint8_t       *pool;
+    const int32_t *bt;
+    int32_t        max_pages, n_pages;
+};
+
 static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int ns,
                                 const float *Q, int32_t T, float scale, const int32_t *sel, int32_t n_sel,
-                                const float *Knew, const float *Vnew, float *out, cudaStream_t st) {
+                                const float *Knew, const float *Vnew, float *out, cudaStream_t st,
+                                const DecodeSrc *src = nullptr) {
     const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H;
     DecodeParams P;
     memset(&P, 0, sizeof P);
-    P.pool = eng->pools[layer];
-    P.block_table = eng->d_bt;
+    P.pool = src ? src->pool : eng->pools[layer];
+    P.block_table = src ? src->bt : eng->d_bt;
     P.Q = Q;
     P.out = out;
     P.partial = eng->d_partial;
@@ -546,8 +584,8 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.Vnew = Vnew;
     P.status = eng->d_status;
     P.page_bytes = eng->page_bytes;
-    P.n_pages = eng->n_pages;
-    P.max_pages = eng->max_pages;
+    P.n_pages = src ? src->n_pages : eng->n_pages;
+    P.max_pages = src ? src->max_pages : eng->max_pages;
     P.n_head = eng->cfg.n_head;
     P.n_head_kv = H;
     P.G = G;
@@ -691,6 +729,273 @@ extern "C" qkv_status qkv_append_attn_decode(qkv_engine *eng, int32_t layer, con
                                              float scale, float *out, void *stream) {
     if (!K || !V) return eng ? fail(eng, QKV_ERR_INVALID, "fused append: null K or V") : QKV_ERR_INVALID;
     return decode_common(eng, layer, slots, pos0, n_seq, Q, T, scale, nullptr, 0, K, V, out, stream);
+}
+
+// ---------------------------------------------------------------------- QSA lightning indexer
+extern "C" qkv_status qkv_indexer_enable(qkv_engine *eng, const qkv_indexer_config *cfg, const float *k_norm) {
+    if (!eng || !cfg) return QKV_ERR_INVALID;
+    const qkv_indexer_config &c = *cfg;
+    if (eng->idx_on) return fail(eng, QKV_ERR_STATE, "indexer already enabled");
+    if (c.n_head < 1 || c.n_head > IDX_MAX_HEAD || c.key_len != IDX_KEY || c.ratio != IDX_R || c.top_k < 1 ||
+        c.rope_dim < 0 || c.rope_dim % 8 || c.rope_dim > IDX_KEY || !(c.rope_freq_base > 0.f) || !(c.rms_eps >= 0.f))
+        return fail(eng, QKV_ERR_INVALID,
+                    "indexer: n_head %d (1..%d), key_len %d (%d), ratio %d (%d), top_k %d, rope_dim %d (multiple of 8, <= %d)",
+                    c.n_head, IDX_MAX_HEAD, c.key_len, IDX_KEY, c.ratio, IDX_R, c.top_k, c.rope_dim, IDX_KEY);
+    eng->icfg = c;
+    eng->k_blocks = (c.top_k + c.ratio - 1 + c.ratio - 1) / c.ratio;   // ceil(width / ratio), engine.cpp:687
+    eng->idx_max_blk = (eng->cfg.n_ctx + IDX_R - 1) / IDX_R;
+    eng->dst_pages = (eng->k_blocks * IDX_R + PAGE_TOK - 1) / PAGE_TOK;
+    if (eng->host_only) {
+        eng->idx_on = true;
+        return QKV_OK;
+    }
+    qkv_status r = use_device(eng);
+    if (r != QKV_OK) return r;
+    eng->idx_pools.assign(eng->cfg.n_layer, nullptr);
+    for (int l = 0; l < eng->cfg.n_layer && r == QKV_OK; l++) {
+        r = dalloc(eng, eng->idx_pools[l], (size_t)eng->n_pages * IDX_PAGE_BYTES, "indexer pool");
+        if (r == QKV_OK) CK(eng, cudaMemset(eng->idx_pools[l], 0, (size_t)eng->n_pages * IDX_PAGE_BYTES));
+    }
+    // rope table of the block positions p = 4b: theta_0 = p, theta_{i+1} = theta_i * freq_base^(-2/rope_dim)
+    // in fp32, as ggml's CPU rope cache is built (one multiplication per pair)
+    const int half = c.rope_dim / 2;
+    std::vector<float2> tab((size_t)eng->idx_max_blk * std::max(half, 1));
+    const float theta_scale = powf(c.rope_freq_base, -2.0f / (float)std::max(c.rope_dim, 1));
+    for (int32_t b = 0; b < eng->idx_max_blk; b++) {
+        float th = (float)(b * IDX_R);
+        for (int i = 0; i < half; i++) {
+            tab[(size_t)b * half + i] = make_float2(cosf(th), sinf(th));
+            th *= theta_scale;
+        }
+    }
+    std::vector<float> w((size_t)eng->cfg.n_layer * IDX_KEY, 1.0f);
+    if (k_norm) memcpy(w.data(), k_norm, w.size() * sizeof(float));
+    if (r == QKV_OK) r = dalloc(eng, eng->d_rope, tab.size() * sizeof(float2), "indexer rope table");
+    if (r == QKV_OK) r = dalloc(eng, eng->d_knorm, w.size() * sizeof(float), "indexer norm weights");
+    if (r != QKV_OK) return r;
+    CK(eng, cudaMemcpy(eng->d_rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    CK(eng, cudaMemcpy(eng->d_knorm, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice));
+    eng->idx_on = true;
+    return QKV_OK;
+}
+
+static qkv_status idx_check(qkv_engine *eng, int32_t layer) {
+    if (!eng) return QKV_ERR_INVALID;
+    if (!eng->idx_on) return fail(eng, QKV_ERR_STATE, "indexer not enabled (qkv_indexer_enable)");
+    return check_layer(eng, layer);
+}
+
+extern "C" qkv_status qkv_idx_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, const float *k_raw,
+                                     int32_t n_rows, void *stream) {
+    qkv_status r;
+    if ((r = idx_check(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    if (n_rows < 1 || !k_raw || ((uintptr_t)k_raw & 15))
+        return fail(eng, QKV_ERR_INVALID, "idx_append: %d rows, keys %p (16-byte aligned)", n_rows, (const void *)k_raw);
+    const qkv_engine::Slot &sl = eng->slots[slot];
+    if (pos < 0 || pos > sl.n_past || (int64_t)pos + n_rows > eng->cfg.n_ctx)
+        return fail(eng, QKV_ERR_INVALID, "idx_append at %d (+%d): slot %d holds %d, n_ctx %d", pos, n_rows, slot, sl.n_past,
+                    eng->cfg.n_ctx);
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if ((r = reserve(eng, slot, pos, n_rows, st)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    IdxAppendParams p;
+    p.pool = eng->idx_pools[layer];
+    p.bt = eng->d_bt + (size_t)slot * eng->max_pages;
+    p.k_raw = k_raw;
+    p.norm_w = eng->d_knorm + (size_t)layer * IDX_KEY;
+    p.rope = eng->d_rope;
+    p.status = eng->d_status;
+    p.n_pages = eng->n_pages;
+    p.max_pages = eng->max_pages;
+    p.pos = pos;
+    p.n_rows = n_rows;
+    p.rope_half = eng->icfg.rope_dim / 2;
+    p.eps = eng->icfg.rms_eps;
+    CK(eng, launch_idx_append(p, st));
+    return QKV_OK;
+}
+
+// Validate (sequence, token) entries: every position already appended to its slot.
+static qkv_status idx_entries(qkv_engine *eng, const int32_t *slots, const int32_t *pos0, int32_t n_seq, int32_t T,
+                              const void *q) {
+    if (!slots || !pos0 || !q || n_seq < 1 || T < 1 || T > 4)
+        return fail(eng, QKV_ERR_INVALID, "indexer: n_seq %d, T %d (1..4), null pointer", n_seq, T);
+    for (int i = 0; i < n_seq; i++) {
+        qkv_status r = check_slot(eng, slots[i]);
+        if (r != QKV_OK) return r;
+        if (pos0[i] < 0 || pos0[i] + T > eng->slots[slots[i]].n_past)
+            return fail(eng, QKV_ERR_INVALID, "indexer: sequence %d positions %d..%d but slot %d holds %d", i, pos0[i],
+                        pos0[i] + T - 1, slots[i], eng->slots[slots[i]].n_past);
+    }
+    return QKV_OK;
+}
+
+// Scores + top-k for entries [v0, v0 + nv) of n_seq x T (entry v = i * T + t).
+static qkv_status idx_select_chunk(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int32_t T,
+                                   int32_t v0, int32_t nv, const float *q_idx, int32_t *blocks, int32_t *n_out,
+                                   float *scores, int32_t score_stride, cudaStream_t st) {
+    IdxSelectParams p;
+    memset(&p, 0, sizeof p);
+    p.pool = eng->idx_pools[layer];
+    p.bt = eng->d_bt;
+    p.q = q_idx + (size_t)v0 * eng->icfg.n_head * IDX_KEY;
+    p.scores = scores;
+    p.blocks = blocks;
+    p.n_out = n_out;
+    p.status = eng->d_status;
+    p.n_v = nv;
+    p.n_head = eng->icfg.n_head;
+    p.k_blocks = eng->k_blocks;
+    p.score_stride = score_stride;
+    p.n_pages = eng->n_pages;
+    p.max_pages = eng->max_pages;
+    int32_t max_whole = 0;
+    for (int k = 0; k < nv; k++) {
+        const int v = v0 + k;
+        p.v_slot[k] = slots[v / T];
+        p.v_pos[k] = pos0[v / T] + v % T;
+        max_whole = std::max(max_whole, (p.v_pos[k] + 1) / IDX_R);
+    }
+    CK(eng, launch_idx_select(p, max_whole, st));
+    return QKV_OK;
+}
+
+static qkv_status idx_scratch(qkv_engine *eng, int32_t nv) {
+    if (nv <= eng->iscratch_v) return QKV_OK;
+    cudaFree(eng->d_iscore);
+    cudaFree(eng->d_isel);
+    cudaFree(eng->d_inout);
+    eng->d_iscore = nullptr;
+    eng->d_isel = eng->d_inout = nullptr;
+    eng->iscratch_v = 0;
+    qkv_status r = dalloc(eng, eng->d_iscore, (size_t)nv * eng->idx_max_blk * sizeof(float), "indexer scores");
+    if (r == QKV_OK) r = dalloc(eng, eng->d_isel, (size_t)nv * eng->k_blocks * sizeof(int32_t), "indexer blocks");
+    if (r == QKV_OK) r = dalloc(eng, eng->d_inout, (size_t)nv * sizeof(int32_t), "indexer counts");
+    if (r == QKV_OK) eng->iscratch_v = nv;
+    return r;
+}
+
+extern "C" qkv_status qkv_idx_select(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                     int32_t n_seq, const float *q_idx, int32_t T, int32_t *blocks_out, int32_t *n_out_out,
+                                     float *scores_out, void *stream) {
+    qkv_status r;
+    if ((r = idx_check(eng, layer)) != QKV_OK || (r = idx_entries(eng, slots, pos0, n_seq, T, q_idx)) != QKV_OK) return r;
+    if (!blocks_out || !n_out_out) return fail(eng, QKV_ERR_INVALID, "idx_select: null output");
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    const int32_t n_v = n_seq * T;
+    if (!scores_out && (r = idx_scratch(eng, std::min(n_v, IDX_MAX_VSEQ))) != QKV_OK) return r;
+    for (int32_t v0 = 0; v0 < n_v; v0 += IDX_MAX_VSEQ) {
+        const int32_t nv = std::min(IDX_MAX_VSEQ, n_v - v0);
+        float *sc = scores_out ? scores_out + (size_t)v0 * eng->idx_max_blk : eng->d_iscore;
+        if ((r = idx_select_chunk(eng, layer, slots, pos0, T, v0, nv, q_idx, blocks_out + (size_t)v0 * eng->k_blocks,
+                                  n_out_out + v0, sc, eng->idx_max_blk, st)) != QKV_OK)
+            return r;
+    }
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
+                                          int32_t n_seq, const float *q_idx, const float *Q, int32_t T, float scale,
+                                          float *out, void *stream) {
+    qkv_status r;
+    if ((r = idx_check(eng, layer)) != QKV_OK || (r = idx_entries(eng, slots, pos0, n_seq, T, q_idx)) != QKV_OK) return r;
+    if (!Q || !out) return fail(eng, QKV_ERR_INVALID, "decode_qsa: null Q or out");
+    if (eng->cfg.n_head / eng->cfg.n_head_kv > decode_max_nq())
+        return fail(eng, QKV_ERR_UNSUPPORTED, "decode_qsa: %d query heads per KV head", eng->cfg.n_head / eng->cfg.n_head_kv);
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    // entries go through in chunks of MAX_SEQ (one decode launch each), reusing the scratch
+    if ((r = idx_scratch(eng, MAX_SEQ)) != QKV_OK) return r;
+    if (eng->vpool_v < MAX_SEQ) {
+        const int32_t pages = MAX_SEQ * eng->dst_pages;
+        if ((r = dalloc(eng, eng->d_vpool, (size_t)pages * eng->page_bytes, "indexer gather pages")) != QKV_OK) return r;
+        if ((r = dalloc(eng, eng->d_vbt, (size_t)pages * sizeof(int32_t), "indexer gather table")) != QKV_OK) return r;
+        std::vector<int32_t> ids(pages);
+        for (int32_t i = 0; i < pages; i++) ids[i] = i;
+        CK(eng, cudaMemset(eng->d_vpool, 0, (size_t)pages * eng->page_bytes));
+        CK(eng, cudaMemcpy(eng->d_vbt, ids.data(), ids.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+        eng->vpool_v = MAX_SEQ;
+    }
+    const int32_t n_v = n_seq * T, K = eng->k_blocks;
+    const size_t qrow = (size_t)eng->cfg.n_head * HD;
+    for (int32_t v0 = 0; v0 < n_v; v0 += MAX_SEQ) {
+        const int32_t nv = std::min(MAX_SEQ, n_v - v0);
+        if ((r = idx_select_chunk(eng, layer, slots, pos0, T, v0, nv, q_idx, eng->d_isel, eng->d_inout, eng->d_iscore,
+                                  eng->idx_max_blk, st)) != QKV_OK)
+            return r;
+        IdxGatherParams g;
+        memset(&g, 0, sizeof g);
+        g.pool = eng->pools[layer];
+        g.bt = eng->d_bt;
+        g.dst = eng->d_vpool;
+        g.dst_bt = eng->d_vbt;
+        g.blocks = eng->d_isel;
+        g.n_out = eng->d_inout;
+        g.status = eng->d_status;
+        g.page_bytes = eng->page_bytes;
+        g.n_v = nv;
+        g.k_blocks = K;
+        g.n_head_kv = eng->cfg.n_head_kv;
+        g.n_pages = eng->n_pages;
+        g.max_pages = eng->max_pages;
+        g.dst_pages = eng->dst_pages;
+        int32_t vslot[MAX_SEQ], vpos[MAX_SEQ];
+        for (int k = 0; k < nv; k++) {
+            const int v = v0 + k;
+            const int32_t p = pos0[v / T] + v % T, b_last = p / IDX_R, whole = (p + 1) / IDX_R;
+            const int32_t tail = b_last >= whole ? 1 : 0;
+            g.v_slot[k] = slots[v / T];
+            g.v_pos[k] = p;
+            // the dense copy: every block (cells 0 .. p), or k_blocks blocks with the tail's
+            // cells up to p last
+            const int32_t len = b_last + 1 <= K ? p + 1 : IDX_R * (K - tail) + (tail ? p - IDX_R * b_last + 1 : 0);
+            vslot[k] = k;
+            vpos[k] = len - 1;
+        }
+        CK(eng, launch_idx_gather(g, st));
+        const DecodeSrc src{eng->d_vpool, eng->d_vbt, eng->dst_pages, MAX_SEQ * eng->dst_pages};
+        if ((r = decode_launch(eng, layer, vslot, vpos, nv, Q + (size_t)v0 * qrow, 1, scale, nullptr, 0, nullptr, nullptr,
+                               out + (size_t)v0 * qrow, st, &src)) != QKV_OK)
+            return r;
+    }
+    return QKV_OK;
+}
+
+extern "C" qkv_status qkv_idx_read(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, int32_t n,
+                                   uint16_t *keys_out, int32_t b0, int32_t n_blk, uint16_t *pooled_out, void *stream) {
+    qkv_status r;
+    if ((r = idx_check(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    const qkv_engine::Slot &sl = eng->slots[slot];
+    const int64_t have = (int64_t)sl.pages.size() * PAGE_TOK;
+    if ((keys_out && (pos < 0 || n < 0 || pos + (int64_t)n > have)) ||
+        (pooled_out && (b0 < 0 || n_blk < 0 || (int64_t)(b0 + n_blk) * IDX_R > have)))
+        return fail(eng, QKV_ERR_INVALID, "idx_read: positions %d+%d / blocks %d+%d outside the slot's %lld pages", pos, n, b0,
+                    n_blk, (long long)sl.pages.size());
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    const uint8_t *pool = eng->idx_pools[layer];
+    for (int32_t c = pos; keys_out && c < pos + n;) {   // runs within one page
+        const int32_t run = std::min(pos + n - c, PAGE_TOK - (c & (PAGE_TOK - 1)));
+        const uint8_t *src = pool + (int64_t)sl.pages[c / PAGE_TOK] * IDX_PAGE_BYTES + (int64_t)(c & (PAGE_TOK - 1)) * IDX_KEY * 2;
+        CK(eng, cudaMemcpyAsync(keys_out + (size_t)(c - pos) * IDX_KEY, src, (size_t)run * IDX_KEY * 2, cudaMemcpyDeviceToDevice, st));
+        c += run;
+    }
+    for (int32_t b = b0; pooled_out && b < b0 + n_blk;) {
+        const int32_t run = std::min(b0 + n_blk - b, IDX_BPP - (b & (IDX_BPP - 1)));
+        const uint8_t *src = pool + (int64_t)sl.pages[b / IDX_BPP] * IDX_PAGE_BYTES + IDX_RAW_BYTES +
+                             (int64_t)(b & (IDX_BPP - 1)) * IDX_KEY * 2;
+        CK(eng, cudaMemcpyAsync(pooled_out + (size_t)(b - b0) * IDX_KEY, src, (size_t)run * IDX_KEY * 2, cudaMemcpyDeviceToDevice, st));
+        b += run;
+    }
+    return QKV_OK;
 }
 
 // --------------------------------------------------------------------------------- selection

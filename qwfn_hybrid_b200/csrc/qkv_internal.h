@@ -101,6 +101,60 @@ struct SelectParams {
 };
 cudaError_t launch_select(const SelectParams &p, cudaStream_t st);
 
+// ---- QSA lightning indexer --------------------------------------------------------------------
+// Per attention layer an indexer pool parallel to the KV pool (same page ids).  An indexer page
+// holds the raw keys of its 256 positions, fp16 [256][IDX_KEY], then the pooled keys of its 64
+// blocks of IDX_R cells, fp16 [64][IDX_KEY].
+constexpr int IDX_KEY        = 128;
+constexpr int IDX_R          = 4;
+constexpr int IDX_BPP        = PAGE_TOK / IDX_R;
+constexpr int IDX_RAW_BYTES  = PAGE_TOK * IDX_KEY * 2;
+constexpr int IDX_PAGE_BYTES = IDX_RAW_BYTES + IDX_BPP * IDX_KEY * 2;
+constexpr int IDX_MAX_HEAD   = 8;
+constexpr int IDX_MAX_VSEQ   = 256;   // (sequence, token) pairs per selection launch
+
+struct IdxAppendParams {
+    uint8_t       *pool;          // layer indexer pool
+    const int32_t *bt;            // block-table row of the slot
+    const float   *k_raw;         // [n_rows][IDX_KEY]
+    const float   *norm_w;        // [IDX_KEY]
+    const float2  *rope;          // [block][rope_half] {cos, sin}
+    int32_t       *status;
+    int32_t n_pages, max_pages, pos, n_rows, rope_half;
+    float   eps;
+};
+cudaError_t launch_idx_append(const IdxAppendParams &p, cudaStream_t st);
+
+// One entry per (sequence, token): v = i * T + t.
+struct IdxSelectParams {
+    const uint8_t *pool;          // layer indexer pool
+    const int32_t *bt;            // engine block table [n_slots][max_pages]
+    const float   *q;             // [n_v][n_head][IDX_KEY]
+    float         *scores;        // [n_v][score_stride]
+    int32_t       *blocks;        // [n_v][k_blocks]
+    int32_t       *n_out;         // [n_v]
+    int32_t       *status;
+    int32_t n_v, n_head, k_blocks, score_stride, n_pages, max_pages;
+    int32_t v_slot[IDX_MAX_VSEQ], v_pos[IDX_MAX_VSEQ];
+};
+cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaStream_t st);
+
+// Copies the kept cells of entry v (blocks[v][0 .. n_out[v]), cells <= v_pos[v]) from the KV pool
+// into the entry's scratch pages (dst_bt row v), in block order, as a dense sequence for kernel C.
+struct IdxGatherParams {
+    const uint8_t *pool;          // layer KV pool
+    const int32_t *bt;            // engine block table
+    uint8_t       *dst;           // scratch pool
+    const int32_t *dst_bt;        // [n_v][dst_pages]
+    const int32_t *blocks;
+    const int32_t *n_out;
+    int32_t       *status;
+    int64_t page_bytes;
+    int32_t n_v, k_blocks, n_head_kv, n_pages, max_pages, dst_pages;
+    int32_t v_slot[IDX_MAX_VSEQ], v_pos[IDX_MAX_VSEQ];
+};
+cudaError_t launch_idx_gather(const IdxGatherParams &p, cudaStream_t st);
+
 // ---- kernel C -----------------------------------------------------------------------------------
 constexpr int MAX_PAIRS = MAX_SEQ * 8;
 struct DecodeParams {

@@ -65,6 +65,10 @@ typedef struct qkv_config {
     int32_t conv_hist;      /* d_conv - 1 (3)                                                    */
     int32_t n_rollback;     /* rollback snapshots of the recurrent state kept per slot (0..4)    */
     int32_t select_block;   /* tokens per selection block (64), 0 = no block summaries           */
+    int32_t attn_interval;  /* host-blob layer order: absolute layer il is attention iff           *
+                             * (il+1) % attn_interval == 0 (hparams::is_attn_layer, 4 in the model; *
+                             * needs n_layer * attn_interval == n_layer + rec_n_layer); 0 = all    *
+                             * attention layers first, then the recurrent ones                     */
 } qkv_config;
 
 /* ------------------------------------------------------------------ engine / state ------ */
@@ -257,9 +261,12 @@ qkv_status qkv_snapshot_restore_many(qkv_engine *eng, const qkv_snapshot *snap, 
                                      const int32_t *n_keep, int32_t n, void *stream);
 void qkv_snapshot_release(qkv_engine *eng, qkv_snapshot *snap);
 qkv_status qkv_snapshot_info(const qkv_snapshot *snap, int32_t *n_past, size_t *host_bytes);
-/* Host blobs in the reference's snapshot_parts order (src/qwfn_engine.cpp:988-999): for each
- * attention layer the first n_past K rows then V rows (ggml q8_0 layout), then for each
- * recurrent layer its state then its conv history (F32).  dst/src are host memory. */
+/* Host blobs in the reference's snapshot_parts order (src/qwfn_engine.cpp:987-998): layer by
+ * layer (absolute order when attn_interval is set, else attention layers first), an attention
+ * layer contributes its first n_past K rows, then V rows (ggml q8_0 layout), then -- with the
+ * indexer on -- its n_past raw indexer keys (fp16 [n_past][128]); a recurrent layer its state
+ * then its conv history (F32).  The PLE conv state that ends the reference's blob is not held by
+ * this engine.  Importing re-pools the indexer's whole blocks.  dst/src are host memory. */
 qkv_status qkv_snapshot_to_host(qkv_engine *eng, const qkv_snapshot *snap, void *dst, size_t bytes,
                                 void *stream);
 qkv_status qkv_snapshot_from_host(qkv_engine *eng, const void *src, size_t bytes, int32_t n_past,

@@ -81,8 +81,12 @@ public:
             err = "qkv::state::init: the config's layer counts do not match the layer map";
             return false;
         }
+        qkv_config c = cfg;   // host blobs in the model's layer order unless the caller chose one
+        if (c.attn_interval == 0 && c.rec_n_layer > 0 &&
+            (int64_t)c.n_layer * map.full_attention_interval == (int64_t)c.n_layer + c.rec_n_layer)
+            c.attn_interval = (int32_t)map.full_attention_interval;
         qkv_engine *e = nullptr;
-        qkv_status st = qkv_create(&cfg, device, &e);
+        qkv_status st = qkv_create(&c, device, &e);
         if (st != QKV_OK) {
             err = std::string("qkv_create: ") + qkv_status_string(st);
             return false;

@@ -42,7 +42,8 @@ class QkvError(RuntimeError):
 class QkvConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "n_layer", "n_head", "n_head_kv", "head_dim", "n_ctx", "n_slots", "n_pages", "rec_n_layer",
-        "rec_head_dim", "rec_n_head", "conv_channels", "conv_hist", "n_rollback", "select_block")]
+        "rec_head_dim", "rec_n_head", "conv_channels", "conv_hist", "n_rollback", "select_block",
+        "attn_interval")]
 
 
 class QkvIndexerConfig(ctypes.Structure):
@@ -265,9 +266,10 @@ class Engine:
     def __init__(self, *, n_layer: int, n_head: int, n_head_kv: int, n_ctx: int, n_slots: int, head_dim: int = 256,
                  n_pages: int = 0, rec_n_layer: int = 0, rec_head_dim: int = 128, rec_n_head: int = 32,
                  conv_channels: int = 8192, conv_hist: int = 3, n_rollback: int = 0, select_block: int = 0,
-                 device: int = 0):
+                 attn_interval: int = 0, device: int = 0):
         self.cfg = QkvConfig(n_layer, n_head, n_head_kv, head_dim, n_ctx, n_slots, n_pages, rec_n_layer,
-                             rec_head_dim, rec_n_head, conv_channels, conv_hist, n_rollback, select_block)
+                             rec_head_dim, rec_n_head, conv_channels, conv_hist, n_rollback, select_block,
+                             attn_interval)
         self.device = device
         h = ctypes.c_void_p()
         st = lib().qkv_create(ctypes.byref(self.cfg), device, ctypes.byref(h))

@@ -343,7 +343,8 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
     const qkv_config &c = *cfg;
     if (c.n_layer < 1 || c.n_head < 1 || c.n_head_kv < 1 || c.n_head % c.n_head_kv || c.head_dim != HD ||
         c.n_ctx < 1 || c.n_slots < 1 || c.n_pages < 0 || c.rec_n_layer < 0 || c.n_rollback < 0 || c.n_rollback > 4 ||
-        (c.select_block != 0 && c.select_block != TILE_TOK) || c.n_head_kv > 8 || c.n_head / c.n_head_kv > 16)
+        (c.select_block != 0 && c.select_block != TILE_TOK) || c.n_head_kv > 8 || c.n_head / c.n_head_kv > 16 ||
+        c.attn_interval < 0 || (c.attn_interval > 0 && (int64_t)c.n_layer * c.attn_interval != c.n_layer + c.rec_n_layer))
         return QKV_ERR_INVALID;
     if (c.rec_n_layer > 0 && (c.rec_head_dim < 1 || c.rec_n_head < 1 || c.conv_channels < 1 || c.conv_hist < 1))
         return QKV_ERR_INVALID;
@@ -1418,8 +1419,38 @@ extern "C" qkv_status qkv_snapshot_info(const qkv_snapshot *snap, int32_t *n_pas
     if (n_past) *n_past = snap->n_past;
     if (host_bytes)
         *host_bytes = (size_t)eng->cfg.n_layer * 2 * snap->n_past * eng->cfg.n_head_kv * ROW_Q8 +
+                      (eng->idx_on ? (size_t)eng->cfg.n_layer * snap->n_past * IDX_KEY * 2 : 0) +
                       (size_t)eng->cfg.rec_n_layer * ((size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4 +
                                                       (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4);
+    return QKV_OK;
+}
+
+// Layer order of a host blob: {attention?, index} per absolute layer (snapshot_parts walks the
+// model's layers in order), or attention layers first when no interval is configured.
+static std::vector<std::pair<bool, int>> blob_layers(const qkv_engine *eng) {
+    std::vector<std::pair<bool, int>> o;
+    const int A = eng->cfg.n_layer, R = eng->cfg.rec_n_layer, I = eng->cfg.attn_interval;
+    if (I > 0) {
+        for (int il = 0; il < A + R; il++)
+            o.push_back((il + 1) % I == 0 ? std::make_pair(true, il / I) : std::make_pair(false, il - (il + 1) / I));
+    } else {
+        for (int a = 0; a < A; a++) o.push_back({true, a});
+        for (int r = 0; r < R; r++) o.push_back({false, r});
+    }
+    return o;
+}
+
+// Raw indexer keys of positions 0 .. n-1 between the pages of `pages` and host memory, one copy
+// per page run.
+static qkv_status idx_rows_copy(qkv_engine *eng, int layer, const std::vector<int32_t> &pages, int32_t n, uint8_t *host,
+                                bool to_host, cudaStream_t st) {
+    for (int32_t c = 0; c < n; c += PAGE_TOK) {
+        const int32_t run = std::min(PAGE_TOK, n - c);
+        uint8_t *dev = eng->idx_pools[layer] + (int64_t)pages[c / PAGE_TOK] * IDX_PAGE_BYTES;
+        uint8_t *h = host + (size_t)c * IDX_KEY * 2;
+        CK(eng, cudaMemcpyAsync(to_host ? (void *)h : (void *)dev, to_host ? (const void *)dev : (const void *)h,
+                                (size_t)run * IDX_KEY * 2, to_host ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice, st));
+    }
     return QKV_OK;
 }
 
@@ -1451,21 +1482,27 @@ extern "C" qkv_status qkv_snapshot_to_host(qkv_engine *eng, const qkv_snapshot *
         return s;
     };
     if ((r = upload_i32(eng, snap->pages, d_pages, st)) != QKV_OK) return done(r);
-    for (int l = 0; l < eng->cfg.n_layer && snap->n_past > 0; l++) {
-        if (launch_read_rows(pool_ref(eng, l, d_pages), nullptr, 0, snap->n_past, stage, stage + rows, st) != cudaSuccess ||
-            cudaMemcpyAsync(out, stage, 2 * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess)
-            return done(fail(eng, QKV_ERR_CUDA, "snapshot export of layer %d: %s", l, cudaGetErrorString(cudaGetLastError())));
-        out += 2 * rows;
-    }
     const size_t rs = (size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4;
     const size_t cv = (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4;
-    for (int l = 0; l < eng->cfg.rec_n_layer; l++) {
-        const uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
-        if (cudaMemcpyAsync(out, base, rs, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-            cudaMemcpyAsync(out + rs, base + eng->rs_bytes, cv, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-            return done(fail(eng, QKV_ERR_CUDA, "snapshot export of recurrent layer %d", l));
-        out += rs + cv;
+    for (const auto &[attn, l] : blob_layers(eng)) {
+        if (attn) {
+            if (snap->n_past == 0) continue;
+            if (launch_read_rows(pool_ref(eng, l, d_pages), nullptr, 0, snap->n_past, stage, stage + rows, st) != cudaSuccess ||
+                cudaMemcpyAsync(out, stage, 2 * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess)
+                return done(fail(eng, QKV_ERR_CUDA, "snapshot export of layer %d: %s", l, cudaGetErrorString(cudaGetLastError())));
+            out += 2 * rows;
+            if (eng->idx_on) {
+                if ((r = idx_rows_copy(eng, l, snap->pages, snap->n_past, out, true, st)) != QKV_OK) return done(r);
+                out += (size_t)snap->n_past * IDX_KEY * 2;
+            }
+        } else {
+            const uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
+            if (cudaMemcpyAsync(out, base, rs, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                cudaMemcpyAsync(out + rs, base + eng->rs_bytes, cv, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                return done(fail(eng, QKV_ERR_CUDA, "snapshot export of recurrent layer %d", l));
+            out += rs + cv;
+        }
     }
     return done(QKV_OK);
 }
@@ -1514,21 +1551,41 @@ extern "C" qkv_status qkv_snapshot_from_host(qkv_engine *eng, const void *src, s
     }
     if ((r = upload_i32(eng, snap->pages, d_pages, st)) != QKV_OK) return undo(r);
     const uint8_t *in = static_cast<const uint8_t *>(src);
-    for (int l = 0; l < eng->cfg.n_layer && n_past > 0; l++) {
-        if (cudaMemcpyAsync(stage, in, 2 * rows, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            launch_write_rows(pool_ref(eng, l, d_pages), 0, n_past, stage, stage + rows, st) != cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess)
-            return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of layer %d", l));
-        in += 2 * rows;
-    }
     const size_t rs = (size_t)eng->cfg.rec_head_dim * eng->cfg.rec_head_dim * eng->cfg.rec_n_head * 4;
     const size_t cv = (size_t)eng->cfg.conv_hist * eng->cfg.conv_channels * 4;
-    for (int l = 0; l < eng->cfg.rec_n_layer; l++) {
-        uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
-        if (cudaMemcpyAsync(base, in, rs, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(base + eng->rs_bytes, in + rs, cv, cudaMemcpyHostToDevice, st) != cudaSuccess)
-            return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of recurrent layer %d", l));
-        in += rs + cv;
+    for (const auto &[attn, l] : blob_layers(eng)) {
+        if (attn) {
+            if (n_past == 0) continue;
+            if (cudaMemcpyAsync(stage, in, 2 * rows, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                launch_write_rows(pool_ref(eng, l, d_pages), 0, n_past, stage, stage + rows, st) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess)
+                return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of layer %d", l));
+            in += 2 * rows;
+            if (eng->idx_on) {   // raw keys, then the whole blocks pooled again
+                if ((r = idx_rows_copy(eng, l, snap->pages, n_past, const_cast<uint8_t *>(in), false, st)) != QKV_OK)
+                    return undo(r);
+                IdxAppendParams p;
+                memset(&p, 0, sizeof p);
+                p.pool = eng->idx_pools[l];
+                p.bt = d_pages;
+                p.norm_w = eng->d_knorm + (size_t)l * IDX_KEY;
+                p.rope = eng->d_rope;
+                p.status = eng->d_status;
+                p.n_pages = eng->n_pages;
+                p.max_pages = np;
+                p.rope_half = eng->icfg.rope_dim / 2;
+                p.eps = eng->icfg.rms_eps;
+                if (launch_idx_pool(p, 0, n_past / IDX_R, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+                    return undo(fail(eng, QKV_ERR_CUDA, "snapshot import: pooling indexer keys of layer %d", l));
+                in += (size_t)n_past * IDX_KEY * 2;
+            }
+        } else {
+            uint8_t *base = snap->rec + (size_t)l * eng->rec_layer_bytes;
+            if (cudaMemcpyAsync(base, in, rs, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaMemcpyAsync(base + eng->rs_bytes, in + rs, cv, cudaMemcpyHostToDevice, st) != cudaSuccess)
+                return undo(fail(eng, QKV_ERR_CUDA, "snapshot import of recurrent layer %d", l));
+            in += rs + cv;
+        }
     }
     cudaStreamSynchronize(st);
     cudaFree(stage);

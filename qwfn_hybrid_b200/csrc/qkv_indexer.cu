@@ -130,6 +130,17 @@ cudaError_t launch_idx_append(const IdxAppendParams &p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// Pool blocks b_lo .. b_lo+n_blk-1 from the raw keys already in the pages (a snapshot import).
+cudaError_t launch_idx_pool(const IdxAppendParams &p, int32_t b_lo, int32_t n_blk, cudaStream_t st) {
+    if (n_blk <= 0) return cudaSuccess;
+    IdxAppendParams q = p;
+    q.n_rows = 0;
+    q.pos = 0x7fffffff;   // every member from the cache
+    k_idx_append<<<(n_blk + 7) / 8, 256, 0, st>>>(q, b_lo, n_blk);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------- scores
 // score[v][b] = (float)(((0.0 + r_0) + r_1) + ... )  in double, r_h = max(0, dot_h), dot_h the
 // butterfly sum over lanes of ((q0*k0 + q1*k1) + q2*k2) + q3*k3 with q = fp16(q_idx) (ggml's

@@ -124,6 +124,7 @@ struct IdxAppendParams {
     float   eps;
 };
 cudaError_t launch_idx_append(const IdxAppendParams &p, cudaStream_t st);
+cudaError_t launch_idx_pool(const IdxAppendParams &p, int32_t b_lo, int32_t n_blk, cudaStream_t st);
 
 // One entry per (sequence, token): v = i * T + t.
 struct IdxSelectParams {

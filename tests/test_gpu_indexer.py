@@ -168,3 +168,49 @@ def test_copy_on_write_keeps_snapshot_keys(cuda, qkvlib, oracle):
     np.testing.assert_array_equal(p1, oracle.idx_pool(k1, (n + 4) // 4, w[1], EPS, ROPE_DIM, BASE))
     snap.release()
     assert eng.device_status() == 0
+
+
+def test_host_blob_order_and_indexer_rows(cuda, qkvlib, oracle):
+    """snapshot_parts order (src/qwfn_engine.cpp:987-998): layer by layer in the model's order, an
+    attention layer's K rows, V rows and indexer rows, a recurrent layer's state and conv; import
+    re-pools the indexer's whole blocks."""
+    import torch
+    from test_gpu_snapshot import rec_state, set_rec_state
+    rec = dict(rec_n_layer=6, rec_head_dim=16, rec_n_head=2, conv_channels=32, conv_hist=3)
+    eng, w = idx_engine(qkvlib, n_layer=2, n_ctx=4096, attn_interval=4, **rec)
+    eng.seq_alloc(0)
+    eng.seq_alloc(1)
+    n = 530
+    kr = [fill(eng, l, 0, n, 500 + 10 * l)[2] for l in range(2)]
+    state = set_rec_state(eng, 0, seed=9)
+    snap = eng.snapshot_save(0)
+    blob = bytes(eng.snapshot_to_host(snap))
+    rows = n * 2 * 272
+    off = 0
+    for il in range(8):
+        if (il + 1) % 4 == 0:
+            a = il // 4
+            kq, vq = read_rows(eng, a, 0, 0, n)
+            assert blob[off:off + rows] == kq.tobytes(); off += rows
+            assert blob[off:off + rows] == vq.tobytes(); off += rows
+            assert blob[off:off + n * 256] == kr[a].astype(np.float16).tobytes(); off += n * 256
+        else:
+            r = il - (il + 1) // 4
+            for kind in (0, 1):
+                part = state[2 * r + kind].tobytes()
+                assert blob[off:off + len(part)] == part, (il, kind); off += len(part)
+    assert off == len(blob) == snap.info()[1]
+    snap2 = eng.snapshot_from_host(blob, n)
+    eng.snapshot_load(snap2, 1)
+    torch.cuda.synchronize()
+    for a in range(2):
+        k1, p1 = read_idx(eng, a, 1, n, n // 4)
+        k0, p0 = read_idx(eng, a, 0, n, n // 4)
+        np.testing.assert_array_equal(k1, k0)
+        np.testing.assert_array_equal(p1, p0)
+        np.testing.assert_array_equal(p1, oracle.idx_pool(k1, n // 4, w[a], EPS, ROPE_DIM, BASE))
+    for x, y in zip(rec_state(eng, 1), state):
+        np.testing.assert_array_equal(x, y)
+    snap.release()
+    snap2.release()
+    assert eng.device_status() == 0

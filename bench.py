@@ -46,9 +46,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5", "qsa"], default="cfg2",
                     help="cfg2 (default, the headline line): BASELINE configs[1]; cfg3: configs[2] chunked "
-                         "prefill; cfg5: configs[4]")
+                         "prefill; cfg5: configs[4]; qsa: configs[3]'s context and tokens through the model's own "
+                         "lightning indexer (select + gather + sparse attention)")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
@@ -627,6 +628,147 @@ def run_cfg3(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+QSA_CTX, QSA_LAYERS = 73728, 1
+
+
+def qsa_inputs(r, n: int):
+    """Indexer raw keys with a per-block offset (N(0,1) plus an offset of variance 2 drawn per
+    4-cell block), so that blocks differ in relevance as configs[3]'s K does per 64-token block."""
+    import numpy as np
+    kr = r.standard_normal((n, 128), dtype=np.float32)
+    kr += np.repeat(r.standard_normal(((n + 3) // 4, 128), dtype=np.float32) * np.float32(np.sqrt(2.0)), 4, axis=0)[:n]
+    return kr
+
+
+def cpu_qsa_baseline(steps: int = 2) -> dict:
+    """The oracle's indexer + sparse attention for the same step on the host's cores."""
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+    threads = O.max_threads()
+    r = np.random.default_rng(33)
+    n = QSA_CTX
+    K = O.quantize_rows(r.standard_normal((n, N_HEAD_KV * HD), dtype=np.float32))
+    V = O.quantize_rows(r.standard_normal((n, N_HEAD_KV * HD), dtype=np.float32))
+    keys16 = qsa_inputs(r, n).astype(np.float16).view(np.uint16)
+    w = np.ones(128, np.float32)
+    t0 = time.perf_counter()
+    pooled = O.idx_pool(keys16, n // 4, w, 1e-6, 64, 1e7)      # maintained incrementally on the GPU
+    t_pool = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for t in range(T):
+            pos = n - T + t
+            q = r.standard_normal((4, 128), dtype=np.float32)
+            kept, _ = O.idx_select(q, pooled, pos, 513)
+            cells = (4 * kept[:, None] + np.arange(4)[None, :]).reshape(-1)
+            cells = cells[cells <= pos].astype(np.int32)
+            Qt = r.standard_normal((1, N_HEAD, HD), dtype=np.float32)
+            O.attn(Qt, K, V, [pos], N_HEAD_KV, SCALE, cells=cells, threads=threads)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} steps of 3 tokens at ctx {n}: score all whole blocks, top-513, attention over the "
+                      f"kept cells (oracle/qkv_oracle.c, {threads} threads); pooling all {n // 4} blocks once took "
+                      f"{t_pool * 1e3:.0f} ms and is not counted"}
+
+
+def run_qsa(args) -> None:
+    """configs[3]'s context (73728) and 3 MTP tokens, decoded through the model's own selector:
+    each step appends the 3 tokens' K/V rows and indexer keys, then qkv_attn_decode_qsa scores
+    every whole 4-cell block, keeps 513 per token (2052 cells), gathers them and attends."""
+    import numpy as np
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import qwfn_hybrid_b200 as Q
+    steps, warm = args.steps, max(args.warmup, 3)
+    total = warm + steps
+    n0 = QSA_CTX - T * (total + 1)
+    eng = Q.Engine(n_layer=QSA_LAYERS, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=QSA_CTX, n_slots=1, device=local)
+    eng.indexer_enable(4, 2048, 64, 1e7, 1e-6)
+    eng.seq_alloc(0)
+    r = np.random.default_rng(3 + 1000 * rank)
+    kr = torch.from_numpy(qsa_inputs(r, QSA_CTX)).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(3 + 1000 * rank)
+    for c in range(0, n0, 4096):
+        m = min(4096, n0 - c)
+        eng.append(0, 0, c, torch.randn(m, N_HEAD_KV * HD, generator=gen, device=dev),
+                   torch.randn(m, N_HEAD_KV * HD, generator=gen, device=dev))
+        eng.idx_append(0, 0, c, kr[c:c + m])
+    eng.reserve(0, QSA_CTX)
+    Kd = torch.randn(total, T, N_HEAD_KV * HD, generator=gen, device=dev)
+    Vd = torch.randn(total, T, N_HEAD_KV * HD, generator=gen, device=dev)
+    Qd = torch.randn(total, T, N_HEAD, HD, generator=gen, device=dev)
+    qi = torch.randn(total, T, 4, 128, generator=gen, device=dev)
+    out = torch.empty(T, N_HEAD, HD, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i: int, attn_ev=None):
+        p = n0 + T * i
+        eng.append(0, 0, p, Kd[i], Vd[i])
+        eng.idx_append(0, 0, p, kr[p:p + T])
+        if attn_ev:
+            attn_ev[0].record(stream)
+        eng.attn_decode_qsa(0, [0], [p], qi[i], Qd[i], T, SCALE, out)
+        if attn_ev:
+            attn_ev[1].record(stream)
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = Q.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(warm + i, evs[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = Q.launch_count() - launches0
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    attn_us = 1e3 * statistics.median(a.elapsed_time(b) for a, b in evs)
+    if eng.device_status() != 0:
+        raise RuntimeError("device status reported a bounds violation")
+    if ws > 1:
+        t = torch.tensor([ms, attn_us], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, attn_us = t.tolist()
+    if rank != 0:
+        return
+    n_whole = (QSA_CTX - 1) // 4
+    algo = n_whole * 128 * 2 + T * 2052 * N_HEAD_KV * 2 * 272 + 2 * T * N_HEAD * HD * 4 + T * 4 * 128 * 4
+    hbm, hbm_src = 6650.0, "fallback 6650 GB/s"
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        hbm, hbm_src = json.load(open(pk)).get("hbm_gbs", hbm), "measured hbm_gbs"
+    gbs = algo / (attn_us * 1e-6) / 1e9
+    line = {
+        "metric": "QSA sparse decode (model's indexer) tokens/s and µs per select+attend step, ctx 73728, T=3",
+        "value": ws * T * steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": steps, "warmup": warm,
+        "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_0 KV (int8 QK / f16 PV, f32 softmax); fp16 indexer keys, f32 scores",
+        "data": "synthetic N(0,1) (torch Philox / numpy PCG64, seed 3+1000*rank); indexer keys with a per-block "
+                "offset of variance 2",
+        "config": {"workload": "configs[3]'s context and tokens through the model's own lightning indexer: ctx 73728, "
+                               "1 layer, T=3, 4 indexer heads x 128, 4-cell blocks, 513 kept per token; each step "
+                               "appends 3 K/V rows + 3 indexer keys, then select + gather + attention",
+                   "parallelism": f"independent sequences x{ws} (replicas, no collective)",
+                   "l2": "working set 4.7 MB of pooled keys + 6.7 MB of kept KV per step fits L2: latency-bound"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_source": hbm_src, "traffic": None,
+                     "kernel": "qkv_attn_decode_qsa: k_idx_score + k_idx_topk + k_idx_gather + k_decode (+ merge)",
+                     "algorithmic_bytes_per_step": algo, "attn_us_per_step": attn_us},
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_qsa_baseline()
+    print(json.dumps(line), flush=True)
+
+
 class _DevRange:
     """A device address range as a float32 tensor (CUDA array interface)."""
 
@@ -643,6 +785,8 @@ def main():
         run_cfg5(args)
     elif args.workload == "cfg3":
         run_cfg3(args)
+    elif args.workload == "qsa":
+        run_qsa(args)
     else:
         run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

@@ -359,24 +359,28 @@ void orc_idx_pool(const uint16_t *keys, int64_t n_blocks, const float *norm_w, f
     }
 }
 
-float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b) {
+/* the score with q already rounded to fp16 values (qh) */
+static float idx_score_rounded(const float *qh, int n_head, const uint16_t *pooled_b) {
+    float k[ORC_IDX_KEY];
+    for (int d = 0; d < ORC_IDX_KEY; d++) k[d] = orc_fp16_to_fp32(pooled_b[d]);
     double tot = 0.0;
     for (int h = 0; h < n_head; h++) {
-        float part[32];
-        for (int l = 0; l < 32; l++) {
+        float q4[4];   /* four quarter sums in dim order; products of fp16 values are exact */
+        for (int j = 0; j < 4; j++) {
             float a = 0.0f;
-            for (int j = 0; j < 4; j++) {
-                const int d = 4 * l + j;
-                const float qh = orc_fp16_to_fp32(orc_fp32_to_fp16(q[h * ORC_IDX_KEY + d]));
-                const float p = qh * orc_fp16_to_fp32(pooled_b[d]);
-                a = j == 0 ? p : a + p;
-            }
-            part[l] = a;
+            for (int d = 32 * j; d < 32 * j + 32; d++) a = a + qh[h * ORC_IDX_KEY + d] * k[d];
+            q4[j] = a;
         }
-        const float dot = bfly32(part);
+        const float dot = (q4[0] + q4[1]) + (q4[2] + q4[3]);
         tot = tot + (double)(dot > 0.0f ? dot : 0.0f);
     }
     return (float)tot;
+}
+
+float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b) {
+    float qh[8 * ORC_IDX_KEY];
+    for (int i = 0; i < n_head * ORC_IDX_KEY && i < 8 * ORC_IDX_KEY; i++) qh[i] = orc_fp16_to_fp32(orc_fp32_to_fp16(q[i]));
+    return idx_score_rounded(qh, n_head < 8 ? n_head : 8, pooled_b);
 }
 
 typedef struct { float s; int32_t b; } idx_scored_t;
@@ -398,8 +402,12 @@ int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64
     const int tail = b_last >= whole;
     for (int k = 0; k < k_blocks; k++) blocks_out[k] = -1;
     idx_scored_t *sc = (idx_scored_t *)malloc(sizeof(idx_scored_t) * (size_t)(whole > 0 ? whole : 1));
+    float qh[8 * ORC_IDX_KEY];
+    const int nh = n_head < 8 ? n_head : 8;
+    for (int i = 0; i < nh * ORC_IDX_KEY; i++) qh[i] = orc_fp16_to_fp32(orc_fp32_to_fp16(q[i]));
+#pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < whole; b++) {
-        sc[b].s = orc_idx_score(q, n_head, pooled + b * ORC_IDX_KEY);
+        sc[b].s = idx_score_rounded(qh, nh, pooled + b * ORC_IDX_KEY);
         sc[b].b = (int32_t)b;
         if (scores) scores[b] = sc[b].s;
     }

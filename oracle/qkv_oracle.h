@@ -108,8 +108,9 @@ void orc_attn_q8_0_sparse(const float *Q, int64_t T, int n_head, int n_head_kv, 
  * QSA lightning indexer, decode path (the reference's own selector: src/qwfn_graph.cpp:280-311
  * qsa_pool_blocks / idx_query, 529-579 qsa_dec_index / qsa_dec_cells; bias and bucket
  * src/qwfn_engine.cpp:1072-1105).  Key length 128, 4 cells per block.  Every fp32 step has a
- * fixed order, the one the device kernels use (lane l of a warp owns dims 4l..4l+3; cross-lane
- * sums are xor butterflies 16,8,4,2,1, emulated here), so pooled keys, scores and kept blocks
+ * fixed order, the one the device kernels use (pooling: lane l of a warp owns dims 4l..4l+3,
+ * cross-lane sums are xor butterflies 16,8,4,2,1, emulated here; scores: four quarter sums
+ * in dim order), so pooled keys, scores and kept blocks
  * must match the device bit for bit.  ggml's own summation orders differ between its CPU and
  * CUDA backends, so these bits are this build's definition; the semantics are the reference's.
  */
@@ -127,8 +128,9 @@ void orc_idx_rope_table(int64_t n_blocks, int rope_dim, float freq_base, float *
 void orc_idx_pool(const uint16_t *keys, int64_t n_blocks, const float *norm_w, float eps, int rope_dim,
                   const float *cs, uint16_t *pooled);
 
-/* Score of one pooled key: (float) of the double sum over heads of max(0, butterfly of
- * ((q0 k0 + q1 k1) + q2 k2) + q3 k3 per lane), q rounded to fp16 first. */
+/* Score of one pooled key: (float) of the double sum over heads of max(0, dot), dot =
+ * (s0 + s1) + (s2 + s3), s_j the fp32 sum in dim order over dims 32j..32j+31 of the exact
+ * fp16 x fp16 products, q rounded to fp16 first. */
 float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b);
 
 /* Kept blocks for the token at position pos (ascending; returns how many, the rest of

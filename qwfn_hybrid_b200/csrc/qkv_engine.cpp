@@ -847,6 +847,7 @@ static qkv_status idx_select_chunk(qkv_engine *eng, int32_t layer, const int32_t
     p.n_out = n_out;
     p.status = eng->d_status;
     p.n_v = nv;
+    p.T = T;
     p.n_head = eng->icfg.n_head;
     p.k_blocks = eng->k_blocks;
     p.score_stride = score_stride;
@@ -889,9 +890,10 @@ extern "C" qkv_status qkv_idx_select(qkv_engine *eng, int32_t layer, const int32
     cudaStream_t st = S(stream);
     if ((r = flush_tables(eng, st)) != QKV_OK) return r;
     const int32_t n_v = n_seq * T;
-    if (!scores_out && (r = idx_scratch(eng, std::min(n_v, IDX_MAX_VSEQ))) != QKV_OK) return r;
-    for (int32_t v0 = 0; v0 < n_v; v0 += IDX_MAX_VSEQ) {
-        const int32_t nv = std::min(IDX_MAX_VSEQ, n_v - v0);
+    const int32_t step = IDX_MAX_VSEQ / T * T;   // whole sequences per launch
+    if (!scores_out && (r = idx_scratch(eng, std::min(n_v, step))) != QKV_OK) return r;
+    for (int32_t v0 = 0; v0 < n_v; v0 += step) {
+        const int32_t nv = std::min(step, n_v - v0);
         float *sc = scores_out ? scores_out + (size_t)v0 * eng->idx_max_blk : eng->d_iscore;
         if ((r = idx_select_chunk(eng, layer, slots, pos0, T, v0, nv, q_idx, blocks_out + (size_t)v0 * eng->k_blocks,
                                   n_out_out + v0, sc, eng->idx_max_blk, st)) != QKV_OK)
@@ -926,8 +928,9 @@ extern "C" qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const 
     }
     const int32_t n_v = n_seq * T, K = eng->k_blocks;
     const size_t qrow = (size_t)eng->cfg.n_head * HD;
-    for (int32_t v0 = 0; v0 < n_v; v0 += MAX_SEQ) {
-        const int32_t nv = std::min(MAX_SEQ, n_v - v0);
+    const int32_t step = MAX_SEQ / T * T;   // whole sequences per launch
+    for (int32_t v0 = 0; v0 < n_v; v0 += step) {
+        const int32_t nv = std::min(step, n_v - v0);
         if ((r = idx_select_chunk(eng, layer, slots, pos0, T, v0, nv, q_idx, eng->d_isel, eng->d_inout, eng->d_iscore,
                                   eng->idx_max_blk, st)) != QKV_OK)
             return r;

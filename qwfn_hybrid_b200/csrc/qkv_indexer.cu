@@ -9,7 +9,10 @@
 // and therefore the kept blocks bit for bit.  All of this is HBM / latency bound byte work.
 #include "qkv_internal.h"
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 namespace qkv {
 
@@ -142,53 +145,104 @@ cudaError_t launch_idx_pool(const IdxAppendParams &p, int32_t b_lo, int32_t n_bl
 }
 
 // ------------------------------------------------------------------------------------- scores
-// score[v][b] = (float)(((0.0 + r_0) + r_1) + ... )  in double, r_h = max(0, dot_h), dot_h the
-// butterfly sum over lanes of ((q0*k0 + q1*k1) + q2*k2) + q3*k3 with q = fp16(q_idx) (ggml's
-// F16 mul_mat converts its F32 operand to F16) and k the pooled fp16 key; the products of two
-// fp16 values are exact in fp32.  Whole blocks b < (pos+1)/4 only.
-__global__ void __launch_bounds__(256) k_idx_score(const IdxSelectParams p) {
-    __shared__ float qs[IDX_MAX_HEAD][IDX_KEY];
-    const int v = blockIdx.y;
-    const int32_t pos = p.v_pos[v], n_whole = (pos + 1) / IDX_R;
-    for (int i = threadIdx.x; i < p.n_head * IDX_KEY; i += blockDim.x)
-        qs[i / IDX_KEY][i % IDX_KEY] = __half2float(__float2half_rn(p.q[(int64_t)v * p.n_head * IDX_KEY + i]));
+// score[v][b] = (float)(((0.0 + r_0) + r_1) + ...)  in double over the heads, r_h = max(0, dot_h),
+// dot_h = (s_0 + s_1) + (s_2 + s_3), s_j the fp32 sum in dim order over dims 32j .. 32j+31 of
+// q_d * k_d, with q = fp16(q_idx) (ggml's F16 mul_mat converts its F32 operand to F16) and k the
+// pooled fp16 key: the products of two fp16 values are exact in fp32, so fused multiply-adds round
+// as the sums do.  Whole blocks b < (pos+1)/4 only.  Four lanes per block (lane quarter j owns
+// s_j; all of its 64 key bytes are loaded up front), 64 blocks per CTA; CTA (x, g) serves the T
+// entries g*T .. g*T+T-1 (the tokens of one sequence), which share every pooled-key load.
+constexpr int SC_THREADS = 256, SC_BLOCKS = SC_THREADS / 4;
+constexpr int QROW = IDX_KEY + 16;   // each 32-dim quarter 4 words further on: conflict-free quarter reads
+__device__ __forceinline__ int qcol(int d) { return d + 4 * (d >> 5); }
+
+__global__ void __launch_bounds__(SC_THREADS) k_idx_score(const IdxSelectParams p) {
+    __shared__ __align__(16) float qs[4][IDX_MAX_HEAD][QROW];
+    const int g = blockIdx.y, T = p.T, H = p.n_head, v0 = g * T;
+    // the key loads first: their latency overlaps the query staging
+    const int j = threadIdx.x & 3;                                 // quarter of the dims
+    const int32_t b = blockIdx.x * SC_BLOCKS + (threadIdx.x >> 2);
+    const int32_t whole_max = (p.v_pos[v0 + T - 1] + 1) / IDX_R;   // positions ascend with t
+    const uint8_t *pg = nullptr;
+    if (b < whole_max) {
+        pg = idx_page(p.pool, p.bt + (int64_t)p.v_slot[v0] * p.max_pages, p.max_pages, p.n_pages, b * IDX_R);
+        if (!pg && j == 0) atomicOr(p.status, ST_BAD_PAGE);
+    }
+    uint4 w[4] = {};
+    if (pg) {
+        const uint4 *key = reinterpret_cast<const uint4 *>(pg + IDX_RAW_BYTES + (int64_t)(b & (IDX_BPP - 1)) * IDX_KEY * 2 + 64 * j);
+#pragma unroll
+        for (int c = 0; c < 4; c++) w[c] = key[c];
+    }
+    for (int i = threadIdx.x; i < T * H * IDX_KEY; i += blockDim.x) {
+        const int th = i / IDX_KEY, d = i % IDX_KEY;
+        qs[th / H][th % H][qcol(d)] = __half2float(__float2half_rn(p.q[(int64_t)v0 * H * IDX_KEY + i]));
+    }
     __syncthreads();
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int32_t *bt = p.bt + (int64_t)p.v_slot[v] * p.max_pages;
-    for (int k = 0; k < 4; k++) {
-        const int32_t b = (blockIdx.x * 8 + wid) * 4 + k;
-        if (b >= n_whole) return;
-        const uint8_t *pg = idx_page(p.pool, bt, p.max_pages, p.n_pages, b * IDX_R);
-        if (!pg) {
-            if (lane == 0) atomicOr(p.status, ST_BAD_PAGE);
-            return;
+    float acc[4][IDX_MAX_HEAD];
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int h = 0; h < IDX_MAX_HEAD; h++) acc[t][h] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const __half2 *hw = reinterpret_cast<const __half2 *>(&w[c]);
+        float k[8];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            k[2 * e] = __low2float(hw[e]);
+            k[2 * e + 1] = __high2float(hw[e]);
         }
-        const uint2 w = *reinterpret_cast<const uint2 *>(pg + IDX_RAW_BYTES + (int64_t)(b & (IDX_BPP - 1)) * IDX_KEY * 2 +
-                                                         8 * lane);
-        const __half2 lo = *reinterpret_cast<const __half2 *>(&w.x), hi = *reinterpret_cast<const __half2 *>(&w.y);
-        const float kk[4] = {__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi)};
+        const int d0 = 32 * j + 8 * c;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            if (t >= T) break;
+#pragma unroll
+            for (int h = 0; h < IDX_MAX_HEAD; h++) {
+                if (h >= H) break;
+                const float4 qa = *reinterpret_cast<const float4 *>(&qs[t][h][qcol(d0)]);
+                const float4 qb = *reinterpret_cast<const float4 *>(&qs[t][h][qcol(d0) + 4]);
+                float a = acc[t][h];
+                a = __fmaf_rn(qa.x, k[0], a);
+                a = __fmaf_rn(qa.y, k[1], a);
+                a = __fmaf_rn(qa.z, k[2], a);
+                a = __fmaf_rn(qa.w, k[3], a);
+                a = __fmaf_rn(qb.x, k[4], a);
+                a = __fmaf_rn(qb.y, k[5], a);
+                a = __fmaf_rn(qb.z, k[6], a);
+                a = __fmaf_rn(qb.w, k[7], a);
+                acc[t][h] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        if (t >= T) break;
         double tot = 0.0;
-        for (int h = 0; h < p.n_head; h++) {
-            const float *q = &qs[h][4 * lane];
-            float a = __fmul_rn(q[0], kk[0]);
-            a = __fadd_rn(a, __fmul_rn(q[1], kk[1]));
-            a = __fadd_rn(a, __fmul_rn(q[2], kk[2]));
-            a = __fadd_rn(a, __fmul_rn(q[3], kk[3]));
-            a = warp_sum_bfly(a);
-            tot = __dadd_rn(tot, (double)(a > 0.0f ? a : 0.0f));
+#pragma unroll
+        for (int h = 0; h < IDX_MAX_HEAD; h++) {
+            if (h >= H) break;
+            float d = __fadd_rn(acc[t][h], __shfl_xor_sync(0xffffffffu, acc[t][h], 1));   // s0+s1, s2+s3
+            d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));                           // (s0+s1)+(s2+s3)
+            tot = __dadd_rn(tot, (double)(d > 0.0f ? d : 0.0f));
         }
-        if (lane == 0) p.scores[(int64_t)v * p.score_stride + b] = __double2float_rn(tot);
+        if (pg && j == 0 && b < (p.v_pos[v0 + t] + 1) / IDX_R)
+            p.scores[(int64_t)(v0 + t) * p.score_stride + b] = __double2float_rn(tot);
     }
 }
 
 // -------------------------------------------------------------------------------------- top-k
-// Per entry v (one CTA of 1024 threads): the k_blocks kept blocks in ascending order.  With more
+// Per entry v (a cluster of TK_CL CTAs): the k_blocks kept blocks in ascending order.  With more
 // than k_blocks candidate blocks, the incomplete tail block (if any) is kept and the other
 // need = k_blocks - tail come from the whole blocks by score, descending, ties by lower index:
 // an exact radix select of the need-th largest key (four 8-bit digits, most significant first)
 // gives the threshold; every key above it is kept and, of the keys equal to it, the lowest
-// indices.  Keys are the scores' bits mapped so that unsigned order is float order.
-constexpr int TK_THREADS = 1024;
+// indices.  Keys are the scores' bits mapped so that unsigned order is float order.  CTA r of the
+// cluster holds the keys of blocks [r*chunk, (r+1)*chunk) in shared memory; per digit every CTA
+// counts its keys, rank 0 sums the TK_CL histograms through distributed shared memory and picks
+// the digit; the CTAs' outputs are contiguous runs of the ascending result.
+constexpr int TK_CL = 8, TK_THREADS = 256;
+constexpr int TK_MAX_CHUNK = 48 * 1024;   // keys per CTA (192 KiB): n_ctx up to 1.5M positions
 
 __device__ __forceinline__ uint32_t score_key(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -224,80 +278,151 @@ __device__ int block_excl_scan(int x, int *warp_tot, int *tot) {
     return base + inc - x;
 }
 
-__global__ void __launch_bounds__(TK_THREADS) k_idx_topk(const IdxSelectParams p) {
+__global__ void __cluster_dims__(TK_CL, 1, 1) __launch_bounds__(TK_THREADS) k_idx_topk(const IdxSelectParams p) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ uint32_t skeys[];
     __shared__ int hist[256];
     __shared__ int warp_tot[32];
-    __shared__ uint32_t s_prefix;
-    __shared__ int s_remaining;
-    const int v = blockIdx.x, tid = threadIdx.x;
+    __shared__ uint32_t s_prefix;                  // rank 0's copies are the cluster's
+    __shared__ int s_remaining, s_eq;
+    __shared__ int s_cnt[2];                       // this CTA's equal / taken counts
+    const int v = blockIdx.y, r = (int)cluster.block_rank(), tid = threadIdx.x, lane = tid & 31;
     const int32_t pos = p.v_pos[v], n_whole = (pos + 1) / IDX_R, b_last = pos / IDX_R;
     const int tail = b_last >= n_whole ? 1 : 0;
     int32_t *out = p.blocks + (int64_t)v * p.k_blocks;
-    if (b_last + 1 <= p.k_blocks) {   // every block is kept
-        for (int i = tid; i < p.k_blocks; i += blockDim.x) out[i] = i <= b_last ? i : -1;
-        if (tid == 0) p.n_out[v] = b_last + 1;
+    if (b_last + 1 <= p.k_blocks) {   // every block is kept (uniform over the cluster: no cluster barrier)
+        if (r == 0) {
+            for (int i = tid; i < p.k_blocks; i += blockDim.x) out[i] = i <= b_last ? i : -1;
+            if (tid == 0) p.n_out[v] = b_last + 1;
+        }
         return;
     }
     const int need = p.k_blocks - tail;
     const float *sc = p.scores + (int64_t)v * p.score_stride;
+    const int chunk = (n_whole + TK_CL - 1) / TK_CL;
+    const int k0 = min(n_whole, r * chunk), k1 = min(n_whole, k0 + chunk), nk = k1 - k0;
+    for (int i = tid; i < nk; i += blockDim.x) skeys[i] = score_key(sc[k0 + i]);
+    int *hist0 = cluster.map_shared_rank(hist, 0);
     uint32_t prefix = 0, mask = 0;
     int remaining = need;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+        if (tid < 256) hist[tid] = 0;
         __syncthreads();
-        for (int i = tid; i < n_whole; i += blockDim.x) {
-            const uint32_t key = score_key(sc[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+        for (int i = tid; i < nk; i += blockDim.x) {
+            const uint32_t key = skeys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1);
         }
-        __syncthreads();
-        if (tid == 0) {
-            int above = 0, d = 255;
-            for (; d > 0; d--) {
-                if (above + hist[d] >= remaining) break;
-                above += hist[d];
+        cluster.sync();                            // every CTA's histogram is complete
+        if (r == 0) {
+            if (tid < 256) {
+                int c = hist[tid];
+#pragma unroll
+                for (int q = 1; q < TK_CL; q++) c += cluster.map_shared_rank(hist, q)[tid];
+                hist[tid] = c;                     // only rank 0 reads its own hist after this
             }
-            s_remaining = remaining - above;
-            s_prefix = prefix | ((uint32_t)d << shift);
+            __syncthreads();
+            if (tid < 32) {   // digit of the need-th largest: lane l holds bins 255-8l .. 248-8l
+                int bins[8], sum = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    bins[j] = hist[255 - 8 * lane - j];
+                    sum += bins[j];
+                }
+                int incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+                if (lane == __ffs(hit) - 1) {
+                    int above = incl - sum, j = 0;
+#pragma unroll
+                    for (int jj = 0; jj < 7; jj++) {
+                        if (j == jj && above + bins[jj] < remaining) {
+                            above += bins[jj];
+                            j = jj + 1;
+                        }
+                    }
+                    int bj = bins[0];
+#pragma unroll
+                    for (int jj = 1; jj < 8; jj++) bj = j == jj ? bins[jj] : bj;
+                    s_remaining = remaining - above;
+                    s_prefix = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
+                    s_eq = bj;
+                }
+            }
         }
-        __syncthreads();
-        remaining = s_remaining;
-        prefix = s_prefix;
+        cluster.sync();                            // rank 0's choice is visible; histograms read
+        prefix = *cluster.map_shared_rank(&s_prefix, 0);
+        remaining = *cluster.map_shared_rank(&s_remaining, 0);
         mask |= 0xffu << shift;
-        __syncthreads();
     }
-    // prefix: the threshold key; keep every key above it and the first `remaining` equal to it
-    const int chunk = (n_whole + blockDim.x - 1) / blockDim.x;
-    const int i0 = min(n_whole, tid * chunk), i1 = min(n_whole, i0 + chunk);
-    int n_eq = 0;
-    for (int i = i0; i < i1; i++) n_eq += score_key(sc[i]) == prefix;
-    int tot;
-    int eq_rank = block_excl_scan(n_eq, warp_tot, &tot);
+    const int eq_total = *cluster.map_shared_rank(&s_eq, 0);
+    const bool all_eq = eq_total == remaining;     // no tie at the threshold to break
+    // per CTA: keys above the threshold, and (ties) the first `remaining` equal keys by index
+    const int per = (nk + blockDim.x - 1) / blockDim.x;
+    const int i0 = min(nk, tid * per), i1 = min(nk, i0 + per);
+    int tot = 0, eq_base = 0, eq_rank = 0;
+    if (!all_eq) {
+        int n_eq = 0;
+        for (int i = i0; i < i1; i++) n_eq += skeys[i] == prefix;
+        eq_rank = block_excl_scan(n_eq, warp_tot, &tot);
+        if (tid == 0) s_cnt[0] = tot;
+    }
+    cluster.sync();                                // equal counts of every CTA published
+    if (!all_eq)
+        for (int q = 0; q < r; q++) eq_base += cluster.map_shared_rank(s_cnt, q)[0];
     int n_take = 0;
-    for (int i = i0, r = eq_rank; i < i1; i++) {
-        const uint32_t key = score_key(sc[i]);
+    for (int i = i0, e = eq_base + eq_rank; i < i1; i++) {
+        const uint32_t key = skeys[i];
         if (key > prefix) n_take++;
-        else if (key == prefix) n_take += r++ < remaining;
+        else if (key == prefix) n_take += all_eq || e++ < remaining;
     }
     int at = block_excl_scan(n_take, warp_tot, &tot);
-    for (int i = i0, r = eq_rank; i < i1; i++) {
-        const uint32_t key = score_key(sc[i]);
-        bool take = key > prefix;
-        if (key == prefix) take = r++ < remaining;
-        if (take && at < need) out[at++] = i;
+    if (tid == 0) s_cnt[1] = tot;
+    cluster.sync();                                // taken counts of every CTA published
+    int base = 0, all = 0;
+    for (int q = 0; q < TK_CL; q++) {
+        const int c = cluster.map_shared_rank(s_cnt, q)[1];
+        if (q < r) base += c;
+        all += c;
     }
-    if (tid == 0) {
-        if (tot != need) atomicOr(p.status, ST_BAD_INDEX);
+    at += base;
+    for (int i = i0, e = eq_base + eq_rank; i < i1; i++) {
+        const uint32_t key = skeys[i];
+        bool take = key > prefix;
+        if (key == prefix) take = all_eq || e++ < remaining;
+        if (take && at < need) out[at++] = k0 + i;
+    }
+    if (r == 0 && tid == 0) {
+        if (all != need) atomicOr(p.status, ST_BAD_INDEX);
         if (tail) out[need] = b_last;
         p.n_out[v] = p.k_blocks;
     }
+    cluster.sync();                                // no CTA leaves while its shared memory is read
 }
 
 cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaStream_t st) {
+    static uint64_t attr_set = 0;   // devices whose k_idx_topk allows TK_MAX_CHUNK keys
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!(attr_set >> dev & 1)) {
+        e = cudaFuncSetAttribute(k_idx_topk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 TK_MAX_CHUNK * (int)sizeof(uint32_t));
+        if (e != cudaSuccess) return e;
+        attr_set |= 1ull << dev;
+    }
     if (max_whole > 0) {
-        k_idx_score<<<dim3((max_whole + 31) / 32, p.n_v), 256, 0, st>>>(p);
+        k_idx_score<<<dim3((max_whole + SC_BLOCKS - 1) / SC_BLOCKS, p.n_v / p.T), SC_THREADS, 0, st>>>(p);
         count_launches(1);
     }
-    k_idx_topk<<<p.n_v, TK_THREADS, 0, st>>>(p);
+    const int chunk = (max_whole + TK_CL - 1) / TK_CL;
+    if (chunk > TK_MAX_CHUNK) return cudaErrorInvalidValue;
+    k_idx_topk<<<dim3(TK_CL, p.n_v), TK_THREADS, (size_t)std::max(chunk, 1) * sizeof(uint32_t), st>>>(p);
     count_launches(1);
     return cudaGetLastError();
 }
@@ -327,34 +452,39 @@ __global__ void __launch_bounds__(256) k_idx_gather(const IdxGatherParams p) {
     uint8_t *dst = p.dst + (int64_t)dp * p.page_bytes + (int64_t)(h * TILES_PER_PAGE + ((j0 >> 6) & 3)) * TILE_BYTES;
     const int ts = c0 & 63, td = j0 & 63;
     const int nv = min(IDX_R, pos - c0 + 1);   // valid cells of the group
+    // every load first (the group's bytes are scattered: many requests in flight), then the stores
+    uint4 kq[2];
 #pragma unroll
-    for (int k = 0; k < 2; k++) {              // K quants
+    for (int k = 0; k < 2; k++) {              // K quants: 4 rows x 16 chunks of 16 B
         const int q = lane + 32 * k, m = q >> 4, c = q & 15;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (m < nv) val = *reinterpret_cast<const uint4 *>(src + TILE_KQ + (ts + m) * HD + ((c ^ kswz(ts + m)) << 4));
-        *reinterpret_cast<uint4 *>(dst + TILE_KQ + (td + m) * HD + ((c ^ kswz(td + m)) << 4)) = val;
+        kq[k] = *reinterpret_cast<const uint4 *>(src + TILE_KQ + (ts + m) * HD + ((c ^ kswz(ts + m)) << 4));
+    }
+    uint32_t vq[HD / 32];
+#pragma unroll
+    for (int k = 0; k < HD / 32; k++)          // V quants: 4 tokens of one dim are one word
+        vq[k] = *reinterpret_cast<const uint32_t *>(src + v_off(lane + 32 * k, ts));
+    uint2 sc = make_uint2(0, 0);
+    if (lane < 16)                             // K scales: [tok][8] fp16, 16 B per token
+        sc.x = *reinterpret_cast<const uint32_t *>(src + kd_off(ts, 0) + 4 * lane);
+    else if (lane < 16 + NBLK)                 // V scales: [8][tok] fp16, 4 tokens = 8 B per block
+        sc = *reinterpret_cast<const uint2 *>(src + vd_off(lane - 16, ts));
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int q = lane + 32 * k, m = q >> 4, c = q & 15;
+        *reinterpret_cast<uint4 *>(dst + TILE_KQ + (td + m) * HD + ((c ^ kswz(td + m)) << 4)) =
+            m < nv ? kq[k] : make_uint4(0, 0, 0, 0);
     }
     const uint32_t vmask = nv >= 4 ? 0xffffffffu : ((1u << (8 * nv)) - 1u);
 #pragma unroll
-    for (int k = 0; k < HD / 32; k++) {        // V quants: 4 tokens of one dim are one word
-        const int dim = lane + 32 * k;
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(src + v_off(dim, ts));
-        *reinterpret_cast<uint32_t *>(dst + v_off(dim, td)) = w & vmask;
-    }
-    if (lane < 16) {                            // K scales: [tok][8] fp16, 16 B per token
-        const int m = lane >> 2;
-        const uint32_t w = m < nv ? *reinterpret_cast<const uint32_t *>(src + kd_off(ts, 0) + 4 * lane) : 0u;
-        *reinterpret_cast<uint32_t *>(dst + kd_off(td, 0) + 4 * lane) = w;
-    } else if (lane < 16 + NBLK) {              // V scales: [8][tok] fp16, 4 tokens = 8 B per block
-        const int blk = lane - 16;
-        uint2 w = *reinterpret_cast<const uint2 *>(src + vd_off(blk, ts));
+    for (int k = 0; k < HD / 32; k++) *reinterpret_cast<uint32_t *>(dst + v_off(lane + 32 * k, td)) = vq[k] & vmask;
+    if (lane < 16) {
+        *reinterpret_cast<uint32_t *>(dst + kd_off(td, 0) + 4 * lane) = (lane >> 2) < nv ? sc.x : 0u;
+    } else if (lane < 16 + NBLK) {
         if (nv < 4) {
-            const uint32_t lo = nv >= 2 ? 0xffffffffu : (nv >= 1 ? 0x0000ffffu : 0u);
-            const uint32_t hi = nv >= 4 ? 0xffffffffu : (nv >= 3 ? 0x0000ffffu : 0u);
-            w.x &= lo;
-            w.y &= hi;
+            sc.x &= nv >= 2 ? 0xffffffffu : (nv >= 1 ? 0x0000ffffu : 0u);
+            sc.y &= nv >= 3 ? 0x0000ffffu : 0u;
         }
-        *reinterpret_cast<uint2 *>(dst + vd_off(blk, td)) = w;
+        *reinterpret_cast<uint2 *>(dst + vd_off(lane - 16, td)) = sc;
     }
 }
 

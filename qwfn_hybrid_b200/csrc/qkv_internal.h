@@ -126,7 +126,7 @@ struct IdxAppendParams {
 cudaError_t launch_idx_append(const IdxAppendParams &p, cudaStream_t st);
 cudaError_t launch_idx_pool(const IdxAppendParams &p, int32_t b_lo, int32_t n_blk, cudaStream_t st);
 
-// One entry per (sequence, token): v = i * T + t.
+// One entry per (sequence, token): v = i * T + t; the T entries of a sequence are adjacent.
 struct IdxSelectParams {
     const uint8_t *pool;          // layer indexer pool
     const int32_t *bt;            // engine block table [n_slots][max_pages]
@@ -135,7 +135,7 @@ struct IdxSelectParams {
     int32_t       *blocks;        // [n_v][k_blocks]
     int32_t       *n_out;         // [n_v]
     int32_t       *status;
-    int32_t n_v, n_head, k_blocks, score_stride, n_pages, max_pages;
+    int32_t n_v, T, n_head, k_blocks, score_stride, n_pages, max_pages;   // n_v a multiple of T
     int32_t v_slot[IDX_MAX_VSEQ], v_pos[IDX_MAX_VSEQ];
 };
 cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaStream_t st);

@@ -48,11 +48,14 @@ def np_score(q: np.ndarray, pooled_b: np.ndarray) -> np.float32:
     k = pooled_b.view(np.float16).astype(f32)
     tot = 0.0
     for h in range(q.shape[0]):
-        p = (qh[h] * k).astype(f32).reshape(32, 4)
-        a = p[:, 0].copy()
-        for j in range(1, 4):
-            a = (a + p[:, j]).astype(f32)
-        d = bfly(a)
+        p = (qh[h] * k).astype(f32)
+        part = []
+        for j in range(4):
+            a = f32(0.0)
+            for e in range(32 * j, 32 * j + 32):
+                a = f32(a + p[e])
+            part.append(a)
+        d = f32(f32(part[0] + part[1]) + f32(part[2] + part[3]))
         tot = tot + float(max(d, f32(0.0)))
     return f32(tot)
 

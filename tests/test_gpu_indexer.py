@@ -214,3 +214,86 @@ def test_host_blob_order_and_indexer_rows(cuda, qkvlib, oracle):
     snap.release()
     snap2.release()
     assert eng.device_status() == 0
+
+
+@pytest.mark.parametrize("T", [1, 4])
+def test_select_and_attend_many_sequences(cuda, qkvlib, oracle, T):
+    """23 sequences x T tokens: launches split into whole sequences (21 or 16 per decode launch),
+    contexts from T tokens to past 513 blocks."""
+    import torch
+    n_seq = 23
+    eng, w = idx_engine(qkvlib, n_ctx=2600, n_slots=n_seq)
+    lens = [T, T + 1, T + 2] + [int(x) for x in np.linspace(40, 2590, n_seq - 3)]
+    for s, n in enumerate(lens):
+        eng.seq_alloc(s)
+        fill(eng, 0, s, n, 600 + 7 * s)
+    q_idx = normal(700, (n_seq, T, N_HEAD_IDX, 128))
+    Q = normal(701, (n_seq, T, 16, 256))
+    pos0 = [n - T for n in lens]
+    blocks, n_out, _ = _select(eng, list(range(n_seq)), pos0, q_idx, T)
+    out = torch.full((n_seq, T, 16, 256), float("nan"), dtype=torch.float32, device="cuda")
+    eng.attn_decode_qsa(0, list(range(n_seq)), pos0, to_dev(q_idx), to_dev(Q), T, 1 / 16, out)
+    torch.cuda.synchronize()
+    assert eng.device_status() == 0
+    got = out.cpu().numpy()
+    for s, n in enumerate(lens):
+        kq, vq = read_rows(eng, 0, s, 0, n)
+        _, pooled = read_idx(eng, 0, s, 0, n // 4)
+        for t in range(T):
+            pos = pos0[s] + t
+            kept, _ = oracle.idx_select(q_idx[s, t], pooled, pos, 513)
+            v = s * T + t
+            np.testing.assert_array_equal(blocks[v, :n_out[v]], kept)
+            cells = (4 * kept[:, None] + np.arange(4)[None, :]).reshape(-1)
+            cells = cells[cells <= pos].astype(np.int32)
+            ref = oracle.attn(Q[s, t:t + 1], kq, vq, [pos], 2, 1 / 16, cells=cells)
+            assert_close(got[s, t:t + 1], ref, f"seq {s} (len {n}) token {t}")
+
+
+def test_rollback_and_reappend_repools(cuda, qkvlib, oracle):
+    """Rewinding n_past and appending new keys over old positions pools the touched blocks again."""
+    import torch
+    eng, w = idx_engine(qkvlib, n_ctx=1030, n_rollback=3)   # n_ctx not a multiple of 4 (last block partial)
+    eng.seq_alloc(0)
+    fill(eng, 0, 0, 1030, 800)
+    eng.rollback_arm(0, 3)
+    eng.rollback_n(0, 3)                           # n_past 1027
+    kr = normal(801, (3, 128), 2.0)
+    append_rows(eng, 0, 0, 1027, normal(802, (3, 512)), normal(803, (3, 512)))
+    eng.idx_append(0, 0, 1027, to_dev(kr))
+    torch.cuda.synchronize()
+    keys, pooled = read_idx(eng, 0, 0, 1030, 1030 // 4)
+    np.testing.assert_array_equal(keys[1027:], kr.astype(np.float16).view(np.uint16))
+    np.testing.assert_array_equal(pooled, oracle.idx_pool(keys, 1030 // 4, w[0], EPS, ROPE_DIM, BASE))
+    assert eng.device_status() == 0
+
+
+def test_indexer_errors(cuda, qkvlib):
+    import ctypes
+    import torch
+    eng = engine(qkvlib, n_ctx=1024, n_slots=1)
+    eng.seq_alloc(0)
+    k = torch.zeros(4, 128, device="cuda")
+    with pytest.raises(qkvlib.QkvError) as e:      # not enabled
+        eng.idx_append(0, 0, 0, k)
+    assert e.value.status == qkvlib.ERR_STATE
+    L = qkvlib.lib()
+    assert L.qkv_indexer_enable(eng.handle, None, None) == qkvlib.ERR_INVALID
+    for bad in ((4, 128, 8, 2048, 64), (4, 64, 4, 2048, 64), (9, 128, 4, 2048, 64), (4, 128, 4, 2048, 62)):
+        c = qkvlib.QkvIndexerConfig(*bad, 1e7, 1e-6)       # ratio, key length, heads, rope dims
+        assert L.qkv_indexer_enable(eng.handle, ctypes.byref(c), None) == qkvlib.ERR_INVALID, bad
+    eng.indexer_enable(4, 2048, 64, 1e7, 1e-6)
+    with pytest.raises(qkvlib.QkvError) as e:      # beyond n_past
+        eng.idx_append(0, 0, 5, k)
+    assert e.value.status == qkvlib.ERR_INVALID
+    with pytest.raises(qkvlib.QkvError) as e:      # keys not 16-byte aligned
+        eng.idx_append(0, 0, 0, k.view(-1)[1:129].view(1, 128), n_rows=1)
+    assert e.value.status == qkvlib.ERR_INVALID
+    blocks = torch.empty(513, dtype=torch.int32, device="cuda")
+    n_out = torch.empty(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(qkvlib.QkvError) as e:      # positions not appended yet
+        eng.idx_select(0, [0], [0], torch.zeros(1, 1, 4, 128, device="cuda"), 1, blocks, n_out)
+    assert e.value.status == qkvlib.ERR_INVALID
+    with pytest.raises(qkvlib.QkvError) as e:      # enabled twice
+        eng.indexer_enable(4, 2048, 64, 1e7, 1e-6)
+    assert e.value.status == qkvlib.ERR_STATE

@@ -282,9 +282,10 @@ __global__ void __cluster_dims__(TK_CL, 1, 1) __launch_bounds__(TK_THREADS) k_id
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ uint32_t skeys[];
-    __shared__ int hist[256];
+    __shared__ int hist[2][256];                   // this CTA's counts, two passes alternating
+    __shared__ int ctot[256];                      // the cluster's counts
     __shared__ int warp_tot[32];
-    __shared__ uint32_t s_prefix;                  // rank 0's copies are the cluster's
+    __shared__ uint32_t s_prefix;                  // the same in every CTA of the cluster
     __shared__ int s_remaining, s_eq;
     __shared__ int s_cnt[2];                       // this CTA's equal / taken counts
     const int v = blockIdx.y, r = (int)cluster.block_rank(), tid = threadIdx.x, lane = tid & 31;
@@ -303,63 +304,63 @@ __global__ void __cluster_dims__(TK_CL, 1, 1) __launch_bounds__(TK_THREADS) k_id
     const int chunk = (n_whole + TK_CL - 1) / TK_CL;
     const int k0 = min(n_whole, r * chunk), k1 = min(n_whole, k0 + chunk), nk = k1 - k0;
     for (int i = tid; i < nk; i += blockDim.x) skeys[i] = score_key(sc[k0 + i]);
-    int *hist0 = cluster.map_shared_rank(hist, 0);
     uint32_t prefix = 0, mask = 0;
     int remaining = need;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        if (tid < 256) hist[tid] = 0;
+    for (int shift = 24, pass = 0; shift >= 0; shift -= 8, pass++) {
+        // histograms alternate between two buffers: the one written now was last read two passes
+        // ago, before every CTA reached the previous pass's barrier
+        int *h = hist[pass & 1];
+        if (tid < 256) h[tid] = 0;
         __syncthreads();
         for (int i = tid; i < nk; i += blockDim.x) {
             const uint32_t key = skeys[i];
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1);
+            if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xffu], 1);
         }
         cluster.sync();                            // every CTA's histogram is complete
-        if (r == 0) {
-            if (tid < 256) {
-                int c = hist[tid];
+        if (tid < 256) {                           // every CTA sums all of them and picks the same digit
+            int c = 0;
 #pragma unroll
-                for (int q = 1; q < TK_CL; q++) c += cluster.map_shared_rank(hist, q)[tid];
-                hist[tid] = c;                     // only rank 0 reads its own hist after this
+            for (int q = 0; q < TK_CL; q++) c += cluster.map_shared_rank(h, q)[tid];
+            ctot[tid] = c;
+        }
+        __syncthreads();
+        if (tid < 32) {   // digit of the need-th largest: lane l holds bins 255-8l .. 248-8l
+            int bins[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                bins[j] = ctot[255 - 8 * lane - j];
+                sum += bins[j];
             }
-            __syncthreads();
-            if (tid < 32) {   // digit of the need-th largest: lane l holds bins 255-8l .. 248-8l
-                int bins[8], sum = 0;
+            int incl = sum;
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    bins[j] = hist[255 - 8 * lane - j];
-                    sum += bins[j];
-                }
-                int incl = sum;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+            if (lane == __ffs(hit) - 1) {
+                int above = incl - sum, j = 0;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
-                if (lane == __ffs(hit) - 1) {
-                    int above = incl - sum, j = 0;
-#pragma unroll
-                    for (int jj = 0; jj < 7; jj++) {
-                        if (j == jj && above + bins[jj] < remaining) {
-                            above += bins[jj];
-                            j = jj + 1;
-                        }
+                for (int jj = 0; jj < 7; jj++) {
+                    if (j == jj && above + bins[jj] < remaining) {
+                        above += bins[jj];
+                        j = jj + 1;
                     }
-                    int bj = bins[0];
-#pragma unroll
-                    for (int jj = 1; jj < 8; jj++) bj = j == jj ? bins[jj] : bj;
-                    s_remaining = remaining - above;
-                    s_prefix = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
-                    s_eq = bj;
                 }
+                int bj = bins[0];
+#pragma unroll
+                for (int jj = 1; jj < 8; jj++) bj = j == jj ? bins[jj] : bj;
+                s_remaining = remaining - above;
+                s_prefix = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
+                s_eq = bj;
             }
         }
-        cluster.sync();                            // rank 0's choice is visible; histograms read
-        prefix = *cluster.map_shared_rank(&s_prefix, 0);
-        remaining = *cluster.map_shared_rank(&s_remaining, 0);
+        __syncthreads();
+        prefix = s_prefix;
+        remaining = s_remaining;
         mask |= 0xffu << shift;
     }
-    const int eq_total = *cluster.map_shared_rank(&s_eq, 0);
+    const int eq_total = s_eq;
     const bool all_eq = eq_total == remaining;     // no tie at the threshold to break
     // per CTA: keys above the threshold, and (ties) the first `remaining` equal keys by index
     const int per = (nk + blockDim.x - 1) / blockDim.x;
@@ -370,10 +371,9 @@ __global__ void __cluster_dims__(TK_CL, 1, 1) __launch_bounds__(TK_THREADS) k_id
         for (int i = i0; i < i1; i++) n_eq += skeys[i] == prefix;
         eq_rank = block_excl_scan(n_eq, warp_tot, &tot);
         if (tid == 0) s_cnt[0] = tot;
+        cluster.sync();                            // equal counts of every CTA published (all_eq is
+        for (int q = 0; q < r; q++) eq_base += cluster.map_shared_rank(s_cnt, q)[0];   // cluster-uniform)
     }
-    cluster.sync();                                // equal counts of every CTA published
-    if (!all_eq)
-        for (int q = 0; q < r; q++) eq_base += cluster.map_shared_rank(s_cnt, q)[0];
     int n_take = 0;
     for (int i = i0, e = eq_base + eq_rank; i < i1; i++) {
         const uint32_t key = skeys[i];

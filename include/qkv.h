@@ -115,6 +115,23 @@ qkv_status qkv_pages_free(const qkv_engine *eng, int32_t *n_free);
 qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos,
                       const float *K, const float *V, int32_t n_rows, void *stream);
 
+/* Projections of the new tokens fused with kernel A: for T <= 4 tokens at positions
+ * pos .. pos+T-1 of a slot, K = rope(rms_norm(Wk x) * k_norm) and V = Wv x per KV head are
+ * quantised to q8_0 into the cache exactly as qkv_append would store them, and (with Wq) the query
+ * Q = rope(rms_norm(Wq x) * q_norm) per query head is written to Q_out for the attention call.
+ * Replaces graph_builder::qsa_dec_qkv + qsa_dec_kv_write (src/qwfn_graph.cpp:582-628: the
+ * projections, the reference's rms() and rope() helpers, src/qwfn_graph.cpp:125-132, and the
+ * set_rows); the F32 K/V rows never reach memory.  x: device F32 [T][n_embd] (n_embd a multiple
+ * of 64, <= 8192); Wq: device bf16 [2*n_head*head_dim][n_embd], query and gate rows interleaved per
+ * head as attn_q.weight is (NULL: no query); Wk, Wv: device bf16 [n_head_kv*head_dim][n_embd];
+ * q_norm, k_norm: device F32 [head_dim]; rope: the first rope_dim dims of each head, NEOX pairs,
+ * theta_i = p * freq_base^(-2i/rope_dim) (text positions); Q_out: device F32 [T][n_head][head_dim].
+ * pos <= n_past; n_past becomes max(n_past, pos+T).  Weight and input pointers 16-byte aligned. */
+qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, const float *x,
+                              int32_t n_embd, int32_t T, const uint16_t *Wq, const uint16_t *Wk,
+                              const uint16_t *Wv, const float *q_norm, const float *k_norm, float rms_eps,
+                              int32_t rope_dim, float rope_freq_base, float *Q_out, void *stream);
+
 /* ------------------------------------------------------------------ kernel C -------------- */
 
 /* Decode / MTP-verify attention for n_seq sequences, T (1..4) query tokens each.

@@ -54,6 +54,7 @@ def lib():
         L.orc_idx_score.restype = f32
         L.orc_idx_select.argtypes = [P, i32, P, i64, i32, P, P]
         L.orc_idx_select.restype = i64
+        L.orc_project.argtypes = [P, i32, i32, P, P, P, i32, i32, P, P, f32, i32, f32, i32, P, P, P]
         _lib = L
     return _lib
 
@@ -192,4 +193,25 @@ def idx_select(q: np.ndarray, pooled: np.ndarray, pos: int, k_blocks: int):
     blocks = np.empty(k_blocks, dtype=np.int32)
     n = lib().orc_idx_select(_p(q), q.shape[0], _p(pooled), pos, k_blocks, _p(scores), _p(blocks))
     return blocks[:n].copy(), scores[:whole]
+
+
+# ---- fused projections (decode) ------------------------------------------------------------------
+def project(x: np.ndarray, Wq, Wk: np.ndarray, Wv: np.ndarray, n_head: int, n_head_kv: int, q_norm, k_norm,
+            eps: float, rope_dim: int, freq_base: float, pos: int):
+    """x float32 [T, n_embd]; W* bf16 bits uint16 [rows, n_embd] (Wq may be None).  Returns
+    (Q [T, n_head, 256] or None, K [T, n_head_kv*256], V [T, n_head_kv*256]) float32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, n_embd = x.shape
+    Q = np.zeros((T, n_head, 256), np.float32) if Wq is not None else None
+    K = np.zeros((T, n_head_kv * 256), np.float32)
+    V = np.zeros_like(K)
+    wq = np.ascontiguousarray(Wq, dtype=np.uint16) if Wq is not None else None
+    qn = np.ascontiguousarray(q_norm, dtype=np.float32) if q_norm is not None else None
+    kn = np.ascontiguousarray(k_norm, dtype=np.float32)
+    wk = np.ascontiguousarray(Wk, dtype=np.uint16)
+    wv = np.ascontiguousarray(Wv, dtype=np.uint16)
+    lib().orc_project(_p(x), T, n_embd, _p(wq) if wq is not None else None, _p(wk), _p(wv), n_head, n_head_kv,
+                      _p(qn) if qn is not None else None, _p(kn), ctypes.c_float(eps), rope_dim,
+                      ctypes.c_float(freq_base), pos, _p(Q) if Q is not None else None, _p(K), _p(V))
+    return Q, K, V
 

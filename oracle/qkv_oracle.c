@@ -427,3 +427,92 @@ int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64
     return n;
 }
 
+/* ------------------------------------------------------------ projections ---- */
+
+static float bf16f(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* one head of 256 rows for T tokens: raw projection, then (kind < 2) norm + rope */
+static void project_head(const float *x, int T, int n_embd, const uint16_t *W, int64_t row0, int kind,
+                         const float *nw, float eps, int rope_dim, const float *cs, float *out, int64_t out_stride) {
+    const int HDIM = 256, D = n_embd / 8;
+    float y[4][256];
+    for (int t = 0; t < T; t++)
+        for (int r = 0; r < HDIM; r++) {
+            const uint16_t *w = W + (row0 + r) * (int64_t)n_embd;
+            float s = 0.0f;
+            for (int q = 0; q < 8; q++) {
+                float part = 0.0f;
+                for (int d = q * D; d < (q + 1) * D; d++) part = fmaf(bf16f(w[d]), x[(int64_t)t * n_embd + d], part);
+                s = q == 0 ? part : s + part;
+            }
+            y[t][r] = s;
+        }
+    const int half = rope_dim / 2;
+    for (int t = 0; t < T; t++) {
+        float o[256];
+        if (kind == 2) {
+            memcpy(o, y[t], sizeof o);
+        } else {
+            float ws[8];
+            for (int w = 0; w < 8; w++) {
+                float sq[32];
+                for (int l = 0; l < 32; l++) sq[l] = y[t][32 * w + l] * y[t][32 * w + l];
+                ws[w] = bfly32(sq);
+            }
+            float s = ws[0];
+            for (int w = 1; w < 8; w++) s = s + ws[w];
+            const float scale = 1.0f / sqrtf(s * (1.0f / 256) + eps);
+            float yb[256];
+            for (int r = 0; r < HDIM; r++) yb[r] = (y[t][r] * scale) * nw[r];
+            for (int r = 0; r < HDIM; r++) {
+                o[r] = yb[r];
+                if (r < half) {
+                    const float c = cs[(t * half + r) * 2], sn = cs[(t * half + r) * 2 + 1];
+                    o[r] = yb[r] * c - yb[r + half] * sn;
+                } else if (r < 2 * half) {
+                    const int i = r - half;
+                    const float c = cs[(t * half + i) * 2], sn = cs[(t * half + i) * 2 + 1];
+                    o[r] = yb[i] * sn + yb[r] * c;
+                }
+            }
+        }
+        memcpy(out + t * out_stride, o, sizeof o);
+    }
+}
+
+void orc_project(const float *x, int T, int n_embd, const uint16_t *Wq, const uint16_t *Wk, const uint16_t *Wv,
+                 int n_head, int n_head_kv, const float *q_norm, const float *k_norm, float eps, int rope_dim,
+                 float freq_base, int pos, float *Q_out, float *K_out, float *V_out) {
+    const int half = rope_dim / 2;
+    float *cs = (float *)malloc(sizeof(float) * 2 * (size_t)(T * (half > 0 ? half : 1)));
+    const float theta_scale = powf(freq_base, -2.0f / (float)(rope_dim > 0 ? rope_dim : 1));
+    for (int t = 0; t < T; t++) {
+        float th = (float)(pos + t);
+        for (int i = 0; i < half; i++) {
+            cs[(t * half + i) * 2] = cosf(th);
+            cs[(t * half + i) * 2 + 1] = sinf(th);
+            th *= theta_scale;
+        }
+    }
+    const int kvd = n_head_kv * 256;
+#pragma omp parallel for schedule(dynamic)
+    for (int u = 0; u < (Wq ? n_head : 0) + 2 * n_head_kv; u++) {
+        const int nq = Wq ? n_head : 0;
+        if (u < nq)
+            project_head(x, T, n_embd, Wq, (int64_t)u * 512, 0, q_norm, eps, rope_dim, cs, Q_out + u * 256,
+                         (int64_t)n_head * 256);
+        else if (u < nq + n_head_kv)
+            project_head(x, T, n_embd, Wk, (int64_t)(u - nq) * 256, 1, k_norm, eps, rope_dim, cs,
+                         K_out + (u - nq) * 256, kvd);
+        else
+            project_head(x, T, n_embd, Wv, (int64_t)(u - nq - n_head_kv) * 256, 2, NULL, eps, rope_dim, cs,
+                         V_out + (u - nq - n_head_kv) * 256, kvd);
+    }
+    free(cs);
+}
+

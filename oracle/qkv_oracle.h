@@ -141,6 +141,20 @@ float orc_idx_score(const float *q, int n_head, const uint16_t *pooled_b);
 int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64_t pos, int k_blocks,
                        float *scores, int32_t *blocks_out);
 
+/*
+ * Projections of new tokens (graph_builder::qsa_dec_qkv, src/qwfn_graph.cpp:582-608, with the
+ * rms() and rope() helpers of src/qwfn_graph.cpp:125-132), in the order the device kernel uses:
+ * per output row, dims split into 8 equal slices, each summed with fmaf in dim order from 0,
+ * the slices added in order; per head rms-norm with the squares summed as 8 warp butterflies
+ * added in warp order; y * (1/sqrtf(sum/256 + eps)) * w; NEOX-paired rope of the first rope_dim
+ * dims with angles theta_0 = p, theta_{i+1} = theta_i * powf(base, -2/rope_dim).  Weights are
+ * bf16 bits; Wq (nullable) holds query and gate rows interleaved per head (attn_q.weight).
+ * Outputs F32: Q [T][n_head][256], K and V [T][n_head_kv*256] (K normed and roped).
+ */
+void orc_project(const float *x, int T, int n_embd, const uint16_t *Wq, const uint16_t *Wk, const uint16_t *Wv,
+                 int n_head, int n_head_kv, const float *q_norm, const float *k_norm, float eps, int rope_dim,
+                 float freq_base, int pos, float *Q_out, float *K_out, float *V_out);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus

@@ -30,6 +30,7 @@ EXPORTS = [
     "qkv_store_create", "qkv_store_destroy", "qkv_store_save", "qkv_store_restore_or_reset",
     "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
     "qkv_indexer_enable", "qkv_idx_append", "qkv_idx_select", "qkv_attn_decode_qsa", "qkv_idx_read",
+    "qkv_project_append",
 ]
 
 
@@ -112,6 +113,7 @@ def lib() -> ctypes.CDLL:
         "qkv_idx_select": [P, I32, pI32, pI32, I32, P, I32, P, P, P, P],
         "qkv_attn_decode_qsa": [P, I32, pI32, pI32, I32, P, P, I32, F32, P, P],
         "qkv_idx_read": [P, I32, I32, I32, I32, P, I32, I32, P, P],
+        "qkv_project_append": [P, I32, I32, I32, P, I32, I32, P, P, P, P, P, F32, I32, F32, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -401,6 +403,14 @@ class Engine:
     def attn_prefill(self, layer: int, slot: int, pos0: int, Q, Tc: int, scale: float, out, stream=None) -> None:
         self._check(lib().qkv_attn_prefill(self.handle, layer, slot, pos0, _ptr(Q), Tc, scale, _ptr(out),
                                            _stream(stream)))
+
+    def project_append(self, layer: int, slot: int, pos: int, x, Wq, Wk, Wv, q_norm, k_norm, Q_out=None,
+                       rms_eps: float = 1e-6, rope_dim: int = 64, rope_freq_base: float = 1e7, stream=None) -> None:
+        """x: F32 [T, n_embd]; W*: bf16 bits (int16 tensors) [rows, n_embd]; Wq/q_norm/Q_out may be None."""
+        T, n_embd = int(x.shape[0]), int(x.shape[1])
+        self._check(lib().qkv_project_append(self.handle, layer, slot, pos, _ptr(x), n_embd, T, _ptr(Wq), _ptr(Wk),
+                                             _ptr(Wv), _ptr(q_norm), _ptr(k_norm), rms_eps, rope_dim, rope_freq_base,
+                                             _ptr(Q_out), _stream(stream)))
 
     # -- QSA lightning indexer ------------------------------------------------------------------
     def indexer_enable(self, n_head: int = 4, top_k: int = 2048, rope_dim: int = 64, rope_freq_base: float = 1e7,

@@ -557,6 +557,60 @@ extern "C" qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, i
     return QKV_OK;
 }
 
+extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos, const float *x,
+                                         int32_t n_embd, int32_t T, const uint16_t *Wq, const uint16_t *Wk,
+                                         const uint16_t *Wv, const float *q_norm, const float *k_norm, float rms_eps,
+                                         int32_t rope_dim, float rope_freq_base, float *Q_out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    qkv_status r;
+    if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    auto aligned = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
+    if (!x || !Wk || !Wv || !k_norm || (Wq && (!q_norm || !Q_out)) || T < 1 || T > PJ_MAX_T || n_embd < 64 ||
+        n_embd % 64 || n_embd > 8192 || rope_dim < 0 || rope_dim % 2 || rope_dim / 2 > PJ_MAX_HALF ||
+        !(rope_freq_base > 0.f) || !(rms_eps >= 0.f) || !aligned(x) || !aligned(Wk) || !aligned(Wv) ||
+        (Wq && !aligned(Wq)))
+        return fail(eng, QKV_ERR_INVALID, "project_append: T %d (1..%d), n_embd %d (multiple of 64, <= 8192), rope_dim %d, "
+                    "null or unaligned pointer", T, PJ_MAX_T, n_embd, rope_dim);
+    qkv_engine::Slot &sl = eng->slots[slot];
+    if (pos < 0 || pos > sl.n_past || (int64_t)pos + T > eng->cfg.n_ctx)
+        return fail(eng, QKV_ERR_INVALID, "project_append at %d: slot %d holds %d, n_ctx %d", pos, slot, sl.n_past, eng->cfg.n_ctx);
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if ((r = reserve(eng, slot, pos, T, st)) != QKV_OK) return r;
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    ProjectParams p;
+    memset(&p, 0, sizeof p);
+    p.pr = pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages);
+    p.x = x;
+    p.Wq = Wq;
+    p.Wk = Wk;
+    p.Wv = Wv;
+    p.q_norm = q_norm;
+    p.k_norm = k_norm;
+    p.Q_out = Q_out;
+    p.n_embd = n_embd;
+    p.T = T;
+    p.pos = pos;
+    p.n_head = eng->cfg.n_head;
+    p.n_head_kv = eng->cfg.n_head_kv;
+    p.rope_half = rope_dim / 2;
+    p.eps = rms_eps;
+    // angles as ggml's CPU rope cache builds them: theta_0 = p, one fp32 multiplication per pair
+    const float theta_scale = powf(rope_freq_base, -2.0f / (float)std::max(rope_dim, 1));
+    for (int t = 0; t < T; t++) {
+        float th = (float)(pos + t);
+        for (int i = 0; i < rope_dim / 2; i++) {
+            p.cs[t][i] = make_float2(cosf(th), sinf(th));
+            th *= theta_scale;
+        }
+    }
+    CK(eng, launch_project(p, st));
+    sl.n_past = std::max(sl.n_past, pos + T);
+    invalidate_summaries(eng, slot, pos);
+    return QKV_OK;
+}
+
 // ------------------------------------------------------------------------------------ decode
 // Plan one launch of kernel C for sequences [base, base+ns): every pair (sequence, KV head) is
 // cut into units in proportion to its tiles so that about two CTAs per SM carry equal work.

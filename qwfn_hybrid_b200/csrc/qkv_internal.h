@@ -70,6 +70,21 @@ struct PoolRef {
 
 cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const float *V, int32_t n_rows,
                           cudaStream_t st);
+
+// Fused projection + rms-norm + rope + q8_0 append for up to PJ_MAX_T tokens (one cluster of
+// PJ_CL CTAs per output head; see k_project).
+constexpr int PJ_CL = 8, PJ_MAX_T = 4, PJ_MAX_HALF = 64;
+struct ProjectParams {
+    PoolRef        pr;            // the slot's pages in the layer's pool
+    const float   *x;             // [T][n_embd]
+    const uint16_t *Wq, *Wk, *Wv; // bf16 weights, rows of n_embd; Wq: query/gate interleaved per head (nullable)
+    const float   *q_norm, *k_norm;   // [HD]
+    float         *Q_out;         // [T][n_head][HD] (with Wq)
+    int32_t n_embd, T, pos, n_head, n_head_kv, rope_half;
+    float   eps;
+    float2  cs[PJ_MAX_T][PJ_MAX_HALF];   // {cos, sin} of pair i at position pos + t
+};
+cudaError_t launch_project(const ProjectParams &p, cudaStream_t st);
 // cells == nullptr: rows pos .. pos+n-1
 cudaError_t launch_read_rows(const PoolRef &pr, const int32_t *cells, int32_t pos, int32_t n, uint8_t *K_out,
                              uint8_t *V_out, cudaStream_t st);

@@ -5,6 +5,7 @@
 // 16-byte vector accesses where the layout allows, grids sized from the SM count.
 #include "qkv_internal.h"
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 namespace qkv {
@@ -62,6 +63,128 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
     const int64_t warps = (int64_t)n_rows * pr.n_head_kv * NBLK;
     const int blocks = (int)((warps * 32 + 255) / 256);
     k_append<<<blocks, 256, 0, st>>>(pr, pos, K, V, n_rows);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------- fused projection + append
+// The decode-time projections of an attention layer (graph_builder::qsa_dec_qkv,
+// src/qwfn_graph.cpp:582-608) ahead of kernel A: for each new token t,
+//   Q_h = rope(rms_norm(Wq_h x_t) * q_norm),  K_h = rope(rms_norm(Wk_h x_t) * k_norm),  V_h = Wv_h x_t
+// (the reference's rms() and rope(), src/qwfn_graph.cpp:125-132), then K and V quantised to q8_0
+// into the page (kernel A's rounding).  Cluster u of PJ_CL CTAs computes output head u (query
+// heads first, then K heads, then V heads); CTA q of the cluster dots its slice of the input,
+// dims [q*D, (q+1)*D) with D = n_embd / PJ_CL, thread r owning row r of the head:
+//   part_q = fmaf(w, x, ...) over the slice in dim order (bf16 weights are exact in fp32)
+//   y      = ((part_0 + part_1) + part_2) + ...  (rank order, read by rank 0 through DSMEM)
+// rms-norm: per warp the xor butterfly of y^2, warp sums added in warp order, scale =
+// 1/sqrt(sum/256 + eps), y * scale * w; rope: pairs (i, i + half) as in kernel A's reference,
+// cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32 multiplication).
+constexpr int PJ_THREADS = HD;
+
+__device__ __forceinline__ float warp_sum_bfly(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__global__ void __cluster_dims__(PJ_CL, 1, 1) __launch_bounds__(PJ_THREADS) k_project(const ProjectParams p) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ float xs[];                       // [T][D] this CTA's slice of the inputs
+    __shared__ float part[PJ_MAX_T][HD];                // this CTA's partial dot of every row
+    __shared__ float yb[HD];
+    __shared__ float wsum[HD / 32];
+    const int q = (int)cluster.block_rank(), u = blockIdx.y, r = threadIdx.x, lane = r & 31, wid = r >> 5;
+    const int nq = p.Wq ? p.n_head : 0, T = p.T, D = p.n_embd / PJ_CL;
+    int kind, h;   // 0 query, 1 key, 2 value
+    if (u < nq) { kind = 0; h = u; }
+    else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
+    else { kind = 2; h = u - nq - p.n_head_kv; }
+    for (int i = r; i < T * D; i += blockDim.x) xs[i] = p.x[(int64_t)(i / D) * p.n_embd + q * D + i % D];
+    __syncthreads();
+    const uint16_t *W = kind == 0 ? p.Wq + ((int64_t)h * 2 * HD + r) * p.n_embd
+                                  : (kind == 1 ? p.Wk : p.Wv) + ((int64_t)h * HD + r) * p.n_embd;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(W + q * D);
+    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < D / 8; c++) {
+        const uint4 w = w4[c];
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float wf = __uint_as_float((e & 1) ? (wv[e >> 1] & 0xffff0000u) : (wv[e >> 1] << 16));
+#pragma unroll
+            for (int t = 0; t < PJ_MAX_T; t++)
+                if (t < T) acc[t] = __fmaf_rn(wf, xs[t * D + 8 * c + e], acc[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++)
+        if (t < T) part[t][r] = acc[t];
+    cluster.sync();                                      // every slice's partials are in place
+    float y[PJ_MAX_T];
+    if (q == 0)
+#pragma unroll
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            float s = part[t][r];
+            for (int k = 1; k < PJ_CL; k++) s = __fadd_rn(s, cluster.map_shared_rank(&part[0][0], k)[t * HD + r]);
+            y[t] = s;
+        }
+    cluster.sync();                                      // rank 0 has read every CTA's partials
+    if (q != 0) return;
+    for (int t = 0; t < T; t++) {
+        float o = y[t];
+        if (kind != 2) {                                 // rms-norm, weight, rope
+            float s2 = warp_sum_bfly(__fmul_rn(o, o));
+            if (lane == 0) wsum[wid] = s2;
+            __syncthreads();
+            float s = wsum[0];
+            for (int k = 1; k < HD / 32; k++) s = __fadd_rn(s, wsum[k]);
+            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, 1.0f / HD), p.eps)));
+            const float *nw = kind == 0 ? p.q_norm : p.k_norm;
+            yb[r] = __fmul_rn(__fmul_rn(o, scale), nw[r]);
+            __syncthreads();
+            const int hh = p.rope_half;
+            o = yb[r];
+            if (r < hh) {
+                const float2 c = p.cs[t][r];
+                o = __fsub_rn(__fmul_rn(yb[r], c.x), __fmul_rn(yb[r + hh], c.y));
+            } else if (r < 2 * hh) {
+                const float2 c = p.cs[t][r - hh];
+                o = __fadd_rn(__fmul_rn(yb[r - hh], c.y), __fmul_rn(yb[r], c.x));
+            }
+            __syncthreads();                             // yb and wsum reused by the next token
+        }
+        if (kind == 0) {
+            p.Q_out[((int64_t)t * p.n_head + h) * HD + r] = o;
+            continue;
+        }
+        const int32_t pp = p.pos + t;
+        uint8_t *tile = tile_ptr(p.pr, pp, h);
+        if (!tile) {
+            if (r == 0) atomicOr(p.pr.status, ST_BAD_PAGE);
+            continue;
+        }
+        int8_t qv;
+        __half dh;
+        quant_block_warp(o, lane, qv, dh);               // warp w holds q8_0 block w of the row
+        const int tt = pp & 63;
+        if (kind == 1) {
+            tile[k_off(tt, r)] = (uint8_t)qv;
+            if (lane == 0) *reinterpret_cast<__half *>(tile + kd_off(tt, wid)) = dh;
+        } else {
+            tile[v_off(r, tt)] = (uint8_t)qv;
+            if (lane == 0) *reinterpret_cast<__half *>(tile + vd_off(wid, tt)) = dh;
+        }
+    }
+}
+
+cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
+    const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv;
+    const size_t smem = (size_t)p.T * (p.n_embd / PJ_CL) * sizeof(float);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    k_project<<<dim3(PJ_CL, units), PJ_THREADS, smem, st>>>(p);
     count_launches(1);
     return cudaGetLastError();
 }

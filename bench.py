@@ -46,10 +46,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5", "qsa"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5", "qsa", "proj"], default="cfg2",
                     help="cfg2 (default, the headline line): BASELINE configs[1]; cfg3: configs[2] chunked "
                          "prefill; cfg5: configs[4]; qsa: configs[3]'s context and tokens through the model's own "
-                         "lightning indexer (select + gather + sparse attention)")
+                         "lightning indexer (select + gather + sparse attention); proj: the fused decode "
+                         "projections + norm + rope + q8_0 append of configs[1]'s step")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
@@ -811,6 +812,93 @@ def run_qsa(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+PJ_EMBD = 2560
+
+
+def run_proj(args) -> None:
+    """configs[1]'s step ahead of attention: per layer, the 3 tokens' query/key/value projections
+    (n_embd 2560 -> 16 query heads, 2 KV heads of 256, bf16 weights), rms-norm + rope of Q and K and
+    the q8_0 append of K and V, in one qkv_project_append call.  Weights of 12 layers (315 MB)
+    exceed L2, so every layer streams its weights from HBM."""
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import qwfn_hybrid_b200 as Q
+    steps, warm = args.steps, max(args.warmup, 3)
+    total = warm + steps
+    n_ctx = CTX0 + T * (total + 2)
+    eng = Q.Engine(n_layer=N_LAYER, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=n_ctx, n_slots=1, device=local)
+    eng.seq_alloc(0)
+    gen = torch.Generator(device=dev).manual_seed(7 + 1000 * rank)
+    s = PJ_EMBD ** -0.5
+    Wq = [(torch.randn(2 * N_HEAD * HD, PJ_EMBD, generator=gen, device=dev) * s).to(torch.bfloat16).view(torch.int16)
+          for _ in range(N_LAYER)]
+    Wk = [(torch.randn(N_HEAD_KV * HD, PJ_EMBD, generator=gen, device=dev) * s).to(torch.bfloat16).view(torch.int16)
+          for _ in range(N_LAYER)]
+    Wv = [(torch.randn(N_HEAD_KV * HD, PJ_EMBD, generator=gen, device=dev) * s).to(torch.bfloat16).view(torch.int16)
+          for _ in range(N_LAYER)]
+    qn = torch.ones(HD, device=dev)
+    kn = torch.ones(HD, device=dev)
+    X = torch.randn(total, N_LAYER, T, PJ_EMBD, generator=gen, device=dev)
+    Qo = torch.empty(N_LAYER, T, N_HEAD, HD, device=dev)
+    eng.reserve(0, n_ctx)
+    stream = torch.cuda.current_stream()
+
+    def step(i: int):
+        p = T * i
+        for l in range(N_LAYER):
+            eng.project_append(l, 0, p, X[i, l], Wq[l], Wk[l], Wv[l], qn, kn, Qo[l])
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = Q.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(warm + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = Q.launch_count() - launches0
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if eng.device_status() != 0:
+        raise RuntimeError("device status reported a bounds violation")
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    if rank != 0:
+        return
+    per_layer = (2 * N_HEAD * HD // 2 + 2 * N_HEAD_KV * HD) * PJ_EMBD * 2     # weight rows read (query, K, V)
+    per_layer += T * PJ_EMBD * 4 + T * N_HEAD * HD * 4 + 2 * T * ROW_BYTES    # x in, Q out, q8_0 rows out
+    hbm, hbm_src = 6650.0, "fallback 6650 GB/s"
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        hbm, hbm_src = json.load(open(pk)).get("hbm_gbs", hbm), "measured hbm_gbs"
+    ms_layer = ms / (steps * N_LAYER)
+    gbs = per_layer / (ms_layer * 1e-3) / 1e9
+    line = {
+        "metric": "fused decode projections + norm + rope + q8_0 append: µs per layer and GB/s of weights streamed",
+        "value": ms_layer * 1e3, "unit": "us/layer", "n_gpus": ws, "steps": steps, "warmup": warm,
+        "ms_per_step": ms / steps, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights, f32 accumulate / norm / rope, q8_0 K/V",
+        "data": "synthetic N(0, 1/n_embd) weights and N(0,1) inputs (torch Philox, seed 7+1000*rank)",
+        "config": {"workload": "configs[1]'s 3 tokens per step, 12 layers: n_embd 2560 -> 16 query heads (of the "
+                               "query/gate interleave), 2 K and 2 V heads of 256",
+                   "parallelism": f"independent sequences x{ws} (replicas, no collective)",
+                   "l2": "12 layers of weights (315 MB) exceed L2: each layer's 26 MB come from HBM"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_source": hbm_src, "traffic": None, "kernel": "k_project (one launch per layer)",
+                     "bytes_per_launch": per_layer},
+        "gpu_launches": launches, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 class _DevRange:
     """A device address range as a float32 tensor (CUDA array interface)."""
 
@@ -829,6 +917,8 @@ def main():
         run_cfg3(args)
     elif args.workload == "qsa":
         run_qsa(args)
+    elif args.workload == "proj":
+        run_proj(args)
     else:
         run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

@@ -122,7 +122,7 @@ qkv_status qkv_append(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos,
  * Replaces graph_builder::qsa_dec_qkv + qsa_dec_kv_write (src/qwfn_graph.cpp:582-628: the
  * projections, the reference's rms() and rope() helpers, src/qwfn_graph.cpp:125-132, and the
  * set_rows); the F32 K/V rows never reach memory.  x: device F32 [T][n_embd] (n_embd a multiple
- * of 64, <= 8192); Wq: device bf16 [2*n_head*head_dim][n_embd], query and gate rows interleaved per
+ * of 256, T * n_embd <= 12288; 2560 in the model); Wq: device bf16 [2*n_head*head_dim][n_embd], query and gate rows interleaved per
  * head as attn_q.weight is (NULL: no query); Wk, Wv: device bf16 [n_head_kv*head_dim][n_embd];
  * q_norm, k_norm: device F32 [head_dim]; rope: the first rope_dim dims of each head, NEOX pairs,
  * theta_i = p * freq_base^(-2i/rope_dim) (text positions); Q_out: device F32 [T][n_head][head_dim].

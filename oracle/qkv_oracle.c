@@ -439,18 +439,19 @@ static float bf16f(uint16_t b) {
 /* one head of 256 rows for T tokens: raw projection, then (kind < 2) norm + rope */
 static void project_head(const float *x, int T, int n_embd, const uint16_t *W, int64_t row0, int kind,
                          const float *nw, float eps, int rope_dim, const float *cs, float *out, int64_t out_stride) {
-    const int HDIM = 256, D = n_embd / 8;
+    const int HDIM = 256;
     float y[4][256];
     for (int t = 0; t < T; t++)
         for (int r = 0; r < HDIM; r++) {
             const uint16_t *w = W + (row0 + r) * (int64_t)n_embd;
-            float s = 0.0f;
-            for (int q = 0; q < 8; q++) {
-                float part = 0.0f;
-                for (int d = q * D; d < (q + 1) * D; d++) part = fmaf(bf16f(w[d]), x[(int64_t)t * n_embd + d], part);
-                s = q == 0 ? part : s + part;
+            float lanes[32];   /* lane l: chunks l, l+32, ... of 8 dims, in order */
+            for (int l = 0; l < 32; l++) {
+                float a = 0.0f;
+                for (int c = l; c < n_embd / 8; c += 32)
+                    for (int e = 0; e < 8; e++) a = fmaf(bf16f(w[8 * c + e]), x[(int64_t)t * n_embd + 8 * c + e], a);
+                lanes[l] = a;
             }
-            y[t][r] = s;
+            y[t][r] = bfly32(lanes);
         }
     const int half = rope_dim / 2;
     for (int t = 0; t < T; t++) {

@@ -144,8 +144,8 @@ int64_t orc_idx_select(const float *q, int n_head, const uint16_t *pooled, int64
 /*
  * Projections of new tokens (graph_builder::qsa_dec_qkv, src/qwfn_graph.cpp:582-608, with the
  * rms() and rope() helpers of src/qwfn_graph.cpp:125-132), in the order the device kernel uses:
- * per output row, dims split into 8 equal slices, each summed with fmaf in dim order from 0,
- * the slices added in order; per head rms-norm with the squares summed as 8 warp butterflies
+ * per output row, 32 lane sums -- lane l takes the 8-dim chunks l, l+32, ... in order, fmaf
+ * from 0 -- combined by an xor butterfly 16,8,4,2,1 (lane 0's value); per head rms-norm with the squares summed as 8 warp butterflies
  * added in warp order; y * (1/sqrtf(sum/256 + eps)) * w; NEOX-paired rope of the first rope_dim
  * dims with angles theta_0 = p, theta_{i+1} = theta_i * powf(base, -2/rope_dim).  Weights are
  * bf16 bits; Wq (nullable) holds query and gate rows interleaved per head (attn_q.weight).

@@ -106,6 +106,7 @@ struct qkv_engine {
     uint8_t  *d_vpool = nullptr;
     int32_t  *d_vbt = nullptr;
     int32_t   vpool_v = 0, dst_pages = 0;
+    float    *d_pj = nullptr;                 // qkv_project_append: raw projections [T][rows]
 };
 
 // ------------------------------------------------------------------------------------ helpers
@@ -318,6 +319,7 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_inout);
     cudaFree(eng->d_vpool);
     cudaFree(eng->d_vbt);
+    cudaFree(eng->d_pj);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
         if (ev) cudaEventDestroy(ev);
@@ -565,11 +567,11 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
     qkv_status r;
     if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
     auto aligned = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
-    if (!x || !Wk || !Wv || !k_norm || (Wq && (!q_norm || !Q_out)) || T < 1 || T > PJ_MAX_T || n_embd < 64 ||
-        n_embd % 64 || n_embd > 8192 || rope_dim < 0 || rope_dim % 2 || rope_dim / 2 > PJ_MAX_HALF ||
+    if (!x || !Wk || !Wv || !k_norm || (Wq && (!q_norm || !Q_out)) || T < 1 || T > PJ_MAX_T || n_embd < 256 ||
+        n_embd % 256 || (size_t)T * n_embd * 4 > 48 * 1024 || rope_dim < 0 || rope_dim % 2 || rope_dim / 2 > PJ_MAX_HALF ||
         !(rope_freq_base > 0.f) || !(rms_eps >= 0.f) || !aligned(x) || !aligned(Wk) || !aligned(Wv) ||
         (Wq && !aligned(Wq)))
-        return fail(eng, QKV_ERR_INVALID, "project_append: T %d (1..%d), n_embd %d (multiple of 64, <= 8192), rope_dim %d, "
+        return fail(eng, QKV_ERR_INVALID, "project_append: T %d (1..%d), n_embd %d (multiple of 256, T * n_embd <= 12288), rope_dim %d, "
                     "null or unaligned pointer", T, PJ_MAX_T, n_embd, rope_dim);
     qkv_engine::Slot &sl = eng->slots[slot];
     if (pos < 0 || pos > sl.n_past || (int64_t)pos + T > eng->cfg.n_ctx)
@@ -579,9 +581,12 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
     cudaStream_t st = S(stream);
     if ((r = reserve(eng, slot, pos, T, st)) != QKV_OK) return r;
     if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    const size_t y_bytes = (size_t)PJ_MAX_T * (2 * eng->cfg.n_head + 2 * eng->cfg.n_head_kv) * HD * sizeof(float);
+    if (!eng->d_pj && (r = dalloc(eng, eng->d_pj, y_bytes, "projection scratch")) != QKV_OK) return r;
     ProjectParams p;
     memset(&p, 0, sizeof p);
     p.pr = pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages);
+    p.y = eng->d_pj;
     p.x = x;
     p.Wq = Wq;
     p.Wk = Wk;

@@ -5,7 +5,6 @@
 // 16-byte vector accesses where the layout allows, grids sized from the SM count.
 #include "qkv_internal.h"
 
-#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 namespace qkv {
@@ -72,15 +71,20 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // src/qwfn_graph.cpp:582-608) ahead of kernel A: for each new token t,
 //   Q_h = rope(rms_norm(Wq_h x_t) * q_norm),  K_h = rope(rms_norm(Wk_h x_t) * k_norm),  V_h = Wv_h x_t
 // (the reference's rms() and rope(), src/qwfn_graph.cpp:125-132), then K and V quantised to q8_0
-// into the page (kernel A's rounding).  Cluster u of PJ_CL CTAs computes output head u (query
-// heads first, then K heads, then V heads); CTA q of the cluster dots its slice of the input,
-// dims [q*D, (q+1)*D) with D = n_embd / PJ_CL, thread r owning row r of the head:
-//   part_q = fmaf(w, x, ...) over the slice in dim order (bf16 weights are exact in fp32)
-//   y      = ((part_0 + part_1) + part_2) + ...  (rank order, read by rank 0 through DSMEM)
-// rms-norm: per warp the xor butterfly of y^2, warp sums added in warp order, scale =
-// 1/sqrt(sum/256 + eps), y * scale * w; rope: pairs (i, i + half) as in kernel A's reference,
-// cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32 multiplication).
-constexpr int PJ_THREADS = HD;
+// into the page (kernel A's rounding).  Two kernels chained by programmatic dependent launch:
+//
+// k_project_dot: a warp per row; lane l reads the row's 16-byte chunks l, l+32, ... (coalesced: a
+// warp load covers 512 contiguous bytes; the row is prefetched into L2 first), and sums
+//   lane_l = fmaf(w, x, ...) over its chunks in order, dims in order within a chunk
+// (bf16 weights are exact in fp32); y = xor butterfly 16, 8, 4, 2, 1 of the lane sums.  Rows in
+// the order: query heads (the query rows of attn_q.weight's per-head query/gate interleave), K
+// heads, V heads; y goes to scratch [T][rows].
+// k_project_post: a CTA per head: rms-norm (per warp the xor butterfly of y^2, warp sums added in
+// warp order, scale = 1/sqrt(sum/256 + eps), y * scale * w), rope on pairs (i, i + half) of the
+// first rope_dim dims with cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32
+// multiplication); the query to Q_out, K and V quantised into the page.
+constexpr int PJ_DOT_THREADS = 256, PJ_ROWS_CTA = PJ_DOT_THREADS / 32;   // a warp per row
+constexpr int PJ_BATCH = 5;    // 16-byte loads in flight per lane (after the row's L2 prefetch)
 
 __device__ __forceinline__ float warp_sum_bfly(float v) {
 #pragma unroll
@@ -88,55 +92,75 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
     return v;
 }
 
-__global__ void __cluster_dims__(PJ_CL, 1, 1) __launch_bounds__(PJ_THREADS) k_project(const ProjectParams p) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ float xs[];                       // [T][D] this CTA's slice of the inputs
-    __shared__ float part[PJ_MAX_T][HD];                // this CTA's partial dot of every row
+__global__ void __launch_bounds__(PJ_DOT_THREADS, 5) k_project_dot(const ProjectParams p) {
+    extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
+    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD, nc = p.n_embd / 8;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int g = blockIdx.x * (PJ_DOT_THREADS / 32) + wid;   // this warp's row (n_rows is a multiple of 8)
+    const uint16_t *W;
+    if (g < nq * HD) W = p.Wq + ((int64_t)(g / HD) * 2 * HD + g % HD) * p.n_embd;
+    else if (g < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g - nq * HD) * p.n_embd;
+    else W = p.Wv + (int64_t)(g - (nq + p.n_head_kv) * HD) * p.n_embd;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);
+    // the whole row is requested at once (into L2, no registers held), then read in batches
+    for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + c));
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
+        xs4[(i & 1) * T * nc + i / 2] = x4[i];
+    __syncthreads();
+    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
+        uint4 wb[PJ_BATCH];
+#pragma unroll
+        for (int j = 0; j < PJ_BATCH; j++) {
+            const int c = lane + 32 * (j0 + j);
+            wb[j] = c < nc ? __ldcs(w4 + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < PJ_BATCH; j++) {
+            const int c = lane + 32 * (j0 + j);
+            if (c >= nc) break;
+            const uint32_t wv[4] = {wb[j].x, wb[j].y, wb[j].z, wb[j].w};
+#pragma unroll
+            for (int t = 0; t < PJ_MAX_T; t++) {
+                if (t >= T) break;
+                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];
+                float a = acc[t];
+                a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
+                acc[t] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++) {
+        if (t >= T) break;
+        const float y = warp_sum_bfly(acc[t]);
+        if (lane == t) p.y[(int64_t)t * n_rows + g] = y;
+    }
+}
+
+__global__ void __launch_bounds__(HD) k_project_post(const ProjectParams p) {
     __shared__ float yb[HD];
     __shared__ float wsum[HD / 32];
-    const int q = (int)cluster.block_rank(), u = blockIdx.y, r = threadIdx.x, lane = r & 31, wid = r >> 5;
-    const int nq = p.Wq ? p.n_head : 0, T = p.T, D = p.n_embd / PJ_CL;
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the dot kernel's rows are complete
+    const int u = blockIdx.x, r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
+    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD;
     int kind, h;   // 0 query, 1 key, 2 value
     if (u < nq) { kind = 0; h = u; }
     else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
     else { kind = 2; h = u - nq - p.n_head_kv; }
-    for (int i = r; i < T * D; i += blockDim.x) xs[i] = p.x[(int64_t)(i / D) * p.n_embd + q * D + i % D];
-    __syncthreads();
-    const uint16_t *W = kind == 0 ? p.Wq + ((int64_t)h * 2 * HD + r) * p.n_embd
-                                  : (kind == 1 ? p.Wk : p.Wv) + ((int64_t)h * HD + r) * p.n_embd;
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(W + q * D);
-    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < D / 8; c++) {
-        const uint4 w = w4[c];
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const float wf = __uint_as_float((e & 1) ? (wv[e >> 1] & 0xffff0000u) : (wv[e >> 1] << 16));
-#pragma unroll
-            for (int t = 0; t < PJ_MAX_T; t++)
-                if (t < T) acc[t] = __fmaf_rn(wf, xs[t * D + 8 * c + e], acc[t]);
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++)
-        if (t < T) part[t][r] = acc[t];
-    cluster.sync();                                      // every slice's partials are in place
-    float y[PJ_MAX_T];
-    if (q == 0)
-#pragma unroll
-        for (int t = 0; t < PJ_MAX_T; t++) {
-            if (t >= T) break;
-            float s = part[t][r];
-            for (int k = 1; k < PJ_CL; k++) s = __fadd_rn(s, cluster.map_shared_rank(&part[0][0], k)[t * HD + r]);
-            y[t] = s;
-        }
-    cluster.sync();                                      // rank 0 has read every CTA's partials
-    if (q != 0) return;
     for (int t = 0; t < T; t++) {
-        float o = y[t];
+        float o = p.y[(int64_t)t * n_rows + u * HD + r];
         if (kind != 2) {                                 // rms-norm, weight, rope
-            float s2 = warp_sum_bfly(__fmul_rn(o, o));
+            const float s2 = warp_sum_bfly(__fmul_rn(o, o));
             if (lane == 0) wsum[wid] = s2;
             __syncthreads();
             float s = wsum[0];
@@ -181,12 +205,24 @@ __global__ void __cluster_dims__(PJ_CL, 1, 1) __launch_bounds__(PJ_THREADS) k_pr
 }
 
 cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
-    const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv;
-    const size_t smem = (size_t)p.T * (p.n_embd / PJ_CL) * sizeof(float);
+    const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv, n_rows = units * HD;
+    const size_t smem = (size_t)p.T * p.n_embd * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    k_project<<<dim3(PJ_CL, units), PJ_THREADS, smem, st>>>(p);
-    count_launches(1);
-    return cudaGetLastError();
+    k_project_dot<<<(n_rows + PJ_ROWS_CTA - 1) / PJ_ROWS_CTA, PJ_DOT_THREADS, smem, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(units);
+    cfg.blockDim = dim3(HD);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, k_project_post, p);
+    count_launches(2);
+    return e;
 }
 
 // --------------------------------------------------------------------- ggml-layout transforms

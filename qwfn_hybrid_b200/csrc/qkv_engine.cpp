@@ -582,11 +582,16 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
     if ((r = reserve(eng, slot, pos, T, st)) != QKV_OK) return r;
     if ((r = flush_tables(eng, st)) != QKV_OK) return r;
     const size_t y_bytes = (size_t)PJ_MAX_T * (2 * eng->cfg.n_head + 2 * eng->cfg.n_head_kv) * HD * sizeof(float);
-    if (!eng->d_pj && (r = dalloc(eng, eng->d_pj, y_bytes, "projection scratch")) != QKV_OK) return r;
+    const size_t cnt_bytes = (size_t)(2 * eng->cfg.n_head + 2 * eng->cfg.n_head_kv) * sizeof(int32_t);
+    if (!eng->d_pj) {
+        if ((r = dalloc(eng, eng->d_pj, y_bytes + cnt_bytes, "projection scratch")) != QKV_OK) return r;
+        CK(eng, cudaMemset(eng->d_pj, 0, y_bytes + cnt_bytes));   // the per-head counters start at zero
+    }
     ProjectParams p;
     memset(&p, 0, sizeof p);
     p.pr = pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages);
     p.y = eng->d_pj;
+    p.cnt = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(eng->d_pj) + y_bytes);
     p.x = x;
     p.Wq = Wq;
     p.Wk = Wk;

@@ -71,13 +71,13 @@ struct PoolRef {
 cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const float *V, int32_t n_rows,
                           cudaStream_t st);
 
-// Fused projection + rms-norm + rope + q8_0 append for up to PJ_MAX_T tokens (k_project_dot,
-// then k_project_post; n_embd a multiple of 256, T * n_embd floats within 48 KiB of shared memory).
+// Fused projection + rms-norm + rope + q8_0 append for up to PJ_MAX_T tokens (k_project_dot; n_embd a multiple of 256, T * n_embd floats within 48 KiB of shared memory).
 constexpr int PJ_MAX_T = 4, PJ_MAX_HALF = 64;
 struct ProjectParams {
     PoolRef        pr;            // the slot's pages in the layer's pool
     const float   *x;             // [T][n_embd]
     float         *y;             // scratch [T][rows]: the raw projections
+    int32_t       *cnt;           // scratch [heads]: CTAs done per head, zero between calls
     const uint16_t *Wq, *Wk, *Wv; // bf16 weights, rows of n_embd; Wq: query/gate interleaved per head (nullable)
     const float   *q_norm, *k_norm;   // [HD]
     float         *Q_out;         // [T][n_head][HD] (with Wq)

@@ -71,7 +71,7 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // src/qwfn_graph.cpp:582-608) ahead of kernel A: for each new token t,
 //   Q_h = rope(rms_norm(Wq_h x_t) * q_norm),  K_h = rope(rms_norm(Wk_h x_t) * k_norm),  V_h = Wv_h x_t
 // (the reference's rms() and rope(), src/qwfn_graph.cpp:125-132), then K and V quantised to q8_0
-// into the page (kernel A's rounding).  Two kernels chained by programmatic dependent launch:
+// into the page (kernel A's rounding).  One kernel:
 //
 // k_project_dot: a warp per row; lane l reads the row's 16-byte chunks l, l+32, ... (coalesced: a
 // warp load covers 512 contiguous bytes; the row is prefetched into L2 first), and sums
@@ -79,7 +79,7 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // (bf16 weights are exact in fp32); y = xor butterfly 16, 8, 4, 2, 1 of the lane sums.  Rows in
 // the order: query heads (the query rows of attn_q.weight's per-head query/gate interleave), K
 // heads, V heads; y goes to scratch [T][rows].
-// k_project_post: a CTA per head: rms-norm (per warp the xor butterfly of y^2, warp sums added in
+// Epilogue, run by the CTA that completes a head's rows (a per-head counter): rms-norm (per warp the xor butterfly of y^2, warp sums added in
 // warp order, scale = 1/sqrt(sum/256 + eps), y * scale * w), rope on pairs (i, i + half) of the
 // first rope_dim dims with cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32
 // multiplication); the query to Q_out, K and V quantised into the page.
@@ -92,73 +92,16 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
     return v;
 }
 
-__global__ void __launch_bounds__(PJ_DOT_THREADS, 5) k_project_dot(const ProjectParams p) {
-    extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
-    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD, nc = p.n_embd / 8;
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int g = blockIdx.x * (PJ_DOT_THREADS / 32) + wid;   // this warp's row (n_rows is a multiple of 8)
-    const uint16_t *W;
-    if (g < nq * HD) W = p.Wq + ((int64_t)(g / HD) * 2 * HD + g % HD) * p.n_embd;
-    else if (g < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g - nq * HD) * p.n_embd;
-    else W = p.Wv + (int64_t)(g - (nq + p.n_head_kv) * HD) * p.n_embd;
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);
-    // the whole row is requested at once (into L2, no registers held), then read in batches
-    for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + c));
-    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
-    for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
-        xs4[(i & 1) * T * nc + i / 2] = x4[i];
-    __syncthreads();
-    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
-    for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
-        uint4 wb[PJ_BATCH];
-#pragma unroll
-        for (int j = 0; j < PJ_BATCH; j++) {
-            const int c = lane + 32 * (j0 + j);
-            wb[j] = c < nc ? __ldcs(w4 + c) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int j = 0; j < PJ_BATCH; j++) {
-            const int c = lane + 32 * (j0 + j);
-            if (c >= nc) break;
-            const uint32_t wv[4] = {wb[j].x, wb[j].y, wb[j].z, wb[j].w};
-#pragma unroll
-            for (int t = 0; t < PJ_MAX_T; t++) {
-                if (t >= T) break;
-                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];
-                float a = acc[t];
-                a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
-                a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
-                a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
-                a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
-                a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
-                a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
-                a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
-                a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
-                acc[t] = a;
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++) {
-        if (t >= T) break;
-        const float y = warp_sum_bfly(acc[t]);
-        if (lane == t) p.y[(int64_t)t * n_rows + g] = y;
-    }
-}
-
-__global__ void __launch_bounds__(HD) k_project_post(const ProjectParams p) {
-    __shared__ float yb[HD];
-    __shared__ float wsum[HD / 32];
-    asm volatile("griddepcontrol.wait;" ::: "memory");   // the dot kernel's rows are complete
-    const int u = blockIdx.x, r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
+// Epilogue of head u by one CTA of HD threads, once all of the head's rows are in p.y.
+__device__ void project_epilogue(const ProjectParams &p, int u, float *yb, float *wsum) {
+    const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
     const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD;
     int kind, h;   // 0 query, 1 key, 2 value
     if (u < nq) { kind = 0; h = u; }
     else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
     else { kind = 2; h = u - nq - p.n_head_kv; }
     for (int t = 0; t < T; t++) {
-        float o = p.y[(int64_t)t * n_rows + u * HD + r];
+        float o = __ldcg(p.y + (int64_t)t * n_rows + u * HD + r);   // written by other CTAs: from L2
         if (kind != 2) {                                 // rms-norm, weight, rope
             const float s2 = warp_sum_bfly(__fmul_rn(o, o));
             if (lane == 0) wsum[wid] = s2;
@@ -204,25 +147,83 @@ __global__ void __launch_bounds__(HD) k_project_post(const ProjectParams p) {
     }
 }
 
+__global__ void __launch_bounds__(PJ_DOT_THREADS, 5) k_project_dot(const ProjectParams p) {
+    extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
+    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD, nc = p.n_embd / 8;
+    const int g = blockIdx.x * (PJ_DOT_THREADS / 32) + wid;   // this warp's row (every CTA full: 8 | 256)
+    const uint16_t *W;
+    if (g < nq * HD) W = p.Wq + ((int64_t)(g / HD) * 2 * HD + g % HD) * p.n_embd;
+    else if (g < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g - nq * HD) * p.n_embd;
+    else W = p.Wv + (int64_t)(g - (nq + p.n_head_kv) * HD) * p.n_embd;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);
+    // the whole row is requested at once (into L2, no registers held), then read in batches
+    for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + c));
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
+        xs4[(i & 1) * T * nc + i / 2] = x4[i];
+    __syncthreads();
+    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
+        uint4 wb[PJ_BATCH];
+#pragma unroll
+        for (int j = 0; j < PJ_BATCH; j++) {
+            const int c = lane + 32 * (j0 + j);
+            wb[j] = c < nc ? __ldcs(w4 + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < PJ_BATCH; j++) {
+            const int c = lane + 32 * (j0 + j);
+            if (c >= nc) break;
+            const uint32_t wv[4] = {wb[j].x, wb[j].y, wb[j].z, wb[j].w};
+#pragma unroll
+            for (int t = 0; t < PJ_MAX_T; t++) {
+                if (t >= T) break;
+                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];
+                float a = acc[t];
+                a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
+                acc[t] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++) {
+        if (t >= T) break;
+        const float y = warp_sum_bfly(acc[t]);
+        if (lane == t) {
+            p.y[(int64_t)t * n_rows + g] = y;
+            __threadfence();
+        }
+    }
+    // the CTA that completes a head's rows (HD / PJ_ROWS_CTA CTAs per head) runs its epilogue and
+    // resets the head's counter for the next call; nothing waits
+    __shared__ float yb[HD];
+    __shared__ float wsum[HD / 32];
+    __shared__ int s_last;
+    const int u = blockIdx.x * PJ_ROWS_CTA / HD;
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(p.cnt + u, 1) == HD / PJ_ROWS_CTA - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    project_epilogue(p, u, yb, wsum);
+    if (tid == 0) p.cnt[u] = 0;
+}
+
 cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
     const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv, n_rows = units * HD;
     const size_t smem = (size_t)p.T * p.n_embd * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    k_project_dot<<<(n_rows + PJ_ROWS_CTA - 1) / PJ_ROWS_CTA, PJ_DOT_THREADS, smem, st>>>(p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(units);
-    cfg.blockDim = dim3(HD);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, k_project_post, p);
-    count_launches(2);
-    return e;
+    k_project_dot<<<n_rows / PJ_ROWS_CTA, PJ_DOT_THREADS, smem, st>>>(p);
+    count_launches(1);
+    return cudaGetLastError();
 }
 
 // --------------------------------------------------------------------- ggml-layout transforms

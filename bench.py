@@ -111,6 +111,8 @@ class Clocks:
 def dist_init(backend: str):
     import torch.distributed as dist
     ws = int(os.environ.get("WORLD_SIZE", "1"))
+    # NCCL's own messages (its version line among them) go to stderr: stdout carries only the JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if ws > 1 and not dist.is_initialized():
         from datetime import timedelta
         dist.init_process_group(backend=backend, timeout=timedelta(seconds=180))

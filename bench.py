@@ -1,19 +1,27 @@
 #!/usr/bin/env python
-"""Benchmark of the q8_0 KV-cache attention path.
+"""Benchmark of the q8_0 KV-cache attention path (BASELINE.json configs[1] is the headline).
 
-Workload ("step"): MTP-verify decode over 12 full-attention layers, 16 query heads / 2 KV
-heads / head_dim 256, q8_0 KV at context 16384 growing by 3 per step; each layer appends the
-step's 3 K/V rows (kernel A) and runs causal verify attention for 3 query tokens (kernel C).
-Reported: tokens/s = 3 * steps / time.  Inputs are seeded N(0,1) synthetic data (the reference's
-model and prompts are not available); the 215 MB of KV a step reads exceeds the 126 MB L2, so
-no flush is needed between steps.
+Headline ("step"): MTP-verify decode over 12 full-attention layers, 16 query heads / 2 KV heads /
+head_dim 256, q8_0 KV at context 16384 growing by 3 per step; each layer appends the step's 3 K/V
+rows and runs causal verify attention for 3 query tokens, in one fused launch (plus the split-K
+merge).  Reported: tokens/s = 3 * steps / time, the median of 5 timed replays of one CUDA graph
+holding the K steps.  Inputs are seeded N(0,1) synthetic data, the same numbers in both arms
+(numpy SeedSequence(1)); the reference's model and prompts are not available.  The 215 MB of KV a
+step reads exceeds the 126 MB L2, so no flush is needed between steps.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+The same JSON line carries sub-records measured in the same run:
+  "ragged"   configs[4] at every N: 64 sequences LPT-sharded over the ranks, restored from an
+             8192-token shared-prefix snapshot, one 1-token decode over 12 layers per step
+             (aggregate tokens/s, per-rank time and GB/s, imbalance, restore latency);
+  "configs"  at N = 1: configs[0] (µs per decode step), configs[2] (chunked prefill, TFLOP/s) and
+             configs[3] (select + sparse decode at 73,728, bit-exact indices), each with its CPU
+             oracle timing.
 
-One process per GPU (torchrun for N > 1); sequences are independent, so every rank runs its
-own sequence with no collective on the data path (weak scaling); rank 0 prints one JSON line.
-`--impl reference` times the reference's CPU algorithm (the C restatement in oracle/, since
-ggml itself cannot be built here) on this host's cores.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+
+One process per GPU (torchrun for N > 1); sequences are independent, so there is no collective on
+the data path.  `--impl reference` times the reference's CPU algorithm (the C restatement in
+oracle/, since ggml itself cannot be built here) on this host's cores.
 """
 from __future__ import annotations
 
@@ -34,22 +42,26 @@ N_LAYER, N_HEAD, N_HEAD_KV, HD, T = 12, 16, 2, 256, 3
 CTX0 = 16384
 SCALE = 1.0 / 16.0
 ROW_BYTES = N_HEAD_KV * 272          # one q8_0 K (or V) row of all KV heads
+KV_DIM = N_HEAD_KV * HD
+REPLAYS = 5
 CONFIG = {"workload": "configs[1]: MTP-verify decode, 12 layers, ctx 16384 (+3/step), T=3, 16q/2kv x 256, q8_0 KV",
           "global_batch": 1, "seq_len": CTX0, "query_tokens": T, "layers": N_LAYER,
           "l2": "inputs larger than L2 (215 MB of KV read per step vs 126 MB L2)"}
+DATA = "synthetic N(0,1), numpy SeedSequence(1) (the same numbers in both arms); no model or prompts available"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5", "qsa", "proj"], default="cfg2",
-                    help="cfg2 (default, the headline line): BASELINE configs[1]; cfg3: configs[2] chunked "
-                         "prefill; cfg5: configs[4]; qsa: configs[3]'s context and tokens through the model's own "
-                         "lightning indexer (select + gather + sparse attention); proj: the fused decode "
+    ap.add_argument("--no-extras", action="store_true", help="headline only: skip the ragged and configs sub-records")
+    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "qsa", "proj"], default="cfg2",
+                    help="cfg2 (default, the headline line with its sub-records): BASELINE configs[1]; cfg1/cfg3/"
+                         "cfg4/cfg5: configs[0]/[2]/[3]/[4] alone; qsa: configs[3]'s context and tokens through the "
+                         "model's own lightning indexer (select + gather + sparse attention); proj: the fused decode "
                          "projections + norm + rope + q8_0 append of configs[1]'s step")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
@@ -119,78 +131,110 @@ def dist_init(backend: str):
     return int(os.environ.get("RANK", "0")), ws, int(os.environ.get("LOCAL_RANK", "0"))
 
 
-# ----------------------------------------------------------------------------- CPU baseline
-def cpu_config2_data(seed: int, n_kv: int):
-    """q8_0 caches of 12 layers (ggml row layout) via the oracle, plus per-step inputs."""
+# ----------------------------------------------------------------------------- shared helpers
+def host_threads() -> int:
+    """Cores this process may run on (torchrun sets OMP_NUM_THREADS=1; the CPU arms ignore it)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def peaks() -> dict:
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    p = json.load(open(pk)) if os.path.exists(pk) else {}
+    out = {"hbm": p.get("hbm_gbs") or 6650.0, "bf16": p.get("bf16_tflops") or 1590.0}
+    out["hbm_src"] = "measured (MEASURED_PEAKS.json hbm_gbs)" if p.get("hbm_gbs") else "fallback 6650 GB/s"
+    out["bf16_src"] = "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if p.get("bf16_tflops") else \
+        "fallback 1590 TFLOP/s"
+    return out
+
+
+def _normals(seed_seq, shape):
     import numpy as np
-    from oracle import oracle as O
-    r = np.random.default_rng(seed)
-    layers = []
-    for _ in range(N_LAYER):
-        K = O.quantize_rows(r.standard_normal((n_kv, N_HEAD_KV * HD), dtype=np.float32))
-        V = O.quantize_rows(r.standard_normal((n_kv, N_HEAD_KV * HD), dtype=np.float32))
-        layers.append((K, V))
-    return layers, r
+    return np.random.default_rng(seed_seq).standard_normal(shape, dtype=np.float32)
 
 
-def cpu_step(O, layers, r, n0: int, threads: int):
-    """One config-2 step on the CPU: per layer quantise-and-append 3 rows, then 3-token verify attention."""
+def cfg2_host_data(n_steps: int):
+    """configs[1]'s inputs, seed 1: the 16384-row K and V prefix of every layer (one child stream
+    each, generated in parallel) and, from the last child, every step's Q, new K and new V."""
     import numpy as np
-    for l, (K, V) in enumerate(layers):
-        kn = O.quantize_rows(r.standard_normal((T, N_HEAD_KV * HD), dtype=np.float32))
-        vn = O.quantize_rows(r.standard_normal((T, N_HEAD_KV * HD), dtype=np.float32))
-        K[n0:n0 + T] = kn
-        V[n0:n0 + T] = vn
-        Q = r.standard_normal((T, N_HEAD, HD), dtype=np.float32)
-        O.attn(Q, K, V, np.arange(n0, n0 + T, dtype=np.int32), N_HEAD_KV, SCALE, n_cells=n0 + T, threads=threads)
+    from concurrent.futures import ThreadPoolExecutor
+    ss = np.random.SeedSequence(1).spawn(2 * N_LAYER + 1)
+    with ThreadPoolExecutor(max(1, min(2 * N_LAYER, host_threads()))) as ex:
+        prefix = list(ex.map(lambda s: _normals(s, (CTX0, KV_DIM)), ss[:2 * N_LAYER]))
+    r = np.random.default_rng(ss[-1])
+    Qs = r.standard_normal((n_steps, N_LAYER, T, N_HEAD, HD), dtype=np.float32)
+    Ks = r.standard_normal((n_steps, N_LAYER, T, KV_DIM), dtype=np.float32)
+    Vs = r.standard_normal((n_steps, N_LAYER, T, KV_DIM), dtype=np.float32)
+    return [(prefix[2 * l], prefix[2 * l + 1]) for l in range(N_LAYER)], Qs, Ks, Vs
 
 
-def cpu_baseline(steps: int) -> dict:
-    from oracle import oracle as O
-    O.build()
-    threads = O.max_threads()
-    layers, r = cpu_config2_data(11, CTX0 + T * (steps + 1))
-    cpu_step(O, layers, r, CTX0, threads)        # warm
-    t0 = time.perf_counter()
-    for i in range(steps):
-        cpu_step(O, layers, r, CTX0 + T * (i + 1), threads)
-    dt = time.perf_counter() - t0
-    return {"value": T * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} full config-2 steps (12 layers x 3-token verify at ctx 16387+) after 1 warm step; "
-                      f"oracle/qkv_oracle.c, OpenMP over (token, head) rows, {threads} threads"}
+# ----------------------------------------------------------------------------- CPU arms (oracle)
+class CpuConfig2:
+    """configs[1] on the host's cores through the oracle: q8_0 caches of 12 layers in ggml's row
+    layout; a step quantises and writes the 3 new rows of every layer, then runs the 3-token verify."""
+
+    def __init__(self, prefix, Qs, Ks, Vs, threads: int):
+        import numpy as np
+        from oracle import oracle as O
+        O.build()
+        self.O, self.threads = O, threads
+        n = CTX0 + T * Qs.shape[0]
+        self.layers = []
+        for Kf, Vf in prefix:
+            K = np.zeros((n, ROW_BYTES), np.uint8)
+            V = np.zeros((n, ROW_BYTES), np.uint8)
+            K[:CTX0] = O.quantize_rows(Kf, threads)
+            V[:CTX0] = O.quantize_rows(Vf, threads)
+            self.layers.append((K, V))
+        self.Qs, self.Ks, self.Vs = Qs, Ks, Vs
+
+    def step(self, i: int):
+        import numpy as np
+        n0 = CTX0 + T * i
+        for l, (K, V) in enumerate(self.layers):
+            K[n0:n0 + T] = self.O.quantize_rows(self.Ks[i, l], self.threads)
+            V[n0:n0 + T] = self.O.quantize_rows(self.Vs[i, l], self.threads)
+            self.O.attn(self.Qs[i, l], K, V, np.arange(n0, n0 + T, dtype=np.int32), N_HEAD_KV, SCALE,
+                        n_cells=n0 + T, threads=self.threads)
+
+    def timed(self, first: int, steps: int) -> list[float]:
+        times = []
+        for i in range(first, first + steps):
+            t0 = time.perf_counter()
+            self.step(i)
+            times.append(time.perf_counter() - t0)
+        return times
 
 
 def run_reference(args) -> None:
     # the CPU arm needs no process group: rank 0 measures, the other ranks have nothing to do
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    from oracle import oracle as O
-    O.build()
-    threads = O.max_threads()
-    layers, r = cpu_config2_data(11, CTX0 + T * (args.warmup + args.steps + 1))
+    threads = host_threads()
+    total = args.warmup + args.steps
+    cpu = CpuConfig2(*cfg2_host_data(total), threads=threads)
     for i in range(args.warmup):
-        cpu_step(O, layers, r, CTX0 + T * i, threads)
-    times = []
-    for i in range(args.steps):
-        t0 = time.perf_counter()
-        cpu_step(O, layers, r, CTX0 + T * (args.warmup + i), threads)
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = T * args.steps / total
+        cpu.step(i)
+    times = cpu.timed(args.warmup, args.steps)
+    total_s = sum(times)
+    value = T * args.steps / total_s
     sample = (f"every step is a full config-2 step: 12 layers, each quantising 3 K/V rows to q8_0 and running "
               f"3-token causal verify attention at ctx {CTX0}+3*step; oracle/qkv_oracle.c (the reference's ggml CPU "
-              f"flash_attn_ext + quantize_row_q8_0 restated; ggml itself is not buildable here), {threads} threads")
+              f"flash_attn_ext + quantize_row_q8_0 restated; ggml itself is not buildable here), OpenMP with "
+              f"{threads} threads (the process's CPU affinity)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
-        "data": "synthetic N(0,1), numpy PCG64 seed 11", "config": CONFIG,
+        "data": DATA, "config": CONFIG,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-# ----------------------------------------------------------------------------- our arm
+# ----------------------------------------------------------------------------- our arm: configs[1]
 def load_traffic() -> tuple[float | None, str | None]:
     """DRAM bytes per decode launch from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "decode_cfg2_ncu.md")
@@ -202,29 +246,50 @@ def load_traffic() -> tuple[float | None, str | None]:
     return None, None
 
 
-def run_ours(args) -> None:
+def _barrier(ws: int, local: int):
     import torch
-    rank, ws, local = dist_init("nccl")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    if ws > 1:
+        torch.distributed.barrier(device_ids=[local])
+
+
+def _max_over_ranks(ws: int, dev, values: list[float]) -> list[float]:
+    import torch
+    if ws == 1:
+        return values
+    t = torch.tensor(values, device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _gather(ws: int, dev, values: list[float]) -> list[list[float]]:
+    """Every rank's `values` (same length on all ranks), in rank order."""
+    import torch
+    if ws == 1:
+        return [values]
+    t = torch.tensor(values, device=dev, dtype=torch.float64)
+    out = [torch.empty_like(t) for _ in range(ws)]
+    torch.distributed.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+def measure_cfg2(args, rank: int, ws: int, local: int) -> dict:
+    import numpy as np
+    import torch
     import qwfn_hybrid_b200 as Q
+    from oracle import oracle as O
+    dev = torch.device("cuda", local)
     steps, warm = args.steps, args.warmup
     total_steps = warm + steps
+    prefix, Qs, Ks, Vs = cfg2_host_data(total_steps)
     n_ctx = CTX0 + T * (total_steps + 8)
     eng = Q.Engine(n_layer=N_LAYER, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=n_ctx, n_slots=1, device=local)
     eng.seq_alloc(0)
-    gen = torch.Generator(device=dev).manual_seed(1 + 1000 * rank)
-    for l in range(N_LAYER):
-        for c in range(0, CTX0, 4096):
-            k = torch.randn(4096, N_HEAD_KV * HD, generator=gen, device=dev)
-            v = torch.randn(4096, N_HEAD_KV * HD, generator=gen, device=dev)
-            eng.append(l, 0, c, k, v)
+    for l, (Kf, Vf) in enumerate(prefix):
+        eng.append(l, 0, 0, torch.from_numpy(Kf).to(dev), torch.from_numpy(Vf).to(dev))
     torch.cuda.synchronize()
     snap = eng.snapshot_save(0)                  # the 16384-token prefix, restored for the e2e pass
     eng.reserve(0, CTX0 + T * total_steps)       # pages for every step: no host uploads while timing
-    Qd = torch.randn(total_steps, N_LAYER, T, N_HEAD, HD, generator=gen, device=dev)
-    Kd = torch.randn(total_steps, N_LAYER, T, N_HEAD_KV * HD, generator=gen, device=dev)
-    Vd = torch.randn(total_steps, N_LAYER, T, N_HEAD_KV * HD, generator=gen, device=dev)
+    Qd, Kd, Vd = (torch.from_numpy(a).to(dev) for a in (Qs, Ks, Vs))
     out = torch.empty(N_LAYER, T, N_HEAD, HD, device=dev)
 
     def step(i: int):
@@ -233,14 +298,10 @@ def run_ours(args) -> None:
         for l in range(N_LAYER):
             eng.append_attn_decode(l, [0], [n0], Kd[i, l], Vd[i, l], Qd[i, l], T, SCALE, out[l])
 
-    def barrier():
-        if ws > 1:
-            torch.distributed.barrier(device_ids=[local])
-
     for i in range(warm):
         step(i)
     torch.cuda.synchronize()
-    # The K timed steps, captured once as a CUDA graph (one kernel node per layer and step).
+    # The K timed steps, captured once as a CUDA graph (the kernels of every layer and step).
     graph = torch.cuda.CUDAGraph()
     launches0 = Q.launch_count()
     with torch.cuda.graph(graph):
@@ -249,38 +310,58 @@ def run_ours(args) -> None:
     launches = Q.launch_count() - launches0
     graph.replay()                               # untimed: the same steps, same bytes
     torch.cuda.synchronize()
-    barrier()
+    _barrier(ws, local)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     clocks = Clocks(local)
     clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    graph.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
+    region_ms = []
+    for _ in range(REPLAYS):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        region_ms.append(e0.elapsed_time(e1))
+    _barrier(ws, local)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
+    ms = statistics.median(region_ms)
     if eng.device_status() != 0:
         raise RuntimeError("device status reported a bounds violation")
     del graph
-    # algorithmic bytes of one launch: the q8_0 K and V rows it attends, Q and the new K/V rows
-    # read, the output and the appended q8_0 rows written
-    io_bytes = 2 * T * N_HEAD * HD * 4 + 2 * T * N_HEAD_KV * HD * 4 + 2 * T * ROW_BYTES
-    dec_bytes = [(CTX0 + T * (i + 1)) * 2 * ROW_BYTES + io_bytes for i in range(warm, total_steps)]
+    # ---- parity of the timed path: the last step's first and last layer against the oracle ----
+    last = total_steps - 1
+    n0 = CTX0 + T * last
+    outh = out.cpu().numpy()
+    parity = {"checked": "layers 0 and 11 of the last timed step (appended q8_0 rows bit-exact; attention vs "
+                         "oracle/qkv_oracle.c)", "atol": 2e-3, "rtol": 1e-3}
+    max_abs, ok = 0.0, True
+    for l in (0, N_LAYER - 1):
+        Kr = torch.empty((n0 + T, ROW_BYTES), dtype=torch.uint8, device=dev)
+        Vr = torch.empty_like(Kr)
+        eng.read_rows(l, 0, 0, n0 + T, Kr, Vr)
+        torch.cuda.synchronize()
+        Kh, Vh = Kr.cpu().numpy(), Vr.cpu().numpy()
+        rows_ok = bool(np.array_equal(Kh[n0:], O.quantize_rows(Ks[last, l])) and
+                       np.array_equal(Vh[n0:], O.quantize_rows(Vs[last, l])))
+        ref = O.attn(Qs[last, l], Kh, Vh, np.arange(n0, n0 + T, dtype=np.int32), N_HEAD_KV, SCALE,
+                     threads=host_threads())
+        err = np.abs(outh[l] - ref)
+        max_abs = max(max_abs, float(err.max()))
+        ok = ok and rows_ok and bool((err <= 2e-3 + 1e-3 * np.abs(ref)).all())
+    parity.update(max_abs=max_abs, ok=ok)
     # ---- e2e: the same steps through the public API with host buffers -----------------------
     # Each step's inputs (per layer: Q, K, V packed) come from pinned host memory and its outputs go
     # back, every step.  Within a step the copies overlap the attention: layers 0-5's inputs go first,
     # layers 6-11's are copied on a side stream while 0-5 run, and 0-5's outputs come back while
     # 6-11 run.  Nothing crosses steps (a decode step's inputs exist only once the step before ended).
     import ctypes
-    qn, kn = T * N_HEAD * HD, T * N_HEAD_KV * HD
+    qn, kn = T * N_HEAD * HD, T * KV_DIM
     rowf = qn + 2 * kn
-    Xh = torch.cat([Qd.reshape(total_steps, N_LAYER, qn), Kd.reshape(total_steps, N_LAYER, kn),
-                    Vd.reshape(total_steps, N_LAYER, kn)], dim=2).cpu().pin_memory()
-    outh = torch.empty(N_LAYER, T, N_HEAD, HD).pin_memory()
+    Xh = torch.from_numpy(np.concatenate([Qs.reshape(total_steps, N_LAYER, qn), Ks.reshape(total_steps, N_LAYER, kn),
+                                          Vs.reshape(total_steps, N_LAYER, kn)], axis=2)).pin_memory()
+    outh_p = torch.empty(N_LAYER, T, N_HEAD, HD).pin_memory()
     xd = torch.empty(N_LAYER, rowf, device=dev)
     eng.snapshot_load(snap, 0)
     # the C ABI as a C++ caller (a ggml custom op) uses it: raw device addresses, argument arrays
@@ -320,10 +401,10 @@ def run_ours(args) -> None:
         ev["doneB"].record(stream)
         with torch.cuda.stream(cs):
             cs.wait_event(ev["doneA"])
-            outh[:HALF].copy_(out[:HALF], non_blocking=True)
+            outh_p[:HALF].copy_(out[:HALF], non_blocking=True)
             ev["outA"].record(cs)
             cs.wait_event(ev["doneB"])
-            outh[HALF:].copy_(out[HALF:], non_blocking=True)
+            outh_p[HALF:].copy_(out[HALF:], non_blocking=True)
             ev["outB"].record(cs)
 
     for k in ev.values():
@@ -331,7 +412,7 @@ def run_ours(args) -> None:
     for i in range(warm):
         step_e2e(i)
     torch.cuda.synchronize()
-    barrier()
+    _barrier(ws, local)
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
@@ -340,45 +421,39 @@ def run_ours(args) -> None:
     stream.wait_event(ev["outB"])                            # the last step's outputs are on the host
     f1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    _barrier(ws, local)
     e2e_ms = f0.elapsed_time(f1)
-    # ---- max over ranks ---------------------------------------------------------------------
-    if ws > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
+    ms, e2e_ms = _max_over_ranks(ws, dev, [ms, e2e_ms])
     snap.release()
-    if rank != 0:
-        return
-    peaks = {}
-    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(pk):
-        peaks = json.load(open(pk))
-    hbm = peaks.get("hbm_gbs")
-    peak_note = "measured (MEASURED_PEAKS.json hbm_gbs)" if hbm else "fallback 6650 GB/s"
-    hbm = hbm or 6650.0
+    eng.close()
+    pk = peaks()
     ms_launch = ms / (steps * N_LAYER)
+    # algorithmic bytes of one launch: the q8_0 K and V rows it attends, Q and the new K/V rows
+    # read, the output and the appended q8_0 rows written
+    io_bytes = 2 * T * N_HEAD * HD * 4 + 2 * T * KV_DIM * 4 + 2 * T * ROW_BYTES
+    dec_bytes = [(CTX0 + T * (i + 1)) * 2 * ROW_BYTES + io_bytes for i in range(warm, total_steps)]
     achieved = statistics.mean(dec_bytes) / (ms_launch * 1e-3) / 1e9
     traffic, traffic_src = load_traffic()
     tokens = ws * T * steps
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": steps,
         "warmup": warm, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
-        "data": "synthetic N(0,1) (torch Philox, seed 1+1000*rank); no model or prompts available",
+        "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate", "data": DATA,
         "config": dict(CONFIG, parallelism=f"sequence-sharded x{ws} (independent sequence per GPU, no collective)",
-                       timing="the K steps replayed from one CUDA graph (per layer: the fused append+attention "
-                              "kernel and its split-K merge), device-resident inputs"),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "frac_of_8000": achieved / 8000.0, "peak_source": peak_note,
-                     "kernel": "k_decode (fused q8_0 append + split-K verify attention) and its k_decode_merge, "
-                               "per layer",
+                       timing=f"the K steps captured once as a CUDA graph (per layer: the fused append+attention "
+                              f"kernel and its split-K merge), device-resident inputs; the timed region is one "
+                              f"replay of the K steps, repeated {REPLAYS} times, median reported (max over ranks)",
+                       region_ms=[round(x, 4) for x in region_ms]),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm"], "frac_of_8000": achieved / 8000.0, "peak_source": pk["hbm_src"],
+                     "kernel": "k_decode (fused q8_0 append + split-K verify attention) and its merge, per layer",
                      "bytes_per_launch": statistics.mean(dec_bytes), "ms_per_launch": ms_launch,
                      "ms_per_launch_note": "graph time / layers: both kernels of a layer and the gaps between "
                                            "layers",
                      "traffic": traffic, "traffic_source": traffic_src},
+        "parity": parity,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": N_LAYER * (T * N_HEAD * HD * 4 + 2 * T * N_HEAD_KV * HD * 4),
+                "h2d_bytes_per_step": N_LAYER * (T * N_HEAD * HD * 4 + 2 * T * KV_DIM * 4),
                 "d2h_bytes_per_step": N_LAYER * T * N_HEAD * HD * 4,
                 "path": "qkv_append_attn_decode (C ABI, called through ctypes with raw device addresses as a C++ "
                         "caller would) per layer, no graph; every step copies its inputs in from pinned host "
@@ -388,11 +463,19 @@ def run_ours(args) -> None:
         "clocks": clk,
     }
     if ws == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(steps=24)
-    print(json.dumps(line), flush=True)
+        threads = host_threads()
+        cpu = CpuConfig2(prefix, Qs, Ks, Vs, threads)
+        cpu.step(0)
+        n_cpu = min(steps, 24)
+        times = cpu.timed(1, n_cpu)
+        line["cpu_baseline"] = {
+            "value": T * n_cpu / sum(times), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n_cpu} full config-2 steps of the same inputs (12 layers x 3-token verify at ctx 16387+) "
+                      f"after 1 warm step; oracle/qkv_oracle.c, OpenMP over (token, head) rows, {threads} threads"}
+    return line
 
 
-# ----------------------------------------------------------------------------- config 5
+# ----------------------------------------------------------------------------- configs[4] (ragged)
 PREFIX = 8192
 
 
@@ -403,16 +486,15 @@ def config5_contexts() -> list[int]:
     return [int(c) for c in np.floor(np.exp(r.uniform(np.log(1024), np.log(65536), 64)))]
 
 
-def run_cfg5(args) -> None:
-    """64 independent sequences sharded by slot (LPT on context), each starting from the
-    8192-token shared-prefix snapshot (its first min(8192, ctx-1) positions shared, recurrent state
-    of 36 DeltaNet layers copied), then one 1-token decode step over 12 layers per timed step."""
+def measure_ragged(args, rank: int, ws: int, local: int, n_seqs: int = 64) -> dict:
+    """the 64 sequences sharded by slot (LPT on context) over the ranks, each restored
+    from the 8192-token shared-prefix snapshot (its first min(8192, ctx-1) positions shared, recurrent
+    state of 36 DeltaNet layers copied), then one 1-token decode step over 12 layers per timed step.
+    Returns the whole-job record (identical on every rank)."""
     import torch
-    rank, ws, local = dist_init("nccl")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     import qwfn_hybrid_b200 as Q
-    ctx = config5_contexts()[:args.seqs]
+    dev = torch.device("cuda", local)
+    ctx = config5_contexts()[:n_seqs]
     owner = Q.shard_lpt(ctx, ws)
     mine = [i for i in range(len(ctx)) if owner[i] == rank]
     n = len(mine)
@@ -425,14 +507,12 @@ def run_cfg5(args) -> None:
     src = n   # the prefix slot
     eng.seq_alloc(src)
     for l in range(N_LAYER):
-        for c in range(0, PREFIX, 4096):
-            eng.append(l, src, c, torch.randn(4096, N_HEAD_KV * HD, generator=gen, device=dev),
-                       torch.randn(4096, N_HEAD_KV * HD, generator=gen, device=dev))
+        eng.append(l, src, 0, torch.randn(PREFIX, KV_DIM, generator=gen, device=dev),
+                   torch.randn(PREFIX, KV_DIM, generator=gen, device=dev))
     for l in range(36):
         for kind in (0, 1):
             ptr, nbytes = eng.state_ptr(src, l, kind)
-            view = torch.as_tensor(_DevRange(ptr, nbytes), device=dev)
-            view.copy_(torch.randn(nbytes // 4, generator=gen, device=dev))
+            torch.as_tensor(_DevRange(ptr, nbytes), device=dev).copy_(torch.randn(nbytes // 4, generator=gen, device=dev))
     snap = eng.snapshot_save(src)
     slots = list(range(n))
     keep = [min(PREFIX, c - 1) for c in my_ctx]
@@ -447,17 +527,19 @@ def run_cfg5(args) -> None:
     torch.cuda.synchronize()
     restore_ms = r0.elapsed_time(r1)
     rec_bytes = 36 * (128 * 128 * 32 * 4 + 3 * 8192 * 4)
-    # each sequence's own positions beyond the shared prefix, up to ctx - 1
+    # each sequence's own positions beyond the shared prefix, up to ctx - 1 (random rows drawn once
+    # per chunk size and reused: their values do not change the work)
+    pool_k = torch.randn(8192, KV_DIM, generator=gen, device=dev)
+    pool_v = torch.randn(8192, KV_DIM, generator=gen, device=dev)
     for s_, c in zip(slots, my_ctx):
         eng.reserve(s_, c + 1)
         for l in range(N_LAYER):
             for p0 in range(keep[s_], c - 1, 8192):
                 m = min(8192, c - 1 - p0)
-                eng.append(l, s_, p0, torch.randn(m, N_HEAD_KV * HD, generator=gen, device=dev),
-                           torch.randn(m, N_HEAD_KV * HD, generator=gen, device=dev))
+                eng.append(l, s_, p0, pool_k[:m], pool_v[:m])
     Qd = torch.randn(N_LAYER, n, 1, N_HEAD, HD, generator=gen, device=dev)
-    Kd = torch.randn(N_LAYER, n, 1, N_HEAD_KV * HD, generator=gen, device=dev)
-    Vd = torch.randn(N_LAYER, n, 1, N_HEAD_KV * HD, generator=gen, device=dev)
+    Kd = torch.randn(N_LAYER, n, 1, KV_DIM, generator=gen, device=dev)
+    Vd = torch.randn(N_LAYER, n, 1, KV_DIM, generator=gen, device=dev)
     out = torch.empty(N_LAYER, n, 1, N_HEAD, HD, device=dev)
     pos = [c - 1 for c in my_ctx]
 
@@ -465,17 +547,11 @@ def run_cfg5(args) -> None:
         for l in range(N_LAYER):
             eng.append_attn_decode(l, slots, pos, Kd[l], Vd[l], Qd[l], 1, SCALE, out[l])
 
-    def barrier():
-        if ws > 1:
-            torch.distributed.barrier(device_ids=[local])
-
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    barrier()
+    _barrier(ws, local)
     torch.cuda.synchronize()
-    clocks = Clocks(local)
-    clocks.start()
     launches0 = Q.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -484,48 +560,260 @@ def run_cfg5(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     launches = Q.launch_count() - launches0
-    barrier()
-    clk = clocks.stop()
+    _barrier(ws, local)
     ms = e0.elapsed_time(e1)
     if eng.device_status() != 0:
         raise RuntimeError("device status reported a bounds violation")
     kv_bytes = sum(my_ctx) * N_LAYER * 2 * ROW_BYTES
-    io_bytes = N_LAYER * n * (2 * N_HEAD * HD * 4 + 2 * N_HEAD_KV * HD * 4 + 2 * ROW_BYTES)
-    gbs_local = (kv_bytes + io_bytes) * args.steps / (ms * 1e-3) / 1e9
-    if ws > 1:
-        t = torch.tensor([ms, restore_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, restore_ms = t.tolist()
-        g = torch.tensor([gbs_local], device=dev)
-        torch.distributed.all_reduce(g, op=torch.distributed.ReduceOp.SUM)
-        gbs_total = g.item()
-    else:
-        gbs_total = gbs_local
+    io_bytes = N_LAYER * n * (2 * N_HEAD * HD * 4 + 2 * KV_DIM * 4 + 2 * ROW_BYTES)
+    step_bytes = kv_bytes + io_bytes
+    per_rank = _gather(ws, dev, [ms, restore_ms, float(step_bytes), float(n), float(sum(my_ctx))])
     snap.release()
+    eng.close()
+    hbm = peaks()
+    rank_ms = [p[0] for p in per_rank]
+    rank_gbs = [p[2] * args.steps / (p[0] * 1e-3) / 1e9 for p in per_rank]
+    t_max = max(rank_ms)
+    return {
+        "workload": f"configs[4]: {len(ctx)} ragged sequences (ctx 1219..61356, sum {sum(ctx)}), 12 layers, paged "
+                    f"256-token pages, restored from an 8192-token shared-prefix snapshot, T=1, one fused append + "
+                    f"decode launch per layer",
+        "parallelism": f"strong scaling: the {len(ctx)} sequences LPT-sharded by context over {ws} rank(s), no "
+                       f"collective", "scaling": "strong",
+        "value": len(ctx) * args.steps / (t_max * 1e-3), "unit": "tokens/s", "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+        "per_rank": [{"rank": i, "seqs": int(p[3]), "tokens": int(p[4]), "ms_per_step": p[0] / args.steps,
+                      "gbs": g, "frac": g / hbm["hbm"]} for i, (p, g) in enumerate(zip(per_rank, rank_gbs))],
+        "imbalance_max_over_min": max(rank_ms) / min(rank_ms),
+        "roofline": {"bound": "hbm", "achieved": statistics.mean(rank_gbs), "peak": hbm["hbm"], "unit": "GB/s",
+                     "frac": statistics.mean(rank_gbs) / hbm["hbm"], "peak_source": hbm["hbm_src"],
+                     "note": "per-GPU GB/s (mean over ranks) of the KV, query, output and appended bytes"},
+        "snapshot_restore": {"ms_max_over_ranks": max(p[1] for p in per_rank),
+                             "slots_per_rank_max": int(max(p[3] for p in per_rank)),
+                             "recurrent_bytes_per_slot": rec_bytes},
+        "gpu_launches_per_rank0": launches,
+    }
+
+
+def run_cfg5(args) -> None:
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    clocks = Clocks(local)
+    clocks.start()
+    r = measure_ragged(args, rank, ws, local, n_seqs=args.seqs)
+    clk = clocks.stop()
     if rank != 0:
         return
-    hbm, hbm_src = 6650.0, "fallback 6650 GB/s"
-    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(pk) and json.load(open(pk)).get("hbm_gbs"):
-        hbm, hbm_src = json.load(open(pk))["hbm_gbs"], "measured (MEASURED_PEAKS.json hbm_gbs)"
-    per_gpu = gbs_total / ws
     print(json.dumps({
-        "metric": METRIC, "value": len(ctx) * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
+        "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 dot + f32 softmax/accumulate",
         "data": "synthetic N(0,1) (torch Philox, seed 4+1000*rank); contexts from numpy default_rng(4)",
-        "config": {"workload": f"configs[4]: {len(ctx)} of 64 ragged sequences (ctx 1219..61356, sum 1300814 for all "
-                               "64), 12 layers, paged 256-token pages, 8192-token shared-prefix snapshot, T=1",
-                   "parallelism": f"sequence-sharded x{ws} (LPT by context, no collective)",
+        "config": {"workload": r["workload"], "parallelism": r["parallelism"],
                    "l2": "inputs larger than L2 (17 GB of KV per step)"},
-        "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,
-                     "frac_of_8000": per_gpu / 8000.0, "peak_source": hbm_src,
-                     "kernel": "k_decode (and k_decode_merge for split pairs), per layer over all sequences"},
-        "snapshot_restore": {"ms": restore_ms, "slots_per_gpu_max": max(sum(1 for o in owner if o == r) for r in range(ws)),
-                             "recurrent_bytes_per_slot": rec_bytes,
-                             "copy_gbs": 2 * rec_bytes * n / (restore_ms * 1e-3) / 1e9 if restore_ms > 0 else None},
-        "gpu_launches": launches, "clocks": clk,
+        "roofline": r["roofline"], "ragged": r, "gpu_launches": r["gpu_launches_per_rank0"], "clocks": clk,
     }), flush=True)
+
+
+# ----------------------------------------------------------------------------- configs[0]
+def measure_cfg1(args, local: int) -> dict:
+    """4096 cached rows, then a step appends the token's K/V and attends for its one
+    query (seed 0: K [4097, 512], V [4097, 512], Q [16, 256] from numpy default_rng(0)).  A step is
+    one fused launch (+ merge); it is captured as a CUDA graph and replayed K times per timed region."""
+    import numpy as np
+    import torch
+    import qwfn_hybrid_b200 as Q
+    from oracle import oracle as O
+    dev = torch.device("cuda", local)
+    r = np.random.default_rng(0)
+    n = 4097
+    Kf = r.standard_normal((n, KV_DIM), dtype=np.float32)
+    Vf = r.standard_normal((n, KV_DIM), dtype=np.float32)
+    Qf = r.standard_normal((1, N_HEAD, HD), dtype=np.float32)
+    eng = Q.Engine(n_layer=1, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=4352, n_slots=1, device=local)
+    eng.seq_alloc(0)
+    eng.append(0, 0, 0, torch.from_numpy(Kf[:n - 1]).to(dev), torch.from_numpy(Vf[:n - 1]).to(dev))
+    eng.reserve(0, n)
+    kd, vd, qd = (torch.from_numpy(a).to(dev) for a in (Kf[n - 1:], Vf[n - 1:], Qf))
+    out = torch.empty(1, N_HEAD, HD, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        eng.append_attn_decode(0, [0], [n - 1], kd, vd, qd, 1, SCALE, out)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        eng.append_attn_decode(0, [0], [n - 1], kd, vd, qd, 1, SCALE, out)
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    per_step = []
+    for _ in range(REPLAYS):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per_step.append(e0.elapsed_time(e1) / args.steps)
+    del graph
+    assert eng.device_status() == 0
+    Kr = torch.empty((n, ROW_BYTES), dtype=torch.uint8, device=dev)
+    Vr = torch.empty_like(Kr)
+    eng.read_rows(0, 0, 0, n, Kr, Vr)
+    torch.cuda.synchronize()
+    Kq, Vq = O.quantize_rows(Kf), O.quantize_rows(Vf)
+    rows_ok = bool(np.array_equal(Kr.cpu().numpy(), Kq) and np.array_equal(Vr.cpu().numpy(), Vq))
+    threads = host_threads()
+    ref = O.attn(Qf, Kq, Vq, [n - 1], N_HEAD_KV, SCALE, threads=threads)
+    err = np.abs(out.cpu().numpy() - ref)
+    eng.close()
+    # the same step on the host's cores: quantise the new row, then the 16-head attention
+    cpu = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        O.quantize_rows(Kf[n - 1:], threads)
+        O.quantize_rows(Vf[n - 1:], threads)
+        O.attn(Qf, Kq, Vq, [n - 1], N_HEAD_KV, SCALE, threads=threads)
+        cpu.append(time.perf_counter() - t0)
+    us = 1e3 * statistics.median(per_step)
+    algo = n * 2 * ROW_BYTES + 2 * N_HEAD * HD * 4 + 2 * KV_DIM * 4 + 2 * ROW_BYTES
+    pk = peaks()
+    return {"workload": "configs[0]: 1 layer, 4096 cached + 1 appended, T=1, seed 0, one fused append + decode",
+            "us_per_step": us, "tokens_per_s": 1e6 / us,
+            "roofline": {"bound": "hbm (launch-bound at this size)", "achieved": algo / (us * 1e-6) / 1e9,
+                         "peak": pk["hbm"], "unit": "GB/s", "frac": algo / (us * 1e-6) / 1e9 / pk["hbm"],
+                         "bytes_per_step": algo},
+            "parity": {"rows_bit_exact": rows_ok, "max_abs": float(err.max()),
+                       "ok": rows_ok and bool((err <= 2e-3 + 1e-3 * np.abs(ref)).all())},
+            "cpu_baseline": {"value": 1e6 * statistics.median(cpu), "unit": "us/step", "cores": threads,
+                             "kind": "port", "sample": "20 steps of the same inputs (quantise the new K/V row + "
+                                                       "16-head attention over 4097 cells), median"}}
+
+
+# ----------------------------------------------------------------------------- configs[3]
+SP_CTX, SP_BLK, SP_TOPK = 73728, 64, 32
+
+
+def cfg4_host_data():
+    """seed 3: K = N(0,1) + an offset of variance 2 drawn per 64-token block and KV head (added to
+    all 256 dims), V = N(0,1); then the step's Q [3, 16, 256]."""
+    import numpy as np
+    r = np.random.default_rng(3)
+    nb = SP_CTX // SP_BLK
+    off = (r.standard_normal((nb, N_HEAD_KV, 1), dtype=np.float32) * np.float32(np.sqrt(2.0)))
+    Kf = (r.standard_normal((nb, SP_BLK, N_HEAD_KV, HD), dtype=np.float32) + off[:, None]).reshape(SP_CTX, KV_DIM)
+    Vf = r.standard_normal((SP_CTX, KV_DIM), dtype=np.float32)
+    Qf = r.standard_normal((T, N_HEAD, HD), dtype=np.float32)
+    return Kf, Vf, Qf
+
+
+def measure_cfg4(args, local: int) -> dict:
+    """a step appends its 3 tokens' K/V rows (positions 73725..73727), scores the 1152
+    64-token blocks per KV head against the 3 query tokens, keeps the top 32 (block 0 and the last
+    two forced) and attends to the selected blocks in place."""
+    import numpy as np
+    import torch
+    import qwfn_hybrid_b200 as Q
+    from oracle import oracle as O
+    dev = torch.device("cuda", local)
+    Kf, Vf, Qf = cfg4_host_data()
+    p0 = SP_CTX - T
+    eng = Q.Engine(n_layer=1, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=SP_CTX, n_slots=1, select_block=SP_BLK,
+                   device=local)
+    eng.seq_alloc(0)
+    for c in range(0, p0, 8192):
+        m = min(8192, p0 - c)
+        eng.append(0, 0, c, torch.from_numpy(Kf[c:c + m]).to(dev), torch.from_numpy(Vf[c:c + m]).to(dev))
+    eng.reserve(0, SP_CTX)
+    kd, vd, qd = (torch.from_numpy(a).to(dev) for a in (Kf[p0:], Vf[p0:], Qf))
+    idx = torch.empty((1, N_HEAD_KV, SP_TOPK), dtype=torch.int32, device=dev)
+    out = torch.empty(T, N_HEAD, HD, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        eng.append(0, 0, p0, kd, vd)
+        if ev:
+            ev[0].record(stream)
+        eng.select_blocks(0, [0], [p0], qd, T, SP_TOPK, idx)
+        eng.attn_decode(0, [0], [p0], qd, T, SCALE, out, sel=idx, n_sel=SP_TOPK)
+        if ev:
+            ev[1].record(stream)
+
+    for _ in range(max(args.warmup, 3)):     # the first select computes the 1150 whole-block summaries
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    assert eng.device_status() == 0
+    sel_us = 1e3 * statistics.median(a.elapsed_time(b) for a, b in evs)
+    step_us = 1e3 * t0.elapsed_time(t1) / args.steps
+    Kr = torch.empty((SP_CTX, ROW_BYTES), dtype=torch.uint8, device=dev)
+    Vr = torch.empty_like(Kr)
+    eng.read_rows(0, 0, 0, SP_CTX, Kr, Vr)
+    torch.cuda.synchronize()
+    Kq, Vq = Kr.cpu().numpy(), Vr.cpu().numpy()
+    got_idx, got = idx.cpu().numpy()[0], out.cpu().numpy()
+    eng.close()
+    threads = host_threads()
+    nb = SP_CTX // SP_BLK
+    rows_ok = bool(np.array_equal(Kq, O.quantize_rows(Kf, threads)) and np.array_equal(Vq, O.quantize_rows(Vf, threads)))
+    summ = np.zeros((N_HEAD_KV, nb, HD), np.uint16)
+    summ[:, :nb - 2] = O.block_summary(Kq, N_HEAD_KV, HD, SP_BLK, nb - 2, threads)
+    c0 = time.perf_counter()
+    ref_idx, _ = O.select_blocks(Qf, N_HEAD_KV, summ, nb, SP_TOPK)
+    cells = [O.blocks_to_cells(ref_idx[h], SP_BLK, SP_CTX) for h in range(N_HEAD_KV)]
+    ref = O.attn_sparse(Qf, Kq, Vq, np.arange(p0, SP_CTX), N_HEAD_KV, SCALE, cells, threads=threads)
+    cpu_us = 1e6 * (time.perf_counter() - c0)
+    err = np.abs(got - ref)
+    algo = N_HEAD_KV * (nb - 2) * HD * 2 + N_HEAD_KV * SP_TOPK * SP_BLK * 2 * 272 + N_HEAD_KV * SP_TOPK * 4 \
+        + 2 * T * N_HEAD * HD * 4
+    pk = peaks()
+    return {"workload": "configs[3]: ctx 73728 (1152 blocks of 64), seed 3 (K offset variance 2 per block and KV "
+                        "head), T=3; per step: append 3 rows, score + top-32 per KV head (block 0 and the last two "
+                        "forced), sparse attention over the 2048 selected tokens read in place",
+            "us_per_select_attend": sel_us, "us_per_step_with_append": step_us,
+            "tokens_per_s": T * 1e6 / step_us,
+            "roofline": {"bound": "hbm (latency-bound)", "achieved": algo / (sel_us * 1e-6) / 1e9, "peak": pk["hbm"],
+                         "unit": "GB/s", "frac": algo / (sel_us * 1e-6) / 1e9 / pk["hbm"],
+                         "bytes_per_select_attend": algo},
+            "parity": {"indices_bit_exact": bool(np.array_equal(got_idx, ref_idx)), "rows_bit_exact": rows_ok,
+                       "max_abs": float(err.max()),
+                       "ok": bool(np.array_equal(got_idx, ref_idx)) and rows_ok and
+                       bool((err <= 2e-3 + 1e-3 * np.abs(ref)).all())},
+            "cpu_baseline": {"value": cpu_us, "unit": "us/select+attend", "cores": threads, "kind": "port",
+                             "sample": "one select (1150 scored summaries per KV head, top-32) + sparse attention "
+                                       "over the 2048 selected cells of 3 tokens x 16 heads"}}
+
+
+def run_single(args, fn) -> None:
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    if rank == 0:
+        print(json.dumps(fn(args, local)), flush=True)
+
+
+# ----------------------------------------------------------------------------- the default line
+def run_ours(args) -> None:
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    line = measure_cfg2(args, rank, ws, local)
+    if not args.no_extras:
+        line["ragged"] = measure_ragged(args, rank, ws, local)
+        if ws == 1:
+            extras = {"configs[0]": measure_cfg1(args, local)}
+            c3 = measure_cfg3(args, rank, ws, local, e2e=False)
+            extras["configs[2]"] = c3
+            extras["configs[3]"] = measure_cfg4(args, local)
+            line["configs"] = extras
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- config 3
@@ -542,7 +830,7 @@ def cpu_prefill_baseline(chunks=(8, 15, 16, 23)) -> dict:
     import numpy as np
     from oracle import oracle as O
     O.build()
-    threads = O.max_threads()
+    threads = host_threads()
     r = np.random.default_rng(2)
     n_kv = (max(chunks) + 1) * PF_C
     K = O.quantize_rows(r.standard_normal((n_kv, N_HEAD_KV * HD), dtype=np.float32), threads)
@@ -560,12 +848,19 @@ def cpu_prefill_baseline(chunks=(8, 15, 16, 23)) -> dict:
 
 
 def run_cfg3(args) -> None:
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    line = measure_cfg3(args, rank, ws, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_cfg3(args, rank: int, ws: int, local: int, e2e: bool = True) -> dict:
     """a 16384-token prompt prefilled in 32 chunks of 512 on one layer; every chunk
     appends its 512 K/V rows (kernel A) and runs causal attention of its bf16 queries over the whole
     cache so far (kernel D, tcgen05).  One step = the whole prompt."""
     import torch
-    rank, ws, local = dist_init("nccl")
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import qwfn_hybrid_b200 as Q
     gen = torch.Generator(device=dev).manual_seed(2 + 1000 * rank)
@@ -618,60 +913,56 @@ def run_cfg3(args) -> None:
     ms = e0.elapsed_time(e1)
     if eng.device_status() != 0:
         raise RuntimeError("device status reported a bounds violation")
-    # end to end through the API: each chunk's K, V and Q from pinned host memory, its output back.
-    # A prefill knows its whole prompt, so the copies run on two side streams and overlap the
-    # attention of other chunks of the same prompt: inputs ahead, each chunk's output as soon as
-    # that chunk is done; every copy of the prompt stays inside the timed region.
-    hK, hV, hQ = K.cpu().pin_memory(), V.cpu().pin_memory(), Qb.cpu().pin_memory()
-    hO = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    dK, dV, dQ, dO = torch.empty_like(K), torch.empty_like(V), torch.empty_like(Qb), torch.empty_like(out)
-    e2e_steps = max(1, min(args.steps, 3))
-    cin, cout = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(nch)]
-    ev_done = [torch.cuda.Event() for _ in range(nch)]
-    ev_out = [torch.cuda.Event() for _ in range(nch)]
-    for c in range(nch):
-        ev_done[c].record(stream)
-        ev_out[c].record(stream)
-    torch.cuda.synchronize()
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record(stream)
-    for _ in range(e2e_steps):
-        with torch.cuda.stream(cin):
+    e2e_ms = None
+    if e2e:
+        # end to end through the API: each chunk's K, V and Q from pinned host memory, its output back.
+        # A prefill knows its whole prompt, so the copies run on two side streams and overlap the
+        # attention of other chunks of the same prompt: inputs ahead, each chunk's output as soon as
+        # that chunk is done; every copy of the prompt stays inside the timed region.
+        hK, hV, hQ = K.cpu().pin_memory(), V.cpu().pin_memory(), Qb.cpu().pin_memory()
+        hO = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        dK, dV, dQ, dO = torch.empty_like(K), torch.empty_like(V), torch.empty_like(Qb), torch.empty_like(out)
+        e2e_steps = max(1, min(args.steps, 3))
+        cin, cout = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ev_in = [torch.cuda.Event() for _ in range(nch)]
+        ev_done = [torch.cuda.Event() for _ in range(nch)]
+        ev_out = [torch.cuda.Event() for _ in range(nch)]
+        for c in range(nch):
+            ev_done[c].record(stream)
+            ev_out[c].record(stream)
+        torch.cuda.synchronize()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for _ in range(e2e_steps):
+            with torch.cuda.stream(cin):
+                for c in range(nch):
+                    a, b = c * PF_C, (c + 1) * PF_C
+                    cin.wait_event(ev_done[c])               # the previous prompt is done with these rows
+                    dK[a:b].copy_(hK[a:b], non_blocking=True)
+                    dV[a:b].copy_(hV[a:b], non_blocking=True)
+                    dQ[a:b].copy_(hQ[a:b], non_blocking=True)
+                    ev_in[c].record(cin)
             for c in range(nch):
                 a, b = c * PF_C, (c + 1) * PF_C
-                cin.wait_event(ev_done[c])               # the previous prompt is done with these rows
-                dK[a:b].copy_(hK[a:b], non_blocking=True)
-                dV[a:b].copy_(hV[a:b], non_blocking=True)
-                dQ[a:b].copy_(hQ[a:b], non_blocking=True)
-                ev_in[c].record(cin)
+                stream.wait_event(ev_in[c])
+                stream.wait_event(ev_out[c])                 # the previous prompt's output rows are out
+                eng.append(0, 0, a, dK[a:b], dV[a:b])
+                eng.attn_prefill(0, 0, a, dQ[a:b], PF_C, SCALE, dO[a:b])
+                ev_done[c].record(stream)
+                with torch.cuda.stream(cout):
+                    cout.wait_event(ev_done[c])
+                    hO[a:b].copy_(dO[a:b], non_blocking=True)
+                    ev_out[c].record(cout)
+        stream.wait_event(ev_out[nch - 1])
         for c in range(nch):
-            a, b = c * PF_C, (c + 1) * PF_C
-            stream.wait_event(ev_in[c])
-            stream.wait_event(ev_out[c])                 # the previous prompt's output rows are out
-            eng.append(0, 0, a, dK[a:b], dV[a:b])
-            eng.attn_prefill(0, 0, a, dQ[a:b], PF_C, SCALE, dO[a:b])
-            ev_done[c].record(stream)
-            with torch.cuda.stream(cout):
-                cout.wait_event(ev_done[c])
-                hO[a:b].copy_(dO[a:b], non_blocking=True)
-                ev_out[c].record(cout)
-    stream.wait_event(ev_out[nch - 1])
-    for c in range(nch):
-        stream.wait_event(ev_out[c])
-    x1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = x0.elapsed_time(x1) / e2e_steps
-    if ws > 1:
-        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, attn_ms, e2e_ms = t.tolist()
-    if rank != 0:
-        return
-    peak, peak_src = 1590.0, "fallback 1590 TFLOP/s"
-    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(pk):
-        peak, peak_src = json.load(open(pk)).get("bf16_tflops", peak), "measured bf16_tflops (burst)"
+            stream.wait_event(ev_out[c])
+        x1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = x0.elapsed_time(x1) / e2e_steps
+    eng.close()
+    ms, attn_ms, e2e_ms = _max_over_ranks(ws, dev, [ms, attn_ms, e2e_ms or 0.0])
+    pk = peaks()
+    peak, peak_src = pk["bf16"], pk["bf16_src"]
     tflops = prefill_flops() / (attn_ms * 1e-3) / 1e12
     line = {
         "metric": "chunked-prefill tokens/s over q8_0 KV (16384-token prompt, 512-token chunks)",
@@ -687,14 +978,15 @@ def run_cfg3(args) -> None:
                      "peak_source": peak_src, "traffic": None,
                      "kernel": "k_prefill_q + k_prefill + k_prefill_merge per chunk (CUDA events around each qkv_attn_prefill call)",
                      "flops_per_step": prefill_flops(), "attn_ms_per_step": attn_ms},
-        "e2e": {"value": ws * PF_N / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": (K.numel() + V.numel()) * 4 + Qb.numel() * 2,
-                "d2h_bytes_per_step": out.numel() * 4},
         "gpu_launches": launches, "clocks": clk,
     }
-    if not args.no_cpu_baseline:
+    if e2e:
+        line["e2e"] = {"value": ws * PF_N / (e2e_ms * 1e-3), "unit": "tokens/s",
+                       "h2d_bytes_per_step": (K.numel() + V.numel()) * 4 + Qb.numel() * 2,
+                       "d2h_bytes_per_step": out.numel() * 4}
+    if not args.no_cpu_baseline and rank == 0:
         line["cpu_baseline"] = cpu_prefill_baseline()
-    print(json.dumps(line), flush=True)
+    return line
 
 
 QSA_CTX, QSA_LAYERS = 73728, 1
@@ -714,7 +1006,7 @@ def cpu_qsa_baseline(steps: int = 2) -> dict:
     import numpy as np
     from oracle import oracle as O
     O.build()
-    threads = O.max_threads()
+    threads = host_threads()
     r = np.random.default_rng(33)
     n = QSA_CTX
     K = O.quantize_rows(r.standard_normal((n, N_HEAD_KV * HD), dtype=np.float32))
@@ -941,6 +1233,10 @@ def main():
         run_cfg5(args)
     elif args.workload == "cfg3":
         run_cfg3(args)
+    elif args.workload == "cfg1":
+        run_single(args, measure_cfg1)
+    elif args.workload == "cfg4":
+        run_single(args, measure_cfg4)
     elif args.workload == "qsa":
         run_qsa(args)
     elif args.workload == "proj":

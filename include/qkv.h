@@ -364,15 +364,30 @@ qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, qkv_cache_vi
  * The split-K scratch is a fixed 6.1 MiB array compiled into the library (held on every GPU that
  * loads it until exit), so T * n_head / n_head_kv must be <= 32 (else QKV_ERR_UNSUPPORTED).
  * Calls share that array: calls that overlap on the GPU race.  The first call on a device looks
- * up the array's address and should come before any stream capture.  Bounds violations seen by
- * the kernel are not reported by this entry point. */
+ * up the array's address and should come before any stream capture.  Bounds violations and
+ * timed-out waits seen by the kernels are recorded in a status word of the same fixed scratch,
+ * which each call clears first: read it with qkv_static_status. */
 qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t n_slots, const int32_t *slots,
                                   const int32_t *pos0, int32_t n_seq, int32_t n_head, const float *Q,
                                   int32_t T, float scale, float *out, void *stream);
 
+/* The device status of the last qkv_attn_decode_static call on the current device (same bits as
+ * qkv_device_status: 1 bad page, 2 bad index, 4 timed-out wait), read on `stream` (synchronising
+ * it) and cleared.  Allocates nothing, like the entry point it reports on.  No counterpart in the
+ * reference.  Returns QKV_ERR_DEVICE when the word was non-zero. */
+qkv_status qkv_static_status(void *stream, int32_t *code);
+
 /* Reads (and clears) the device status word that checked kernels write on a bounds violation.
  * Synchronises the stream. */
 qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code);
+
+/* Failure-detection tests.  No counterpart in the reference.  Sets the limit of the decode kernels'
+ * bounded waits (tile copies, the latency-mode merge barrier; default 2 s) and, when
+ * withhold_unit >= 0, makes the NEXT decode launch of this engine skip the copy of that unit's first
+ * tile while still waiting for its bytes: the wait runs out after wait_limit_ns, the kernel sets
+ * the timed-out bit (4) of the device status and returns, and the context stays usable.  Nothing
+ * faults and nothing hangs.  wait_limit_ns <= 0 restores the default. */
+qkv_status qkv_debug_decode_wait(qkv_engine *eng, int64_t wait_limit_ns, int32_t withhold_unit);
 
 /* Kernels this process has launched through the library so far (all engines, all devices). */
 qkv_status qkv_launch_count(uint64_t *count);

@@ -30,7 +30,7 @@ EXPORTS = [
     "qkv_store_create", "qkv_store_destroy", "qkv_store_save", "qkv_store_restore_or_reset",
     "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
     "qkv_indexer_enable", "qkv_idx_append", "qkv_idx_select", "qkv_attn_decode_qsa", "qkv_idx_read",
-    "qkv_project_append",
+    "qkv_project_append", "qkv_static_status", "qkv_debug_decode_wait",
 ]
 
 
@@ -114,6 +114,9 @@ def lib() -> ctypes.CDLL:
         "qkv_attn_decode_qsa": [P, I32, pI32, pI32, I32, P, P, I32, F32, P, P],
         "qkv_idx_read": [P, I32, I32, I32, I32, P, I32, I32, P, P],
         "qkv_project_append": [P, I32, I32, I32, P, I32, I32, P, P, P, P, P, F32, I32, F32, P, P],
+        "qkv_attn_decode_static": [ctypes.POINTER(QkvCacheView), I32, pI32, pI32, I32, I32, P, I32, F32, P, P],
+        "qkv_static_status": [P, pI32],
+        "qkv_debug_decode_wait": [P, I64, I32],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -357,6 +360,11 @@ class Engine:
         b = ctypes.c_size_t()
         self._check(lib().qkv_state_ptr(self.handle, slot, rec_layer, kind, which, ctypes.byref(p), ctypes.byref(b)))
         return p.value, b.value
+
+    def debug_decode_wait(self, limit_ns: int, withhold_unit: int = -1) -> None:
+        """Failure tests: bounded-wait limit of the decode kernels, and a unit whose first tile copy
+        the next decode launch withholds (include/qkv.h qkv_debug_decode_wait)."""
+        self._check(lib().qkv_debug_decode_wait(self.handle, int(limit_ns), int(withhold_unit)))
 
     def device_status(self, stream=None) -> int:
         c = ctypes.c_int32()

@@ -31,7 +31,9 @@
 #include "qkv_internal.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
+#include <vector>
 #include <cuda_fp16.h>
 
 namespace qkv {
@@ -67,6 +69,28 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Phase timestamps for latency analysis, compiled only with -DQKV_TIMELINE (the product build
+// never defines it): thread 0 of every CTA notes %globaltimer at its phases and appends one record
+// {kernel, block, t[0..9]} to g_tl_rec; qkv_tl_read copies the records out.
+#ifdef QKV_TIMELINE
+__device__ unsigned long long g_tl_rec[1 << 16][12];
+__device__ unsigned int g_tl_n;
+#define TL_DECL unsigned long long tl_[10] = {};
+#define TL(i) do { if (threadIdx.x == 0) tl_[i] = global_ns(); } while (0)
+#define TL_FLUSH(kid)                                                             \
+    do {                                                                          \
+        if (threadIdx.x == 0) {                                                   \
+            const unsigned k_ = atomicAdd(&g_tl_n, 1u) & 0xffffu;                 \
+            g_tl_rec[k_][0] = (kid);                                              \
+            g_tl_rec[k_][1] = blockIdx.x;                                         \
+            for (int i_ = 0; i_ < 10; i_++) g_tl_rec[k_][2 + i_] = tl_[i_];       \
+        }                                                                         \
+    } while (0)
+#else
+#define TL_DECL
+#define TL(i) do { } while (0)
+#define TL_FLUSH(kid) do { } while (0)
+#endif
 // Bounded wait: gives up after limit_ns (a copy that never lands) instead of spinning forever.
 __device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, uint64_t limit_ns) {
     if (mbar_try_wait(bar, phase)) return true;
@@ -77,6 +101,9 @@ __device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, uint64_t l
         if (global_ns() - t0 > limit_ns) return false;
     }
 }
+// Limit of the waits that follow one that gave up (1 ms, or less): they only cover copies issued
+// before it, which land within microseconds; stages whose next copy was never started time out.
+__device__ __forceinline__ uint64_t after_abort(uint64_t limit_ns) { return limit_ns < 1000000ull ? limit_ns : 1000000ull; }
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
@@ -149,6 +176,15 @@ constexpr int OSTR = HD + 4;
 template <int NT>
 struct Stages { static constexpr int N = NT * 8 * OSTR * 4 <= TILE_BYTES ? 1 : 2; };
 
+// Shared memory of the four warps that work on one tile.
+template <int NT>
+struct alignas(16) LaneShared {
+    __half   ps[NT * 8 * PSTR];          // P of the current tile, [row][token]
+    float    red[4 * NT * 8];            // chunk maxima of warps that outgrew the reference
+    float    lpart[4 * NT * 8];          // per-warp row sums (epilogue)
+    int32_t  flag[4];                    // warp outgrew the softmax reference in this tile
+};
+
 template <int NT, int NSR>
 struct Smem {
     static constexpr int NQ = NT * 8;
@@ -156,10 +192,7 @@ struct Smem {
     uint8_t  tile[NS][TILE_BYTES];       // after the tile loop: the unit's O rows [NQ][HD] fp32
     uint8_t  qq[NQ * QSTR];
     float    qd[NBLK * NQ];
-    __half   ps[NQ * PSTR];              // P of the current tile, [row][token]
-    float    red[4 * NQ];                // chunk maxima of warps that outgrew the reference
-    float    lpart[4 * NQ];              // per-warp row sums (epilogue)
-    int32_t  flag[4];                    // warp outgrew the softmax reference in this tile
+    LaneShared<NT> ln;
     float    ml[2 * NQ];                 // the unit's m (log2 domain) and l per row
     uint64_t full[NS];
     int32_t  stage_blk[NS];              // block id of the tile in each stage (-1 skip, < -1 error)
@@ -221,16 +254,19 @@ __device__ __forceinline__ TileRef tile_ref(const DecodeParams &P, const Unit &U
     return r;
 }
 
-// One thread: start the copy of the unit's i-th tile into stage i % NS.
+// One thread: start the copy of the unit's i-th tile into stage i % NS.  `withhold` (failure tests
+// only) arms the barrier for the tile's bytes but starts no copy, so the wait for it runs out.
+// A stage that the CTA's warps have read before is fenced against the copy's (async-proxy)
+// writes; a stage's first copy needs no fence.
 template <typename SM>
-__device__ __forceinline__ void issue_ref(const DecodeParams &P, SM &sm, const TileRef &r, int i) {
+__device__ __forceinline__ void issue_ref(const DecodeParams &P, SM &sm, const TileRef &r, int i, bool withhold) {
     constexpr int NS = SM::NS;
     uint64_t *bar = &sm.full[i % NS];
     sm.stage_blk[i % NS] = r.blk;    // published to the consumers by the barrier's completion
     if (r.blk >= 0) {
-        fence_proxy_async();
+        if (i >= NS) fence_proxy_async();
         mbar_expect_tx(bar, TILE_BYTES);
-        bulk_load(sm.tile[i % NS], r.src, TILE_BYTES, bar);
+        if (!withhold) bulk_load(sm.tile[i % NS], r.src, TILE_BYTES, bar);
     } else {
         if (r.blk < -1) atomicOr(P.status, r.blk == -2 ? ST_BAD_INDEX : ST_BAD_PAGE);
         mbar_arrive(bar);
@@ -238,7 +274,7 @@ __device__ __forceinline__ void issue_ref(const DecodeParams &P, SM &sm, const T
 }
 template <typename SM>
 __device__ __forceinline__ void issue_tile(const DecodeParams &P, SM &sm, const Unit &U, int i) {
-    issue_ref(P, sm, tile_ref(P, U, U.t0 + i), i);
+    issue_ref(P, sm, tile_ref(P, U, U.t0 + i), i, false);
 }
 
 // Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h and store
@@ -282,12 +318,216 @@ __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &
     *reinterpret_cast<__half *>(gtile + (kv ? vd_off(b, t) : kd_off(t, b))) = __float2half_rn(d);
 }
 
-// CTA = 4 warps, up to 4 CTAs per SM.  Per 64-token tile, warp w computes QK for tokens
-// 16w..16w+15 and PV for dims 64w..64w+63; P crosses between them through shared memory.  The
-// softmax uses a per-row reference held in registers (identical in every warp); a warp whose
-// scores outgrow it by more than 2^4 posts its maximum and the whole CTA moves the reference
-// (rescaling O and the row sums) before PV -- rare after the first tile, so a tile normally costs
-// two barriers: P ready, stage free.
+// Row state a thread carries through the tile loop: for its two query rows per 8-row group j
+// (rows 8j + 2tig + e), the last visible position, the softmax reference (log2 domain, the same in
+// every warp that works on the unit), its row sums over its own tokens, and its 64 dims of O.
+template <int NT>
+struct RowState {
+    int   qlim[NT][2];
+    float mref[NT][2];
+    float lsum[NT][2];
+    float O[4][NT][4];
+};
+
+template <int NT>
+__device__ __forceinline__ void row_state_init(RowState<NT> &rs, int nq, int G, int pos0, int tig) {
+#pragma unroll
+    for (int j = 0; j < NT; j++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int n = 8 * j + 2 * tig + e;
+            rs.qlim[j][e] = n < nq ? pos0 + n / G : -1;
+            rs.mref[j][e] = -INFINITY;
+            rs.lsum[j][e] = 0.0f;
+        }
+#pragma unroll
+    for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+        for (int j = 0; j < NT; j++) rs.O[mt][j][0] = rs.O[mt][j][1] = rs.O[mt][j][2] = rs.O[mt][j][3] = 0.0f;
+}
+
+// Barrier of the four warps that share a tile (the whole CTA).
+struct CtaSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// One 64-token tile for the four warps w = 0..3 that share it: QK for the warp's 16 tokens, the
+// causal mask, the lazily rescaled softmax (P through `ls.ps`), and PV for the warp's 64 dims.
+// Ends after PV; the caller's next barrier frees the tile's stage and P.
+template <int NT, class Sync>
+__device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool live, const uint8_t *qq, const float *qd,
+                                          LaneShared<NT> &ls, RowState<NT> &rs, float c2, int w, int lane,
+                                          const Sync &sync) {
+    constexpr int NQ = NT * 8;
+    const int g = lane >> 2, tig = lane & 3;
+    const int lm = lane & 7, lmat = lane >> 3;
+    const int k_tok = 16 * w + pi16(lm + 8 * (lmat & 1));   // K row this lane addresses in ldmatrix
+    const int k_key = kswz(k_tok), k_hi = lmat >> 1;
+    const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);   // tokens of the S rows
+    const int v_dim0 = 64 * w + 8 * lmat + lm;   // V^T row this lane addresses (+32: second block)
+    const int cell0 = blk * TILE_TOK;
+    // ---------------- QK for this warp's 16 tokens ----------------------------------------
+    float S[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+    if (live) {
+        const __half *dkl_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_lo * 16);
+        const __half *dkh_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_hi * 16);
+        const uint32_t kbase = smem_u32(tile) + k_tok * HD;
+#pragma unroll
+        for (int b = 0; b < NBLK; b++) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(kbase + (((2 * b + k_hi) ^ k_key) << 4), a0, a1, a2, a3);
+            const float dlo = __half2float(dkl_h[b]), dhi = __half2float(dkh_h[b]);
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                const uint2 bq = *reinterpret_cast<const uint2 *>(qq + (8 * j + g) * QSTR + b * 32 + tig * 8);
+                uint32_t dd[4];
+                mma_s8(dd, a0, a1, a2, a3, bq.x, bq.y, MAGIC_I);
+                const float2 dq = *reinterpret_cast<const float2 *>(&qd[b * NQ + 8 * j + 2 * tig]);
+                const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(dd[0]), __uint_as_float(dd[1])),
+                                              make_float2(-MAGIC_F, -MAGIC_F));
+                const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(dd[2]), __uint_as_float(dd[3])),
+                                              make_float2(-MAGIC_F, -MAGIC_F));
+                const float2 wlo = __fmul2_rn(dq, make_float2(dlo, dlo));
+                const float2 whi = __fmul2_rn(dq, make_float2(dhi, dhi));
+                const float2 s01 = __ffma2_rn(f01, wlo, make_float2(S[j][0], S[j][1]));
+                const float2 s23 = __ffma2_rn(f23, whi, make_float2(S[j][2], S[j][3]));
+                S[j][0] = s01.x; S[j][1] = s01.y; S[j][2] = s23.x; S[j][3] = s23.y;
+            }
+        }
+    }
+    // ---------------- mask; does this warp outgrow the reference? -----------------------
+    const int clo = cell0 + tk_lo, chi = cell0 + tk_hi;
+    bool over = false;
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        if (!live || clo > rs.qlim[j][0]) S[j][0] = -INFINITY;
+        if (!live || clo > rs.qlim[j][1]) S[j][1] = -INFINITY;
+        if (!live || chi > rs.qlim[j][0]) S[j][2] = -INFINITY;
+        if (!live || chi > rs.qlim[j][1]) S[j][3] = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 4; e++) over = over || S[j][e] * c2 > rs.mref[j][e & 1] + 4.0f;
+    }
+    const bool warp_over = __any_sync(0xffffffffu, over);
+    if (warp_over) {
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            float mx0 = fmaxf(S[j][0], S[j][2]), mx1 = fmaxf(S[j][1], S[j][3]);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
+            if (g == 0) {
+                ls.red[w * NQ + 8 * j + 2 * tig]     = mx0 * c2;
+                ls.red[w * NQ + 8 * j + 2 * tig + 1] = mx1 * c2;
+            }
+        }
+    }
+    if (lane == 0) ls.flag[w] = warp_over;
+    // P relative to the current reference (rewritten below if the reference moves)
+    float psum[NT][2];
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float mm = rs.mref[j][e & 1];
+            pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
+        }
+        psum[j][0] = pr[0] + pr[2];
+        psum[j][1] = pr[1] + pr[3];
+        if (!warp_over) {
+            const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));   // tokens 4tig, 4tig+1 of row 8j+g
+            const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));   // tokens 4tig+2, 4tig+3
+            *reinterpret_cast<uint2 *>(&ls.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
+        }
+    }
+    sync();   // barrier 1: P (or the posted maxima) of every warp are in shared memory
+    if (ls.flag[0] | ls.flag[1] | ls.flag[2] | ls.flag[3]) {
+        // ---- the reference moves: new reference, rescale O and sums, rewrite every P -------
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            float alpha[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int n = 8 * j + 2 * tig + e;
+                float mn = rs.mref[j][e];
+#pragma unroll
+                for (int ww = 0; ww < 4; ww++)
+                    if (ls.flag[ww]) mn = fmaxf(mn, ls.red[ww * NQ + n]);
+                alpha[e] = rs.mref[j][e] == -INFINITY ? 0.0f : exp2f(rs.mref[j][e] - mn);
+                rs.mref[j][e] = mn;
+                rs.lsum[j][e] *= alpha[e];
+            }
+            const float2 al = make_float2(alpha[0], alpha[1]);
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) {
+                const float2 o01 = __fmul2_rn(make_float2(rs.O[mt][j][0], rs.O[mt][j][1]), al);
+                const float2 o23 = __fmul2_rn(make_float2(rs.O[mt][j][2], rs.O[mt][j][3]), al);
+                rs.O[mt][j][0] = o01.x; rs.O[mt][j][1] = o01.y; rs.O[mt][j][2] = o23.x; rs.O[mt][j][3] = o23.y;
+            }
+            float pr[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float mm = rs.mref[j][e & 1];
+                pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
+            }
+            psum[j][0] = pr[0] + pr[2];
+            psum[j][1] = pr[1] + pr[3];
+            const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));
+            const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));
+            *reinterpret_cast<uint2 *>(&ls.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
+        }
+        sync();   // rewritten P visible
+    }
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        rs.lsum[j][0] += psum[j][0];
+        rs.lsum[j][1] += psum[j][1];
+    }
+    // ---------------- PV for this warp's 64 dims ------------------------------------------
+    if (live) {
+        const uint32_t vbase = smem_u32(tile) + TILE_VQ;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t va[8];
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int dim = v_dim0 + 32 * half;
+                ldsm_x4(vbase + dim * TILE_TOK + ((kk ^ ((dim >> 1) & 3)) << 4), va[4 * half], va[4 * half + 1],
+                        va[4 * half + 2], va[4 * half + 3]);
+            }
+#pragma unroll
+            for (int bb = 0; bb < 2; bb++) {   // the warp's two q8_0 blocks (32 dims each)
+                const int blkv = 2 * w + bb;
+                const uint2 dv =
+                    *reinterpret_cast<const uint2 *>(tile + TILE_VD + (blkv * TILE_TOK + 16 * kk + 4 * tig) * 2);
+                uint32_t alo[2], ahi[2], blo[2], bhi[2];
+                s8x4_to_f16(va[4 * bb + 0], alo[0], ahi[0]);
+                s8x4_to_f16(va[4 * bb + 1], alo[1], ahi[1]);
+                s8x4_to_f16(va[4 * bb + 2], blo[0], bhi[0]);
+                s8x4_to_f16(va[4 * bb + 3], blo[1], bhi[1]);
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    const uint2 pb = *reinterpret_cast<const uint2 *>(&ls.ps[(8 * j + g) * PSTR + 16 * kk + 4 * tig]);
+                    const uint32_t b0 = hmul2(pb.x, dv.x), b1 = hmul2(pb.y, dv.y);
+                    mma_f16(rs.O[2 * bb][j], alo[0], alo[1], ahi[0], ahi[1], b0, b1);
+                    mma_f16(rs.O[2 * bb + 1][j], blo[0], blo[1], bhi[0], bhi[1], b0, b1);
+                }
+            }
+        }
+    }
+}
+
+
+// Throughput mode (k_decode): CTA = 4 warps, up to 4 CTAs per SM, one unit per CTA.  Per 64-token
+// tile, warp w computes QK for tokens 16w..16w+15 and PV for dims 64w..64w+63; P crosses between
+// them through shared memory.  The softmax uses a per-row reference held in registers (identical
+// in every warp); a warp whose scores outgrow it by more than 2^4 posts its maximum and the whole
+// CTA moves the reference (rescaling O and the row sums) before PV -- rare after the first tile,
+// so a tile normally costs two barriers: P ready, stage free.
 template <int NT, int NSR>
 __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodeParams P) {
     constexpr int NQ = NT * 8;
@@ -297,6 +537,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, tig = lane & 3;
     const int u = blockIdx.x;
+    TL_DECL
+    TL(0);
     // The next launch on the stream may start as soon as every CTA of this one got here; it then
     // waits (below) until this grid has completed and its writes are visible.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -316,7 +558,11 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             const int n = e / (HD * 4 / 128), t = n / P.G, jj = n % P.G;
             prefetch_l2(qsrc + ((int64_t)t * P.n_head + jj) * HD + (e % (HD * 4 / 128)) * 32);
         }
+#ifdef QKV_TIMELINE
+        if (!P.sel && tid < min(n_tiles, PF_TILES) && !P.tl_nopf) {
+#else
         if (!P.sel && tid < min(n_tiles, PF_TILES)) {
+#endif
             const TileRef r = tile_ref(P, U, U.t0 + tid);
             if (r.blk >= 0) bulk_prefetch_l2(r.src, TILE_BYTES);
         }
@@ -332,14 +578,15 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     // Everything global below (pages, block table, queries, new rows, scratch, output) may have
     // been written by the previous kernel on the stream: wait for it to complete.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    TL(1);
     float *obuf = reinterpret_cast<float *>(sm.tile[0]);   // [NQ][OSTR], valid after the tile loop
     bool aborted = false;
 
     if (has_unit) {
+        const bool withhold = u == P.withhold_unit;
         const int pos0 = P.seq_pos0[U.s];
         const float c2 = P.scale * 1.4426950408889634f;   // softmax in base 2
-        // ---- query rows: loads first (in flight while thread 0 starts the tile copies) --------
-        // 32 threads per row, 8 elements each (4 threads per 32-element block).
+        // ---- query rows: 32 threads per row, 8 elements each (4 threads per 32-element block) ---
         const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
         constexpr int QP = (NQ + 3) / 4;   // rows per warp
         // fused append (dense only): tiles nb_lo .. nb_hi hold the T new positions; the unit that
@@ -375,8 +622,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             if (P.sel)
                 for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             for (int st = 0; st < NS && st < n_tiles; st++)
-                if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st);
+                if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st, withhold && st == 0);
         }
+        TL(6);
         // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row
 #pragma unroll
         for (int it = 0; it < QP; it++) {
@@ -401,28 +649,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
             }
         }
-        int qlim[NT][2];    // last visible position of this lane's query rows (padding: none)
-        float mref[NT][2];  // softmax reference per row, log2 domain (the same in every warp)
-        float lsum[NT][2];  // this warp's row sums over its tokens, relative to mref
-        float O[4][NT][4];  // this warp's 64 dims x the query rows
-#pragma unroll
-        for (int j = 0; j < NT; j++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int n = 8 * j + 2 * tig + e;
-                qlim[j][e] = n < P.nq ? pos0 + n / P.G : -1;
-                mref[j][e] = -INFINITY;
-                lsum[j][e] = 0.0f;
-            }
-#pragma unroll
-        for (int mt = 0; mt < 4; mt++)
-#pragma unroll
-            for (int j = 0; j < NT; j++) O[mt][j][0] = O[mt][j][1] = O[mt][j][2] = O[mt][j][3] = 0.0f;
-        const int lm = lane & 7, lmat = lane >> 3;
-        const int k_tok = 16 * w + pi16(lm + 8 * (lmat & 1));   // K row this lane addresses in ldmatrix
-        const int k_key = kswz(k_tok), k_hi = lmat >> 1;
-        const int tk_lo = 16 * w + pi16(g), tk_hi = 16 * w + pi16(g + 8);   // tokens of the S rows
-        const int v_dim0 = 64 * w + 8 * lmat + lm;   // V^T row this lane addresses (+32: second block)
+        TL(7);
+        RowState<NT> rs;
+        row_state_init(rs, P.nq, P.G, pos0, tig);
         if (appends) {
             for (int t = max(U.t0, nb_lo); t <= min(U.t1 - 1, nb_hi); t++) {
                 const TileRef r = tile_ref(P, U, t);
@@ -431,183 +660,35 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             asm volatile("fence.proxy.async.global;" ::: "memory");   // the rows before the bulk copy reads them
         }
         __syncthreads();   // query rows ready, barriers initialised
+        TL(2);
         if (appends && tid == 0)   // the first tiles held back for the append
             for (int st = 0; st < NS && st < n_tiles; st++)
-                if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref(P, sm, first[st], st);
+                if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref(P, sm, first[st], st, withhold && st == 0);
 
         for (int i = 0; i < n_tiles; i++) {
             const int stage = i % NS;
-            const bool landed = mbar_wait(&sm.full[stage], (uint32_t)((i / NS) & 1), aborted ? 10000000ull : 2000000000ull);
+            const bool landed = mbar_wait(&sm.full[stage], (uint32_t)((i / NS) & 1),
+                                          aborted ? after_abort(P.wait_ns) : P.wait_ns);
             aborted = aborted || !__all_sync(0xffffffffu, landed);
+            if (i == 0) TL(8);
             const int blk = sm.stage_blk[stage];
-            uint8_t *tile = sm.tile[stage];
-            const bool live = blk >= 0 && !aborted;
-            const int cell0 = blk * TILE_TOK;
-            // ---------------- QK for this warp's 16 tokens ----------------------------------------
-            float S[NT][4];
-#pragma unroll
-            for (int j = 0; j < NT; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
-            if (live) {
-                const __half *dkl_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_lo * 16);
-                const __half *dkh_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_hi * 16);
-                const uint32_t kbase = smem_u32(tile) + k_tok * HD;
-#pragma unroll
-                for (int b = 0; b < NBLK; b++) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4(kbase + (((2 * b + k_hi) ^ k_key) << 4), a0, a1, a2, a3);
-                    const float dlo = __half2float(dkl_h[b]), dhi = __half2float(dkh_h[b]);
-#pragma unroll
-                    for (int j = 0; j < NT; j++) {
-                        const uint2 bq = *reinterpret_cast<const uint2 *>(sm.qq + (8 * j + g) * QSTR + b * 32 + tig * 8);
-                        uint32_t dd[4];
-                        mma_s8(dd, a0, a1, a2, a3, bq.x, bq.y, MAGIC_I);
-                        const float2 dq = *reinterpret_cast<const float2 *>(&sm.qd[b * NQ + 8 * j + 2 * tig]);
-                        const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(dd[0]), __uint_as_float(dd[1])),
-                                                      make_float2(-MAGIC_F, -MAGIC_F));
-                        const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(dd[2]), __uint_as_float(dd[3])),
-                                                      make_float2(-MAGIC_F, -MAGIC_F));
-                        const float2 wlo = __fmul2_rn(dq, make_float2(dlo, dlo));
-                        const float2 whi = __fmul2_rn(dq, make_float2(dhi, dhi));
-                        const float2 s01 = __ffma2_rn(f01, wlo, make_float2(S[j][0], S[j][1]));
-                        const float2 s23 = __ffma2_rn(f23, whi, make_float2(S[j][2], S[j][3]));
-                        S[j][0] = s01.x; S[j][1] = s01.y; S[j][2] = s23.x; S[j][3] = s23.y;
-                    }
-                }
-            }
-            // ---------------- mask; does this warp outgrow the reference? -----------------------
-            const int clo = cell0 + tk_lo, chi = cell0 + tk_hi;
-            bool over = false;
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-                if (!live || clo > qlim[j][0]) S[j][0] = -INFINITY;
-                if (!live || clo > qlim[j][1]) S[j][1] = -INFINITY;
-                if (!live || chi > qlim[j][0]) S[j][2] = -INFINITY;
-                if (!live || chi > qlim[j][1]) S[j][3] = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < 4; e++) over = over || S[j][e] * c2 > mref[j][e & 1] + 4.0f;
-            }
-            const bool warp_over = __any_sync(0xffffffffu, over);
-            if (warp_over) {
-#pragma unroll
-                for (int j = 0; j < NT; j++) {
-                    float mx0 = fmaxf(S[j][0], S[j][2]), mx1 = fmaxf(S[j][1], S[j][3]);
-#pragma unroll
-                    for (int o = 4; o < 32; o <<= 1) {
-                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-                    }
-                    if (g == 0) {
-                        sm.red[w * NQ + 8 * j + 2 * tig]     = mx0 * c2;
-                        sm.red[w * NQ + 8 * j + 2 * tig + 1] = mx1 * c2;
-                    }
-                }
-            }
-            if (lane == 0) sm.flag[w] = warp_over;
-            // P relative to the current reference (rewritten below if the reference moves)
-            float psum[NT][2];
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-                float pr[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float mm = mref[j][e & 1];
-                    pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
-                }
-                psum[j][0] = pr[0] + pr[2];
-                psum[j][1] = pr[1] + pr[3];
-                if (!warp_over) {
-                    const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));   // tokens 4tig, 4tig+1 of row 8j+g
-                    const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));   // tokens 4tig+2, 4tig+3
-                    *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
-                }
-            }
-            __syncthreads();   // barrier 1: P (or the posted maxima) of every warp are in shared memory
-            if (sm.flag[0] | sm.flag[1] | sm.flag[2] | sm.flag[3]) {
-                // ---- the reference moves: new reference, rescale O and sums, rewrite every P -------
-#pragma unroll
-                for (int j = 0; j < NT; j++) {
-                    float alpha[2];
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int n = 8 * j + 2 * tig + e;
-                        float mn = mref[j][e];
-#pragma unroll
-                        for (int ww = 0; ww < 4; ww++)
-                            if (sm.flag[ww]) mn = fmaxf(mn, sm.red[ww * NQ + n]);
-                        alpha[e] = mref[j][e] == -INFINITY ? 0.0f : exp2f(mref[j][e] - mn);
-                        mref[j][e] = mn;
-                        lsum[j][e] *= alpha[e];
-                    }
-                    const float2 al = make_float2(alpha[0], alpha[1]);
-#pragma unroll
-                    for (int mt = 0; mt < 4; mt++) {
-                        const float2 o01 = __fmul2_rn(make_float2(O[mt][j][0], O[mt][j][1]), al);
-                        const float2 o23 = __fmul2_rn(make_float2(O[mt][j][2], O[mt][j][3]), al);
-                        O[mt][j][0] = o01.x; O[mt][j][1] = o01.y; O[mt][j][2] = o23.x; O[mt][j][3] = o23.y;
-                    }
-                    float pr[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float mm = mref[j][e & 1];
-                        pr[e] = mm == -INFINITY ? 0.0f : exp2f(fmaf(S[j][e], c2, -mm));
-                    }
-                    psum[j][0] = pr[0] + pr[2];
-                    psum[j][1] = pr[1] + pr[3];
-                    const uint32_t lo = movm_t(pack_f16x2(pr[0], pr[1]));
-                    const uint32_t hi = movm_t(pack_f16x2(pr[2], pr[3]));
-                    *reinterpret_cast<uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * w + 4 * tig]) = make_uint2(lo, hi);
-                }
-                __syncthreads();   // rewritten P visible
-            }
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-                lsum[j][0] += psum[j][0];
-                lsum[j][1] += psum[j][1];
-            }
-            // ---------------- PV for this warp's 64 dims ------------------------------------------
-            if (live) {
-                const uint32_t vbase = smem_u32(tile) + TILE_VQ;
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                    uint32_t va[8];
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        const int dim = v_dim0 + 32 * half;
-                        ldsm_x4(vbase + dim * TILE_TOK + ((kk ^ ((dim >> 1) & 3)) << 4), va[4 * half], va[4 * half + 1],
-                                va[4 * half + 2], va[4 * half + 3]);
-                    }
-#pragma unroll
-                    for (int bb = 0; bb < 2; bb++) {   // the warp's two q8_0 blocks (32 dims each)
-                        const int blkv = 2 * w + bb;
-                        const uint2 dv =
-                            *reinterpret_cast<const uint2 *>(tile + TILE_VD + (blkv * TILE_TOK + 16 * kk + 4 * tig) * 2);
-                        uint32_t alo[2], ahi[2], blo[2], bhi[2];
-                        s8x4_to_f16(va[4 * bb + 0], alo[0], ahi[0]);
-                        s8x4_to_f16(va[4 * bb + 1], alo[1], ahi[1]);
-                        s8x4_to_f16(va[4 * bb + 2], blo[0], bhi[0]);
-                        s8x4_to_f16(va[4 * bb + 3], blo[1], bhi[1]);
-#pragma unroll
-                        for (int j = 0; j < NT; j++) {
-                            const uint2 pb = *reinterpret_cast<const uint2 *>(&sm.ps[(8 * j + g) * PSTR + 16 * kk + 4 * tig]);
-                            const uint32_t b0 = hmul2(pb.x, dv.x), b1 = hmul2(pb.y, dv.y);
-                            mma_f16(O[2 * bb][j], alo[0], alo[1], ahi[0], ahi[1], b0, b1);
-                            mma_f16(O[2 * bb + 1][j], blo[0], blo[1], bhi[0], bhi[1], b0, b1);
-                        }
-                    }
-                }
-            }
+            tile_step<NT>(sm.tile[stage], blk, blk >= 0 && !aborted, sm.qq, sm.qd, sm.ln, rs, c2, w, lane, CtaSync{});
             __syncthreads();   // barrier 2: the stage and P are free
-            if (tid == 0 && i + NS < n_tiles) issue_tile(P, sm, U, i + NS);
+            // After a wait that gave up no new copy starts: every copy this CTA issued has then
+            // been waited for (bounded) by the time it exits.
+            if (tid == 0 && i + NS < n_tiles && !aborted) issue_tile(P, sm, U, i + NS);
+            if (i == 0) TL(3);
         }
+        TL(4);
         // ---------------- unit epilogue: O, m, l into shared memory ------------------------------
 #pragma unroll
         for (int j = 0; j < NT; j++)
 #pragma unroll
             for (int e = 0; e < 2; e++) {
-                float v = lsum[j][e];
+                float v = rs.lsum[j][e];
 #pragma unroll
                 for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (g == 0) sm.lpart[w * NQ + 8 * j + 2 * tig + e] = v;
+                if (g == 0) sm.ln.lpart[w * NQ + 8 * j + 2 * tig + e] = v;
             }
 #pragma unroll
         for (int j = 0; j < NT; j++)
@@ -617,8 +698,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
 #pragma unroll
                 for (int mt = 0; mt < 4; mt++) {
                     const int d0 = 64 * w + 16 * mt + g;
-                    obuf[n * OSTR + d0]     = O[mt][j][e];
-                    obuf[n * OSTR + d0 + 8] = O[mt][j][2 + e];
+                    obuf[n * OSTR + d0]     = rs.O[mt][j][e];
+                    obuf[n * OSTR + d0 + 8] = rs.O[mt][j][2 + e];
                 }
             }
         __syncthreads();
@@ -628,8 +709,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int n = 8 * j + 2 * tig + e;
-                    sm.ml[n] = mref[j][e];   // log2 domain
-                    sm.ml[NQ + n] = sm.lpart[n] + sm.lpart[NQ + n] + sm.lpart[2 * NQ + n] + sm.lpart[3 * NQ + n];
+                    const float *lp = sm.ln.lpart;
+                    sm.ml[n] = rs.mref[j][e];   // log2 domain
+                    sm.ml[NQ + n] = lp[n] + lp[NQ + n] + lp[2 * NQ + n] + lp[3 * NQ + n];
                 }
         }
         if (aborted && lane == 0) atomicOr(P.status, ST_TIMEOUT);
@@ -655,32 +737,42 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             rec[P.nq * HD + tid] = sm.ml[tid];
             rec[P.nq * HD + P.nq + tid] = sm.ml[NQ + tid];
         }
+        TL(5);
+        TL_FLUSH(2);
     }
 }
 
+
 // Merge of the partial records of the pairs with more than one unit (plan positions first, so
-// pairs 0 .. n_merge-1): CTA = (pair, query row, quarter of the dims), MG_THREADS threads.
+// pairs 0 .. n_merge-1): CTA = (pair, query row, 1/SPLIT of the dims), MG_THREADS threads.
 // O = sum_u 2^(m_u - M) O_u / sum_u 2^(m_u - M) l_u in a fixed order: thread group gi (one float4
-// column of the quarter each) sums the units gi, gi + MG_GROUPS, ... and the groups are added in
+// column of the CTA's dims each) sums the units gi, gi + MG_GROUPS, ... and the groups are added in
 // order.  The first MG_GROUPS * MG_UNROLL units' O columns are loaded together with (m, l), so a
-// pair of up to that many units costs one round trip to L2.
-constexpr int MG_THREADS = 512, MG_SPLIT = 4, MG_LANES = HD / 4 / MG_SPLIT, MG_GROUPS = MG_THREADS / MG_LANES;
-constexpr int MG_MAX_UNITS = 1024, MG_UNROLL = 8;
+// pair of up to that many units costs one round trip to L2.  SPLIT is chosen per launch so that
+// the grid stays within two CTAs per SM: then it is resident (waiting) while k_decode runs, and
+// the next launch on the stream can launch and become resident as the decode CTAs leave.
+constexpr int MG_THREADS = 512, MG_MAX_UNITS = 1024;
 static_assert(MG_MAX_UNITS <= 2 * MG_THREADS, "two (m, l) pairs per thread");
+template <int SPLIT>
 __global__ void __launch_bounds__(MG_THREADS) k_decode_merge(const DecodeParams P) {
+    constexpr int MG_LANES = HD / 4 / SPLIT, MG_GROUPS = MG_THREADS / MG_LANES;
+    constexpr int MG_UNROLL = SPLIT == 2 ? 9 : 8;   // units per thread loaded at once (registers <= 64)
     __shared__ float wgt[MG_MAX_UNITS];
     __shared__ float4 part[MG_GROUPS][MG_LANES];
     __shared__ float red[2][MG_THREADS / 32];
     // The next launch on the stream may become resident now; it waits for this grid.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    TL_DECL
+    TL(0);
     const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
-    const int dq = blockIdx.x % MG_SPLIT, rowid = blockIdx.x / MG_SPLIT;
+    const int dq = blockIdx.x % SPLIT, rowid = blockIdx.x / SPLIT;
     const int pair = rowid / P.nq, n = rowid % P.nq;
     const int s = pair / P.n_head_kv, h = pair % P.n_head_kv;
     const int nu = min(P.seq_units[s], MG_MAX_UNITS), u0 = P.seq_unit0[s] + h * P.seq_units[s];
     const int64_t stride = partial_stride(P.nq);
     const int gi = tid / MG_LANES, ql = tid % MG_LANES, q4 = dq * MG_LANES + ql;
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the records of k_decode
+    TL(1);
     const float *base = P.partial + (int64_t)u0 * stride;
     auto ocol = [&](int i) {   // this thread's float4 of unit i's row (i clamped into range)
         return __ldcg(reinterpret_cast<const float4 *>(base + (int64_t)min(i, nu - 1) * stride + n * HD) + q4);
@@ -748,6 +840,8 @@ __global__ void __launch_bounds__(MG_THREADS) k_decode_merge(const DecodeParams 
         float *orow = P.out + (((int64_t)P.seq_idx[s] * P.T + t) * P.n_head + h * P.G + jj) * HD;
         reinterpret_cast<float4 *>(orow)[dq * MG_LANES + tid] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
+    TL(2);
+    TL_FLUSH(3);
 }
 
 // The same merge for pairs of at most MR_MAX_UNITS units (wide batches: many pairs, few units
@@ -757,6 +851,8 @@ __global__ void __launch_bounds__(MG_THREADS) k_decode_merge(const DecodeParams 
 constexpr int MR_ROWS = 8, MR_MAX_UNITS = 16;
 __global__ void __launch_bounds__(64 * MR_ROWS) k_decode_merge_rows(const DecodeParams P) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    TL_DECL
+    TL(0);
     const int tid = threadIdx.x, q4 = tid & 63;
     const int nrb = (P.nq + MR_ROWS - 1) / MR_ROWS;
     const int pair = blockIdx.x / nrb, n = (blockIdx.x % nrb) * MR_ROWS + (tid >> 6);
@@ -764,7 +860,11 @@ __global__ void __launch_bounds__(64 * MR_ROWS) k_decode_merge_rows(const Decode
     const int nu = min(P.seq_units[s], MR_MAX_UNITS), u0 = P.seq_unit0[s] + h * P.seq_units[s];
     const int64_t stride = partial_stride(P.nq);
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the records of k_decode
-    if (n >= P.nq) return;
+    TL(1);
+    if (n >= P.nq) {
+        TL_FLUSH(4);
+        return;
+    }
     const float *base = P.partial + (int64_t)u0 * stride;
     float m[MR_MAX_UNITS], l[MR_MAX_UNITS];
     float4 v[MR_MAX_UNITS];
@@ -799,6 +899,8 @@ __global__ void __launch_bounds__(64 * MR_ROWS) k_decode_merge_rows(const Decode
     const int t = n / P.G, jj = n % P.G;
     float *orow = P.out + (((int64_t)P.seq_idx[s] * P.T + t) * P.n_head + h * P.G + jj) * HD;
     reinterpret_cast<float4 *>(orow)[q4] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    TL(2);
+    TL_FLUSH(4);
 }
 
 }  // namespace dec
@@ -867,8 +969,19 @@ static cudaError_t launch_ns(const DecodeParams &p, cudaStream_t st) {
         if (p.seq_units[0] <= dec::MR_MAX_UNITS)
             e = launch_pdl(dec::k_decode_merge_rows, (unsigned)(p.n_merge * ((p.nq + dec::MR_ROWS - 1) / dec::MR_ROWS)),
                            64 * dec::MR_ROWS, 0, st, p);
-        else
-            e = launch_pdl(dec::k_decode_merge, (unsigned)(p.n_merge * p.nq * dec::MG_SPLIT), dec::MG_THREADS, 0, st, p);
+        else {
+            // the largest split whose grid fits two CTAs per SM beside the decode grid
+            int sms = 148, dev = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                sms = 148;
+            const int64_t rows = (int64_t)p.n_merge * p.nq;
+            if (rows * 4 <= 2 * sms)
+                e = launch_pdl(dec::k_decode_merge<4>, (unsigned)(rows * 4), dec::MG_THREADS, 0, st, p);
+            else if (rows * 2 <= 2 * sms)
+                e = launch_pdl(dec::k_decode_merge<2>, (unsigned)(rows * 2), dec::MG_THREADS, 0, st, p);
+            else
+                e = launch_pdl(dec::k_decode_merge<1>, (unsigned)rows, dec::MG_THREADS, 0, st, p);
+        }
         if (e != cudaSuccess) return e;
         count_launches(1);
     }
@@ -899,6 +1012,67 @@ int decode_max_ctas(int nq) {
     }
 }
 
+void plan_decode(DecodeParams &P, const int32_t *slots, const int32_t *pos0, const int32_t *tiles, int ns,
+                 int64_t target, int64_t umax, int64_t max_units) {
+    const int H = P.n_head_kv;
+#ifdef QKV_TIMELINE
+    P.tl_nopf = getenv("QKV_TL_NOPF") != nullptr;   // analysis builds: no pre-wait tile prefetch
+#endif
+    std::vector<int32_t> units(ns);
+    int64_t total = 0;
+    for (int i = 0; i < ns; i++) total += (int64_t)H * tiles[i];
+    // Units: proportional to tiles, about one wave of co-resident CTAs in total, at least two
+    // tiles each.  A pair with one unit writes its output itself; the units of the others
+    // leave partial records for the merge kernel, which takes the pairs at the front of the plan.
+    target = std::min(target, max_units);
+    double scale_u = (double)target / (double)total;
+    int64_t n_units = 0;
+    for (int attempt = 0; attempt < 8; attempt++) {
+        n_units = 0;
+        for (int i = 0; i < ns; i++) {
+            int64_t u = (int64_t)((double)tiles[i] * scale_u);
+            u = std::min<int64_t>(std::min<int64_t>(u, tiles[i] / 2), umax);
+            u = std::max<int64_t>(1, u);
+            units[i] = (int32_t)u;
+            n_units += u * H;
+        }
+        if (n_units <= target) break;
+        scale_u *= 0.9 * (double)target / (double)n_units;
+    }
+    // The launch lasts as long as its longest unit: where the budget allows, raise a pair's
+    // units until the most tiles any unit gets drops by one.
+    for (int i = 0; i < ns; i++) {
+        const int64_t u = units[i];
+        const int64_t k = (tiles[i] + u - 1) / u;
+        if (k <= 1) continue;
+        const int64_t u2 = std::min<int64_t>((tiles[i] + k - 2) / (k - 1), umax);
+        if (u2 > u && n_units + (u2 - u) * H <= target) {
+            n_units += (u2 - u) * H;
+            units[i] = (int32_t)u2;
+        }
+    }
+    // plan order: multi-unit pairs first (the merge kernel takes pairs 0 .. n_merge-1)
+    std::vector<int32_t> order(ns);
+    for (int i = 0; i < ns; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return units[a] > units[b]; });
+    int64_t acc = 0;
+    int n_multi = 0;
+    for (int j = 0; j < ns; j++) {
+        const int i = order[j];
+        P.seq_idx[j] = i;
+        P.seq_slot[j] = slots[i];
+        P.seq_pos0[j] = pos0[i];
+        P.seq_tiles[j] = tiles[i];
+        P.seq_units[j] = units[i];
+        P.seq_unit0[j] = (int32_t)acc;
+        acc += (int64_t)units[i] * H;
+        n_multi += units[i] > 1;
+    }
+    P.seq_unit0[ns] = (int32_t)acc;
+    P.n_units = (int32_t)acc;
+    P.n_merge = n_multi * H;
+}
+
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
     switch ((p.nq + 7) / 8) {
         case 1: return launch_nt<1>(p, st);
@@ -921,9 +1095,9 @@ cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
 // For callers that must not allocate device memory -- e.g. a custom op running inside ggml's
 // graph executor, whose memory is planned ahead by ggml-alloc and may not grow mid-graph, or code
 // running under an allocator that owns all of the device's memory.  The kernels' split-K scratch
-// lives in the file-scope arrays below (6.3 MiB of partial records for up to 192 units of 32
-// query rows), allocated once by the CUDA module on every GPU that loads the library and held
-// until exit.  Every call shares them: calls that overlap on the GPU race.
+// lives in the file-scope arrays below (6,340,608 bytes = 6.05 MiB of partial records for up to
+// 192 units of 32 query rows), allocated once by the CUDA module on every GPU that loads the library and held until exit.
+// Every call shares them: calls that overlap on the GPU race.
 // ============================================================================================
 namespace qkv {
 namespace stat {
@@ -1010,40 +1184,39 @@ extern "C" qkv_status qkv_attn_decode_static(const qkv_cache_view *view, int32_t
         P.nq = T * G;
         P.n_seq = ns;
         P.scale = scale;
-        int64_t total = 0;
-        int32_t tiles[MAX_SEQ], units[MAX_SEQ];
-        for (int i = 0; i < ns; i++) {
-            tiles[i] = (pos0[base + i] + T + TILE_TOK - 1) / TILE_TOK;
-            total += (int64_t)H * tiles[i];
-        }
-        int64_t acc = 0;
-        for (int i = 0; i < ns; i++) {   // units in proportion to tiles, >= 1, in total <= budget
-            int64_t u = (int64_t)((double)tiles[i] * (double)(target - (int64_t)ns * H) / (double)total);
-            u = std::min<int64_t>(std::min<int64_t>(u, tiles[i] / 2), decode_merge_max_units());
-            u = std::max<int64_t>(1, u);
-            units[i] = (int32_t)u;
-        }
-        // multi-unit pairs first (the merge kernel takes pairs 0 .. n_merge-1)
-        int order[MAX_SEQ];
-        for (int i = 0; i < ns; i++) order[i] = i;
-        std::stable_sort(order, order + ns, [&](int a, int b) { return units[a] > units[b]; });
-        int n_multi = 0;
-        for (int j = 0; j < ns; j++) {
-            const int i = order[j];
-            P.seq_idx[j] = i;
-            P.seq_slot[j] = slots[base + i];
-            P.seq_pos0[j] = pos0[base + i];
-            P.seq_tiles[j] = tiles[i];
-            P.seq_units[j] = units[i];
-            P.seq_unit0[j] = (int32_t)acc;
-            acc += (int64_t)units[i] * H;
-            n_multi += units[i] > 1;
-        }
-        P.seq_unit0[ns] = (int32_t)acc;
-        P.n_units = (int32_t)acc;
-        P.n_merge = n_multi * H;
+        P.wait_ns = WAIT_NS_DEFAULT;
+        P.withhold_unit = -1;
+        int32_t tiles[MAX_SEQ];
+        for (int i = 0; i < ns; i++) tiles[i] = (pos0[base + i] + T + TILE_TOK - 1) / TILE_TOK;
+        plan_decode(P, slots + base, pos0 + base, tiles, ns, target, decode_merge_max_units(), stat::MAX_UNITS);
         if (P.n_units > stat::MAX_UNITS) return QKV_ERR_UNSUPPORTED;
         if (launch_decode(P, st) != cudaSuccess) return QKV_ERR_CUDA;
     }
     return QKV_OK;
 }
+
+extern "C" qkv_status qkv_static_status(void *stream, int32_t *code) {
+    using namespace qkv;
+    if (!code) return QKV_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    stat::Scratch sc;
+    if (stat::scratch_for_current_device(sc) != cudaSuccess) return QKV_ERR_CUDA;
+    int32_t h = 0;
+    if (cudaMemcpyAsync(&h, sc.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess || cudaMemsetAsync(sc.status, 0, sizeof(int32_t), st) != cudaSuccess)
+        return QKV_ERR_CUDA;
+    *code = h;
+    return h ? QKV_ERR_DEVICE : QKV_OK;
+}
+
+#ifdef QKV_TIMELINE
+extern "C" int qkv_tl_read(unsigned long long *host, int max_records) {
+    unsigned int n = 0;
+    if (cudaMemcpyFromSymbol(&n, qkv::dec::g_tl_n, sizeof n) != cudaSuccess) return -1;
+    const int m = (int)(n < (unsigned)max_records ? n : (unsigned)max_records);
+    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::dec::g_tl_rec, (size_t)m * 12 * 8) != cudaSuccess) return -1;
+    const unsigned int zero = 0;
+    cudaMemcpyToSymbol(qkv::dec::g_tl_n, &zero, sizeof zero);
+    return m;
+}
+#endif

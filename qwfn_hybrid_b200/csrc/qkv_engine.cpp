@@ -72,6 +72,8 @@ struct qkv_engine {
     float    *d_partial = nullptr;    // kernel C: per-cluster partial records
     size_t    partial_bytes = 0;
     int32_t  *d_status  = nullptr;
+    uint64_t  wait_ns = WAIT_NS_DEFAULT;   // limit of the decode kernels' bounded waits
+    int32_t   withhold_unit = -1;     // failure tests: the next decode launch withholds this unit's first tile
     // kernel D scratch, allocated by the first prefill call
     uint8_t  *d_pf_q        = nullptr;    // query tiles
     float    *d_pf_partial  = nullptr;    // split-segment partials
@@ -623,7 +625,8 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
 
 // ------------------------------------------------------------------------------------ decode
 // Plan one launch of kernel C for sequences [base, base+ns): every pair (sequence, KV head) is
-// cut into units in proportion to its tiles so that about two CTAs per SM carry equal work.
+// cut into units in proportion to its tiles (plan_decode) so that about a wave of CTAs carries
+// equal work.
 // Where kernel C reads from: by default the layer's pool through the engine's block table; the
 // indexer path points it at dense scratch copies of the kept cells instead.
 struct DecodeSrc {
@@ -659,63 +662,15 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.n_seq = ns;
     P.n_sel = n_sel;
     P.scale = scale;
-    // Units: proportional to tiles, about one wave of co-resident CTAs in total, at least two
-    // tiles each.  A pair with one unit writes its output itself; the units of the others leave
-    // partial records for the merge kernel, which takes the pairs at the front of the plan.
-    std::vector<int32_t> tiles(ns), units(ns);
-    int64_t total = 0;
-    for (int i = 0; i < ns; i++) {
-        tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
-        total += (int64_t)H * tiles[i];
-    }
+    P.wait_ns = eng->wait_ns;
+    P.withhold_unit = eng->withhold_unit;
+    eng->withhold_unit = -1;   // one launch only
+    std::vector<int32_t> tiles(ns);
+    for (int i = 0; i < ns; i++) tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
     const int max_ctas = decode_max_ctas(T * G);
     const int64_t target = max_ctas > 0 ? max_ctas : (int64_t)eng->num_sms * 2;
-    const int64_t umax = decode_merge_max_units();
-    double scale_u = (double)target / (double)total;
-    int64_t n_units = 0;
-    for (int attempt = 0; attempt < 8; attempt++) {
-        n_units = 0;
-        for (int i = 0; i < ns; i++) {
-            int64_t u = (int64_t)((double)tiles[i] * scale_u);
-            u = std::min<int64_t>(std::min<int64_t>(u, tiles[i] / 2), umax);
-            u = std::max<int64_t>(1, u);
-            units[i] = (int32_t)u;
-            n_units += u * H;
-        }
-        if (n_units <= target) break;
-        scale_u *= 0.9 * (double)target / (double)n_units;
-    }
-    // The launch lasts as long as its longest unit: where the budget allows, raise a pair's units
-    // until the most tiles any unit gets drops by one.
-    for (int i = 0; i < ns; i++) {
-        const int64_t u = units[i];
-        const int64_t k = (tiles[i] + u - 1) / u;
-        if (k <= 1) continue;
-        const int64_t u2 = std::min<int64_t>((tiles[i] + k - 2) / (k - 1), umax);
-        if (u2 > u && n_units + (u2 - u) * H <= target) {
-            n_units += (u2 - u) * H;
-            units[i] = (int32_t)u2;
-        }
-    }
-    std::vector<int32_t> order(ns);
-    for (int i = 0; i < ns; i++) order[i] = i;
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return units[a] > units[b]; });
-    int64_t acc = 0;
-    int n_multi = 0;
-    for (int j = 0; j < ns; j++) {
-        const int i = order[j];
-        P.seq_idx[j] = i;
-        P.seq_slot[j] = slots[i];
-        P.seq_pos0[j] = pos0[i];
-        P.seq_tiles[j] = tiles[i];
-        P.seq_units[j] = units[i];
-        P.seq_unit0[j] = (int32_t)acc;
-        acc += (int64_t)units[i] * H;
-        n_multi += units[i] > 1;
-    }
-    P.seq_unit0[ns] = (int32_t)acc;
-    P.n_units = (int32_t)acc;
-    P.n_merge = n_multi * H;
+    plan_decode(P, slots, pos0, tiles.data(), ns, target, decode_merge_max_units(),
+                (int64_t)(eng->partial_bytes / (partial_stride(P.nq) * sizeof(float))));
     if ((size_t)P.n_units * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
         return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small for %d units", P.n_units);
     CK(eng, launch_decode(P, st));
@@ -1729,6 +1684,13 @@ extern "C" qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, q
     return QKV_OK;
 }
 
+extern "C" qkv_status qkv_debug_decode_wait(qkv_engine *eng, int64_t wait_limit_ns, int32_t withhold_unit) {
+    if (!eng) return QKV_ERR_INVALID;
+    eng->wait_ns = wait_limit_ns > 0 ? (uint64_t)wait_limit_ns : WAIT_NS_DEFAULT;
+    eng->withhold_unit = withhold_unit >= 0 ? withhold_unit : -1;
+    return QKV_OK;
+}
+
 extern "C" qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code) {
     if (!eng || !code) return QKV_ERR_INVALID;
     qkv_status r = use_device(eng);
@@ -1738,7 +1700,7 @@ extern "C" qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *
     CK(eng, cudaStreamSynchronize(S(stream)));
     CK(eng, cudaMemsetAsync(eng->d_status, 0, 4, S(stream)));
     *code = h;
-    return h ? fail(eng, QKV_ERR_DEVICE, "device status 0x%x (1 = bad page, 2 = bad index)", h) : QKV_OK;
+    return h ? fail(eng, QKV_ERR_DEVICE, "device status 0x%x (1 = bad page, 2 = bad index, 4 = timed-out wait)", h) : QKV_OK;
 }
 
 // ------------------------------------------------------------------------------- multi-GPU

@@ -187,6 +187,11 @@ struct DecodeParams {
     int32_t n_pages, max_pages, n_head, n_head_kv, G, T, nq, n_seq, n_sel, n_units;
     int32_t n_merge;              // pairs with more than one unit: plan positions first, pairs 0 .. n_merge-1
     float   scale;
+    uint64_t wait_ns;             // limit of every bounded wait (tile copies, the pair barrier)
+    int32_t withhold_unit;        // failure tests: this unit's first tile copy is never started (-1: none)
+#ifdef QKV_TIMELINE
+    int32_t tl_nopf;              // analysis builds only: no tile prefetch before the dependency wait
+#endif
     // per plan position j (sequences ordered by units, largest first):
     int32_t seq_idx[MAX_SEQ];        // the sequence's index in the caller's arrays
     int32_t seq_slot[MAX_SEQ];
@@ -199,10 +204,17 @@ struct DecodeParams {
 // domain), l [nq]
 __host__ __device__ __forceinline__ int64_t partial_stride(int nq) { return (int64_t)nq * HD + 2 * nq; }
 
-cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);   // k_decode, then k_decode_merge
+cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st);   // k_decode, then a merge kernel
 int decode_max_nq();
 int decode_max_ctas(int nq);       // co-resident CTAs of the decode kernel (0 = unknown)
 int decode_merge_max_units();      // units per pair the merge kernel takes
+constexpr uint64_t WAIT_NS_DEFAULT = 2000000000ull;   // limit of the decode kernels' bounded waits
+// Plans one decode launch of ns sequences (P.n_head_kv, P.nq set; tiles[i] = tiles of each pair of
+// sequence i): the per-position arrays, n_units and n_merge.  Units in proportion to tiles, about
+// `target` CTAs in all, at least two tiles and at most `umax` units per pair, no more than
+// `max_units` (the caller's scratch).
+void plan_decode(DecodeParams &P, const int32_t *slots, const int32_t *pos0, const int32_t *tiles, int ns,
+                 int64_t target, int64_t umax, int64_t max_units);
 
 // ---- kernel D -----------------------------------------------------------------------------------
 // A prefill tile is 128 rows = (128 / G) query tokens x the G q-heads of one KV head.  Two tiles

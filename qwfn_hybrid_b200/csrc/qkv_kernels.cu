@@ -5,9 +5,11 @@
 // 16-byte vector accesses where the layout allows, grids sized from the SM count.
 #include "qkv_internal.h"
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 namespace qkv {
+namespace cg = cooperative_groups;
 
 __device__ __forceinline__ uint8_t *tile_ptr(const PoolRef &pr, int32_t pos, int h) {
     if (pos < 0 || (pos >> 8) >= pr.max_pages) return nullptr;
@@ -374,22 +376,30 @@ cudaError_t launch_block_summary(const PoolRef &pr, int32_t b0, int32_t b1, uint
 }
 
 // ------------------------------------------------------------------------------------ kernel B1
-// Block scores and top-k.  One CTA of 256 threads per (sequence, KV head).  Groups of 8 lanes
-// compute one dot product in the oracle's fixed order: lane l takes dims 32l..32l+31 with
-// sequential fmaf, then a fixed tree over the 8 lanes.  The group's lane 0 sums relu(dot) over
-// the G*T query rows in order (t-major), so the score of every block is bit-exact with the CPU
-// restatement.  Ranking: score descending, block index ascending; a candidate's rank is the
-// number of candidates ahead of it (early exit once >= top_k).
-__global__ void __launch_bounds__(256) k_select(const SelectParams p) {
+// Block scores and top-k.  A cluster of SEL_CL CTAs (256 threads each) per (sequence, KV head);
+// CTA r scores the candidate blocks [r*nb/SEL_CL, (r+1)*nb/SEL_CL).  Groups of 8 lanes compute one
+// dot product in the oracle's fixed order: lane l takes dims 32l..32l+31 with sequential fmaf,
+// then a fixed tree over the 8 lanes.  The group's lane 0 sums relu(dot) over the G*T query rows
+// in order (t-major), so the score of every block is bit-exact with the CPU restatement.  The
+// query rows sit in shared memory as 8 segments of 32 dims padded to 36 floats, so the 8 lanes of
+// a group read their segments with conflict-free 16-byte loads.  Every CTA then copies the other
+// CTAs' scores through distributed shared memory and ranks its own blocks: score descending, block
+// index ascending; a candidate's rank is the number of candidates ahead of it (early exit once
+// >= top_k).
+constexpr int SEL_CL = 8, SEL_SEG = 36;
+__global__ void __cluster_dims__(SEL_CL, 1, 1) __launch_bounds__(256) k_select(const SelectParams p) {
     extern __shared__ float sm_sel[];
-    const int s = blockIdx.x, h = blockIdx.y;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int r = (int)cluster.block_rank(), sh = blockIdx.x / SEL_CL;
+    const int s = sh / p.n_head_kv, h = sh % p.n_head_kv;
     const int nq = p.T * p.G;
-    float *qs     = sm_sel;                 // [nq][HD]
-    float *scores = sm_sel + nq * HD;       // [max_blocks]
+    float *qs     = sm_sel;                          // [nq][8][SEL_SEG]
+    float *scores = sm_sel + nq * 8 * SEL_SEG;       // [max_blocks]: every candidate's score
     const int slot = p.seq_slot[s], nb = p.seq_nblk[s];
+    const int c0 = (int)((int64_t)nb * r / SEL_CL), c1 = (int)((int64_t)nb * (r + 1) / SEL_CL);
     for (int e = threadIdx.x; e < nq * HD; e += blockDim.x) {
         const int n = e / HD, i = e % HD, t = n / p.G, j = n % p.G;
-        qs[e] = p.Q[(((int64_t)s * p.T + t) * p.n_head + h * p.G + j) * HD + i];
+        qs[(n * 8 + (i >> 5)) * SEL_SEG + (i & 31)] = p.Q[(((int64_t)s * p.T + t) * p.n_head + h * p.G + j) * HD + i];
     }
     __syncthreads();
     // Warp-uniform loop: each warp takes 4 blocks per round (one per 8-lane group); every lane
@@ -397,10 +407,10 @@ __global__ void __launch_bounds__(256) k_select(const SelectParams p) {
     const int lane8 = threadIdx.x & 7, grp = (threadIdx.x & 31) >> 3;
     const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
     const uint16_t *sum_base = p.summary + ((int64_t)slot * p.n_head_kv + h) * p.max_blocks * HD;
-    for (int bw = warp * 4; bw < nb; bw += nwarp * 4) {
+    for (int bw = c0 + warp * 4; bw < c1; bw += nwarp * 4) {
         const int b = bw + grp;
         const bool forced = b == 0 || b >= nb - 2;
-        const bool live   = b < nb && !forced;
+        const bool live   = b < c1 && !forced;
         float sv[32];
         const uint16_t *srow = sum_base + (int64_t)(live ? b : 0) * HD + lane8 * 32;
 #pragma unroll
@@ -416,10 +426,16 @@ __global__ void __launch_bounds__(256) k_select(const SelectParams p) {
         }
         float score = 0.0f;
         for (int n = 0; n < nq; n++) {
-            const float *q = qs + n * HD + lane8 * 32;
+            const float4 *q = reinterpret_cast<const float4 *>(qs + (n * 8 + lane8) * SEL_SEG);
             float acc = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 32; k++) acc = __fmaf_rn(q[k], sv[k], acc);
+            for (int k = 0; k < 8; k++) {
+                const float4 qk = q[k];
+                acc = __fmaf_rn(qk.x, sv[4 * k], acc);
+                acc = __fmaf_rn(qk.y, sv[4 * k + 1], acc);
+                acc = __fmaf_rn(qk.z, sv[4 * k + 2], acc);
+                acc = __fmaf_rn(qk.w, sv[4 * k + 3], acc);
+            }
             // fixed tree: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
@@ -427,18 +443,27 @@ __global__ void __launch_bounds__(256) k_select(const SelectParams p) {
             score = __fadd_rn(score, acc > 0.0f ? acc : 0.0f);
         }
         if (forced) score = __int_as_float(0x7f800000);
-        if (lane8 == 0 && b < nb) {
+        if (lane8 == 0 && b < c1) {
             scores[b] = score;
             if (p.scores_out) p.scores_out[((int64_t)s * p.n_head_kv + h) * p.max_blocks + b] = score;
         }
     }
-    __syncthreads();
+    cluster.sync();   // every CTA's scores are in its shared memory
+    for (int q = 0; q < SEL_CL; q++) {
+        if (q == r) continue;
+        const int q0 = (int)((int64_t)nb * q / SEL_CL), q1 = (int)((int64_t)nb * (q + 1) / SEL_CL);
+        const float *remote = cluster.map_shared_rank(scores, q);
+        for (int i = q0 + threadIdx.x; i < q1; i += blockDim.x) scores[i] = remote[i];
+    }
+    cluster.sync();   // no CTA leaves while its shared memory is read; every CTA holds all scores
     int32_t *out = p.idx_out + ((int64_t)s * p.n_head_kv + h) * p.top_k;
     if (nb <= p.top_k) {
-        for (int k = threadIdx.x; k < p.top_k; k += blockDim.x) out[k] = k < nb ? k : -1;
+        for (int k = c0 + threadIdx.x; k < c1; k += blockDim.x) out[k] = k;
+        if (r == SEL_CL - 1)
+            for (int k = nb + threadIdx.x; k < p.top_k; k += blockDim.x) out[k] = -1;
         return;
     }
-    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
         const float si = scores[i];
         int rank = 0;
         for (int j = 0; j < nb && rank < p.top_k; j++) {
@@ -450,13 +475,12 @@ __global__ void __launch_bounds__(256) k_select(const SelectParams p) {
 }
 
 cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
-    const size_t smem = ((size_t)p.T * p.G * HD + p.max_blocks) * sizeof(float);
+    const size_t smem = ((size_t)p.T * p.G * 8 * SEL_SEG + p.max_blocks) * sizeof(float);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    dim3 grid(p.n_seq, p.n_head_kv);
-    k_select<<<grid, 256, smem, st>>>(p);
+    k_select<<<(unsigned)(p.n_seq * p.n_head_kv * SEL_CL), 256, smem, st>>>(p);
     count_launches(1);
     return cudaGetLastError();
 }

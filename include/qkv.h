@@ -243,6 +243,19 @@ qkv_status qkv_idx_select(qkv_engine *eng, int32_t layer, const int32_t *slots, 
 qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0,
                                int32_t n_seq, const float *q_idx, const float *Q, int32_t T, float scale, float *out,
                                void *stream);
+
+/* The indexer's prefill side (graph_builder::sparse_attn with qsa_top_k + qsa_mask,
+ * src/qwfn_graph.cpp:313-415, tables of engine::fill_chunk_qsa, src/qwfn_engine.cpp:1276-1320):
+ * every query row of the chunk (position pos0 + t) keeps the incomplete block that holds it (if
+ * any) and the best k_blocks - 1 (or k_blocks) whole blocks before it by the indexer score, as the
+ * decode path does per token (all blocks when there are no more), and attends causally to the
+ * kept cells only.  q_idx: device F32 [Tc][n_head_idx][key_len] (the rows' indexer queries);
+ * Q: bf16 [Tc][n_head][head_dim] as qkv_attn_prefill.  The chunk's K/V rows (qkv_append) and
+ * indexer keys (qkv_idx_append) must be appended first.  blocks_out / n_out (nullable, both or
+ * neither): device int32 [Tc][k_blocks] kept block ids ascending and [Tc] counts. */
+qkv_status qkv_attn_prefill_qsa(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const float *q_idx,
+                                const uint16_t *Q, int32_t Tc, float scale, float *out, int32_t *blocks_out,
+                                int32_t *n_out, void *stream);
 /* Stored indexer data for tests and snapshots: raw keys of positions pos .. pos+n-1 (device fp16
  * [n][key_len]) and pooled keys of blocks b0 .. b0+n_blk-1 (device fp16 [n_blk][key_len]); either
  * output may be NULL. */

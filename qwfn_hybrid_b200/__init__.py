@@ -30,7 +30,7 @@ EXPORTS = [
     "qkv_store_create", "qkv_store_destroy", "qkv_store_save", "qkv_store_restore_or_reset",
     "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
     "qkv_indexer_enable", "qkv_idx_append", "qkv_idx_select", "qkv_attn_decode_qsa", "qkv_idx_read",
-    "qkv_project_append", "qkv_static_status", "qkv_debug_decode_wait",
+    "qkv_project_append", "qkv_static_status", "qkv_debug_decode_wait", "qkv_attn_prefill_qsa",
 ]
 
 
@@ -117,6 +117,7 @@ def lib() -> ctypes.CDLL:
         "qkv_attn_decode_static": [ctypes.POINTER(QkvCacheView), I32, pI32, pI32, I32, I32, P, I32, F32, P, P],
         "qkv_static_status": [P, pI32],
         "qkv_debug_decode_wait": [P, I64, I32],
+        "qkv_attn_prefill_qsa": [P, I32, I32, I32, P, P, I32, F32, P, P, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -447,6 +448,12 @@ class Engine:
     def attn_decode_qsa(self, layer: int, slots, pos0, q_idx, Q, T: int, scale: float, out, stream=None) -> None:
         self._check(lib().qkv_attn_decode_qsa(self.handle, layer, _i32_array(slots), _i32_array(pos0), len(slots),
                                                _ptr(q_idx), _ptr(Q), T, scale, _ptr(out), _stream(stream)))
+
+    def attn_prefill_qsa(self, layer: int, slot: int, pos0: int, q_idx, Q, Tc: int, scale: float, out,
+                         blocks_out=None, n_out=None, stream=None) -> None:
+        """Sparse prefill: each query row attends to the cells of its kept indexer blocks."""
+        self._check(lib().qkv_attn_prefill_qsa(self.handle, layer, slot, pos0, _ptr(q_idx), _ptr(Q), Tc, scale, _ptr(out),
+                                                _ptr(blocks_out), _ptr(n_out), _stream(stream)))
 
     def idx_read(self, layer: int, slot: int, pos: int = 0, n: int = 0, keys_out=None, b0: int = 0, n_blk: int = 0,
                  pooled_out=None, stream=None) -> None:

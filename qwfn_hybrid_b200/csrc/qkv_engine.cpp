@@ -109,6 +109,11 @@ struct qkv_engine {
     int32_t  *d_vbt = nullptr;
     int32_t   vpool_v = 0, dst_pages = 0;
     float    *d_pj = nullptr;                 // qkv_project_append: raw projections [T][rows]
+    // qkv_attn_prefill_qsa scratch (grown on demand): kept blocks and counts per row, bitsets
+    int32_t  *d_psel = nullptr, *d_pnout = nullptr;
+    int32_t   psel_rows = 0;
+    uint32_t *d_pbits = nullptr;
+    int64_t   pbits_words = 0;
 };
 
 // ------------------------------------------------------------------------------------ helpers
@@ -322,6 +327,9 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_vpool);
     cudaFree(eng->d_vbt);
     cudaFree(eng->d_pj);
+    cudaFree(eng->d_psel);
+    cudaFree(eng->d_pnout);
+    cudaFree(eng->d_pbits);
     if (eng->ring) cudaFreeHost(eng->ring);
     for (auto &ev : eng->ring_ev)
         if (ev) cudaEventDestroy(ev);
@@ -1252,9 +1260,10 @@ static qkv_status pf_scratch(qkv_engine *eng) {
     return r;
 }
 
-extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const uint16_t *Q,
-                                       int32_t Tc, float scale, float *out, void *stream) {
-    if (!eng) return QKV_ERR_INVALID;
+// Kernel D over the chunk's Tc queries; with qsa_bits (sparse prefill) each query sees only the
+// kept indexer blocks of its row (qsa_words words per row).
+static qkv_status prefill_run(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const uint16_t *Q, int32_t Tc,
+                              float scale, float *out, const uint32_t *qsa_bits, int32_t qsa_words, void *stream) {
     qkv_status r;
     if ((r = check_layer(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
     const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H;
@@ -1333,8 +1342,75 @@ extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t s
     P.n_kv = pos0 + Tc;
     P.n_ctas = 2 * n_runs;
     P.scale_log2 = scale * 1.4426950408889634f;
+    P.qsa_bits = qsa_bits;
+    P.qsa_words = qsa_words;
     CK(eng, launch_prefill(P, eng->pf_plan_inline, S(stream)));
     return QKV_OK;
+}
+
+extern "C" qkv_status qkv_attn_prefill(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const uint16_t *Q,
+                                       int32_t Tc, float scale, float *out, void *stream) {
+    if (!eng) return QKV_ERR_INVALID;
+    return prefill_run(eng, layer, slot, pos0, Q, Tc, scale, out, nullptr, 0, stream);
+}
+
+extern "C" qkv_status qkv_attn_prefill_qsa(qkv_engine *eng, int32_t layer, int32_t slot, int32_t pos0, const float *q_idx,
+                                           const uint16_t *Q, int32_t Tc, float scale, float *out, int32_t *blocks_out,
+                                           int32_t *n_out_out, void *stream) {
+    qkv_status r;
+    if ((r = idx_check(eng, layer)) != QKV_OK || (r = check_slot(eng, slot)) != QKV_OK) return r;
+    if (!q_idx || !Q || !out || Tc < 1 || Tc > PF_MAX_TC || pos0 < 0 || (!blocks_out) != (!n_out_out))
+        return fail(eng, QKV_ERR_INVALID, "prefill_qsa: Tc %d (1..%d), pos0 %d, null pointer", Tc, PF_MAX_TC, pos0);
+    if ((int64_t)pos0 + Tc > eng->slots[slot].n_past)
+        return fail(eng, QKV_ERR_STATE, "prefill_qsa: positions %d..%d not appended (slot %d holds %d)", pos0, pos0 + Tc - 1,
+                    slot, eng->slots[slot].n_past);
+    if (eng->host_only) return fail(eng, QKV_ERR_UNSUPPORTED, "host-only engine: no device work");
+    if ((r = use_device(eng)) != QKV_OK) return r;
+    cudaStream_t st = S(stream);
+    if ((r = flush_tables(eng, st)) != QKV_OK) return r;
+    // the rows' kept blocks: the decode selection for every query row (groups of 4 rows share the
+    // pooled-key loads), IDX_MAX_VSEQ rows per launch
+    const int32_t K = eng->k_blocks, words = (pos0 + Tc - 1) / PF_KT + 1;
+    if ((r = idx_scratch(eng, IDX_MAX_VSEQ)) != QKV_OK) return r;
+    int32_t *sel = blocks_out, *nout = n_out_out;
+    if (!sel) {
+        if (eng->psel_rows < Tc) {
+            cudaFree(eng->d_psel);
+            cudaFree(eng->d_pnout);
+            eng->d_psel = eng->d_pnout = nullptr;
+            eng->psel_rows = 0;
+            if ((r = dalloc(eng, eng->d_psel, (size_t)PF_MAX_TC * K * sizeof(int32_t), "prefill kept blocks")) != QKV_OK ||
+                (r = dalloc(eng, eng->d_pnout, (size_t)PF_MAX_TC * sizeof(int32_t), "prefill kept counts")) != QKV_OK)
+                return r;
+            eng->psel_rows = PF_MAX_TC;
+        }
+        sel = eng->d_psel;
+        nout = eng->d_pnout;
+    }
+    if ((int64_t)Tc * words > eng->pbits_words) {
+        cudaFree(eng->d_pbits);
+        eng->d_pbits = nullptr;
+        eng->pbits_words = 0;
+        const int64_t need = (int64_t)PF_MAX_TC * ((eng->cfg.n_ctx + PF_KT - 1) / PF_KT);
+        if ((r = dalloc(eng, eng->d_pbits, (size_t)need * sizeof(uint32_t), "prefill kept-block bitsets")) != QKV_OK) return r;
+        eng->pbits_words = need;
+    }
+    const size_t qrow = (size_t)eng->icfg.n_head * IDX_KEY;
+    for (int32_t v0 = 0; v0 < Tc; v0 += IDX_MAX_VSEQ) {
+        const int32_t nv = std::min<int32_t>(IDX_MAX_VSEQ, Tc - v0);
+        for (const int32_t T : {4, 1}) {
+            const int32_t a = T == 4 ? 0 : nv / 4 * 4, n = T == 4 ? nv / 4 * 4 : nv - nv / 4 * 4;
+            if (n == 0) continue;
+            std::vector<int32_t> slots(n / T, slot), pos(n / T);
+            for (int32_t k = 0; k < n / T; k++) pos[k] = pos0 + v0 + a + T * k;
+            if ((r = idx_select_chunk(eng, layer, slots.data(), pos.data(), T, 0, n, q_idx + (size_t)(v0 + a) * qrow,
+                                      sel + (size_t)(v0 + a) * K, nout + v0 + a, eng->d_iscore, eng->idx_max_blk, st)) !=
+                QKV_OK)
+                return r;
+        }
+    }
+    CK(eng, launch_idx_bits(sel, nout, K, Tc, eng->d_pbits, words, st));
+    return prefill_run(eng, layer, slot, pos0, Q, Tc, scale, out, eng->d_pbits, words, stream);
 }
 
 // -------------------------------------------------------------------------------- snapshots

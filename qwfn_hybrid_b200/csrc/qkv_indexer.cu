@@ -427,6 +427,32 @@ cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaS
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------------------ bitsets
+// Sparse prefill: the kept blocks of each row v (blocks[v][0 .. n_out[v])) as a bitset of `words`
+// words, bit b & 31 of word b >> 5 (kernel D reads word w for KV tile w).
+__global__ void __launch_bounds__(256) k_idx_bits(const int32_t *blocks, const int32_t *n_out, int32_t k_blocks,
+                                                  uint32_t *bits, int32_t words) {
+    extern __shared__ uint32_t row[];
+    const int v = blockIdx.x;
+    for (int w = threadIdx.x; w < words; w += blockDim.x) row[w] = 0u;
+    __syncthreads();
+    const int n = min(n_out[v], k_blocks);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int b = blocks[(int64_t)v * k_blocks + i];
+        if (b >= 0 && (b >> 5) < words) atomicOr(&row[b >> 5], 1u << (b & 31));
+    }
+    __syncthreads();
+    for (int w = threadIdx.x; w < words; w += blockDim.x) bits[(int64_t)v * words + w] = row[w];
+}
+
+cudaError_t launch_idx_bits(const int32_t *blocks, const int32_t *n_out, int32_t k_blocks, int32_t n_v, uint32_t *bits,
+                            int32_t words, cudaStream_t st) {
+    if (n_v < 1 || words < 1 || (size_t)words * 4 > 48 * 1024) return cudaErrorInvalidValue;
+    k_idx_bits<<<n_v, 256, (size_t)words * 4, st>>>(blocks, n_out, k_blocks, bits, words);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
 // --------------------------------------------------------------------------------------- gather
 // CTA (i, v), warp h: kept block i of entry v, KV head h.  Its 4 cells c0 .. c0+3 (c0 = 4 b) go to
 // cells 4i .. 4i+3 of the entry's scratch sequence; cells past v_pos are written as zeros.  Per

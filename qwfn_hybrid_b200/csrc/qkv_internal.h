@@ -171,6 +171,9 @@ struct IdxGatherParams {
     int32_t v_slot[IDX_MAX_VSEQ], v_pos[IDX_MAX_VSEQ];
 };
 cudaError_t launch_idx_gather(const IdxGatherParams &p, cudaStream_t st);
+// Kept-block bitsets for the sparse prefill: bits[v][words] from blocks[v][k_blocks] / n_out[v].
+cudaError_t launch_idx_bits(const int32_t *blocks, const int32_t *n_out, int32_t k_blocks, int32_t n_v, uint32_t *bits,
+                            int32_t words, cudaStream_t st);
 
 // ---- kernel C -----------------------------------------------------------------------------------
 constexpr int MAX_PAIRS = MAX_SEQ * 8;
@@ -249,6 +252,10 @@ struct PrefillParams {
     int32_t n_gpairs;             // pairs of query groups per KV head (the plan's pair tiles: kvh * n_gpairs + pair)
     int32_t n_ctas;               // 2 per pair run
     float   scale_log2;           // softmax scale x log2(e)
+    // QSA prefill (nullable): per query token of the chunk, qsa_words words of kept indexer blocks
+    // (4 cells each, bit b & 31 of word b >> 5); word w covers KV tile w (PF_KT = 32 blocks)
+    const uint32_t *qsa_bits;
+    int32_t         qsa_words;
 };
 // A plan of up to PF_PLAN_INLINE ints travels with the launch (kernel parameters), so a call
 // needs no host-to-device copy ahead of its kernels.

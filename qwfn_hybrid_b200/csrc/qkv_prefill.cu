@@ -263,10 +263,15 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
-// Max of the thread's S row (KT columns from TMEM address scol); columns >= nvis count as -inf
+// Key i of a 128-key tile is visible to the row if i < nvis (causal) and its 4-cell block's bit
+// is set in the row's kept-block word (all ones without a sparse selection).
+__device__ __forceinline__ bool key_vis(int i, int nvis, uint32_t word) {
+    return i < nvis && ((word >> (i >> 2)) & 1u);
+}
+// Max of the thread's S row (KT columns from TMEM address scol); invisible columns count as -inf
 // unless FULL.  Read 64 columns per round trip (two loads, one wait), each 32 reduced as a tree.
 template <bool FULL>
-__device__ __forceinline__ float row_max(uint32_t scol, int nvis) {
+__device__ __forceinline__ float row_max(uint32_t scol, int nvis, uint32_t word) {
     float m = -INFINITY;
 #pragma unroll 1
     for (int c = 0; c < KT / 32; c += 2) {
@@ -278,7 +283,7 @@ __device__ __forceinline__ float row_max(uint32_t scol, int nvis) {
         for (int h = 0; h < 2; h++) {
             float x[32];
 #pragma unroll
-            for (int e = 0; e < 32; e++) x[e] = (FULL || 32 * (c + h) + e < nvis) ? __uint_as_float(v[h][e]) : -INFINITY;
+            for (int e = 0; e < 32; e++) x[e] = (FULL || key_vis(32 * (c + h) + e, nvis, word)) ? __uint_as_float(v[h][e]) : -INFINITY;
 #pragma unroll
             for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
             m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
@@ -290,7 +295,7 @@ __device__ __forceinline__ float row_max(uint32_t scol, int nvis) {
 // stored as fp16 pairs in columns 64 half .. 64 half + 31, inside the S columns this half just
 // read.  Returns the sum of the P values.
 template <bool FULL>
-__device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, float sl2, float mu) {
+__device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, uint32_t word, float sl2, float mu) {
     const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-mu, -mu);
     float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
     uint32_t v[2][32];
@@ -303,8 +308,8 @@ __device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, float 
 #pragma unroll
         for (int e = 0; e < 16; e++) {
             const int i = 64 * half + 32 * h + 2 * e;
-            const float2 y = __ffma2_rn(make_float2(FULL || i < nvis ? __uint_as_float(v[h][2 * e]) : -INFINITY,
-                                                    FULL || i + 1 < nvis ? __uint_as_float(v[h][2 * e + 1]) : -INFINITY),
+            const float2 y = __ffma2_rn(make_float2(FULL || key_vis(i, nvis, word) ? __uint_as_float(v[h][2 * e]) : -INFINITY,
+                                                    FULL || key_vis(i + 1, nvis, word) ? __uint_as_float(v[h][2 * e + 1]) : -INFINITY),
                                         sc2, nm2);
             const float2 p = make_float2(ex2(y.x), ex2(y.y));
             if (e & 1) lb = __fadd2_rn(lb, p);
@@ -753,14 +758,20 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
             const int tok = g * P.tpt + r / P.G;
             const int qpos = g < P.n_groups && tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
+            // the row's kept-block word of each KV tile (sparse prefill), one tile ahead
+            const uint32_t *wrow = P.qsa_bits && qpos >= 0 ? P.qsa_bits + (int64_t)tok * P.qsa_words : nullptr;
+            const int kt_vis = qpos >= 0 ? qpos / KT : -1;   // last KV tile with a visible key
+            uint32_t word_next = wrow && sg.kt0 <= kt_vis ? __ldg(wrow + sg.kt0) : ~0u;
             for (int k = 0; k < sg.nk; k++) {
                 const uint32_t j = it + k, b = j & 1;
                 if (!(ok = wait_all(&B->s_full[b], (j >> 1) & 1))) break;
                 tc_fence_after();
                 const uint32_t scol = tmem + lane_base + TM_S + b * KT;
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
-                const bool full = __all_sync(0xffffffffu, nvis == KT);
-                const float smax = full ? row_max<true>(scol, nvis) : row_max<false>(scol, nvis);
+                const uint32_t word = word_next;
+                if (wrow) word_next = sg.kt0 + k + 1 <= kt_vis && k + 1 < sg.nk ? __ldg(wrow + sg.kt0 + k + 1) : ~0u;
+                const bool full = __all_sync(0xffffffffu, nvis == KT && word == ~0u);
+                const float smax = full ? row_max<true>(scol, nvis, word) : row_max<false>(scol, nvis, word);
                 tc_fence_before();
                 mbar_arrive(&B->s_read[b]);
                 // lazily raised reference max: O and l are rescaled only when a row max grows by
@@ -773,8 +784,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: p = 0
                 if (!(ok = wait_all(&B->s_read[b], (j >> 1) & 1))) break;
                 tc_fence_after();
-                l += full ? row_p<true>(scol, half, nvis, P.scale_log2, mu)
-                          : row_p<false>(scol, half, nvis, P.scale_log2, mu);
+                l += full ? row_p<true>(scol, half, nvis, word, P.scale_log2, mu)
+                          : row_p<false>(scol, half, nvis, word, P.scale_log2, mu);
                 if (k > 0 && __any_sync(0xffffffffu, F != 1.0f)) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;

@@ -913,6 +913,28 @@ def measure_cfg3(args, rank: int, ws: int, local: int, e2e: bool = True) -> dict
     ms = e0.elapsed_time(e1)
     if eng.device_status() != 0:
         raise RuntimeError("device status reported a bounds violation")
+    # kernel A alone: appends of 4096 rows (F32 K and V in, q8_0 rows out) rewriting the prompt's
+    # rows, four per replay of one CUDA graph (back to back, no host time between them)
+    ap_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ap_graph):
+        for a in range(0, PF_N, 4096):
+            eng.append(0, 0, a, K[a:a + 4096], V[a:a + 4096])
+    ap_graph.replay()
+    torch.cuda.synchronize()
+    ap_ms = []
+    for _ in range(5):
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        ap_graph.replay()
+        x1.record(stream)
+        torch.cuda.synchronize()
+        ap_ms.append(x0.elapsed_time(x1) / (PF_N // 4096))
+    del ap_graph
+    ap_bytes = 4096 * N_HEAD_KV * HD * 4 * 2 + 4096 * 2 * ROW_BYTES
+    append_rec = {"rows": 4096, "us_per_append": 1e3 * statistics.median(ap_ms),
+                  "gbs": ap_bytes / (statistics.median(ap_ms) * 1e-3) / 1e9, "bytes_per_append": ap_bytes,
+                  "kernel": "k_append (F32 K/V rows in, q8_0 rows out)",
+                  "timing": "4 appends per replay of one CUDA graph, median of 5 replays"}
     e2e_ms = None
     if e2e:
         # end to end through the API: each chunk's K, V and Q from pinned host memory, its output back.
@@ -979,6 +1001,7 @@ def measure_cfg3(args, rank: int, ws: int, local: int, e2e: bool = True) -> dict
                      "kernel": "k_prefill_q + k_prefill + k_prefill_merge per chunk (CUDA events around each qkv_attn_prefill call)",
                      "flops_per_step": prefill_flops(), "attn_ms_per_step": attn_ms},
         "gpu_launches": launches, "clocks": clk,
+        "append": dict(append_rec, frac=append_rec["gbs"] / peaks()["hbm"]),
     }
     if e2e:
         line["e2e"] = {"value": ws * PF_N / (e2e_ms * 1e-3), "unit": "tokens/s",

@@ -5,6 +5,7 @@
 // 16-byte vector accesses where the layout allows, grids sized from the SM count.
 #include "qkv_internal.h"
 
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
@@ -34,36 +35,130 @@ __device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t &q, _
     (void)lane;
 }
 
+// CTA = (16-token group g, KV head h), 256 threads.  A team of 4 threads quantises one 32-element
+// block (8 elements each, amax by two shuffles); a warp's 8 teams cover one token's 256 dims of
+// the head, so its loads read 1 KiB contiguously.  K and V quants are staged token-major in shared
+// memory (8-byte stores, conflict-free), then each thread writes one 16-byte chunk: a K row's
+// chunk, and for its dim the transposed V chunk of the group's 16 tokens, gathered byte by byte
+// from the 16 token rows (same-word reads of neighbouring dims).  Only a group that the append
+// covers partly (its first or last) writes the transposed V byte by byte.
+constexpr int AP_TOK = 16;
+// The group's F32 inputs of this thread: 2 teams x (K, V) x 8 elements (team p = token p / 8,
+// block p % 8); positions outside [lo, hi) read as zeros.
+struct ApIn {
+    float x[2][2][8];
+};
+__device__ __forceinline__ void ap_load(ApIn &in, const float *__restrict__ K, const float *__restrict__ V, int32_t pos,
+                                        int32_t g0, int32_t lo, int32_t hi, int n_head_kv, int h, int tid) {
+    const int sub = tid & 3;
+#pragma unroll
+    for (int it = 0; it < 2; it++) {
+        const int p = (tid >> 2) + 64 * it, t = p >> 3, b = p & 7;
+        const int32_t row = g0 + t;
+#pragma unroll
+        for (int kv = 0; kv < 2; kv++) {
+            if (row >= lo && row < hi) {
+                const float4 *src = reinterpret_cast<const float4 *>((kv ? V : K) + (int64_t)(row - pos) * n_head_kv * HD +
+                                                                     h * HD + b * QK + sub * 8);
+                const float4 u0 = __ldcs(src), u1 = __ldcs(src + 1);   // streamed: read once
+                in.x[it][kv][0] = u0.x; in.x[it][kv][1] = u0.y; in.x[it][kv][2] = u0.z; in.x[it][kv][3] = u0.w;
+                in.x[it][kv][4] = u1.x; in.x[it][kv][5] = u1.y; in.x[it][kv][6] = u1.z; in.x[it][kv][7] = u1.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) in.x[it][kv][e] = 0.0f;
+            }
+        }
+    }
+}
+
+// CTA = (16-token group blockIdx.x, KV head blockIdx.y), 256 threads, one wave for 4096-row
+// appends: every CTA issues all of its loads at once (a grid-stride loop with the next group's
+// loads in flight measured slower: twice the registers, half the CTAs per SM).  A team of 4
+// threads quantises one 32-element block (8 elements each, amax by two shuffles); a warp's 8 teams
+// cover one token's 256 dims of the head, so its loads read 1 KiB contiguously.  K and V quants
+// are staged token-major in shared memory (8-byte stores, conflict-free), then each thread writes
+// one 16-byte chunk: a K row's chunk, and for its dim the transposed V chunk of the group's 16
+// tokens, gathered byte by byte from the 16 token rows (same-word reads of neighbouring dims).
+// Only a group that the append covers partly (its first or last) writes the transposed V byte by
+// byte.
 __global__ void __launch_bounds__(256) k_append(PoolRef pr, int32_t pos, const float *__restrict__ K,
                                                 const float *__restrict__ V, int32_t n_rows) {
-    const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
-    const int lane = threadIdx.x & 31;
-    const int per_row = pr.n_head_kv * NBLK;
-    if (warp >= n_rows * per_row) return;
-    const int r = warp / per_row, hb = warp % per_row, h = hb / NBLK, b = hb % NBLK;
-    const int32_t p = pos + r;
-    uint8_t *tile = tile_ptr(pr, p, h);
+    __shared__ __align__(16) uint8_t ks[AP_TOK][HD];            // K quants of the group's tokens
+    __shared__ __align__(16) uint8_t vs[AP_TOK][HD];            // V quants of the group's tokens
+    __shared__ __align__(16) __half kd[AP_TOK][NBLK];           // K scales [token][block]
+    __shared__ __align__(16) __half vd[NBLK][AP_TOK];           // V scales [block][token]
+    const int h = blockIdx.y, tid = threadIdx.x, sub = tid & 3;
+    const int32_t g0 = (pos / AP_TOK + (int32_t)blockIdx.x) * AP_TOK;          // first position of the group
+    const int32_t lo = max(pos, g0), hi = min(pos + n_rows, g0 + AP_TOK);       // new positions [lo, hi)
+    uint8_t *tile = tile_ptr(pr, g0, h);
     if (!tile) {
-        if (lane == 0) atomicOr(pr.status, ST_BAD_PAGE);
+        if (tid == 0) atomicOr(pr.status, ST_BAD_PAGE);
         return;
     }
-    const int t = p & 63, dim = b * QK + lane;
-    const int64_t src = (int64_t)r * pr.n_head_kv * HD + h * HD + dim;
-    int8_t q;
-    __half dh;
-    quant_block_warp(K[src], lane, q, dh);
-    tile[k_off(t, dim)] = (uint8_t)q;
-    if (lane == 0) *reinterpret_cast<__half *>(tile + kd_off(t, b)) = dh;
-    quant_block_warp(V[src], lane, q, dh);
-    tile[v_off(dim, t)] = (uint8_t)q;
-    if (lane == 0) *reinterpret_cast<__half *>(tile + vd_off(b, t)) = dh;
+    ApIn in;
+    ap_load(in, K, V, pos, g0, lo, hi, pr.n_head_kv, h, tid);
+#pragma unroll
+    for (int it = 0; it < 2; it++) {
+        const int p = (tid >> 2) + 64 * it, t = p >> 3, b = p & 7;
+#pragma unroll
+        for (int kv = 0; kv < 2; kv++) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(in.x[it][kv][e]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float d  = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+            uint8_t q[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) q[e] = (uint8_t)(int8_t)(int)roundf(__fmul_rn(in.x[it][kv][e], id));
+            const int dim0 = b * QK + sub * 8;
+            *reinterpret_cast<uint2 *>(kv ? &vs[t][dim0] : &ks[t][dim0]) =
+                make_uint2(q[0] | q[1] << 8 | q[2] << 16 | (uint32_t)q[3] << 24,
+                           q[4] | q[5] << 8 | q[6] << 16 | (uint32_t)q[7] << 24);
+            if (sub == 0) {
+                if (kv) vd[b][t] = __float2half_rn(d);
+                else kd[t][b] = __float2half_rn(d);
+            }
+        }
+    }
+    __syncthreads();
+    const int tt0 = g0 & 63;   // the group's first token inside the tile
+    {   // K: row tid >> 4, chunk tid & 15
+        const int t = tid >> 4, c = tid & 15;
+        if (g0 + t >= lo && g0 + t < hi)
+            *reinterpret_cast<uint4 *>(tile + TILE_KQ + (tt0 + t) * HD + ((c ^ kswz(tt0 + t)) << 4)) =
+                *reinterpret_cast<const uint4 *>(&ks[t][c * 16]);
+    }
+    {   // V: dim tid, the group's 16-token chunk of that dim
+        const int dim = tid;
+        uint8_t *dst = tile + v_off(dim, tt0);   // 16-byte aligned: tt0 is a multiple of 16
+        if (lo == g0 && hi == g0 + AP_TOK) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                w[k] = vs[4 * k][dim] | vs[4 * k + 1][dim] << 8 | vs[4 * k + 2][dim] << 16 | (uint32_t)vs[4 * k + 3][dim] << 24;
+            *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+            for (int32_t r = lo; r < hi; r++) dst[r - g0] = vs[r - g0][dim];
+        }
+    }
+    if (tid < AP_TOK) {   // K scales of token tid (16 bytes), V scales of the group per block
+        const int t = tid;
+        if (g0 + t >= lo && g0 + t < hi)
+            *reinterpret_cast<uint4 *>(tile + kd_off(tt0 + t, 0)) = *reinterpret_cast<const uint4 *>(&kd[t][0]);
+    } else if (tid < AP_TOK + NBLK) {
+        const int b = tid - AP_TOK;
+        for (int32_t r = lo; r < hi; r++)
+            *reinterpret_cast<__half *>(tile + vd_off(b, tt0 + (r - g0))) = vd[b][r - g0];
+    }
 }
 
 cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const float *V, int32_t n_rows,
                           cudaStream_t st) {
-    const int64_t warps = (int64_t)n_rows * pr.n_head_kv * NBLK;
-    const int blocks = (int)((warps * 32 + 255) / 256);
-    k_append<<<blocks, 256, 0, st>>>(pr, pos, K, V, n_rows);
+    if (n_rows < 1) return cudaSuccess;
+    const int32_t groups = (pos + n_rows - 1) / AP_TOK - pos / AP_TOK + 1;
+    k_append<<<dim3((unsigned)groups, (unsigned)pr.n_head_kv), 256, 0, st>>>(pr, pos, K, V, n_rows);
     count_launches(1);
     return cudaGetLastError();
 }

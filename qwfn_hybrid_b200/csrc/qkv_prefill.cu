@@ -589,6 +589,9 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
         if (!store(A, uA)) return;
 }
 
+// SPARSE: P.qsa_bits holds each query row's kept-block bitset (qkv_attn_prefill_qsa); the dense
+// instantiation has no trace of it.
+template <bool SPARSE>
 __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ PrefillParams P,
                                                      const __grid_constant__ PfPlanInline PL) {
     extern __shared__ uint8_t smem_raw[];
@@ -759,18 +762,18 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
             const int qpos = g < P.n_groups && tok < P.Tc ? P.pos0 + tok : -1;
             float m_ref = -INFINITY, l = 0.f;
             // the row's kept-block word of each KV tile (sparse prefill), one tile ahead
-            const uint32_t *wrow = P.qsa_bits && qpos >= 0 ? P.qsa_bits + (int64_t)tok * P.qsa_words : nullptr;
+            const uint32_t *wrow = SPARSE && qpos >= 0 ? P.qsa_bits + (int64_t)tok * P.qsa_words : nullptr;
             const int kt_vis = qpos >= 0 ? qpos / KT : -1;   // last KV tile with a visible key
-            uint32_t word_next = wrow && sg.kt0 <= kt_vis ? __ldg(wrow + sg.kt0) : ~0u;
+            uint32_t word_next = SPARSE && wrow && sg.kt0 <= kt_vis ? __ldg(wrow + sg.kt0) : ~0u;
             for (int k = 0; k < sg.nk; k++) {
                 const uint32_t j = it + k, b = j & 1;
                 if (!(ok = wait_all(&B->s_full[b], (j >> 1) & 1))) break;
                 tc_fence_after();
                 const uint32_t scol = tmem + lane_base + TM_S + b * KT;
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
-                const uint32_t word = word_next;
-                if (wrow) word_next = sg.kt0 + k + 1 <= kt_vis && k + 1 < sg.nk ? __ldg(wrow + sg.kt0 + k + 1) : ~0u;
-                const bool full = __all_sync(0xffffffffu, nvis == KT && word == ~0u);
+                const uint32_t word = SPARSE ? word_next : ~0u;
+                if (SPARSE && wrow) word_next = sg.kt0 + k + 1 <= kt_vis && k + 1 < sg.nk ? __ldg(wrow + sg.kt0 + k + 1) : ~0u;
+                const bool full = __all_sync(0xffffffffu, nvis == KT && (!SPARSE || word == ~0u));
                 const float smax = full ? row_max<true>(scol, nvis, word) : row_max<false>(scol, nvis, word);
                 tc_fence_before();
                 mbar_arrive(&B->s_read[b]);
@@ -947,7 +950,9 @@ static cudaError_t configure_prefill() {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64 && configured[dev]) return cudaSuccess;
-    e = cudaFuncSetAttribute(pf::k_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
+    e = cudaFuncSetAttribute(pf::k_prefill<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(pf::k_prefill<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM_BYTES);
     if (e == cudaSuccess && dev >= 0 && dev < 64) configured[dev] = true;
     return e;
 }
@@ -978,7 +983,7 @@ int prefill_max_pairs() {
     cudaLaunchAttribute attr[2];
     prefill_config(cfg, attr, 2 * 64, nullptr);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, pf::k_prefill, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, pf::k_prefill<false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -994,7 +999,9 @@ cudaError_t launch_prefill(const PrefillParams &p, const PfPlanInline &plan, cud
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
     prefill_config(cfg, attr, (unsigned)p.n_ctas, st);
-    if ((e = cudaLaunchKernelEx(&cfg, pf::k_prefill, p, plan)) != cudaSuccess) return e;
+    if ((e = p.qsa_bits ? cudaLaunchKernelEx(&cfg, pf::k_prefill<true>, p, plan)
+                        : cudaLaunchKernelEx(&cfg, pf::k_prefill<false>, p, plan)) != cudaSuccess)
+        return e;
     if ((e = launch_pdl(pf::k_prefill_merge, (unsigned)(p.n_tiles * (PF_ROWS / pf::MG_ROWS)), 256, 0, st, p, plan)) !=
         cudaSuccess)
         return e;

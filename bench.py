@@ -58,11 +58,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline only: skip the ragged and configs sub-records")
-    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "qsa", "proj"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "qsa", "proj", "append"],
+                    default="cfg2",
                     help="cfg2 (default, the headline line with its sub-records): BASELINE configs[1]; cfg1/cfg3/"
                          "cfg4/cfg5: configs[0]/[2]/[3]/[4] alone; qsa: configs[3]'s context and tokens through the "
                          "model's own lightning indexer (select + gather + sparse attention); proj: the fused decode "
-                         "projections + norm + rope + q8_0 append of configs[1]'s step")
+                         "projections + norm + rope + q8_0 append of configs[1]'s step; append: kernel A alone")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
@@ -1240,6 +1241,63 @@ def run_proj(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_append(args) -> None:
+    """Kernel A alone (BASELINE configs[2]'s append step at 4096 rows per call): F32 K and V rows
+    into a 2-head q8_0 engine.  16 launches fill 65536 positions, then a CUDA graph of 16
+    back-to-back 4096-row appends (rewriting those positions) is replayed."""
+    import torch
+    rank, ws, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import qwfn_hybrid_b200 as Q
+    n, R = 65536, 4096
+    eng = Q.Engine(n_layer=1, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=n, n_slots=1, device=local)
+    eng.seq_alloc(0)
+    gen = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
+    K = torch.randn(n, KV_DIM, generator=gen, device=dev)
+    V = torch.randn(n, KV_DIM, generator=gen, device=dev)
+    for a in range(0, n, R):
+        eng.append(0, 0, a, K[a:a + R], V[a:a + R])
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for a in range(0, n, R):
+            eng.append(0, 0, a, K[a:a + R], V[a:a + R])
+    for _ in range(max(args.warmup, 3)):
+        g.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    per = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per.append(e0.elapsed_time(e1) / (n // R))
+    clk = clocks.stop()
+    del g
+    assert eng.device_status() == 0
+    us = 1e3 * statistics.median(per)
+    nbytes = R * (2 * KV_DIM * 4 + 2 * ROW_BYTES)
+    pk = peaks()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "q8_0 append (kernel A): µs per 4096-row append of F32 K and V rows", "value": us,
+            "unit": "us/append", "n_gpus": ws, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32 in, q8_0 out",
+            "data": "synthetic N(0,1) (torch Philox, seed 5+1000*rank)",
+            "config": {"workload": "4096-row appends, 2 KV heads x 256, 16 per CUDA-graph replay (median of the steps)",
+                       "parallelism": f"independent engines x{ws} (replicas)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm"], "unit": "GB/s", "frac": gbs / pk["hbm"],
+                         "peak_source": pk["hbm_src"], "bytes_per_launch": nbytes, "kernel": "k_append"},
+            "gpu_launches": n // R, "clocks": clk,
+        }), flush=True)
+
+
 class _DevRange:
     """A device address range as a float32 tensor (CUDA array interface)."""
 
@@ -1264,6 +1322,8 @@ def main():
         run_qsa(args)
     elif args.workload == "proj":
         run_proj(args)
+    elif args.workload == "append":
+        run_append(args)
     else:
         run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

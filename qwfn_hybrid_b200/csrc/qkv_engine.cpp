@@ -69,6 +69,7 @@ struct qkv_engine {
     uint8_t  *d_rec     = nullptr;    // [n_slots][rec_slot_bytes]
     uint8_t  *d_rb      = nullptr;    // [n_slots][n_rollback][rec_slot_bytes]
     uint16_t *d_summary = nullptr;    // [n_layer][n_slots][n_head_kv][max_blocks][HD]
+    float    *d_sel_scores = nullptr; // kernel B1 scratch: [MAX_SEQ][n_head_kv][max_blocks] block scores
     float    *d_partial = nullptr;    // kernel C: per-cluster partial records
     size_t    partial_bytes = 0;
     int32_t  *d_status  = nullptr;
@@ -312,6 +313,7 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_rec);
     cudaFree(eng->d_rb);
     cudaFree(eng->d_summary);
+    cudaFree(eng->d_sel_scores);
     cudaFree(eng->d_partial);
     cudaFree(eng->d_status);
     cudaFree(eng->d_pf_q);
@@ -397,6 +399,9 @@ extern "C" qkv_status qkv_create(const qkv_config *cfg, int device, qkv_engine *
         if (r == QKV_OK)
             r = dalloc(eng, eng->d_summary, (size_t)c.n_layer * c.n_slots * c.n_head_kv * eng->max_blocks * HD * 2,
                        "block summaries");
+        if (r == QKV_OK && eng->max_blocks > 0)
+            r = dalloc(eng, eng->d_sel_scores, (size_t)MAX_SEQ * c.n_head_kv * eng->max_blocks * sizeof(float),
+                       "block scores");
         if (r == QKV_OK) {
             // one record per unit: at most one wave of co-resident CTAs plus one unit per pair of
             // a launch, for the widest query group of each kernel instance
@@ -1082,7 +1087,7 @@ extern "C" qkv_status qkv_select_blocks(qkv_engine *eng, int32_t layer, const in
         P.Q = Q + (size_t)base * T * eng->cfg.n_head * HD;
         P.summary = eng->d_summary + (size_t)layer * eng->cfg.n_slots * eng->cfg.n_head_kv * eng->max_blocks * HD;
         P.idx_out = idx_out + (size_t)base * eng->cfg.n_head_kv * top_k;
-        P.scores_out = scores_out ? scores_out + (size_t)base * eng->cfg.n_head_kv * eng->max_blocks : nullptr;
+        P.scores = scores_out ? scores_out + (size_t)base * eng->cfg.n_head_kv * eng->max_blocks : eng->d_sel_scores;
         P.n_seq = ns;
         P.T = T;
         P.n_head = eng->cfg.n_head;

@@ -110,7 +110,7 @@ struct SelectParams {
     const float    *Q;            // [n_seq][T][n_head][HD]
     const uint16_t *summary;      // layer base: [slot][n_head_kv][max_blocks][HD] fp16
     int32_t        *idx_out;      // [n_seq][n_head_kv][top_k]
-    float          *scores_out;   // nullable [n_seq][n_head_kv][max_blocks]
+    float          *scores;       // [n_seq][n_head_kv][max_blocks]: the caller's scores_out, or engine scratch
     int32_t n_seq, T, n_head, n_head_kv, G, top_k, max_blocks;
     int32_t seq_slot[MAX_SEQ];
     int32_t seq_nblk[MAX_SEQ];    // candidate blocks of each sequence

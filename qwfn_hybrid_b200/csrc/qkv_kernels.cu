@@ -170,8 +170,8 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // (the reference's rms() and rope(), src/qwfn_graph.cpp:125-132), then K and V quantised to q8_0
 // into the page (kernel A's rounding).  One kernel:
 //
-// k_project_dot: a warp per row; lane l reads the row's 16-byte chunks l, l+32, ... (coalesced: a
-// warp load covers 512 contiguous bytes; the row is prefetched into L2 first), and sums
+// k_project_dot: a warp per four rows; lane l reads each row's 16-byte chunks l, l+32, ... (coalesced:
+// a warp load covers 512 contiguous bytes; the rows are prefetched into L2 first), and sums
 //   lane_l = fmaf(w, x, ...) over its chunks in order, dims in order within a chunk
 // (bf16 weights are exact in fp32); y = xor butterfly 16, 8, 4, 2, 1 of the lane sums.  Rows in
 // the order: query heads (the query rows of attn_q.weight's per-head query/gate interleave), K
@@ -180,8 +180,9 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // warp order, scale = 1/sqrt(sum/256 + eps), y * scale * w), rope on pairs (i, i + half) of the
 // first rope_dim dims with cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32
 // multiplication); the query to Q_out, K and V quantised into the page.
-constexpr int PJ_DOT_THREADS = 256, PJ_ROWS_CTA = PJ_DOT_THREADS / 32;   // a warp per row
-constexpr int PJ_BATCH = 5;    // 16-byte loads in flight per lane (after the row's L2 prefetch)
+constexpr int PJ_RW = 4;       // rows per warp: each x value read from shared memory serves four rows
+constexpr int PJ_DOT_THREADS = 256, PJ_ROWS_CTA = PJ_DOT_THREADS / 32 * PJ_RW;
+constexpr int PJ_BATCH = 2;    // chunks per row in flight per lane (x PJ_RW rows; after the rows' L2 prefetch)
 
 __device__ __forceinline__ float warp_sum_bfly(float v) {
 #pragma unroll
@@ -244,69 +245,77 @@ __device__ void project_epilogue(const ProjectParams &p, int u, float *yb, float
     }
 }
 
-__global__ void __launch_bounds__(PJ_DOT_THREADS, 5) k_project_dot(const ProjectParams p) {
+__global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const ProjectParams p) {
     extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
     const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD, nc = p.n_embd / 8;
-    const int g = blockIdx.x * (PJ_DOT_THREADS / 32) + wid;   // this warp's row (every CTA full: 8 | 256)
+    const int g0 = (blockIdx.x * (PJ_DOT_THREADS / 32) + wid) * PJ_RW;   // this warp's first row (all in one head)
     const uint16_t *W;
-    if (g < nq * HD) W = p.Wq + ((int64_t)(g / HD) * 2 * HD + g % HD) * p.n_embd;
-    else if (g < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g - nq * HD) * p.n_embd;
-    else W = p.Wv + (int64_t)(g - (nq + p.n_head_kv) * HD) * p.n_embd;
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);
-    // the whole row is requested at once (into L2, no registers held), then read in batches
-    for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + c));
+    if (g0 < nq * HD) W = p.Wq + ((int64_t)(g0 / HD) * 2 * HD + g0 % HD) * p.n_embd;
+    else if (g0 < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g0 - nq * HD) * p.n_embd;
+    else W = p.Wv + (int64_t)(g0 - (nq + p.n_head_kv) * HD) * p.n_embd;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);   // row r at w4 + r * nc
+    // the warp's rows are requested at once (into L2, no registers held), then read in batches
+    for (int r = 0; r < PJ_RW; r++)
+        for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + (int64_t)r * nc + c));
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
     for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
         xs4[(i & 1) * T * nc + i / 2] = x4[i];
     __syncthreads();
-    float acc[PJ_MAX_T] = {0.f, 0.f, 0.f, 0.f};
+    float acc[PJ_RW][PJ_MAX_T] = {};
     for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
-        uint4 wb[PJ_BATCH];
+        uint4 wb[PJ_BATCH][PJ_RW];
 #pragma unroll
         for (int j = 0; j < PJ_BATCH; j++) {
             const int c = lane + 32 * (j0 + j);
-            wb[j] = c < nc ? __ldcs(w4 + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int r = 0; r < PJ_RW; r++) wb[j][r] = c < nc ? __ldcs(w4 + (int64_t)r * nc + c) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int j = 0; j < PJ_BATCH; j++) {
             const int c = lane + 32 * (j0 + j);
             if (c >= nc) break;
-            const uint32_t wv[4] = {wb[j].x, wb[j].y, wb[j].z, wb[j].w};
 #pragma unroll
             for (int t = 0; t < PJ_MAX_T; t++) {
                 if (t >= T) break;
-                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];
-                float a = acc[t];
-                a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
-                a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
-                a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
-                a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
-                a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
-                a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
-                a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
-                a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
-                acc[t] = a;
+                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];   // one read for the warp's rows
+#pragma unroll
+                for (int r = 0; r < PJ_RW; r++) {
+                    const uint32_t wv[4] = {wb[j][r].x, wb[j][r].y, wb[j][r].z, wb[j][r].w};
+                    float a = acc[r][t];
+                    a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
+                    a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
+                    a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
+                    a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
+                    a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
+                    a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
+                    a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
+                    a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
+                    acc[r][t] = a;
+                }
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++) {
-        if (t >= T) break;
-        const float y = warp_sum_bfly(acc[t]);
-        if (lane == t) {
-            p.y[(int64_t)t * n_rows + g] = y;
-            __threadfence();
+    for (int r = 0; r < PJ_RW; r++)
+#pragma unroll
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            const float y = warp_sum_bfly(acc[r][t]);
+            if (lane == t) p.y[(int64_t)t * n_rows + g0 + r] = y;
         }
-    }
     // the CTA that completes a head's rows (HD / PJ_ROWS_CTA CTAs per head) runs its epilogue and
-    // resets the head's counter for the next call; nothing waits
+    // resets the head's counter for the next call; nothing waits.  One release per CTA: the
+    // barrier orders every warp's rows before thread 0's fence and arrival.
     __shared__ float yb[HD];
     __shared__ float wsum[HD / 32];
     __shared__ int s_last;
     const int u = blockIdx.x * PJ_ROWS_CTA / HD;
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(p.cnt + u, 1) == HD / PJ_ROWS_CTA - 1;
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(p.cnt + u, 1) == HD / PJ_ROWS_CTA - 1;
+    }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
@@ -471,30 +480,45 @@ cudaError_t launch_block_summary(const PoolRef &pr, int32_t b0, int32_t b1, uint
 }
 
 // ------------------------------------------------------------------------------------ kernel B1
-// Block scores and top-k.  A cluster of SEL_CL CTAs (256 threads each) per (sequence, KV head);
-// CTA r scores the candidate blocks [r*nb/SEL_CL, (r+1)*nb/SEL_CL).  Groups of 8 lanes compute one
-// dot product in the oracle's fixed order: lane l takes dims 32l..32l+31 with sequential fmaf,
-// then a fixed tree over the 8 lanes.  The group's lane 0 sums relu(dot) over the G*T query rows
-// in order (t-major), so the score of every block is bit-exact with the CPU restatement.  The
-// query rows sit in shared memory as 8 segments of 32 dims padded to 36 floats, so the 8 lanes of
-// a group read their segments with conflict-free 16-byte loads.  Every CTA then copies the other
-// CTAs' scores through distributed shared memory and ranks its own blocks: score descending, block
-// index ascending; a candidate's rank is the number of candidates ahead of it (early exit once
-// >= top_k).
-constexpr int SEL_CL = 8, SEL_SEG = 36;
-__global__ void __cluster_dims__(SEL_CL, 1, 1) __launch_bounds__(256) k_select(const SelectParams p) {
-    extern __shared__ float sm_sel[];
-    cg::cluster_group cluster = cg::this_cluster();
-    const int r = (int)cluster.block_rank(), sh = blockIdx.x / SEL_CL;
-    const int s = sh / p.n_head_kv, h = sh % p.n_head_kv;
+// Block scores and top-k, two kernels.
+// k_select_score: CTA (sequence x KV head, chunk of SEL_CHUNK candidate blocks), 256 threads.
+// Groups of 8 lanes compute one dot product in the oracle's fixed order: lane l takes dims
+// 32l..32l+31 with sequential fmaf, then a fixed tree over the 8 lanes.  The group's lane 0 sums
+// relu(dot) over the G*T query rows in order (t-major), so every score is bit-exact with the CPU
+// restatement; four rows' dot products run side by side.  The query rows sit in shared memory as
+// 8 segments of 32 dims padded to 36 floats, so the 8 lanes of a group read their segments with
+// conflict-free 16-byte loads; the next round's summary bytes are loaded during the current round.
+// k_select_rank: CTA (sequence x KV head, 1/SEL_RK of the candidates): all scores into shared
+// memory, then each candidate's rank (score descending, block index ascending) is the number of
+// candidates ahead of it, counted by a whole warp.
+constexpr int SEL_SEG = 36, SEL_CHUNK = 64, SEL_RK = 8;
+__global__ void __launch_bounds__(256) k_select_score(const SelectParams p) {
+    extern __shared__ float qs[];                    // [nq][8][SEL_SEG]
+    const int sh = blockIdx.x, s = sh / p.n_head_kv, h = sh % p.n_head_kv;
     const int nq = p.T * p.G;
-    float *qs     = sm_sel;                          // [nq][8][SEL_SEG]
-    float *scores = sm_sel + nq * 8 * SEL_SEG;       // [max_blocks]: every candidate's score
     const int slot = p.seq_slot[s], nb = p.seq_nblk[s];
-    const int c0 = (int)((int64_t)nb * r / SEL_CL), c1 = (int)((int64_t)nb * (r + 1) / SEL_CL);
-    for (int e = threadIdx.x; e < nq * HD; e += blockDim.x) {
-        const int n = e / HD, i = e % HD, t = n / p.G, j = n % p.G;
-        qs[(n * 8 + (i >> 5)) * SEL_SEG + (i & 31)] = p.Q[(((int64_t)s * p.T + t) * p.n_head + h * p.G + j) * HD + i];
+    const int c0 = blockIdx.y * SEL_CHUNK, c1 = min(nb, c0 + SEL_CHUNK);
+    if (c0 >= nb) return;
+    // the group's query rows, float4 loads all issued before the stores (nq * HD / 4 <= 16 per thread)
+    {
+        constexpr int QV = 16;
+        float4 v[QV];
+#pragma unroll
+        for (int k = 0; k < QV; k++) {
+            const int e = threadIdx.x + k * 256;   // float4 index
+            if (e < nq * HD / 4) {
+                const int n = e / (HD / 4), i = 4 * (e % (HD / 4)), t = n / p.G, j = n % p.G;
+                v[k] = *reinterpret_cast<const float4 *>(p.Q + (((int64_t)s * p.T + t) * p.n_head + h * p.G + j) * HD + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < QV; k++) {
+            const int e = threadIdx.x + k * 256;
+            if (e < nq * HD / 4) {
+                const int n = e / (HD / 4), i = 4 * (e % (HD / 4));
+                *reinterpret_cast<float4 *>(&qs[(n * 8 + (i >> 5)) * SEL_SEG + (i & 31)]) = v[k];
+            }
+        }
     }
     __syncthreads();
     // Warp-uniform loop: each warp takes 4 blocks per round (one per 8-lane group); every lane
@@ -502,16 +526,27 @@ __global__ void __cluster_dims__(SEL_CL, 1, 1) __launch_bounds__(256) k_select(c
     const int lane8 = threadIdx.x & 7, grp = (threadIdx.x & 31) >> 3;
     const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
     const uint16_t *sum_base = p.summary + ((int64_t)slot * p.n_head_kv + h) * p.max_blocks * HD;
+    auto load_sum = [&](int bw_, uint4 (&w)[4]) {   // the lane's 64 summary bytes of the group's block
+        const int b_ = bw_ + grp;
+        const bool live_ = b_ < c1 && !(b_ == 0 || b_ >= nb - 2);
+        const uint4 *srow = reinterpret_cast<const uint4 *>(sum_base + (int64_t)(live_ ? b_ : 0) * HD + lane8 * 32);
+#pragma unroll
+        for (int k = 0; k < 4; k++) w[k] = live_ ? srow[k] : make_uint4(0, 0, 0, 0);
+    };
+    float *scores = p.scores + ((int64_t)s * p.n_head_kv + h) * p.max_blocks;
+    uint4 wnext[4];
+    if (c0 + warp * 4 < c1) load_sum(c0 + warp * 4, wnext);
     for (int bw = c0 + warp * 4; bw < c1; bw += nwarp * 4) {
         const int b = bw + grp;
         const bool forced = b == 0 || b >= nb - 2;
-        const bool live   = b < c1 && !forced;
+        uint4 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) w[k] = wnext[k];
+        if (bw + nwarp * 4 < c1) load_sum(bw + nwarp * 4, wnext);
         float sv[32];
-        const uint16_t *srow = sum_base + (int64_t)(live ? b : 0) * HD + lane8 * 32;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const uint4 w = live ? reinterpret_cast<const uint4 *>(srow)[k] : make_uint4(0, 0, 0, 0);
-            const __half2 *hh = reinterpret_cast<const __half2 *>(&w);
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&w[k]);
 #pragma unroll
             for (int m = 0; m < 4; m++) {
                 const float2 f = __half22float2(hh[m]);
@@ -520,63 +555,76 @@ __global__ void __cluster_dims__(SEL_CL, 1, 1) __launch_bounds__(256) k_select(c
             }
         }
         float score = 0.0f;
-        for (int n = 0; n < nq; n++) {
-            const float4 *q = reinterpret_cast<const float4 *>(qs + (n * 8 + lane8) * SEL_SEG);
-            float acc = 0.0f;
+        for (int n0 = 0; n0 < nq; n0 += 4) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                const float4 qk = q[k];
-                acc = __fmaf_rn(qk.x, sv[4 * k], acc);
-                acc = __fmaf_rn(qk.y, sv[4 * k + 1], acc);
-                acc = __fmaf_rn(qk.z, sv[4 * k + 2], acc);
-                acc = __fmaf_rn(qk.w, sv[4 * k + 3], acc);
+#pragma unroll
+                for (int rr = 0; rr < 4; rr++) {
+                    const int n = min(n0 + rr, nq - 1);
+                    const float4 qk = reinterpret_cast<const float4 *>(qs + (n * 8 + lane8) * SEL_SEG)[k];
+                    acc[rr] = __fmaf_rn(qk.x, sv[4 * k], acc[rr]);
+                    acc[rr] = __fmaf_rn(qk.y, sv[4 * k + 1], acc[rr]);
+                    acc[rr] = __fmaf_rn(qk.z, sv[4 * k + 2], acc[rr]);
+                    acc[rr] = __fmaf_rn(qk.w, sv[4 * k + 3], acc[rr]);
+                }
             }
-            // fixed tree: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))
-            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
-            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-            score = __fadd_rn(score, acc > 0.0f ? acc : 0.0f);
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) {
+                // fixed tree: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))
+                float a = acc[rr];
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+                if (n0 + rr < nq) score = __fadd_rn(score, a > 0.0f ? a : 0.0f);
+            }
         }
         if (forced) score = __int_as_float(0x7f800000);
-        if (lane8 == 0 && b < c1) {
-            scores[b] = score;
-            if (p.scores_out) p.scores_out[((int64_t)s * p.n_head_kv + h) * p.max_blocks + b] = score;
-        }
+        if (lane8 == 0 && b < c1) scores[b] = score;
     }
-    cluster.sync();   // every CTA's scores are in its shared memory
-    for (int q = 0; q < SEL_CL; q++) {
-        if (q == r) continue;
-        const int q0 = (int)((int64_t)nb * q / SEL_CL), q1 = (int)((int64_t)nb * (q + 1) / SEL_CL);
-        const float *remote = cluster.map_shared_rank(scores, q);
-        for (int i = q0 + threadIdx.x; i < q1; i += blockDim.x) scores[i] = remote[i];
-    }
-    cluster.sync();   // no CTA leaves while its shared memory is read; every CTA holds all scores
+}
+
+__global__ void __launch_bounds__(256) k_select_rank(const SelectParams p) {
+    extern __shared__ float sc[];                    // [nb] every candidate's score
+    const int sh = blockIdx.x, s = sh / p.n_head_kv, h = sh % p.n_head_kv, r = blockIdx.y;
+    const int nb = p.seq_nblk[s];
+    const int c0 = (int)((int64_t)nb * r / SEL_RK), c1 = (int)((int64_t)nb * (r + 1) / SEL_RK);
     int32_t *out = p.idx_out + ((int64_t)s * p.n_head_kv + h) * p.top_k;
     if (nb <= p.top_k) {
         for (int k = c0 + threadIdx.x; k < c1; k += blockDim.x) out[k] = k;
-        if (r == SEL_CL - 1)
+        if (r == SEL_RK - 1)
             for (int k = nb + threadIdx.x; k < p.top_k; k += blockDim.x) out[k] = -1;
         return;
     }
-    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
-        const float si = scores[i];
-        int rank = 0;
-        for (int j = 0; j < nb && rank < p.top_k; j++) {
-            const float sj = scores[j];
-            rank += (sj > si) || (sj == si && j < i);
+    const float *scores = p.scores + ((int64_t)s * p.n_head_kv + h) * p.max_blocks;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) sc[i] = scores[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    for (int i = c0 + warp; i < c1; i += nwarp) {
+        const float si = sc[i];
+        int cnt = 0;
+#pragma unroll 8
+        for (int j = lane; j < nb; j += 32) {
+            const float sj = sc[j];
+            cnt += (sj > si) || (sj == si && j < i);
         }
-        if (rank < p.top_k) out[rank] = i;
+        const int rank = __reduce_add_sync(0xffffffffu, cnt);
+        if (lane == 0 && rank < p.top_k) out[rank] = i;
     }
 }
 
 cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
-    const size_t smem = ((size_t)p.T * p.G * 8 * SEL_SEG + p.max_blocks) * sizeof(float);
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    k_select<<<(unsigned)(p.n_seq * p.n_head_kv * SEL_CL), 256, smem, st>>>(p);
-    count_launches(1);
+    int max_nb = 1;
+    for (int i = 0; i < p.n_seq; i++) max_nb = std::max(max_nb, p.seq_nblk[i]);
+    const size_t qsm = (size_t)p.T * p.G * 8 * SEL_SEG * sizeof(float), rsm = (size_t)max_nb * sizeof(float);
+    cudaError_t e;
+    if (qsm > 48 * 1024 && (e = cudaFuncSetAttribute(k_select_score, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm)) != cudaSuccess)
+        return e;
+    if (rsm > 48 * 1024 && (e = cudaFuncSetAttribute(k_select_rank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm)) != cudaSuccess)
+        return e;
+    k_select_score<<<dim3((unsigned)(p.n_seq * p.n_head_kv), (unsigned)((max_nb + SEL_CHUNK - 1) / SEL_CHUNK)), 256, qsm, st>>>(p);
+    k_select_rank<<<dim3((unsigned)(p.n_seq * p.n_head_kv), SEL_RK), 256, rsm, st>>>(p);
+    count_launches(2);
     return cudaGetLastError();
 }
 

@@ -374,7 +374,7 @@ qkv_status qkv_cache_view_get(const qkv_engine *eng, int32_t layer, qkv_cache_vi
  * ggml-alloc, nothing may grow mid-graph) or code under an allocator that owns the whole device.
  * Same attention as qkv_attn_decode over a cache described by a qkv_cache_view (from
  * qkv_cache_view_get; block_table has n_slots rows), Q/out device F32 [n_seq][T][n_head][head_dim].
- * The split-K scratch is a fixed 6.1 MiB array compiled into the library (held on every GPU that
+ * The split-K scratch is a fixed 6.05 MiB array compiled into the library (held on every GPU that
  * loads it until exit), so T * n_head / n_head_kv must be <= 32 (else QKV_ERR_UNSUPPORTED).
  * Calls share that array: calls that overlap on the GPU race.  The first call on a device looks
  * up the array's address and should come before any stream capture.  Bounds violations and

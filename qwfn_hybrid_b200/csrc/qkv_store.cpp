@@ -72,10 +72,12 @@ extern "C" qkv_status qkv_store_save(qkv_store *store, int32_t slot, const int32
     e.tok.assign(tok, tok + n_tok);
     if ((r = qkv_snapshot_save(store->eng, slot, &e.snap, stream)) != QKV_OK) return r;
     e.bytes = qkv::snapshot_held_bytes(e.snap);
-    if (e.bytes > store->cap) {   // a snapshot above the cap is not kept
+    if (e.bytes > store->cap) {   // larger than the whole budget on its own: released at once
         qkv_snapshot_release(store->eng, e.snap);
         return QKV_OK;
     }
+    // an entry with the same token list gives way to the new one, which goes to the most recent
+    // end; then the least recently used entries leave until the count and the bytes fit
     for (size_t k = 0; k < store->saved.size(); k++)
         if (store->saved[k].tok == e.tok) {
             store->drop(k);
@@ -91,7 +93,8 @@ extern "C" qkv_status qkv_store_save(qkv_store *store, int32_t slot, const int32
     return QKV_OK;
 }
 
-// the longest saved sequence that prompt strictly extends, -1 if none (best_saved)
+// Index of the entry whose token list is a proper prefix of `prompt` and has the most tokens (the
+// server's best_saved), or -1 when no entry qualifies.
 static int best_saved(const qkv_store *s, const int32_t *prompt, int32_t n) {
     int best = -1;
     for (size_t k = 0; k < s->saved.size(); k++) {
@@ -123,6 +126,7 @@ extern "C" qkv_status qkv_store_prefix_split(const qkv_store *store, const int32
         return QKV_ERR_INVALID;
     *split_at = 0;
     if (n_consumed >= min_prefix) return QKV_OK;
+    // L: the longest run of leading tokens the prompt shares with any entry
     size_t L = 0;
     for (const Entry &e : store->saved) {
         const size_t m = std::min(e.tok.size(), (size_t)n_prompt);
@@ -130,7 +134,7 @@ extern "C" qkv_status qkv_store_prefix_split(const qkv_store *store, const int32
         while (l < m && e.tok[l] == prompt[l]) l++;
         L = std::max(L, l);
     }
-    bool have = false;   // already saved at exactly this point
+    bool have = false;   // some entry ends exactly where the shared run ends
     for (const Entry &e : store->saved) have |= e.tok.size() == L && std::equal(e.tok.begin(), e.tok.end(), prompt);
     if (L >= (size_t)min_prefix && L + 16 < (size_t)n_prompt && L >= (size_t)n_consumed + 2 && !have)
         *split_at = (int32_t)L;

@@ -71,11 +71,11 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 // Phase timestamps for latency analysis, compiled only with -DQKV_TIMELINE (the product build
 // never defines it): thread 0 of every CTA notes %globaltimer at its phases and appends one record
-// {kernel, block, t[0..9]} to g_tl_rec; qkv_tl_read copies the records out.
+// {kernel, block, t[0..17]} to g_tl_rec; qkv_tl_read copies the records out.
 #ifdef QKV_TIMELINE
-__device__ unsigned long long g_tl_rec[1 << 16][12];
+__device__ unsigned long long g_tl_rec[1 << 16][20];
 __device__ unsigned int g_tl_n;
-#define TL_DECL unsigned long long tl_[10] = {};
+#define TL_DECL unsigned long long tl_[18] = {};
 #define TL(i) do { if (threadIdx.x == 0) tl_[i] = global_ns(); } while (0)
 #define TL_FLUSH(kid)                                                             \
     do {                                                                          \
@@ -83,13 +83,23 @@ __device__ unsigned int g_tl_n;
             const unsigned k_ = atomicAdd(&g_tl_n, 1u) & 0xffffu;                 \
             g_tl_rec[k_][0] = (kid);                                              \
             g_tl_rec[k_][1] = blockIdx.x;                                         \
-            for (int i_ = 0; i_ < 10; i_++) g_tl_rec[k_][2 + i_] = tl_[i_];       \
+            for (int i_ = 0; i_ < 18; i_++) g_tl_rec[k_][2 + i_] = tl_[i_];       \
         }                                                                         \
     } while (0)
 #else
 #define TL_DECL
 #define TL(i) do { } while (0)
 #define TL_FLUSH(kid) do { } while (0)
+#endif
+// Stamps inside the tile body (first two tiles of a unit), timeline build only.
+#ifdef QKV_TIMELINE
+#define TLT_ARG , unsigned long long *tl_, int tli
+#define TLT_PASS(x) , tl_, (x)
+#define TLT(k) do { if (threadIdx.x == 0 && tli >= 0) tl_[tli + (k)] = global_ns(); } while (0)
+#else
+#define TLT_ARG
+#define TLT_PASS(x)
+#define TLT(k) do { } while (0)
 #endif
 // Bounded wait: gives up after limit_ns (a copy that never lands) instead of spinning forever.
 __device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, uint64_t limit_ns) {
@@ -357,7 +367,7 @@ struct CtaSync {
 template <int NT, class Sync>
 __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool live, const uint8_t *qq, const float *qd,
                                           LaneShared<NT> &ls, RowState<NT> &rs, float c2, int w, int lane,
-                                          const Sync &sync) {
+                                          const Sync &sync TLT_ARG) {
     constexpr int NQ = NT * 8;
     const int g = lane >> 2, tig = lane & 3;
     const int lm = lane & 7, lmat = lane >> 3;
@@ -397,6 +407,7 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
             }
         }
     }
+    TLT(0);
     // ---------------- mask; does this warp outgrow the reference? -----------------------
     const int clo = cell0 + tk_lo, chi = cell0 + tk_hi;
     bool over = false;
@@ -445,6 +456,7 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
         }
     }
     sync();   // barrier 1: P (or the posted maxima) of every warp are in shared memory
+    TLT(1);
     if (ls.flag[0] | ls.flag[1] | ls.flag[2] | ls.flag[3]) {
         // ---- the reference moves: new reference, rescale O and sums, rewrite every P -------
 #pragma unroll
@@ -487,6 +499,7 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
         rs.lsum[j][0] += psum[j][0];
         rs.lsum[j][1] += psum[j][1];
     }
+    TLT(2);
     // ---------------- PV for this warp's 64 dims ------------------------------------------
     if (live) {
         const uint32_t vbase = smem_u32(tile) + TILE_VQ;
@@ -519,6 +532,14 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
             }
         }
     }
+#ifdef QKV_TIMELINE
+    if (tli >= 0) {   // the accumulators are complete once this warp's MMAs have retired
+        float z = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NT; j++) z += rs.O[0][j][0] + rs.O[3][j][3];
+        if (threadIdx.x == 0) tl_[tli + 3] = global_ns() + (z == 12345.0f ? 1 : 0);
+    }
+#endif
 }
 
 
@@ -672,7 +693,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             aborted = aborted || !__all_sync(0xffffffffu, landed);
             if (i == 0) TL(8);
             const int blk = sm.stage_blk[stage];
-            tile_step<NT>(sm.tile[stage], blk, blk >= 0 && !aborted, sm.qq, sm.qd, sm.ln, rs, c2, w, lane, CtaSync{});
+            tile_step<NT>(sm.tile[stage], blk, blk >= 0 && !aborted, sm.qq, sm.qd, sm.ln, rs, c2, w, lane, CtaSync{} TLT_PASS(i == 0 ? 10 : i == 1 ? 14 : -1));
             __syncthreads();   // barrier 2: the stage and P are free
             // After a wait that gave up no new copy starts: every copy this CTA issued has then
             // been waited for (bounded) by the time it exits.
@@ -1214,7 +1235,7 @@ extern "C" int qkv_tl_read(unsigned long long *host, int max_records) {
     unsigned int n = 0;
     if (cudaMemcpyFromSymbol(&n, qkv::dec::g_tl_n, sizeof n) != cudaSuccess) return -1;
     const int m = (int)(n < (unsigned)max_records ? n : (unsigned)max_records);
-    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::dec::g_tl_rec, (size_t)m * 12 * 8) != cudaSuccess) return -1;
+    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::dec::g_tl_rec, (size_t)m * 20 * 8) != cudaSuccess) return -1;
     const unsigned int zero = 0;
     cudaMemcpyToSymbol(qkv::dec::g_tl_n, &zero, sizeof zero);
     return m;

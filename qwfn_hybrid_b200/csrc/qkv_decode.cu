@@ -71,11 +71,11 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 // Phase timestamps for latency analysis, compiled only with -DQKV_TIMELINE (the product build
 // never defines it): thread 0 of every CTA notes %globaltimer at its phases and appends one record
-// {kernel, block, t[0..17]} to g_tl_rec; qkv_tl_read copies the records out.
+// {kernel, block, t[0..19]} to g_tl_rec; qkv_tl_read copies the records out.
 #ifdef QKV_TIMELINE
-__device__ unsigned long long g_tl_rec[1 << 16][20];
+__device__ unsigned long long g_tl_rec[1 << 16][22];
 __device__ unsigned int g_tl_n;
-#define TL_DECL unsigned long long tl_[18] = {};
+#define TL_DECL unsigned long long tl_[20] = {};
 #define TL(i) do { if (threadIdx.x == 0) tl_[i] = global_ns(); } while (0)
 #define TL_FLUSH(kid)                                                             \
     do {                                                                          \
@@ -83,7 +83,7 @@ __device__ unsigned int g_tl_n;
             const unsigned k_ = atomicAdd(&g_tl_n, 1u) & 0xffffu;                 \
             g_tl_rec[k_][0] = (kid);                                              \
             g_tl_rec[k_][1] = blockIdx.x;                                         \
-            for (int i_ = 0; i_ < 18; i_++) g_tl_rec[k_][2 + i_] = tl_[i_];       \
+            for (int i_ = 0; i_ < 20; i_++) g_tl_rec[k_][2 + i_] = tl_[i_];       \
         }                                                                         \
     } while (0)
 #else
@@ -132,19 +132,19 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
 }
 __device__ __forceinline__ void mma_s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1, uint32_t c) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
                  : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
     uint32_t y;
-    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
     return y;
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
@@ -384,10 +384,15 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
         const __half *dkl_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_lo * 16);
         const __half *dkh_h = reinterpret_cast<const __half *>(tile + TILE_KD + tk_hi * 16);
         const uint32_t kbase = smem_u32(tile) + k_tok * HD;
+        // the A fragments are loaded one block ahead of their MMAs
+        uint32_t af[2][4];
+        ldsm_x4(kbase + ((k_hi ^ k_key) << 4), af[0][0], af[0][1], af[0][2], af[0][3]);
 #pragma unroll
         for (int b = 0; b < NBLK; b++) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(kbase + (((2 * b + k_hi) ^ k_key) << 4), a0, a1, a2, a3);
+            if (b + 1 < NBLK)
+                ldsm_x4(kbase + (((2 * (b + 1) + k_hi) ^ k_key) << 4), af[(b + 1) & 1][0], af[(b + 1) & 1][1],
+                        af[(b + 1) & 1][2], af[(b + 1) & 1][3]);
+            const uint32_t a0 = af[b & 1][0], a1 = af[b & 1][1], a2 = af[b & 1][2], a3 = af[b & 1][3];
             const float dlo = __half2float(dkl_h[b]), dhi = __half2float(dkh_h[b]);
 #pragma unroll
             for (int j = 0; j < NT; j++) {
@@ -503,15 +508,21 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
     // ---------------- PV for this warp's 64 dims ------------------------------------------
     if (live) {
         const uint32_t vbase = smem_u32(tile) + TILE_VQ;
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++) {
-            uint32_t va[8];
+        // V^T fragments one 16-token step ahead of their MMAs
+        uint32_t vf[2][8];
+        auto load_v = [&](int kk, uint32_t (&va)[8]) {
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 const int dim = v_dim0 + 32 * half;
                 ldsm_x4(vbase + dim * TILE_TOK + ((kk ^ ((dim >> 1) & 3)) << 4), va[4 * half], va[4 * half + 1],
                         va[4 * half + 2], va[4 * half + 3]);
             }
+        };
+        load_v(0, vf[0]);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            if (kk + 1 < 4) load_v(kk + 1, vf[(kk + 1) & 1]);
+            const uint32_t (&va)[8] = vf[kk & 1];
 #pragma unroll
             for (int bb = 0; bb < 2; bb++) {   // the warp's two q8_0 blocks (32 dims each)
                 const int blkv = 2 * w + bb;
@@ -606,6 +617,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     if (has_unit) {
         const bool withhold = u == P.withhold_unit;
         const int pos0 = P.seq_pos0[U.s];
+#ifdef QKV_TIMELINE
+        if (tid == 0) tl_[9] = global_ns() + (pos0 == -12345 ? 1 : 0);   // pos0 resolved
+#endif
         const float c2 = P.scale * 1.4426950408889634f;   // softmax in base 2
         // ---- query rows: 32 threads per row, 8 elements each (4 threads per 32-element block) ---
         const float *qsrc = P.Q + (int64_t)U.io * P.T * P.n_head * HD + U.h * P.G * HD;
@@ -646,28 +660,51 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st, withhold && st == 0);
         }
         TL(6);
-        // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row
+#ifdef QKV_TIMELINE
+        if (tid == 0) tl_[18] = global_ns() + (qv[0][0] == -12345.0f ? 1 : 0);   // thread 0's query values in
+        {
+            float z = 0.0f;
 #pragma unroll
-        for (int it = 0; it < QP; it++) {
-            const int n = it * 4 + w, b = lane >> 2, sub = lane & 3;
-            float amax = 0.0f;
+            for (int it = 0; it < QP; it++) z += qv[it][0] + qv[it][7];
+            if (tid == 0) tl_[19] = global_ns() + (z == -12345.0f ? 1 : 0);        // all of them
+        }
+#endif
+        // q8_0 quantisation exactly as ggml's CPU flash_attn_ext converts its query row.  Each step
+        // runs over all of the warp's rows before the next (block maxima, then d = amax / 127 and
+        // 1 / d, then the rounding), so the rows' dependent chains overlap instead of queueing.
+        {
+            const int b = lane >> 2, sub = lane & 3;
+            float d[QP], id[QP];
 #pragma unroll
-            for (int q = 0; q < 8; q++) amax = fmaxf(amax, fabsf(qv[it][q]));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            const float d  = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-            uint32_t w0 = 0, w1 = 0;
+            for (int it = 0; it < QP; it++) {
+                float amax = 0.0f;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][q], id)) << (8 * q);
-                w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][4 + q], id)) << (8 * q);
+                for (int q = 0; q < 8; q++) amax = fmaxf(amax, fabsf(qv[it][q]));
+                d[it] = amax;
             }
-            if (n < NQ) {
-                uint8_t *row = sm.qq + n * QSTR + b * 32;
-                *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
-                *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
-                if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d));
+#pragma unroll
+            for (int it = 0; it < QP; it++) d[it] = fmaxf(d[it], __shfl_xor_sync(0xffffffffu, d[it], 1));
+#pragma unroll
+            for (int it = 0; it < QP; it++) d[it] = fmaxf(d[it], __shfl_xor_sync(0xffffffffu, d[it], 2));
+#pragma unroll
+            for (int it = 0; it < QP; it++) d[it] = __fdiv_rn(d[it], 127.0f);
+#pragma unroll
+            for (int it = 0; it < QP; it++) id[it] = d[it] != 0.0f ? __frcp_rn(d[it]) : 0.0f;
+#pragma unroll
+            for (int it = 0; it < QP; it++) {
+                const int n = it * 4 + w;
+                uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][q], id[it])) << (8 * q);
+                    w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][4 + q], id[it])) << (8 * q);
+                }
+                if (n < NQ) {
+                    uint8_t *row = sm.qq + n * QSTR + b * 32;
+                    *reinterpret_cast<uint32_t *>(row + qperm(sub * 8)) = w0;
+                    *reinterpret_cast<uint32_t *>(row + qperm(sub * 8 + 4)) = w1;
+                    if (sub == 0) sm.qd[b * NQ + n] = __half2float(__float2half_rn(d[it]));
+                }
             }
         }
         TL(7);
@@ -1235,7 +1272,7 @@ extern "C" int qkv_tl_read(unsigned long long *host, int max_records) {
     unsigned int n = 0;
     if (cudaMemcpyFromSymbol(&n, qkv::dec::g_tl_n, sizeof n) != cudaSuccess) return -1;
     const int m = (int)(n < (unsigned)max_records ? n : (unsigned)max_records);
-    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::dec::g_tl_rec, (size_t)m * 20 * 8) != cudaSuccess) return -1;
+    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::dec::g_tl_rec, (size_t)m * 22 * 8) != cudaSuccess) return -1;
     const unsigned int zero = 0;
     cudaMemcpyToSymbol(qkv::dec::g_tl_n, &zero, sizeof zero);
     return m;

@@ -180,6 +180,35 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 // warp order, scale = 1/sqrt(sum/256 + eps), y * scale * w), rope on pairs (i, i + half) of the
 // first rope_dim dims with cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32
 // multiplication); the query to Q_out, K and V quantised into the page.
+// Phase timestamps of k_project_dot, compiled only with -DQKV_TIMELINE (analysis builds; the
+// product build never defines it): thread 0 of every CTA notes %globaltimer at its phases.
+#ifdef QKV_TIMELINE
+__device__ unsigned long long g_ktl_rec[1 << 14][8];
+__device__ unsigned int g_ktl_n;
+#define KTL_DECL unsigned long long ktl_[6] = {};
+#define KTL(i, dep)                                                                              \
+    do {                                                                                         \
+        if (threadIdx.x == 0) {                                                                  \
+            unsigned long long t_;                                                               \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                               \
+            ktl_[i] = t_ + ((dep) ? 1 : 0);                                                      \
+        }                                                                                        \
+    } while (0)
+#define KTL_FLUSH()                                                                              \
+    do {                                                                                         \
+        if (threadIdx.x == 0) {                                                                  \
+            const unsigned k_ = atomicAdd(&g_ktl_n, 1u) & 0x3fffu;                               \
+            g_ktl_rec[k_][0] = 5;                                                                \
+            g_ktl_rec[k_][1] = blockIdx.x;                                                       \
+            for (int i_ = 0; i_ < 6; i_++) g_ktl_rec[k_][2 + i_] = ktl_[i_];                     \
+        }                                                                                        \
+    } while (0)
+#else
+#define KTL_DECL
+#define KTL(i, dep) do { } while (0)
+#define KTL_FLUSH() do { } while (0)
+#endif
+
 constexpr int PJ_RW = 4;       // rows per warp: each x value read from shared memory serves four rows
 constexpr int PJ_DOT_THREADS = 256, PJ_ROWS_CTA = PJ_DOT_THREADS / 32 * PJ_RW;
 constexpr int PJ_BATCH = 2;    // chunks per row in flight per lane (x PJ_RW rows; after the rows' L2 prefetch)
@@ -255,13 +284,17 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
     else if (g0 < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g0 - nq * HD) * p.n_embd;
     else W = p.Wv + (int64_t)(g0 - (nq + p.n_head_kv) * HD) * p.n_embd;
     const uint4 *w4 = reinterpret_cast<const uint4 *>(W);   // row r at w4 + r * nc
-    // the warp's rows are requested at once (into L2, no registers held), then read in batches
-    for (int r = 0; r < PJ_RW; r++)
-        for (int c = lane; c < nc; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4 + (int64_t)r * nc + c));
+    KTL_DECL
+    KTL(0, false);
+    // the warp's rows are requested at once (into L2 by the bulk-copy engine, one request per
+    // row, no registers held), then read in batches
+    if (lane < PJ_RW)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w4 + (int64_t)lane * nc), "r"(nc * 16) : "memory");
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
     for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
         xs4[(i & 1) * T * nc + i / 2] = x4[i];
     __syncthreads();
+    KTL(1, false);
     float acc[PJ_RW][PJ_MAX_T] = {};
     for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
         uint4 wb[PJ_BATCH][PJ_RW];
@@ -296,6 +329,7 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
             }
         }
     }
+    KTL(2, acc[0][0] == 12345.0f);
 #pragma unroll
     for (int r = 0; r < PJ_RW; r++)
 #pragma unroll
@@ -317,10 +351,16 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
         s_last = atomicAdd(p.cnt + u, 1) == HD / PJ_ROWS_CTA - 1;
     }
     __syncthreads();
-    if (!s_last) return;
+    KTL(3, false);
+    if (!s_last) {
+        KTL_FLUSH();
+        return;
+    }
     __threadfence();
     project_epilogue(p, u, yb, wsum);
     if (tid == 0) p.cnt[u] = 0;
+    KTL(4, false);
+    KTL_FLUSH();
 }
 
 cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
@@ -629,3 +669,16 @@ cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
 }
 
 }  // namespace qkv
+
+#ifdef QKV_TIMELINE
+// Analysis builds only: copy out (and reset) the projection kernel's phase records.
+extern "C" int qkv_tl_read_k(unsigned long long *host, int max_records) {
+    unsigned int n = 0;
+    if (cudaMemcpyFromSymbol(&n, qkv::g_ktl_n, sizeof n) != cudaSuccess) return -1;
+    const int m = (int)(n < (unsigned)max_records ? n : (unsigned)max_records);
+    if (m > 0 && cudaMemcpyFromSymbol(host, qkv::g_ktl_rec, (size_t)m * 8 * 8) != cudaSuccess) return -1;
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(qkv::g_ktl_n, &zero, sizeof zero) != cudaSuccess) return -1;
+    return m;
+}
+#endif

@@ -395,12 +395,18 @@ qkv_status qkv_static_status(void *stream, int32_t *code);
 qkv_status qkv_device_status(qkv_engine *eng, void *stream, int32_t *code);
 
 /* Failure-detection tests.  No counterpart in the reference.  Sets the limit of the decode kernels'
- * bounded waits (tile copies, the latency-mode merge barrier; default 2 s) and, when
+ * bounded waits (the tile copies; default 2 s) and, when
  * withhold_unit >= 0, makes the NEXT decode launch of this engine skip the copy of that unit's first
  * tile while still waiting for its bytes: the wait runs out after wait_limit_ns, the kernel sets
  * the timed-out bit (4) of the device status and returns, and the context stays usable.  Nothing
  * faults and nothing hangs.  wait_limit_ns <= 0 restores the default. */
 qkv_status qkv_debug_decode_wait(qkv_engine *eng, int64_t wait_limit_ns, int32_t withhold_unit);
+
+/* Numerics test.  No counterpart in the reference.  For every non-negative float x (bit patterns
+ * 0 .. 0x7F800000) compares the library's q8_0 block-scale arithmetic -- d = x / 127 and 1 / x as
+ * the quantisers of kernels A, C and D compute them -- with the device's IEEE division and
+ * reciprocal, and writes the number of differing results.  Synchronous on the current device. */
+qkv_status qkv_debug_check_q8_scale(uint64_t *mismatch_div, uint64_t *mismatch_rcp);
 
 /* Kernels this process has launched through the library so far (all engines, all devices). */
 qkv_status qkv_launch_count(uint64_t *count);

@@ -31,6 +31,7 @@ EXPORTS = [
     "qkv_store_prefix_split", "qkv_store_evict", "qkv_store_info", "qkv_store_entry",
     "qkv_indexer_enable", "qkv_idx_append", "qkv_idx_select", "qkv_attn_decode_qsa", "qkv_idx_read",
     "qkv_project_append", "qkv_static_status", "qkv_debug_decode_wait", "qkv_attn_prefill_qsa",
+    "qkv_debug_check_q8_scale",
 ]
 
 
@@ -118,6 +119,7 @@ def lib() -> ctypes.CDLL:
         "qkv_static_status": [P, pI32],
         "qkv_debug_decode_wait": [P, I64, I32],
         "qkv_attn_prefill_qsa": [P, I32, I32, I32, P, P, I32, F32, P, P, P, P],
+        "qkv_debug_check_q8_scale": [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)],
     }
     for name, args in sig.items():
         fn = getattr(L, name)

@@ -308,14 +308,14 @@ __device__ __forceinline__ void fused_append(const DecodeParams &P, const Unit &
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < QK; i++) amax = fmaxf(amax, fabsf(x[i]));
-    const float d  = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    const float d  = div127_rn(amax);
+    const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
     uint32_t q[QK / 4];
 #pragma unroll
     for (int i = 0; i < QK / 4; i++) {
         q[i] = 0;
 #pragma unroll
-        for (int e = 0; e < 4; e++) q[i] |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(x[4 * i + e], id)) << (8 * e);
+        for (int e = 0; e < 4; e++) q[i] |= (uint32_t)(uint8_t)(int8_t)round_half_away(__fmul_rn(x[4 * i + e], id)) << (8 * e);
     }
     const int t = row - cell0;
     if (!kv) {   // two swizzled 16-byte chunks of the token's K row
@@ -687,17 +687,17 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
 #pragma unroll
             for (int it = 0; it < QP; it++) d[it] = fmaxf(d[it], __shfl_xor_sync(0xffffffffu, d[it], 2));
 #pragma unroll
-            for (int it = 0; it < QP; it++) d[it] = __fdiv_rn(d[it], 127.0f);
+            for (int it = 0; it < QP; it++) d[it] = div127_rn(d[it]);
 #pragma unroll
-            for (int it = 0; it < QP; it++) id[it] = d[it] != 0.0f ? __frcp_rn(d[it]) : 0.0f;
+            for (int it = 0; it < QP; it++) id[it] = d[it] != 0.0f ? rcp_rn(d[it]) : 0.0f;
 #pragma unroll
             for (int it = 0; it < QP; it++) {
                 const int n = it * 4 + w;
                 uint32_t w0 = 0, w1 = 0;
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    w0 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][q], id[it])) << (8 * q);
-                    w1 |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(qv[it][4 + q], id[it])) << (8 * q);
+                    w0 |= (uint32_t)(uint8_t)(int8_t)round_half_away(__fmul_rn(qv[it][q], id[it])) << (8 * q);
+                    w1 |= (uint32_t)(uint8_t)(int8_t)round_half_away(__fmul_rn(qv[it][4 + q], id[it])) << (8 * q);
                 }
                 if (n < NQ) {
                     uint8_t *row = sm.qq + n * QSTR + b * 32;

@@ -41,6 +41,48 @@ constexpr int TILE_VD        = 33792;
 constexpr int TILE_BYTES     = 34816;
 
 __host__ __device__ __forceinline__ int kswz(int t) { return (((t >> 2) & 3) << 1) | (t & 1); }
+
+#ifdef __CUDACC__
+// roundf(v) -- round half away from zero, as ggml's quantize_row_q8_0 rounds -- for |v| <= 128,
+// in FP32 adds instead of the conversion pipe (which bounds kernels that round many values):
+// with both additions rounded toward zero, rz(rz(|v| + 0.5) + 2^23) = 2^23 + floor(|v| + 0.5)
+// exactly, so the integer is the low mantissa bits.  Checked against roundf for every float in
+// [-128, 128] (an exhaustive host run of the same two round-toward-zero additions).
+__device__ __forceinline__ int round_half_away(float v) {
+    const float r = __fadd_rz(__fadd_rz(fabsf(v), 0.5f), 8388608.0f);
+    const int mag = __float_as_int(r) - 0x4B000000;
+    return v < 0.0f ? -mag : mag;
+}
+// The same rounding as a float (roundf's value, sign of zero included).
+__device__ __forceinline__ float round_half_away_f(float v) {
+    const float r = __fadd_rz(__fadd_rz(fabsf(v), 0.5f), 8388608.0f);
+    return copysignf(__fadd_rn(r, -8388608.0f), v);
+}
+// The q8_0 block scale of ggml's quantize_row_q8_0: d = amax / 127 and id = 1 / d (0 when d is 0),
+// both correctly rounded, on the FMA pipe instead of the library's division and reciprocal
+// sequences (which bound kernels that quantise many blocks):
+//  * quotient by the constant 127: q = RN(x c) with c = RN(1/127), the residual x - 127 q exactly
+//    by one FMA, then RN(q + residual c) (Markstein's correction step for a constant divisor);
+//  * reciprocal: the hardware estimate r0 (rcp.approx), e = 1 - d r0 exactly by one FMA, then
+//    RN(r0 + r0 e) (one Newton-Raphson step).
+// Inputs outside [2^-100, 2^100] (never met by real activations) take __fdiv_rn / __frcp_rn.  The
+// fast paths equal __fdiv_rn(x, 127) and __frcp_rn(x) for every float in that range
+// (qkv_debug_check_q8_scale runs the exhaustive comparison on the device).
+__device__ __forceinline__ float div127_rn(float x) {
+    if (!(x >= 0x1p-100f && x <= 0x1p100f)) return __fdiv_rn(x, 127.0f);
+    constexpr float c = 1.0f / 127.0f;
+    const float q = __fmul_rn(x, c);
+    const float r = __fmaf_rn(-q, 127.0f, x);
+    return __fmaf_rn(r, c, q);
+}
+__device__ __forceinline__ float rcp_rn(float d) {
+    if (!(d >= 0x1p-100f && d <= 0x1p100f)) return __frcp_rn(d);
+    float r0;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d));
+    const float e = __fmaf_rn(-d, r0, 1.0f);
+    return __fmaf_rn(r0, e, r0);
+}
+#endif
 // byte offset of K quant (token t, element j) inside a tile
 __host__ __device__ __forceinline__ int k_off(int t, int j) {
     return TILE_KQ + t * HD + ((((j >> 4) ^ kswz(t))) << 4) + (j & 15);

@@ -28,9 +28,9 @@ __device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t &q, _
     float amax = fabsf(x);
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d  = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-    q  = (int8_t)(int)roundf(__fmul_rn(x, id));
+    const float d  = div127_rn(amax);
+    const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
+    q  = (int8_t)round_half_away(__fmul_rn(x, id));
     dh = __float2half_rn(d);
     (void)lane;
 }
@@ -107,11 +107,11 @@ __global__ void __launch_bounds__(256) k_append(PoolRef pr, int32_t pos, const f
             for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(in.x[it][kv][e]));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            const float d  = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+            const float d  = div127_rn(amax);
+            const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
             uint8_t q[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) q[e] = (uint8_t)(int8_t)(int)roundf(__fmul_rn(in.x[it][kv][e], id));
+            for (int e = 0; e < 8; e++) q[e] = (uint8_t)(int8_t)round_half_away(__fmul_rn(in.x[it][kv][e], id));
             const int dim0 = b * QK + sub * 8;
             *reinterpret_cast<uint2 *>(kv ? &vs[t][dim0] : &ks[t][dim0]) =
                 make_uint2(q[0] | q[1] << 8 | q[2] << 16 | (uint32_t)q[3] << 24,
@@ -219,57 +219,78 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
     return v;
 }
 
-// Epilogue of head u by one CTA of HD threads, once all of the head's rows are in p.y.
-__device__ void project_epilogue(const ProjectParams &p, int u, float *yb, float *wsum) {
+// Epilogue of head u by one CTA of HD threads, once all of the head's rows are in p.y.  The T
+// tokens go through each step together (their loads in flight at once, one pair of barriers for
+// all of them); every token's arithmetic is the same sequence as for a token alone.
+__device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD], float (*wsum)[HD / 32]) {
     const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
     const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD;
     int kind, h;   // 0 query, 1 key, 2 value
     if (u < nq) { kind = 0; h = u; }
     else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
     else { kind = 2; h = u - nq - p.n_head_kv; }
-    for (int t = 0; t < T; t++) {
-        float o = __ldcg(p.y + (int64_t)t * n_rows + u * HD + r);   // written by other CTAs: from L2
-        if (kind != 2) {                                 // rms-norm, weight, rope
-            const float s2 = warp_sum_bfly(__fmul_rn(o, o));
-            if (lane == 0) wsum[wid] = s2;
-            __syncthreads();
-            float s = wsum[0];
-            for (int k = 1; k < HD / 32; k++) s = __fadd_rn(s, wsum[k]);
+    float o[PJ_MAX_T];
+    uint8_t *tile[PJ_MAX_T];
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++) {
+        if (t >= T) break;
+        o[t] = __ldcg(p.y + (int64_t)t * n_rows + u * HD + r);   // written by other CTAs: from L2
+        tile[t] = kind == 0 ? nullptr : tile_ptr(p.pr, p.pos + t, h);
+    }
+    if (kind != 2) {                                             // rms-norm, weight, rope
+#pragma unroll
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            const float s2 = warp_sum_bfly(__fmul_rn(o[t], o[t]));
+            if (lane == 0) wsum[t][wid] = s2;
+        }
+        __syncthreads();
+        const float *nw = kind == 0 ? p.q_norm : p.k_norm;
+        const float w = nw[r];
+#pragma unroll
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            float s = wsum[t][0];
+            for (int k = 1; k < HD / 32; k++) s = __fadd_rn(s, wsum[t][k]);
             const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, 1.0f / HD), p.eps)));
-            const float *nw = kind == 0 ? p.q_norm : p.k_norm;
-            yb[r] = __fmul_rn(__fmul_rn(o, scale), nw[r]);
-            __syncthreads();
-            const int hh = p.rope_half;
-            o = yb[r];
+            yb[t][r] = __fmul_rn(__fmul_rn(o[t], scale), w);
+        }
+        __syncthreads();
+        const int hh = p.rope_half;
+#pragma unroll
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            o[t] = yb[t][r];
             if (r < hh) {
                 const float2 c = p.cs[t][r];
-                o = __fsub_rn(__fmul_rn(yb[r], c.x), __fmul_rn(yb[r + hh], c.y));
+                o[t] = __fsub_rn(__fmul_rn(yb[t][r], c.x), __fmul_rn(yb[t][r + hh], c.y));
             } else if (r < 2 * hh) {
                 const float2 c = p.cs[t][r - hh];
-                o = __fadd_rn(__fmul_rn(yb[r - hh], c.y), __fmul_rn(yb[r], c.x));
+                o[t] = __fadd_rn(__fmul_rn(yb[t][r - hh], c.y), __fmul_rn(yb[t][r], c.x));
             }
-            __syncthreads();                             // yb and wsum reused by the next token
         }
+    }
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++) {
+        if (t >= T) break;
         if (kind == 0) {
-            p.Q_out[((int64_t)t * p.n_head + h) * HD + r] = o;
+            p.Q_out[((int64_t)t * p.n_head + h) * HD + r] = o[t];
             continue;
         }
-        const int32_t pp = p.pos + t;
-        uint8_t *tile = tile_ptr(p.pr, pp, h);
-        if (!tile) {
+        if (!tile[t]) {
             if (r == 0) atomicOr(p.pr.status, ST_BAD_PAGE);
             continue;
         }
         int8_t qv;
         __half dh;
-        quant_block_warp(o, lane, qv, dh);               // warp w holds q8_0 block w of the row
-        const int tt = pp & 63;
+        quant_block_warp(o[t], lane, qv, dh);               // warp w holds q8_0 block w of the row
+        const int tt = (p.pos + t) & 63;
         if (kind == 1) {
-            tile[k_off(tt, r)] = (uint8_t)qv;
-            if (lane == 0) *reinterpret_cast<__half *>(tile + kd_off(tt, wid)) = dh;
+            tile[t][k_off(tt, r)] = (uint8_t)qv;
+            if (lane == 0) *reinterpret_cast<__half *>(tile[t] + kd_off(tt, wid)) = dh;
         } else {
-            tile[v_off(r, tt)] = (uint8_t)qv;
-            if (lane == 0) *reinterpret_cast<__half *>(tile + vd_off(wid, tt)) = dh;
+            tile[t][v_off(r, tt)] = (uint8_t)qv;
+            if (lane == 0) *reinterpret_cast<__half *>(tile[t] + vd_off(wid, tt)) = dh;
         }
     }
 }
@@ -291,8 +312,23 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
     if (lane < PJ_RW)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w4 + (int64_t)lane * nc), "r"(nc * 16) : "memory");
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
-    for (int i = tid; i < T * p.n_embd / 4; i += blockDim.x)   // conflict-free reads: lane stride 16 B
-        xs4[(i & 1) * T * nc + i / 2] = x4[i];
+    {   // a thread's loads all in flight before its stores (conflict-free reads: lane stride 16 B)
+        constexpr int XU = 8;
+        const int nx = T * p.n_embd / 4;
+        for (int i0 = tid; i0 < nx; i0 += XU * PJ_DOT_THREADS) {
+            float4 v[XU];
+#pragma unroll
+            for (int k = 0; k < XU; k++) {
+                const int i = i0 + k * PJ_DOT_THREADS;
+                if (i < nx) v[k] = x4[i];
+            }
+#pragma unroll
+            for (int k = 0; k < XU; k++) {
+                const int i = i0 + k * PJ_DOT_THREADS;
+                if (i < nx) xs4[(i & 1) * T * nc + i / 2] = v[k];
+            }
+        }
+    }
     __syncthreads();
     KTL(1, false);
     float acc[PJ_RW][PJ_MAX_T] = {};
@@ -341,8 +377,8 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
     // the CTA that completes a head's rows (HD / PJ_ROWS_CTA CTAs per head) runs its epilogue and
     // resets the head's counter for the next call; nothing waits.  One release per CTA: the
     // barrier orders every warp's rows before thread 0's fence and arrival.
-    __shared__ float yb[HD];
-    __shared__ float wsum[HD / 32];
+    __shared__ float yb[PJ_MAX_T][HD];
+    __shared__ float wsum[PJ_MAX_T][HD / 32];
     __shared__ int s_last;
     const int u = blockIdx.x * PJ_ROWS_CTA / HD;
     __syncthreads();
@@ -668,7 +704,42 @@ cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------- numerics check
+// Every non-negative float against the device's IEEE division and reciprocal (test entry).
+__global__ void __launch_bounds__(256) k_check_q8_scale(unsigned long long *bad) {
+    unsigned long long nd = 0, nr = 0;
+    for (uint64_t u = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u <= 0x7F800000ull;
+         u += (uint64_t)gridDim.x * blockDim.x) {
+        const float x = __uint_as_float((uint32_t)u);
+        nd += __float_as_uint(div127_rn(x)) != __float_as_uint(__fdiv_rn(x, 127.0f));
+        nr += __float_as_uint(rcp_rn(x)) != __float_as_uint(__frcp_rn(x));
+    }
+    if (nd) atomicAdd(&bad[0], nd);
+    if (nr) atomicAdd(&bad[1], nr);
+}
+
 }  // namespace qkv
+
+extern "C" qkv_status qkv_debug_check_q8_scale(uint64_t *mismatch_div, uint64_t *mismatch_rcp) {
+    if (!mismatch_div || !mismatch_rcp) return QKV_ERR_INVALID;
+    unsigned long long *bad = nullptr, host[2] = {0, 0};
+    int sms = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaMalloc(&bad, sizeof host) != cudaSuccess)
+        return QKV_ERR_CUDA;
+    cudaError_t e = cudaMemset(bad, 0, sizeof host);
+    if (e == cudaSuccess) {
+        qkv::k_check_q8_scale<<<sms * 8, 256>>>(bad);
+        qkv::count_launches(1);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(host, bad, sizeof host, cudaMemcpyDeviceToHost);
+    cudaFree(bad);
+    if (e != cudaSuccess) return QKV_ERR_CUDA;
+    *mismatch_div = host[0];
+    *mismatch_rcp = host[1];
+    return QKV_OK;
+}
 
 #ifdef QKV_TIMELINE
 // Analysis builds only: copy out (and reset) the projection kernel's phase records.

@@ -377,14 +377,14 @@ __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
         for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        const float d  = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float d  = div127_rn(amax);
+        const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
         const __half dh = __float2half_rn(d);
         uint32_t h[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const __half a = __hmul(__float2half_rn(roundf(__fmul_rn(x[2 * i], id))), dh);
-            const __half b = __hmul(__float2half_rn(roundf(__fmul_rn(x[2 * i + 1], id))), dh);
+            const __half a = __hmul(__float2half_rn(round_half_away_f(__fmul_rn(x[2 * i], id))), dh);
+            const __half b = __hmul(__float2half_rn(round_half_away_f(__fmul_rn(x[2 * i + 1], id))), dh);
             h[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
         }
         o = make_uint4(h[0], h[1], h[2], h[3]);

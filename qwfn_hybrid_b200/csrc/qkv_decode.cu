@@ -121,6 +121,19 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
                  : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// One arrival on bar once all of this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 __device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -285,6 +298,58 @@ __device__ __forceinline__ void issue_ref(const DecodeParams &P, SM &sm, const T
 template <typename SM>
 __device__ __forceinline__ void issue_tile(const DecodeParams &P, SM &sm, const Unit &U, int i) {
     issue_ref(P, sm, tile_ref(P, U, U.t0 + i), i, false);
+}
+
+// QSA mode: tile k of a sequence is its kept blocks 16k .. 16k+15 (4 cells each).  Thread tid
+// serves block g = tid >> 3 of the tile: it resolves the block's source (its 4 cells in the slot's
+// page tile), then copies an eighth of them -- 8 of the 64 16-byte K chunks (re-swizzled for the
+// destination rows), one token's K scales (threads 0-3), 32 of the 256 4-byte V words (the 4 cells
+// of one dim are one word of the transposed V) and one block's 4 V scales -- and arrives on the
+// stage barrier (128 arrivals per phase) when they have landed.  Slots past the kept list copy the
+// last kept block: their cells lie past the sequence's length and are masked.
+struct GrpSrc {
+    const uint8_t *src;   // the block's page tile (nullptr: bad index or page, reported)
+    int ts;               // the block's first cell inside it
+};
+__device__ __forceinline__ GrpSrc grp_resolve(const DecodeParams &P, const Unit &U, int k, int tid) {
+    GrpSrc r{nullptr, 0};
+    const int ng = P.grp_n[U.io];
+    if (ng < 1) return r;
+    const int j = min(16 * k + (tid >> 3), ng - 1);
+    const int32_t b = P.grp[(int64_t)U.io * P.grp_stride + j], c0 = b * 4;
+    if (b < 0 || c0 > P.seq_vpos[U.s] || (c0 >> 8) >= P.max_pages) {
+        if ((tid & 7) == 0) atomicOr(P.status, ST_BAD_INDEX);
+        return r;
+    }
+    const int32_t page = P.block_table[(int64_t)P.seq_slot[U.s] * P.max_pages + (c0 >> 8)];
+    if (page < 0 || page >= P.n_pages) {
+        if ((tid & 7) == 0) atomicOr(P.status, ST_BAD_PAGE);
+        return r;
+    }
+    r.src = P.pool + (int64_t)page * P.page_bytes + (int64_t)(U.h * TILES_PER_PAGE + ((c0 >> 6) & 3)) * TILE_BYTES;
+    r.ts = c0 & 63;
+    return r;
+}
+template <typename SM>
+__device__ __forceinline__ void grp_issue(SM &sm, const GrpSrc &r, int i, int tid) {
+    uint8_t *dst = sm.tile[i % SM::NS];
+    if (r.src) {
+        const int td = 4 * (tid >> 3), q0 = tid & 7;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const int e = q0 + 8 * q, m = e >> 4, c = e & 15;
+            cp_async16(dst + TILE_KQ + (td + m) * HD + ((c ^ kswz(td + m)) << 4),
+                       r.src + TILE_KQ + (r.ts + m) * HD + ((c ^ kswz(r.ts + m)) << 4));
+        }
+        if (q0 < 4) cp_async16(dst + kd_off(td + q0, 0), r.src + kd_off(r.ts + q0, 0));
+#pragma unroll 8
+        for (int q = 0; q < HD / 8; q++) {
+            const int dim = q0 + 8 * q;
+            cp_async4(dst + v_off(dim, td), r.src + v_off(dim, r.ts));
+        }
+        cp_async8(dst + vd_off(q0, td), r.src + vd_off(q0, r.ts));
+    }
+    cp_async_arrive(&sm.full[i % SM::NS]);
 }
 
 // Quantise the new rows of this tile (positions pos0..pos0+T-1 inside it) for KV head h and store
@@ -591,9 +656,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             prefetch_l2(qsrc + ((int64_t)t * P.n_head + jj) * HD + (e % (HD * 4 / 128)) * 32);
         }
 #ifdef QKV_TIMELINE
-        if (!P.sel && tid < min(n_tiles, PF_TILES) && !P.tl_nopf) {
+        if (!P.sel && !P.grp && tid < min(n_tiles, PF_TILES) && !P.tl_nopf) {
 #else
-        if (!P.sel && tid < min(n_tiles, PF_TILES)) {
+        if (!P.sel && !P.grp && tid < min(n_tiles, PF_TILES)) {
 #endif
             const TileRef r = tile_ref(P, U, U.t0 + tid);
             if (r.blk >= 0) bulk_prefetch_l2(r.src, TILE_BYTES);
@@ -601,8 +666,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         // thread 0: the barriers, and the first tiles' pages (dense), resolved before the wait
         if (tid == 0) {
             for (int st = 0; st < NS; st++) {
-                mbar_init(&sm.full[st], 1);
-                first[st] = !P.sel && st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+                mbar_init(&sm.full[st], P.grp ? 128 : 1);   // QSA mode: every thread's copies arrive
+                first[st] = !P.sel && !P.grp && st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             }
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
@@ -617,6 +682,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     if (has_unit) {
         const bool withhold = u == P.withhold_unit;
         const int pos0 = P.seq_pos0[U.s];
+        GrpSrc gfirst[NS];   // QSA mode: this thread's kept block of the first tiles (the list is the
+        if (P.grp)           // previous kernel's output), copied once the barriers are seen initialised
+            for (int st = 0; st < NS; st++) gfirst[st] = st < n_tiles ? grp_resolve(P, U, U.t0 + st, tid) : GrpSrc{nullptr, 0};
 #ifdef QKV_TIMELINE
         if (tid == 0) tl_[9] = global_ns() + (pos0 == -12345 ? 1 : 0);   // pos0 resolved
 #endif
@@ -653,7 +721,7 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         }
         // thread 0 starts the first tiles' copies once its query loads are in flight (sparse
         // units resolve their block ids only now: the previous kernel wrote them)
-        if (tid == 0) {
+        if (tid == 0 && !P.grp) {
             if (P.sel)
                 for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             for (int st = 0; st < NS && st < n_tiles; st++)
@@ -722,6 +790,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         if (appends && tid == 0)   // the first tiles held back for the append
             for (int st = 0; st < NS && st < n_tiles; st++)
                 if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref(P, sm, first[st], st, withhold && st == 0);
+        if (P.grp)
+            for (int st = 0; st < NS && st < n_tiles; st++) grp_issue(sm, gfirst[st], st, tid);
 
         for (int i = 0; i < n_tiles; i++) {
             const int stage = i % NS;
@@ -729,14 +799,18 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                                           aborted ? after_abort(P.wait_ns) : P.wait_ns);
             aborted = aborted || !__all_sync(0xffffffffu, landed);
             if (i == 0) TL(8);
-            const int blk = sm.stage_blk[stage];
+            const int blk = P.grp ? U.t0 + i : sm.stage_blk[stage];
             tile_step<NT>(sm.tile[stage], blk, blk >= 0 && !aborted, sm.qq, sm.qd, sm.ln, rs, c2, w, lane, CtaSync{} TLT_PASS(i == 0 ? 10 : i == 1 ? 14 : -1));
             __syncthreads();   // barrier 2: the stage and P are free
             // After a wait that gave up no new copy starts: every copy this CTA issued has then
             // been waited for (bounded) by the time it exits.
-            if (tid == 0 && i + NS < n_tiles && !aborted) issue_tile(P, sm, U, i + NS);
+            if (i + NS < n_tiles && !aborted) {
+                if (P.grp) grp_issue(sm, grp_resolve(P, U, U.t0 + i + NS, tid), i + NS, tid);
+                else if (tid == 0) issue_tile(P, sm, U, i + NS);
+            }
             if (i == 0) TL(3);
         }
+        if (P.grp) asm volatile("cp.async.wait_all;" ::: "memory");   // nothing of this thread still in flight
         TL(4);
         // ---------------- unit epilogue: O, m, l into shared memory ------------------------------
 #pragma unroll

@@ -101,14 +101,10 @@ struct qkv_engine {
     std::vector<uint8_t *> idx_pools;         // per layer, n_pages x IDX_PAGE_BYTES
     float2   *d_rope  = nullptr;              // [idx_max_blk][rope_dim/2] {cos, sin}
     float    *d_knorm = nullptr;              // [n_layer][IDX_KEY]
-    // qkv_attn_decode_qsa scratch (grown on demand): scores, kept blocks, dense copies of the
-    // kept cells (dst_pages pages per (sequence, token) entry) and their block table
+    // qkv_attn_decode_qsa scratch (grown on demand): scores, kept blocks and their counts
     float    *d_iscore = nullptr;
     int32_t  *d_isel = nullptr, *d_inout = nullptr;
     int32_t   iscratch_v = 0;
-    uint8_t  *d_vpool = nullptr;
-    int32_t  *d_vbt = nullptr;
-    int32_t   vpool_v = 0, dst_pages = 0;
     float    *d_pj = nullptr;                 // qkv_project_append: raw projections [T][rows]
     // qkv_attn_prefill_qsa scratch (grown on demand): kept blocks and counts per row, bitsets
     int32_t  *d_psel = nullptr, *d_pnout = nullptr;
@@ -326,8 +322,6 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_iscore);
     cudaFree(eng->d_isel);
     cudaFree(eng->d_inout);
-    cudaFree(eng->d_vpool);
-    cudaFree(eng->d_vbt);
     cudaFree(eng->d_pj);
     cudaFree(eng->d_psel);
     cudaFree(eng->d_pnout);
@@ -642,21 +636,24 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
 // equal work.
 // Where kernel C reads from: by default the layer's pool through the engine's block table; the
 // indexer path points it at dense scratch copies of the kept cells instead.
-struct DecodeSrc {
-    uint8_t       *pool;
-    const int32_t *bt;
-    int32_t        max_pages, n_pages;
+// QSA mode of a decode launch: sequence i attends to its kept 4-cell blocks blocks[i][0 .. n_out[i])
+// (device arrays, ascending) of its slot; pos0[i] + 1 is the number of kept cells and vpos[i] the
+// query's position.
+struct DecodeGroups {
+    const int32_t *blocks, *n_out;
+    int32_t        stride;
+    const int32_t *vpos;   // host [ns]
 };
 
 static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *slots, const int32_t *pos0, int ns,
                                 const float *Q, int32_t T, float scale, const int32_t *sel, int32_t n_sel,
                                 const float *Knew, const float *Vnew, float *out, cudaStream_t st,
-                                const DecodeSrc *src = nullptr) {
+                                const DecodeGroups *grp = nullptr) {
     const int H = eng->cfg.n_head_kv, G = eng->cfg.n_head / H;
     DecodeParams P;
     memset(&P, 0, sizeof P);
-    P.pool = src ? src->pool : eng->pools[layer];
-    P.block_table = src ? src->bt : eng->d_bt;
+    P.pool = eng->pools[layer];
+    P.block_table = eng->d_bt;
     P.Q = Q;
     P.out = out;
     P.partial = eng->d_partial;
@@ -665,8 +662,8 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.Vnew = Vnew;
     P.status = eng->d_status;
     P.page_bytes = eng->page_bytes;
-    P.n_pages = src ? src->n_pages : eng->n_pages;
-    P.max_pages = src ? src->max_pages : eng->max_pages;
+    P.n_pages = eng->n_pages;
+    P.max_pages = eng->max_pages;
     P.n_head = eng->cfg.n_head;
     P.n_head_kv = H;
     P.G = G;
@@ -678,12 +675,19 @@ static qkv_status decode_launch(qkv_engine *eng, int32_t layer, const int32_t *s
     P.wait_ns = eng->wait_ns;
     P.withhold_unit = eng->withhold_unit;
     eng->withhold_unit = -1;   // one launch only
+    if (grp) {
+        P.grp = grp->blocks;
+        P.grp_n = grp->n_out;
+        P.grp_stride = grp->stride;
+    }
     std::vector<int32_t> tiles(ns);
     for (int i = 0; i < ns; i++) tiles[i] = sel ? n_sel : (pos0[i] + T + TILE_TOK - 1) / TILE_TOK;
     const int max_ctas = decode_max_ctas(T * G);
     const int64_t target = max_ctas > 0 ? max_ctas : (int64_t)eng->num_sms * 2;
     plan_decode(P, slots, pos0, tiles.data(), ns, target, decode_merge_max_units(),
                 (int64_t)(eng->partial_bytes / (partial_stride(P.nq) * sizeof(float))));
+    if (grp)
+        for (int j = 0; j < ns; j++) P.seq_vpos[j] = grp->vpos[P.seq_idx[j]];
     if ((size_t)P.n_units * partial_stride(P.nq) * sizeof(float) > eng->partial_bytes)
         return fail(eng, QKV_ERR_NO_MEMORY, "decode: split-K scratch too small for %d units", P.n_units);
     CK(eng, launch_decode(P, st));
@@ -777,7 +781,6 @@ extern "C" qkv_status qkv_indexer_enable(qkv_engine *eng, const qkv_indexer_conf
     eng->icfg = c;
     eng->k_blocks = (c.top_k + c.ratio - 1 + c.ratio - 1) / c.ratio;   // ceil(width / ratio), engine.cpp:687
     eng->idx_max_blk = (eng->cfg.n_ctx + IDX_R - 1) / IDX_R;
-    eng->dst_pages = (eng->k_blocks * IDX_R + PAGE_TOK - 1) / PAGE_TOK;
     if (eng->host_only) {
         eng->idx_on = true;
         return QKV_OK;
@@ -946,18 +949,9 @@ extern "C" qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const 
     if ((r = use_device(eng)) != QKV_OK) return r;
     cudaStream_t st = S(stream);
     if ((r = flush_tables(eng, st)) != QKV_OK) return r;
-    // entries go through in chunks of MAX_SEQ (one decode launch each), reusing the scratch
+    // entries go through in chunks of MAX_SEQ (one selection and one decode launch each), reusing
+    // the scratch; the decode reads each entry's kept blocks in place (QSA mode)
     if ((r = idx_scratch(eng, MAX_SEQ)) != QKV_OK) return r;
-    if (eng->vpool_v < MAX_SEQ) {
-        const int32_t pages = MAX_SEQ * eng->dst_pages;
-        if ((r = dalloc(eng, eng->d_vpool, (size_t)pages * eng->page_bytes, "indexer gather pages")) != QKV_OK) return r;
-        if ((r = dalloc(eng, eng->d_vbt, (size_t)pages * sizeof(int32_t), "indexer gather table")) != QKV_OK) return r;
-        std::vector<int32_t> ids(pages);
-        for (int32_t i = 0; i < pages; i++) ids[i] = i;
-        CK(eng, cudaMemset(eng->d_vpool, 0, (size_t)pages * eng->page_bytes));
-        CK(eng, cudaMemcpy(eng->d_vbt, ids.data(), ids.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
-        eng->vpool_v = MAX_SEQ;
-    }
     const int32_t n_v = n_seq * T, K = eng->k_blocks;
     const size_t qrow = (size_t)eng->cfg.n_head * HD;
     const int32_t step = MAX_SEQ / T * T;   // whole sequences per launch
@@ -966,39 +960,21 @@ extern "C" qkv_status qkv_attn_decode_qsa(qkv_engine *eng, int32_t layer, const 
         if ((r = idx_select_chunk(eng, layer, slots, pos0, T, v0, nv, q_idx, eng->d_isel, eng->d_inout, eng->d_iscore,
                                   eng->idx_max_blk, st)) != QKV_OK)
             return r;
-        IdxGatherParams g;
-        memset(&g, 0, sizeof g);
-        g.pool = eng->pools[layer];
-        g.bt = eng->d_bt;
-        g.dst = eng->d_vpool;
-        g.dst_bt = eng->d_vbt;
-        g.blocks = eng->d_isel;
-        g.n_out = eng->d_inout;
-        g.status = eng->d_status;
-        g.page_bytes = eng->page_bytes;
-        g.n_v = nv;
-        g.k_blocks = K;
-        g.n_head_kv = eng->cfg.n_head_kv;
-        g.n_pages = eng->n_pages;
-        g.max_pages = eng->max_pages;
-        g.dst_pages = eng->dst_pages;
-        int32_t vslot[MAX_SEQ], vpos[MAX_SEQ];
+        int32_t vslot[MAX_SEQ], vlast[MAX_SEQ], vpos[MAX_SEQ];
         for (int k = 0; k < nv; k++) {
             const int v = v0 + k;
             const int32_t p = pos0[v / T] + v % T, b_last = p / IDX_R, whole = (p + 1) / IDX_R;
             const int32_t tail = b_last >= whole ? 1 : 0;
-            g.v_slot[k] = slots[v / T];
-            g.v_pos[k] = p;
-            // the dense copy: every block (cells 0 .. p), or k_blocks blocks with the tail's
-            // cells up to p last
+            // kept cells: every block (cells 0 .. p), or k_blocks blocks with the tail's cells up
+            // to p last
             const int32_t len = b_last + 1 <= K ? p + 1 : IDX_R * (K - tail) + (tail ? p - IDX_R * b_last + 1 : 0);
-            vslot[k] = k;
-            vpos[k] = len - 1;
+            vslot[k] = slots[v / T];
+            vlast[k] = len - 1;
+            vpos[k] = p;
         }
-        CK(eng, launch_idx_gather(g, st));
-        const DecodeSrc src{eng->d_vpool, eng->d_vbt, eng->dst_pages, MAX_SEQ * eng->dst_pages};
-        if ((r = decode_launch(eng, layer, vslot, vpos, nv, Q + (size_t)v0 * qrow, 1, scale, nullptr, 0, nullptr, nullptr,
-                               out + (size_t)v0 * qrow, st, &src)) != QKV_OK)
+        const DecodeGroups grp{eng->d_isel, eng->d_inout, K, vpos};
+        if ((r = decode_launch(eng, layer, vslot, vlast, nv, Q + (size_t)v0 * qrow, 1, scale, nullptr, 0, nullptr, nullptr,
+                               out + (size_t)v0 * qrow, st, &grp)) != QKV_OK)
             return r;
     }
     return QKV_OK;

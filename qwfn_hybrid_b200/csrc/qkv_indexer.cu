@@ -1,7 +1,7 @@
-// qkv_indexer.cu -- the QSA lightning indexer, decode path: raw indexer keys and pooled block
-// keys (k_idx_append), block scores (k_idx_score), exact top-k per token (k_idx_topk), and the
-// gather of each token's kept cells into scratch pages that the decode kernel reads as a dense
-// sequence (k_idx_gather).
+// qkv_indexer.cu -- the QSA lightning indexer: raw indexer keys and pooled block keys
+// (k_idx_append), block scores (k_idx_score), exact top-k per token (k_idx_topk) and the kept-block
+// bitsets of the sparse prefill (k_idx_bits).  The decode kernel reads each token's kept blocks in
+// place (its QSA mode), so no copy of them is made.
 //
 // Every floating-point step is written with explicit round-to-nearest operations in a fixed
 // order (lane l of a warp owns dims 4l .. 4l+3; cross-lane sums are xor butterflies 16, 8, 4, 2,
@@ -449,73 +449,6 @@ cudaError_t launch_idx_bits(const int32_t *blocks, const int32_t *n_out, int32_t
                             int32_t words, cudaStream_t st) {
     if (n_v < 1 || words < 1 || (size_t)words * 4 > 48 * 1024) return cudaErrorInvalidValue;
     k_idx_bits<<<n_v, 256, (size_t)words * 4, st>>>(blocks, n_out, k_blocks, bits, words);
-    count_launches(1);
-    return cudaGetLastError();
-}
-
-// --------------------------------------------------------------------------------------- gather
-// CTA (i, v), warp h: kept block i of entry v, KV head h.  Its 4 cells c0 .. c0+3 (c0 = 4 b) go to
-// cells 4i .. 4i+3 of the entry's scratch sequence; cells past v_pos are written as zeros.  Per
-// 4-cell group and head: 4 K rows (64 chunks of 16 B, re-swizzled), one 4-byte word per dim of
-// the transposed V, 64 B of K scales and 8 x 8 B of V scales.
-__global__ void __launch_bounds__(256) k_idx_gather(const IdxGatherParams p) {
-    const int v = blockIdx.y, i = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (h >= p.n_head_kv || i >= p.n_out[v]) return;
-    const int32_t b = p.blocks[(int64_t)v * p.k_blocks + i], pos = p.v_pos[v], c0 = b * IDX_R;
-    if (b < 0 || c0 > pos) {
-        if (lane == 0) atomicOr(p.status, ST_BAD_INDEX);
-        return;
-    }
-    const int32_t *bt = p.bt + (int64_t)p.v_slot[v] * p.max_pages;
-    const int32_t sp = (c0 >> 8) < p.max_pages ? bt[c0 >> 8] : -1;
-    const int32_t j0 = i * IDX_R;
-    const int32_t dp = (j0 >> 8) < p.dst_pages ? p.dst_bt[(int64_t)v * p.dst_pages + (j0 >> 8)] : -1;
-    if (sp < 0 || sp >= p.n_pages || dp < 0) {
-        if (lane == 0) atomicOr(p.status, ST_BAD_PAGE);
-        return;
-    }
-    const uint8_t *src = p.pool + (int64_t)sp * p.page_bytes + (int64_t)(h * TILES_PER_PAGE + ((c0 >> 6) & 3)) * TILE_BYTES;
-    uint8_t *dst = p.dst + (int64_t)dp * p.page_bytes + (int64_t)(h * TILES_PER_PAGE + ((j0 >> 6) & 3)) * TILE_BYTES;
-    const int ts = c0 & 63, td = j0 & 63;
-    const int nv = min(IDX_R, pos - c0 + 1);   // valid cells of the group
-    // every load first (the group's bytes are scattered: many requests in flight), then the stores
-    uint4 kq[2];
-#pragma unroll
-    for (int k = 0; k < 2; k++) {              // K quants: 4 rows x 16 chunks of 16 B
-        const int q = lane + 32 * k, m = q >> 4, c = q & 15;
-        kq[k] = *reinterpret_cast<const uint4 *>(src + TILE_KQ + (ts + m) * HD + ((c ^ kswz(ts + m)) << 4));
-    }
-    uint32_t vq[HD / 32];
-#pragma unroll
-    for (int k = 0; k < HD / 32; k++)          // V quants: 4 tokens of one dim are one word
-        vq[k] = *reinterpret_cast<const uint32_t *>(src + v_off(lane + 32 * k, ts));
-    uint2 sc = make_uint2(0, 0);
-    if (lane < 16)                             // K scales: [tok][8] fp16, 16 B per token
-        sc.x = *reinterpret_cast<const uint32_t *>(src + kd_off(ts, 0) + 4 * lane);
-    else if (lane < 16 + NBLK)                 // V scales: [8][tok] fp16, 4 tokens = 8 B per block
-        sc = *reinterpret_cast<const uint2 *>(src + vd_off(lane - 16, ts));
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-        const int q = lane + 32 * k, m = q >> 4, c = q & 15;
-        *reinterpret_cast<uint4 *>(dst + TILE_KQ + (td + m) * HD + ((c ^ kswz(td + m)) << 4)) =
-            m < nv ? kq[k] : make_uint4(0, 0, 0, 0);
-    }
-    const uint32_t vmask = nv >= 4 ? 0xffffffffu : ((1u << (8 * nv)) - 1u);
-#pragma unroll
-    for (int k = 0; k < HD / 32; k++) *reinterpret_cast<uint32_t *>(dst + v_off(lane + 32 * k, td)) = vq[k] & vmask;
-    if (lane < 16) {
-        *reinterpret_cast<uint32_t *>(dst + kd_off(td, 0) + 4 * lane) = (lane >> 2) < nv ? sc.x : 0u;
-    } else if (lane < 16 + NBLK) {
-        if (nv < 4) {
-            sc.x &= nv >= 2 ? 0xffffffffu : (nv >= 1 ? 0x0000ffffu : 0u);
-            sc.y &= nv >= 3 ? 0x0000ffffu : 0u;
-        }
-        *reinterpret_cast<uint2 *>(dst + vd_off(lane - 16, td)) = sc;
-    }
-}
-
-cudaError_t launch_idx_gather(const IdxGatherParams &p, cudaStream_t st) {
-    k_idx_gather<<<dim3(p.k_blocks, p.n_v), 32 * p.n_head_kv, 0, st>>>(p);
     count_launches(1);
     return cudaGetLastError();
 }

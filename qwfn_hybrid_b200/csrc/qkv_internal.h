@@ -198,21 +198,6 @@ struct IdxSelectParams {
 };
 cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaStream_t st);
 
-// Copies the kept cells of entry v (blocks[v][0 .. n_out[v]), cells <= v_pos[v]) from the KV pool
-// into the entry's scratch pages (dst_bt row v), in block order, as a dense sequence for kernel C.
-struct IdxGatherParams {
-    const uint8_t *pool;          // layer KV pool
-    const int32_t *bt;            // engine block table
-    uint8_t       *dst;           // scratch pool
-    const int32_t *dst_bt;        // [n_v][dst_pages]
-    const int32_t *blocks;
-    const int32_t *n_out;
-    int32_t       *status;
-    int64_t page_bytes;
-    int32_t n_v, k_blocks, n_head_kv, n_pages, max_pages, dst_pages;
-    int32_t v_slot[IDX_MAX_VSEQ], v_pos[IDX_MAX_VSEQ];
-};
-cudaError_t launch_idx_gather(const IdxGatherParams &p, cudaStream_t st);
 // Kept-block bitsets for the sparse prefill: bits[v][words] from blocks[v][k_blocks] / n_out[v].
 cudaError_t launch_idx_bits(const int32_t *blocks, const int32_t *n_out, int32_t k_blocks, int32_t n_v, uint32_t *bits,
                             int32_t words, cudaStream_t st);
@@ -234,6 +219,11 @@ struct DecodeParams {
     float   scale;
     uint64_t wait_ns;             // limit of every bounded wait (tile copies, the pair barrier)
     int32_t withhold_unit;        // failure tests: this unit's first tile copy is never started (-1: none)
+    // QSA mode (grp non-null): sequence i's dense sequence is its kept 4-cell blocks
+    // grp[i][0 .. grp_n[i]) (ascending) of the slot's pages; a tile is 16 of them
+    const int32_t *grp;
+    const int32_t *grp_n;
+    int32_t grp_stride;
 #ifdef QKV_TIMELINE
     int32_t tl_nopf;              // analysis builds only: no tile prefetch before the dependency wait
 #endif
@@ -244,6 +234,7 @@ struct DecodeParams {
     int32_t seq_tiles[MAX_SEQ];      // tiles of each pair of the sequence
     int32_t seq_units[MAX_SEQ];      // units (CTAs) per pair of the sequence
     int32_t seq_unit0[MAX_SEQ + 1];  // prefix of n_head_kv * seq_units
+    int32_t seq_vpos[MAX_SEQ];       // QSA mode: the query's position (every kept cell is <= it)
 };
 // partial record size in floats for nq query rows: O [nq][HD] unnormalised, m [nq] (log2
 // domain), l [nq]

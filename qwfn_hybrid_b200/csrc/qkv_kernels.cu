@@ -307,26 +307,28 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
     const uint4 *w4 = reinterpret_cast<const uint4 *>(W);   // row r at w4 + r * nc
     KTL_DECL
     KTL(0, false);
-    // the warp's rows are requested at once (into L2 by the bulk-copy engine, one request per
-    // row, no registers held), then read in batches
-    if (lane < PJ_RW)
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w4 + (int64_t)lane * nc), "r"(nc * 16) : "memory");
+    // x first (a thread's loads all in flight before its stores; conflict-free reads: lane stride
+    // 16 B), then the warp's weight rows are requested at once behind them (into L2 by the
+    // bulk-copy engine, one request per row, no registers held) and read in batches below
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
-    {   // a thread's loads all in flight before its stores (conflict-free reads: lane stride 16 B)
+    {
         constexpr int XU = 8;
         const int nx = T * p.n_embd / 4;
-        for (int i0 = tid; i0 < nx; i0 += XU * PJ_DOT_THREADS) {
+        for (int i0 = tid, first = 1;; i0 += XU * PJ_DOT_THREADS, first = 0) {
             float4 v[XU];
 #pragma unroll
             for (int k = 0; k < XU; k++) {
                 const int i = i0 + k * PJ_DOT_THREADS;
                 if (i < nx) v[k] = x4[i];
             }
+            if (first && lane < PJ_RW)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w4 + (int64_t)lane * nc), "r"(nc * 16) : "memory");
 #pragma unroll
             for (int k = 0; k < XU; k++) {
                 const int i = i0 + k * PJ_DOT_THREADS;
                 if (i < nx) xs4[(i & 1) * T * nc + i / 2] = v[k];
             }
+            if (i0 + XU * PJ_DOT_THREADS >= nx) break;
         }
     }
     __syncthreads();

@@ -9,21 +9,25 @@
 // exact), products accumulate in fp32.
 //
 // Tile: 128 rows = (128 / G) query tokens x the G q-heads sharing one KV head, so each K/V tile
-// is dequantised once for all of them.  A CTA (24 warps, one per SM) runs a contiguous run of
-// segments (tile, KV range) from a host plan that gives every CTA the same number of KV tiles;
-// each segment leaves a partial record, merged per tile by k_prefill_merge.
-//   warp 0      TMEM allocation; one thread issues all MMAs and the query-tile bulk copies
-//   warps 4-7   softmax: thread r owns row r (TMEM lane r): S row from TMEM, causal mask,
-//               online softmax with a lazily raised reference max (O in TMEM rescaled only when
-//               the row max grows by more than 2^8), P as fp16 into shared memory
-//   warps 8-15  K producers, warps 16-23 V producers: read q8_0 tiles from the pages (issued
-//               before the stage is free), dequantise to fp16 into the 128-byte-swizzled K-major
-//               layouts the MMAs read.  A K stage frees when its S MMA completes, a V stage when
-//               its PV MMA completes, so K of tile j+2 is written while PV of tile j runs.
-// Per KV tile j (stage s = j % 2):  S[s] = Q K_j^T  (M128 N64 K256: 16 MMAs),  then after the
-// softmax wrote P_j:  O += P_j V_j  (M128 N256 K64: 4 MMAs).  S_{j+1} is issued before PV_j so
-// the tensor core works while the softmax runs.  Every wait is bounded (ST_TIMEOUT, then all
-// roles leave their loops, the issuing thread drains its MMAs and the CTA frees its TMEM).
+// is dequantised once for all of them.  Two tiles of a KV head run on a CTA pair (a cluster of
+// two, one CTA per SM) whose MMAs are tcgen05.mma.cta_group::2 with M = 256: each CTA holds its
+// query tile and dequantises half of every K tile (64 keys) and V tile (128 dims) into its own
+// shared memory.  A pair runs a contiguous run of segments (pair tile, KV range) from a host plan
+// that gives every pair the same number of KV tiles; each segment leaves a partial record per
+// tile, merged by k_prefill_merge.  17 warps per CTA:
+//   warp 0      TMEM allocation; in the leader one thread issues all MMAs, in the follower one
+//               thread copies its query tiles and reports them to the leader
+//   warps 1-8   softmax in two halves of the S row's 128 keys: thread r owns row r (TMEM lane
+//               r): its half's S from TMEM, causal (and kept-block) mask, online softmax with a
+//               lazily raised reference max (O rescaled only when the row max grows by more
+//               than 2^8), P as fp16 over the half's S columns
+//   warps 9-16  K producers (9-12) and V producers (13-16): read q8_0 tiles from the pages and
+//               dequantise to fp16 into the 128-byte-swizzled layouts the MMAs read, in a ring
+//               of five 32 KiB slots freed by the commits of the MMAs that read them.
+// Per KV tile j (S buffer b = j % 2): S_b = Q K_j^T (N = 128), then after the softmax wrote P_j:
+// O += P_j V_j.  S_{j+1} is issued before PV_j so the tensor core works while the softmax runs.
+// Every wait is bounded (ST_TIMEOUT, then all roles leave their loops, the issuing thread drains
+// its MMAs and the CTAs free their TMEM).
 #include "qkv.h"
 #include "qkv_internal.h"
 
@@ -49,7 +53,8 @@ constexpr int SM_RING    = 65536;      // NSLOT x 32 KiB slots: this CTA's half 
 constexpr int NSLOT      = 5;
 constexpr int SLOT_BYTES = 32768;
 constexpr int SM_BAR     = SM_RING + NSLOT * SLOT_BYTES;
-constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;
+constexpr int SM_PMAX    = SM_BAR + 256;   // [2 S buffers][2 softmax halves][128 rows] bf16: the halves' row maxima
+constexpr int SMEM_BYTES = SM_PMAX + 2 * 2 * 128 * 2 + 1024;
 // tensor memory columns: O, then two S buffers (P of a tile is stored over its S)
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_COLS = 512;
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;
@@ -62,7 +67,7 @@ struct Bars {
     uint64_t slot_full[NSLOT];   // leader: producers of both CTAs (2 x 128 NGRP arrivals): the pair's slot u filled
     uint64_t slot_free[NSLOT];   // both: commit after the MMAs reading slot u
     uint64_t s_full[2];          // both: commit after S_j
-    uint64_t s_read[2];          // both, local: the CTA's softmax groups (256 arrivals) read S_j
+    uint64_t s_read[2];          // both, local: the CTA's softmax threads (256 arrivals) posted their halves' maxima of S_j
     uint64_t p_full[2];          // leader: softmax of both CTAs (2 x 256 arrivals): P_j stored (and O rescaled)
     uint64_t pv_done[2];         // both: commit after PV_j
     uint64_t q_full;             // both, local: the CTA's query tile landed (expect_tx)
@@ -268,34 +273,38 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 __device__ __forceinline__ bool key_vis(int i, int nvis, uint32_t word) {
     return i < nvis && ((word >> (i >> 2)) & 1u);
 }
-// Max of the thread's S row (KT columns from TMEM address scol); invisible columns count as -inf
-// unless FULL.  Read 64 columns per round trip (two loads, one wait), each 32 reduced as a tree.
+// A row max as bf16 rounded toward +inf (never below the max; +-inf and 0 exact), and back: the
+// two softmax halves exchange their maxima this way and both use the larger rounded value, so they
+// hold the same reference (the softmax does not depend on which reference, beyond P's rounding).
+__device__ __forceinline__ uint16_t max_up_bf16(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return (uint16_t)((x > 0.0f ? u + 0xFFFFu : u) >> 16);
+}
+__device__ __forceinline__ float bf16_bits(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+// Max of this half's 64 keys (64 half .. 64 half + 63) of the thread's S row (two loads, one wait;
+// tree of 3-input max); invisible keys count as -inf unless FULL.
 template <bool FULL>
-__device__ __forceinline__ float row_max(uint32_t scol, int nvis, uint32_t word) {
+__device__ __forceinline__ float half_max(uint32_t scol, int half, int nvis, uint32_t word) {
+    uint32_t v[2][32];
+    tmem_ld32(scol + 64 * half, v[0]);
+    tmem_ld32(scol + 64 * half + 32, v[1]);
+    tmem_wait_ld();
     float m = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < KT / 32; c += 2) {
-        uint32_t v[2][32];
-        tmem_ld32(scol + 32 * c, v[0]);
-        tmem_ld32(scol + 32 * c + 32, v[1]);
-        tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            float x[32];
+    for (int h = 0; h < 2; h++) {
+        float x[32];
 #pragma unroll
-            for (int e = 0; e < 32; e++) x[e] = (FULL || key_vis(32 * (c + h) + e, nvis, word)) ? __uint_as_float(v[h][e]) : -INFINITY;
+        for (int e = 0; e < 32; e++) x[e] = (FULL || key_vis(64 * half + 32 * h + e, nvis, word)) ? __uint_as_float(v[h][e]) : -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
-            m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
-        }
+        for (int e = 0; e < 8; e++) x[e] = fmaxf(max3(x[e], x[e + 8], x[e + 16]), x[e + 24]);
+        m = max3(m, fmaxf(max3(x[0], x[1], x[2]), x[3]), fmaxf(max3(x[4], x[5], x[6]), x[7]));
     }
     return m;
 }
-// P = 2^(s * sl2 - mu) of keys 64 half .. 64 half + 63 of the thread's row (one round trip),
-// stored as fp16 pairs in columns 64 half .. 64 half + 31, inside the S columns this half just
-// read.  Returns the sum of the P values.
+// P = 2^(s * sl2 - mu) of this half's keys (read again: one round trip), stored as fp16 pairs in
+// S columns 64 half .. 64 half + 31, inside the columns this half read.  Returns the sum of P.
 template <bool FULL>
-__device__ __forceinline__ float row_p(uint32_t scol, int half, int nvis, uint32_t word, float sl2, float mu) {
+__device__ __forceinline__ float half_p(uint32_t scol, int half, int nvis, uint32_t word, float sl2, float mu) {
     const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-mu, -mu);
     float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
     uint32_t v[2][32];
@@ -575,7 +584,8 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
     };
     auto store = [&](const Load &ld, uint32_t u) -> bool {
         const uint32_t sl = u % NSLOT;
-        if (u >= NSLOT && !wait_bar(&B->slot_free[sl], ((u / NSLOT) - 1) & 1, B, P.status)) return false;
+        if (u >= NSLOT && !__all_sync(0xffffffffu, wait_bar(&B->slot_free[sl], ((u / NSLOT) - 1) & 1, B, P.status)))
+            return false;   // warp-uniform: every lane leaves together
         const uint32_t slot = sbase + SM_RING + sl * SLOT_BYTES;
         if constexpr (KGRP) k_store(slot, t, ld);
         else v_store(slot, t, ld);
@@ -743,12 +753,14 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
         // Warps 1-4 (half 0) and 5-8 (half 1): warp w reads TMEM lanes 32 (w & 3) .. +31, so
         // thread r owns row r of this CTA's tile in both halves.  Control flow is warp-uniform
         // (tcgen05.ld/st are warp-collective): every wait's result is agreed with __all_sync.  Per
-        // 128-key tile both halves read the whole S row for its max (so both raise the lazily
-        // raised reference the same way), meet at s_read, then half h turns keys 64h .. 64h+63
-        // into P (fp16 pairs) and stores them over S columns 64h .. 64h+31, which only it read
-        // since the meeting.  If the row max grows by more than 2^8 over the reference, the
+        // 128-key tile half h reads only its keys 64h .. 64h+63, posts their max (bf16, rounded
+        // up) in shared memory and meets the other half at s_read; both take the larger posted
+        // value, so both raise the lazily raised reference the same way.  Half h then reads its
+        // keys again, turns them into P (fp16 pairs) and stores them over S columns
+        // 64h .. 64h+31.  If the row max grows by more than 2^8 over the reference, the
         // reference moves up and l and O (half h rescales O columns 128h .. 128h+127) are scaled.
         const int half = (warp - 1) >> 2, r = (warp & 3) * 32 + lane;
+        uint16_t *pmax = reinterpret_cast<uint16_t *>(sm + SM_PMAX);
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, wait_bar(bar, parity, B, P.status));
@@ -774,9 +786,16 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 const uint32_t word = SPARSE ? word_next : ~0u;
                 if (SPARSE && wrow) word_next = sg.kt0 + k + 1 <= kt_vis && k + 1 < sg.nk ? __ldg(wrow + sg.kt0 + k + 1) : ~0u;
                 const bool full = __all_sync(0xffffffffu, nvis == KT && (!SPARSE || word == ~0u));
-                const float smax = full ? row_max<true>(scol, nvis, word) : row_max<false>(scol, nvis, word);
+                const float hmax = full ? half_max<true>(scol, half, nvis, word) : half_max<false>(scol, half, nvis, word);
+                // this half's max (bf16, rounded up) to shared memory; the other half reads it after
+                // the meeting.  Slot b is written again for tile j + 2, whose S needs P_j consumed,
+                // i.e. both halves past this read.
+                pmax[(2 * b + half) * PF_ROWS + r] = max_up_bf16(hmax);
                 tc_fence_before();
                 mbar_arrive(&B->s_read[b]);
+                if (!(ok = wait_all(&B->s_read[b], (j >> 1) & 1))) break;
+                tc_fence_after();
+                const float smax = fmaxf(bf16_bits(pmax[(2 * b) * PF_ROWS + r]), bf16_bits(pmax[(2 * b + 1) * PF_ROWS + r]));
                 // lazily raised reference max: O and l are rescaled only when a row max grows by
                 // more than 2^8 over the reference (P stays <= 256, exact enough in fp16)
                 const float mx = smax * P.scale_log2;   // scale > 0: max of scaled = scaled max
@@ -785,10 +804,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 if (need) m_ref = mx;
                 l *= F;
                 const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: p = 0
-                if (!(ok = wait_all(&B->s_read[b], (j >> 1) & 1))) break;
-                tc_fence_after();
-                l += full ? row_p<true>(scol, half, nvis, word, P.scale_log2, mu)
-                          : row_p<false>(scol, half, nvis, word, P.scale_log2, mu);
+                l += full ? half_p<true>(scol, half, nvis, word, P.scale_log2, mu)
+                          : half_p<false>(scol, half, nvis, word, P.scale_log2, mu);
                 if (k > 0 && __any_sync(0xffffffffu, F != 1.0f)) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;

@@ -682,9 +682,6 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
     if (has_unit) {
         const bool withhold = u == P.withhold_unit;
         const int pos0 = P.seq_pos0[U.s];
-        GrpSrc gfirst[NS];   // QSA mode: this thread's kept block of the first tiles (the list is the
-        if (P.grp)           // previous kernel's output), copied once the barriers are seen initialised
-            for (int st = 0; st < NS; st++) gfirst[st] = st < n_tiles ? grp_resolve(P, U, U.t0 + st, tid) : GrpSrc{nullptr, 0};
 #ifdef QKV_TIMELINE
         if (tid == 0) tl_[9] = global_ns() + (pos0 == -12345 ? 1 : 0);   // pos0 resolved
 #endif
@@ -726,6 +723,10 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                 for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             for (int st = 0; st < NS && st < n_tiles; st++)
                 if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st, withhold && st == 0);
+        }
+        if (P.grp) {   // QSA mode: every thread's share of the first tiles, behind its query loads
+            __syncthreads();   // thread 0 initialised the stage barriers (before the dependency wait)
+            for (int st = 0; st < NS && st < n_tiles; st++) grp_issue(sm, grp_resolve(P, U, U.t0 + st, tid), st, tid);
         }
         TL(6);
 #ifdef QKV_TIMELINE
@@ -790,8 +791,6 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         if (appends && tid == 0)   // the first tiles held back for the append
             for (int st = 0; st < NS && st < n_tiles; st++)
                 if (U.t0 + st >= nb_lo && U.t0 + st <= nb_hi) issue_ref(P, sm, first[st], st, withhold && st == 0);
-        if (P.grp)
-            for (int st = 0; st < NS && st < n_tiles; st++) grp_issue(sm, gfirst[st], st, tid);
 
         for (int i = 0; i < n_tiles; i++) {
             const int stage = i % NS;

@@ -743,16 +743,46 @@ def measure_cfg4(args, local: int) -> dict:
     for _ in range(max(args.warmup, 3)):     # the first select computes the 1150 whole-block summaries
         step()
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(args.steps):
-        step(evs[i])
-    t1.record(stream)
-    torch.cuda.synchronize()
+    # timed as replays of CUDA graphs (the step, and select + attend alone), so no host time sits
+    # between the launches; eager steps with per-step events if capture is refused
+    timing = "replays of CUDA graphs of a step and of its select + attend, median of 5"
+    try:
+        g_step, g_sel = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step):
+            step()
+        with torch.cuda.graph(g_sel):
+            eng.select_blocks(0, [0], [p0], qd, T, SP_TOPK, idx)
+            eng.attn_decode(0, [0], [p0], qd, T, SCALE, out, sel=idx, n_sel=SP_TOPK)
+        g_step.replay()
+        torch.cuda.synchronize()
+
+        def timed(g):
+            per = []
+            for _ in range(REPLAYS):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(args.steps):
+                    g.replay()
+                b.record(stream)
+                torch.cuda.synchronize()
+                per.append(a.elapsed_time(b) / args.steps)
+            return 1e3 * statistics.median(per)
+
+        step_us, sel_us = timed(g_step), timed(g_sel)
+        del g_step, g_sel
+    except RuntimeError:
+        timing = "eager steps, CUDA events around each step's select + attend"
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+        sel_us = 1e3 * statistics.median(a.elapsed_time(b) for a, b in evs)
+        step_us = 1e3 * t0.elapsed_time(t1) / args.steps
     assert eng.device_status() == 0
-    sel_us = 1e3 * statistics.median(a.elapsed_time(b) for a, b in evs)
-    step_us = 1e3 * t0.elapsed_time(t1) / args.steps
     Kr = torch.empty((SP_CTX, ROW_BYTES), dtype=torch.uint8, device=dev)
     Vr = torch.empty_like(Kr)
     eng.read_rows(0, 0, 0, SP_CTX, Kr, Vr)
@@ -777,7 +807,7 @@ def measure_cfg4(args, local: int) -> dict:
     return {"workload": "configs[3]: ctx 73728 (1152 blocks of 64), seed 3 (K offset variance 2 per block and KV "
                         "head), T=3; per step: append 3 rows, score + top-32 per KV head (block 0 and the last two "
                         "forced), sparse attention over the 2048 selected tokens read in place",
-            "us_per_select_attend": sel_us, "us_per_step_with_append": step_us,
+            "us_per_select_attend": sel_us, "us_per_step_with_append": step_us, "timing": timing,
             "tokens_per_s": T * 1e6 / step_us,
             "roofline": {"bound": "hbm (latency-bound)", "achieved": algo / (sel_us * 1e-6) / 1e9, "peak": pk["hbm"],
                          "unit": "GB/s", "frac": algo / (sel_us * 1e-6) / 1e9 / pk["hbm"],
@@ -923,14 +953,31 @@ def measure_cfg3(args, rank: int, ws: int, local: int, e2e: bool = True) -> dict
     torch.cuda.synchronize()
     clocks = Clocks(local)
     clocks.start()
+    # the timed prompts: replays of one CUDA graph of a whole prompt (32 appends + 32 prefill calls),
+    # so no host time sits between the launches (eager prompts if capture is refused)
+    launches0 = Q.launch_count()
+    try:
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(step_graph):
+            step()
+        per_prompt = (Q.launch_count() - launches0)
+        step_graph.replay()
+        torch.cuda.synchronize()
+    except RuntimeError:
+        step_graph, per_prompt = None, 0
+        torch.cuda.synchronize()
     launches0 = Q.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        if step_graph is not None:
+            step_graph.replay()
+        else:
+            step()
     e1.record(stream)
     torch.cuda.synchronize()
-    launches = Q.launch_count() - launches0
+    launches = per_prompt * args.steps if step_graph is not None else Q.launch_count() - launches0
+    del step_graph
     barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
@@ -1018,7 +1065,8 @@ def measure_cfg3(args, rank: int, ws: int, local: int, e2e: bool = True) -> dict
         "config": {"workload": "configs[2]: 16384-token prompt, 32 chunks of 512, 1 layer, 16q/2kv x 256, q8_0 KV, "
                                "each chunk appends 512 rows then attends causally over the whole cache",
                    "parallelism": f"independent prompts x{ws} (replicas, no collective)",
-                   "l2": "inputs larger than L2 (134 MB of bf16 queries + 268 MB of outputs per step)"},
+                   "l2": "inputs larger than L2 (134 MB of bf16 queries + 268 MB of outputs per step)",
+                   "timing": "replays of one CUDA graph of a whole prompt" if per_prompt else "eager prompts"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
                      "peak_source": peak_src, "traffic": None,
                      "kernel": "k_prefill_q + k_prefill + k_prefill_merge per chunk", "attn_timing": attn_timing,

@@ -625,7 +625,7 @@ __device__ __forceinline__ void tile_step(const uint8_t *tile, int blk, bool liv
 // in every warp); a warp whose scores outgrow it by more than 2^4 posts its maximum and the whole
 // CTA moves the reference (rescaling O and the row sums) before PV -- rare after the first tile,
 // so a tile normally costs two barriers: P ready, stage free.
-template <int NT, int NSR>
+template <int NT, int NSR, bool QSA>
 __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodeParams P) {
     constexpr int NQ = NT * 8;
     using SM = Smem<NT, NSR>;
@@ -656,9 +656,9 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
             prefetch_l2(qsrc + ((int64_t)t * P.n_head + jj) * HD + (e % (HD * 4 / 128)) * 32);
         }
 #ifdef QKV_TIMELINE
-        if (!P.sel && !P.grp && tid < min(n_tiles, PF_TILES) && !P.tl_nopf) {
+        if (!P.sel && !QSA && tid < min(n_tiles, PF_TILES) && !P.tl_nopf) {
 #else
-        if (!P.sel && !P.grp && tid < min(n_tiles, PF_TILES)) {
+        if (!P.sel && !QSA && tid < min(n_tiles, PF_TILES)) {
 #endif
             const TileRef r = tile_ref(P, U, U.t0 + tid);
             if (r.blk >= 0) bulk_prefetch_l2(r.src, TILE_BYTES);
@@ -666,8 +666,8 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         // thread 0: the barriers, and the first tiles' pages (dense), resolved before the wait
         if (tid == 0) {
             for (int st = 0; st < NS; st++) {
-                mbar_init(&sm.full[st], P.grp ? 128 : 1);   // QSA mode: every thread's copies arrive
-                first[st] = !P.sel && !P.grp && st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
+                mbar_init(&sm.full[st], QSA ? 128 : 1);   // QSA mode: every thread's copies arrive
+                first[st] = !P.sel && !QSA && st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             }
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
@@ -718,13 +718,13 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
         }
         // thread 0 starts the first tiles' copies once its query loads are in flight (sparse
         // units resolve their block ids only now: the previous kernel wrote them)
-        if (tid == 0 && !P.grp) {
+        if (tid == 0 && !QSA) {
             if (P.sel)
                 for (int st = 0; st < NS; st++) first[st] = st < n_tiles ? tile_ref(P, U, U.t0 + st) : TileRef{-1, nullptr};
             for (int st = 0; st < NS && st < n_tiles; st++)
                 if (!(appends && U.t0 + st >= nb_lo && U.t0 + st <= nb_hi)) issue_ref(P, sm, first[st], st, withhold && st == 0);
         }
-        if (P.grp) {   // QSA mode: every thread's share of the first tiles, behind its query loads
+        if constexpr (QSA) {   // every thread's share of the first tiles, behind its query loads
             __syncthreads();   // thread 0 initialised the stage barriers (before the dependency wait)
             for (int st = 0; st < NS && st < n_tiles; st++) grp_issue(sm, grp_resolve(P, U, U.t0 + st, tid), st, tid);
         }
@@ -798,18 +798,18 @@ __global__ void __launch_bounds__(128, NT <= 3 ? 4 : 2) k_decode(const DecodePar
                                           aborted ? after_abort(P.wait_ns) : P.wait_ns);
             aborted = aborted || !__all_sync(0xffffffffu, landed);
             if (i == 0) TL(8);
-            const int blk = P.grp ? U.t0 + i : sm.stage_blk[stage];
+            const int blk = QSA ? U.t0 + i : sm.stage_blk[stage];
             tile_step<NT>(sm.tile[stage], blk, blk >= 0 && !aborted, sm.qq, sm.qd, sm.ln, rs, c2, w, lane, CtaSync{} TLT_PASS(i == 0 ? 10 : i == 1 ? 14 : -1));
             __syncthreads();   // barrier 2: the stage and P are free
             // After a wait that gave up no new copy starts: every copy this CTA issued has then
             // been waited for (bounded) by the time it exits.
             if (i + NS < n_tiles && !aborted) {
-                if (P.grp) grp_issue(sm, grp_resolve(P, U, U.t0 + i + NS, tid), i + NS, tid);
+                if constexpr (QSA) grp_issue(sm, grp_resolve(P, U, U.t0 + i + NS, tid), i + NS, tid);
                 else if (tid == 0) issue_tile(P, sm, U, i + NS);
             }
             if (i == 0) TL(3);
         }
-        if (P.grp) asm volatile("cp.async.wait_all;" ::: "memory");   // nothing of this thread still in flight
+        if constexpr (QSA) asm volatile("cp.async.wait_all;" ::: "memory");   // nothing of this thread still in flight
         TL(4);
         // ---------------- unit epilogue: O, m, l into shared memory ------------------------------
 #pragma unroll
@@ -1055,29 +1055,29 @@ static cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t sm
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <int NT, int NSR>
+template <int NT, int NSR, bool QSA>
 static cudaError_t configure_nt() {
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64 && configured[dev]) return cudaSuccess;
-    e = cudaFuncSetAttribute(dec::k_decode<NT, NSR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(dec::k_decode<NT, NSR, QSA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)sizeof(dec::Smem<NT, NSR>));
     if (e == cudaSuccess && dev >= 0 && dev < 64) configured[dev] = true;
     return e;
 }
 
 // Co-resident CTAs of the decode kernel (0 = unknown).
-template <int NT, int NSR>
+template <int NT, int NSR, bool QSA = false>
 static int max_ctas_nt() {
     static int cached[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (cached[dev]) return cached[dev];
     int per_sm = 0, sms = 0;
-    if (configure_nt<NT, NSR>() != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec::k_decode<NT, NSR>, 128, sizeof(dec::Smem<NT, NSR>)) !=
+    if (configure_nt<NT, NSR, QSA>() != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec::k_decode<NT, NSR, QSA>, 128, sizeof(dec::Smem<NT, NSR>)) !=
             cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
         cudaGetLastError();
@@ -1087,11 +1087,11 @@ static int max_ctas_nt() {
     return cached[dev];
 }
 
-template <int NT, int NSR>
+template <int NT, int NSR, bool QSA>
 static cudaError_t launch_ns(const DecodeParams &p, cudaStream_t st) {
-    cudaError_t e = configure_nt<NT, NSR>();
+    cudaError_t e = configure_nt<NT, NSR, QSA>();
     if (e != cudaSuccess) return e;
-    if ((e = launch_pdl(dec::k_decode<NT, NSR>, (unsigned)p.n_units, 128, sizeof(dec::Smem<NT, NSR>), st, p)) !=
+    if ((e = launch_pdl(dec::k_decode<NT, NSR, QSA>, (unsigned)p.n_units, 128, sizeof(dec::Smem<NT, NSR>), st, p)) !=
         cudaSuccess)
         return e;
     count_launches(1);
@@ -1120,10 +1120,12 @@ static cudaError_t launch_ns(const DecodeParams &p, cudaStream_t st) {
 }
 
 // Two tile stages when every unit fits co-resident with them, else one (more CTAs per SM).
-template <int NT>
+// The QSA mode (kept 4-cell blocks read in place) is an instantiation of its own, so the dense and
+// selected-block kernels carry none of its code (measured: 2.5% on the ragged batch).
+template <int NT, bool QSA = false>
 static cudaError_t launch_nt(const DecodeParams &p, cudaStream_t st) {
-    if (dec::Stages<NT>::N == 2 || p.n_units <= max_ctas_nt<NT, 2>()) return launch_ns<NT, 2>(p, st);
-    return launch_ns<NT, 1>(p, st);
+    if (dec::Stages<NT>::N == 2 || p.n_units <= max_ctas_nt<NT, 2, QSA>()) return launch_ns<NT, 2, QSA>(p, st);
+    return launch_ns<NT, 1, QSA>(p, st);
 }
 
 int decode_max_nq() { return 64; }
@@ -1205,6 +1207,13 @@ void plan_decode(DecodeParams &P, const int32_t *slots, const int32_t *pos0, con
 }
 
 cudaError_t launch_decode(const DecodeParams &p, cudaStream_t st) {
+    if (p.grp) {   // QSA mode: T = 1, so G query rows (up to 16)
+        switch ((p.nq + 7) / 8) {
+            case 1: return launch_nt<1, true>(p, st);
+            case 2: return launch_nt<2, true>(p, st);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch ((p.nq + 7) / 8) {
         case 1: return launch_nt<1>(p, st);
         case 2: return launch_nt<2>(p, st);

@@ -152,46 +152,77 @@ cudaError_t launch_idx_pool(const IdxAppendParams &p, int32_t b_lo, int32_t n_bl
 // as the sums do.  Whole blocks b < (pos+1)/4 only.  Four lanes per block (lane quarter j owns
 // s_j; all of its 64 key bytes are loaded up front), 64 blocks per CTA; CTA (x, g) serves the T
 // entries g*T .. g*T+T-1 (the tokens of one sequence), which share every pooled-key load.
-constexpr int SC_THREADS = 256, SC_BLOCKS = SC_THREADS / 4;
+constexpr int SC_THREADS = 256, SC_BLOCKS = SC_THREADS / 4, SC_PER = 2;   // blocks per thread
 constexpr int QROW = IDX_KEY + 16;   // each 32-dim quarter 4 words further on: conflict-free quarter reads
 __device__ __forceinline__ int qcol(int d) { return d + 4 * (d >> 5); }
 
+// TT, HH > 0: the token and head counts fixed at compile time (the loops over them have no
+// runtime bounds); 0: taken from the parameters.
+template <int TT, int HH>
 __global__ void __launch_bounds__(SC_THREADS) k_idx_score(const IdxSelectParams p) {
     __shared__ __align__(16) float qs[4][IDX_MAX_HEAD][QROW];
-    const int g = blockIdx.y, T = p.T, H = p.n_head, v0 = g * T;
-    // the key loads first: their latency overlaps the query staging
+    const int T = TT > 0 ? TT : p.T, H = HH > 0 ? HH : p.n_head, g = blockIdx.y, v0 = g * T;
+    // the key loads first: their latency overlaps the query staging.  Thread: quarter j of the
+    // dims of SC_PER blocks (SC_BLOCKS apart), so each query read from shared memory serves SC_PER
+    // keys; every block's sums run in the same order as for a block alone.
     const int j = threadIdx.x & 3;                                 // quarter of the dims
-    const int32_t b = blockIdx.x * SC_BLOCKS + (threadIdx.x >> 2);
     const int32_t whole_max = (p.v_pos[v0 + T - 1] + 1) / IDX_R;   // positions ascend with t
-    const uint8_t *pg = nullptr;
-    if (b < whole_max) {
-        pg = idx_page(p.pool, p.bt + (int64_t)p.v_slot[v0] * p.max_pages, p.max_pages, p.n_pages, b * IDX_R);
-        if (!pg && j == 0) atomicOr(p.status, ST_BAD_PAGE);
-    }
-    uint4 w[4] = {};
-    if (pg) {
-        const uint4 *key = reinterpret_cast<const uint4 *>(pg + IDX_RAW_BYTES + (int64_t)(b & (IDX_BPP - 1)) * IDX_KEY * 2 + 64 * j);
+    int32_t b[SC_PER];
+    const uint8_t *pg[SC_PER];
+    uint4 w[SC_PER][4];
 #pragma unroll
-        for (int c = 0; c < 4; c++) w[c] = key[c];
+    for (int k = 0; k < SC_PER; k++) {
+        b[k] = blockIdx.x * (SC_PER * SC_BLOCKS) + k * SC_BLOCKS + (threadIdx.x >> 2);
+        pg[k] = nullptr;
+        if (b[k] < whole_max) {
+            pg[k] = idx_page(p.pool, p.bt + (int64_t)p.v_slot[v0] * p.max_pages, p.max_pages, p.n_pages, b[k] * IDX_R);
+            if (!pg[k] && j == 0) atomicOr(p.status, ST_BAD_PAGE);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++) w[k][c] = make_uint4(0, 0, 0, 0);
+        if (pg[k]) {
+            const uint4 *key = reinterpret_cast<const uint4 *>(pg[k] + IDX_RAW_BYTES + (int64_t)(b[k] & (IDX_BPP - 1)) * IDX_KEY * 2 + 64 * j);
+#pragma unroll
+            for (int c = 0; c < 4; c++) w[k][c] = key[c];
+        }
     }
-    for (int i = threadIdx.x; i < T * H * IDX_KEY; i += blockDim.x) {
-        const int th = i / IDX_KEY, d = i % IDX_KEY;
-        qs[th / H][th % H][qcol(d)] = __half2float(__float2half_rn(p.q[(int64_t)v0 * H * IDX_KEY + i]));
+    {   // the queries (fp16-rounded): a thread's loads all in flight before its stores
+        constexpr int QU = 4 * IDX_MAX_HEAD * IDX_KEY / SC_THREADS;   // the most any thread stages
+        const int nq = T * H * IDX_KEY;
+        float qv[QU];
+#pragma unroll
+        for (int k = 0; k < QU; k++) {
+            const int i = threadIdx.x + k * SC_THREADS;
+            qv[k] = i < nq ? p.q[(int64_t)v0 * H * IDX_KEY + i] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < QU; k++) {
+            const int i = threadIdx.x + k * SC_THREADS;
+            if (i < nq) {
+                const int th = i / IDX_KEY, d = i % IDX_KEY;
+                qs[th / H][th % H][qcol(d)] = __half2float(__float2half_rn(qv[k]));
+            }
+        }
     }
     __syncthreads();
-    float acc[4][IDX_MAX_HEAD];
+    float acc[SC_PER][4][IDX_MAX_HEAD];
 #pragma unroll
-    for (int t = 0; t < 4; t++)
+    for (int k = 0; k < SC_PER; k++)
 #pragma unroll
-        for (int h = 0; h < IDX_MAX_HEAD; h++) acc[t][h] = 0.0f;
+        for (int t = 0; t < 4; t++)
+#pragma unroll
+            for (int h = 0; h < IDX_MAX_HEAD; h++) acc[k][t][h] = 0.0f;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-        const __half2 *hw = reinterpret_cast<const __half2 *>(&w[c]);
-        float k[8];
+        float kv[SC_PER][8];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            k[2 * e] = __low2float(hw[e]);
-            k[2 * e + 1] = __high2float(hw[e]);
+        for (int k = 0; k < SC_PER; k++) {
+            const __half2 *hw = reinterpret_cast<const __half2 *>(&w[k][c]);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                kv[k][2 * e] = __low2float(hw[e]);
+                kv[k][2 * e + 1] = __high2float(hw[e]);
+            }
         }
         const int d0 = 32 * j + 8 * c;
 #pragma unroll
@@ -202,33 +233,38 @@ __global__ void __launch_bounds__(SC_THREADS) k_idx_score(const IdxSelectParams 
                 if (h >= H) break;
                 const float4 qa = *reinterpret_cast<const float4 *>(&qs[t][h][qcol(d0)]);
                 const float4 qb = *reinterpret_cast<const float4 *>(&qs[t][h][qcol(d0) + 4]);
-                float a = acc[t][h];
-                a = __fmaf_rn(qa.x, k[0], a);
-                a = __fmaf_rn(qa.y, k[1], a);
-                a = __fmaf_rn(qa.z, k[2], a);
-                a = __fmaf_rn(qa.w, k[3], a);
-                a = __fmaf_rn(qb.x, k[4], a);
-                a = __fmaf_rn(qb.y, k[5], a);
-                a = __fmaf_rn(qb.z, k[6], a);
-                a = __fmaf_rn(qb.w, k[7], a);
-                acc[t][h] = a;
+#pragma unroll
+                for (int k = 0; k < SC_PER; k++) {
+                    float a = acc[k][t][h];
+                    a = __fmaf_rn(qa.x, kv[k][0], a);
+                    a = __fmaf_rn(qa.y, kv[k][1], a);
+                    a = __fmaf_rn(qa.z, kv[k][2], a);
+                    a = __fmaf_rn(qa.w, kv[k][3], a);
+                    a = __fmaf_rn(qb.x, kv[k][4], a);
+                    a = __fmaf_rn(qb.y, kv[k][5], a);
+                    a = __fmaf_rn(qb.z, kv[k][6], a);
+                    a = __fmaf_rn(qb.w, kv[k][7], a);
+                    acc[k][t][h] = a;
+                }
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-        if (t >= T) break;
-        double tot = 0.0;
+    for (int k = 0; k < SC_PER; k++)
 #pragma unroll
-        for (int h = 0; h < IDX_MAX_HEAD; h++) {
-            if (h >= H) break;
-            float d = __fadd_rn(acc[t][h], __shfl_xor_sync(0xffffffffu, acc[t][h], 1));   // s0+s1, s2+s3
-            d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));                           // (s0+s1)+(s2+s3)
-            tot = __dadd_rn(tot, (double)(d > 0.0f ? d : 0.0f));
+        for (int t = 0; t < 4; t++) {
+            if (t >= T) break;
+            double tot = 0.0;
+#pragma unroll
+            for (int h = 0; h < IDX_MAX_HEAD; h++) {
+                if (h >= H) break;
+                float d = __fadd_rn(acc[k][t][h], __shfl_xor_sync(0xffffffffu, acc[k][t][h], 1));   // s0+s1, s2+s3
+                d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));                                 // (s0+s1)+(s2+s3)
+                tot = __dadd_rn(tot, (double)(d > 0.0f ? d : 0.0f));
+            }
+            if (pg[k] && j == 0 && b[k] < (p.v_pos[v0 + t] + 1) / IDX_R)
+                p.scores[(int64_t)(v0 + t) * p.score_stride + b[k]] = __double2float_rn(tot);
         }
-        if (pg && j == 0 && b < (p.v_pos[v0 + t] + 1) / IDX_R)
-            p.scores[(int64_t)(v0 + t) * p.score_stride + b] = __double2float_rn(tot);
-    }
 }
 
 // -------------------------------------------------------------------------------------- top-k
@@ -417,7 +453,12 @@ cudaError_t launch_idx_select(const IdxSelectParams &p, int32_t max_whole, cudaS
         attr_set |= 1ull << dev;
     }
     if (max_whole > 0) {
-        k_idx_score<<<dim3((max_whole + SC_BLOCKS - 1) / SC_BLOCKS, p.n_v / p.T), SC_THREADS, 0, st>>>(p);
+        const dim3 grid((max_whole + SC_PER * SC_BLOCKS - 1) / (SC_PER * SC_BLOCKS), p.n_v / p.T);
+        if (p.n_head == 4 && p.T == 1) k_idx_score<1, 4><<<grid, SC_THREADS, 0, st>>>(p);
+        else if (p.n_head == 4 && p.T == 2) k_idx_score<2, 4><<<grid, SC_THREADS, 0, st>>>(p);
+        else if (p.n_head == 4 && p.T == 3) k_idx_score<3, 4><<<grid, SC_THREADS, 0, st>>>(p);
+        else if (p.n_head == 4 && p.T == 4) k_idx_score<4, 4><<<grid, SC_THREADS, 0, st>>>(p);
+        else k_idx_score<0, 0><<<grid, SC_THREADS, 0, st>>>(p);
         count_launches(1);
     }
     const int chunk = (max_whole + TK_CL - 1) / TK_CL;

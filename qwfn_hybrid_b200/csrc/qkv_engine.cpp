@@ -105,7 +105,6 @@ struct qkv_engine {
     float    *d_iscore = nullptr;
     int32_t  *d_isel = nullptr, *d_inout = nullptr;
     int32_t   iscratch_v = 0;
-    float    *d_pj = nullptr;                 // qkv_project_append: raw projections [T][rows]
     // qkv_attn_prefill_qsa scratch (grown on demand): kept blocks and counts per row, bitsets
     int32_t  *d_psel = nullptr, *d_pnout = nullptr;
     int32_t   psel_rows = 0;
@@ -322,7 +321,6 @@ static void free_device(qkv_engine *eng) {
     cudaFree(eng->d_iscore);
     cudaFree(eng->d_isel);
     cudaFree(eng->d_inout);
-    cudaFree(eng->d_pj);
     cudaFree(eng->d_psel);
     cudaFree(eng->d_pnout);
     cudaFree(eng->d_pbits);
@@ -590,17 +588,9 @@ extern "C" qkv_status qkv_project_append(qkv_engine *eng, int32_t layer, int32_t
     cudaStream_t st = S(stream);
     if ((r = reserve(eng, slot, pos, T, st)) != QKV_OK) return r;
     if ((r = flush_tables(eng, st)) != QKV_OK) return r;
-    const size_t y_bytes = (size_t)PJ_MAX_T * (2 * eng->cfg.n_head + 2 * eng->cfg.n_head_kv) * HD * sizeof(float);
-    const size_t cnt_bytes = (size_t)(2 * eng->cfg.n_head + 2 * eng->cfg.n_head_kv) * sizeof(int32_t);
-    if (!eng->d_pj) {
-        if ((r = dalloc(eng, eng->d_pj, y_bytes + cnt_bytes, "projection scratch")) != QKV_OK) return r;
-        CK(eng, cudaMemset(eng->d_pj, 0, y_bytes + cnt_bytes));   // the per-head counters start at zero
-    }
     ProjectParams p;
     memset(&p, 0, sizeof p);
     p.pr = pool_ref(eng, layer, eng->d_bt + (size_t)slot * eng->max_pages);
-    p.y = eng->d_pj;
-    p.cnt = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(eng->d_pj) + y_bytes);
     p.x = x;
     p.Wq = Wq;
     p.Wk = Wk;

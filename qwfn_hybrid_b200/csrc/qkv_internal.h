@@ -118,8 +118,6 @@ constexpr int PJ_MAX_T = 4, PJ_MAX_HALF = 64;
 struct ProjectParams {
     PoolRef        pr;            // the slot's pages in the layer's pool
     const float   *x;             // [T][n_embd]
-    float         *y;             // scratch [T][rows]: the raw projections
-    int32_t       *cnt;           // scratch [heads]: CTAs done per head, zero between calls
     const uint16_t *Wq, *Wk, *Wv; // bf16 weights, rows of n_embd; Wq: query/gate interleaved per head (nullable)
     const float   *q_norm, *k_norm;   // [HD]
     float         *Q_out;         // [T][n_head][HD] (with Wq)

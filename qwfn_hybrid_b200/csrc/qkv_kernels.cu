@@ -175,8 +175,10 @@ cudaError_t launch_append(const PoolRef &pr, int32_t pos, const float *K, const 
 //   lane_l = fmaf(w, x, ...) over its chunks in order, dims in order within a chunk
 // (bf16 weights are exact in fp32); y = xor butterfly 16, 8, 4, 2, 1 of the lane sums.  Rows in
 // the order: query heads (the query rows of attn_q.weight's per-head query/gate interleave), K
-// heads, V heads; y goes to scratch [T][rows].
-// Epilogue, run by the CTA that completes a head's rows (a per-head counter): rms-norm (per warp the xor butterfly of y^2, warp sums added in
+// heads, V heads; a head's 256 rows are the 8 CTAs of one cluster, each keeping its rows' y in
+// shared memory.
+// Epilogue, run by the first CTA of each head's cluster once it has gathered the head's y through
+// distributed shared memory: rms-norm (per warp the xor butterfly of y^2, warp sums added in
 // warp order, scale = 1/sqrt(sum/256 + eps), y * scale * w), rope on pairs (i, i + half) of the
 // first rope_dim dims with cos/sin from the host (glibc cosf/sinf of angles built by repeated fp32
 // multiplication); the query to Q_out, K and V quantised into the page.
@@ -219,12 +221,13 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
     return v;
 }
 
-// Epilogue of head u by one CTA of HD threads, once all of the head's rows are in p.y.  The T
+// Epilogue of head u by one CTA of HD threads, from the head's raw projections in yb (each thread
+// reads its own before the buffer is reused for the normalised rows).  The T
 // tokens go through each step together (their loads in flight at once, one pair of barriers for
 // all of them); every token's arithmetic is the same sequence as for a token alone.
 __device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD], float (*wsum)[HD / 32]) {
     const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
-    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD;
+    const int nq = p.Wq ? p.n_head : 0;
     int kind, h;   // 0 query, 1 key, 2 value
     if (u < nq) { kind = 0; h = u; }
     else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
@@ -234,7 +237,7 @@ __device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD],
 #pragma unroll
     for (int t = 0; t < PJ_MAX_T; t++) {
         if (t >= T) break;
-        o[t] = __ldcg(p.y + (int64_t)t * n_rows + u * HD + r);   // written by other CTAs: from L2
+        o[t] = yb[t][r];
         tile[t] = kind == 0 ? nullptr : tile_ptr(p.pr, p.pos + t, h);
     }
     if (kind != 2) {                                             // rms-norm, weight, rope
@@ -295,10 +298,11 @@ __device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD],
     }
 }
 
-__global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const ProjectParams p) {
+static_assert(PJ_DOT_THREADS == HD && HD / PJ_ROWS_CTA == 8, "a head is one cluster of 8 CTAs of HD threads");
+__global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const ProjectParams p) {
     extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
-    const int nq = p.Wq ? p.n_head : 0, n_rows = (nq + 2 * p.n_head_kv) * HD, nc = p.n_embd / 8;
+    const int nq = p.Wq ? p.n_head : 0, nc = p.n_embd / 8;
     const int g0 = (blockIdx.x * (PJ_DOT_THREADS / 32) + wid) * PJ_RW;   // this warp's first row (all in one head)
     const uint16_t *W;
     if (g0 < nq * HD) W = p.Wq + ((int64_t)(g0 / HD) * 2 * HD + g0 % HD) * p.n_embd;
@@ -368,35 +372,34 @@ __global__ void __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const Project
         }
     }
     KTL(2, acc[0][0] == 12345.0f);
+    // a head's rows are the 8 CTAs of one cluster: each keeps its rows' raw projections in shared
+    // memory; after one cluster barrier the first CTA reads the head's 256 through distributed
+    // shared memory, a second barrier lets the others leave, and it runs the head's epilogue
+    __shared__ float ys[PJ_MAX_T][PJ_ROWS_CTA];
 #pragma unroll
     for (int r = 0; r < PJ_RW; r++)
 #pragma unroll
         for (int t = 0; t < PJ_MAX_T; t++) {
             if (t >= T) break;
             const float y = warp_sum_bfly(acc[r][t]);
-            if (lane == t) p.y[(int64_t)t * n_rows + g0 + r] = y;
+            if (lane == t) ys[t][wid * PJ_RW + r] = y;
         }
-    // the CTA that completes a head's rows (HD / PJ_ROWS_CTA CTAs per head) runs its epilogue and
-    // resets the head's counter for the next call; nothing waits.  One release per CTA: the
-    // barrier orders every warp's rows before thread 0's fence and arrival.
     __shared__ float yb[PJ_MAX_T][HD];
     __shared__ float wsum[PJ_MAX_T][HD / 32];
-    __shared__ int s_last;
-    const int u = blockIdx.x * PJ_ROWS_CTA / HD;
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        s_last = atomicAdd(p.cnt + u, 1) == HD / PJ_ROWS_CTA - 1;
+    cg::cluster_group cluster = cg::this_cluster();
+    const bool lead = cluster.block_rank() == 0;
+    cluster.sync();   // every CTA's rows in its shared memory
+    if (lead) {
+        const float *src = cluster.map_shared_rank(&ys[0][0], tid / PJ_ROWS_CTA);
+        for (int t = 0; t < T; t++) yb[t][tid] = src[t * PJ_ROWS_CTA + tid % PJ_ROWS_CTA];
     }
-    __syncthreads();
+    cluster.sync();   // the head's rows read: the other CTAs may leave
     KTL(3, false);
-    if (!s_last) {
+    if (!lead) {
         KTL_FLUSH();
         return;
     }
-    __threadfence();
-    project_epilogue(p, u, yb, wsum);
-    if (tid == 0) p.cnt[u] = 0;
+    project_epilogue(p, blockIdx.x * PJ_ROWS_CTA / HD, yb, wsum);
     KTL(4, false);
     KTL_FLUSH();
 }
@@ -405,6 +408,18 @@ cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
     const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv, n_rows = units * HD;
     const size_t smem = (size_t)p.T * p.n_embd * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    // 48 KiB of staged x plus the kernel's own shared memory exceed the default window: opt in
+    // once per device
+    static uint64_t opted = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!(opted >> dev & 1)) {
+        if ((e = cudaFuncSetAttribute(k_project_dot, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024)) != cudaSuccess)
+            return e;
+        opted |= 1ull << dev;
+    }
     k_project_dot<<<n_rows / PJ_ROWS_CTA, PJ_DOT_THREADS, smem, st>>>(p);
     count_launches(1);
     return cudaGetLastError();

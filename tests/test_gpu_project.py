@@ -14,12 +14,12 @@ pytestmark = pytest.mark.gpu
 N_EMBD = 2560
 
 
-def weights(seed, n_head=16, n_head_kv=2):
+def weights(seed, n_head=16, n_head_kv=2, n_embd=N_EMBD):
     r = np.random.default_rng(seed)
-    s = 1 / np.sqrt(N_EMBD)
-    Wq = bf16_bits(r.standard_normal((2 * n_head * 256, N_EMBD), dtype=np.float32) * s)
-    Wk = bf16_bits(r.standard_normal((n_head_kv * 256, N_EMBD), dtype=np.float32) * s)
-    Wv = bf16_bits(r.standard_normal((n_head_kv * 256, N_EMBD), dtype=np.float32) * s)
+    s = 1 / np.sqrt(n_embd)
+    Wq = bf16_bits(r.standard_normal((2 * n_head * 256, n_embd), dtype=np.float32) * s)
+    Wk = bf16_bits(r.standard_normal((n_head_kv * 256, n_embd), dtype=np.float32) * s)
+    Wv = bf16_bits(r.standard_normal((n_head_kv * 256, n_embd), dtype=np.float32) * s)
     qn = (1 + 0.1 * r.standard_normal(256)).astype(np.float32)
     kn = (1 + 0.1 * r.standard_normal(256)).astype(np.float32)
     return Wq, Wk, Wv, qn, kn
@@ -30,15 +30,16 @@ def dev16(a):
     return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()
 
 
-@pytest.mark.parametrize("T,pos,with_q", [(3, 100, True), (1, 0, False), (4, 254, True)])
-def test_project_append_bit_exact(cuda, qkvlib, oracle, T, pos, with_q):
+@pytest.mark.parametrize("T,pos,with_q,n_embd", [(3, 100, True, N_EMBD), (1, 0, False, N_EMBD), (4, 254, True, N_EMBD),
+                                                 (4, 17, True, 3072)])   # the last: T x n_embd at its limit
+def test_project_append_bit_exact(cuda, qkvlib, oracle, T, pos, with_q, n_embd):
     import torch
     eng = engine(qkvlib, n_layer=2, n_ctx=1024, n_slots=1)
     eng.seq_alloc(0)
     if pos:
         append_rows(eng, 1, 0, 0, normal(90, (pos, 512)), normal(91, (pos, 512)))
-    Wq, Wk, Wv, qn, kn = weights(92 + T)
-    x = normal(93 + T, (T, N_EMBD))
+    Wq, Wk, Wv, qn, kn = weights(92 + T, n_embd=n_embd)
+    x = normal(93 + T, (T, n_embd))
     Qout = torch.full((T, 16, 256), float("nan"), device="cuda") if with_q else None
     eng.project_append(1, 0, pos, to_dev(x), dev16(Wq) if with_q else None, dev16(Wk), dev16(Wv),
                        to_dev(qn) if with_q else None, to_dev(kn), Qout)

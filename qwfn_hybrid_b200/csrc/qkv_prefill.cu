@@ -361,11 +361,14 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) { return ba
 // Query preparation: bf16 rows -> q8_0 (ggml quantize_row_q8_0 rounding) -> fp16(d * q), written
 // as the 64 KiB A-operand image of each tile.  One warp per row; lane l holds elements 8l..8l+7.
 __global__ void __launch_bounds__(256) k_prefill_q(const PrefillParams P) {
-    // k_prefill may become resident now; it waits for this grid before reading the query tiles.
-    // This grid itself may have started early: the queries may come from the kernel before it,
-    // and the previous call's k_prefill reads the query tiles this grid rewrites.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // This grid may have started early: the queries may come from the kernel before it, and the
+    // previous call's k_prefill reads the query tiles this grid rewrites.  k_prefill may become
+    // resident only once this wait has returned: its producers read the KV pages without a wait
+    // of their own, and an earlier kernel of the chain may still be writing them until then (the
+    // decode kernel appends its new rows into the pages and lets its dependents start at entry;
+    // its merge does the same).  k_prefill waits for this grid before reading the query tiles.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (warp >= P.n_tiles * PF_ROWS) return;
     const int tile = warp / PF_ROWS, r = warp % PF_ROWS;

@@ -105,6 +105,22 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Phase timestamps for latency analysis, compiled only with -DQKV_TIMELINE (the product build
+// never defines it): g_pf_tl[CTA][role][tile][phase], written on every launch by one thread of
+// each role for the first PF_TL_TILES KV tiles of the CTA.  Roles: 0 / 1 softmax halves (warps 1
+// and 5), 2 MMA issue (leader), 3 K producers (warp 9), 4 V producers (warp 13).
+// qkv_pf_tl_read copies the table out.
+#ifdef QKV_TIMELINE
+constexpr int PF_TL_CTAS = 160, PF_TL_TILES = 16, PF_TL_PH = 6;
+__device__ unsigned long long g_pf_tl[PF_TL_CTAS][5][PF_TL_TILES][PF_TL_PH];
+#define PF_TL(cond, role, idx, ph)                                                                   \
+    do {                                                                                             \
+        if ((cond) && (idx) >= 0 && (idx) < PF_TL_TILES && blockIdx.x < PF_TL_CTAS)                  \
+            g_pf_tl[blockIdx.x][role][idx][ph] = global_ns();                                        \
+    } while (0)
+#else
+#define PF_TL(cond, role, idx, ph) do { } while (0)
+#endif
 // Non-blocking test of the phase of `parity`.
 __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
@@ -561,6 +577,9 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
     using Load = typename std::conditional<KGRP, KLoad, VLoad>::type;
     int si = s0, k = 0;
     uint32_t op0 = 0;
+#ifdef QKV_TIMELINE
+    int jt = 0;   // operands stored so far (the KV tile of the next store)
+#endif
     Seg sg{};
     int32_t page = -1;
     if (si < s1) {
@@ -587,13 +606,19 @@ __device__ __forceinline__ void produce(const PrefillParams &P, const int4 *segs
     };
     auto store = [&](const Load &ld, uint32_t u) -> bool {
         const uint32_t sl = u % NSLOT;
+        PF_TL(t == 0, KGRP ? 3 : 4, jt, 0);
         if (u >= NSLOT && !__all_sync(0xffffffffu, wait_bar(&B->slot_free[sl], ((u / NSLOT) - 1) & 1, B, P.status)))
             return false;   // warp-uniform: every lane leaves together
+        PF_TL(t == 0, KGRP ? 3 : 4, jt, 1);
         const uint32_t slot = sbase + SM_RING + sl * SLOT_BYTES;
         if constexpr (KGRP) k_store(slot, t, ld);
         else v_store(slot, t, ld);
         fence_proxy_async();
         mbar_arrive_leader(&B->slot_full[sl], rank);
+        PF_TL(t == 0, KGRP ? 3 : 4, jt, 2);
+#ifdef QKV_TIMELINE
+        jt++;
+#endif
         return true;
     };
     Load A;
@@ -712,9 +737,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 if (!(ok = wait_bar(&B->q_peer, (si - s0) & 1, B, P.status))) break;
                 tc_fence_after();
                 for (int k = 0; k < sg.nk && ok; k++) {
+                    PF_TL(true, 2, (int)(it + k), 0);
                     ok = issue_s(it + k, op0 + op_k(k));
+                    PF_TL(true, 2, (int)(it + k), 1);
                     if (ok && k == sg.nk - 1) mma_commit_pair(&B->q_empty);
                     if (ok && k >= 1) ok = issue_pv(it + k - 1, op0 + op_v(k - 1, sg.nk), k == 1);
+                    PF_TL(true, 2, (int)(it + k), 2);
                 }
                 if (ok) ok = issue_pv(it + sg.nk - 1, op0 + op_v(sg.nk - 1, sg.nk), sg.nk == 1);
                 it += sg.nk;
@@ -783,6 +811,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
             for (int k = 0; k < sg.nk; k++) {
                 const uint32_t j = it + k, b = j & 1;
                 if (!(ok = wait_all(&B->s_full[b], (j >> 1) & 1))) break;
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 0);
                 tc_fence_after();
                 const uint32_t scol = tmem + lane_base + TM_S + b * KT;
                 const int nvis = min(max(qpos - (sg.kt0 + k) * KT + 1, 0), KT);
@@ -793,10 +822,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 // this half's max (bf16, rounded up) to shared memory; the other half reads it after
                 // the meeting.  Slot b is written again for tile j + 2, whose S needs P_j consumed,
                 // i.e. both halves past this read.
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 1);
                 pmax[(2 * b + half) * PF_ROWS + r] = max_up_bf16(hmax);
                 tc_fence_before();
                 mbar_arrive(&B->s_read[b]);
                 if (!(ok = wait_all(&B->s_read[b], (j >> 1) & 1))) break;
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 2);
                 tc_fence_after();
                 const float smax = fmaxf(bf16_bits(pmax[(2 * b) * PF_ROWS + r]), bf16_bits(pmax[(2 * b + 1) * PF_ROWS + r]));
                 // lazily raised reference max: O and l are rescaled only when a row max grows by
@@ -809,6 +840,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                 const float mu = m_ref == -INFINITY ? 0.f : m_ref;   // fully masked so far: p = 0
                 l += full ? half_p<true>(scol, half, nvis, word, P.scale_log2, mu)
                           : half_p<false>(scol, half, nvis, word, P.scale_log2, mu);
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 3);
                 if (k > 0 && __any_sync(0xffffffffu, F != 1.0f)) {
                     // O holds PV of the previous tile: rescale it once that product has landed
                     if (!(ok = wait_all(&B->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
@@ -824,8 +856,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_prefill(const __grid_constant__ Pre
                     }
                 }
                 tmem_wait_st();
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 4);
                 tc_fence_before();
                 mbar_arrive_leader(&B->p_full[b], rank);
+                PF_TL(lane == 0 && (warp & 3) == 1, half, (int)j, 5);
             }
             if (!ok) break;
             // ---- epilogue: this half's O columns of the segment's partial record
@@ -942,6 +976,19 @@ __global__ void __launch_bounds__(256) k_prefill_merge(const __grid_constant__ P
 }
 
 }  // namespace pf
+#ifdef QKV_TIMELINE
+}  // namespace qkv
+extern "C" int qkv_pf_tl_read(unsigned long long *host, int reset) {
+    const size_t bytes = sizeof(qkv::pf::g_pf_tl);
+    if (host && cudaMemcpyFromSymbol(host, qkv::pf::g_pf_tl, bytes) != cudaSuccess) return -1;
+    if (reset) {
+        void *d = nullptr;
+        if (cudaGetSymbolAddress(&d, qkv::pf::g_pf_tl) != cudaSuccess || cudaMemset(d, 0, bytes) != cudaSuccess) return -1;
+    }
+    return (int)(bytes / 8);
+}
+namespace qkv {
+#endif
 
 // Launch of a kernel that may start while the previous kernel on the stream finishes
 // (programmatic dependent launch); it synchronises itself with griddepcontrol.wait.

@@ -3,6 +3,7 @@
     python -m qwfn_hybrid_b200.build --timeline         # libqkv_timeline.so (-DQKV_TIMELINE)
     python -m qwfn_hybrid_b200.timeline decode           # configs[1]'s layer: 12 layers, T = 3, ctx 16384
     python -m qwfn_hybrid_b200.timeline proj             # qkv_project_append, 12 layers, T = 3
+    python -m qwfn_hybrid_b200.timeline prefill          # configs[2]'s last chunk (kernel D roles)
 
 In the timeline build, thread 0 of every CTA notes %globaltimer at fixed points of its kernel and
 appends one record per CTA; this tool replays a CUDA graph of the workload once, reads the records
@@ -14,8 +15,9 @@ copies issued, 18 / 19 thread 0's first / all query values arrived, 7 query rows
 2 rows in shared memory (CTA barrier), 8 first tile landed, 10-13 first tile: QK done, P barrier,
 after the reference move, PV done; 3 first tile finished; 14-17 the same for the second tile; 4 all
 tiles done; 5 partial record written.  Merge phases: 0 entry, 1 wait returned, 2 output written.
-Projection phases: 0 entry, 1 x staged, 2 dot products done, 3 head counter taken, 4 epilogue done
-(the head's last CTA only).
+Projection phases: 0 entry, 1 x staged, 2 dot products done, 3 the head's rows gathered by the
+cluster's lead CTA (after the second cluster barrier), 4 epilogue done (the lead CTA only).
+Prefill: per-role phase durations of kernel D (see `prefill`).
 """
 from __future__ import annotations
 
@@ -159,6 +161,66 @@ def proj() -> None:
         print(f"layer {layer} ({len(r)} CTAs) phase: median/max ns -> " + ", ".join(cells))
 
 
+def prefill(chunk: int = 31) -> None:
+    """configs[2]'s chunk `chunk` (512 queries at 512 chunk .. over the 16384 cached keys), called
+    eagerly; the table of the last call.  Per role, the median over CTAs of each phase's duration
+    in ns, for the first KV tiles of each CTA."""
+    import torch
+    Q, L = _engine_lib()
+    L.qkv_pf_tl_read.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    L.qkv_pf_tl_read.restype = ctypes.c_int
+    N, C = 16384, 512
+    dev = torch.device("cuda", 0)
+    eng = Q.Engine(n_layer=1, n_head=16, n_head_kv=2, n_ctx=N, n_slots=1, device=0)
+    eng.seq_alloc(0)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    eng.append(0, 0, 0, torch.randn(N, 512, generator=gen, device=dev), torch.randn(N, 512, generator=gen, device=dev))
+    Qb = torch.randn(C, 16, 256, generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
+    out = torch.empty(C, 16, 256, device=dev)
+    a = chunk * C
+    for _ in range(5):
+        eng.attn_prefill(0, 0, a, Qb, C, 1 / 16, out)
+    torch.cuda.synchronize()
+    n = L.qkv_pf_tl_read(None, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.attn_prefill(0, 0, a, Qb, C, 1 / 16, out)
+    e1.record()
+    torch.cuda.synchronize()
+    buf = np.zeros(n, dtype=np.uint64)
+    L.qkv_pf_tl_read(buf.ctypes.data, 0)
+    tl = buf.reshape(-1, 5, 16, 6).astype(np.int64)
+    print(f"prefill chunk {chunk}: {e0.elapsed_time(e1) * 1e3:.1f} us for the call (3 launches, eager)")
+
+    def med(x):
+        x = [v for v in x if v is not None]
+        return f"{statistics.median(x):6.0f}" if x else "     -"
+
+    def dur(role, k, p1, k2, p2, rank=None):   # per-CTA durations: stamp (k2, p2) - stamp (k, p1)
+        out = []
+        for c in range(tl.shape[0]):
+            if rank is not None and c % 2 != rank:
+                continue
+            a, b = tl[c, role, k, p1], tl[c, role, k2, p2]
+            out.append(int(b - a) if a > 0 and b > 0 else None)
+        return out
+
+    names = ["max pass", "exchange", "P pass", "rescale+st", "arrive", "to next S"]
+    for role in (0, 1):
+        for rank in (0, 1):
+            print(f"softmax half {role}, {('leader', 'follower')[rank]} CTAs: per KV tile j, ns: " + " | ".join(names) + " | period")
+            for k in range(15):
+                cells = [med(dur(role, k, i, k, i + 1, rank)) for i in range(5)] + \
+                        [med(dur(role, k, 5, k + 1, 0, rank)), med(dur(role, k, 0, k + 1, 0, rank))]
+                print(f"  j={k:2d} " + " ".join(cells))
+    print("MMA issue (leader): per KV tile j, ns: K slot + S_j issue | p_full(j-1) + V slot + PV_{j-1} issue | period")
+    for k in range(15):
+        print(f"  j={k:2d} {med(dur(2, k, 0, k, 1))} {med(dur(2, k, 1, k, 2))} {med(dur(2, k, 0, k + 1, 0))}")
+    for role, nm in ((3, "K"), (4, "V")):
+        print(f"{nm} producers: per KV tile j, ns: slot free wait | dequantise + store + arrive | period")
+        for u in range(15):
+            print(f"  j={u:2d} {med(dur(role, u, 0, u, 1))} {med(dur(role, u, 1, u, 2))} {med(dur(role, u, 0, u + 1, 0))}")
+
 if __name__ == "__main__":
     what = sys.argv[1] if len(sys.argv) > 1 else "decode"
-    {"decode": decode, "proj": proj}[what]()
+    {"decode": decode, "proj": proj, "prefill": prefill}[what]()

@@ -12,11 +12,17 @@
 namespace qkv {
 namespace cg = cooperative_groups;
 
-__device__ __forceinline__ uint8_t *tile_ptr(const PoolRef &pr, int32_t pos, int h) {
-    if (pos < 0 || (pos >> 8) >= pr.max_pages) return nullptr;
-    const int32_t page = pr.bt[pos >> 8];
+// The block-table entry of position pos (-1 outside the table), and the tile of KV head h at pos
+// in that page (nullptr for an entry outside the pool).
+__device__ __forceinline__ int32_t page_of_pos(const PoolRef &pr, int32_t pos) {
+    return pos < 0 || (pos >> 8) >= pr.max_pages ? -1 : pr.bt[pos >> 8];
+}
+__device__ __forceinline__ uint8_t *tile_in_page(const PoolRef &pr, int32_t page, int32_t pos, int h) {
     if (page < 0 || page >= pr.n_pages) return nullptr;
     return pr.pool + (int64_t)page * pr.page_bytes + (int64_t)(h * TILES_PER_PAGE + ((pos >> 6) & 3)) * TILE_BYTES;
+}
+__device__ __forceinline__ uint8_t *tile_ptr(const PoolRef &pr, int32_t pos, int h) {
+    return tile_in_page(pr, page_of_pos(pr, pos), pos, h);
 }
 
 // ------------------------------------------------------------------------------------ kernel A
@@ -213,7 +219,19 @@ __device__ unsigned int g_ktl_n;
 
 constexpr int PJ_RW = 4;       // rows per warp: each x value read from shared memory serves four rows
 constexpr int PJ_DOT_THREADS = 256, PJ_ROWS_CTA = PJ_DOT_THREADS / 32 * PJ_RW;
-constexpr int PJ_BATCH = 2;    // chunks per row in flight per lane (x PJ_RW rows; after the rows' L2 prefetch)
+// Weight chunks stream through a ring of PJ_NS stages in shared memory by per-thread asynchronous
+// copies: in stage s, lane l of a warp copies 8-dim chunk 32 s + l of each of its PJ_RW rows (16
+// bytes each) into its own slots and later reads exactly those, so no barrier is involved; a
+// lane keeps PJ_NS - 1 stages (4 x 16 B each) in flight without holding registers.
+constexpr int PJ_NS = 3, PJ_STAGE = PJ_DOT_THREADS * PJ_RW * 16;   // 16 KiB per stage
+
+__device__ __forceinline__ void pj_cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void pj_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pj_wait_groups() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ float warp_sum_bfly(float v) {
 #pragma unroll
@@ -225,20 +243,28 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
 // reads its own before the buffer is reused for the normalised rows).  The T
 // tokens go through each step together (their loads in flight at once, one pair of barriers for
 // all of them); every token's arithmetic is the same sequence as for a token alone.
-__device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD], float (*wsum)[HD / 32]) {
-    const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
+// Head u's kind (0 query, 1 key, 2 value) and index within its kind.
+__device__ __forceinline__ int pj_kind(const ProjectParams &p, int u, int &h) {
     const int nq = p.Wq ? p.n_head : 0;
-    int kind, h;   // 0 query, 1 key, 2 value
-    if (u < nq) { kind = 0; h = u; }
-    else if (u < nq + p.n_head_kv) { kind = 1; h = u - nq; }
-    else { kind = 2; h = u - nq - p.n_head_kv; }
+    if (u < nq) { h = u; return 0; }
+    if (u < nq + p.n_head_kv) { h = u - nq; return 1; }
+    h = u - nq - p.n_head_kv;
+    return 2;
+}
+// w: this thread's norm weight, page: the tokens' block-table entries (keys and values), both
+// loaded by the caller before the dot products so that their latency is hidden.
+__device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD], float (*wsum)[HD / 32], float w,
+                                 const int32_t (&page)[PJ_MAX_T]) {
+    const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
+    int h;
+    const int kind = pj_kind(p, u, h);
     float o[PJ_MAX_T];
     uint8_t *tile[PJ_MAX_T];
 #pragma unroll
     for (int t = 0; t < PJ_MAX_T; t++) {
         if (t >= T) break;
         o[t] = yb[t][r];
-        tile[t] = kind == 0 ? nullptr : tile_ptr(p.pr, p.pos + t, h);
+        tile[t] = kind == 0 ? nullptr : tile_in_page(p.pr, page[t], p.pos + t, h);
     }
     if (kind != 2) {                                             // rms-norm, weight, rope
 #pragma unroll
@@ -248,8 +274,6 @@ __device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD],
             if (lane == 0) wsum[t][wid] = s2;
         }
         __syncthreads();
-        const float *nw = kind == 0 ? p.q_norm : p.k_norm;
-        const float w = nw[r];
 #pragma unroll
         for (int t = 0; t < PJ_MAX_T; t++) {
             if (t >= T) break;
@@ -300,20 +324,48 @@ __device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD],
 
 static_assert(PJ_DOT_THREADS == HD && HD / PJ_ROWS_CTA == 8, "a head is one cluster of 8 CTAs of HD threads");
 __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k_project_dot(const ProjectParams p) {
-    extern __shared__ float4 xs4[];   // [2][T][n_embd / 8]: dims 0-3 then dims 4-7 of every 8-dim chunk
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, T = p.T;
-    const int nq = p.Wq ? p.n_head : 0, nc = p.n_embd / 8;
+    const int nq = p.Wq ? p.n_head : 0;
     const int g0 = (blockIdx.x * (PJ_DOT_THREADS / 32) + wid) * PJ_RW;   // this warp's first row (all in one head)
     const uint16_t *W;
     if (g0 < nq * HD) W = p.Wq + ((int64_t)(g0 / HD) * 2 * HD + g0 % HD) * p.n_embd;
     else if (g0 < (nq + p.n_head_kv) * HD) W = p.Wk + (int64_t)(g0 - nq * HD) * p.n_embd;
     else W = p.Wv + (int64_t)(g0 - (nq + p.n_head_kv) * HD) * p.n_embd;
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(W);   // row r at w4 + r * nc
+    // dynamic shared memory: x as [2][T][n_embd / 8] float4 (dims 0-3, then dims 4-7 of every
+    // 8-dim chunk), then the ring [PJ_NS][warp][row][lane] of 16-byte weight chunks
+    extern __shared__ __align__(128) uint8_t pj_dyn[];
+    float4 *xs4 = reinterpret_cast<float4 *>(pj_dyn);
+    uint4 *ring = reinterpret_cast<uint4 *>(pj_dyn + (size_t)T * p.n_embd * sizeof(float)) + (wid * PJ_RW) * 32 + lane;
+    const int nc = p.n_embd / 8, nst = nc / 32;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(W) + lane;   // row r, stage s at w4 + r nc + 32 s
+    auto issue = [&](int s) {
+        if (s < nst)
+#pragma unroll
+            for (int r = 0; r < PJ_RW; r++) pj_cp16(ring + (s % PJ_NS) * (PJ_STAGE / 16) + r * 32, w4 + (int64_t)r * nc + 32 * s);
+        pj_commit();   // an empty group past the end keeps the group count uniform
+    };
     KTL_DECL
     KTL(0, false);
-    // x first (a thread's loads all in flight before its stores; conflict-free reads: lane stride
-    // 16 B), then the warp's weight rows are requested at once behind them (into L2 by the
-    // bulk-copy engine, one request per row, no registers held) and read in batches below
+    // the weight copies of the first stages go out first; then the lead CTA's epilogue inputs
+    // (norm weight, block-table entries: nothing waits for them before the epilogue); then x (a
+    // thread's loads all in flight before its stores; conflict-free reads: lane stride 16 B), the
+    // rest of the warp's rows requested into L2 behind them (one bulk prefetch per row)
+#pragma unroll
+    for (int s = 0; s < PJ_NS - 1; s++) issue(s);
+    const bool lead = (blockIdx.x & 7) == 0;
+    float nwt = 0.f;
+    int32_t page[PJ_MAX_T];
+#pragma unroll
+    for (int t = 0; t < PJ_MAX_T; t++) page[t] = -1;
+    if (lead) {
+        int h;
+        const int kind = pj_kind(p, blockIdx.x * PJ_ROWS_CTA / HD, h);
+        if (kind != 2) nwt = (kind == 0 ? p.q_norm : p.k_norm)[tid];
+        if (kind != 0)
+#pragma unroll
+            for (int t = 0; t < PJ_MAX_T; t++)
+                if (t < T) page[t] = page_of_pos(p.pr, p.pos + t);
+    }
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
     {
         constexpr int XU = 8;
@@ -325,8 +377,10 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
                 const int i = i0 + k * PJ_DOT_THREADS;
                 if (i < nx) v[k] = x4[i];
             }
-            if (first && lane < PJ_RW)
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w4 + (int64_t)lane * nc), "r"(nc * 16) : "memory");
+            if (first && lane < PJ_RW && nst > PJ_NS - 1)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(W + (int64_t)lane * p.n_embd + (PJ_NS - 1) * 256),
+                             "r"((nst - PJ_NS + 1) * 512)
+                             : "memory");
 #pragma unroll
             for (int k = 0; k < XU; k++) {
                 const int i = i0 + k * PJ_DOT_THREADS;
@@ -337,40 +391,36 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
     }
     __syncthreads();
     KTL(1, false);
+    // lane l takes chunk 32 s + l of its rows in stage s: chunks l, l + 32, ... in order
     float acc[PJ_RW][PJ_MAX_T] = {};
-    for (int j0 = 0; 32 * j0 < nc; j0 += PJ_BATCH) {
-        uint4 wb[PJ_BATCH][PJ_RW];
+    for (int s = 0; s < nst; s++) {
+        issue(s + PJ_NS - 1);          // into the slot this lane finished reading last iteration
+        pj_wait_groups<PJ_NS - 1>();   // stage s landed (this lane's own copies)
+        const int c = 32 * s + lane;
+        uint4 wb[PJ_RW];
 #pragma unroll
-        for (int j = 0; j < PJ_BATCH; j++) {
-            const int c = lane + 32 * (j0 + j);
+        for (int r = 0; r < PJ_RW; r++) wb[r] = ring[(s % PJ_NS) * (PJ_STAGE / 16) + r * 32];
 #pragma unroll
-            for (int r = 0; r < PJ_RW; r++) wb[j][r] = c < nc ? __ldcs(w4 + (int64_t)r * nc + c) : make_uint4(0, 0, 0, 0);
-        }
+        for (int t = 0; t < PJ_MAX_T; t++) {
+            if (t >= T) break;
+            const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];   // one read for the warp's rows
 #pragma unroll
-        for (int j = 0; j < PJ_BATCH; j++) {
-            const int c = lane + 32 * (j0 + j);
-            if (c >= nc) break;
-#pragma unroll
-            for (int t = 0; t < PJ_MAX_T; t++) {
-                if (t >= T) break;
-                const float4 xa = xs4[t * nc + c], xb = xs4[(T + t) * nc + c];   // one read for the warp's rows
-#pragma unroll
-                for (int r = 0; r < PJ_RW; r++) {
-                    const uint32_t wv[4] = {wb[j][r].x, wb[j][r].y, wb[j][r].z, wb[j][r].w};
-                    float a = acc[r][t];
-                    a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
-                    a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
-                    a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
-                    a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
-                    a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
-                    a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
-                    a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
-                    a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
-                    acc[r][t] = a;
-                }
+            for (int r = 0; r < PJ_RW; r++) {
+                const uint32_t wv[4] = {wb[r].x, wb[r].y, wb[r].z, wb[r].w};
+                float a = acc[r][t];
+                a = __fmaf_rn(__uint_as_float(wv[0] << 16), xa.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[0] & 0xffff0000u), xa.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] << 16), xa.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[1] & 0xffff0000u), xa.w, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] << 16), xb.x, a);
+                a = __fmaf_rn(__uint_as_float(wv[2] & 0xffff0000u), xb.y, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] << 16), xb.z, a);
+                a = __fmaf_rn(__uint_as_float(wv[3] & 0xffff0000u), xb.w, a);
+                acc[r][t] = a;
             }
         }
     }
+    pj_wait_groups<0>();   // nothing in flight at exit (the trailing groups are empty)
     KTL(2, acc[0][0] == 12345.0f);
     // a head's rows are the 8 CTAs of one cluster: each keeps its rows' raw projections in shared
     // memory; after one cluster barrier the first CTA reads the head's 256 through distributed
@@ -387,7 +437,6 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
     __shared__ float yb[PJ_MAX_T][HD];
     __shared__ float wsum[PJ_MAX_T][HD / 32];
     cg::cluster_group cluster = cg::this_cluster();
-    const bool lead = cluster.block_rank() == 0;
     cluster.sync();   // every CTA's rows in its shared memory
     if (lead) {
         const float *src = cluster.map_shared_rank(&ys[0][0], tid / PJ_ROWS_CTA);
@@ -399,24 +448,25 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
         KTL_FLUSH();
         return;
     }
-    project_epilogue(p, blockIdx.x * PJ_ROWS_CTA / HD, yb, wsum);
+    project_epilogue(p, blockIdx.x * PJ_ROWS_CTA / HD, yb, wsum, nwt, page);
     KTL(4, false);
     KTL_FLUSH();
 }
 
 cudaError_t launch_project(const ProjectParams &p, cudaStream_t st) {
     const int units = (p.Wq ? p.n_head : 0) + 2 * p.n_head_kv, n_rows = units * HD;
-    const size_t smem = (size_t)p.T * p.n_embd * sizeof(float);
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    // 48 KiB of staged x plus the kernel's own shared memory exceed the default window: opt in
-    // once per device
+    const size_t xbytes = (size_t)p.T * p.n_embd * sizeof(float);
+    if (xbytes > 48 * 1024 || p.n_embd % 256) return cudaErrorInvalidValue;
+    constexpr int SMEM_MAX = 48 * 1024 + PJ_NS * PJ_STAGE;
+    const size_t smem = xbytes + PJ_NS * PJ_STAGE;   // staged x, then the ring of weight stages
+    // beyond the default 48 KiB window: opt in once per device (up to 96 KiB: two CTAs per SM)
     static uint64_t opted = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!(opted >> dev & 1)) {
-        if ((e = cudaFuncSetAttribute(k_project_dot, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024)) != cudaSuccess)
+        if ((e = cudaFuncSetAttribute(k_project_dot, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX)) != cudaSuccess)
             return e;
         opted |= 1ull << dev;
     }

@@ -239,10 +239,6 @@ __device__ __forceinline__ float warp_sum_bfly(float v) {
     return v;
 }
 
-// Epilogue of head u by one CTA of HD threads, from the head's raw projections in yb (each thread
-// reads its own before the buffer is reused for the normalised rows).  The T
-// tokens go through each step together (their loads in flight at once, one pair of barriers for
-// all of them); every token's arithmetic is the same sequence as for a token alone.
 // Head u's kind (0 query, 1 key, 2 value) and index within its kind.
 __device__ __forceinline__ int pj_kind(const ProjectParams &p, int u, int &h) {
     const int nq = p.Wq ? p.n_head : 0;
@@ -250,76 +246,6 @@ __device__ __forceinline__ int pj_kind(const ProjectParams &p, int u, int &h) {
     if (u < nq + p.n_head_kv) { h = u - nq; return 1; }
     h = u - nq - p.n_head_kv;
     return 2;
-}
-// w: this thread's norm weight, page: the tokens' block-table entries (keys and values), both
-// loaded by the caller before the dot products so that their latency is hidden.
-__device__ void project_epilogue(const ProjectParams &p, int u, float (*yb)[HD], float (*wsum)[HD / 32], float w,
-                                 const int32_t (&page)[PJ_MAX_T]) {
-    const int r = threadIdx.x, lane = r & 31, wid = r >> 5, T = p.T;
-    int h;
-    const int kind = pj_kind(p, u, h);
-    float o[PJ_MAX_T];
-    uint8_t *tile[PJ_MAX_T];
-#pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++) {
-        if (t >= T) break;
-        o[t] = yb[t][r];
-        tile[t] = kind == 0 ? nullptr : tile_in_page(p.pr, page[t], p.pos + t, h);
-    }
-    if (kind != 2) {                                             // rms-norm, weight, rope
-#pragma unroll
-        for (int t = 0; t < PJ_MAX_T; t++) {
-            if (t >= T) break;
-            const float s2 = warp_sum_bfly(__fmul_rn(o[t], o[t]));
-            if (lane == 0) wsum[t][wid] = s2;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int t = 0; t < PJ_MAX_T; t++) {
-            if (t >= T) break;
-            float s = wsum[t][0];
-            for (int k = 1; k < HD / 32; k++) s = __fadd_rn(s, wsum[t][k]);
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, 1.0f / HD), p.eps)));
-            yb[t][r] = __fmul_rn(__fmul_rn(o[t], scale), w);
-        }
-        __syncthreads();
-        const int hh = p.rope_half;
-#pragma unroll
-        for (int t = 0; t < PJ_MAX_T; t++) {
-            if (t >= T) break;
-            o[t] = yb[t][r];
-            if (r < hh) {
-                const float2 c = p.cs[t][r];
-                o[t] = __fsub_rn(__fmul_rn(yb[t][r], c.x), __fmul_rn(yb[t][r + hh], c.y));
-            } else if (r < 2 * hh) {
-                const float2 c = p.cs[t][r - hh];
-                o[t] = __fadd_rn(__fmul_rn(yb[t][r - hh], c.y), __fmul_rn(yb[t][r], c.x));
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++) {
-        if (t >= T) break;
-        if (kind == 0) {
-            p.Q_out[((int64_t)t * p.n_head + h) * HD + r] = o[t];
-            continue;
-        }
-        if (!tile[t]) {
-            if (r == 0) atomicOr(p.pr.status, ST_BAD_PAGE);
-            continue;
-        }
-        int8_t qv;
-        __half dh;
-        quant_block_warp(o[t], lane, qv, dh);               // warp w holds q8_0 block w of the row
-        const int tt = (p.pos + t) & 63;
-        if (kind == 1) {
-            tile[t][k_off(tt, r)] = (uint8_t)qv;
-            if (lane == 0) *reinterpret_cast<__half *>(tile[t] + kd_off(tt, wid)) = dh;
-        } else {
-            tile[t][v_off(r, tt)] = (uint8_t)qv;
-            if (lane == 0) *reinterpret_cast<__half *>(tile[t] + vd_off(wid, tt)) = dh;
-        }
-    }
 }
 
 static_assert(PJ_DOT_THREADS == HD && HD / PJ_ROWS_CTA == 8, "a head is one cluster of 8 CTAs of HD threads");
@@ -346,26 +272,19 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
     };
     KTL_DECL
     KTL(0, false);
-    // the weight copies of the first stages go out first; then the lead CTA's epilogue inputs
-    // (norm weight, block-table entries: nothing waits for them before the epilogue); then x (a
+    // the weight copies of the first stages go out first; then the epilogue's inputs (norm
+    // weight, block-table entry: nothing waits for them before the epilogue); then x (a
     // thread's loads all in flight before its stores; conflict-free reads: lane stride 16 B), the
     // rest of the warp's rows requested into L2 behind them (one bulk prefetch per row)
 #pragma unroll
     for (int s = 0; s < PJ_NS - 1; s++) issue(s);
-    const bool lead = (blockIdx.x & 7) == 0;
-    float nwt = 0.f;
-    int32_t page[PJ_MAX_T];
-#pragma unroll
-    for (int t = 0; t < PJ_MAX_T; t++) page[t] = -1;
-    if (lead) {
-        int h;
-        const int kind = pj_kind(p, blockIdx.x * PJ_ROWS_CTA / HD, h);
-        if (kind != 2) nwt = (kind == 0 ? p.q_norm : p.k_norm)[tid];
-        if (kind != 0)
-#pragma unroll
-            for (int t = 0; t < PJ_MAX_T; t++)
-                if (t < T) page[t] = page_of_pos(p.pr, p.pos + t);
-    }
+    // the epilogue's inputs: this CTA's 32 dims of head u are 32 k .. 32 k + 31 (k: its rank in
+    // the cluster), a lane's dim is 32 k + lane
+    const int u = blockIdx.x * PJ_ROWS_CTA / HD, k8 = blockIdx.x & 7, d = 32 * k8 + lane;
+    int h;
+    const int kind = pj_kind(p, u, h);
+    const float nwt = kind != 2 ? (kind == 0 ? p.q_norm : p.k_norm)[d] : 0.f;
+    const int32_t page = kind != 0 && wid < T ? page_of_pos(p.pr, p.pos + wid) : -1;   // warp t: token t
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
     {
         constexpr int XU = 8;
@@ -422,10 +341,15 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
     }
     pj_wait_groups<0>();   // nothing in flight at exit (the trailing groups are empty)
     KTL(2, acc[0][0] == 12345.0f);
-    // a head's rows are the 8 CTAs of one cluster: each keeps its rows' raw projections in shared
-    // memory; after one cluster barrier the first CTA reads the head's 256 through distributed
-    // shared memory, a second barrier lets the others leave, and it runs the head's epilogue
-    __shared__ float ys[PJ_MAX_T][PJ_ROWS_CTA];
+    // A head's 256 rows are the 8 CTAs of one cluster, CTA k holding dims 32 k .. 32 k + 31: one
+    // warp butterfly of the rms norm and one q8_0 block.  Warp t runs token t's epilogue for this
+    // CTA's dims; the eight sums of squares and rope's partner dims cross the cluster through
+    // distributed shared memory.  Each step is the single-head arithmetic of the reference's
+    // rms() / rope() and kernel A's rounding, in the same order (the sum of squares: warp
+    // butterflies of 32 dims, added in dim order).
+    __shared__ float ys[PJ_MAX_T][PJ_ROWS_CTA];   // raw projections of this CTA's dims
+    __shared__ float ssq[PJ_MAX_T];               // per token: their sum of squares
+    __shared__ float yn[PJ_MAX_T][PJ_ROWS_CTA];   // normalised and weighted
 #pragma unroll
     for (int r = 0; r < PJ_RW; r++)
 #pragma unroll
@@ -434,22 +358,63 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(PJ_DOT_THREADS, 2) k
             const float y = warp_sum_bfly(acc[r][t]);
             if (lane == t) ys[t][wid * PJ_RW + r] = y;
         }
-    __shared__ float yb[PJ_MAX_T][HD];
-    __shared__ float wsum[PJ_MAX_T][HD / 32];
+    __syncthreads();
+    const int t = wid;   // this warp's token (t < T)
+    float o = t < T ? ys[t][lane] : 0.f;
+    if (t < T && kind != 2) {
+        const float s2 = warp_sum_bfly(__fmul_rn(o, o));
+        if (lane == 0) ssq[t] = s2;
+    }
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();   // every CTA's rows in its shared memory
-    if (lead) {
-        const float *src = cluster.map_shared_rank(&ys[0][0], tid / PJ_ROWS_CTA);
-        for (int t = 0; t < T; t++) yb[t][tid] = src[t * PJ_ROWS_CTA + tid % PJ_ROWS_CTA];
+    cluster.sync();   // every CTA's sums of squares posted
+    if (t < T && kind != 2) {
+        float sq[HD / 32];
+#pragma unroll
+        for (int k = 0; k < HD / 32; k++) sq[k] = *cluster.map_shared_rank(&ssq[t], k);
+        float sum = sq[0];
+#pragma unroll
+        for (int k = 1; k < HD / 32; k++) sum = __fadd_rn(sum, sq[k]);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum, 1.0f / HD), p.eps)));
+        yn[t][lane] = __fmul_rn(__fmul_rn(o, scale), nwt);
     }
-    cluster.sync();   // the head's rows read: the other CTAs may leave
+    cluster.sync();   // every CTA's normalised dims posted
     KTL(3, false);
-    if (!lead) {
-        KTL_FLUSH();
-        return;
+    if (t < T) {
+        if (kind != 2) {
+            const int hh = p.rope_half;
+            const float v = yn[t][lane];
+            o = v;
+            if (d < hh) {
+                const float2 c = p.cs[t][d];
+                const float w2 = *cluster.map_shared_rank(&yn[t][(d + hh) % 32], (d + hh) / 32);
+                o = __fsub_rn(__fmul_rn(v, c.x), __fmul_rn(w2, c.y));
+            } else if (d < 2 * hh) {
+                const float2 c = p.cs[t][d - hh];
+                const float w1 = *cluster.map_shared_rank(&yn[t][(d - hh) % 32], (d - hh) / 32);
+                o = __fadd_rn(__fmul_rn(w1, c.y), __fmul_rn(v, c.x));
+            }
+        }
+        if (kind == 0) {
+            p.Q_out[((int64_t)t * p.n_head + h) * HD + d] = o;
+        } else {
+            uint8_t *tile = tile_in_page(p.pr, page, p.pos + t, h);
+            int8_t qv;
+            __half dh;
+            quant_block_warp(o, lane, qv, dh);   // this CTA's dims are q8_0 block k8 of the row
+            const int tt = (p.pos + t) & 63;
+            if (!tile) {
+                if (lane == 0) atomicOr(p.pr.status, ST_BAD_PAGE);
+            } else if (kind == 1) {
+                tile[k_off(tt, d)] = (uint8_t)qv;
+                if (lane == 0) *reinterpret_cast<__half *>(tile + kd_off(tt, k8)) = dh;
+            } else {
+                tile[v_off(d, tt)] = (uint8_t)qv;
+                if (lane == 0) *reinterpret_cast<__half *>(tile + vd_off(k8, tt)) = dh;
+            }
+        }
     }
-    project_epilogue(p, blockIdx.x * PJ_ROWS_CTA / HD, yb, wsum, nwt, page);
     KTL(4, false);
+    cluster.sync();   // the partners' reads of this CTA's dims are done before it exits
     KTL_FLUSH();
 }
 

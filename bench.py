@@ -58,12 +58,13 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline only: skip the ragged and configs sub-records")
-    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "qsa", "proj", "append"],
+    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "qsa", "proj", "append", "long"],
                     default="cfg2",
                     help="cfg2 (default, the headline line with its sub-records): BASELINE configs[1]; cfg1/cfg3/"
                          "cfg4/cfg5: configs[0]/[2]/[3]/[4] alone; qsa: configs[3]'s context and tokens through the "
                          "model's own lightning indexer (select + sparse attention over the kept blocks in place); proj: the fused decode "
-                         "projections + norm + rope + q8_0 append of configs[1]'s step; append: kernel A alone")
+                         "projections + norm + rope + q8_0 append of configs[1]'s step; append: kernel A alone; long: "
+                         "configs[1]'s step for one sequence at ctx 73728")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5: use the first N of the 64 sequences (profiling)")
     return ap.parse_args()
 
@@ -476,6 +477,91 @@ def measure_cfg2(args, rank: int, ws: int, local: int) -> dict:
     return line
 
 
+# ----------------------------------------------------------------------------- ctx 73,728
+CTX_LONG = 73728
+
+
+def measure_long(args, local: int, steps: int = 10) -> dict:
+    """configs[1]'s step (12 layers, T = 3, one fused append + verify launch per layer) for one
+    sequence at context 73,728, the top of the metric's 16K-73K range.  The prefix is device-seeded
+    N(0,1) (torch Philox, seed 73); the K steps are one CUDA graph, median of REPLAYS replays; the
+    last step's layer 0 is checked against the oracle."""
+    import numpy as np
+    import torch
+    import qwfn_hybrid_b200 as Q
+    from oracle import oracle as O
+    dev = torch.device("cuda", local)
+    warm = max(args.warmup, 3)
+    total = warm + steps
+    eng = Q.Engine(n_layer=N_LAYER, n_head=N_HEAD, n_head_kv=N_HEAD_KV, n_ctx=CTX_LONG + T * (total + 8), n_slots=1,
+                   device=local)
+    eng.seq_alloc(0)
+    gen = torch.Generator(device=dev).manual_seed(73)
+    for l in range(N_LAYER):
+        eng.append(l, 0, 0, torch.randn(CTX_LONG, KV_DIM, generator=gen, device=dev),
+                   torch.randn(CTX_LONG, KV_DIM, generator=gen, device=dev))
+    eng.reserve(0, CTX_LONG + T * total)
+    Qd = torch.randn(total, N_LAYER, T, N_HEAD, HD, generator=gen, device=dev)
+    Kd = torch.randn(total, N_LAYER, T, KV_DIM, generator=gen, device=dev)
+    Vd = torch.randn(total, N_LAYER, T, KV_DIM, generator=gen, device=dev)
+    out = torch.empty(N_LAYER, T, N_HEAD, HD, device=dev)
+
+    def step(i: int):
+        for l in range(N_LAYER):
+            eng.append_attn_decode(l, [0], [CTX_LONG + T * i], Kd[i, l], Vd[i, l], Qd[i, l], T, SCALE, out[l])
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(warm, total):
+            step(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    per = []
+    for _ in range(REPLAYS):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per.append(e0.elapsed_time(e1))
+    del graph
+    if eng.device_status() != 0:
+        raise RuntimeError("device status reported a bounds violation")
+    ms = statistics.median(per)
+    # parity: layer 0 of the last step (its appended rows bit-exact, attention vs the oracle)
+    last, l = total - 1, 0
+    n0 = CTX_LONG + T * last
+    Kr = torch.empty((n0 + T, ROW_BYTES), dtype=torch.uint8, device=dev)
+    Vr = torch.empty_like(Kr)
+    eng.read_rows(l, 0, 0, n0 + T, Kr, Vr)
+    torch.cuda.synchronize()
+    Kh, Vh = Kr.cpu().numpy(), Vr.cpu().numpy()
+    rows_ok = bool(np.array_equal(Kh[n0:], O.quantize_rows(Kd[last, l].cpu().numpy())) and
+                   np.array_equal(Vh[n0:], O.quantize_rows(Vd[last, l].cpu().numpy())))
+    ref = O.attn(Qd[last, l].cpu().numpy(), Kh, Vh, np.arange(n0, n0 + T, dtype=np.int32), N_HEAD_KV, SCALE,
+                 threads=host_threads())
+    err = np.abs(out[l].cpu().numpy() - ref)
+    ok = rows_ok and bool((err <= 2e-3 + 1e-3 * np.abs(ref)).all())
+    eng.close()
+    ms_launch = ms / (steps * N_LAYER)
+    io_bytes = 2 * T * N_HEAD * HD * 4 + 2 * T * KV_DIM * 4 + 2 * T * ROW_BYTES
+    dec_bytes = statistics.mean([(CTX_LONG + T * (i + 1)) * 2 * ROW_BYTES + io_bytes for i in range(warm, total)])
+    gbs = dec_bytes / (ms_launch * 1e-3) / 1e9
+    hbm = peaks()["hbm"]
+    return {"workload": f"configs[1]'s step at ctx {CTX_LONG}: 1 sequence, 12 layers, T=3, one fused append + decode "
+                        "launch (and its merge) per layer; device-seeded N(0,1) prefix (seed 73)",
+            "tokens_per_s": T * steps / (ms * 1e-3), "us_per_layer": 1e3 * ms_launch, "steps": steps,
+            "timing": f"the {steps} steps as one CUDA graph, median of {REPLAYS} replays",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "bytes_per_launch": dec_bytes},
+            "parity": {"checked": "layer 0 of the last step (appended rows bit-exact; attention vs oracle/qkv_oracle.c)",
+                       "atol": 2e-3, "rtol": 1e-3, "max_abs": float(err.max()), "ok": ok}}
+
+
 # ----------------------------------------------------------------------------- configs[4] (ragged)
 PREFIX = 8192
 
@@ -842,6 +928,7 @@ def run_ours(args) -> None:
             c3 = measure_cfg3(args, rank, ws, local, e2e=False)
             extras["configs[2]"] = c3
             extras["configs[3]"] = measure_cfg4(args, local)
+            extras["ctx73728"] = measure_long(args, local)
             line["configs"] = extras
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1440,6 +1527,8 @@ def main():
         run_proj(args)
     elif args.workload == "append":
         run_append(args)
+    elif args.workload == "long":
+        run_single(args, measure_long)
     else:
         run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

@@ -152,6 +152,7 @@ struct SelectParams {
     int32_t        *idx_out;      // [n_seq][n_head_kv][top_k]
     float          *scores;       // [n_seq][n_head_kv][max_blocks]: the caller's scores_out, or engine scratch
     int32_t n_seq, T, n_head, n_head_kv, G, top_k, max_blocks;
+    int32_t chunk, rk;            // set by launch_select: candidates per score CTA, rank CTAs per (sequence, head)
     int32_t seq_slot[MAX_SEQ];
     int32_t seq_nblk[MAX_SEQ];    // candidate blocks of each sequence
 };

@@ -589,23 +589,26 @@ cudaError_t launch_block_summary(const PoolRef &pr, int32_t b0, int32_t b1, uint
 
 // ------------------------------------------------------------------------------------ kernel B1
 // Block scores and top-k, two kernels.
-// k_select_score: CTA (sequence x KV head, chunk of SEL_CHUNK candidate blocks), 256 threads.
+// k_select_score: CTA (sequence x KV head, chunk of p.chunk candidate blocks), 256 threads.
 // Groups of 8 lanes compute one dot product in the oracle's fixed order: lane l takes dims
 // 32l..32l+31 with sequential fmaf, then a fixed tree over the 8 lanes.  The group's lane 0 sums
 // relu(dot) over the G*T query rows in order (t-major), so every score is bit-exact with the CPU
 // restatement; four rows' dot products run side by side.  The query rows sit in shared memory as
 // 8 segments of 32 dims padded to 36 floats, so the 8 lanes of a group read their segments with
 // conflict-free 16-byte loads; the next round's summary bytes are loaded during the current round.
-// k_select_rank: CTA (sequence x KV head, 1/SEL_RK of the candidates): all scores into shared
+// k_select_rank: CTA (sequence x KV head, 1/p.rk of the candidates): all scores into shared
 // memory, then each candidate's rank (score descending, block index ascending) is the number of
 // candidates ahead of it, counted by a whole warp.
-constexpr int SEL_SEG = 36, SEL_CHUNK = 64, SEL_RK = 8;
+// Both are latency chains over few blocks: launch_select splits the candidates as finely as keeps
+// the grids within about two CTAs per SM (a finer split repeats each CTA's staging: the query rows,
+// all scores), so a single sequence's selection runs on most SMs and a wide batch as before.
+constexpr int SEL_SEG = 36, SEL_CHUNK_MIN = 16, SEL_CHUNK_MAX = 64, SEL_RK_MIN = 8, SEL_RK_MAX = 144;
 __global__ void __launch_bounds__(256) k_select_score(const SelectParams p) {
     extern __shared__ float qs[];                    // [nq][8][SEL_SEG]
     const int sh = blockIdx.x, s = sh / p.n_head_kv, h = sh % p.n_head_kv;
     const int nq = p.T * p.G;
     const int slot = p.seq_slot[s], nb = p.seq_nblk[s];
-    const int c0 = blockIdx.y * SEL_CHUNK, c1 = min(nb, c0 + SEL_CHUNK);
+    const int c0 = blockIdx.y * p.chunk, c1 = min(nb, c0 + p.chunk);
     if (c0 >= nb) return;
     // the group's query rows, float4 loads all issued before the stores (nq * HD / 4 <= 16 per thread)
     {
@@ -696,11 +699,11 @@ __global__ void __launch_bounds__(256) k_select_rank(const SelectParams p) {
     extern __shared__ float sc[];                    // [nb] every candidate's score
     const int sh = blockIdx.x, s = sh / p.n_head_kv, h = sh % p.n_head_kv, r = blockIdx.y;
     const int nb = p.seq_nblk[s];
-    const int c0 = (int)((int64_t)nb * r / SEL_RK), c1 = (int)((int64_t)nb * (r + 1) / SEL_RK);
+    const int c0 = (int)((int64_t)nb * r / p.rk), c1 = (int)((int64_t)nb * (r + 1) / p.rk);
     int32_t *out = p.idx_out + ((int64_t)s * p.n_head_kv + h) * p.top_k;
     if (nb <= p.top_k) {
         for (int k = c0 + threadIdx.x; k < c1; k += blockDim.x) out[k] = k;
-        if (r == SEL_RK - 1)
+        if (r == p.rk - 1)
             for (int k = nb + threadIdx.x; k < p.top_k; k += blockDim.x) out[k] = -1;
         return;
     }
@@ -721,17 +724,25 @@ __global__ void __launch_bounds__(256) k_select_rank(const SelectParams p) {
     }
 }
 
-cudaError_t launch_select(const SelectParams &p, cudaStream_t st) {
+cudaError_t launch_select(const SelectParams &p_in, cudaStream_t st) {
+    SelectParams p = p_in;
     int max_nb = 1;
     for (int i = 0; i < p.n_seq; i++) max_nb = std::max(max_nb, p.seq_nblk[i]);
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        sms = 148;
+    const int64_t heads = (int64_t)p.n_seq * p.n_head_kv, budget = 2 * (int64_t)sms;
+    p.chunk = SEL_CHUNK_MIN;
+    while (p.chunk < SEL_CHUNK_MAX && heads * ((max_nb + p.chunk - 1) / p.chunk) > budget) p.chunk *= 2;
+    p.rk = (int)std::max<int64_t>(SEL_RK_MIN, std::min<int64_t>(SEL_RK_MAX, budget / std::max<int64_t>(heads, 1)));
     const size_t qsm = (size_t)p.T * p.G * 8 * SEL_SEG * sizeof(float), rsm = (size_t)max_nb * sizeof(float);
     cudaError_t e;
     if (qsm > 48 * 1024 && (e = cudaFuncSetAttribute(k_select_score, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm)) != cudaSuccess)
         return e;
     if (rsm > 48 * 1024 && (e = cudaFuncSetAttribute(k_select_rank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm)) != cudaSuccess)
         return e;
-    k_select_score<<<dim3((unsigned)(p.n_seq * p.n_head_kv), (unsigned)((max_nb + SEL_CHUNK - 1) / SEL_CHUNK)), 256, qsm, st>>>(p);
-    k_select_rank<<<dim3((unsigned)(p.n_seq * p.n_head_kv), SEL_RK), 256, rsm, st>>>(p);
+    k_select_score<<<dim3((unsigned)(p.n_seq * p.n_head_kv), (unsigned)((max_nb + p.chunk - 1) / p.chunk)), 256, qsm, st>>>(p);
+    k_select_rank<<<dim3((unsigned)(p.n_seq * p.n_head_kv), (unsigned)p.rk), 256, rsm, st>>>(p);
     count_launches(2);
     return cudaGetLastError();
 }

@@ -15,8 +15,9 @@ copies issued, 18 / 19 thread 0's first / all query values arrived, 7 query rows
 2 rows in shared memory (CTA barrier), 8 first tile landed, 10-13 first tile: QK done, P barrier,
 after the reference move, PV done; 3 first tile finished; 14-17 the same for the second tile; 4 all
 tiles done; 5 partial record written.  Merge phases: 0 entry, 1 wait returned, 2 output written.
-Projection phases: 0 entry, 1 x staged, 2 dot products done, 3 the head's rows gathered by the
-cluster's lead CTA (after the second cluster barrier), 4 epilogue done (the lead CTA only).
+Projection phases: 0 entry, 1 x staged, 2 dot products done, 3 the cluster's normalised dims
+posted (after its second barrier), 4 the CTA's epilogue done (every CTA: each holds 32 dims of
+the head).
 Prefill: per-role phase durations of kernel D (see `prefill`).
 """
 from __future__ import annotations

@@ -152,6 +152,38 @@ def test_sparse_select_fewer_blocks_than_topk(cuda, qkvlib, oracle):
     assert list(idx[0]) == [0, 1, 2, 3, 4, -1, -1, -1]
 
 
+def test_sparse_select_wide_batch(cuda, qkvlib, oracle):
+    """40 sequences x 2 KV heads of 64 blocks: the selection grids take their coarser split
+    (32 candidates per score CTA, 8 rank CTAs per head) instead of a single sequence's finest
+    one; every sequence's scores and indices bit-exact."""
+    import torch
+    n_seq, n_kv, T, top_k = 40, 64 * 64, 3, 8
+    nb = n_kv // 64
+    eng = engine(qkvlib, n_ctx=n_kv + 64, n_slots=n_seq, select_block=64)
+    Qs, refs = [], []
+    for s in range(n_seq):
+        r = np.random.default_rng(100 + s)
+        off = (r.standard_normal((nb, 2, 1)) * np.sqrt(2.0)).astype(np.float32)
+        Kf = (normal(200 + s, (nb * 64, 2, HD)) + off.repeat(64, axis=0)).reshape(n_kv, 512)
+        Vf = normal(300 + s, (n_kv, 512))
+        eng.seq_alloc(s)
+        append_rows(eng, 0, s, 0, Kf, Vf)
+        Q = normal(400 + s, (T, 16, HD))
+        Qs.append(Q)
+        summ_full = np.zeros((2, nb, HD), np.uint16)
+        summ_full[:, :nb - 2] = oracle.block_summary(oracle.quantize_rows(Kf), 2, HD, 64, nb - 2)
+        refs.append(oracle.select_blocks(Q, 2, summ_full, nb, top_k))
+    idx = torch.empty((n_seq, 2, top_k), dtype=torch.int32, device="cuda")
+    scores = torch.full((n_seq, 2, eng.cfg.n_ctx // 64), float("nan"), dtype=torch.float32, device="cuda")
+    eng.select_blocks(0, list(range(n_seq)), [n_kv - T] * n_seq, to_dev(np.stack(Qs)), T, top_k, idx, scores)
+    torch.cuda.synchronize()
+    assert eng.device_status() == 0
+    got_idx, got_sc = idx.cpu().numpy(), scores.cpu().numpy()
+    for s, (ref_idx, ref_sc) in enumerate(refs):
+        assert np.array_equal(got_sc[s][:, :nb].view(np.uint32), ref_sc.view(np.uint32)), f"scores of sequence {s}"
+        assert np.array_equal(got_idx[s], ref_idx), f"indices of sequence {s}"
+
+
 def test_sparse_config4_full_size(cuda, qkvlib, oracle):
     """ctx 73728, 64-token blocks, top-32 per KV head, T = 3."""
     sparse_case(cuda, qkvlib, oracle, n_kv=73728, T=3, top_k=32, seed=3)
